@@ -1,0 +1,280 @@
+// pybind11 bindings of the connex_b200._C extension (sm_100a kernels plus
+// CUDA IPC plumbing for peer buffers).  Every op launches on the current
+// torch stream of the tensor's device and never allocates device memory
+// itself: outputs and workspaces come from the caller.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include <string>
+#include <vector>
+
+#include "comm.h"
+#include "gemm.h"
+#include "layers.h"
+#include "moe.h"
+
+namespace {
+
+#define CHECK_CUDA(x) TORCH_CHECK((x).is_cuda(), #x " must be a CUDA tensor")
+#define CHECK_BF16(x) TORCH_CHECK((x).scalar_type() == at::kBFloat16, #x " must be bf16")
+
+cudaStream_t cur_stream(const at::Tensor& t) { return at::cuda::getCurrentCUDAStream(t.get_device()).stream(); }
+
+int* status_ptr(const c10::optional<at::Tensor>& st) {
+  if (!st.has_value()) return nullptr;
+  TORCH_CHECK(st->scalar_type() == at::kInt && st->is_cuda(), "status must be an int32 CUDA tensor");
+  return st->data_ptr<int>();
+}
+
+int row_ld(const at::Tensor& t) {
+  TORCH_CHECK(t.dim() == 2, "expected a 2-D tensor");
+  TORCH_CHECK(t.stride(1) == 1, "rows must be contiguous");
+  return (int)t.stride(0);
+}
+
+// D = A . B^T (+ R) | SiLU-mul epilogue.  A [M,K], B [N,K], D [M,N or N/2].
+void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10::optional<at::Tensor>& R, int64_t epi,
+          int64_t bn, const c10::optional<at::Tensor>& status, int64_t max_ctas) {
+  CHECK_CUDA(A);
+  CHECK_CUDA(B);
+  CHECK_CUDA(D);
+  CHECK_BF16(A);
+  CHECK_BF16(B);
+  CHECK_BF16(D);
+  const c10::cuda::CUDAGuard g(A.device());
+  const int M = (int)A.size(0), K = (int)A.size(1), N = (int)B.size(0);
+  TORCH_CHECK(B.size(1) == K, "gemm: K mismatch");
+  if (epi == cx::EPI_SILU_MUL) {
+    TORCH_CHECK(D.size(0) == M && D.size(1) == N / 2, "gemm: SiLU-mul output must be [M, N/2]");
+  } else {
+    TORCH_CHECK(D.size(0) == M && D.size(1) == N, "gemm: output shape mismatch");
+  }
+  const void* rp = nullptr;
+  int ldr = 0;
+  if (epi == cx::EPI_ADD) {
+    TORCH_CHECK(R.has_value(), "gemm: residual epilogue needs R");
+    CHECK_BF16((*R));
+    rp = R->data_ptr();
+    ldr = row_ld(*R);
+  }
+  if (M == 0) return;
+  cx::gemm_bf16_tn(A.data_ptr(), B.data_ptr(), D.data_ptr(), rp, M, N, K, row_ld(A), row_ld(B), row_ld(D), ldr,
+                   (int)epi, (int)bn, status_ptr(status), (int)max_ctas, cur_stream(A));
+}
+
+void rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual, const at::Tensor& w, at::Tensor& out,
+             double eps) {
+  CHECK_BF16(x);
+  CHECK_BF16(w);
+  CHECK_BF16(out);
+  const c10::cuda::CUDAGuard g(x.device());
+  void* rp = nullptr;
+  int ldr = 0;
+  if (residual.has_value()) {
+    rp = residual->data_ptr();
+    ldr = row_ld(*residual);
+  }
+  const int H = (int)x.size(1);
+  TORCH_CHECK(H % 8 == 0, "rmsnorm: hidden size must be a multiple of 8");
+  cx::rmsnorm(x.data_ptr(), row_ld(x), rp, ldr, w.data_ptr(), out.data_ptr(), row_ld(out), (int)x.size(0), H,
+              (float)eps, cur_stream(x));
+}
+
+void rope_cache(at::Tensor& qkv, const at::Tensor& pos, const at::Tensor& cos_sin,
+                const c10::optional<at::Tensor>& slots, const c10::optional<at::Tensor>& kc,
+                const c10::optional<at::Tensor>& vc, int64_t Hq, int64_t Hkv, const c10::optional<at::Tensor>& status) {
+  CHECK_BF16(qkv);
+  TORCH_CHECK(pos.scalar_type() == at::kInt, "positions must be int32");
+  TORCH_CHECK(cos_sin.scalar_type() == at::kFloat, "cos_sin must be fp32");
+  const c10::cuda::CUDAGuard g(qkv.device());
+  const int64_t* sp = nullptr;
+  void *kp = nullptr, *vp = nullptr;
+  int BS = 16, nb = 0;
+  if (slots.has_value()) {
+    TORCH_CHECK(slots->scalar_type() == at::kLong, "slot_mapping must be int64");
+    TORCH_CHECK(kc.has_value() && vc.has_value(), "rope_cache: caches required with a slot mapping");
+    sp = slots->data_ptr<int64_t>();
+    kp = kc->data_ptr();
+    vp = vc->data_ptr();
+    nb = (int)kc->size(0);
+    BS = (int)kc->size(2);
+  }
+  cx::rope_cache(qkv.data_ptr(), row_ld(qkv), pos.data_ptr<int>(), cos_sin.data_ptr<float>(), sp, kp, vp,
+                 (int)qkv.size(0), (int)Hq, (int)Hkv, 128, BS, nb, (int)cos_sin.size(0), status_ptr(status),
+                 cur_stream(qkv));
+}
+
+void embedding(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out,
+               const c10::optional<at::Tensor>& status) {
+  TORCH_CHECK(ids.scalar_type() == at::kInt, "ids must be int32");
+  const c10::cuda::CUDAGuard g(table.device());
+  cx::embedding(ids.data_ptr<int>(), table.data_ptr(), out.data_ptr(), (int)ids.numel(), (int)table.size(1),
+                (int)table.size(0), status_ptr(status), cur_stream(table));
+}
+
+void argmax(const at::Tensor& logits, at::Tensor& out) {
+  CHECK_BF16(logits);
+  TORCH_CHECK(out.scalar_type() == at::kInt, "argmax output must be int32");
+  const c10::cuda::CUDAGuard g(logits.device());
+  cx::argmax(logits.data_ptr(), row_ld(logits), (int)logits.size(0), (int)logits.size(1), out.data_ptr<int>(),
+             cur_stream(logits));
+}
+
+void gather_rows(const at::Tensor& src, const at::Tensor& idx, at::Tensor& out) {
+  const c10::cuda::CUDAGuard g(src.device());
+  cx::gather_rows(src.data_ptr(), row_ld(src), idx.data_ptr<int>(), out.data_ptr(), row_ld(out), (int)idx.numel(),
+                  (int)src.size(1), cur_stream(src));
+}
+
+void prefill_attention(const at::Tensor& qkv, at::Tensor& out, const at::Tensor& tile_info, int64_t Hq, int64_t Hkv,
+                       double scale) {
+  CHECK_BF16(qkv);
+  CHECK_BF16(out);
+  TORCH_CHECK(tile_info.scalar_type() == at::kInt && tile_info.dim() == 2 && tile_info.size(1) == 3,
+              "tile_info must be int32 [n, 3]");
+  const c10::cuda::CUDAGuard g(qkv.device());
+  cx::prefill_attention(qkv.data_ptr(), row_ld(qkv), out.data_ptr(), row_ld(out), tile_info.data_ptr<int>(),
+                        (int)tile_info.size(0), (int)Hq, (int)Hkv, (float)scale, cur_stream(qkv));
+}
+
+void decode_attention(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc, const at::Tensor& block_tables,
+                      const at::Tensor& ctx_lens, at::Tensor& out, int64_t Hq, int64_t max_ctx, double scale,
+                      at::Tensor& workspace) {
+  CHECK_BF16(q);
+  CHECK_BF16(kc);
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt && ctx_lens.scalar_type() == at::kInt, "int32 tables");
+  TORCH_CHECK(workspace.scalar_type() == at::kFloat, "workspace must be fp32");
+  const c10::cuda::CUDAGuard g(q.device());
+  const int B = (int)q.size(0);
+  const int Hkv = (int)kc.size(1), BS = (int)kc.size(2);
+  const int splits = cx::decode_attention_splits((int)max_ctx);
+  TORCH_CHECK(workspace.numel() >= (int64_t)B * Hq * splits * 130, "decode workspace too small");
+  cx::decode_attention(q.data_ptr(), row_ld(q), kc.data_ptr(), vc.data_ptr(), block_tables.data_ptr<int>(),
+                       (int)block_tables.size(1), ctx_lens.data_ptr<int>(), out.data_ptr(), row_ld(out), B, (int)Hq,
+                       Hkv, BS, (int)max_ctx, (float)scale, workspace.data_ptr<float>(), cur_stream(q));
+}
+
+int64_t decode_workspace_floats(int64_t B, int64_t Hq, int64_t max_ctx) {
+  return B * Hq * cx::decode_attention_splits((int)max_ctx) * 130;
+}
+
+// ---- peer-memory movement (addresses may be local or peer-mapped) ----------
+int64_t kv_push_layer(int64_t src_k, int64_t src_v, int64_t dst_k, int64_t dst_v, const at::Tensor& pairs,
+                      int64_t src_heads, int64_t dst_heads, int64_t src_h0, int64_t dst_h0, int64_t n_heads,
+                      int64_t chunk_bytes, int64_t src_blocks, int64_t dst_blocks, int64_t ready, int64_t max_ctas,
+                      const c10::optional<at::Tensor>& status) {
+  TORCH_CHECK(pairs.scalar_type() == at::kInt && pairs.is_cuda(), "pairs must be int32 CUDA [n, 2]");
+  const c10::cuda::CUDAGuard g(pairs.device());
+  return cx::kv_push_layer(reinterpret_cast<const void*>(src_k), reinterpret_cast<const void*>(src_v),
+                           reinterpret_cast<void*>(dst_k), reinterpret_cast<void*>(dst_v), pairs.data_ptr<int>(),
+                           (int)pairs.size(0), (int)src_heads, (int)dst_heads, (int)src_h0, (int)dst_h0, (int)n_heads,
+                           (int)chunk_bytes, (int)src_blocks, (int)dst_blocks, reinterpret_cast<uint32_t*>(ready),
+                           (int)max_ctas, status_ptr(status), cur_stream(pairs));
+}
+
+int64_t copy_segments(const at::Tensor& segs, int64_t total_bytes, int64_t ready, int64_t max_ctas,
+                      const c10::optional<at::Tensor>& status) {
+  TORCH_CHECK(segs.scalar_type() == at::kLong && segs.is_cuda() && segs.dim() == 2 && segs.size(1) == 3,
+              "segs must be int64 CUDA [n, 3]");
+  const c10::cuda::CUDAGuard g(segs.device());
+  return cx::copy_segments(segs.data_ptr<int64_t>(), (int)segs.size(0), total_bytes,
+                           reinterpret_cast<uint32_t*>(ready), (int)max_ctas, status_ptr(status), cur_stream(segs));
+}
+
+void wait_flag(int64_t flag, int64_t target, int64_t timeout_ns, const at::Tensor& status) {
+  const c10::cuda::CUDAGuard g(status.device());
+  cx::wait_flag(reinterpret_cast<const uint32_t*>(flag), (uint32_t)target, (uint64_t)timeout_ns,
+                status.data_ptr<int>(), cur_stream(status));
+}
+
+void write_flag(int64_t flag, int64_t value, bool add, const at::Tensor& like) {
+  const c10::cuda::CUDAGuard g(like.device());
+  cx::write_flag(reinterpret_cast<uint32_t*>(flag), (uint32_t)value, add, cur_stream(like));
+}
+
+// ---- CUDA IPC ---------------------------------------------------------------
+// Export the allocation that contains `ptr`: returns (handle bytes, offset of
+// ptr inside the allocation).
+std::pair<py::bytes, int64_t> ipc_export(int64_t ptr, int64_t device) {
+  const c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  CUdeviceptr base = 0;
+  size_t size = 0;
+  using RangeFn = CUresult (*)(CUdeviceptr*, size_t*, CUdeviceptr);
+  static RangeFn range = nullptr;
+  if (range == nullptr) {
+    void* p = nullptr;
+    cudaDriverEntryPointQueryResult q;
+    C10_CUDA_CHECK(cudaGetDriverEntryPoint("cuMemGetAddressRange", &p, cudaEnableDefault, &q));
+    TORCH_CHECK(q == cudaDriverEntryPointSuccess && p, "cuMemGetAddressRange unavailable");
+    range = reinterpret_cast<RangeFn>(p);
+  }
+  TORCH_CHECK(range(&base, &size, (CUdeviceptr)ptr) == CUDA_SUCCESS, "cuMemGetAddressRange failed");
+  cudaIpcMemHandle_t h;
+  C10_CUDA_CHECK(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(base)));
+  return {py::bytes(reinterpret_cast<const char*>(&h), sizeof(h)), (int64_t)(ptr - (int64_t)base)};
+}
+
+int64_t ipc_open(const std::string& handle, int64_t device) {
+  TORCH_CHECK(handle.size() == sizeof(cudaIpcMemHandle_t), "bad IPC handle size");
+  const c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  cudaIpcMemHandle_t h;
+  memcpy(&h, handle.data(), sizeof(h));
+  void* p = nullptr;
+  C10_CUDA_CHECK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  return reinterpret_cast<int64_t>(p);
+}
+
+void ipc_close(int64_t ptr, int64_t device) {
+  const c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  C10_CUDA_CHECK(cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr)));
+}
+
+bool enable_peer_access(int64_t device, int64_t peer) {
+  const c10::cuda::CUDAGuard g((c10::DeviceIndex)device);
+  int can = 0;
+  C10_CUDA_CHECK(cudaDeviceCanAccessPeer(&can, (int)device, (int)peer));
+  if (!can) return false;
+  cudaError_t e = cudaDeviceEnablePeerAccess((int)peer, 0);
+  if (e == cudaErrorPeerAccessAlreadyEnabled) {
+    (void)cudaGetLastError();
+    return true;
+  }
+  C10_CUDA_CHECK(e);
+  return true;
+}
+
+// Wrap a raw device address as a tensor view (no ownership).
+at::Tensor from_ptr(int64_t ptr, std::vector<int64_t> shape, at::ScalarType dtype, int64_t device) {
+  auto opts = at::TensorOptions().dtype(dtype).device(at::kCUDA, (c10::DeviceIndex)device);
+  return torch::from_blob(reinterpret_cast<void*>(ptr), shape, opts);
+}
+
+}  // namespace
+
+
+PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
+  m.doc() = "connex_b200 sm_100a kernels";
+  m.def("gemm", &gemm, py::arg("A"), py::arg("B"), py::arg("D"), py::arg("R") = py::none(), py::arg("epi") = 0,
+        py::arg("bn") = 0, py::arg("status") = py::none(), py::arg("max_ctas") = 0);
+  m.def("rmsnorm", &rmsnorm);
+  m.def("rope_cache", &rope_cache);
+  m.def("embedding", &embedding);
+  m.def("argmax", &argmax);
+  m.def("gather_rows", &gather_rows);
+  m.def("prefill_attention", &prefill_attention);
+  m.def("decode_attention", &decode_attention);
+  m.def("decode_workspace_floats", &decode_workspace_floats);
+  m.def("kv_push_layer", &kv_push_layer);
+  m.def("copy_segments", &copy_segments);
+  m.def("wait_flag", &wait_flag);
+  m.def("write_flag", &write_flag);
+  m.def("ipc_export", &ipc_export);
+  m.def("ipc_open", &ipc_open);
+  m.def("ipc_close", &ipc_close);
+  m.def("enable_peer_access", &enable_peer_access);
+  m.def("from_ptr", &from_ptr);
+  m.attr("EPI_STORE") = (int)cx::EPI_STORE;
+  m.attr("EPI_ADD") = (int)cx::EPI_ADD;
+  m.attr("EPI_SILU_MUL") = (int)cx::EPI_SILU_MUL;
+}

@@ -1,0 +1,22 @@
+// Host entry points of the peer-memory kernels (kv_push.cu, moe.cu, wsync.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdexcept>
+
+namespace cx {
+
+int num_sms_comm();
+
+// Returns the number of CTAs launched (each releases `ready` by one).
+int kv_push_layer(const void* src_k, const void* src_v, void* dst_k, void* dst_v, const int* pairs, int n_pairs,
+                  int src_heads, int dst_heads, int src_h0, int dst_h0, int n_heads, int chunk_bytes, int src_blocks,
+                  int dst_blocks, uint32_t* ready, int max_ctas, int* status, cudaStream_t s);
+
+int copy_segments(const int64_t* segs, int n, int64_t total_bytes, uint32_t* ready, int max_ctas, int* status,
+                  cudaStream_t s);
+
+void wait_flag(const uint32_t* flag, uint32_t target, uint64_t timeout_ns, int* status, cudaStream_t s);
+void write_flag(uint32_t* flag, uint32_t value, bool add, cudaStream_t s);
+
+}  // namespace cx

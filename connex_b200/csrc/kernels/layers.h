@@ -1,0 +1,31 @@
+// Host entry points of the runtime kernels (layers.cu, attention.cu).
+#pragma once
+#include <cuda_runtime.h>
+#include <stdint.h>
+#include <stdexcept>
+
+namespace cx {
+
+void rmsnorm(const void* x, int ldx, void* residual, int ldr, const void* w, void* out, int ldo, int T, int H,
+             float eps, cudaStream_t s);
+void rope_cache(void* qkv, int ldq, const int* pos, const float* cos_sin, const int64_t* slots, void* kc, void* vc,
+                int T, int Hq, int Hkv, int D, int BS, int num_blocks, int max_pos, int* status, cudaStream_t s);
+void embedding(const int* ids, const void* table, void* out, int T, int H, int V, int* status, cudaStream_t s);
+void argmax(const void* logits, int ldl, int B, int V, int* out, cudaStream_t s);
+void gather_rows(const void* src, int lds, const int* idx, void* out, int ldo, int n, int H, cudaStream_t s);
+
+// Causal varlen prefill attention (GQA, head_dim 128).  q/k/v rows live in the
+// fused QKV buffer [T, (Hq+2Hkv)*128]; tile_info: [n_tiles, 3] int32 of
+// (seq start row, seq length, first query row of the tile within the seq).
+void prefill_attention(const void* qkv, int ldq, void* out, int ldo, const int* tile_info, int n_tiles, int Hq,
+                       int Hkv, float scale, cudaStream_t s);
+
+// Paged decode attention.  q: [B, *] rows (ld ldq, q heads first).
+// Caches [blocks, Hkv, BS, 128]; block_tables [B, max_blocks]; ctx_lens [B].
+// workspace: fp32, at least B*Hq*max_splits*(128+2) floats.
+void decode_attention(const void* q, int ldq, const void* kc, const void* vc, const int* block_tables,
+                      int max_blocks, const int* ctx_lens, void* out, int ldo, int B, int Hq, int Hkv, int BS,
+                      int max_ctx, float scale, float* workspace, cudaStream_t s);
+int decode_attention_splits(int max_ctx);
+
+}  // namespace cx

@@ -1,0 +1,203 @@
+"""Python surface of the sm_100a kernels in ``connex_b200._C``.
+
+Every function here launches one of this package's own CUDA kernels on the
+current torch stream.  There is no fallback: if the extension is missing the
+import of :mod:`connex_b200.ops` raises, so a GPU run can never silently
+execute a PyTorch re-statement instead of the native kernels.  (The fp32
+PyTorch re-statements used as test oracles live in
+:mod:`connex_b200.ops.reference` and are never called from here.)
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+
+try:
+    from connex_b200 import _C  # noqa: F401
+except ImportError as e:  # pragma: no cover - exercised only on broken installs
+    raise ImportError(
+        "connex_b200._C is not built; run `python setup.py build_ext --inplace` "
+        f"(sm_100a) before using connex_b200.ops: {e}") from e
+
+EPI_STORE = _C.EPI_STORE
+EPI_ADD = _C.EPI_ADD
+EPI_SILU_MUL = _C.EPI_SILU_MUL
+
+# Tile width of the fused SiLU(gate)*up epilogue: weights for it are stored
+# with gate and up rows interleaved in blocks of GATE_UP_TILE // 2.
+GATE_UP_TILE = 256
+
+
+def new_status(device) -> torch.Tensor:
+    """An int32 device status word (0 = ok) that kernels write error codes to."""
+    return torch.zeros(1, dtype=torch.int32, device=device)
+
+
+STATUS_NAMES = {0: "ok", 1: "timeout", 2: "bounds", 3: "peer-abort"}
+
+
+def check_status(status: torch.Tensor, what: str = "kernel") -> None:
+    code = int(status.item())
+    if code != 0:
+        raise RuntimeError(f"{what}: device status {code} ({STATUS_NAMES.get(code, '?')})")
+
+
+# ----------------------------------------------------------------- GEMM
+def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, *,
+         residual: Optional[torch.Tensor] = None, silu_mul: bool = False, bn: int = 0,
+         status: Optional[torch.Tensor] = None, max_ctas: int = 0) -> torch.Tensor:
+    """``a[M,K] @ b[N,K]^T`` on tcgen05 tensor cores (bf16 in/out, fp32 accumulate).
+
+    ``residual`` adds a bf16 tensor in the epilogue (may alias ``out``).
+    ``silu_mul`` treats ``b`` as gate/up rows interleaved per 256-row tile
+    (see :func:`interleave_gate_up`) and writes ``SiLU(gate) * up`` of width N/2.
+    """
+    M, N = a.shape[0], b.shape[0]
+    if out is None:
+        out = torch.empty(M, N // 2 if silu_mul else N, dtype=torch.bfloat16, device=a.device)
+    epi = EPI_SILU_MUL if silu_mul else (EPI_ADD if residual is not None else EPI_STORE)
+    _C.gemm(a, b, out, residual, epi, bn, status, max_ctas)
+    return out
+
+
+def interleave_gate_up(gate: torch.Tensor, up: torch.Tensor, tile: int = GATE_UP_TILE) -> torch.Tensor:
+    """Stack gate [F,K] and up [F,K] as [2F,K] with rows interleaved in blocks
+    of tile/2, the weight layout of the fused SiLU-mul GEMM epilogue."""
+    F, K = gate.shape
+    half = tile // 2
+    assert F % half == 0, "FFN width must be a multiple of half the tile"
+    g = gate.reshape(F // half, half, K)
+    u = up.reshape(F // half, half, K)
+    return torch.stack([g, u], dim=1).reshape(2 * F, K).contiguous()
+
+
+def deinterleave_gate_up(w: torch.Tensor, tile: int = GATE_UP_TILE):
+    F2, K = w.shape
+    half = tile // 2
+    x = w.reshape(F2 // tile, 2, half, K)
+    return x[:, 0].reshape(-1, K), x[:, 1].reshape(-1, K)
+
+
+# ------------------------------------------------------------- layers
+def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: Optional[torch.Tensor] = None,
+            residual: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """RMSNorm of ``x`` (or of ``x + residual``, written back into ``residual``)."""
+    if out is None:
+        out = torch.empty_like(x)
+    _C.rmsnorm(x, residual, weight, out, eps)
+    return out
+
+
+def rope_cache(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor, n_q_heads: int,
+               n_kv_heads: int, slot_mapping: Optional[torch.Tensor] = None,
+               k_cache: Optional[torch.Tensor] = None, v_cache: Optional[torch.Tensor] = None,
+               status: Optional[torch.Tensor] = None) -> None:
+    """Rotate q/k of the fused QKV rows in place; write k/v to their paged slots."""
+    _C.rope_cache(qkv, positions, cos_sin, slot_mapping, k_cache, v_cache, n_q_heads, n_kv_heads, status)
+
+
+def rope_cos_sin(max_pos: int, head_dim: int, theta: float, device) -> torch.Tensor:
+    """fp32 [max_pos, head_dim] table: cos in the first half, sin in the second."""
+    inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
+    ang = torch.arange(max_pos, dtype=torch.float64)[:, None] * inv[None, :]
+    return torch.cat([ang.cos(), ang.sin()], dim=1).to(torch.float32).to(device)
+
+
+def embedding(ids: torch.Tensor, table: torch.Tensor, out: Optional[torch.Tensor] = None,
+              status: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty(ids.numel(), table.shape[1], dtype=table.dtype, device=table.device)
+    _C.embedding(ids, table, out, status)
+    return out
+
+
+def argmax(logits: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
+    _C.argmax(logits, out)
+    return out
+
+
+def gather_rows(src: torch.Tensor, idx: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty(idx.numel(), src.shape[1], dtype=src.dtype, device=src.device)
+    _C.gather_rows(src, idx, out)
+    return out
+
+
+# ---------------------------------------------------------- attention
+PREFILL_TILE = 64
+
+
+def prefill_tile_info(seq_lens, device) -> torch.Tensor:
+    """[n_tiles, 3] int32 (seq start row, seq length, first query of tile)."""
+    rows = []
+    start = 0
+    for n in seq_lens:
+        for q0 in range(0, n, PREFILL_TILE):
+            rows.append((start, n, q0))
+        start += n
+    t = torch.tensor(rows if rows else [(0, 0, 0)], dtype=torch.int32)
+    return t.to(device, non_blocking=True) if rows else t[:0].to(device)
+
+
+def prefill_attention(qkv: torch.Tensor, tile_info: torch.Tensor, n_q_heads: int, n_kv_heads: int,
+                      out: Optional[torch.Tensor] = None, scale: Optional[float] = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty(qkv.shape[0], n_q_heads * 128, dtype=qkv.dtype, device=qkv.device)
+    _C.prefill_attention(qkv, out, tile_info, n_q_heads, n_kv_heads,
+                         scale if scale is not None else 1.0 / math.sqrt(128))
+    return out
+
+
+def decode_workspace(batch: int, n_q_heads: int, max_ctx: int, device) -> torch.Tensor:
+    return torch.empty(_C.decode_workspace_floats(batch, n_q_heads, max_ctx), dtype=torch.float32,
+                       device=device)
+
+
+def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                     block_tables: torch.Tensor, ctx_lens: torch.Tensor, n_q_heads: int, max_ctx: int,
+                     workspace: torch.Tensor, out: Optional[torch.Tensor] = None,
+                     scale: Optional[float] = None) -> torch.Tensor:
+    if out is None:
+        out = torch.empty(q.shape[0], n_q_heads * 128, dtype=q.dtype, device=q.device)
+    _C.decode_attention(q, k_cache, v_cache, block_tables, ctx_lens, out, n_q_heads, max_ctx,
+                        scale if scale is not None else 1.0 / math.sqrt(128), workspace)
+    return out
+
+
+# ------------------------------------------------------- peer memory
+def kv_push_layer(src_k: int, src_v: int, dst_k: int, dst_v: int, pairs: torch.Tensor, *,
+                  src_heads: int, dst_heads: int, src_h0: int = 0, dst_h0: int = 0,
+                  n_heads: Optional[int] = None, chunk_bytes: int, src_blocks: int, dst_blocks: int,
+                  ready: int = 0, max_ctas: int = 0, status: Optional[torch.Tensor] = None) -> int:
+    """Push one layer's paged KV blocks (pairs: int32 [n, 2] of src/dst block
+    ids) from local caches to (peer-mapped) destination caches.  Returns the
+    number of CTAs, each of which adds 1 to the u32 at ``ready`` when done."""
+    return _C.kv_push_layer(src_k, src_v, dst_k, dst_v, pairs, src_heads, dst_heads, src_h0, dst_h0,
+                            n_heads if n_heads is not None else src_heads, chunk_bytes, src_blocks,
+                            dst_blocks, ready, max_ctas, status)
+
+
+def copy_segments(segs: torch.Tensor, total_bytes: int, ready: int = 0, max_ctas: int = 0,
+                  status: Optional[torch.Tensor] = None) -> int:
+    """Copy (src, dst, bytes) int64 segments (16-byte aligned) with SM loads/stores."""
+    return _C.copy_segments(segs, total_bytes, ready, max_ctas, status)
+
+
+def wait_flag(flag_addr: int, target: int, status: torch.Tensor, timeout_s: float = 2.0) -> None:
+    """Stream-ordered bounded wait until the u32 at ``flag_addr`` reaches ``target``."""
+    _C.wait_flag(flag_addr, target & 0xFFFFFFFF, int(timeout_s * 1e9), status)
+
+
+def write_flag(flag_addr: int, value: int, like: torch.Tensor, add: bool = False) -> None:
+    _C.write_flag(flag_addr, value & 0xFFFFFFFF, add, like)
+
+
+ipc_export = _C.ipc_export
+ipc_open = _C.ipc_open
+ipc_close = _C.ipc_close
+enable_peer_access = _C.enable_peer_access
+from_ptr = _C.from_ptr
