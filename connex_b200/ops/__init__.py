@@ -30,6 +30,18 @@ EPI_SILU_MUL = _C.EPI_SILU_MUL
 GATE_UP_TILE = 256
 
 
+_LAUNCHES = [0]
+
+
+def launch_count() -> int:
+    """Number of this package's kernel launches issued so far by this process."""
+    return _LAUNCHES[0]
+
+
+def _n(k: int = 1) -> None:
+    _LAUNCHES[0] += k
+
+
 def new_status(device) -> torch.Tensor:
     """An int32 device status word (0 = ok) that kernels write error codes to."""
     return torch.zeros(1, dtype=torch.int32, device=device)
@@ -59,6 +71,7 @@ def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, *
         out = torch.empty(M, N // 2 if silu_mul else N, dtype=torch.bfloat16, device=a.device)
     epi = EPI_SILU_MUL if silu_mul else (EPI_ADD if residual is not None else EPI_STORE)
     _C.gemm(a, b, out, residual, epi, bn, status, max_ctas)
+    _n()
     return out
 
 
@@ -87,6 +100,7 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: Optional[tor
     if out is None:
         out = torch.empty_like(x)
     _C.rmsnorm(x, residual, weight, out, eps)
+    _n()
     return out
 
 
@@ -96,6 +110,7 @@ def rope_cache(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor
                status: Optional[torch.Tensor] = None) -> None:
     """Rotate q/k of the fused QKV rows in place; write k/v to their paged slots."""
     _C.rope_cache(qkv, positions, cos_sin, slot_mapping, k_cache, v_cache, n_q_heads, n_kv_heads, status)
+    _n()
 
 
 def rope_cos_sin(max_pos: int, head_dim: int, theta: float, device) -> torch.Tensor:
@@ -110,6 +125,7 @@ def embedding(ids: torch.Tensor, table: torch.Tensor, out: Optional[torch.Tensor
     if out is None:
         out = torch.empty(ids.numel(), table.shape[1], dtype=table.dtype, device=table.device)
     _C.embedding(ids, table, out, status)
+    _n()
     return out
 
 
@@ -117,6 +133,7 @@ def argmax(logits: torch.Tensor, out: Optional[torch.Tensor] = None) -> torch.Te
     if out is None:
         out = torch.empty(logits.shape[0], dtype=torch.int32, device=logits.device)
     _C.argmax(logits, out)
+    _n()
     return out
 
 
@@ -124,6 +141,7 @@ def gather_rows(src: torch.Tensor, idx: torch.Tensor, out: Optional[torch.Tensor
     if out is None:
         out = torch.empty(idx.numel(), src.shape[1], dtype=src.dtype, device=src.device)
     _C.gather_rows(src, idx, out)
+    _n()
     return out
 
 
@@ -149,6 +167,7 @@ def prefill_attention(qkv: torch.Tensor, tile_info: torch.Tensor, n_q_heads: int
         out = torch.empty(qkv.shape[0], n_q_heads * 128, dtype=qkv.dtype, device=qkv.device)
     _C.prefill_attention(qkv, out, tile_info, n_q_heads, n_kv_heads,
                          scale if scale is not None else 1.0 / math.sqrt(128))
+    _n()
     return out
 
 
@@ -165,6 +184,7 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
         out = torch.empty(q.shape[0], n_q_heads * 128, dtype=q.dtype, device=q.device)
     _C.decode_attention(q, k_cache, v_cache, block_tables, ctx_lens, out, n_q_heads, max_ctx,
                         scale if scale is not None else 1.0 / math.sqrt(128), workspace)
+    _n(1 if max_ctx <= 512 else 2)
     return out
 
 
@@ -176,6 +196,7 @@ def kv_push_layer(src_k: int, src_v: int, dst_k: int, dst_v: int, pairs: torch.T
     """Push one layer's paged KV blocks (pairs: int32 [n, 2] of src/dst block
     ids) from local caches to (peer-mapped) destination caches.  Returns the
     number of CTAs, each of which adds 1 to the u32 at ``ready`` when done."""
+    _n()
     return _C.kv_push_layer(src_k, src_v, dst_k, dst_v, pairs, src_heads, dst_heads, src_h0, dst_h0,
                             n_heads if n_heads is not None else src_heads, chunk_bytes, src_blocks,
                             dst_blocks, ready, max_ctas, status)
@@ -184,16 +205,19 @@ def kv_push_layer(src_k: int, src_v: int, dst_k: int, dst_v: int, pairs: torch.T
 def copy_segments(segs: torch.Tensor, total_bytes: int, ready: int = 0, max_ctas: int = 0,
                   status: Optional[torch.Tensor] = None) -> int:
     """Copy (src, dst, bytes) int64 segments (16-byte aligned) with SM loads/stores."""
+    _n()
     return _C.copy_segments(segs, total_bytes, ready, max_ctas, status)
 
 
 def wait_flag(flag_addr: int, target: int, status: torch.Tensor, timeout_s: float = 2.0) -> None:
     """Stream-ordered bounded wait until the u32 at ``flag_addr`` reaches ``target``."""
     _C.wait_flag(flag_addr, target & 0xFFFFFFFF, int(timeout_s * 1e9), status)
+    _n()
 
 
 def write_flag(flag_addr: int, value: int, like: torch.Tensor, add: bool = False) -> None:
     _C.write_flag(flag_addr, value & 0xFFFFFFFF, add, like)
+    _n()
 
 
 ipc_export = _C.ipc_export

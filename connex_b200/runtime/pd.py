@@ -1,0 +1,190 @@
+"""Prefill -> decode disaggregation on B200: layer-by-layer paged-KV push.
+
+The reference pulls a request's KV only after its whole prefill finished
+(``connex/adapters/vllm/pd_connector.py:420-428``: the per-layer hooks are
+no-ops; ``connex/pd/transfer.py:397-462`` issues one-sided reads).  Here the
+prefill instance pushes instead, one kernel per layer:
+
+* right after layer l's K/V land in the prefill cache (RoPE + cache-write
+  kernel), an event is recorded on the compute stream and the push stream
+  launches ``kv_push_layer`` for every (src block, dst block) pair of the
+  batch -- so the transfer of layer l overlaps the compute of layers l+1..;
+* the kernel stores straight into the decode instance's cache through its
+  NVLink peer mapping (CUDA IPC) -- no staging, no host involvement -- and
+  every CTA releases +1 on a u32 ready counter in the decode GPU's memory;
+* the decode stream acquire-waits (bounded, status word on timeout) for the
+  counter to reach the value the prefill side announced, then decodes.
+
+Hold / acquire / release leases of :mod:`connex.pd.transfer` stay on the
+host, so a decode instance that dies can still re-pull (the KV remains held
+on the prefill side until released).
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass
+from typing import List, Optional, Sequence
+
+import torch
+
+from connex_b200 import ops
+from connex_b200.models.llama import LlamaModel, PagedKVCache, slot_mapping
+
+
+@dataclass
+class KVDestination:
+    """Where a prefill instance writes KV: a decode cache (local or peer-mapped)."""
+
+    base: int              # address of cache[0, 0] (layer 0, K)
+    layer_stride: int      # bytes between layers
+    kv_stride: int         # bytes between K and V of a layer
+    heads: int             # KV heads per block in the destination cache
+    num_blocks: int
+    ready_addr: int        # u32 ready counter in the decode GPU's memory
+    head_offset: int = 0   # first destination head written by this source
+
+    @classmethod
+    def of_cache(cls, cache: PagedKVCache, ready: torch.Tensor, base: Optional[int] = None,
+                 ready_addr: Optional[int] = None) -> "KVDestination":
+        return cls(base=base if base is not None else cache.kv.data_ptr(),
+                   layer_stride=cache.layer_stride_bytes, kv_stride=cache.kv_stride_bytes,
+                   heads=cache.cfg.kv_heads, num_blocks=cache.num_blocks,
+                   ready_addr=ready_addr if ready_addr is not None else ready.data_ptr())
+
+    def k(self, layer: int) -> int:
+        return self.base + layer * self.layer_stride
+
+    def v(self, layer: int) -> int:
+        return self.base + layer * self.layer_stride + self.kv_stride
+
+
+class LayerwiseKVPusher:
+    """Launches one ``kv_push_layer`` per layer on a side stream, in step with
+    the prefill's per-layer hook; counts the CTAs the decode side must see."""
+
+    def __init__(self, src: PagedKVCache, max_ctas: int = 0, priority: int = -1):
+        self.src = src
+        # High priority: push CTAs take SM slots ahead of the queued prefill
+        # CTAs (they need no shared memory, so they co-reside with GEMM CTAs).
+        self.stream = torch.cuda.Stream(device=src.kv.device, priority=priority)
+        self.status = ops.new_status(src.kv.device)
+        self.max_ctas = max_ctas
+        self._pairs: Optional[torch.Tensor] = None
+        self._dst: Optional[KVDestination] = None
+        self.launched = 0
+        self.bytes = 0
+        self.timing = False
+        self._ev: List[tuple] = []
+
+    def begin(self, pairs: torch.Tensor, dst: KVDestination, n_heads: Optional[int] = None,
+              src_h0: int = 0, timing: bool = False) -> None:
+        self._pairs, self._dst = pairs, dst
+        self._nh = n_heads if n_heads is not None else self.src.cfg.kv_heads
+        self._sh0 = src_h0
+        self.launched = 0
+        self.bytes = 0
+        self.timing = timing
+        self._ev = []
+
+    def hook(self, layer: int) -> None:
+        """Called on the host right after layer ``layer``'s KV write was enqueued."""
+        cur = torch.cuda.current_stream(self.src.kv.device)
+        ev = torch.cuda.Event()
+        ev.record(cur)
+        self.stream.wait_event(ev)
+        d, c = self._dst, self.src
+        with torch.cuda.stream(self.stream):
+            if self.timing:
+                e0 = torch.cuda.Event(enable_timing=True)
+                e0.record(self.stream)
+            n = ops.kv_push_layer(c.k(layer).data_ptr(), c.v(layer).data_ptr(), d.k(layer), d.v(layer),
+                                  self._pairs, src_heads=c.cfg.kv_heads, dst_heads=d.heads,
+                                  src_h0=self._sh0, dst_h0=d.head_offset, n_heads=self._nh,
+                                  chunk_bytes=c.head_slice_bytes, src_blocks=c.num_blocks,
+                                  dst_blocks=d.num_blocks, ready=d.ready_addr, max_ctas=self.max_ctas,
+                                  status=self.status)
+            if self.timing:
+                e1 = torch.cuda.Event(enable_timing=True)
+                e1.record(self.stream)
+                self._ev.append((e0, e1))
+        self.launched += n
+        self.bytes += self._pairs.shape[0] * 2 * self._nh * c.head_slice_bytes
+
+    def push_ms(self) -> float:
+        """Summed device time of this batch's push kernels (needs timing=True, synced)."""
+        return sum(a.elapsed_time(b) for a, b in self._ev)
+
+    def span_events(self):
+        return (self._ev[0][0], self._ev[-1][1]) if self._ev else (None, None)
+
+    def join(self) -> None:
+        torch.cuda.current_stream(self.src.kv.device).wait_stream(self.stream)
+
+
+@dataclass
+class PrefillBatch:
+    """A packed prefill batch with its device-side metadata."""
+
+    seq_lens: List[int]
+    ids: torch.Tensor
+    positions: torch.Tensor
+    slots: torch.Tensor
+    last_rows: torch.Tensor
+    tile_info: torch.Tensor
+    src_blocks: List[List[int]]
+
+    @property
+    def tokens(self) -> int:
+        return sum(self.seq_lens)
+
+
+def build_prefill_batch(cache: PagedKVCache, prompts: Sequence[Sequence[int]], device,
+                        ids: Optional[torch.Tensor] = None) -> PrefillBatch:
+    """Allocate source blocks and build positions / slots / tile metadata.
+    ``ids`` may be given already on the device (e.g. copied from pinned memory)."""
+    bs = cache.cfg.block_size
+    seq_lens = [len(p) for p in prompts]
+    blocks, pos, slots, rows = [], [], [], []
+    r = 0
+    for n in seq_lens:
+        b = cache.allocate(cache.blocks_needed(n))
+        blocks.append(b)
+        pos.extend(range(n))
+        slots.extend(slot_mapping(b, 0, n, bs))
+        r += n
+        rows.append(r - 1)
+    if ids is None:
+        flat = [t for p in prompts for t in p]
+        ids = torch.tensor(flat, dtype=torch.int32).pin_memory().to(device, non_blocking=True)
+    return PrefillBatch(seq_lens=seq_lens, ids=ids,
+                        positions=torch.tensor(pos, dtype=torch.int32).pin_memory().to(device, non_blocking=True),
+                        slots=torch.tensor(slots, dtype=torch.int64).pin_memory().to(device, non_blocking=True),
+                        last_rows=torch.tensor(rows, dtype=torch.int32).pin_memory().to(device, non_blocking=True),
+                        tile_info=ops.prefill_tile_info(seq_lens, device), src_blocks=blocks)
+
+
+def block_pairs(src_blocks: Sequence[Sequence[int]], dst_blocks: Sequence[Sequence[int]], device) -> torch.Tensor:
+    flat = [(s, d) for sb, db in zip(src_blocks, dst_blocks) for s, d in zip(sb, db)]
+    return torch.tensor(flat, dtype=torch.int32).pin_memory().to(device, non_blocking=True)
+
+
+class DecodeBatch:
+    """Device metadata of one decode step for sequences whose KV is in `cache`."""
+
+    def __init__(self, cache: PagedKVCache, blocks: Sequence[Sequence[int]], ctx_lens: Sequence[int], device):
+        bs = cache.cfg.block_size
+        self.B = len(blocks)
+        maxb = max(len(b) for b in blocks)
+        self.block_tables = torch.tensor([list(b) + [0] * (maxb - len(b)) for b in blocks],
+                                         dtype=torch.int32).to(device, non_blocking=True)
+        # position of the new token = current context length (before append)
+        self.positions = torch.tensor(list(ctx_lens), dtype=torch.int32).to(device, non_blocking=True)
+        self.slots = torch.tensor([slot_mapping(b, n, 1, bs)[0] for b, n in zip(blocks, ctx_lens)],
+                                  dtype=torch.int64).to(device, non_blocking=True)
+        self.ctx_lens = (self.positions + 1)
+        self.max_ctx = max(ctx_lens) + 1
+        self.rows = torch.arange(self.B, dtype=torch.int32, device=device)
+
+
+def decode_step(model: LlamaModel, batch: DecodeBatch, ids: torch.Tensor, workspace: torch.Tensor) -> torch.Tensor:
+    return model.decode(ids, batch.positions, batch.slots, batch.block_tables, batch.ctx_lens, batch.max_ctx,
+                        workspace, batch.rows)

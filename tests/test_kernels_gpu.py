@@ -195,8 +195,7 @@ def test_copy_segments(dev):
     src = torch.arange(1 << 20, dtype=torch.int32, device=dev)
     dst = torch.zeros_like(src)
     segs = torch.tensor([[src.data_ptr() + 64, dst.data_ptr() + 4096, 65536],
-                         [src.data_ptr() + 1 << 20, dst.data_ptr(), 1 << 18]], dtype=torch.int64)
-    segs[1, 0] = src.data_ptr() + (1 << 20)
+                         [src.data_ptr() + (1 << 20), dst.data_ptr(), 1 << 18]], dtype=torch.int64)
     ops.copy_segments(segs.to(dev), 65536 + (1 << 18))
     torch.cuda.synchronize()
     d8, s8 = dst.view(torch.uint8), src.view(torch.uint8)
