@@ -195,12 +195,12 @@ def test_copy_segments(dev):
     src = torch.arange(1 << 20, dtype=torch.int32, device=dev)
     dst = torch.zeros_like(src)
     segs = torch.tensor([[src.data_ptr() + 64, dst.data_ptr() + 4096, 65536],
-                         [src.data_ptr() + (1 << 20), dst.data_ptr(), 1 << 18]], dtype=torch.int64)
+                         [src.data_ptr() + (1 << 20), dst.data_ptr() + (1 << 19), 1 << 18]], dtype=torch.int64)
     ops.copy_segments(segs.to(dev), 65536 + (1 << 18))
     torch.cuda.synchronize()
     d8, s8 = dst.view(torch.uint8), src.view(torch.uint8)
     assert torch.equal(d8[4096:4096 + 65536], s8[64:64 + 65536])
-    assert torch.equal(d8[:1 << 18], s8[1 << 20:(1 << 20) + (1 << 18)])
+    assert torch.equal(d8[1 << 19:(1 << 19) + (1 << 18)], s8[1 << 20:(1 << 20) + (1 << 18)])
 
 
 def test_wait_flag_times_out_with_status(dev):
