@@ -91,6 +91,7 @@ class Replica:
     def close_old(self) -> None:
         with self._lock:
             old, self._socks = self._socks[:-1], self._socks[-1:]
+        time.sleep(0.05)  # let the receive loop switch to the new socket set first
         for s in old:
             s.close(0)
 
@@ -117,7 +118,12 @@ class Replica:
                 for s in socks:
                     poller.register(s, zmq.POLLIN)
                 poller_socks = socks
-            for s, _ in poller.poll(20):
+            try:
+                ready = poller.poll(20)
+            except zmq.ZMQError:  # a socket was closed by close_old() meanwhile
+                poller_socks = []
+                continue
+            for s, _ in ready:
                 try:
                     msg = s.recv(zmq.NOBLOCK)
                 except zmq.ZMQError:

@@ -20,6 +20,11 @@ void gather_rows(const void* src, int lds, const int* idx, void* out, int ldo, i
 void prefill_attention(const void* qkv, int ldq, void* out, int ldo, const int* tile_info, int n_tiles, int Hq,
                        int Hkv, float scale, cudaStream_t s);
 
+// Same operation on the tcgen05 tensor cores with 128-query tiles (tile_info
+// built with 128-row tiles).  qkv_cols = (Hq+2Hkv)*128, T = rows of qkv.
+void prefill_attention_tc(const void* qkv, int ldq, int qkv_cols, int T, void* out, int ldo, const int* tile_info,
+                          int n_tiles, int Hq, int Hkv, float scale, int* status, cudaStream_t s);
+
 // Paged decode attention.  q: [B, *] rows (ld ldq, q heads first).
 // Caches [blocks, Hkv, BS, 128]; block_tables [B, max_blocks]; ctx_lens [B].
 // workspace: fp32, at least B*Hq*max_splits*(128+2) floats.

@@ -171,6 +171,33 @@ def prefill_attention(qkv: torch.Tensor, tile_info: torch.Tensor, n_q_heads: int
     return out
 
 
+PREFILL_TILE_TC = 128
+
+
+def prefill_tile_info_tc(seq_lens, device) -> torch.Tensor:
+    """Tile table of :func:`prefill_attention_tc` (128-query tiles)."""
+    rows = []
+    start = 0
+    for n in seq_lens:
+        for q0 in range(0, n, PREFILL_TILE_TC):
+            rows.append((start, n, q0))
+        start += n
+    t = torch.tensor(rows if rows else [(0, 0, 0)], dtype=torch.int32)
+    return t.pin_memory().to(device, non_blocking=True) if rows else t[:0].to(device)
+
+
+def prefill_attention_tc(qkv: torch.Tensor, tile_info: torch.Tensor, n_q_heads: int, n_kv_heads: int,
+                         out: Optional[torch.Tensor] = None, scale: Optional[float] = None,
+                         status: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Causal varlen prefill attention on tcgen05 (tile_info from :func:`prefill_tile_info_tc`)."""
+    if out is None:
+        out = torch.empty(qkv.shape[0], n_q_heads * 128, dtype=qkv.dtype, device=qkv.device)
+    _C.prefill_attention_tc(qkv, out, tile_info, n_q_heads, n_kv_heads,
+                            scale if scale is not None else 1.0 / math.sqrt(128), status)
+    _n()
+    return out
+
+
 def decode_workspace(batch: int, n_q_heads: int, max_ctx: int, device) -> torch.Tensor:
     return torch.empty(_C.decode_workspace_floats(batch, n_q_heads, max_ctx), dtype=torch.float32,
                        device=device)

@@ -129,6 +129,25 @@ def test_prefill_attention(dev, lens):
     _close(out.view(T, Hq, 128), R.causal_attention(q, k, v, lens))
 
 
+@pytest.mark.parametrize("lens", [[1], [128], [100, 37, 1], [513, 130, 7], [1100]])
+@pytest.mark.parametrize("G", [4, 1])
+def test_prefill_attention_tc(dev, lens, G):
+    from connex_b200 import ops
+    from connex_b200.ops import reference as R
+    Hkv = 2
+    Hq, T = Hkv * G, sum(lens)
+    qkv = _rnd(T, (Hq + 2 * Hkv) * 128, dev=dev, seed=31)
+    ti = ops.prefill_tile_info_tc(lens, dev)
+    st = ops.new_status(dev)
+    out = ops.prefill_attention_tc(qkv, ti, Hq, Hkv, status=st)
+    torch.cuda.synchronize()
+    ops.check_status(st, "prefill_attention_tc")
+    q = qkv[:, :Hq * 128].view(T, Hq, 128)
+    k = qkv[:, Hq * 128:(Hq + Hkv) * 128].view(T, Hkv, 128)
+    v = qkv[:, (Hq + Hkv) * 128:].view(T, Hkv, 128)
+    _close(out.view(T, Hq, 128), R.causal_attention(q, k, v, lens))
+
+
 @pytest.mark.parametrize("G", [4, 8])
 def test_decode_attention(dev, G):
     from connex_b200 import ops
