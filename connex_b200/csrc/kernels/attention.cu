@@ -1,245 +1,14 @@
-// Attention kernels of the serving runtime (head_dim 128, GQA).
+// Paged decode attention of the serving runtime (head_dim 128, GQA).
 //
-// prefill_attention: causal attention over a packed batch of prompts whose
-//   q/k/v rows sit in the fused QKV projection output.  Flash-attention
-//   structure: one CTA per (64-query tile, q head), 4 warps x 16 query rows,
-//   64-key tiles double-buffered in XOR-swizzled shared memory by cp.async,
-//   online softmax in fp32 (exp2 domain), bf16 tensor-core MMAs
-//   (mma.sync m16n8k16) for S = Q.K^T and O += P.V.
-//
-// decode_attention: one query token per sequence against its paged KV cache
-//   ([blocks, Hkv, 16, 128] per layer, i.e. one head of one block is 4 KB
-//   contiguous).  Split-K over the context (512 tokens per CTA), one CTA per
-//   (sequence, kv head, split) computing all q heads of the GQA group, then a
-//   log-sum-exp merge of the splits.
+// One query token per sequence against its paged KV cache ([blocks, Hkv, 16,
+// 128] per layer, i.e. one head of one block is 4 KB contiguous).  Split-K
+// over the context (512 tokens per CTA), one CTA per (sequence, kv head,
+// split) computing all q heads of the GQA group, then a log-sum-exp merge of
+// the splits.  (Prefill attention runs on tcgen05: attention_tc.cu.)
 #include "common.cuh"
 #include "layers.h"
 
 namespace cx {
-
-namespace fa {
-constexpr int D = 128;
-constexpr int BM = 64;
-constexpr int BN = 64;
-constexpr int THREADS = 128;
-constexpr int TILE_BYTES = BM * D * 2;  // 16 KB
-constexpr int SMEM = TILE_BYTES * 5;    // Q + 2x K + 2x V
-
-// byte offset of 16-byte chunk `c` of row `r` in a [rows][128] bf16 tile
-__device__ __forceinline__ uint32_t swz(int r, int c) { return (uint32_t)(r * 256 + ((c ^ (r & 7)) << 4)); }
-
-__device__ __forceinline__ void cp_async16(uint32_t dst, const void* src, bool valid) {
-  const int n = valid ? 16 : 0;
-  asm volatile("cp.async.cg.shared.global [%0], [%1], 16, %2;" ::"r"(dst), "l"(src), "r"(n) : "memory");
-}
-__device__ __forceinline__ void cp_async_commit() { asm volatile("cp.async.commit_group;" ::: "memory"); }
-template <int N>
-__device__ __forceinline__ void cp_async_wait() {
-  asm volatile("cp.async.wait_group %0;" ::"n"(N) : "memory");
-}
-__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
-  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0,%1,%2,%3}, [%4];"
-               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
-               : "r"(addr));
-}
-__device__ __forceinline__ void mma16816(float (&c)[4], const uint32_t (&a)[4], uint32_t b0, uint32_t b1) {
-  asm volatile(
-      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, {%4,%5,%6,%7}, {%8,%9}, "
-      "{%0,%1,%2,%3};"
-      : "+f"(c[0]), "+f"(c[1]), "+f"(c[2]), "+f"(c[3])
-      : "r"(a[0]), "r"(a[1]), "r"(a[2]), "r"(a[3]), "r"(b0), "r"(b1));
-}
-
-// Load `BM` rows x 128 dims starting at packed row `row0` (rows >= row_end are zero-filled).
-__device__ __forceinline__ void load_tile(uint32_t sbase, const __nv_bfloat16* base, int ld, int row0,
-                                          int row_end) {
-  for (int i = threadIdx.x; i < BM * 16; i += THREADS) {
-    const int r = i >> 4, c = i & 15;
-    const bool valid = row0 + r < row_end;
-    const __nv_bfloat16* src = base + (size_t)(valid ? row0 + r : row0) * ld + c * 8;
-    cp_async16(sbase + swz(r, c), src, valid);
-  }
-}
-}  // namespace fa
-
-__global__ void __launch_bounds__(fa::THREADS) prefill_attn_kernel(const __nv_bfloat16* __restrict__ qkv, int ldq,
-                                                                    __nv_bfloat16* __restrict__ out, int ldo,
-                                                                    const int* __restrict__ tile_info, int Hq,
-                                                                    int Hkv, float scale_log2) {
-  using namespace fa;
-  extern __shared__ __align__(128) uint8_t smem[];
-  const uint32_t sQ = smem_u32(smem);
-  const uint32_t sK0 = sQ + TILE_BYTES, sV0 = sQ + 3 * TILE_BYTES;
-
-  const int tile = blockIdx.x, h = blockIdx.y;
-  const int seq_start = tile_info[tile * 3 + 0];
-  const int seq_len = tile_info[tile * 3 + 1];
-  const int q0 = tile_info[tile * 3 + 2];
-  const int kvh = h / (Hq / Hkv);
-  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
-
-  const __nv_bfloat16* Qb = qkv + (size_t)h * D;
-  const __nv_bfloat16* Kb = qkv + (size_t)(Hq + kvh) * D;
-  const __nv_bfloat16* Vb = qkv + (size_t)(Hq + Hkv + kvh) * D;
-  const int end = seq_start + seq_len;
-  const int kv_len = min(seq_len, q0 + BM);
-  const int nkv = (kv_len + BN - 1) / BN;
-
-  load_tile(sQ, Qb, ldq, seq_start + q0, end);
-  cp_async_commit();
-  load_tile(sK0, Kb, ldq, seq_start, end);
-  load_tile(sV0, Vb, ldq, seq_start, end);
-  cp_async_commit();
-
-  uint32_t qf[8][4];
-  float o[16][4];
-#pragma unroll
-  for (int i = 0; i < 16; ++i) o[i][0] = o[i][1] = o[i][2] = o[i][3] = 0.f;
-  float m0 = -INFINITY, m1 = -INFINITY, l0 = 0.f, l1 = 0.f;
-  const int qr0 = q0 + warp * 16 + (lane >> 2);  // query position (within seq) of c0/c1
-  const int qr1 = qr0 + 8;                       // of c2/c3
-
-  for (int j = 0; j < nkv; ++j) {
-    const int buf = j & 1;
-    if (j + 1 < nkv) {
-      const int nb = (j + 1) & 1;
-      load_tile(sK0 + nb * TILE_BYTES, Kb, ldq, seq_start + (j + 1) * BN, end);
-      load_tile(sV0 + nb * TILE_BYTES, Vb, ldq, seq_start + (j + 1) * BN, end);
-      cp_async_commit();
-      cp_async_wait<1>();
-    } else {
-      cp_async_wait<0>();
-    }
-    __syncthreads();
-    if (j == 0) {
-#pragma unroll
-      for (int ks = 0; ks < 8; ++ks) {
-        const int r = warp * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-        const int c = ks * 2 + (lane >> 4);
-        ldsm_x4(sQ + swz(r, c), qf[ks][0], qf[ks][1], qf[ks][2], qf[ks][3]);
-      }
-    }
-    const uint32_t sK = sK0 + buf * TILE_BYTES, sV = sV0 + buf * TILE_BYTES;
-    float s[8][4];
-#pragma unroll
-    for (int i = 0; i < 8; ++i) s[i][0] = s[i][1] = s[i][2] = s[i][3] = 0.f;
-#pragma unroll
-    for (int ks = 0; ks < 8; ++ks) {
-#pragma unroll
-      for (int nb2 = 0; nb2 < 4; ++nb2) {
-        uint32_t k0, k1, k2, k3;
-        const int r = nb2 * 16 + (lane & 7) + (lane >> 4) * 8;
-        const int c = ks * 2 + ((lane >> 3) & 1);
-        ldsm_x4(sK + swz(r, c), k0, k1, k2, k3);
-        mma16816(s[nb2 * 2], qf[ks], k0, k1);
-        mma16816(s[nb2 * 2 + 1], qf[ks], k2, k3);
-      }
-    }
-    // scale + causal / length mask, row maxima
-    float mx0 = m0, mx1 = m1;
-    const bool need_mask = (j * BN + BN - 1 > q0 + warp * 16) || ((j + 1) * BN > seq_len);
-#pragma unroll
-    for (int nb = 0; nb < 8; ++nb) {
-#pragma unroll
-      for (int e = 0; e < 4; ++e) {
-        float v = s[nb][e] * scale_log2;
-        if (need_mask) {
-          const int key = j * BN + nb * 8 + 2 * (lane & 3) + (e & 1);
-          const int qr = (e < 2) ? qr0 : qr1;
-          if (key > qr || key >= seq_len) v = -INFINITY;
-        }
-        s[nb][e] = v;
-      }
-      mx0 = fmaxf(mx0, fmaxf(s[nb][0], s[nb][1]));
-      mx1 = fmaxf(mx1, fmaxf(s[nb][2], s[nb][3]));
-    }
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 1));
-    mx0 = fmaxf(mx0, __shfl_xor_sync(0xffffffffu, mx0, 2));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 1));
-    mx1 = fmaxf(mx1, __shfl_xor_sync(0xffffffffu, mx1, 2));
-    const float c0 = (mx0 == -INFINITY) ? 1.f : exp2f(m0 - mx0);
-    const float c1 = (mx1 == -INFINITY) ? 1.f : exp2f(m1 - mx1);
-    const float b0 = (mx0 == -INFINITY) ? 0.f : mx0;
-    const float b1 = (mx1 == -INFINITY) ? 0.f : mx1;
-    m0 = mx0;
-    m1 = mx1;
-    float ps0 = 0.f, ps1 = 0.f;
-#pragma unroll
-    for (int nb = 0; nb < 8; ++nb) {
-      s[nb][0] = exp2f(s[nb][0] - b0);
-      s[nb][1] = exp2f(s[nb][1] - b0);
-      s[nb][2] = exp2f(s[nb][2] - b1);
-      s[nb][3] = exp2f(s[nb][3] - b1);
-      ps0 += s[nb][0] + s[nb][1];
-      ps1 += s[nb][2] + s[nb][3];
-    }
-    l0 = l0 * c0 + ps0;
-    l1 = l1 * c1 + ps1;
-#pragma unroll
-    for (int i = 0; i < 16; ++i) {
-      o[i][0] *= c0;
-      o[i][1] *= c0;
-      o[i][2] *= c1;
-      o[i][3] *= c1;
-    }
-#pragma unroll
-    for (int kk = 0; kk < 4; ++kk) {
-      uint32_t pa[4];
-      pa[0] = pack_bf16x2(s[2 * kk][0], s[2 * kk][1]);
-      pa[1] = pack_bf16x2(s[2 * kk][2], s[2 * kk][3]);
-      pa[2] = pack_bf16x2(s[2 * kk + 1][0], s[2 * kk + 1][1]);
-      pa[3] = pack_bf16x2(s[2 * kk + 1][2], s[2 * kk + 1][3]);
-#pragma unroll
-      for (int db2 = 0; db2 < 8; ++db2) {
-        uint32_t v0, v1, v2, v3;
-        const int r = kk * 16 + (lane & 7) + ((lane >> 3) & 1) * 8;
-        const int c = db2 * 2 + (lane >> 4);
-        ldsm_x4_t(sV + swz(r, c), v0, v1, v2, v3);
-        mma16816(o[db2 * 2], pa, v0, v1);
-        mma16816(o[db2 * 2 + 1], pa, v2, v3);
-      }
-    }
-    __syncthreads();
-  }
-  l0 += __shfl_xor_sync(0xffffffffu, l0, 1);
-  l0 += __shfl_xor_sync(0xffffffffu, l0, 2);
-  l1 += __shfl_xor_sync(0xffffffffu, l1, 1);
-  l1 += __shfl_xor_sync(0xffffffffu, l1, 2);
-  const float i0 = l0 > 0.f ? 1.f / l0 : 0.f;
-  const float i1 = l1 > 0.f ? 1.f / l1 : 0.f;
-  __nv_bfloat16* ob = out + (size_t)h * D;
-#pragma unroll
-  for (int db = 0; db < 16; ++db) {
-    const int col = db * 8 + 2 * (lane & 3);
-    if (qr0 < seq_len)
-      *reinterpret_cast<uint32_t*>(ob + (size_t)(seq_start + qr0) * ldo + col) =
-          pack_bf16x2(o[db][0] * i0, o[db][1] * i0);
-    if (qr1 < seq_len)
-      *reinterpret_cast<uint32_t*>(ob + (size_t)(seq_start + qr1) * ldo + col) =
-          pack_bf16x2(o[db][2] * i1, o[db][3] * i1);
-  }
-}
-
-void prefill_attention(const void* qkv, int ldq, void* out, int ldo, const int* tile_info, int n_tiles, int Hq,
-                       int Hkv, float scale, cudaStream_t s) {
-  if (n_tiles == 0) return;
-  static bool attr[64] = {false};
-  int dev;
-  cudaGetDevice(&dev);
-  if (!attr[dev & 63]) {
-    cudaFuncSetAttribute(prefill_attn_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fa::SMEM);
-    attr[dev & 63] = true;
-  }
-  dim3 grid(n_tiles, Hq);
-  prefill_attn_kernel<<<grid, fa::THREADS, fa::SMEM, s>>>(reinterpret_cast<const __nv_bfloat16*>(qkv), ldq,
-                                                           reinterpret_cast<__nv_bfloat16*>(out), ldo, tile_info, Hq,
-                                                           Hkv, scale * 1.4426950408889634f);
-}
 
 // ------------------------------------------------------- paged decode
 namespace dec {

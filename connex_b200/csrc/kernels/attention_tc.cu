@@ -1,19 +1,22 @@
 // Causal varlen prefill attention on the sm_100a tensor cores (tcgen05 + TMA + TMEM).
 //
-// One CTA per (128-query tile, q head); 6 warps:
-//   warp 0    : TMA producer.  Q once (2 boxes of [128 rows x 64 dims]), then
-//               K and V of each 128-key tile into a 2-stage ring, straight from
-//               the fused QKV buffer (one 2-D tensor map covers q, k and v).
-//   warp 1    : allocates 512 TMEM columns (S0 | S1 | O) and one thread issues
-//               the MMAs: S_j = Q.K_j^T (M=128, N=128, K=128; both K-major)
-//               into S[j%2], then O += P_{j-1}.V_{j-1} (A = P from shared
-//               memory, B = V MN-major), so Q.K of the next tile overlaps the
-//               softmax of the current one.
-//   warps 2-5 : softmax, one thread per query row (TMEM lane): two passes over
-//               the S row (max, then exp2 + sum + bf16 P written into the
-//               128-byte-swizzled K-major layout the MMA reads), lazy
-//               rescaling of O in TMEM only when the running max grew by more
-//               than 2^8, and the final normalisation + store.
+// One CTA per (128-query tile, q head); two CTAs per SM (112 KB shared
+// memory and 256 TMEM columns each), so one CTA's softmax overlaps the other
+// CTA's MMAs.  6 warps per CTA:
+//   warp 0    : TMA producer.  Q once ([128 rows x 128 dims] as two 64-dim
+//               boxes), then K and V of each 64-key tile into a 2-stage ring,
+//               straight from the fused QKV buffer.
+//   warp 1    : allocates TMEM (S0 | S1 | O = 64 + 64 + 128 columns); one
+//               thread issues S_j = Q.K_j^T (M=128, N=64, K=128, both
+//               K-major) into S[j%2] and O += P_{j-1}.V_{j-1} (A = P from
+//               shared memory, B = V MN-major, N=128, K=64), so Q.K of the
+//               next tile overlaps the current softmax.
+//   warps 2-5 : softmax, one thread per query row (its TMEM lane): the 64
+//               scores of the row are loaded once into registers, masked,
+//               exponentiated (ex2.approx) and packed to bf16 before waiting
+//               for the previous P.V; O in TMEM is rescaled lazily (only
+//               when the running max grew by more than 2^8); P is written
+//               into the 128-byte-swizzled K-major layout the MMA reads.
 // All waits are bounded (status word on timeout); no cluster multicast.
 #include "common.cuh"
 #include "gemm.h"
@@ -24,21 +27,29 @@ namespace cx {
 namespace fatc {
 constexpr int D = 128;
 constexpr int BM = 128;
-constexpr int BN = 128;
+constexpr int BN = 64;
 constexpr int THREADS = 192;
-constexpr int HALF_BYTES = 128 * 64 * 2;     // one [128 x 64] bf16 swizzled box: 16 KB
-constexpr int TILE_BYTES = 2 * HALF_BYTES;   // [128 x 128]: 32 KB
+constexpr int Q_HALF = 128 * 64 * 2;   // [128 rows x 64 dims]: 16 KB
+constexpr int KV_HALF = 64 * 64 * 2;   // [64 rows x 64 dims]: 8 KB
+constexpr int KV_TILE = 2 * KV_HALF;   // [64 keys x 128 dims]: 16 KB
 constexpr int OFF_Q = 0;
-constexpr int OFF_K = OFF_Q + TILE_BYTES;        // 2 stages
-constexpr int OFF_V = OFF_K + 2 * TILE_BYTES;    // 2 stages
-constexpr int OFF_P = OFF_V + 2 * TILE_BYTES;
-constexpr int OFF_BAR = OFF_P + TILE_BYTES;
-constexpr int SMEM = 1024 + OFF_BAR + 256;
+constexpr int OFF_K = OFF_Q + 2 * Q_HALF;     // 2 stages
+constexpr int OFF_V = OFF_K + 2 * KV_TILE;    // 2 stages
+constexpr int OFF_P = OFF_V + 2 * KV_TILE;    // [128 q x 64 keys]: 16 KB
+constexpr int OFF_BAR = OFF_P + 128 * 64 * 2;
+constexpr int SMEM = OFF_BAR + 256;
+constexpr int TMEM_COLS = 256;
 constexpr float RESCALE_THRESHOLD = 8.0f;  // log2 units
 
-// MN-major, 128-byte-swizzled operand (V as the B operand of P.V): 64 contiguous
-// elements per 128-byte row, rows = K index; 8-row groups 1024 B apart (SBO),
-// 64-element MN blocks `lbo` bytes apart (LBO).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
+// MN-major, 128-byte-swizzled operand (V as the B operand of P.V): 64
+// contiguous elements per 128-byte row (rows = K index), 8-row groups 1024 B
+// apart (SBO), 64-element MN blocks `lbo` bytes apart (LBO).
 __device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t smem_addr, uint32_t lbo) {
   uint64_t d = 0;
   d |= (uint64_t)((smem_addr >> 4) & 0x3FFFu);
@@ -50,13 +61,16 @@ __device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t smem_addr, uint3
 }
 }  // namespace fatc
 
-__global__ void __launch_bounds__(fatc::THREADS, 1)
-    prefill_attn_tc_kernel(const __grid_constant__ CUtensorMap tm, __nv_bfloat16* __restrict__ out, int ldo,
-                           const int* __restrict__ tile_info, int n_tiles, int Hq, int Hkv, float scale_log2,
-                           int* status) {
+__global__ void __launch_bounds__(fatc::THREADS, 2)
+    prefill_attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmkv,
+                           __nv_bfloat16* __restrict__ out, int ldo, const int* __restrict__ tile_info, int n_tiles,
+                           int Hq, int Hkv, float scale_log2, int* status) {
   using namespace fatc;
-  extern __shared__ uint8_t smem_raw[];
-  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  extern __shared__ __align__(1024) uint8_t smem[];
+  if ((smem_u32(smem) & 1023u) != 0) {  // swizzled operands need a 1 KB-aligned base
+    if (threadIdx.x == 0) record_status(status, CX_ERR_BOUNDS);
+    return;
+  }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
   uint64_t* q_full = bars + 0;
   uint64_t* kv_full = bars + 1;   // [2]
@@ -68,8 +82,7 @@ __global__ void __launch_bounds__(fatc::THREADS, 1)
   uint64_t* drain = bars + 11;
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
 
-  // heaviest (latest) query tiles first
-  const int tile = n_tiles - 1 - (int)blockIdx.x;
+  const int tile = n_tiles - 1 - (int)blockIdx.x;  // heaviest (latest) tiles first
   const int h = blockIdx.y;
   const int seq_start = tile_info[tile * 3 + 0];
   const int seq_len = tile_info[tile * 3 + 1];
@@ -92,36 +105,36 @@ __global__ void __launch_bounds__(fatc::THREADS, 1)
     mbar_init(pv_done, 1);
     mbar_init(drain, 1);
     fence_barrier_init();
-    prefetch_tmap(&tm);
+    prefetch_tmap(&tmq);
+    prefetch_tmap(&tmkv);
   }
   if (warp == 1) {
-    tmem_alloc(tmem_slot, 512);
+    tmem_alloc(tmem_slot, TMEM_COLS);
     tmem_relinquish();
     tc_fence_before();
   }
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
-  const uint32_t tS[2] = {tmem, tmem + 128};
-  const uint32_t tO = tmem + 256;
+  const uint32_t tS0 = tmem, tS1 = tmem + BN, tO = tmem + 2 * BN;
 
   if (warp == 0) {
     if (lane == 0) {
       const int row0 = seq_start + q0;
-      mbar_arrive_expect_tx(q_full, TILE_BYTES);
-      tma_load_2d(smem + OFF_Q, &tm, q_full, qcol, row0);
-      tma_load_2d(smem + OFF_Q + HALF_BYTES, &tm, q_full, qcol + 64, row0);
+      mbar_arrive_expect_tx(q_full, 2 * Q_HALF);
+      tma_load_2d(smem + OFF_Q, &tmq, q_full, qcol, row0);
+      tma_load_2d(smem + OFF_Q + Q_HALF, &tmq, q_full, qcol + 64, row0);
       for (int j = 0; j < nkv; ++j) {
         const int s = j & 1;
         if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, status)) break;
         const int r = seq_start + j * BN;
-        mbar_arrive_expect_tx(&kv_full[s], 2 * TILE_BYTES);
-        uint8_t* kb = smem + OFF_K + s * TILE_BYTES;
-        uint8_t* vb = smem + OFF_V + s * TILE_BYTES;
-        tma_load_2d(kb, &tm, &kv_full[s], kcol, r);
-        tma_load_2d(kb + HALF_BYTES, &tm, &kv_full[s], kcol + 64, r);
-        tma_load_2d(vb, &tm, &kv_full[s], vcol, r);
-        tma_load_2d(vb + HALF_BYTES, &tm, &kv_full[s], vcol + 64, r);
+        mbar_arrive_expect_tx(&kv_full[s], 2 * KV_TILE);
+        uint8_t* kb = smem + OFF_K + s * KV_TILE;
+        uint8_t* vb = smem + OFF_V + s * KV_TILE;
+        tma_load_2d(kb, &tmkv, &kv_full[s], kcol, r);
+        tma_load_2d(kb + KV_HALF, &tmkv, &kv_full[s], kcol + 64, r);
+        tma_load_2d(vb, &tmkv, &kv_full[s], vcol, r);
+        tma_load_2d(vb + KV_HALF, &tmkv, &kv_full[s], vcol + 64, r);
       }
     }
     __syncwarp();
@@ -135,12 +148,11 @@ __global__ void __launch_bounds__(fatc::THREADS, 1)
       auto issue_pv = [&](int jj) -> bool {
         if (!mbar_wait(p_full, jj & 1, status)) return false;
         tc_fence_after();
-        const uint32_t sV = smem_u32(smem + OFF_V + (jj & 1) * TILE_BYTES);
+        const uint32_t sV = smem_u32(smem + OFF_V + (jj & 1) * KV_TILE);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
-          const uint64_t a = umma_desc_sw128(sP + (kk >> 2) * HALF_BYTES + (kk & 3) * 32);
-          const uint64_t b = umma_desc_sw128_mn(sV + kk * 2048, HALF_BYTES);
-          umma_bf16(tO, a, b, IDESC_PV, (jj > 0 || kk > 0) ? 1u : 0u);
+          umma_bf16(tO, umma_desc_sw128(sP + kk * 32), umma_desc_sw128_mn(sV + kk * 2048, KV_HALF), IDESC_PV,
+                    (jj > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(pv_done);
         umma_commit(&kv_empty[jj & 1]);
@@ -151,11 +163,11 @@ __global__ void __launch_bounds__(fatc::THREADS, 1)
         if (!mbar_wait(&kv_full[s], (j >> 1) & 1, status)) { ok = false; break; }
         if (!mbar_wait(&s_free[s], ((j >> 1) & 1) ^ 1, status)) { ok = false; break; }
         tc_fence_after();
-        const uint32_t sK = smem_u32(smem + OFF_K + s * TILE_BYTES);
+        const uint32_t sK = smem_u32(smem + OFF_K + s * KV_TILE);
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
-          const uint32_t off = (k >> 2) * HALF_BYTES + (k & 3) * 32;
-          umma_bf16(tS[s], umma_desc_sw128(sQ + off), umma_desc_sw128(sK + off), IDESC_QK, k > 0 ? 1u : 0u);
+          umma_bf16(s ? tS1 : tS0, umma_desc_sw128(sQ + (k >> 2) * Q_HALF + (k & 3) * 32),
+                    umma_desc_sw128(sK + (k >> 2) * KV_HALF + (k & 3) * 32), IDESC_QK, k > 0 ? 1u : 0u);
         }
         issued = true;
         umma_commit(&s_full[s]);
@@ -169,10 +181,9 @@ __global__ void __launch_bounds__(fatc::THREADS, 1)
     }
     __syncwarp();
   } else {
-    // softmax / correction / epilogue: thread <-> query row (TMEM lane)
     const int q = warp & 3;
-    const int row = q * 32 + lane;          // row within the tile
-    const int qpos = q0 + row;              // query position within its sequence
+    const int row = q * 32 + lane;
+    const int qpos = q0 + row;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     uint8_t* prow = smem + OFF_P + row * 128;
     const uint32_t swz = (uint32_t)(row & 7);
@@ -182,79 +193,67 @@ __global__ void __launch_bounds__(fatc::THREADS, 1)
       const int s = j & 1;
       if (!mbar_wait(&s_full[s], (j >> 1) & 1, status)) { ok = false; break; }
       tc_fence_after();
+      uint32_t r[64];
+      {
+        uint32_t (&r0)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[0]);
+        uint32_t (&r1)[32] = *reinterpret_cast<uint32_t(*)[32]>(&r[32]);
+        const uint32_t ts = (s ? tS1 : tS0) + lane_off;
+        tmem_ld32(ts, r0);
+        tmem_ld32(ts + 32, r1);
+        tmem_ld_wait();
+      }
+      tc_fence_before();
+      mbar_arrive(&s_free[s]);  // S[s] is in registers now
       const int key0 = j * BN;
       const bool mask = (key0 + BN - 1 > q0) || (key0 + BN > seq_len);
-      // pass 1: row max
       float mx = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tS[s] + lane_off + c * 32, r);
-        tmem_ld_wait();
 #pragma unroll
-        for (int e = 0; e < 32; ++e) {
-          const int key = key0 + c * 32 + e;
-          float v = __uint_as_float(r[e]);
-          if (mask && (key > qpos || key >= seq_len)) v = -INFINITY;
-          mx = fmaxf(mx, v);
-        }
+      for (int e = 0; e < BN; ++e) {
+        float v = __uint_as_float(r[e]) * scale_log2;
+        if (mask && (key0 + e > qpos || key0 + e >= seq_len)) v = -INFINITY;
+        r[e] = __float_as_uint(v);
+        mx = fmaxf(mx, v);
       }
-      mx *= scale_log2;
-      // lazy rescale: keep the stale max unless it grew by more than 2^8
       float m_new = m;
       bool resc = false;
-      if (j == 0 || mx > m + RESCALE_THRESHOLD) {
+      if (j == 0 || mx > m + RESCALE_THRESHOLD) {  // lazy rescale
         m_new = fmaxf(m, mx);
         resc = (j > 0);
       }
       const float base = (m_new == -INFINITY) ? 0.f : m_new;
-      // pass 2: P = exp2(s*scale - m), row sum, bf16 P into swizzled smem
+      float sum = 0.f;
+      uint32_t pk[BN / 2];
+#pragma unroll
+      for (int e = 0; e < BN; e += 2) {
+        const float p0 = fast_exp2(__uint_as_float(r[e]) - base);
+        const float p1 = fast_exp2(__uint_as_float(r[e + 1]) - base);
+        sum += p0 + p1;
+        pk[e >> 1] = pack_bf16x2(p0, p1);
+      }
+      const float alpha = resc ? fast_exp2(m - m_new) : 1.f;
+      l = l * alpha + sum;
+      m = m_new;
       if (j >= 1) {
         // P smem and O are free once P_{j-1}.V_{j-1} has completed
         if (!mbar_wait(pv_done, (j - 1) & 1, status)) { ok = false; break; }
         tc_fence_after();
-      }
-      float sum = 0.f;
+        if (__any_sync(0xffffffffu, resc)) {
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tS[s] + lane_off + c * 32, r);
-        tmem_ld_wait();
-        uint32_t pk[16];
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + lane_off + c * 32, o);
+            tmem_ld_wait();
 #pragma unroll
-        for (int e = 0; e < 32; e += 2) {
-          const int key = key0 + c * 32 + e;
-          float v0 = __uint_as_float(r[e]) * scale_log2 - base;
-          float v1 = __uint_as_float(r[e + 1]) * scale_log2 - base;
-          float p0 = (mask && (key > qpos || key >= seq_len)) ? 0.f : exp2f(v0);
-          float p1 = (mask && (key + 1 > qpos || key + 1 >= seq_len)) ? 0.f : exp2f(v1);
-          sum += p0 + p1;
-          pk[e >> 1] = pack_bf16x2(p0, p1);
-        }
-        // 32 keys = 4 chunks of 16 B; chunk index within the 64-key block
-#pragma unroll
-        for (int v = 0; v < 4; ++v) {
-          const int chunk = c * 4 + v;  // 0..15 over 128 keys
-          uint8_t* dst = prow + (chunk >> 3) * HALF_BYTES + ((((uint32_t)chunk & 7u) ^ swz) << 4);
-          *reinterpret_cast<uint4*>(dst) = make_uint4(pk[4 * v], pk[4 * v + 1], pk[4 * v + 2], pk[4 * v + 3]);
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st32(tO + lane_off + c * 32, o);
+          }
+          tmem_st_wait();
         }
       }
-      tc_fence_before();
-      mbar_arrive(&s_free[s]);  // S[s] fully read
-      const float alpha = resc ? exp2f(m - m_new) : 1.f;
-      l = l * alpha + sum;
-      m = m_new;
-      if (__any_sync(0xffffffffu, resc)) {
-#pragma unroll 1
-        for (int c = 0; c < D / 32; ++c) {
-          uint32_t r[32];
-          tmem_ld32(tO + lane_off + c * 32, r);
-          tmem_ld_wait();
 #pragma unroll
-          for (int e = 0; e < 32; ++e) r[e] = __float_as_uint(__uint_as_float(r[e]) * alpha);
-          tmem_st32(tO + lane_off + c * 32, r);
-        }
-        tmem_st_wait();
+      for (int c = 0; c < 8; ++c) {
+        uint8_t* dst = prow + ((((uint32_t)c) ^ swz) << 4);
+        *reinterpret_cast<uint4*>(dst) = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
       }
       fence_proxy_async_smem();  // P stores -> visible to the tensor core
       tc_fence_before();
@@ -267,18 +266,18 @@ __global__ void __launch_bounds__(fatc::THREADS, 1)
       __nv_bfloat16* orow = out + (size_t)(seq_start + qpos) * ldo + (size_t)h * D;
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
-        uint32_t r[32];
-        tmem_ld32(tO + lane_off + c * 32, r);
+        uint32_t o[32];
+        tmem_ld32(tO + lane_off + c * 32, o);
         tmem_ld_wait();
         if (valid) {
 #pragma unroll
           for (int v = 0; v < 4; ++v) {
-            u128 o;
-            o.x = pack_bf16x2(__uint_as_float(r[8 * v + 0]) * inv, __uint_as_float(r[8 * v + 1]) * inv);
-            o.y = pack_bf16x2(__uint_as_float(r[8 * v + 2]) * inv, __uint_as_float(r[8 * v + 3]) * inv);
-            o.z = pack_bf16x2(__uint_as_float(r[8 * v + 4]) * inv, __uint_as_float(r[8 * v + 5]) * inv);
-            o.w = pack_bf16x2(__uint_as_float(r[8 * v + 6]) * inv, __uint_as_float(r[8 * v + 7]) * inv);
-            st_v4(orow + c * 32 + v * 8, o);
+            u128 w;
+            w.x = pack_bf16x2(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
+            w.y = pack_bf16x2(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
+            w.z = pack_bf16x2(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
+            w.w = pack_bf16x2(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
+            st_v4(orow + c * 32 + v * 8, w);
           }
         }
       }
@@ -287,7 +286,7 @@ __global__ void __launch_bounds__(fatc::THREADS, 1)
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 512);
+    tmem_dealloc(tmem, TMEM_COLS);
   }
 }
 
@@ -301,10 +300,11 @@ void prefill_attention_tc(const void* qkv, int ldq, int qkv_cols, int T, void* o
     cudaFuncSetAttribute(prefill_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fatc::SMEM);
     attr[dev & 63] = true;
   }
-  const CUtensorMap tm = make_tmap_bf16_2d(qkv, (uint64_t)qkv_cols, (uint64_t)T, (uint64_t)ldq * 2, 64, 128, true);
+  const CUtensorMap tq = make_tmap_bf16_2d(qkv, (uint64_t)qkv_cols, (uint64_t)T, (uint64_t)ldq * 2, 64, 128, true);
+  const CUtensorMap tkv = make_tmap_bf16_2d(qkv, (uint64_t)qkv_cols, (uint64_t)T, (uint64_t)ldq * 2, 64, 64, true);
   dim3 grid(n_tiles, Hq);
-  prefill_attn_tc_kernel<<<grid, fatc::THREADS, fatc::SMEM, s>>>(tm, reinterpret_cast<__nv_bfloat16*>(out), ldo,
-                                                                  tile_info, n_tiles, Hq, Hkv,
+  prefill_attn_tc_kernel<<<grid, fatc::THREADS, fatc::SMEM, s>>>(tq, tkv, reinterpret_cast<__nv_bfloat16*>(out),
+                                                                  ldo, tile_info, n_tiles, Hq, Hkv,
                                                                   scale * 1.4426950408889634f, status);
 }
 

@@ -127,17 +127,6 @@ void gather_rows(const at::Tensor& src, const at::Tensor& idx, at::Tensor& out) 
                   (int)src.size(1), cur_stream(src));
 }
 
-void prefill_attention(const at::Tensor& qkv, at::Tensor& out, const at::Tensor& tile_info, int64_t Hq, int64_t Hkv,
-                       double scale) {
-  CHECK_BF16(qkv);
-  CHECK_BF16(out);
-  TORCH_CHECK(tile_info.scalar_type() == at::kInt && tile_info.dim() == 2 && tile_info.size(1) == 3,
-              "tile_info must be int32 [n, 3]");
-  const c10::cuda::CUDAGuard g(qkv.device());
-  cx::prefill_attention(qkv.data_ptr(), row_ld(qkv), out.data_ptr(), row_ld(out), tile_info.data_ptr<int>(),
-                        (int)tile_info.size(0), (int)Hq, (int)Hkv, (float)scale, cur_stream(qkv));
-}
-
 void prefill_attention_tc(const at::Tensor& qkv, at::Tensor& out, const at::Tensor& tile_info, int64_t Hq,
                           int64_t Hkv, double scale, const c10::optional<at::Tensor>& status) {
   CHECK_BF16(qkv);
@@ -275,8 +264,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding", &embedding);
   m.def("argmax", &argmax);
   m.def("gather_rows", &gather_rows);
-  m.def("prefill_attention", &prefill_attention);
-  m.def("prefill_attention_tc", &prefill_attention_tc);
+  m.def("prefill_attention", &prefill_attention_tc);
   m.def("decode_attention", &decode_attention);
   m.def("decode_workspace_floats", &decode_workspace_floats);
   m.def("kv_push_layer", &kv_push_layer);

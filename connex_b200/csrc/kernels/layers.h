@@ -14,14 +14,10 @@ void embedding(const int* ids, const void* table, void* out, int T, int H, int V
 void argmax(const void* logits, int ldl, int B, int V, int* out, cudaStream_t s);
 void gather_rows(const void* src, int lds, const int* idx, void* out, int ldo, int n, int H, cudaStream_t s);
 
-// Causal varlen prefill attention (GQA, head_dim 128).  q/k/v rows live in the
-// fused QKV buffer [T, (Hq+2Hkv)*128]; tile_info: [n_tiles, 3] int32 of
-// (seq start row, seq length, first query row of the tile within the seq).
-void prefill_attention(const void* qkv, int ldq, void* out, int ldo, const int* tile_info, int n_tiles, int Hq,
-                       int Hkv, float scale, cudaStream_t s);
-
-// Same operation on the tcgen05 tensor cores with 128-query tiles (tile_info
-// built with 128-row tiles).  qkv_cols = (Hq+2Hkv)*128, T = rows of qkv.
+// Causal varlen prefill attention (GQA, head_dim 128) on the tcgen05 tensor
+// cores.  q/k/v rows live in the fused QKV buffer [T, (Hq+2Hkv)*128];
+// tile_info: [n_tiles, 3] int32 of (seq start row, seq length, first query of
+// the 128-row tile).  qkv_cols = (Hq+2Hkv)*128, T = rows of qkv.
 void prefill_attention_tc(const void* qkv, int ldq, int qkv_cols, int T, void* out, int ldo, const int* tile_info,
                           int n_tiles, int Hq, int Hkv, float scale, int* status, cudaStream_t s);
 

@@ -146,11 +146,11 @@ def gather_rows(src: torch.Tensor, idx: torch.Tensor, out: Optional[torch.Tensor
 
 
 # ---------------------------------------------------------- attention
-PREFILL_TILE = 64
+PREFILL_TILE = 128
 
 
 def prefill_tile_info(seq_lens, device) -> torch.Tensor:
-    """[n_tiles, 3] int32 (seq start row, seq length, first query of tile)."""
+    """[n_tiles, 3] int32 (seq start row, seq length, first query of the 128-row tile)."""
     rows = []
     start = 0
     for n in seq_lens:
@@ -158,42 +158,20 @@ def prefill_tile_info(seq_lens, device) -> torch.Tensor:
             rows.append((start, n, q0))
         start += n
     t = torch.tensor(rows if rows else [(0, 0, 0)], dtype=torch.int32)
-    return t.to(device, non_blocking=True) if rows else t[:0].to(device)
+    if not rows:
+        return t[:0].to(device)
+    return t.pin_memory().to(device, non_blocking=True) if torch.cuda.is_available() else t.to(device)
 
 
 def prefill_attention(qkv: torch.Tensor, tile_info: torch.Tensor, n_q_heads: int, n_kv_heads: int,
-                      out: Optional[torch.Tensor] = None, scale: Optional[float] = None) -> torch.Tensor:
+                      out: Optional[torch.Tensor] = None, scale: Optional[float] = None,
+                      status: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Causal varlen prefill attention on the tcgen05 tensor cores.  ``qkv``
+    is the fused [T, (Hq + 2 Hkv) * 128] projection output."""
     if out is None:
         out = torch.empty(qkv.shape[0], n_q_heads * 128, dtype=qkv.dtype, device=qkv.device)
     _C.prefill_attention(qkv, out, tile_info, n_q_heads, n_kv_heads,
-                         scale if scale is not None else 1.0 / math.sqrt(128))
-    _n()
-    return out
-
-
-PREFILL_TILE_TC = 128
-
-
-def prefill_tile_info_tc(seq_lens, device) -> torch.Tensor:
-    """Tile table of :func:`prefill_attention_tc` (128-query tiles)."""
-    rows = []
-    start = 0
-    for n in seq_lens:
-        for q0 in range(0, n, PREFILL_TILE_TC):
-            rows.append((start, n, q0))
-        start += n
-    t = torch.tensor(rows if rows else [(0, 0, 0)], dtype=torch.int32)
-    return t.pin_memory().to(device, non_blocking=True) if rows else t[:0].to(device)
-
-
-def prefill_attention_tc(qkv: torch.Tensor, tile_info: torch.Tensor, n_q_heads: int, n_kv_heads: int,
-                         out: Optional[torch.Tensor] = None, scale: Optional[float] = None,
-                         status: Optional[torch.Tensor] = None) -> torch.Tensor:
-    """Causal varlen prefill attention on tcgen05 (tile_info from :func:`prefill_tile_info_tc`)."""
-    if out is None:
-        out = torch.empty(qkv.shape[0], n_q_heads * 128, dtype=qkv.dtype, device=qkv.device)
-    _C.prefill_attention_tc(qkv, out, tile_info, n_q_heads, n_kv_heads,
-                            scale if scale is not None else 1.0 / math.sqrt(128), status)
+                         scale if scale is not None else 1.0 / math.sqrt(128), status)
     _n()
     return out
 

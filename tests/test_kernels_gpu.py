@@ -115,33 +115,19 @@ def test_embedding_argmax(dev):
     assert torch.equal(ops.argmax(logits).long(), logits.float().argmax(-1))
 
 
-@pytest.mark.parametrize("lens", [[1], [64], [100, 37, 1], [513, 64, 7]])
-def test_prefill_attention(dev, lens):
-    from connex_b200 import ops
-    from connex_b200.ops import reference as R
-    Hq, Hkv, T = 8, 2, sum(lens)
-    qkv = _rnd(T, (Hq + 2 * Hkv) * 128, dev=dev, seed=17)
-    ti = ops.prefill_tile_info(lens, dev)
-    out = ops.prefill_attention(qkv, ti, Hq, Hkv)
-    q = qkv[:, :Hq * 128].view(T, Hq, 128)
-    k = qkv[:, Hq * 128:(Hq + Hkv) * 128].view(T, Hkv, 128)
-    v = qkv[:, (Hq + Hkv) * 128:].view(T, Hkv, 128)
-    _close(out.view(T, Hq, 128), R.causal_attention(q, k, v, lens))
-
-
 @pytest.mark.parametrize("lens", [[1], [128], [100, 37, 1], [513, 130, 7], [1100]])
 @pytest.mark.parametrize("G", [4, 1])
-def test_prefill_attention_tc(dev, lens, G):
+def test_prefill_attention(dev, lens, G):
     from connex_b200 import ops
     from connex_b200.ops import reference as R
     Hkv = 2
     Hq, T = Hkv * G, sum(lens)
     qkv = _rnd(T, (Hq + 2 * Hkv) * 128, dev=dev, seed=31)
-    ti = ops.prefill_tile_info_tc(lens, dev)
+    ti = ops.prefill_tile_info(lens, dev)
     st = ops.new_status(dev)
-    out = ops.prefill_attention_tc(qkv, ti, Hq, Hkv, status=st)
+    out = ops.prefill_attention(qkv, ti, Hq, Hkv, status=st)
     torch.cuda.synchronize()
-    ops.check_status(st, "prefill_attention_tc")
+    ops.check_status(st, "prefill_attention")
     q = qkv[:, :Hq * 128].view(T, Hq, 128)
     k = qkv[:, Hq * 128:(Hq + Hkv) * 128].view(T, Hkv, 128)
     v = qkv[:, (Hq + Hkv) * 128:].view(T, Hkv, 128)
