@@ -15,7 +15,7 @@ Every CUDA file is compiled for exactly one target: sm_100a (B200).
 import os
 import glob
 
-from setuptools import setup, find_packages
+from setuptools import Extension, setup, find_packages
 from torch.utils.cpp_extension import BuildExtension, CUDAExtension, CppExtension
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
@@ -42,13 +42,16 @@ ext_modules = [
     ),
 ]
 if engine_sources:
+    # plain pybind11 module: importing the engine does not load libtorch
+    import pybind11
     ext_modules.append(
-        CppExtension(
+        Extension(
             name="connex_b200._cxengine",
             sources=engine_sources,
-            include_dirs=[os.path.join(ROOT, EDIR)],
-            extra_compile_args={"cxx": CXX_FLAGS + ["-pthread"]},
+            include_dirs=[os.path.join(ROOT, EDIR), pybind11.get_include()],
+            extra_compile_args=CXX_FLAGS + ["-pthread", "-fvisibility=hidden"],
             extra_link_args=["-pthread"],
+            language="c++",
         )
     )
 
