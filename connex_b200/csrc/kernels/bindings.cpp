@@ -195,6 +195,70 @@ void write_flag(int64_t flag, int64_t value, bool add, const at::Tensor& like) {
   cx::write_flag(reinterpret_cast<uint32_t*>(flag), (uint32_t)value, add, cur_stream(like));
 }
 
+// ---- expert parallelism -------------------------------------------------------
+// peers: int64 CUDA tensor [7, N] of addresses (counts, count_flag, recv,
+// recv_meta, data_flag, comb, comb_flag) on every rank.
+cx::EpPeers ep_peers(const at::Tensor& peers) {
+  TORCH_CHECK(peers.scalar_type() == at::kLong && peers.is_cuda() && peers.dim() == 2 && peers.size(0) == 7,
+              "peers must be int64 CUDA [7, N]");
+  const uint64_t* p = reinterpret_cast<const uint64_t*>(peers.data_ptr<int64_t>());
+  const int64_t N = peers.size(1);
+  return cx::EpPeers{p, p + N, p + 2 * N, p + 3 * N, p + 4 * N, p + 5 * N, p + 6 * N};
+}
+
+void ep_count(const at::Tensor& topk_idx, const at::Tensor& l2p, const at::Tensor& l2p_cnt, int64_t S, int64_t me,
+              at::Tensor& pos, at::Tensor& slot_of, const at::Tensor& peers, at::Tensor& comb_expect,
+              int64_t arrivals_per_row, const c10::optional<at::Tensor>& status) {
+  const c10::cuda::CUDAGuard g(topk_idx.device());
+  TORCH_CHECK(topk_idx.scalar_type() == at::kInt && topk_idx.is_contiguous() && topk_idx.dim() == 2,
+              "topk_idx must be contiguous int32 [T, K]");
+  TORCH_CHECK(pos.numel() >= topk_idx.numel() && slot_of.numel() >= topk_idx.numel(),
+              "ep_count: pos / slot_of hold fewer than T*K entries (more tokens than the layer's capacity)");
+  TORCH_CHECK(l2p.scalar_type() == at::kInt && l2p.dim() == 2 && l2p_cnt.numel() == l2p.size(0),
+              "l2p must be int32 [E, R] with l2p_cnt [E]");
+  cx::ep_count(topk_idx.data_ptr<int>(), l2p.data_ptr<int>(), l2p_cnt.data_ptr<int>(), (int)l2p.size(1),
+               (int)topk_idx.size(0), (int)topk_idx.size(1), (int)peers.size(1), (int)S, (int)me, pos.data_ptr<int>(),
+               slot_of.data_ptr<int>(), ep_peers(peers), reinterpret_cast<uint32_t*>(comb_expect.data_ptr<int>()),
+               (int)arrivals_per_row, status_ptr(status), cur_stream(topk_idx));
+}
+
+void ep_dispatch(const at::Tensor& x, const at::Tensor& topk_w, const at::Tensor& pos, const at::Tensor& slot_of,
+                 const at::Tensor& counts_local, int64_t K, int64_t S, int64_t me, int64_t R_max, int64_t count_target,
+                 const at::Tensor& peers, const c10::optional<at::Tensor>& status) {
+  CHECK_BF16(x);
+  const c10::cuda::CUDAGuard g(x.device());
+  TORCH_CHECK(x.is_contiguous() && topk_w.is_contiguous() && topk_w.numel() == x.size(0) * K,
+              "ep_dispatch: x [T, H] and topk_w [T, K] must be contiguous and agree");
+  TORCH_CHECK(pos.numel() >= x.size(0) * K, "ep_dispatch: more tokens than the layer's capacity");
+  cx::ep_dispatch(x.data_ptr(), topk_w.data_ptr<float>(), pos.data_ptr<int>(), slot_of.data_ptr<int>(),
+                  counts_local.data_ptr<int>(), (int)x.size(0), (int)K, (int)x.size(1), (int)peers.size(1), (int)S,
+                  (int)me, (int)R_max, (uint32_t)count_target, ep_peers(peers), status_ptr(status), cur_stream(x));
+}
+
+void ep_grouped_gemm(const at::Tensor& A, const at::Tensor& B, int64_t n_per_expert, at::Tensor& D,
+                     const at::Tensor& counts_local, int64_t S, int64_t me, int64_t mode, const at::Tensor& recv_meta,
+                     const at::Tensor& peers, int64_t H, int64_t wait_flag, int64_t wait_target,
+                     const c10::optional<at::Tensor>& status) {
+  CHECK_BF16(A);
+  CHECK_BF16(B);
+  const c10::cuda::CUDAGuard g(A.device());
+  cx::ep_grouped_gemm(A.data_ptr(), row_ld(A), B.data_ptr(), (int)n_per_expert, (int)A.size(1), D.data_ptr(),
+                      (int)D.stride(0), counts_local.data_ptr<int>(), (int)peers.size(1), (int)S, (int)me,
+                      (int)A.size(0), (int)mode, recv_meta.data_ptr<int>(), ep_peers(peers), (int)H,
+                      reinterpret_cast<const uint32_t*>(wait_flag), (uint32_t)wait_target, status_ptr(status),
+                      cur_stream(A));
+}
+
+void ep_combine(const at::Tensor& comb, const at::Tensor& slot_of, int64_t T, int64_t K, at::Tensor& y,
+                int64_t comb_flag, const at::Tensor& expect, const c10::optional<at::Tensor>& status) {
+  const c10::cuda::CUDAGuard g(comb.device());
+  TORCH_CHECK(comb.size(0) >= T * K && slot_of.numel() >= T * K && y.size(0) >= T && y.size(1) == comb.size(1),
+              "ep_combine: buffers smaller than T*K rows");
+  cx::ep_combine(comb.data_ptr(), slot_of.data_ptr<int>(), (int)T, (int)K, (int)y.size(1), y.data_ptr(),
+                 reinterpret_cast<const uint32_t*>(comb_flag), reinterpret_cast<const uint32_t*>(expect.data_ptr<int>()),
+                 status_ptr(status), cur_stream(comb));
+}
+
 // ---- CUDA IPC ---------------------------------------------------------------
 // Export the allocation that contains `ptr`: returns (handle bytes, offset of
 // ptr inside the allocation).
@@ -271,6 +335,11 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("copy_segments", &copy_segments);
   m.def("wait_flag", &wait_flag);
   m.def("write_flag", &write_flag);
+  m.def("ep_count", &ep_count);
+  m.def("ep_dispatch", &ep_dispatch);
+  m.def("ep_grouped_gemm", &ep_grouped_gemm);
+  m.def("ep_combine", &ep_combine);
+  m.attr("EP_DISPATCH_CTAS") = cx::EP_DISPATCH_CTAS;
   m.def("ipc_export", &ipc_export);
   m.def("ipc_open", &ipc_open);
   m.def("ipc_close", &ipc_close);
