@@ -1,0 +1,206 @@
+"""EP MoE layer benchmark: fused peer-memory path vs an NCCL baseline.
+
+Workload (Qwen3-30B-A3B-style MoE layer): hidden 2048, 128 experts, top-8,
+expert FFN 768, EP = world size (128 / N experts per rank), bf16, router
+logits ~ N(0, 1) plus a Zipf(1.2) popularity bias over experts (seeded),
+T tokens per rank.  Measures one full MoE layer (dispatch + expert GEMMs +
+combine) per step:
+
+* ``cx``   -- this package's five kernels over NVLink peer memory (no NCCL),
+* ``nccl`` -- ``all_to_all_single`` of counts, tokens and results (NCCL) with
+  per-expert torch matmuls, the conventional EP implementation.
+
+Device time by CUDA events around ``iters`` steps after warm-up, max over
+ranks.  Both paths are checked against each other before timing.
+"""
+from __future__ import annotations
+
+import statistics
+from typing import Dict, List, Optional
+
+import numpy as np
+import torch
+import torch.distributed as dist
+import torch.nn.functional as F
+
+from connex_b200 import ops
+from connex_b200.parallel.ep import EPBuffers, EPConfig, EPMoE, map_remote, peer_table
+from connex_b200.parallel.peer import PeerMapper
+
+H, FFN, E, TOPK = 2048, 768, 128, 8
+
+
+def zipf_routing(T: int, seed: int, device, skew: float = 1.2):
+    rng = np.random.default_rng(seed)
+    ranks = rng.permutation(E) + 1
+    bias = torch.tensor(-skew * np.log(ranks), dtype=torch.float32, device=device)
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    logits = torch.randn(T, E, generator=g, device=device) + bias
+    w, idx = torch.topk(torch.softmax(logits, -1), TOPK, dim=-1)
+    return idx.to(torch.int32).contiguous(), (w / w.sum(-1, keepdim=True)).float().contiguous()
+
+
+def make_weights(S: int, rank: int, device):
+    g = torch.Generator(device=device)
+    g.manual_seed(1000 + rank)
+    gate = torch.randn(S, FFN, H, generator=g, device=device) * 0.02
+    up = torch.randn(S, FFN, H, generator=g, device=device) * 0.02
+    w13 = torch.stack([ops.interleave_gate_up(gate[i].bfloat16(), up[i].bfloat16()) for i in range(S)]).contiguous()
+    w2 = (torch.randn(S, H, FFN, generator=g, device=device) * 0.02).bfloat16().contiguous()
+    return w13, w2
+
+
+def nccl_moe(x, idx, w, w13, w2, N: int, S: int, group=None):
+    """Baseline: NCCL all_to_all_single dispatch/combine + torch matmuls."""
+    T, K = idx.shape
+    flat = idx.flatten().long()
+    dst = flat // S
+    order = torch.argsort(dst, stable=True)
+    send_counts = torch.bincount(dst, minlength=N)
+    recv_counts = torch.empty_like(send_counts)
+    if N > 1:
+        dist.all_to_all_single(recv_counts, send_counts, group=group)
+    else:
+        recv_counts.copy_(send_counts)
+    sc, rc = send_counts.tolist(), recv_counts.tolist()
+    send_x = x[order // K]
+    send_e = (flat[order] % S).to(torch.int32)
+    recv_x = torch.empty(sum(rc), x.shape[1], dtype=x.dtype, device=x.device)
+    recv_e = torch.empty(sum(rc), dtype=torch.int32, device=x.device)
+    if N > 1:
+        dist.all_to_all_single(recv_x, send_x, rc, sc, group=group)
+        dist.all_to_all_single(recv_e, send_e, rc, sc, group=group)
+    else:
+        recv_x.copy_(send_x)
+        recv_e.copy_(send_e)
+    out = torch.empty_like(recv_x)
+    for e in range(S):
+        rows = (recv_e == e).nonzero(as_tuple=True)[0]
+        if rows.numel() == 0:
+            continue
+        xe = recv_x[rows]
+        gu = xe @ w13[e].t()
+        g_, u_ = gu.view(-1, 2 * FFN // 256, 2, 128)[:, :, 0].reshape(-1, FFN), \
+            gu.view(-1, 2 * FFN // 256, 2, 128)[:, :, 1].reshape(-1, FFN)
+        out[rows] = (F.silu(g_) * u_) @ w2[e].t()
+    back = torch.empty_like(send_x)
+    if N > 1:
+        dist.all_to_all_single(back, out, sc, rc, group=group)
+    else:
+        back.copy_(out)
+    y = torch.zeros(T, x.shape[1], dtype=torch.float32, device=x.device)
+    y.index_add_(0, order // K, back.float() * w.flatten()[order][:, None])
+    return y.to(x.dtype)
+
+
+class FusedEP:
+    """One rank's fused EP layer with peers mapped through CUDA IPC."""
+
+    def __init__(self, world: int, rank: int, device, max_tokens: int, cpu_group=None):
+        self.world, self.rank = world, rank
+        S = E // world
+        self.cfg = EPConfig(world, S, H, FFN, TOPK, max_tokens=max_tokens)
+        self.bufs = EPBuffers(self.cfg, device)
+        self.mapper = PeerMapper(device.index)
+        if world > 1:
+            allx = [None] * world
+            dist.all_gather_object(allx, self.bufs.exports(), group=cpu_group)
+            addrs = [self.bufs.addresses() if r == rank else map_remote(allx[r], self.mapper)
+                     for r in range(world)]
+        else:
+            addrs = [self.bufs.addresses()]
+        self.peers = peer_table(addrs, device)
+        self.w13, self.w2 = make_weights(S, rank, device)
+        self.layer = EPMoE(self.cfg, rank, self.bufs, self.peers, self.w13, self.w2)
+        self.l2p = torch.arange(E, dtype=torch.int32, device=device).view(E, 1).contiguous()
+        self.cnt = torch.ones(E, dtype=torch.int32, device=device)
+
+    def forward(self, x, idx, w, out=None):
+        return self.layer.forward(x, idx, w, self.l2p, self.cnt, out)
+
+    def close(self):
+        self.mapper.close()
+
+
+def _time(fn, iters: int, warmup: int, barrier) -> float:
+    for _ in range(warmup):
+        fn()
+    barrier()
+    torch.cuda.synchronize()
+    e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    e0.record()
+    for _ in range(iters):
+        fn()
+    e1.record()
+    torch.cuda.synchronize()
+    return e0.elapsed_time(e1) * 1000.0 / iters  # us
+
+
+def run_ep_bench(world: int, rank: int, device, cpu_group=None, nccl_group=None,
+                 tokens=(128, 4096), iters: int = 20, warmup: int = 5) -> Dict:
+    barrier = (lambda: dist.barrier(group=cpu_group)) if world > 1 else (lambda: None)
+    fused = FusedEP(world, rank, device, max(tokens), cpu_group)
+    res: Dict = {}
+    for T in tokens:
+        idx, w = zipf_routing(T, seed=7 * rank + T, device=device)
+        g = torch.Generator(device=device)
+        g.manual_seed(rank + T)
+        x = (torch.randn(T, H, generator=g, device=device) * 0.5).bfloat16()
+        y_cx = fused.forward(x, idx, w)
+        y_ref = nccl_moe(x, idx, w, fused.w13, fused.w2, world, E // world, nccl_group)
+        torch.cuda.synchronize()
+        ops.check_status(fused.bufs.status, "ep")
+        err = (y_cx.float() - y_ref.float()).abs().max().item()
+        scale = y_ref.float().abs().max().item() + 1e-6
+        out = torch.empty_like(x)
+        t_cx = _time(lambda: fused.forward(x, idx, w, out), iters, warmup, barrier)
+        t_nccl = _time(lambda: nccl_moe(x, idx, w, fused.w13, fused.w2, world, E // world, nccl_group),
+                       iters, warmup, barrier)
+        ops.check_status(fused.bufs.status, "ep")
+        res[T] = {"cx_us": t_cx, "nccl_us": t_nccl, "max_err": err, "scale": scale}
+    fused.close()
+    return res
+
+
+def reduce_max(per_rank: List[Dict]) -> Dict:
+    out = {}
+    for T in per_rank[0]:
+        out[str(T)] = {k: max(r[T][k] for r in per_rank) for k in ("cx_us", "nccl_us", "max_err", "scale")}
+        out[str(T)]["speedup_vs_nccl"] = round(out[str(T)]["nccl_us"] / out[str(T)]["cx_us"], 2)
+        out[str(T)] = {k: (float(f"{v:.4g}") if isinstance(v, float) else v) for k, v in out[str(T)].items()}
+    return out
+
+
+def main() -> None:
+    import argparse
+    import json
+    import os
+    from datetime import timedelta
+    p = argparse.ArgumentParser()
+    p.add_argument("--tokens", default="128,4096")
+    p.add_argument("--iters", type=int, default=20)
+    a = p.parse_args()
+    world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    cpu = nccl = None
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+        cpu = dist.new_group(backend="gloo", timeout=timedelta(seconds=120))
+    res = run_ep_bench(world, rank, dev, cpu, nccl, tokens=tuple(int(t) for t in a.tokens.split(",")),
+                       iters=a.iters)
+    allr = [None] * world
+    if world > 1:
+        dist.all_gather_object(allr, res, group=cpu)
+    else:
+        allr = [res]
+    if rank == 0:
+        print(json.dumps({"ep_layer_us": reduce_max(allr), "n_gpus": world}), flush=True)
+    if world > 1:
+        dist.barrier(group=cpu)
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

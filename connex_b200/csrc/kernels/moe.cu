@@ -122,7 +122,7 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const __nv_bfloat16* _
 
 // ------------------------------------------------------- grouped GEMM
 namespace epg {
-constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4, THREADS = 192, MAXS = 64;
+constexpr int BM = 128, BN = 256, BK = 64, STAGES = 4, THREADS = 192, MAXS = 256;
 constexpr int A_BYTES = BM * BK * 2, B_BYTES = BN * BK * 2, STAGE_BYTES = A_BYTES + B_BYTES;
 constexpr int SMEM = 1024 + STAGES * STAGE_BYTES + 256 + (MAXS + 1) * 4 * 2;
 }  // namespace epg
@@ -195,8 +195,12 @@ __global__ void __launch_bounds__(epg::THREADS, 1)
   const int nk = (K + BK - 1) / BK;
 
   auto locate = [&](int t, int& e, int& mt, int& nt) {
-    e = 0;
-    while (e + 1 < S && tpre[e + 1] <= t) ++e;
+    int lo = 0, hi = S - 1;  // last e with tpre[e] <= t (empty experts share a prefix)
+    while (lo < hi) {
+      const int mid = (lo + hi + 1) >> 1;
+      if (tpre[mid] <= t) lo = mid; else hi = mid - 1;
+    }
+    e = lo;
     const int r = t - tpre[e];
     mt = r / n_tiles;
     nt = r - mt * n_tiles;
