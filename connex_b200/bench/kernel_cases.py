@@ -1,0 +1,143 @@
+"""Single-kernel cases for timing and profiling the sm_100a kernels.
+
+``python -m connex_b200.bench.kernel_cases <case> [--iters K]`` runs one
+kernel on a fixed case (inputs larger than the 126 MB L2 where the kernel is
+memory-bound, a few GB on the device at most), times it with CUDA events
+after warm-up and prints one JSON line with the achieved rate and its
+fraction of the measured peaks in ``MEASURED_PEAKS.json`` (copy bandwidth,
+cuBLAS bf16 burst throughput).  The same command line is what a profiler
+capture of the case runs.
+
+Cases: gemm (8192^3), gemm_qkv (T=8192 Llama-3-8B QKV), gemm_silu (T=8192
+gate/up + SiLU-mul), attn (8 x 2048-token causal prefill, 32/8 heads),
+decode_attn (64 x 4096-token paged decode), kv_push (one layer of a 64k-token
+KV push, local), wsync (Llama-3-8B 2-layer slice, fp32 -> bf16 fused
+re-layout), ep_gemm (grouped expert GEMM, 1 GPU).
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+
+import torch
+
+from connex_b200 import ops
+
+ROOT = os.path.dirname(os.path.dirname(os.path.dirname(os.path.abspath(__file__))))
+
+
+def _peaks():
+    try:
+        with open(os.path.join(ROOT, "MEASURED_PEAKS.json")) as f:
+            p = json.load(f)
+        return p["hbm_gbs"], p["bf16_tflops"], "measured"
+    except (OSError, KeyError, ValueError):
+        return 6650.0, 1590.0, "fallback"
+
+
+def _time(fn, iters: int, warmup: int = 3) -> float:
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+    a.record()
+    for _ in range(iters):
+        fn()
+    b.record()
+    torch.cuda.synchronize()
+    return a.elapsed_time(b) / iters
+
+
+def case_gemm(dev, M=8192, N=8192, K=8192, silu=False):
+    a = torch.randn(M, K, device=dev).bfloat16()
+    b = torch.randn(N, K, device=dev).bfloat16()
+    out = torch.empty(M, N // 2 if silu else N, dtype=torch.bfloat16, device=dev)
+    return (lambda: ops.gemm(a, b, out, silu_mul=silu)), {"flops": 2 * M * N * K}
+
+
+def case_attn(dev, n_seq=8, L=2048, hq=32, hkv=8):
+    T = n_seq * L
+    qkv = (torch.randn(T, (hq + 2 * hkv) * 128, device=dev) * 0.5).bfloat16()
+    ti = ops.prefill_tile_info([L] * n_seq, dev)
+    out = torch.empty(T, hq * 128, dtype=torch.bfloat16, device=dev)
+    flops = n_seq * hq * 2 * 2 * 128 * L * L / 2   # causal: half of QK^T and PV
+    return (lambda: ops.prefill_attention(qkv, ti, hq, hkv, out)), {"flops": flops}
+
+
+def case_decode_attn(dev, B=64, ctx=4096, hq=32, hkv=8):
+    bs = 16
+    nb = B * ctx // bs
+    k = torch.randn(nb, hkv, bs, 128, device=dev).bfloat16()
+    v = torch.randn(nb, hkv, bs, 128, device=dev).bfloat16()
+    bt = torch.arange(nb, dtype=torch.int32, device=dev).view(B, ctx // bs)
+    cl = torch.full((B,), ctx, dtype=torch.int32, device=dev)
+    q = torch.randn(B, hq * 128, device=dev).bfloat16()
+    ws = ops.decode_workspace(B, hq, ctx, dev)
+    out = torch.empty(B, hq * 128, dtype=torch.bfloat16, device=dev)
+    return (lambda: ops.decode_attention(q, k, v, bt, cl, hq, ctx, ws, out)), {"bytes": 2 * k.numel() * 2}
+
+
+def case_kv_push(dev, tokens=65536, hkv=8):
+    bs = 16
+    nb = tokens // bs
+    src = torch.randn(2, nb, hkv, bs, 128, device=dev).bfloat16()
+    dst = torch.empty_like(src)
+    pairs = torch.stack([torch.arange(nb), torch.randperm(nb)], 1).int().to(dev)
+    chunk = bs * 128 * 2
+
+    def run():
+        ops.kv_push_layer(src[0].data_ptr(), src[1].data_ptr(), dst[0].data_ptr(), dst[1].data_ptr(), pairs,
+                          src_heads=hkv, dst_heads=hkv, chunk_bytes=chunk, src_blocks=nb, dst_blocks=nb)
+    return run, {"bytes": 2 * src.numel() * 2}   # read + write
+
+
+def case_wsync(dev, layers=2):
+    from connex_b200.models.llama import LlamaConfig, random_trainer_weights
+    from connex_b200.parallel.wsync import apply_local, engine_manifest, plan_jobs
+    cfg = LlamaConfig(layers=layers)
+    named = random_trainer_weights(cfg, dev, dtype=torch.float32)
+    m = engine_manifest(cfg)
+    jobs, _, _ = plan_jobs(cfg, m, named)
+    arena = torch.empty(m.total, dtype=torch.uint8, device=dev)
+    return (lambda: apply_local(jobs, arena)), {"bytes": m.total * 3}    # 4 B read + 2 B written per element
+
+
+def case_ep_gemm(dev):
+    from connex_b200.bench.ep_bench import H, FFN, FusedEP, zipf_routing
+    T = 4096
+    fused = FusedEP(1, 0, dev, T)
+    idx, w = zipf_routing(T, seed=3, device=dev)
+    x = (torch.randn(T, H, device=dev) * 0.5).bfloat16()
+    out = torch.empty_like(x)
+    flops = 2 * T * 8 * H * 3 * FFN
+    return (lambda: fused.forward(x, idx, w, out)), {"flops": flops}
+
+
+CASES = {"gemm": lambda d: case_gemm(d), "gemm_qkv": lambda d: case_gemm(d, 8192, 6144, 4096),
+         "gemm_silu": lambda d: case_gemm(d, 8192, 28672, 4096, silu=True), "attn": case_attn,
+         "decode_attn": case_decode_attn, "kv_push": case_kv_push, "wsync": case_wsync, "ep_gemm": case_ep_gemm}
+
+
+def main() -> None:
+    p = argparse.ArgumentParser()
+    p.add_argument("case", choices=sorted(CASES))
+    p.add_argument("--iters", type=int, default=20)
+    a = p.parse_args()
+    dev = torch.device("cuda", 0)
+    fn, work = CASES[a.case](dev)
+    ms = _time(fn, a.iters)
+    hbm, tf, src = _peaks()
+    res = {"case": a.case, "ms": round(ms, 4)}
+    if "flops" in work:
+        res["tflops"] = round(work["flops"] / ms / 1e9, 1)
+        res[f"frac_of_{src}_bf16"] = round(res["tflops"] / tf, 3)
+    if "bytes" in work:
+        res["gbps"] = round(work["bytes"] / ms / 1e6, 1)
+        res[f"frac_of_{src}_hbm"] = round(res["gbps"] / hbm, 3)
+    print(json.dumps(res), flush=True)
+
+
+if __name__ == "__main__":
+    main()

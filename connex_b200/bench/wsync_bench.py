@@ -1,0 +1,132 @@
+"""RL weight-sync benchmark: Llama-3-8B trainer fp32 master weights ->
+bf16 engine weights (fused q|k|v, interleaved gate/up) on every other GPU
+of one box.
+
+Arms (all end with the engine-layout bf16 weights in every receiver's live
+weight arena):
+
+* ``fused_mc``  -- :class:`WeightBroadcast` over NVLink multicast (one
+  kernel reads fp32, casts, re-lays out and stores through the multicast
+  address; receivers wait on a device flag);
+* ``fused_p2p`` -- the same kernel storing to each receiver's peer address;
+* ``nccl``      -- conventional: PyTorch cast + cat + interleave on the
+  trainer into a bf16 staging arena, then ``dist.broadcast`` (NCCL).
+
+N = 1 times the local fused conversion only (``local``).  Device time by
+CUDA events from a common barrier, max over ranks; weights (32 GB fp32,
+16 GB bf16) exceed L2.
+"""
+from __future__ import annotations
+
+import json
+import os
+from datetime import timedelta
+from typing import Dict
+
+import torch
+import torch.distributed as dist
+
+from connex_b200.models.llama import LlamaConfig, random_trainer_weights
+from connex_b200.parallel.wsync import WeightBroadcast, apply_local, engine_manifest, fuse_reference, plan_jobs
+
+
+def _ev():
+    return torch.cuda.Event(enable_timing=True)
+
+
+def _max(x: float, world: int) -> float:
+    if world == 1:
+        return x
+    t = torch.tensor([x], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def _time(fn, iters: int, world: int) -> float:
+    ms = []
+    for _ in range(iters):
+        if world > 1:
+            dist.barrier()
+        torch.cuda.synchronize()
+        a, b = _ev(), _ev()
+        a.record()
+        fn()
+        b.record()
+        torch.cuda.synchronize()
+        ms.append(_max(a.elapsed_time(b), world))
+    return sorted(ms)[len(ms) // 2]
+
+
+def run(cfg: LlamaConfig, iters: int = 5, warmup: int = 3) -> Dict:
+    world = dist.get_world_size() if dist.is_initialized() else 1
+    rank = dist.get_rank() if dist.is_initialized() else 0
+    dev = torch.device("cuda", torch.cuda.current_device())
+    m = engine_manifest(cfg)
+    named = random_trainer_weights(cfg, dev, dtype=torch.float32, seed=1) if rank == 0 else None
+    out: Dict = {"engine_bytes": m.total, "receivers": max(world - 1, 1)}
+    if world == 1:
+        jobs, _, _ = plan_jobs(cfg, m, named)
+        arena = torch.empty(m.total, dtype=torch.uint8, device=dev)
+        for _ in range(warmup):
+            apply_local(jobs, arena)
+        out["local_ms"] = _time(lambda: apply_local(jobs, arena), iters, 1)
+        return out
+    for mode in ("multicast", "p2p"):
+        try:
+            bc = WeightBroadcast(cfg, mode=mode)
+        except RuntimeError as e:
+            out[f"fused_{mode}_ms"] = None
+            out[f"fused_{mode}_error"] = str(e)[:120]
+            continue
+        n_tasks = plan_jobs(cfg, m, named)[1] if rank == 0 else None
+        box = [n_tasks]
+        dist.broadcast_object_list(box, src=0)
+        n_tasks = box[0]
+        for _ in range(warmup):
+            bc.sync(named, n_tasks)
+        out[f"fused_{mode}_ms"] = _time(lambda: bc.sync(named, n_tasks), iters, world)
+        torch.cuda.synchronize()
+        bc.check()
+        bc.close()
+        del bc
+        torch.cuda.empty_cache()
+    staging = torch.empty(m.total, dtype=torch.uint8, device=dev)
+
+    def nccl():
+        if rank == 0:
+            fused = fuse_reference(cfg, named)
+            for e in m.entries:
+                staging[e.offset:e.offset + e.nbytes].copy_(fused[e.name].view(-1).view(torch.uint8))
+            del fused
+        dist.broadcast(staging, src=0)
+    for _ in range(warmup):
+        nccl()
+    out["nccl_ms"] = _time(nccl, iters, world)
+    return out
+
+
+def main() -> None:
+    import argparse
+    p = argparse.ArgumentParser()
+    p.add_argument("--iters", type=int, default=5)
+    p.add_argument("--layers", type=int, default=32)
+    a = p.parse_args()
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+    torch.cuda.set_device(dev)
+    if world > 1:
+        dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
+    cfg = LlamaConfig(layers=a.layers)
+    res = run(cfg, a.iters)
+    if (dist.get_rank() if world > 1 else 0) == 0:
+        gb = res["engine_bytes"] / 1e9
+        for k in [k for k in list(res) if k.endswith("_ms") and res[k]]:
+            res[k.replace("_ms", "_GBps_per_receiver")] = round(gb / (res[k] / 1e3), 1)
+        print(json.dumps({"wsync": res, "n_gpus": world, "model": "llama3-8b", "src_dtype": "fp32"}), flush=True)
+    if world > 1:
+        dist.barrier()
+        dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

@@ -184,6 +184,25 @@ int64_t copy_segments(const at::Tensor& segs, int64_t total_bytes, int64_t ready
                            reinterpret_cast<uint32_t*>(ready), (int)max_ctas, status_ptr(status), cur_stream(segs));
 }
 
+// Weight sync: jobs int64 [n, WS_JOB_COLS] on the device and its host copy
+// (validated here); destinations are a multicast address or up to
+// WS_MAX_DST plain bases (with optional flag words).
+int64_t wsync(const at::Tensor& jobs_dev, const at::Tensor& jobs_cpu, int64_t dst_bytes, std::vector<int64_t> bases,
+              std::vector<int64_t> flags, int64_t mc_base, int64_t mc_flag, int64_t max_ctas) {
+  TORCH_CHECK(jobs_dev.is_cuda() && jobs_dev.scalar_type() == at::kLong && jobs_dev.is_contiguous() &&
+                  jobs_dev.dim() == 2 && jobs_dev.size(1) == cx::WS_JOB_COLS,
+              "jobs_dev must be contiguous int64 CUDA [n, ", cx::WS_JOB_COLS, "]");
+  TORCH_CHECK(!jobs_cpu.is_cuda() && jobs_cpu.scalar_type() == at::kLong && jobs_cpu.is_contiguous() &&
+                  jobs_cpu.sizes() == jobs_dev.sizes(),
+              "jobs_cpu must be the contiguous host copy of jobs_dev");
+  TORCH_CHECK(flags.empty() || flags.size() == bases.size(), "one flag per destination (or none)");
+  const c10::cuda::CUDAGuard g(jobs_dev.device());
+  return cx::wsync(jobs_dev.data_ptr<int64_t>(), jobs_cpu.data_ptr<int64_t>(), (int)jobs_dev.size(0), dst_bytes,
+                   reinterpret_cast<const uint64_t*>(bases.data()),
+                   flags.empty() ? nullptr : reinterpret_cast<const uint64_t*>(flags.data()), (int)bases.size(),
+                   (uint64_t)mc_base, (uint64_t)mc_flag, (int)max_ctas, cur_stream(jobs_dev));
+}
+
 void wait_flag(int64_t flag, int64_t target, int64_t timeout_ns, const at::Tensor& status) {
   const c10::cuda::CUDAGuard g(status.device());
   cx::wait_flag(reinterpret_cast<const uint32_t*>(flag), (uint32_t)target, (uint64_t)timeout_ns,
@@ -333,6 +352,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_workspace_floats", &decode_workspace_floats);
   m.def("kv_push_layer", &kv_push_layer);
   m.def("copy_segments", &copy_segments);
+  m.def("wsync", &wsync);
+  m.attr("WS_JOB_COLS") = cx::WS_JOB_COLS;
+  m.attr("WS_MAX_DST") = cx::WS_MAX_DST;
   m.def("wait_flag", &wait_flag);
   m.def("write_flag", &write_flag);
   m.def("ep_count", &ep_count);

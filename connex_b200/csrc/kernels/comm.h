@@ -16,6 +16,13 @@ int kv_push_layer(const void* src_k, const void* src_v, void* dst_k, void* dst_v
 int copy_segments(const int64_t* segs, int n, int64_t total_bytes, uint32_t* ready, int max_ctas, int* status,
                   cudaStream_t s);
 
+// Weight sync (wsync.cu): fused cast + re-layout broadcast.  Returns the CTA
+// count; each CTA releases +1 on every destination flag when it is done.
+constexpr int WS_JOB_COLS = 12;
+constexpr int WS_MAX_DST = 8;
+int wsync(const int64_t* jobs_dev, const int64_t* jobs_host, int n_jobs, int64_t dst_bytes, const uint64_t* dst_bases,
+          const uint64_t* dst_flags, int n_dst, uint64_t mc_base, uint64_t mc_flag, int max_ctas, cudaStream_t s);
+
 void wait_flag(const uint32_t* flag, uint32_t target, uint64_t timeout_ns, int* status, cudaStream_t s);
 void write_flag(uint32_t* flag, uint32_t value, bool add, cudaStream_t s);
 

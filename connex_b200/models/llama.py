@@ -112,6 +112,37 @@ class LlamaWeights:
         return cls(cfg=cfg, embed=rnd(cfg.vocab_size, cfg.hidden), layers=layers,
                    final_norm=ones(cfg.hidden), lm_head=rnd(cfg.vocab_size, cfg.hidden))
 
+    @staticmethod
+    def layout(cfg: LlamaConfig):
+        """``(name, shape)`` of every engine tensor, in :meth:`named_tensors` order."""
+        yield "model.embed_tokens.weight", (cfg.vocab_size, cfg.hidden)
+        for i in range(cfg.layers):
+            p = f"model.layers.{i}."
+            yield p + "input_layernorm.weight", (cfg.hidden,)
+            yield p + "self_attn.qkv_proj.weight", (cfg.qkv_dim, cfg.hidden)
+            yield p + "self_attn.o_proj.weight", (cfg.hidden, cfg.heads * cfg.head_dim)
+            yield p + "post_attention_layernorm.weight", (cfg.hidden,)
+            yield p + "mlp.gate_up_proj.weight", (2 * cfg.ffn, cfg.hidden)
+            yield p + "mlp.down_proj.weight", (cfg.hidden, cfg.ffn)
+        yield "model.norm.weight", (cfg.hidden,)
+        yield "lm_head.weight", (cfg.vocab_size, cfg.hidden)
+
+    @classmethod
+    def from_arena(cls, cfg: LlamaConfig, arena: torch.Tensor, manifest) -> "LlamaWeights":
+        """Weights as views into one uint8 arena laid out by ``manifest``
+        (a ``connex.rl.weights.WeightManifest`` of :meth:`layout`)."""
+        t = {e.name: arena[e.offset:e.offset + e.nbytes].view(torch.bfloat16).view(e.shape)
+             for e in manifest.entries}
+        layers = []
+        for i in range(cfg.layers):
+            p = f"model.layers.{i}."
+            layers.append(LayerWeights(attn_norm=t[p + "input_layernorm.weight"],
+                                       wqkv=t[p + "self_attn.qkv_proj.weight"], wo=t[p + "self_attn.o_proj.weight"],
+                                       mlp_norm=t[p + "post_attention_layernorm.weight"],
+                                       w13=t[p + "mlp.gate_up_proj.weight"], w2=t[p + "mlp.down_proj.weight"]))
+        return cls(cfg=cfg, embed=t["model.embed_tokens.weight"], layers=layers, final_norm=t["model.norm.weight"],
+                   lm_head=t["lm_head.weight"])
+
     def named_tensors(self):
         """(name, tensor) in HF-style naming with fused qkv / gate_up tensors."""
         yield "model.embed_tokens.weight", self.embed
@@ -125,6 +156,39 @@ class LlamaWeights:
             yield p + "mlp.down_proj.weight", lw.w2
         yield "model.norm.weight", self.final_norm
         yield "lm_head.weight", self.lm_head
+
+
+def trainer_layout(cfg: LlamaConfig):
+    """``(name, shape)`` of the unfused HF checkpoint tensors a trainer holds."""
+    yield "model.embed_tokens.weight", (cfg.vocab_size, cfg.hidden)
+    for i in range(cfg.layers):
+        p = f"model.layers.{i}."
+        yield p + "input_layernorm.weight", (cfg.hidden,)
+        yield p + "self_attn.q_proj.weight", (cfg.heads * cfg.head_dim, cfg.hidden)
+        yield p + "self_attn.k_proj.weight", (cfg.kv_heads * cfg.head_dim, cfg.hidden)
+        yield p + "self_attn.v_proj.weight", (cfg.kv_heads * cfg.head_dim, cfg.hidden)
+        yield p + "self_attn.o_proj.weight", (cfg.hidden, cfg.heads * cfg.head_dim)
+        yield p + "post_attention_layernorm.weight", (cfg.hidden,)
+        yield p + "mlp.gate_proj.weight", (cfg.ffn, cfg.hidden)
+        yield p + "mlp.up_proj.weight", (cfg.ffn, cfg.hidden)
+        yield p + "mlp.down_proj.weight", (cfg.hidden, cfg.ffn)
+    yield "model.norm.weight", (cfg.hidden,)
+    yield "lm_head.weight", (cfg.vocab_size, cfg.hidden)
+
+
+def random_trainer_weights(cfg: LlamaConfig, device, dtype=torch.float32, seed: int = 0, std: float = 0.02):
+    """Random unfused HF-named weights (e.g. a trainer's fp32 master copy)."""
+    g = torch.Generator(device=device)
+    g.manual_seed(seed)
+    out = {}
+    for name, shape in trainer_layout(cfg):
+        t = torch.empty(shape, dtype=dtype, device=device)
+        if "norm" in name:
+            t.uniform_(0.5, 1.5, generator=g)
+        else:
+            t.normal_(0.0, std, generator=g)
+        out[name] = t
+    return out
 
 
 class PagedKVCache:
