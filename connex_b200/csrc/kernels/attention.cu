@@ -52,7 +52,9 @@ __global__ void __launch_bounds__(dec::THREADS)
     qs[h][d] = __bfloat162float(q[(size_t)b * ldq + (size_t)(g * G + h) * D + d]) * scale_log2;
   }
   __syncthreads();
-  // phase 1: logits.  4 threads per token, 32 dims each.
+  // phase 1: logits.  4 threads per token; thread `sub` takes dims
+  // v*32 + sub*8 + [0, 8) for v = 0..3, so the 4 threads of a token read q
+  // from 4 different shared-memory banks (no conflicts; tokens broadcast).
   {
     const int sub = tid & 3;
     for (int base = 0; base < n; base += THREADS / 4) {
@@ -63,15 +65,17 @@ __global__ void __launch_bounds__(dec::THREADS)
       if (tl < n) {
         const int t = t0 + tl;
         const int blk = bt[t / BS];
-        const __nv_bfloat16* kr = kc + (((size_t)blk * Hkv + g) * BS + (t % BS)) * D + sub * 32;
+        const __nv_bfloat16* kr = kc + (((size_t)blk * Hkv + g) * BS + (t % BS)) * D + sub * 8;
+        u128 kv4[4];
+#pragma unroll
+        for (int v = 0; v < 4; ++v) kv4[v] = ld_nc_v4(kr + v * 32);
 #pragma unroll
         for (int v = 0; v < 4; ++v) {
-          u128 kv = ld_nc_v4(kr + v * 8);
-          const uint32_t* pk = reinterpret_cast<const uint32_t*>(&kv);
+          const uint32_t* pk = reinterpret_cast<const uint32_t*>(&kv4[v]);
 #pragma unroll
           for (int j = 0; j < 4; ++j) {
             const float a = bf16_lo(pk[j]), c = bf16_hi(pk[j]);
-            const int d = sub * 32 + v * 8 + 2 * j;
+            const int d = v * 32 + sub * 8 + 2 * j;
 #pragma unroll
             for (int h = 0; h < G; ++h) acc[h] += a * qs[h][d] + c * qs[h][d + 1];
           }
@@ -115,22 +119,36 @@ __global__ void __launch_bounds__(dec::THREADS)
     for (int h = 0; h < G; ++h)
 #pragma unroll
       for (int e = 0; e < 8; ++e) acc[h][e] = 0.f;
-    for (int tl = tp; tl < n; tl += 8) {
-      const int t = t0 + tl;
-      const int blk = bt[t / BS];
-      u128 vv = ld_nc_v4(vc + (((size_t)blk * Hkv + g) * BS + (t % BS)) * D + dg * 8);
-      const uint32_t* pv = reinterpret_cast<const uint32_t*>(&vv);
-      float vf[8];
+    constexpr int VU = 4;  // V rows in flight per thread
+    for (int tl0 = tp; tl0 < n; tl0 += 8 * VU) {
+      u128 vv[VU];
 #pragma unroll
-      for (int j = 0; j < 4; ++j) {
-        vf[2 * j] = bf16_lo(pv[j]);
-        vf[2 * j + 1] = bf16_hi(pv[j]);
+      for (int u = 0; u < VU; ++u) {
+        const int tl = tl0 + 8 * u;
+        if (tl < n) {
+          const int t = t0 + tl;
+          const int blk = bt[t / BS];
+          vv[u] = ld_nc_v4(vc + (((size_t)blk * Hkv + g) * BS + (t % BS)) * D + dg * 8);
+        }
       }
 #pragma unroll
-      for (int h = 0; h < G; ++h) {
-        const float p = lg[h][tl];
+      for (int u = 0; u < VU; ++u) {
+        const int tl = tl0 + 8 * u;
+        if (tl < n) {
+          const uint32_t* pv = reinterpret_cast<const uint32_t*>(&vv[u]);
+          float vf[8];
 #pragma unroll
-        for (int e = 0; e < 8; ++e) acc[h][e] += p * vf[e];
+          for (int j = 0; j < 4; ++j) {
+            vf[2 * j] = bf16_lo(pv[j]);
+            vf[2 * j + 1] = bf16_hi(pv[j]);
+          }
+#pragma unroll
+          for (int h = 0; h < G; ++h) {
+            const float p = lg[h][tl];
+#pragma unroll
+            for (int e = 0; e < 8; ++e) acc[h][e] += p * vf[e];
+          }
+        }
       }
     }
 #pragma unroll
