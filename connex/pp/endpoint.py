@@ -144,10 +144,8 @@ class PipelineEndpoint:
         if self.data == "engine":
             self._setup_ring(ring_bytes)
         self._stop = threading.Event()
-        if membership is not None and hasattr(membership, "on_event"):
-            from connex.front_router import EventType
-            for ev in (EventType.ENDPOINT_DEREGISTERED, EventType.ENDPOINT_UNHEALTHY):
-                membership.on_event(ev, self._on_membership_event)
+        if membership is not None:
+            self.attach_membership(membership)
         self._io = threading.Thread(target=self._io_loop, name=f"cx-pp-io-{stage_idx}", daemon=True)
         self._io.start()
 
@@ -377,11 +375,25 @@ class PipelineEndpoint:
     def on_peer_alive(self, stage_idx: int, replica_idx: int) -> None:
         self.deregistered.discard((stage_idx, replica_idx))
 
+    def attach_membership(self, membership) -> None:
+        """Route with ``membership`` and follow its deregister / register events."""
+        self.membership = membership
+        if hasattr(membership, "on_event"):
+            from connex.front_router import EventType
+            for ev in (EventType.ENDPOINT_DEREGISTERED, EventType.ENDPOINT_UNHEALTHY):
+                membership.on_event(ev, self._on_membership_event)
+            membership.on_event(EventType.ENDPOINT_REGISTERED, self._on_membership_join)
+
     def _on_membership_event(self, ev) -> None:
         payload = getattr(ev, "payload", {}) or {}
         lid = payload.get("lid") or {}
         if "stage_idx" in lid:
             self.on_peer_dead(lid["stage_idx"], lid.get("replica_idx", 0), payload.get("reason", "event"))
+
+    def _on_membership_join(self, ev) -> None:
+        lid = (getattr(ev, "payload", {}) or {}).get("lid") or {}
+        if "stage_idx" in lid:
+            self.on_peer_alive(lid["stage_idx"], lid.get("replica_idx", 0))
 
     def confirm_peer_failure(self) -> bool:
         """After a timeout: probe the downstream; a refused connect confirms death."""

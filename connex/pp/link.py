@@ -126,6 +126,11 @@ class StageWorker:
         td, ctx = self.t.recv_forward()
         if td is None:
             return False
+        self.serve(td, ctx)
+        return True
+
+    def serve(self, td: dict, ctx) -> None:
+        """Process one received step (``recv_forward`` output) and send it on."""
         self.stats["steps"] += 1
         rids = td.get(REQUEST_IDS) or []
         fin = td.get(FINISHED)
@@ -152,4 +157,3 @@ class StageWorker:
                 if k in td and k not in out:
                     out[k] = td[k]
         self.t.send_reply(out, ctx)
-        return True

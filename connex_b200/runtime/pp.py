@@ -1,0 +1,212 @@
+"""Elastic pipeline-parallel serving of the Llama decoder on sm_100a.
+
+A pipeline stage owns layers ``[l0, l1)`` of the model (their weights and
+their paged KV cache); stage 0 also owns the embedding, the last stage the
+final norm, LM head and the greedy sampler.  Between stages only the
+residual stream ``x`` ([tokens, hidden] bf16) travels, over the endpoint's
+data plane (elastic NCCL pair links inside a box).
+
+:class:`StageRuntime` is a stage's compute for the step protocol: a step
+carries ``request_ids``, ``cx_ctx`` (tokens of each request already in the
+KV cache before this step) and ``n_new`` (tokens of each request in this
+step: the prompt for a prefill, 1 for a decode).  A stage allocates KV
+blocks per request on demand and answers ``kv_held`` for the handover rules,
+so after a failover the rows whose KV is not here come back as
+``cx_missing`` and stage 0 prefills them again (reference semantics:
+``connex/pp/handover.py``, ``connex/pp/link.py``).
+
+Weights are random N(0, 0.02) per layer from ``seed + layer`` so a split
+model equals the unsplit one layer for layer (tests compare them).
+"""
+from __future__ import annotations
+
+from typing import Dict, List, Optional, Sequence
+
+import torch
+
+from connex.pp.handover import CX_CTX, REQUEST_IDS
+from connex_b200 import ops
+from connex_b200.models.llama import LayerWeights, LlamaConfig, LlamaModel, LlamaWeights, PagedKVCache
+
+
+def layer_weights(cfg: LlamaConfig, layer: int, device, seed: int = 0, std: float = 0.02) -> LayerWeights:
+    g = torch.Generator(device=device)
+    g.manual_seed(seed * 1000 + layer + 1)
+
+    def rnd(*shape):
+        t = torch.empty(*shape, dtype=torch.bfloat16, device=device)
+        t.normal_(0.0, std, generator=g)
+        return t
+    ones = torch.ones(cfg.hidden, dtype=torch.bfloat16, device=device)
+    gate, up = rnd(cfg.ffn, cfg.hidden), rnd(cfg.ffn, cfg.hidden)
+    return LayerWeights(attn_norm=ones, wqkv=rnd(cfg.qkv_dim, cfg.hidden), wo=rnd(cfg.hidden, cfg.heads * cfg.head_dim),
+                        mlp_norm=ones.clone(), w13=ops.interleave_gate_up(gate, up), w2=rnd(cfg.hidden, cfg.ffn))
+
+
+def stage_weights(cfg: LlamaConfig, l0: int, l1: int, device, seed: int = 0, std: float = 0.02) -> LlamaWeights:
+    g = torch.Generator(device=device)
+    g.manual_seed(seed * 1000 + 999)
+
+    def rnd(*shape):
+        t = torch.empty(*shape, dtype=torch.bfloat16, device=device)
+        t.normal_(0.0, std, generator=g)
+        return t
+    embed = rnd(cfg.vocab_size, cfg.hidden)            # same draw order on every stage
+    head = rnd(cfg.vocab_size, cfg.hidden)
+    return LlamaWeights(cfg=cfg, embed=embed if l0 == 0 else None,
+                        layers=[layer_weights(cfg, l, device, seed, std) for l in range(l0, l1)],
+                        final_norm=torch.ones(cfg.hidden, dtype=torch.bfloat16, device=device) if l1 == cfg.layers
+                        else None, lm_head=head if l1 == cfg.layers else None)
+
+
+class StageModel(LlamaModel):
+    """Layers ``[l0, l1)`` of the decoder on their own KV cache."""
+
+    def __init__(self, weights: LlamaWeights, l0: int, l1: int, cache: PagedKVCache, max_tokens: int,
+                 max_batch: int = 256, device=None):
+        self.l0, self.l1 = l0, l1
+        self.first, self.last = l0 == 0, l1 == weights.cfg.layers
+        dev = torch.device(device) if device is not None else weights.layers[0].wqkv.device
+        if weights.embed is None:          # LlamaModel reads the device from the embedding
+            weights.embed = torch.empty(0, weights.cfg.hidden, dtype=torch.bfloat16, device=dev)
+        super().__init__(weights, cache, max_tokens, max_batch)
+
+    def _next_norm(self, i: int):
+        if i + 1 < len(self.w.layers):
+            return self.w.layers[i + 1].attn_norm
+        return self.w.final_norm if self.last else None
+
+    def _tail(self, i: int, T: int) -> None:
+        cfg, lw = self.cfg, self.w.layers[i]
+        x, h = self.x[:T], self.h[:T]
+        ops.gemm(self.attn[:T], lw.wo, x, residual=x, status=self.status)
+        ops.rmsnorm(x, lw.mlp_norm, cfg.eps, out=h)
+        ops.gemm(h, lw.w13, self.mid[:T], silu_mul=True, status=self.status)
+        ops.gemm(self.mid[:T], lw.w2, x, residual=x, status=self.status)
+        nw = self._next_norm(i)
+        if nw is not None:
+            ops.rmsnorm(x, nw, self.cfg.eps, out=h)
+
+    def _enter(self, inp: torch.Tensor, T: int) -> None:
+        if self.first:
+            ops.embedding(inp, self.w.embed, self.x[:T], status=self.status)
+        else:
+            self.x[:T].copy_(inp)
+        ops.rmsnorm(self.x[:T], self.w.layers[0].attn_norm, self.cfg.eps, out=self.h[:T])
+
+    def run(self, inp: torch.Tensor, positions, slots, *, prefill: bool, tile_info=None, block_tables=None,
+            ctx_lens=None, max_ctx: int = 0, workspace=None, rows=None, B: int = 0):
+        """Ids (first stage) or the residual stream in; the residual stream
+        (``x[:T]``) or, on the last stage, the greedy next ids of ``rows`` out."""
+        cfg, T = self.cfg, inp.shape[0]
+        assert T <= self.max_tokens
+        self._enter(inp, T)
+        for i, lw in enumerate(self.w.layers):
+            qkv = self.qkv[:T]
+            ops.gemm(self.h[:T], lw.wqkv, qkv, status=self.status)
+            ops.rope_cache(qkv, positions, self.cos_sin, cfg.heads, cfg.kv_heads, slots, self.cache.k(i),
+                           self.cache.v(i), status=self.status)
+            if prefill:
+                ops.prefill_attention(qkv, tile_info, cfg.heads, cfg.kv_heads, out=self.attn[:T])
+            else:
+                ops.decode_attention(qkv, self.cache.k(i), self.cache.v(i), block_tables, ctx_lens, cfg.heads,
+                                     max_ctx, workspace, out=self.attn[:T])
+            self._tail(i, T)
+        if self.last:
+            return self._head(rows, B)
+        return self.x[:T]
+
+
+class StageRuntime:
+    """One stage's compute for the step protocol (``StageWorker`` compute + hooks)."""
+
+    def __init__(self, cfg: LlamaConfig, l0: int, l1: int, device, num_blocks: int, max_tokens: int,
+                 max_batch: int = 256, max_ctx: int = 8192, seed: int = 0):
+        self.cfg = cfg
+        self.device = torch.device(device)
+        self.weights = stage_weights(cfg, l0, l1, self.device, seed)
+        stage_cfg = LlamaConfig(**{**cfg.__dict__, "layers": l1 - l0})
+        self.cache = PagedKVCache(stage_cfg, num_blocks, self.device)
+        self.model = StageModel(self.weights, l0, l1, self.cache, max_tokens, max_batch, self.device)
+        self.model.cfg = cfg
+        self.bs = cfg.block_size
+        self.max_ctx = max_ctx
+        self.tables: Dict[object, List[int]] = {}
+        self.held: Dict[object, int] = {}
+        self.ws = ops.decode_workspace(max_batch, cfg.heads, max_ctx, self.device)
+        self.steps = 0
+
+    # EngineHooks
+    def kv_held(self, rid) -> int:
+        return self.held.get(rid, 0)
+
+    def release(self, rids) -> None:
+        for r in rids:
+            self.held.pop(r, None)
+            self.cache.free(self.tables.pop(r, []))
+
+    def reprefill(self, rids) -> None:
+        pass
+
+    def abort(self, rids) -> None:
+        self.release(rids)
+
+    def _blocks_for(self, rid, upto: int) -> List[int]:
+        t = self.tables.setdefault(rid, [])
+        need = -(-upto // self.bs)
+        if len(t) < need:
+            t += self.cache.allocate(need - len(t))
+        return t
+
+    def compute(self, td: dict, missing: Sequence) -> dict:
+        rids = list(td[REQUEST_IDS])
+        ctx = list(td[CX_CTX])
+        n_new = list(td["n_new"])
+        prefill = td["kind"] == "prefill"
+        miss = set(missing)
+        pos, slots, lens = [], [], []
+        for r, c, n in zip(rids, ctx, n_new):
+            if r in miss:
+                self.release([r])
+            t = self._blocks_for(r, c + n)
+            for p in range(c, c + n):
+                pos.append(p)
+                slots.append(t[p // self.bs] * self.bs + p % self.bs)
+            lens.append(c + n)
+        dev = self.device
+        positions = torch.tensor(pos, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
+        slot_t = torch.tensor(slots, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
+        B = len(rids)
+        inp = td["ids"] if self.model.first else td["x"]
+        kw = {}
+        if prefill:
+            rows, start, q0s = [], 0, []
+            for r, c, n in zip(rids, ctx, n_new):
+                if c:
+                    raise NotImplementedError("prefill continuation (chunked prefill) is not supported")
+                rows.append(start + n - 1)
+                start += n
+            kw["tile_info"] = ops.prefill_tile_info(n_new, dev)
+            kw["rows"] = torch.tensor(rows, dtype=torch.int64, device=dev)
+        else:
+            mb = -(-max(lens) // self.bs)
+            bt = torch.zeros(B, mb, dtype=torch.int32)
+            for i, r in enumerate(rids):
+                t = self.tables[r]
+                bt[i, :len(t)] = torch.tensor(t[:mb], dtype=torch.int32)
+            kw.update(block_tables=bt.pin_memory().to(dev, non_blocking=True),
+                      ctx_lens=torch.tensor(lens, dtype=torch.int32).pin_memory().to(dev, non_blocking=True),
+                      max_ctx=max(lens), workspace=self.ws,
+                      rows=torch.arange(B, dtype=torch.int64, device=dev))
+        out = self.model.run(inp, positions, slot_t, prefill=prefill, B=B, **kw)
+        for r, c, n in zip(rids, ctx, n_new):
+            if r in miss:           # computed without its KV: not held here; stage 0 prefills it again
+                self.release([r])
+            else:
+                self.held[r] = c + n
+        self.steps += 1
+        res = {"kind": td["kind"], "n_new": n_new}
+        # a copy: the model's buffers are rewritten by the next step while the
+        # link may still be sending this one
+        res["next" if self.model.last else "x"] = out.clone()
+        return res
