@@ -35,7 +35,8 @@ int row_ld(const at::Tensor& t) {
 
 // D = A . B^T (+ R) | SiLU-mul epilogue.  A [M,K], B [N,K], D [M,N or N/2].
 void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10::optional<at::Tensor>& R, int64_t epi,
-          int64_t bn, const c10::optional<at::Tensor>& status, int64_t max_ctas) {
+          int64_t bn, const c10::optional<at::Tensor>& status, int64_t max_ctas,
+          const c10::optional<at::Tensor>& workspace, int64_t splits) {
   CHECK_CUDA(A);
   CHECK_CUDA(B);
   CHECK_CUDA(D);
@@ -59,8 +60,19 @@ void gemm(const at::Tensor& A, const at::Tensor& B, at::Tensor& D, const c10::op
     ldr = row_ld(*R);
   }
   if (M == 0) return;
+  float* W = nullptr;
+  if (splits > 1) {
+    TORCH_CHECK(workspace.has_value() && workspace->is_cuda() && workspace->scalar_type() == at::kFloat &&
+                    workspace->is_contiguous() && workspace->numel() >= (int64_t)M * N,
+                "gemm: split-K needs a contiguous fp32 CUDA workspace of at least M*N elements (kept zero)");
+    W = workspace->data_ptr<float>();
+  }
   cx::gemm_bf16_tn(A.data_ptr(), B.data_ptr(), D.data_ptr(), rp, M, N, K, row_ld(A), row_ld(B), row_ld(D), ldr,
-                   (int)epi, (int)bn, status_ptr(status), (int)max_ctas, cur_stream(A));
+                   (int)epi, (int)bn, status_ptr(status), (int)max_ctas, cur_stream(A), W, (int)splits);
+}
+
+int64_t gemm_splits(int64_t M, int64_t N, int64_t K, int64_t epi, int64_t bn) {
+  return cx::gemm_splits((int)M, (int)N, (int)K, (int)epi, (int)bn);
 }
 
 void rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual, const at::Tensor& w, at::Tensor& out,
@@ -83,8 +95,18 @@ void rmsnorm(const at::Tensor& x, const c10::optional<at::Tensor>& residual, con
 
 void rope_cache(at::Tensor& qkv, const at::Tensor& pos, const at::Tensor& cos_sin,
                 const c10::optional<at::Tensor>& slots, const c10::optional<at::Tensor>& kc,
-                const c10::optional<at::Tensor>& vc, int64_t Hq, int64_t Hkv, const c10::optional<at::Tensor>& status) {
+                const c10::optional<at::Tensor>& vc, int64_t Hq, int64_t Hkv, const c10::optional<at::Tensor>& status,
+                const c10::optional<at::Tensor>& q_norm, const c10::optional<at::Tensor>& k_norm, double eps) {
   CHECK_BF16(qkv);
+  const void* qn = nullptr;
+  const void* kn = nullptr;
+  for (const auto* w : {&q_norm, &k_norm})
+    if (w->has_value())
+      TORCH_CHECK((*w)->is_cuda() && (*w)->scalar_type() == at::kBFloat16 && (*w)->numel() == 128 &&
+                      (*w)->is_contiguous(),
+                  "rope_cache: q/k norm weights must be contiguous bf16 CUDA [128]");
+  if (q_norm.has_value()) qn = q_norm->data_ptr();
+  if (k_norm.has_value()) kn = k_norm->data_ptr();
   TORCH_CHECK(pos.scalar_type() == at::kInt, "positions must be int32");
   TORCH_CHECK(cos_sin.scalar_type() == at::kFloat, "cos_sin must be fp32");
   const c10::cuda::CUDAGuard g(qkv.device());
@@ -102,7 +124,7 @@ void rope_cache(at::Tensor& qkv, const at::Tensor& pos, const at::Tensor& cos_si
   }
   cx::rope_cache(qkv.data_ptr(), row_ld(qkv), pos.data_ptr<int>(), cos_sin.data_ptr<float>(), sp, kp, vp,
                  (int)qkv.size(0), (int)Hq, (int)Hkv, 128, BS, nb, (int)cos_sin.size(0), status_ptr(status),
-                 cur_stream(qkv));
+                 cur_stream(qkv), qn, kn, (float)eps);
 }
 
 void embedding(const at::Tensor& ids, const at::Tensor& table, at::Tensor& out,
@@ -341,9 +363,12 @@ at::Tensor from_ptr(int64_t ptr, std::vector<int64_t> shape, at::ScalarType dtyp
 PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.doc() = "connex_b200 sm_100a kernels";
   m.def("gemm", &gemm, py::arg("A"), py::arg("B"), py::arg("D"), py::arg("R") = py::none(), py::arg("epi") = 0,
-        py::arg("bn") = 0, py::arg("status") = py::none(), py::arg("max_ctas") = 0);
+        py::arg("bn") = 0, py::arg("status") = py::none(), py::arg("max_ctas") = 0,
+        py::arg("workspace") = py::none(), py::arg("splits") = 1);
   m.def("rmsnorm", &rmsnorm);
-  m.def("rope_cache", &rope_cache);
+  m.def("rope_cache", &rope_cache, py::arg("qkv"), py::arg("pos"), py::arg("cos_sin"), py::arg("slots"),
+        py::arg("kc"), py::arg("vc"), py::arg("Hq"), py::arg("Hkv"), py::arg("status") = py::none(),
+        py::arg("q_norm") = py::none(), py::arg("k_norm") = py::none(), py::arg("eps") = 1e-6);
   m.def("embedding", &embedding);
   m.def("argmax", &argmax);
   m.def("gather_rows", &gather_rows);
@@ -351,6 +376,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_attention", &decode_attention);
   m.def("decode_workspace_floats", &decode_workspace_floats);
   m.def("kv_push_layer", &kv_push_layer);
+  m.def("gemm_splits", &gemm_splits);
   m.def("copy_segments", &copy_segments);
   m.def("wsync", &wsync);
   m.attr("WS_JOB_COLS") = cx::WS_JOB_COLS;

@@ -14,8 +14,12 @@ enum GemmEpilogue : int {
 
 // D[M,N] (ld ldd) = A[M,K] (ld lda) . B[N,K]^T (ld ldb); bf16 in/out, fp32 accumulate.
 // bn = 0 picks the tile width.  status: int32 device word (0 = ok).
+// splits > 1: split-K into W (fp32 [M, N], zero on entry, left zero) + a finalize kernel.
 void gemm_bf16_tn(const void* A, const void* B, void* D, const void* R, int M, int N, int K, int lda, int ldb,
-                  int ldd, int ldr, int epi, int bn, int* status, int max_ctas, cudaStream_t stream);
+                  int ldd, int ldr, int epi, int bn, int* status, int max_ctas, cudaStream_t stream,
+                  float* W = nullptr, int splits = 1);
+// The K split gemm_bf16_tn would profit from (1 = none).
+int gemm_splits(int M, int N, int K, int epi, int bn);
 
 CUtensorMap make_tmap_bf16_2d(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
                               uint32_t box_inner, uint32_t box_outer, bool swizzle128);

@@ -21,6 +21,7 @@
 #include "common.cuh"
 #include "gemm.h"
 
+#include <algorithm>
 #include <cstdio>
 #include <mutex>
 #include <stdexcept>
@@ -52,13 +53,29 @@ __device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& tm
   tn = r / gm;
 }
 
+__device__ __forceinline__ void tile_coords_split(int t, int num_m, int num_n, int splits, int& tm, int& tn,
+                                                  int& ks) {
+  const int tt = t / splits;
+  ks = t - tt * splits;
+  tile_coords(tt, num_m, num_n, tm, tn);
+}
+
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
 
-template <int BN, int STAGES, int EPI>
+// Vector fp32 reduction into global memory (split-K partial sums).
+__device__ __forceinline__ void red_add_v4_f32(float* p, float a, float b, float c, float d) {
+  asm volatile("red.global.add.v4.f32 [%0], {%1,%2,%3,%4};" ::"l"(p), "f"(a), "f"(b), "f"(c), "f"(d) : "memory");
+}
+
+// SPLIT: the K loop of each output tile is cut into `splits` chunks of `kper`
+// k-blocks, one work item each, and the epilogue adds the fp32 partial sums
+// into W (zero on entry) with vector reductions; gemm_splitk_finalize applies
+// the epilogue.  Small-M (decode) GEMMs get enough work items to fill the SMs.
+template <int BN, int STAGES, int EPI, bool SPLIT>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         __nv_bfloat16* __restrict__ D, const __nv_bfloat16* R, int M, int N, int K, int ldd,
-                        int ldr, int* status) {
+                        int ldr, int* status, float* __restrict__ W, int ldw, int splits, int kper) {
   using Cfg = GemmCfg<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -75,7 +92,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   const int lane = lane_id();
   const int num_m = (M + GEMM_BM - 1) / GEMM_BM;
   const int num_n = (N + BN - 1) / BN;
-  const int total = num_m * num_n;
+  const int total = num_m * num_n * splits;
   const int nk = (K + GEMM_BK - 1) / GEMM_BK;
 
   if (warp == 0 && lane == 0) {
@@ -106,9 +123,10 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     if (lane == 0) {
       uint32_t stage = 0, phase = 0;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
-        int tm, tn;
-        tile_coords(t, num_m, num_n, tm, tn);
-        for (int kb = 0; kb < nk; ++kb) {
+        int tm, tn, ks;
+        tile_coords_split(t, num_m, num_n, splits, tm, tn, ks);
+        const int kb0 = ks * kper, kb1 = min(nk, kb0 + kper);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, status)) {
             ok = false;
             break;
@@ -140,7 +158,9 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
         }
         tc_fence_after();
         const uint32_t d = tmem_base + acc * BN;
-        for (int kb = 0; kb < nk; ++kb) {
+        const int ks = t % splits;
+        const int kb0 = ks * kper, kb1 = min(nk, kb0 + kper);
+        for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&full[stage], phase, status)) {
             ok = false;
             break;
@@ -151,7 +171,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
 #pragma unroll
           for (int k = 0; k < GEMM_BK / 16; ++k) {
             umma_bf16(d, umma_desc_sw128(a0 + k * 32), umma_desc_sw128(b0 + k * 32), IDESC,
-                      (kb | k) != 0 ? 1u : 0u);
+                      (kb != kb0 || k != 0) ? 1u : 0u);
           }
           issued = true;
           umma_commit(&empty[stage]);
@@ -177,13 +197,29 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     const int q = warp & 3;
     uint32_t acc = 0, acc_phase = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
-      int tm, tn;
-      tile_coords(t, num_m, num_n, tm, tn);
+      int tm, tn, ks;
+      tile_coords_split(t, num_m, num_n, splits, tm, tn, ks);
       if (!mbar_wait(&tfull[acc], acc_phase, status)) break;
       tc_fence_after();
       const int row = tm * GEMM_BM + q * 32 + lane;
       const uint32_t tb = tmem_base + acc * BN + ((uint32_t)(q * 32) << 16);
-      if constexpr (EPI == EPI_SILU_MUL) {
+      if constexpr (SPLIT) {
+#pragma unroll 1
+        for (int c = 0; c < BN / 32; ++c) {
+          uint32_t r[32];
+          tmem_ld32(tb + c * 32, r);
+          tmem_ld_wait();
+          const int col = tn * BN + c * 32;
+          if (row < M) {
+            float* dst = W + (size_t)row * ldw + col;
+#pragma unroll
+            for (int v = 0; v < 8; ++v)
+              if (col + v * 4 < N)
+                red_add_v4_f32(dst + v * 4, __uint_as_float(r[4 * v]), __uint_as_float(r[4 * v + 1]),
+                               __uint_as_float(r[4 * v + 2]), __uint_as_float(r[4 * v + 3]));
+          }
+        }
+      } else if constexpr (EPI == EPI_SILU_MUL) {
         constexpr int HALF = BN / 2;
 #pragma unroll 1
         for (int c = 0; c < HALF / 32; ++c) {
@@ -255,6 +291,50 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
   }
 }
 
+// D = epilogue(W) for a split-K GEMM; W is read once and left zero for the next call.
+template <int EPI>
+__global__ void __launch_bounds__(256) gemm_splitk_finalize(float* __restrict__ W, int ldw, __nv_bfloat16* D, int ldd,
+                                                            const __nv_bfloat16* R, int ldr, int M, int Nout) {
+  const int per_row = Nout / 8;
+  const long total = (long)M * per_row;
+  for (long i = blockIdx.x * (long)blockDim.x + threadIdx.x; i < total; i += (long)gridDim.x * blockDim.x) {
+    const int row = (int)(i / per_row), c8 = (int)(i - (long)row * per_row) * 8;
+    float v[8];
+    float* w = W + (size_t)row * ldw;
+    if constexpr (EPI == EPI_SILU_MUL) {
+      const int base = (c8 / 128) * 256 + (c8 % 128);   // gate / up rows interleaved per 256-wide tile
+      float4* g = reinterpret_cast<float4*>(w + base);
+      float4* u = reinterpret_cast<float4*>(w + base + 128);
+      const float4 g0 = g[0], g1 = g[1], u0 = u[0], u1 = u[1];
+      const float gg[8] = {g0.x, g0.y, g0.z, g0.w, g1.x, g1.y, g1.z, g1.w};
+      const float uu[8] = {u0.x, u0.y, u0.z, u0.w, u1.x, u1.y, u1.z, u1.w};
+#pragma unroll
+      for (int j = 0; j < 8; ++j) v[j] = silu(gg[j]) * uu[j];
+      g[0] = g[1] = u[0] = u[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+    } else {
+      float4* p = reinterpret_cast<float4*>(w + c8);
+      const float4 a = p[0], b = p[1];
+      v[0] = a.x; v[1] = a.y; v[2] = a.z; v[3] = a.w; v[4] = b.x; v[5] = b.y; v[6] = b.z; v[7] = b.w;
+      p[0] = p[1] = make_float4(0.f, 0.f, 0.f, 0.f);
+      if constexpr (EPI == EPI_ADD) {
+        const u128 rv = ld_v4(R + (size_t)row * ldr + c8);
+        const uint32_t* rr = reinterpret_cast<const uint32_t*>(&rv);
+#pragma unroll
+        for (int j = 0; j < 4; ++j) {
+          v[2 * j] += bf16_lo(rr[j]);
+          v[2 * j + 1] += bf16_hi(rr[j]);
+        }
+      }
+    }
+    u128 o;
+    o.x = pack_bf16x2(v[0], v[1]);
+    o.y = pack_bf16x2(v[2], v[3]);
+    o.z = pack_bf16x2(v[4], v[5]);
+    o.w = pack_bf16x2(v[6], v[7]);
+    st_v4(D + (size_t)row * ldd + c8, o);
+  }
+}
+
 // ------------------------------------------------------------------ host side
 using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType, cuuint32_t, void*, const cuuint64_t*,
                                    const cuuint64_t*, const cuuint32_t*, const cuuint32_t*, CUtensorMapInterleave,
@@ -301,11 +381,12 @@ int num_sms() {
   return n;
 }
 
-template <int BN, int STAGES, int EPI>
+template <int BN, int STAGES, int EPI, bool SPLIT = false>
 static void launch_gemm(const void* A, const void* B, void* D, const void* R, int M, int N, int K, int lda, int ldb,
-                        int ldd, int ldr, int* status, int max_ctas, cudaStream_t stream) {
+                        int ldd, int ldr, int* status, int max_ctas, cudaStream_t stream, float* W = nullptr,
+                        int splits = 1, int kper = 0) {
   using Cfg = GemmCfg<BN, STAGES>;
-  auto kern = gemm_bf16_tn_kernel<BN, STAGES, EPI>;
+  auto kern = gemm_bf16_tn_kernel<BN, STAGES, EPI, SPLIT>;
   static bool attr_set[64] = {false};
   int dev;
   cudaGetDevice(&dev);
@@ -315,16 +396,33 @@ static void launch_gemm(const void* A, const void* B, void* D, const void* R, in
   }
   CUtensorMap ta = make_tmap_bf16_2d(A, (uint64_t)K, (uint64_t)M, (uint64_t)lda * 2, GEMM_BK, GEMM_BM, true);
   CUtensorMap tb = make_tmap_bf16_2d(B, (uint64_t)K, (uint64_t)N, (uint64_t)ldb * 2, GEMM_BK, BN, true);
-  const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * ((N + BN - 1) / BN);
+  const int tiles = ((M + GEMM_BM - 1) / GEMM_BM) * ((N + BN - 1) / BN) * splits;
   int grid = tiles < num_sms() ? tiles : num_sms();
   if (max_ctas > 0 && grid > max_ctas) grid = max_ctas;
+  if (kper <= 0) kper = (K + GEMM_BK - 1) / GEMM_BK;
   kern<<<grid, GEMM_THREADS, Cfg::SMEM, stream>>>(ta, tb, reinterpret_cast<__nv_bfloat16*>(D),
                                                    reinterpret_cast<const __nv_bfloat16*>(R), M, N, K, ldd, ldr,
-                                                   status);
+                                                   status, W, N, splits, kper);
+}
+
+// Work-item split of the K loop: only when the output tiles alone would
+// leave most SMs idle (small-M decode GEMMs) and K is long enough.
+int gemm_splits(int M, int N, int K, int epi, int bn) {
+  if (bn == 0) bn = epi == EPI_SILU_MUL ? 256 : 128;
+  const long tiles = (long)((M + GEMM_BM - 1) / GEMM_BM) * ((N + bn - 1) / bn);
+  const int nk = (K + GEMM_BK - 1) / GEMM_BK;
+  const int sms = num_sms();
+  if (tiles * 2 > sms || nk < 8) return 1;
+  int s = (int)(sms / tiles);
+  if (s > nk / 4) s = nk / 4;
+  if (s < 2) return 1;
+  const int kper = (nk + s - 1) / s;
+  return (nk + kper - 1) / kper;  // no empty split
 }
 
 void gemm_bf16_tn(const void* A, const void* B, void* D, const void* R, int M, int N, int K, int lda, int ldb,
-                  int ldd, int ldr, int epi, int bn, int* status, int max_ctas, cudaStream_t stream) {
+                  int ldd, int ldr, int epi, int bn, int* status, int max_ctas, cudaStream_t stream, float* W,
+                  int splits) {
   if (K % 8 != 0) throw std::runtime_error("cx gemm: K must be a multiple of 8");
   if ((lda | ldb | ldd) % 8 != 0 || (R != nullptr && ldr % 8 != 0))
     throw std::runtime_error("cx gemm: leading dimensions must be multiples of 8 elements");
@@ -339,6 +437,31 @@ void gemm_bf16_tn(const void* A, const void* B, void* D, const void* R, int M, i
   }
   if (epi == EPI_SILU_MUL && (N % bn) != 0)
     throw std::runtime_error("cx gemm: SiLU-mul epilogue needs N to be a multiple of the tile width");
+  if (splits > 1) {
+    if (W == nullptr || ((uintptr_t)W & 15)) throw std::runtime_error("cx gemm: split-K needs a 16-byte aligned workspace");
+    const int sbn = epi == EPI_SILU_MUL ? 256 : 128;
+    const int nk = (K + GEMM_BK - 1) / GEMM_BK;
+    const int kper = (nk + splits - 1) / splits;
+    splits = (nk + kper - 1) / kper;
+    if (sbn == 256)
+      launch_gemm<256, 4, EPI_STORE, true>(A, B, D, R, M, N, K, lda, ldb, ldd, ldr, status, max_ctas, stream, W,
+                                           splits, kper);
+    else
+      launch_gemm<128, 6, EPI_STORE, true>(A, B, D, R, M, N, K, lda, ldb, ldd, ldr, status, max_ctas, stream, W,
+                                           splits, kper);
+    const int Nout = epi == EPI_SILU_MUL ? N / 2 : N;
+    const long chunks = (long)M * (Nout / 8);
+    const int blocks = (int)std::min<long>((chunks + 255) / 256, (long)num_sms() * 8);
+    auto* d = reinterpret_cast<__nv_bfloat16*>(D);
+    auto* r = reinterpret_cast<const __nv_bfloat16*>(R);
+    if (epi == EPI_SILU_MUL)
+      gemm_splitk_finalize<EPI_SILU_MUL><<<blocks, 256, 0, stream>>>(W, N, d, ldd, r, ldr, M, Nout);
+    else if (epi == EPI_ADD)
+      gemm_splitk_finalize<EPI_ADD><<<blocks, 256, 0, stream>>>(W, N, d, ldd, r, ldr, M, Nout);
+    else
+      gemm_splitk_finalize<EPI_STORE><<<blocks, 256, 0, stream>>>(W, N, d, ldd, r, ldr, M, Nout);
+    return;
+  }
 #define CX_GEMM_CASE(BNV, ST, E)                                                                   \
   if (bn == BNV && epi == E) {                                                                     \
     launch_gemm<BNV, ST, E>(A, B, D, R, M, N, K, lda, ldb, ldd, ldr, status, max_ctas, stream); \

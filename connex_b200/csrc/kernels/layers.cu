@@ -103,10 +103,13 @@ void rmsnorm(const void* x, int ldx, void* residual, int ldr, const void* w, voi
 // cos_sin: [max_pos, D] fp32, cos in [0, D/2), sin in [D/2, D).
 // slot_mapping: [T] int64 (-1 = do not cache).  Caches: [blocks, Hkv, BS, D].
 // One warp per (token, head); D = 128 -> 4 elements per lane.
+// Optional per-head RMSNorm of q and k before the rotation (``qn`` / ``kn``:
+// [D] bf16 weights, Qwen3-style query/key norm), fused into the same pass.
 __global__ void rope_cache_kernel(__nv_bfloat16* qkv, int ldq, const int* __restrict__ pos,
                                   const float* __restrict__ cos_sin, const int64_t* __restrict__ slots,
                                   __nv_bfloat16* kc, __nv_bfloat16* vc, int T, int Hq, int Hkv, int BS,
-                                  int num_blocks, int max_pos, int* status) {
+                                  int num_blocks, int max_pos, int* status, const __nv_bfloat16* __restrict__ qn,
+                                  const __nv_bfloat16* __restrict__ kn, float eps) {
   constexpr int D = 128;
   const int gw = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
@@ -127,7 +130,19 @@ __global__ void rope_cache_kernel(__nv_bfloat16* qkv, int ldq, const int* __rest
     }
     const float* cs = cos_sin + (size_t)p * D;
     const float c0 = cs[i], c1 = cs[i + 1], s0 = cs[D / 2 + i], s1 = cs[D / 2 + i + 1];
-    const float x0 = bf16_lo(lo), x1 = bf16_hi(lo), y0 = bf16_lo(hi), y1 = bf16_hi(hi);
+    float x0 = bf16_lo(lo), x1 = bf16_hi(lo), y0 = bf16_lo(hi), y1 = bf16_hi(hi);
+    const __nv_bfloat16* nw = h < Hq ? qn : kn;
+    if (nw != nullptr) {
+      const float ss = warp_sum(x0 * x0 + x1 * x1 + y0 * y0 + y1 * y1);
+      const float r = rsqrtf(ss * (1.0f / D) + eps);
+      const uint32_t wl = *reinterpret_cast<const uint32_t*>(nw + i);
+      const uint32_t wh = *reinterpret_cast<const uint32_t*>(nw + i + D / 2);
+      // round to bf16 between the norm and the rotation, like a separate norm layer
+      x0 = __bfloat162float(__float2bfloat16(x0 * r * bf16_lo(wl)));
+      x1 = __bfloat162float(__float2bfloat16(x1 * r * bf16_hi(wl)));
+      y0 = __bfloat162float(__float2bfloat16(y0 * r * bf16_lo(wh)));
+      y1 = __bfloat162float(__float2bfloat16(y1 * r * bf16_hi(wh)));
+    }
     lo = pack_bf16x2(x0 * c0 - y0 * s0, x1 * c1 - y1 * s1);
     hi = pack_bf16x2(y0 * c0 + x0 * s0, y1 * c1 + x1 * s1);
     *reinterpret_cast<uint32_t*>(row + i) = lo;
@@ -151,7 +166,8 @@ __global__ void rope_cache_kernel(__nv_bfloat16* qkv, int ldq, const int* __rest
 }
 
 void rope_cache(void* qkv, int ldq, const int* pos, const float* cos_sin, const int64_t* slots, void* kc, void* vc,
-                int T, int Hq, int Hkv, int D, int BS, int num_blocks, int max_pos, int* status, cudaStream_t s) {
+                int T, int Hq, int Hkv, int D, int BS, int num_blocks, int max_pos, int* status, cudaStream_t s,
+                const void* q_norm, const void* k_norm, float eps) {
   if (T == 0) return;
   if (D != 128) throw std::runtime_error("cx rope: head_dim must be 128");
   const long warps = (long)T * (Hq + 2 * Hkv);
@@ -160,7 +176,8 @@ void rope_cache(void* qkv, int ldq, const int* pos, const float* cos_sin, const 
   rope_cache_kernel<<<blocks, threads, 0, s>>>(reinterpret_cast<__nv_bfloat16*>(qkv), ldq, pos, cos_sin, slots,
                                                reinterpret_cast<__nv_bfloat16*>(kc),
                                                reinterpret_cast<__nv_bfloat16*>(vc), T, Hq, Hkv, BS, num_blocks,
-                                               max_pos, status);
+                                               max_pos, status, reinterpret_cast<const __nv_bfloat16*>(q_norm),
+                                               reinterpret_cast<const __nv_bfloat16*>(k_norm), eps);
 }
 
 // --------------------------------------------------------------- embedding

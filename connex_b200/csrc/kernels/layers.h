@@ -9,7 +9,8 @@ namespace cx {
 void rmsnorm(const void* x, int ldx, void* residual, int ldr, const void* w, void* out, int ldo, int T, int H,
              float eps, cudaStream_t s);
 void rope_cache(void* qkv, int ldq, const int* pos, const float* cos_sin, const int64_t* slots, void* kc, void* vc,
-                int T, int Hq, int Hkv, int D, int BS, int num_blocks, int max_pos, int* status, cudaStream_t s);
+                int T, int Hq, int Hkv, int D, int BS, int num_blocks, int max_pos, int* status, cudaStream_t s,
+                const void* q_norm = nullptr, const void* k_norm = nullptr, float eps = 1e-6f);
 void embedding(const int* ids, const void* table, void* out, int T, int H, int V, int* status, cudaStream_t s);
 void argmax(const void* logits, int ldl, int B, int V, int* out, cudaStream_t s);
 void gather_rows(const void* src, int lds, const int* idx, void* out, int ldo, int n, int H, cudaStream_t s);

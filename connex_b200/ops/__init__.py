@@ -57,21 +57,37 @@ def check_status(status: torch.Tensor, what: str = "kernel") -> None:
 
 
 # ----------------------------------------------------------------- GEMM
+_SPLIT_WS: dict = {}
+
+
+def _split_workspace(device, n: int) -> torch.Tensor:
+    """Per-device fp32 split-K workspace; the finalize kernel leaves it zero."""
+    ws = _SPLIT_WS.get(device)
+    if ws is None or ws.numel() < n:
+        ws = torch.zeros(max(n, 1 << 20), dtype=torch.float32, device=device)
+        _SPLIT_WS[device] = ws
+    return ws
+
+
 def gemm(a: torch.Tensor, b: torch.Tensor, out: Optional[torch.Tensor] = None, *,
          residual: Optional[torch.Tensor] = None, silu_mul: bool = False, bn: int = 0,
-         status: Optional[torch.Tensor] = None, max_ctas: int = 0) -> torch.Tensor:
+         status: Optional[torch.Tensor] = None, max_ctas: int = 0, splits: Optional[int] = None) -> torch.Tensor:
     """``a[M,K] @ b[N,K]^T`` on tcgen05 tensor cores (bf16 in/out, fp32 accumulate).
 
     ``residual`` adds a bf16 tensor in the epilogue (may alias ``out``).
     ``silu_mul`` treats ``b`` as gate/up rows interleaved per 256-row tile
     (see :func:`interleave_gate_up`) and writes ``SiLU(gate) * up`` of width N/2.
+    ``splits`` cuts the K loop for small-M GEMMs (None: the kernel's choice,
+    1: never); a split GEMM is two launches (MMA + finalize).
     """
-    M, N = a.shape[0], b.shape[0]
+    M, N, K = a.shape[0], b.shape[0], a.shape[1]
     if out is None:
         out = torch.empty(M, N // 2 if silu_mul else N, dtype=torch.bfloat16, device=a.device)
     epi = EPI_SILU_MUL if silu_mul else (EPI_ADD if residual is not None else EPI_STORE)
-    _C.gemm(a, b, out, residual, epi, bn, status, max_ctas)
-    _n()
+    s = _C.gemm_splits(M, N, K, epi, bn) if splits is None else splits
+    ws = _split_workspace(a.device, M * N) if s > 1 else None
+    _C.gemm(a, b, out, residual, epi, bn, status, max_ctas, ws, s)
+    _n(2 if s > 1 else 1)
     return out
 
 
@@ -107,9 +123,12 @@ def rmsnorm(x: torch.Tensor, weight: torch.Tensor, eps: float, out: Optional[tor
 def rope_cache(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor, n_q_heads: int,
                n_kv_heads: int, slot_mapping: Optional[torch.Tensor] = None,
                k_cache: Optional[torch.Tensor] = None, v_cache: Optional[torch.Tensor] = None,
-               status: Optional[torch.Tensor] = None) -> None:
-    """Rotate q/k of the fused QKV rows in place; write k/v to their paged slots."""
-    _C.rope_cache(qkv, positions, cos_sin, slot_mapping, k_cache, v_cache, n_q_heads, n_kv_heads, status)
+               status: Optional[torch.Tensor] = None, q_norm: Optional[torch.Tensor] = None,
+               k_norm: Optional[torch.Tensor] = None, eps: float = 1e-6) -> None:
+    """Rotate q/k of the fused QKV rows in place; write k/v to their paged slots.
+    ``q_norm`` / ``k_norm`` ([128] bf16): per-head RMSNorm of q / k first (Qwen3)."""
+    _C.rope_cache(qkv, positions, cos_sin, slot_mapping, k_cache, v_cache, n_q_heads, n_kv_heads, status, q_norm,
+                  k_norm, eps)
     _n()
 
 

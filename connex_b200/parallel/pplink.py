@@ -2,12 +2,14 @@
 
 Pipeline activations (``[batch, hidden]`` bf16 per hop) travel over NCCL
 send/recv, but a fixed NCCL world cannot lose or gain a member.  Here every
-pair of stage endpoints that talk gets its own two-rank process group,
-created on demand: both sides rendezvous through a shared ``TCPStore`` under
-the prefix ``cxpp/<lo>/<hi>/<generation>`` (``lo``/``hi`` = the two endpoint
-names in sorted order, which also fixes the ranks).  When a peer dies only
-its pair groups are aborted; a replacement joins by opening fresh pairs with
-a higher generation.  The same code runs on ``gloo`` (CPU tests).
+direction between two stage endpoints that talk gets its own two-rank
+process group, created on demand: both sides rendezvous through a shared
+``TCPStore`` under the prefix ``cxpp/<sender>><receiver>/<generation>``
+(rank 0 = sender).  One group per direction keeps a stage's forward sends
+and its reply receives on different NCCL streams, so K steps in flight in
+both directions cannot wait on each other.  When a peer dies only its
+groups are aborted; a replacement opens fresh ones (a new generation when
+it reuses the name).  The same code runs on ``gloo`` (CPU tests).
 
 Sends and receives run on a dedicated CUDA stream per link so they overlap
 the stage's compute; the caller orders them with events.  Which peer to talk
@@ -41,13 +43,18 @@ class PairLink:
 
     def _run(self, fn, tensors: Sequence[torch.Tensor], after: Optional[torch.cuda.Event]):
         if self.dead:
-            raise LinkError(f"link {self.me}<->{self.peer} (gen {self.gen}) is closed")
+            raise LinkError(f"link {self.me}->{self.peer} (gen {self.gen}) is closed")
         if self.stream is None:
-            return [fn(t) for t in tensors]
+            works = [fn(t) for t in tensors]
+            for w in works:
+                w.wait()
+            return works
         cur = torch.cuda.current_stream(self.device)
         self.stream.wait_stream(cur) if after is None else self.stream.wait_event(after)
-        with torch.cuda.stream(self.stream):
+        with torch.cuda.device(self.device), torch.cuda.stream(self.stream):
             works = [fn(t) for t in tensors]
+            for w in works:       # the link stream (not the host) waits for the NCCL stream
+                w.wait()
         for t in tensors:
             t.record_stream(self.stream)
         return works
@@ -94,25 +101,32 @@ class PairLinks:
         self.device = torch.device(device)
         self.backend = backend or ("nccl" if self.device.type == "cuda" else "gloo")
         self.timeout = timedelta(seconds=timeout_s)
-        self.links: Dict[Tuple[str, int], PairLink] = {}
+        self.links: Dict[Tuple[str, int, bool], PairLink] = {}
         self._lock = threading.Lock()
 
     @staticmethod
-    def prefix(a: str, b: str, gen: int) -> str:
-        lo, hi = sorted((a, b))
-        return f"cxpp/{lo}/{hi}/{gen}/"
+    def prefix(sender: str, receiver: str, gen: int) -> str:
+        return f"cxpp/{sender}>{receiver}/{gen}/"
 
-    def open(self, peer: str, gen: int = 0) -> PairLink:
-        """Open (or return) the link to ``peer``; the peer calls ``open(me, gen)`` too."""
-        key = (peer, gen)
+    def open_tx(self, peer: str, gen: int = 0) -> PairLink:
+        """Link for sending to ``peer`` (which opens it with ``open_rx(me, gen)``)."""
+        return self._open(peer, gen, True)
+
+    def open_rx(self, peer: str, gen: int = 0) -> PairLink:
+        """Link for receiving from ``peer`` (which opens it with ``open_tx(me, gen)``)."""
+        return self._open(peer, gen, False)
+
+    def _open(self, peer: str, gen: int, tx: bool) -> PairLink:
+        key = (peer, gen, tx)
         with self._lock:
             link = self.links.get(key)
             if link is not None and not link.dead:
                 return link
         if peer == self.me:
             raise ValueError("a link needs two endpoints")
-        rank = 0 if self.me < peer else 1
-        pstore = dist.PrefixStore(self.prefix(self.me, peer, gen), self.store)
+        rank = 0 if tx else 1
+        pstore = dist.PrefixStore(self.prefix(self.me, peer, gen) if tx else self.prefix(peer, self.me, gen),
+                                  self.store)
         if self.backend == "nccl":
             opts = dist.ProcessGroupNCCL.Options()
             opts._timeout = self.timeout
@@ -124,8 +138,8 @@ class PairLinks:
             self.links[key] = link
         return link
 
-    def get(self, peer: str, gen: int = 0) -> Optional[PairLink]:
-        return self.links.get((peer, gen))
+    def get(self, peer: str, gen: int = 0, tx: bool = True) -> Optional[PairLink]:
+        return self.links.get((peer, gen, tx))
 
     def drop_peer(self, peer: str, abort: bool = True) -> int:
         """Close every link to ``peer`` (it died or left); returns how many."""

@@ -68,6 +68,31 @@ def test_gemm_silu_mul(dev):
     _close(out, R.silu_mul_gemm(a, w))
 
 
+@pytest.mark.parametrize("M", [1, 64, 130])
+def test_gemm_split_k(dev, M):
+    """Small-M (decode) GEMMs split the K loop: plain, residual and SiLU-mul
+    epilogues against the fp32 reference; the workspace is left zero."""
+    from connex_b200 import ops
+    from connex_b200.ops import reference as R
+    a, b = _rnd(M, 4096, dev=dev, seed=20), _rnd(1024, 4096, dev=dev, seed=21)
+    assert ops._C.gemm_splits(M, 1024, 4096, ops.EPI_STORE, 0) > 1
+    st = ops.new_status(dev)
+    n0 = ops.launch_count()
+    out = ops.gemm(a, b, status=st)
+    assert ops.launch_count() == n0 + 2
+    _close(out, R.gemm(a, b))
+    x = _rnd(M, 1024, dev=dev, seed=22)
+    ref = R.gemm(a, b, residual=x)
+    ops.gemm(a, b, x, residual=x, splits=4)
+    _close(x, ref)
+    gate, up = _rnd(512, 4096, dev=dev, seed=23, std=0.1), _rnd(512, 4096, dev=dev, seed=24, std=0.1)
+    w = ops.interleave_gate_up(gate, up)
+    _close(ops.gemm(a, w, silu_mul=True, splits=8), R.silu_mul_gemm(a, w))
+    torch.cuda.synchronize()
+    ops.check_status(st, "gemm split-k")
+    assert float(ops._SPLIT_WS[a.device].abs().max()) == 0.0
+
+
 def test_rmsnorm(dev):
     from connex_b200 import ops
     from connex_b200.ops import reference as R
@@ -104,6 +129,28 @@ def test_rope_cache(dev):
         s = int(slots[t])
         _close(kc[s // BS, :, s % BS], kr[t])
         assert torch.equal(vc[s // BS, :, s % BS], v[t])
+
+
+def test_rope_cache_qk_norm(dev):
+    """Per-head q/k RMSNorm (Qwen3) fused before the rotation."""
+    from connex_b200 import ops
+    from connex_b200.ops import reference as R
+    Hq, Hkv, T = 8, 2, 33
+    qkv = _rnd(T, (Hq + 2 * Hkv) * 128, dev=dev, seed=31, std=0.5)
+    pos = torch.randint(0, 2000, (T,), device=dev, dtype=torch.int32)
+    cs = ops.rope_cos_sin(2048, 128, 1e6, dev)
+    qn, kn = _rnd(128, dev=dev, seed=32) + 1, _rnd(128, dev=dev, seed=33) + 1
+    orig = qkv.clone()
+    ops.rope_cache(qkv, pos, cs, Hq, Hkv, q_norm=qn.bfloat16(), k_norm=kn.bfloat16(), eps=1e-6)
+
+    def ref(x, w):
+        n = x.float() * torch.rsqrt(x.float().pow(2).mean(-1, keepdim=True) + 1e-6) * w.bfloat16().float()
+        return R.rope(n.bfloat16(), pos, cs)
+    q = orig[:, :Hq * 128].view(T, Hq, 128)
+    k = orig[:, Hq * 128:(Hq + Hkv) * 128].view(T, Hkv, 128)
+    _close(qkv[:, :Hq * 128].view(T, Hq, 128), ref(q, qn))
+    _close(qkv[:, Hq * 128:(Hq + Hkv) * 128].view(T, Hkv, 128), ref(k, kn))
+    assert torch.equal(qkv[:, (Hq + Hkv) * 128:], orig[:, (Hq + Hkv) * 128:])
 
 
 def test_embedding_argmax(dev):
