@@ -129,13 +129,26 @@ def main() -> None:
     p.add_argument("--max-len", type=int, default=8192)
     p.add_argument("--layers", type=int, default=32, help="model depth (32 = Llama-3-8B)")
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--no-sub-metrics", action="store_true",
+                   help="skip the EP layer and weight-sync measurements after the PD steps")
     args = p.parse_args()
     if args.impl == "reference":
         reference_arm(args)
         return
     sys.path.insert(0, ROOT)
     from connex_b200.bench.pd_bench import run_pd_bench
-    res = run_pd_bench(args, ClockSampler)
+    res = run_pd_bench(args, ClockSampler, finalize=False)
+    import torch
+    import torch.distributed as dist
+    world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
+    if not args.no_sub_metrics:
+        from connex_b200.bench.sub_metrics import run_sub_metrics
+        dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
+        sub = run_sub_metrics(world, rank, dev, layers=args.layers)
+        if res is not None:
+            res["sub_metrics"] = sub
+    if world > 1 and dist.is_initialized():
+        dist.destroy_process_group()
     if res is not None:
         res.update({"metric": METRIC, "higher_is_better": True, "scaling": "weak", "dtype": "bf16",
                     "vs_baseline": round(res["value"] / PUBLISHED_KV_GBPS, 2) if res.get("value") else None})

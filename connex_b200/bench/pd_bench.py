@@ -36,7 +36,9 @@ def _prompts(seed: int, step: int, pair: int, batch: int, lo: int, hi: int, voca
     return [rng.integers(0, vocab, size=int(n)).tolist() for n in lens]
 
 
-def run_pd_bench(args, ClockSampler):
+def run_pd_bench(args, ClockSampler, finalize: bool = True):
+    """The PD steps; with ``finalize=False`` the process group stays up for
+    further collective measurements (the caller destroys it)."""
     world = int(os.environ.get("WORLD_SIZE", "1"))
     rank = int(os.environ.get("RANK", "0"))
     local = int(os.environ.get("LOCAL_RANK", "0"))
@@ -211,5 +213,6 @@ def run_pd_bench(args, ClockSampler):
     if world > 1:
         barrier()
         mapper.close()
-        dist.destroy_process_group()
+        if finalize:
+            dist.destroy_process_group()
     return result

@@ -70,5 +70,10 @@ setup(
             "connex-pd-router=connex.serving.pd_router:main",
             "connex-proxy=connex.serving.proxy:main",
         ],
+        # upstream engines find the plugins by name (no fork)
+        "vllm.general_plugins": [
+            "connex_pd = connex.adapters.vllm.plugin:register",
+            "connex_rl = connex.rl.vllm_plugin:register",
+        ],
     },
 )
