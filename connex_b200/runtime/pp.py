@@ -65,7 +65,7 @@ class StageModel(LlamaModel):
     def __init__(self, weights: LlamaWeights, l0: int, l1: int, cache: PagedKVCache, max_tokens: int,
                  max_batch: int = 256, device=None):
         self.l0, self.l1 = l0, l1
-        self.first, self.last = l0 == 0, l1 == weights.cfg.layers
+        self.is_first, self.is_last = l0 == 0, l1 == weights.cfg.layers
         dev = torch.device(device) if device is not None else weights.layers[0].wqkv.device
         if weights.embed is None:          # LlamaModel reads the device from the embedding
             weights.embed = torch.empty(0, weights.cfg.hidden, dtype=torch.bfloat16, device=dev)
@@ -74,7 +74,7 @@ class StageModel(LlamaModel):
     def _next_norm(self, i: int):
         if i + 1 < len(self.w.layers):
             return self.w.layers[i + 1].attn_norm
-        return self.w.final_norm if self.last else None
+        return self.w.final_norm if self.is_last else None
 
     def _tail(self, i: int, T: int) -> None:
         cfg, lw = self.cfg, self.w.layers[i]
@@ -88,7 +88,7 @@ class StageModel(LlamaModel):
             ops.rmsnorm(x, nw, self.cfg.eps, out=h)
 
     def _enter(self, inp: torch.Tensor, T: int) -> None:
-        if self.first:
+        if self.is_first:
             ops.embedding(inp, self.w.embed, self.x[:T], status=self.status)
         else:
             self.x[:T].copy_(inp)
@@ -112,7 +112,7 @@ class StageModel(LlamaModel):
                 ops.decode_attention(qkv, self.cache.k(i), self.cache.v(i), block_tables, ctx_lens, cfg.heads,
                                      max_ctx, workspace, out=self.attn[:T])
             self._tail(i, T)
-        if self.last:
+        if self.is_last:
             return self._head(rows, B)
         return self.x[:T]
 
@@ -177,7 +177,7 @@ class StageRuntime:
         positions = torch.tensor(pos, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
         slot_t = torch.tensor(slots, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
         B = len(rids)
-        inp = td["ids"] if self.model.first else td["x"]
+        inp = td["ids"] if self.model.is_first else td["x"]
         kw = {}
         if prefill:
             rows, start, q0s = [], 0, []
@@ -208,5 +208,5 @@ class StageRuntime:
         res = {"kind": td["kind"], "n_new": n_new}
         # a copy: the model's buffers are rewritten by the next step while the
         # link may still be sending this one
-        res["next" if self.model.last else "x"] = out.clone()
+        res["next" if self.model.is_last else "x"] = out.clone()
         return res
