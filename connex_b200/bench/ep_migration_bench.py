@@ -15,8 +15,9 @@ context per step):
    agreed step boundary;
 3. at step ``--fail-at`` rank 3 leaves between steps; the survivors learn it
    from the store before their next launch, drop its slots from the placement
-   and rebuild the EP group over N-1 ranks (fresh buffers, IPC handles
-   exchanged through the store), and decode continues.
+   and mark it dead in the EP layer (its peer-table column points at local
+   sinks, wait targets count live ranks: no buffer or IPC mapping is rebuilt),
+   and decode continues.
 
 Reported (rank 0): decode step time before / during / after migration and
 after the failure (device time, max over ranks), the migration copy time and
@@ -160,11 +161,8 @@ def main() -> None:
             store.wait(["fail_t"], timedelta(seconds=300))
             table.mark_down(victim)
             table.commit()
-            members = [r for r in range(N) if r != victim]
-            group.close()
-            cfg_ep = EPConfig(len(members), S, cfg.hidden, cfg.moe_ffn, cfg.top_k, max_tokens=B)
-            group = Group("ep1", store, rank, members, cfg_ep, model, dev)
             l2p, cnt = l2p_for(table, members, S, dev, L, max_rep)
+            group.moe.mark_dead(victim)        # same buffers and mappings; its memory is never touched again
             failed = True
             first_after_fail = step
         if step == a.migrate_at and mine and not copy_started:

@@ -95,6 +95,34 @@ class EPMoE:
         self.w13 = w13.reshape(cfg.slots_per_rank * 2 * cfg.ffn, cfg.hidden)
         self.w2 = w2.reshape(cfg.slots_per_rank * cfg.hidden, cfg.ffn)
         self.epoch = 0
+        self.live = [True] * cfg.n_ranks
+        self.count_expected = 0      # cumulative u32 targets: + live ranks per forward
+        self.data_expected = 0
+        self._sink = None
+
+    @property
+    def n_live(self) -> int:
+        return sum(self.live)
+
+    def mark_dead(self, rank: int) -> None:
+        """Stop exchanging with ``rank`` (it left between forwards; every rank
+        calls this at the same forward boundary, after its l2p stops routing to
+        ``rank``'s slots).  Its column of the peer table points at local sinks
+        from now on, so no kernel touches its memory again, its stale row of the
+        count matrix is cleared, and the wait targets count live ranks only --
+        no buffer is reallocated and no IPC mapping reopened."""
+        if not self.live[rank] or rank == self.rank:
+            return
+        c, b = self.cfg, self.b
+        if self._sink is None:
+            self._sink = (torch.zeros_like(b.counts), torch.zeros(16, dtype=torch.int32, device=b.device))
+        sc, sf = self._sink
+        col = torch.tensor([sc.data_ptr(), sf.data_ptr() + 4 * FLAG_COUNT, b.recv.data_ptr(), b.recv_meta.data_ptr(),
+                            sf.data_ptr() + 4 * FLAG_DATA, b.comb.data_ptr(), sf.data_ptr() + 4 * FLAG_COMB],
+                           dtype=torch.int64, device=self.peers.device)
+        self.peers[:, rank] = col
+        b.counts[rank].zero_()
+        self.live[rank] = False
 
     # the five phases (separately callable for the single-GPU emulation)
     def phase_count(self, topk_idx, l2p, l2p_cnt):
@@ -102,6 +130,8 @@ class EPMoE:
         if topk_idx.shape[0] > c.max_tokens or topk_idx.shape[1] != c.top_k:
             raise ValueError(f"EP layer holds {c.max_tokens} tokens x top-{c.top_k}; got {tuple(topk_idx.shape)}")
         self.epoch += 1
+        self.count_expected = (self.count_expected + self.n_live) & 0xFFFFFFFF
+        self.data_expected = (self.data_expected + self.n_live * _C.EP_DISPATCH_CTAS) & 0xFFFFFFFF
         _C.ep_count(topk_idx, l2p, l2p_cnt, c.slots_per_rank, self.rank, self.b.pos, self.b.slot_of, self.peers,
                     self.b.flags[FLAG_EXPECT:FLAG_EXPECT + 1], c.hidden // 256, self.b.status)
         ops._n()
@@ -109,11 +139,11 @@ class EPMoE:
     def phase_dispatch(self, x, topk_w):
         c = self.cfg
         _C.ep_dispatch(x, topk_w, self.b.pos, self.b.slot_of, self.b.counts, c.top_k, c.slots_per_rank, self.rank,
-                       c.recv_rows, (self.epoch * c.n_ranks) & 0xFFFFFFFF, self.peers, self.b.status)
+                       c.recv_rows, self.count_expected, self.peers, self.b.status)
         ops._n()
 
     def _data_target(self) -> int:
-        return (self.epoch * self.cfg.n_ranks * _C.EP_DISPATCH_CTAS) & 0xFFFFFFFF
+        return self.data_expected
 
     def phase_gate_up(self):
         c = self.cfg

@@ -86,3 +86,41 @@ def test_ep_replicas_and_unroutable_expert():
         ops.check_status(L.b.status, "ep")
     for r in range(N):
         _close(ys[r], reference_moe(xs[r], routes[r][0], routes[r][1], w13, w2, l2p, cnt))
+
+
+def test_ep_rank_leaves_without_rebuild():
+    """Rank 2 of 3 leaves between forwards: survivors route around its slots
+    and mark it dead (its peer-table column points at local sinks, wait
+    targets count live ranks) and keep going on the same buffers."""
+    from connex_b200 import ops
+    from connex_b200.parallel.ep import EPConfig, emulated_forward, emulated_group, reference_moe
+    dev = torch.device("cuda", 0)
+    N, S, H, F, K = 3, 4, 512, 256, 2
+    E = N * S
+    cfg = EPConfig(N, S, H, F, K, max_tokens=64)
+    w13, w2 = _weights(E, H, F, dev, seed=5)
+    layers = emulated_group(cfg, w13, w2, dev)
+    l2p, cnt = _identity_l2p(E, dev)
+    Ts = [40, 64, 13]
+    for step in range(2):
+        xs = [(torch.randn(T, H, device=dev) * 0.5).bfloat16() for T in Ts]
+        routes = [_routing(T, E, K, dev, 7 * step + r) for r, T in enumerate(Ts)]
+        emulated_forward(layers, xs, [r[0] for r in routes], [r[1] for r in routes], l2p, cnt)
+    torch.cuda.synchronize()
+    # rank 2 dies; its experts move (here: logical experts 8..11 now served by slots 0..3 copies)
+    w13s, w2s = w13.clone(), w2.clone()
+    survivors = layers[:2]
+    for L in survivors:
+        L.mark_dead(2)
+    l2p2 = l2p.clone()
+    for e in range(8, 12):
+        l2p2[e, 0] = e - 8 + 4          # served by rank 1's slots (weights of those slots)
+    for step in range(3):
+        xs = [(torch.randn(T, H, device=dev) * 0.5).bfloat16() for T in Ts[:2]]
+        routes = [_routing(T, E, K, dev, 100 + 7 * step + r) for r, T in enumerate(Ts[:2])]
+        ys = emulated_forward(survivors, xs, [r[0] for r in routes], [r[1] for r in routes], l2p2, cnt)
+        torch.cuda.synchronize()
+        for L in survivors:
+            ops.check_status(L.b.status, f"ep rank {L.rank}")
+        for r in range(2):
+            _close(ys[r], reference_moe(xs[r], routes[r][0], routes[r][1], w13s, w2s, l2p2, cnt))
