@@ -187,7 +187,7 @@ class StageRuntime:
                 rows.append(start + n - 1)
                 start += n
             kw["tile_info"] = ops.prefill_tile_info(n_new, dev)
-            kw["rows"] = torch.tensor(rows, dtype=torch.int64, device=dev)
+            kw["rows"] = torch.tensor(rows, dtype=torch.int32, device=dev)
         else:
             mb = -(-max(lens) // self.bs)
             bt = torch.zeros(B, mb, dtype=torch.int32)
@@ -197,7 +197,7 @@ class StageRuntime:
             kw.update(block_tables=bt.pin_memory().to(dev, non_blocking=True),
                       ctx_lens=torch.tensor(lens, dtype=torch.int32).pin_memory().to(dev, non_blocking=True),
                       max_ctx=max(lens), workspace=self.ws,
-                      rows=torch.arange(B, dtype=torch.int64, device=dev))
+                      rows=torch.arange(B, dtype=torch.int32, device=dev))
         out = self.model.run(inp, positions, slot_t, prefill=prefill, B=B, **kw)
         for r, c, n in zip(rids, ctx, n_new):
             if r in miss:           # computed without its KV: not held here; stage 0 prefills it again

@@ -35,7 +35,7 @@ def test_two_stage_split_matches_whole_model():
     slots = torch.tensor(sum((slot_mapping(t, 0, n, 16) for t, n in zip(tables, lens)), []), dtype=torch.int64,
                          device=dev)
     pos = torch.tensor(sum((list(range(n)) for n in lens), []), dtype=torch.int32, device=dev)
-    last = torch.tensor([sum(lens[:i + 1]) - 1 for i in range(3)], dtype=torch.int64, device=dev)
+    last = torch.tensor([sum(lens[:i + 1]) - 1 for i in range(3)], dtype=torch.int32, device=dev)
     want = model.prefill(ids, pos, slots, lens, last, ops.prefill_tile_info(lens, dev))
     torch.cuda.synchronize()
     assert nxt.tolist() == want.tolist()
@@ -54,7 +54,7 @@ def test_two_stage_split_matches_whole_model():
         ws = ops.decode_workspace(3, cfg.heads, 512, dev)
         ref = model.decode(cur.to(torch.int32), torch.tensor(ctx, dtype=torch.int32, device=dev), dslots,
                            bt.to(dev), torch.tensor([c + 1 for c in ctx], dtype=torch.int32, device=dev),
-                           max(ctx) + 1, ws, torch.arange(3, device=dev))
+                           max(ctx) + 1, ws, torch.arange(3, dtype=torch.int32, device=dev))
         torch.cuda.synchronize()
         assert got.tolist() == ref.tolist()
         cur = ref.clone()
