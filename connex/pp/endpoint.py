@@ -144,6 +144,9 @@ class PipelineEndpoint:
         if self.data == "engine":
             self._setup_ring(ring_bytes)
         self._stop = threading.Event()
+        self._send_lock = threading.Lock()      # a signal and its link sends stay together, per process
+        self.auto_warm = False
+        self._warm_threads: List[threading.Thread] = []
         if membership is not None:
             self.attach_membership(membership)
         self._io = threading.Thread(target=self._io_loop, name=f"cx-pp-io-{stage_idx}", daemon=True)
@@ -257,9 +260,10 @@ class PipelineEndpoint:
             extra = [bytes(buf)]
         url = (self.engine.local_url if self.data == "engine" else self.link_id).encode()
         tail = wire.encode_g2(token, layout_b or b"", self.address.encode(), origin.encode(), nt_b)
-        self._post(address, [wire.encode_signal(src, total, url, corr, tail)] + extra)
-        if self.data == "link" and tensors:
-            self.links.open_tx(self._peer_name(address)).send([v.contiguous() for _, v in tensors])
+        with self._send_lock:
+            self._post(address, [wire.encode_signal(src, total, url, corr, tail)] + extra)
+            if self.data == "link" and tensors:
+                self.links.open_tx(self._peer_name(address)).send([v.contiguous() for _, v in tensors])
         self.stats["sent"] += 1
 
     def _peer_name(self, address: str) -> str:
@@ -391,9 +395,35 @@ class PipelineEndpoint:
             self.on_peer_dead(lid["stage_idx"], lid.get("replica_idx", 0), payload.get("reason", "event"))
 
     def _on_membership_join(self, ev) -> None:
-        lid = (getattr(ev, "payload", {}) or {}).get("lid") or {}
+        payload = getattr(ev, "payload", {}) or {}
+        lid = payload.get("lid") or {}
         if "stage_idx" in lid:
             self.on_peer_alive(lid["stage_idx"], lid.get("replica_idx", 0))
+            addrs = payload.get("addresses") or []
+            if self.auto_warm and self.is_first and lid["stage_idx"] == 1 and addrs:
+                t = threading.Thread(target=self.warm, args=(addrs[0],), daemon=True, name="cx-pp-warm")
+                t.start()
+                self._warm_threads.append(t)
+
+    # ------------------------------------------------------------- warm-up
+    def warm(self, address: str, timeout_s: float = 120.0) -> bool:
+        """Send one empty ``warmup`` step through the chain starting at
+        ``address`` and wait for it to come back (stage 0), so the data-plane
+        links of a (new) replica are set up before traffic is routed to it."""
+        import torch
+        corr = self.new_step_id()
+        w = torch.zeros(8, dtype=torch.bfloat16, device=self.device)
+        try:
+            self.send_step({"kind": "warmup", "w": w}, corr, dst=address)
+            return self.recv_step(corr, timeout_s) is not None
+        finally:
+            self.abandon_step(corr)
+
+    def warm_stage(self, stage_idx: int = 1) -> int:
+        """Warm every listed replica of ``stage_idx``; returns how many answered."""
+        if self.membership is None:
+            return 0
+        return sum(self.warm(r.addresses[0]) for r in self.membership.get_stage_peers(stage_idx) if r.addresses)
 
     def confirm_peer_failure(self) -> bool:
         """After a timeout: probe the downstream; a refused connect confirms death."""

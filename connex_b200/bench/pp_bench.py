@@ -45,10 +45,17 @@ from connex_b200.runtime.pp import StageRuntime
 MODEL = "llama3-8b-pp"
 
 
+DATA_PLANE = {"links": "nccl"}
+
+
 def _make_endpoint(stage, replica, dev, store, dir_addr, port=0):
     ep = PipelineEndpoint(MODEL, stage, 2, replica, data="link", links=None, device=str(dev), recv_timeout_s=30.0,
                           port=port)
-    ep.links = PairLinks(dist.PrefixStore("pplinks/", store), ep.link_id, dev, timeout_s=60)
+    if DATA_PLANE["links"] == "chan":
+        from connex_b200.parallel.p2pchan import ChanLinks
+        ep.links = ChanLinks(dist.PrefixStore("ppchan/", store), ep.link_id, dev, slots=2, slot_bytes=256 << 20)
+    else:
+        ep.links = PairLinks(dist.PrefixStore("pplinks/", store), ep.link_id, dev, timeout_s=60)
     client = DirectoryClient(dir_addr, MODEL, stage, replica_idx=replica, local_addresses=[ep.address])
     client.start()
     client.start_event_listener()
@@ -137,6 +144,8 @@ def stage0_main(args, rank, replica, dev, store, dir_addr):
     rt = StageRuntime(cfg, 0, cfg.layers // 2, dev, num_blocks=B * (P + S + 16) // 16 + 64, max_tokens=B * (P + S),
                       max_batch=B, max_ctx=P + S + 16, seed=0)
     ep, client = _make_endpoint(0, replica, dev, store, dir_addr)
+    warmed = ep.warm_stage(1)          # every stage-1 replica's links are set up before traffic
+    ep.auto_warm = True                # and a replica that (re)joins gets warmed in the background
     hooks = _Stage0Hooks()
     link = Stage0Link(ep, hooks, recv_timeout_s=30.0)
     g = torch.Generator().manual_seed(1234 + replica)
@@ -210,7 +219,10 @@ def main() -> None:
     p.add_argument("--kill2-at", type=int, default=180)
     p.add_argument("--rejoin-after", type=float, default=1.0)
     p.add_argument("--tiny", action="store_true", help="small model of the same geometry (smoke run)")
+    p.add_argument("--links", choices=["nccl", "chan"], default="nccl",
+                   help="activation data plane: NCCL pair groups, or GPU-driven NVLink channels")
     a = p.parse_args()
+    DATA_PLANE["links"] = a.links
     world, rank = int(os.environ["WORLD_SIZE"]), int(os.environ["RANK"])
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
     torch.cuda.set_device(dev)
@@ -240,7 +252,8 @@ def main() -> None:
         s0 = [r for r in allr if r]
         steady = [statistics.median(r["dev_ms"][5:a.kill_at - 2]) for r in s0]
         ms = max(steady)
-        print(json.dumps({"pp": {"n_gpus": world, "stages": 2, "replicas_per_stage": n_s0, "batch": a.batch,
+        print(json.dumps({"pp": {"n_gpus": world, "links": a.links, "stages": 2, "replicas_per_stage": n_s0,
+                                 "batch": a.batch,
                                  "prompt": a.prompt, "decode_steps": a.steps, "step_ms_p50_max_over_ranks": ms,
                                  "decode_tok_s": round(n_s0 * a.batch / (ms / 1e3), 1),
                                  "handovers": [h for r in s0 for h in r["handovers"]],

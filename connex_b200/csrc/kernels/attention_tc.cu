@@ -47,22 +47,6 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
-// 2^x on the FMA pipe (x <= 0), to take half of the softmax exponentials off
-// the 16-per-clock special-function unit: x = n + f with n = round(x)
-// (1.5 * 2^23 magic add), f in [-0.5, 0.5]; 2^f from a cubic whose
-// coefficients were fitted here for minimum relative error on that interval
-// (Lawson iteration; max rel. error 1.2e-4, below bf16's 3.9e-3 step);
-// 2^n is added to the exponent field.  x is clamped at -126 (the result is
-// then ~1e-38, i.e. zero for a bf16 probability).
-__device__ __forceinline__ float poly_exp2(float x) {
-  constexpr float MAGIC = 12582912.0f;
-  x = fmaxf(x, -126.0f);
-  const float t = x + MAGIC;
-  const float f = x - (t - MAGIC);
-  const int n = __float_as_int(t) - __float_as_int(MAGIC);
-  const float p = fmaf(fmaf(fmaf(0.0553351939f, f, 0.2422975004f), f, 0.6932254434f), f, 1.0f);
-  return __int_as_float(__float_as_int(p) + (n << 23));
-}
 
 // MN-major, 128-byte-swizzled operand (V as the B operand of P.V): 64
 // contiguous elements per 128-byte row (rows = K index), 8-row groups 1024 B
@@ -242,10 +226,8 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
       uint32_t pk[BN / 2];
 #pragma unroll
       for (int e = 0; e < BN; e += 2) {
-        // pairs alternate between the SFU and the FMA-pipe polynomial
-        const float x0 = __uint_as_float(r[e]) - base, x1 = __uint_as_float(r[e + 1]) - base;
-        const float p0 = (e & 2) ? poly_exp2(x0) : fast_exp2(x0);
-        const float p1 = (e & 2) ? poly_exp2(x1) : fast_exp2(x1);
+        const float p0 = fast_exp2(__uint_as_float(r[e]) - base);
+        const float p1 = fast_exp2(__uint_as_float(r[e + 1]) - base);
         sum += p0 + p1;
         pk[e >> 1] = pack_bf16x2(p0, p1);
       }

@@ -1,0 +1,209 @@
+"""GPU-driven point-to-point channels over NVLink peer memory (no NCCL).
+
+A channel from endpoint A to endpoint B is a ring of ``slots`` x
+``slot_bytes`` in B's GPU memory plus two u32 counters: ``ready`` (in B's
+memory; A's copy kernel adds its CTA count when a ring message has landed)
+and ``credit`` (in A's memory; B stores the sequence number of the last
+message it has copied out).  Everything is stream-ordered on both sides:
+
+* sender, message ``k``: wait (bounded) until ``credit >= k - slots``, then
+  this package's copy kernel stores the tensors straight into B's ring slot
+  over the peer mapping and releases ``ready`` (system scope);
+* receiver: wait (bounded) until ``ready`` reaches the running target, copy
+  the slot out into the destination tensors, store ``credit = k`` into A's
+  memory.
+
+Messages larger than a slot go as consecutive slot-sized pieces.  Both sides
+derive the pieces and CTA counts from the tensor sizes, so only the tensor
+layout has to travel on the control channel (the step protocol's signal).
+Handles are exchanged through a ``torch.distributed`` store under
+``cxch/<sender>><receiver>/``.  ``ChanLinks`` has the interface of
+:class:`connex_b200.parallel.pplink.PairLinks` (``open_tx`` / ``open_rx``
+returning links with ``send`` / ``recv`` / ``done_event``), so a pipeline
+endpoint uses either data plane unchanged.
+"""
+from __future__ import annotations
+
+import pickle
+import threading
+from datetime import timedelta
+from typing import Dict, List, Optional, Sequence, Tuple
+
+import torch
+import torch.distributed as dist
+
+from connex_b200 import ops
+from connex_b200.parallel.peer import PeerHandle, PeerMapper, export_tensor
+
+ALIGN = 256
+CHAN_CTAS = 64
+
+
+def _layout(tensors: Sequence[torch.Tensor]) -> Tuple[List[Tuple[int, int]], int]:
+    offs, total = [], 0
+    for t in tensors:
+        n = t.numel() * t.element_size()
+        if n % 16:
+            raise ValueError("channel tensors must be a multiple of 16 bytes")
+        offs.append((total, n))
+        total += -(-n // ALIGN) * ALIGN
+    return offs, total
+
+
+def _pieces(offs, total: int, slot_bytes: int):
+    """[(piece start, piece len, [(tensor idx, t_off, p_off, n)])] covering the layout."""
+    out = []
+    for p0 in range(0, max(total, 1), slot_bytes):
+        p1 = min(total, p0 + slot_bytes)
+        parts = []
+        for i, (o, n) in enumerate(offs):
+            a, b = max(o, p0), min(o + n, p1)
+            if a < b:
+                parts.append((i, a - o, a - p0, b - a))
+        out.append((p0, p1 - p0, parts))
+    return out
+
+
+def _ctas(nbytes: int) -> int:
+    return max(1, min(CHAN_CTAS, -(-nbytes // 65536)))
+
+
+class _Stream:
+    def __init__(self, device):
+        self.device = device
+        self.stream = torch.cuda.Stream(device)
+        self.status = ops.new_status(device)
+
+    def done_event(self):
+        ev = torch.cuda.Event()
+        ev.record(self.stream)
+        return ev
+
+
+class ChanTx(_Stream):
+    def __init__(self, device, ring: int, ready: int, slots: int, slot_bytes: int, credit: torch.Tensor,
+                 timeout_s: float):
+        super().__init__(device)
+        self.ring, self.ready, self.slots, self.slot_bytes = ring, ready, slots, slot_bytes
+        self.credit = credit
+        self.seq = 0
+        self.timeout_s = timeout_s
+        self.sent = 0
+
+    def send(self, tensors: Sequence[torch.Tensor], after: Optional[torch.cuda.Event] = None):
+        tensors = [t.contiguous() for t in tensors]
+        offs, total = _layout(tensors)
+        cur = torch.cuda.current_stream(self.device)
+        self.stream.wait_stream(cur) if after is None else self.stream.wait_event(after)
+        with torch.cuda.device(self.device), torch.cuda.stream(self.stream):
+            for _, n, parts in _pieces(offs, total, self.slot_bytes):
+                self.seq += 1
+                if self.seq > self.slots:      # the slot's previous message must have been copied out
+                    ops.wait_flag(self.credit.data_ptr(), self.seq - self.slots, self.status, self.timeout_s)
+                base = self.ring + ((self.seq - 1) % self.slots) * self.slot_bytes
+                segs = [(tensors[i].data_ptr() + to, base + po, ln) for i, to, po, ln in parts]
+                segs_t = torch.tensor(segs, dtype=torch.int64).pin_memory().to(self.device, non_blocking=True)
+                ops.copy_segments(segs_t, -(-n // 16) * 16, ready=self.ready, max_ctas=_ctas(n), status=self.status)
+        for t in tensors:
+            t.record_stream(self.stream)
+        self.sent += len(tensors)
+
+
+class ChanRx(_Stream):
+    def __init__(self, device, slots: int, slot_bytes: int, timeout_s: float):
+        super().__init__(device)
+        self.slots, self.slot_bytes = slots, slot_bytes
+        self.ring = torch.empty(slots, slot_bytes, dtype=torch.uint8, device=device)
+        self.ready = torch.zeros(4, dtype=torch.int32, device=device)
+        self.credit_addr = 0            # the sender's credit counter (peer mapping)
+        self.seq = 0
+        self.expected = 0
+        self.timeout_s = timeout_s
+        self.received = 0
+
+    def recv(self, tensors: Sequence[torch.Tensor]):
+        offs, total = _layout(tensors)
+        with torch.cuda.device(self.device), torch.cuda.stream(self.stream):
+            for _, n, parts in _pieces(offs, total, self.slot_bytes):
+                self.seq += 1
+                self.expected = (self.expected + _ctas(n)) & 0xFFFFFFFF
+                ops.wait_flag(self.ready.data_ptr(), self.expected, self.status, self.timeout_s)
+                base = self.ring.data_ptr() + ((self.seq - 1) % self.slots) * self.slot_bytes
+                segs = [(base + po, tensors[i].data_ptr() + to, ln) for i, to, po, ln in parts]
+                segs_t = torch.tensor(segs, dtype=torch.int64).pin_memory().to(self.device, non_blocking=True)
+                ops.copy_segments(segs_t, -(-n // 16) * 16, status=self.status)
+                ops.write_flag(self.credit_addr, self.seq, self.ready)
+        for t in tensors:
+            t.record_stream(self.stream)
+        self.received += len(tensors)
+
+
+class ChanLinks:
+    """All channels of one endpoint ``me`` (the PairLinks interface)."""
+
+    def __init__(self, store: dist.Store, me: str, device, slots: int = 4, slot_bytes: int = 64 << 20,
+                 timeout_s: float = 10.0, wait_s: float = 60.0):
+        self.store, self.me = store, me
+        self.device = torch.device(device)
+        self.slots, self.slot_bytes = slots, slot_bytes
+        self.timeout_s, self.wait = timeout_s, timedelta(seconds=wait_s)
+        self.mapper = PeerMapper(self.device.index)
+        self._links: Dict[Tuple[str, bool], object] = {}
+        self._lock = threading.Lock()
+
+    @staticmethod
+    def _key(sender: str, receiver: str, what: str) -> str:
+        return f"cxch/{sender}>{receiver}/{what}"
+
+    def _get(self, key: str):
+        self.store.wait([key], self.wait)
+        return pickle.loads(self.store.get(key))
+
+    def open_tx(self, peer: str, gen: int = 0) -> ChanTx:
+        with self._lock:
+            hit = self._links.get((peer, True))
+        if hit is not None:
+            return hit
+        credit = torch.zeros(4, dtype=torch.int32, device=self.device)
+        self.store.set(self._key(self.me, peer, "tx"), pickle.dumps(export_tensor(credit).to_dict()))
+        rx = self._get(self._key(self.me, peer, "rx"))
+        ring = self.mapper.open(PeerHandle.from_dict(rx["ring"]))
+        ready = self.mapper.open(PeerHandle.from_dict(rx["ready"]))
+        link = ChanTx(self.device, ring, ready, rx["slots"], rx["slot_bytes"], credit, self.timeout_s)
+        with self._lock:
+            self._links[(peer, True)] = link
+        return link
+
+    def open_rx(self, peer: str, gen: int = 0) -> ChanRx:
+        with self._lock:
+            hit = self._links.get((peer, False))
+        if hit is not None:
+            return hit
+        link = ChanRx(self.device, self.slots, self.slot_bytes, self.timeout_s)
+        self.store.set(self._key(peer, self.me, "rx"), pickle.dumps({
+            "ring": export_tensor(link.ring).to_dict(), "ready": export_tensor(link.ready).to_dict(),
+            "slots": self.slots, "slot_bytes": self.slot_bytes}))
+        tx = self._get(self._key(peer, self.me, "tx"))
+        link.credit_addr = self.mapper.open(PeerHandle.from_dict(tx))
+        with self._lock:
+            self._links[(peer, False)] = link
+        return link
+
+    def get(self, peer: str, gen: int = 0, tx: bool = True):
+        return self._links.get((peer, tx))
+
+    def drop_peer(self, peer: str, abort: bool = True) -> int:
+        with self._lock:
+            keys = [k for k in self._links if k[0] == peer]
+            for k in keys:
+                self._links.pop(k)
+        return len(keys)
+
+    def check(self) -> None:
+        for l in list(self._links.values()):
+            ops.check_status(l.status, "p2p channel")
+
+    def close(self) -> None:
+        torch.cuda.synchronize(self.device)
+        self._links.clear()
+        self.mapper.close()

@@ -159,6 +159,8 @@ class StageRuntime:
         return t
 
     def compute(self, td: dict, missing: Sequence) -> dict:
+        if td.get("kind") == "warmup":      # link set-up step: echo, no model work
+            return {"kind": "warmup", "w": td["w"].clone()}
         rids = list(td[REQUEST_IDS])
         ctx = list(td[CX_CTX])
         n_new = list(td["n_new"])
