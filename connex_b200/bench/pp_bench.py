@@ -143,6 +143,8 @@ def stage0_main(args, rank, replica, dev, store, dir_addr):
     B, P, S = args.batch, args.prompt, args.steps
     rt = StageRuntime(cfg, 0, cfg.layers // 2, dev, num_blocks=B * (P + S + 16) // 16 + 64, max_tokens=B * (P + S),
                       max_batch=B, max_ctx=P + S + 16, seed=0)
+    if args.replay:
+        rt.enable_activation_log(B)
     ep, client = _make_endpoint(0, replica, dev, store, dir_addr)
     warmed = ep.warm_stage(1)          # every stage-1 replica's links are set up before traffic
     ep.auto_warm = True                # and a replica that (re)joins gets warmed in the background
@@ -180,7 +182,14 @@ def stage0_main(args, rank, replica, dev, store, dir_addr):
         nxt = nxt.tolist()
         if again:
             idx = [rids.index(r) for r in again]
-            fixed = prefill(idx)       # prompt + generated so far: its last position is this step's token
+            if args.replay:            # stage 0 still holds its part: replay its logged outputs
+                x, lens = rt.replay([rids[i] for i in idx])
+                hooks.reprefill_rids = []
+                out = link.step({"x": x, "kind": "prefill", "n_new": lens}, request_ids=[rids[i] for i in idx],
+                                num_computed=[0] * len(idx))
+                fixed = out["next"].tolist()
+            else:
+                fixed = prefill(idx)   # prompt + generated so far: its last position is this step's token
             for j, i in enumerate(idx):
                 nxt[i] = fixed[j]
             t_ok = time.time()
@@ -219,6 +228,8 @@ def main() -> None:
     p.add_argument("--kill2-at", type=int, default=180)
     p.add_argument("--rejoin-after", type=float, default=1.0)
     p.add_argument("--tiny", action="store_true", help="small model of the same geometry (smoke run)")
+    p.add_argument("--no-replay", dest="replay", action="store_false",
+                   help="after a failover, recompute stage 0 instead of replaying its logged outputs")
     p.add_argument("--links", choices=["nccl", "chan"], default="nccl",
                    help="activation data plane: NCCL pair groups, or GPU-driven NVLink channels")
     a = p.parse_args()
@@ -252,7 +263,8 @@ def main() -> None:
         s0 = [r for r in allr if r]
         steady = [statistics.median(r["dev_ms"][5:a.kill_at - 2]) for r in s0]
         ms = max(steady)
-        print(json.dumps({"pp": {"n_gpus": world, "links": a.links, "stages": 2, "replicas_per_stage": n_s0,
+        print(json.dumps({"pp": {"n_gpus": world, "links": a.links, "replay": a.replay, "stages": 2,
+                                 "replicas_per_stage": n_s0,
                                  "batch": a.batch,
                                  "prompt": a.prompt, "decode_steps": a.steps, "step_ms_p50_max_over_ranks": ms,
                                  "decode_tok_s": round(n_s0 * a.batch / (ms / 1e3), 1),

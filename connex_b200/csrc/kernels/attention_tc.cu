@@ -207,14 +207,19 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
       mbar_arrive(&s_free[s]);  // S[s] is in registers now
       const int key0 = j * BN;
       const bool mask = (key0 + BN - 1 > q0) || (key0 + BN > seq_len);
-      float mx = -INFINITY;
+      // raw scores stay unscaled: the scale is folded into one FFMA per
+      // element below (scale > 0, so the max commutes with it)
+      float mx_raw = -INFINITY;
 #pragma unroll
       for (int e = 0; e < BN; ++e) {
-        float v = __uint_as_float(r[e]) * scale_log2;
-        if (mask && (key0 + e > qpos || key0 + e >= seq_len)) v = -INFINITY;
-        r[e] = __float_as_uint(v);
-        mx = fmaxf(mx, v);
+        float v = __uint_as_float(r[e]);
+        if (mask && (key0 + e > qpos || key0 + e >= seq_len)) {
+          v = -INFINITY;
+          r[e] = __float_as_uint(v);
+        }
+        mx_raw = fmaxf(mx_raw, v);
       }
+      const float mx = mx_raw * scale_log2;
       float m_new = m;
       bool resc = false;
       if (j == 0 || mx > m + RESCALE_THRESHOLD) {  // lazy rescale
@@ -226,8 +231,8 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
       uint32_t pk[BN / 2];
 #pragma unroll
       for (int e = 0; e < BN; e += 2) {
-        const float p0 = fast_exp2(__uint_as_float(r[e]) - base);
-        const float p1 = fast_exp2(__uint_as_float(r[e + 1]) - base);
+        const float p0 = fast_exp2(fmaf(__uint_as_float(r[e]), scale_log2, -base));
+        const float p1 = fast_exp2(fmaf(__uint_as_float(r[e + 1]), scale_log2, -base));
         sum += p0 + p1;
         pk[e >> 1] = pack_bf16x2(p0, p1);
       }

@@ -23,6 +23,13 @@ constexpr int WS_MAX_DST = 8;
 int wsync(const int64_t* jobs_dev, const int64_t* jobs_host, int n_jobs, int64_t dst_bytes, const uint64_t* dst_bases,
           const uint64_t* dst_flags, int n_dst, uint64_t mc_base, uint64_t mc_flag, int max_ctas, cudaStream_t s);
 
+// P2P channel copy (chan.cu): wait, copy up to CH_MAX_SEGS segments, signal
+// (mode 1: +1 per CTA on `signal`; mode 2: the last CTA stores `value`).
+constexpr int CH_MAX_SEGS = 8;
+void chan_copy(const uint64_t* src, const uint64_t* dst, const uint64_t* bytes, int n, const uint32_t* wait_on,
+               uint32_t wait_target, uint64_t timeout_ns, uint32_t* signal, uint32_t value, int mode,
+               uint32_t* done_ctr, int ctas, int* status, cudaStream_t s);
+
 void wait_flag(const uint32_t* flag, uint32_t target, uint64_t timeout_ns, int* status, cudaStream_t s);
 void write_flag(uint32_t* flag, uint32_t value, bool add, cudaStream_t s);
 

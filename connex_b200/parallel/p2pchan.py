@@ -6,12 +6,12 @@ memory; A's copy kernel adds its CTA count when a ring message has landed)
 and ``credit`` (in A's memory; B stores the sequence number of the last
 message it has copied out).  Everything is stream-ordered on both sides:
 
-* sender, message ``k``: wait (bounded) until ``credit >= k - slots``, then
-  this package's copy kernel stores the tensors straight into B's ring slot
-  over the peer mapping and releases ``ready`` (system scope);
-* receiver: wait (bounded) until ``ready`` reaches the running target, copy
-  the slot out into the destination tensors, store ``credit = k`` into A's
-  memory.
+* sender, message ``k``: one kernel waits (bounded) until
+  ``credit >= k - slots``, stores the tensors straight into B's ring slot
+  over the peer mapping and releases ``ready`` (+1 per CTA, system scope);
+* receiver: one kernel waits (bounded) until ``ready`` reaches the running
+  target, copies the slot out into the destination tensors, and its last
+  CTA stores ``credit = k`` into A's memory (``chan.cu``).
 
 Messages larger than a slot go as consecutive slot-sized pieces.  Both sides
 derive the pieces and CTA counts from the tensor sizes, so only the tensor
@@ -68,6 +68,12 @@ def _ctas(nbytes: int) -> int:
     return max(1, min(CHAN_CTAS, -(-nbytes // 65536)))
 
 
+def _groups(parts):
+    """Launch groups of at most CH_MAX_SEGS segments (both sides split alike)."""
+    m = ops._C.CH_MAX_SEGS
+    return [parts[i:i + m] for i in range(0, len(parts), m)] or [[]]
+
+
 class _Stream:
     def __init__(self, device):
         self.device = device
@@ -95,15 +101,19 @@ class ChanTx(_Stream):
         offs, total = _layout(tensors)
         cur = torch.cuda.current_stream(self.device)
         self.stream.wait_stream(cur) if after is None else self.stream.wait_event(after)
+        tmo = int(self.timeout_s * 1e9)
         with torch.cuda.device(self.device), torch.cuda.stream(self.stream):
             for _, n, parts in _pieces(offs, total, self.slot_bytes):
                 self.seq += 1
-                if self.seq > self.slots:      # the slot's previous message must have been copied out
-                    ops.wait_flag(self.credit.data_ptr(), self.seq - self.slots, self.status, self.timeout_s)
                 base = self.ring + ((self.seq - 1) % self.slots) * self.slot_bytes
-                segs = [(tensors[i].data_ptr() + to, base + po, ln) for i, to, po, ln in parts]
-                segs_t = torch.tensor(segs, dtype=torch.int64).pin_memory().to(self.device, non_blocking=True)
-                ops.copy_segments(segs_t, -(-n // 16) * 16, ready=self.ready, max_ctas=_ctas(n), status=self.status)
+                for gi, grp in enumerate(_groups(parts)):
+                    # the slot's previous message must have been copied out first
+                    wait = self.credit.data_ptr() if (gi == 0 and self.seq > self.slots) else 0
+                    nb = sum(p[3] for p in grp)
+                    ops._C.chan_copy([tensors[i].data_ptr() + to for i, to, _, _ in grp], [base + po for _, _, po, _ in grp],
+                                     [ln for *_, ln in grp], wait, (self.seq - self.slots) & 0xFFFFFFFF, tmo,
+                                     self.ready, 0, 1, 0, _ctas(nb), self.status)
+                    ops._n()
         for t in tensors:
             t.record_stream(self.stream)
         self.sent += len(tensors)
@@ -114,7 +124,7 @@ class ChanRx(_Stream):
         super().__init__(device)
         self.slots, self.slot_bytes = slots, slot_bytes
         self.ring = torch.empty(slots, slot_bytes, dtype=torch.uint8, device=device)
-        self.ready = torch.zeros(4, dtype=torch.int32, device=device)
+        self.ready = torch.zeros(4, dtype=torch.int32, device=device)      # [0] ready, [1] CTA counter
         self.credit_addr = 0            # the sender's credit counter (peer mapping)
         self.seq = 0
         self.expected = 0
@@ -123,16 +133,23 @@ class ChanRx(_Stream):
 
     def recv(self, tensors: Sequence[torch.Tensor]):
         offs, total = _layout(tensors)
+        tmo = int(self.timeout_s * 1e9)
+        ready, ctr = self.ready.data_ptr(), self.ready.data_ptr() + 4
         with torch.cuda.device(self.device), torch.cuda.stream(self.stream):
             for _, n, parts in _pieces(offs, total, self.slot_bytes):
                 self.seq += 1
-                self.expected = (self.expected + _ctas(n)) & 0xFFFFFFFF
-                ops.wait_flag(self.ready.data_ptr(), self.expected, self.status, self.timeout_s)
+                groups = _groups(parts)
+                for grp in groups:
+                    self.expected = (self.expected + _ctas(sum(p[3] for p in grp))) & 0xFFFFFFFF
                 base = self.ring.data_ptr() + ((self.seq - 1) % self.slots) * self.slot_bytes
-                segs = [(base + po, tensors[i].data_ptr() + to, ln) for i, to, po, ln in parts]
-                segs_t = torch.tensor(segs, dtype=torch.int64).pin_memory().to(self.device, non_blocking=True)
-                ops.copy_segments(segs_t, -(-n // 16) * 16, status=self.status)
-                ops.write_flag(self.credit_addr, self.seq, self.ready)
+                for gi, grp in enumerate(groups):
+                    last = gi == len(groups) - 1
+                    nb = sum(p[3] for p in grp)
+                    ops._C.chan_copy([base + po for _, _, po, _ in grp], [tensors[i].data_ptr() + to for i, to, _, _ in grp],
+                                     [ln for *_, ln in grp], ready, self.expected, tmo,
+                                     self.credit_addr if last else 0, self.seq & 0xFFFFFFFF, 2 if last else 0, ctr,
+                                     _ctas(nb), self.status)
+                    ops._n()
         for t in tensors:
             t.record_stream(self.stream)
         self.received += len(tensors)

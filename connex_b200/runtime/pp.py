@@ -135,6 +135,39 @@ class StageRuntime:
         self.held: Dict[object, int] = {}
         self.ws = ops.decode_workspace(max_batch, cfg.heads, max_ctx, self.device)
         self.steps = 0
+        self.act: Optional[torch.Tensor] = None      # activation log (non-last stages)
+        self.act_slot: Dict[object, int] = {}
+
+    def enable_activation_log(self, max_requests: int) -> None:
+        """Keep every output row of this stage per request ([requests, max_ctx,
+        hidden] bf16, ~0.6 GB for 64 x 1280 x 4096).  After a failover the
+        next stage's new replica is refilled by replaying these rows
+        (:meth:`replay`) instead of recomputing this stage's layers."""
+        if self.model.is_last:
+            return
+        self.act = torch.empty(max_requests, self.max_ctx, self.cfg.hidden, dtype=torch.bfloat16,
+                               device=self.device)
+
+    def _log(self, rids, ctx, n_new, out) -> None:
+        slots, poss = [], []
+        for r, c, n in zip(rids, ctx, n_new):
+            sl = self.act_slot.get(r)
+            if sl is None:
+                sl = self.act_slot[r] = len(self.act_slot)
+                if sl >= self.act.shape[0]:
+                    raise MemoryError("activation log full")
+            slots += [sl] * n
+            poss += range(c, c + n)
+        idx = (torch.tensor(slots, dtype=torch.int64).pin_memory().to(self.device, non_blocking=True),
+               torch.tensor(poss, dtype=torch.int64).pin_memory().to(self.device, non_blocking=True))
+        self.act.index_put_(idx, out)
+
+    def replay(self, rids) -> tuple:
+        """(rows [sum of tokens, hidden], tokens per request) of the logged
+        outputs of ``rids`` -- the input of a re-prefill on the next stage."""
+        lens = [self.held[r] for r in rids]
+        x = torch.cat([self.act[self.act_slot[r], :n] for r, n in zip(rids, lens)])
+        return x, lens
 
     # EngineHooks
     def kv_held(self, rid) -> int:
@@ -201,6 +234,8 @@ class StageRuntime:
                       max_ctx=max(lens), workspace=self.ws,
                       rows=torch.arange(B, dtype=torch.int32, device=dev))
         out = self.model.run(inp, positions, slot_t, prefill=prefill, B=B, **kw)
+        if self.act is not None:
+            self._log(rids, ctx, n_new, out)
         for r, c, n in zip(rids, ctx, n_new):
             if r in miss:           # computed without its KV: not held here; stage 0 prefills it again
                 self.release([r])

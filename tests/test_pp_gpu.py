@@ -16,6 +16,7 @@ def test_two_stage_split_matches_whole_model():
     dev = torch.device("cuda", 0)
     cfg = LlamaConfig.tiny(layers=4)
     s0 = StageRuntime(cfg, 0, 2, dev, num_blocks=256, max_tokens=2048, max_batch=8, max_ctx=512)
+    s0.enable_activation_log(8)
     s1 = StageRuntime(cfg, 2, 4, dev, num_blocks=256, max_tokens=2048, max_batch=8, max_ctx=512)
     whole = LlamaWeights(cfg=cfg, embed=s0.weights.embed, layers=s0.weights.layers + s1.weights.layers,
                          final_norm=s1.weights.final_norm, lm_head=s1.weights.lm_head)
@@ -59,6 +60,14 @@ def test_two_stage_split_matches_whole_model():
         assert got.tolist() == ref.tolist()
         cur = ref.clone()
         ctx = [c + 1 for c in ctx]
+    # failover: a fresh replica of stage 1 is refilled from stage 0's logged outputs (no stage-0
+    # recompute) and then predicts exactly what the old replica would have
+    s1b = StageRuntime(cfg, 2, 4, dev, num_blocks=256, max_tokens=2048, max_batch=8, max_ctx=512)
+    x, lens2 = s0.replay(rids)
+    assert lens2 == ctx
+    nb = s1b.compute({"kind": "prefill", REQUEST_IDS: rids, CX_CTX: [0, 0, 0], "n_new": lens2, "x": x}, [])["next"]
+    torch.cuda.synchronize()
+    assert nb.tolist() == cur.tolist()
     # a stage that lost a request's KV reports it and does not claim it
     td = {"kind": "decode", REQUEST_IDS: ["zz"], CX_CTX: [40], "n_new": [1], "ids": cur[:1].to(torch.int32)}
     s0.compute(td, ["zz"])
