@@ -192,12 +192,8 @@ def main() -> None:
         if step > a.migrate_at and not committed and commit_at is None and rank == 0:
             if int(store.add("copied", 0)) >= len(receivers):
                 store.set("commit_at", str(step + 2))
-        if step > a.migrate_at and commit_at is None:
-            try:
-                store.wait(["commit_at"], timedelta(milliseconds=1))
-                commit_at = int(store.get("commit_at"))
-            except Exception:  # noqa: BLE001 - not yet
-                pass
+        if step > a.migrate_at and commit_at is None and store.check(["commit_at"]):
+            commit_at = int(store.get("commit_at"))
         if commit_at is not None and step == commit_at and not committed:
             table.finish_moves(moves)          # epoch 2: the new slots are routable
             table.commit()

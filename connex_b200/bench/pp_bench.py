@@ -212,11 +212,8 @@ def stage0_main(args, rank, replica, dev, store, dir_addr):
 
 
 def _has(store, key) -> bool:
-    try:
-        store.wait([key], timedelta(milliseconds=1))
-        return True
-    except Exception:  # noqa: BLE001
-        return False
+    """Non-blocking existence check (a timed-out ``wait`` costs a socket poll)."""
+    return bool(store.check([key]))
 
 
 def main() -> None:
