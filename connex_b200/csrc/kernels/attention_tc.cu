@@ -74,14 +74,16 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
   }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
   uint64_t* q_full = bars + 0;
-  uint64_t* kv_full = bars + 1;   // [2]
-  uint64_t* kv_empty = bars + 3;  // [2]
-  uint64_t* s_full = bars + 5;    // [2]
+  uint64_t* k_full = bars + 1;    // [2]  K and V have their own rings: K_j is released as
+  uint64_t* k_empty = bars + 3;   // [2]  soon as S_j = Q.K_j^T is done, so K_{j+2} streams in
+  uint64_t* s_full = bars + 5;    // [2]  while softmax j / P_j.V_j are still running
   uint64_t* s_free = bars + 7;    // [2]
   uint64_t* p_full = bars + 9;
   uint64_t* pv_done = bars + 10;
   uint64_t* drain = bars + 11;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 12);
+  uint64_t* v_full = bars + 12;   // [2]
+  uint64_t* v_empty = bars + 14;  // [2]
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
 
   const int tile = n_tiles - 1 - (int)blockIdx.x;  // heaviest (latest) tiles first
   const int h = blockIdx.y;
@@ -97,8 +99,10 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
   if (warp == 0 && lane == 0) {
     mbar_init(q_full, 1);
     for (int s = 0; s < 2; ++s) {
-      mbar_init(&kv_full[s], 1);
-      mbar_init(&kv_empty[s], 1);
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
       mbar_init(&s_full[s], 1);
       mbar_init(&s_free[s], 128);
     }
@@ -125,18 +129,31 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
       mbar_arrive_expect_tx(q_full, 2 * Q_HALF);
       tma_load_2d(smem + OFF_Q, &tmq, q_full, qcol, row0);
       tma_load_2d(smem + OFF_Q + Q_HALF, &tmq, q_full, qcol + 64, row0);
-      for (int j = 0; j < nkv; ++j) {
+      // K_j goes out before V_{j-1}: K stages free up earlier (after Q.K^T)
+      auto load_k = [&](int j) -> bool {
         const int s = j & 1;
-        if (!mbar_wait(&kv_empty[s], ((j >> 1) & 1) ^ 1, status)) break;
-        const int r = seq_start + j * BN;
-        mbar_arrive_expect_tx(&kv_full[s], 2 * KV_TILE);
+        if (!mbar_wait(&k_empty[s], ((j >> 1) & 1) ^ 1, status)) return false;
+        mbar_arrive_expect_tx(&k_full[s], KV_TILE);
         uint8_t* kb = smem + OFF_K + s * KV_TILE;
+        tma_load_2d(kb, &tmkv, &k_full[s], kcol, seq_start + j * BN);
+        tma_load_2d(kb + KV_HALF, &tmkv, &k_full[s], kcol + 64, seq_start + j * BN);
+        return true;
+      };
+      auto load_v = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait(&v_empty[s], ((j >> 1) & 1) ^ 1, status)) return false;
+        mbar_arrive_expect_tx(&v_full[s], KV_TILE);
         uint8_t* vb = smem + OFF_V + s * KV_TILE;
-        tma_load_2d(kb, &tmkv, &kv_full[s], kcol, r);
-        tma_load_2d(kb + KV_HALF, &tmkv, &kv_full[s], kcol + 64, r);
-        tma_load_2d(vb, &tmkv, &kv_full[s], vcol, r);
-        tma_load_2d(vb + KV_HALF, &tmkv, &kv_full[s], vcol + 64, r);
+        tma_load_2d(vb, &tmkv, &v_full[s], vcol, seq_start + j * BN);
+        tma_load_2d(vb + KV_HALF, &tmkv, &v_full[s], vcol + 64, seq_start + j * BN);
+        return true;
+      };
+      bool good = true;
+      for (int j = 0; j < nkv && good; ++j) {
+        good = load_k(j);
+        if (good && j >= 1) good = load_v(j - 1);
       }
+      if (good) load_v(nkv - 1);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -147,6 +164,7 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
       bool ok = mbar_wait(q_full, 0, status);
       bool issued = false;
       auto issue_pv = [&](int jj) -> bool {
+        if (!mbar_wait(&v_full[jj & 1], (jj >> 1) & 1, status)) return false;
         if (!mbar_wait(p_full, jj & 1, status)) return false;
         tc_fence_after();
         const uint32_t sV = smem_u32(smem + OFF_V + (jj & 1) * KV_TILE);
@@ -156,12 +174,12 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
                     (jj > 0 || kk > 0) ? 1u : 0u);
         }
         umma_commit(pv_done);
-        umma_commit(&kv_empty[jj & 1]);
+        umma_commit(&v_empty[jj & 1]);
         return true;
       };
       for (int j = 0; j < nkv && ok; ++j) {
         const int s = j & 1;
-        if (!mbar_wait(&kv_full[s], (j >> 1) & 1, status)) { ok = false; break; }
+        if (!mbar_wait(&k_full[s], (j >> 1) & 1, status)) { ok = false; break; }
         if (!mbar_wait(&s_free[s], ((j >> 1) & 1) ^ 1, status)) { ok = false; break; }
         tc_fence_after();
         const uint32_t sK = smem_u32(smem + OFF_K + s * KV_TILE);
@@ -172,6 +190,7 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
         }
         issued = true;
         umma_commit(&s_full[s]);
+        umma_commit(&k_empty[s]);      // K_j is no longer needed once S_j is done
         if (j >= 1 && !issue_pv(j - 1)) { ok = false; break; }
       }
       if (ok) ok = issue_pv(nkv - 1);
