@@ -138,7 +138,7 @@ def _time(fn, iters: int, warmup: int, barrier) -> float:
 
 
 def run_ep_bench(world: int, rank: int, device, cpu_group=None, nccl_group=None,
-                 tokens=(128, 4096), iters: int = 20, warmup: int = 5) -> Dict:
+                 tokens=(128, 4096), iters: int = 20, warmup: int = 5, failover: bool = False) -> Dict:
     barrier = (lambda: dist.barrier(group=cpu_group)) if world > 1 else (lambda: None)
     fused = FusedEP(world, rank, device, max(tokens), cpu_group)
     res: Dict = {}
@@ -159,13 +159,40 @@ def run_ep_bench(world: int, rank: int, device, cpu_group=None, nccl_group=None,
                        iters, warmup, barrier)
         ops.check_status(fused.bufs.status, "ep")
         res[T] = {"cx_us": t_cx, "nccl_us": t_nccl, "max_err": err, "scale": scale}
+    if failover and world > 1:
+        res["failover_ms"] = ep_failover_ms(fused, world, rank, device, barrier, x, idx, w)
     fused.close()
     return res
 
 
+def ep_failover_ms(fused: "FusedEP", world: int, rank: int, device, barrier, x, idx, w) -> float:
+    """The last rank leaves between forwards; the others learn it from the
+    store, stop routing to its experts, mark it dead in the EP layer (no
+    rebuild) and run the next forward.  Returns leave -> that forward done
+    (host clock of the box, ms); the leaving rank returns 0."""
+    import time
+    store = dist.distributed_c10d._get_default_store()
+    victim = world - 1
+    barrier()
+    torch.cuda.synchronize(device)
+    if rank == victim:
+        store.set("ep_failover/t", repr(time.time()))
+        return 0.0
+    store.wait(["ep_failover/t"])
+    t_leave = float(store.get("ep_failover/t"))
+    S = E // world
+    cnt = fused.cnt.clone()
+    cnt[victim * S:(victim + 1) * S] = 0          # its experts are no longer routable
+    fused.layer.mark_dead(victim)
+    fused.layer.forward(x, idx, w, fused.l2p, cnt)
+    torch.cuda.synchronize(device)
+    ops.check_status(fused.bufs.status, "ep after failover")
+    return (time.time() - t_leave) * 1e3
+
+
 def reduce_max(per_rank: List[Dict]) -> Dict:
     out = {}
-    for T in per_rank[0]:
+    for T in [k for k in per_rank[0] if k != "failover_ms"]:
         out[str(T)] = {k: max(r[T][k] for r in per_rank) for k in ("cx_us", "nccl_us", "max_err", "scale")}
         out[str(T)]["speedup_vs_nccl"] = round(out[str(T)]["nccl_us"] / out[str(T)]["cx_us"], 2)
         out[str(T)] = {k: (float(f"{v:.4g}") if isinstance(v, float) else v) for k, v in out[str(T)].items()}

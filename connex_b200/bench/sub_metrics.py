@@ -1,10 +1,12 @@
 """Secondary metrics of the flagship benchmark line, measured in the same job
-right after the PD steps: the fused EP MoE layer latency (dispatch + expert
-GEMMs + combine, Qwen3-30B-A3B layer geometry, 128 tokens per rank) against
-the NCCL all-to-all baseline, and the fused Llama-3-8B weight broadcast
-(fp32 trainer weights -> bf16 engine layout on every other GPU) against an
-NCCL broadcast.  Both are device-timed, max over ranks; every rank must
-call :func:`run_sub_metrics` (it is collective when N > 1).
+right after the PD steps: the fused Llama-3-8B weight broadcast (fp32
+trainer weights -> bf16 engine layout on every other GPU) against an NCCL
+broadcast, the fused EP MoE layer latency (dispatch + expert GEMMs +
+combine, Qwen3-30B-A3B layer geometry, 128 tokens per rank) against the
+NCCL all-to-all baseline, and (N > 1) the EP failover time: the last rank
+leaves, the others route around it and finish their next forward (host
+clock of the box).  The rest are device-timed, max over ranks.  Every rank
+must call :func:`run_sub_metrics` (it is collective when N > 1).
 """
 from __future__ import annotations
 
@@ -20,9 +22,9 @@ def run_sub_metrics(world: int, rank: int, dev, layers: int = 32) -> Optional[di
     from connex_b200.bench.wsync_bench import run as run_wsync
     from connex_b200.models.llama import LlamaConfig
     cpu = dist.new_group(backend="gloo", timeout=timedelta(seconds=180)) if world > 1 else None
-    ep = run_ep_bench(world, rank, dev, cpu, None, tokens=(128,), iters=10, warmup=3)
-    torch.cuda.empty_cache()
     ws = run_wsync(LlamaConfig(layers=layers), iters=3, warmup=2)
+    torch.cuda.empty_cache()
+    ep = run_ep_bench(world, rank, dev, cpu, None, tokens=(128,), iters=10, warmup=3, failover=True)
     torch.cuda.empty_cache()
     allr = [ep]
     if world > 1:
@@ -33,6 +35,8 @@ def run_sub_metrics(world: int, rank: int, dev, layers: int = 32) -> Optional[di
     e = reduce_max(allr)["128"]
     out = {"ep_layer_us_t128": e["cx_us"], "ep_layer_us_t128_nccl_baseline": e["nccl_us"],
            "weight_sync_bytes": ws["engine_bytes"]}
+    if world > 1:
+        out["ep_failover_ms"] = round(max(r.get("failover_ms", 0.0) for r in allr), 2)
     if world == 1:
         out["weight_convert_ms_local"] = round(ws["local_ms"], 3)
     else:
