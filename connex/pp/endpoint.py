@@ -56,6 +56,13 @@ from connex.pp.steps import CorrFilter, ReplyCache, StepIds
 log = logging.getLogger("connex.pp.endpoint")
 
 DEFAULT_RECV_TIMEOUT_S = float(os.getenv("CONNEXTE_RECV_TIMEOUT_MS", "8000")) / 1000
+# CONNEXTE_TRACE=/path/prefix: append "time stage event corr" lines to
+# <prefix>.stage<N>.txt (send called / signal posted / arrived / receive done)
+# to rebuild the cross-stage timeline of each step.  CONNEXTE_PROFILE=1: log
+# mean milliseconds per phase every CONNEXTE_PROFILE_EVERY receives.
+TRACE_PREFIX = os.getenv("CONNEXTE_TRACE", "")
+PROFILE = os.getenv("CONNEXTE_PROFILE", "0") == "1"
+PROFILE_EVERY = int(os.getenv("CONNEXTE_PROFILE_EVERY", "64"))
 PROBE_TIMEOUT_S = float(os.getenv("CONNEXTE_PROBE_TIMEOUT_S", "0.5") or "0.5")
 ACK_TIMEOUT_S = float(os.getenv("CONNEXTE_GDR_ACK_TIMEOUT_S", "10.0"))
 
@@ -76,6 +83,44 @@ def probe_tcp(address: Optional[str], timeout_s: float = PROBE_TIMEOUT_S) -> Opt
         return False
     except OSError:
         return None
+
+
+class _Tracer:
+    def __init__(self, prefix: str, stage: int):
+        self.f = open(f"{prefix}.stage{stage}.txt", "a", buffering=1 << 16) if prefix else None
+        self.stage = stage
+        self.lock = threading.Lock()
+
+    def __call__(self, event: str, corr) -> None:
+        if self.f is not None:
+            with self.lock:
+                self.f.write(f"{time.time():.6f} {self.stage} {event} {corr}\n")
+
+    def close(self) -> None:
+        if self.f is not None:
+            self.f.close()
+
+
+class _Profiler:
+    """Per-phase wall time (ms), logged as means every ``every`` receives."""
+
+    def __init__(self, enabled: bool, every: int, stage: int):
+        self.enabled, self.every, self.stage = enabled, every, stage
+        self.acc: Dict[str, float] = defaultdict(float)
+        self.n = 0
+
+    def add(self, phase: str, seconds: float) -> None:
+        if self.enabled:
+            self.acc[phase] += seconds * 1e3
+
+    def tick(self) -> None:
+        if not self.enabled:
+            return
+        self.n += 1
+        if self.n % self.every == 0:
+            log.info("stage %s phases (mean ms over %d): %s", self.stage, self.every,
+                     {k: round(v / self.every, 3) for k, v in self.acc.items()})
+            self.acc.clear()
 
 
 class ChainFailed(RuntimeError):
@@ -140,6 +185,8 @@ class PipelineEndpoint:
         self.deregistered: set = set()
         self.codec = wire.LayoutCodec()
         self.stats = defaultdict(int)
+        self.trace = _Tracer(TRACE_PREFIX, stage_idx)
+        self.prof = _Profiler(PROFILE, PROFILE_EVERY, stage_idx)
         self._ring = None
         if self.data == "engine":
             self._setup_ring(ring_bytes)
@@ -232,6 +279,8 @@ class PipelineEndpoint:
 
     def _send(self, address: str, td: dict, corr: int, origin: str) -> None:
         import torch
+        self.trace("send_called", corr)
+        t0 = time.perf_counter()
         tensors, nt, layout, total, layout_b = self._pack(td)
         nt_b = pickle.dumps(nt) if nt else b""
         token, src, extra = 0, 0, []
@@ -265,6 +314,8 @@ class PipelineEndpoint:
             if self.data == "link" and tensors:
                 self.links.open_tx(self._peer_name(address)).send([v.contiguous() for _, v in tensors])
         self.stats["sent"] += 1
+        self.trace("signaled", corr)
+        self.prof.add("send", time.perf_counter() - t0)
 
     def _peer_name(self, address: str) -> str:
         """Link identity of the endpoint at ``address`` (carried after '#')."""
@@ -289,6 +340,7 @@ class PipelineEndpoint:
             ready = self._receive_tensors(sig, layout, td, frames[1:])
         if token and ack_ep:
             self._post(ack_ep, [wire.encode_ack(token)])
+        self.trace("arrived", sig.corr)
         self._deliver(_Msg(sig.corr, td, origin, sig.url, ready))
 
     def _receive_tensors(self, sig, layout, td, extra):
@@ -459,6 +511,7 @@ class PipelineEndpoint:
         self._send(addr, td, corr, self.address)
 
     def recv_step(self, corr: int, timeout_s: Optional[float] = None) -> Optional[dict]:
+        w0 = time.perf_counter()
         deadline = time.monotonic() + (self._recv_timeout_s() if timeout_s is None else timeout_s)
         with self._cv:
             while corr not in self._done:
@@ -483,6 +536,9 @@ class PipelineEndpoint:
             self.slowest_step_s = max(self.slowest_step_s * 0.99, dt)
             self.metrics.observe("step_latency", dt)
         self._sent_epoch.pop(corr, None)
+        self.trace("recv_done", corr)
+        self.prof.add("recv_wait", time.perf_counter() - w0)
+        self.prof.tick()
         return m.td
 
     def abandon_step(self, corr: int) -> None:
@@ -494,10 +550,14 @@ class PipelineEndpoint:
 
     # ------------------------------------------------------ later stages
     def recv_forward(self, timeout_s: Optional[float] = None):
+        w0 = time.perf_counter()
         try:
             m = self.inbox.get(timeout=self._recv_timeout_s() if timeout_s is None else timeout_s)
         except queue.Empty:
             return None, None
+        self.trace("recv_done", m.corr)
+        self.prof.add("recv_wait", time.perf_counter() - w0)
+        self.prof.tick()
         if m.ready is not None:
             import torch
             torch.cuda.current_stream().wait_event(m.ready)
@@ -534,6 +594,7 @@ class PipelineEndpoint:
     def close(self) -> None:
         self._stop.set()
         self._io.join(timeout=2)
+        self.trace.close()
         for s in list(self._dealers.values()) + [self.router, self._wake_rx, self._wake_tx]:
             s.close(0)
         if self._ring is not None:

@@ -228,3 +228,28 @@ def test_backend_selection(monkeypatch):
     assert backend_from_env(has_cuda=True) == "nccl"
     monkeypatch.delenv("CONNEX_PP_BACKEND")
     assert engine_port(1, 2) == 51201
+
+
+def test_trace_and_profile_hooks(tmp_path, monkeypatch, caplog):
+    import logging
+    import connex.pp.endpoint as E
+    monkeypatch.setattr(E, "TRACE_PREFIX", str(tmp_path / "tr"))
+    monkeypatch.setattr(E, "PROFILE", True)
+    monkeypatch.setattr(E, "PROFILE_EVERY", 2)
+    mem, eps = _chain(2)
+    stop = threading.Event()
+    _serve(eps[1], lambda td: _add_stage(td, 1), stop)
+    try:
+        link = Stage0Link(eps[0], Hooks(), recv_timeout_s=2.0)
+        with caplog.at_level(logging.INFO, logger="connex.pp.endpoint"):
+            for i in range(4):
+                link.step({"x": torch.zeros(2), "step": i})
+    finally:
+        stop.set()
+        for ep in eps:
+            ep.close()
+    lines = (tmp_path / "tr.stage0.txt").read_text().split("\n")
+    events = [ln.split()[2] for ln in lines if ln]
+    assert events.count("send_called") == 4 and events.count("recv_done") == 4
+    assert (tmp_path / "tr.stage1.txt").read_text().count("arrived") == 4
+    assert any("phases" in r.getMessage() for r in caplog.records)
