@@ -48,7 +48,7 @@ class ExpertStore:
         if self.t is not None:
             for ps in self.layers:
                 for p in ps:
-                    self.t.register(p.data_ptr(), p.numel() * p.element_size())
+                    self.t.register(p)
         self.stats: dict = defaultdict(float)
         if ipc is None:
             ipc = os.environ.get("CONNEX_EP_IPC", "1") != "0"
@@ -148,17 +148,19 @@ class ExpertStore:
             return self._copy_nvlink(bases, moves, S)
         if self.t is None:
             raise TransferError(f"no transport to reach rank {peer['rank']}")
-        ops = []
+        # one batch per destination tensor: (remote addr, byte offset in the tensor, bytes)
+        per_tensor = defaultdict(list)
         for m in moves:
             si, di = m.src % S, m.dst % S
-            for i, p in enumerate(self.layers[m.layer]):
-                rb = self.row_bytes(m.layer, i)
-                ops.append((p.data_ptr() + di * rb, peer["layers"][m.layer][i][0] + si * rb, rb))
-        rc = self.t.read_many(peer["url"], ops, timeout_ms) if hasattr(self.t, "read_many") else \
-            self.t.read(peer["url"], ops)
-        if rc not in (0, None):
-            raise TransferError(f"read from rank {peer['rank']} returned {rc}")
-        self.stats["bytes"] += sum(n for _, _, n in ops)
+            for i, (base, rb) in enumerate(peer["layers"][m.layer]):
+                per_tensor[(m.layer, i)].append((base + si * rb, di * rb, rb))
+        batches = [(self.layers[l][i], ops) for (l, i), ops in per_tensor.items()]
+        if hasattr(self.t, "read_many"):
+            self.t.read_many(peer["url"], batches, timeout_ms=timeout_ms)
+        else:
+            for dst, ops in batches:
+                self.t.read_batch(peer["url"], ops, dst, timeout_ms=timeout_ms)
+        self.stats["bytes"] += sum(n for _, ops in batches for _, _, n in ops)
 
     def _copy_nvlink(self, bases, moves, S: int) -> None:
         """All rows from one peer in one copy_segments launch (bounded CTAs)."""
@@ -192,3 +194,11 @@ class ExpertStore:
         """NaN-fill a slot (negative control: a routed token would turn NaN)."""
         for p in self.layers[layer]:
             p[slot_local].fill_(float("nan"))
+
+
+def moves_by_rank(moves, slots_per_rank: int) -> dict:
+    """``{destination rank: [moves]}`` (reference ``connex/ep/mover.py:236``)."""
+    out = defaultdict(list)
+    for m in moves:
+        out[m.dst // slots_per_rank].append(m)
+    return dict(out)

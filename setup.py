@@ -74,6 +74,11 @@ setup(
         "vllm.general_plugins": [
             "connex_pd = connex.adapters.vllm.plugin:register",
             "connex_rl = connex.rl.vllm_plugin:register",
+            "connex_ep = connex.ep.vllm_ext:register",
+        ],
+        "sglang.srt.plugins": [
+            "connex = connex.adapters.sglang.pd_backend:register",
+            "connex_ep = connex.ep.sglang_ext:register",
         ],
     },
 )

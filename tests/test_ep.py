@@ -62,7 +62,8 @@ def test_plan_repair_prefers_empty_then_most_replicated():
     assert len(mv) == 1 and mv[0].expert in (1, 2) and mv[0].evicts == 0
 
 
-def _stores(R, S, L, E, dtype=torch.float32):
+def _stores(R, S, L, E, dtype=torch.float32, transport=False):
+    from connex.rl.transport import LocalTransport
     stores = []
     for r in range(R):
         layers = []
@@ -71,31 +72,14 @@ def _stores(R, S, L, E, dtype=torch.float32):
             for i in range(S):
                 w[i].fill_((r * S + i) % E + 100 * l)  # slot p holds expert p % E
             layers.append([w])
-        stores.append(ExpertStore(r, layers))
+        stores.append(ExpertStore(r, layers, LocalTransport(f"ep-r{r}") if transport else None))
     return stores
-
-
-class _HostReadTransport:
-    """Host-memory one-sided reads between in-process stores (tests)."""
-    url = "local"
-
-    def register(self, ptr, n):
-        pass
-
-    def read(self, url, ops):
-        import ctypes
-        for d, s, n in ops:
-            ctypes.memmove(d, s, n)
-        return 0
 
 
 def test_controller_fail_migrate_and_rejoin_two_epochs():
     R, S, L, E = 4, 4, 2, 8
     table = PlacementTable.linear(E, R, S, num_layers=L)   # slots 8..15 are replicas
-    stores = _stores(R, S, L, E)
-    t = _HostReadTransport()
-    for s in stores:
-        s.t = t
+    stores = _stores(R, S, L, E, transport=True)   # one-sided host reads between the stores
     eng = LocalEngine(stores, E)
     eng.loader = lambda layer, expert: [torch.full((4, 4), float(expert + 100 * layer))]
     ctl = EPController(table, eng)
