@@ -63,6 +63,9 @@ DEFAULT_RECV_TIMEOUT_S = float(os.getenv("CONNEXTE_RECV_TIMEOUT_MS", "8000")) / 
 TRACE_PREFIX = os.getenv("CONNEXTE_TRACE", "")
 PROFILE = os.getenv("CONNEXTE_PROFILE", "0") == "1"
 PROFILE_EVERY = int(os.getenv("CONNEXTE_PROFILE_EVERY", "64"))
+# CONNEX_RS_STATS_S=N: every N seconds log the native engine's counters with
+# this process's open file descriptors and resident memory (leak checks).
+RS_STATS_S = float(os.getenv("CONNEX_RS_STATS_S", "0") or 0)
 PROBE_TIMEOUT_S = float(os.getenv("CONNEXTE_PROBE_TIMEOUT_S", "0.5") or "0.5")
 ACK_TIMEOUT_S = float(os.getenv("CONNEXTE_GDR_ACK_TIMEOUT_S", "10.0"))
 
@@ -121,6 +124,20 @@ class _Profiler:
             log.info("stage %s phases (mean ms over %d): %s", self.stage, self.every,
                      {k: round(v / self.every, 3) for k, v in self.acc.items()})
             self.acc.clear()
+
+
+def process_stats() -> dict:
+    """Open file descriptors and resident set size (MiB) of this process."""
+    try:
+        fds = len(os.listdir("/proc/self/fd"))
+    except OSError:
+        fds = -1
+    try:
+        with open("/proc/self/statm") as f:
+            rss_mb = int(f.read().split()[1]) * os.sysconf("SC_PAGE_SIZE") / (1 << 20)
+    except (OSError, ValueError, IndexError):
+        rss_mb = -1.0
+    return {"fds": fds, "rss_mb": round(rss_mb, 1)}
 
 
 class ChainFailed(RuntimeError):
@@ -237,11 +254,16 @@ class PipelineEndpoint:
         poller = zmq.Poller()
         poller.register(self.router, zmq.POLLIN)
         poller.register(self._wake_rx, zmq.POLLIN)
+        next_stats = time.monotonic() + RS_STATS_S
         while not self._stop.is_set():
             try:
                 ready = dict(poller.poll(50))
             except zmq.ZMQError:
                 break
+            if RS_STATS_S > 0 and time.monotonic() >= next_stats:
+                next_stats = time.monotonic() + RS_STATS_S
+                eng = self.engine.stats() if self.engine is not None and hasattr(self.engine, "stats") else {}
+                log.info("stage %s engine %s process %s", self.stage_idx, eng, process_stats())
             if self._wake_rx in ready:
                 while True:
                     try:

@@ -16,6 +16,7 @@ from typing import Callable, Optional, Sequence
 
 from connex.pp.handover import (CX_CTX, CX_MISSING, FINISHED, REQUEST_IDS, FinishedOutbox, RewindBudget,
                                 find_missing, merge_missing)
+from connex.pp.steptrace import tr
 
 _log = logging.getLogger("connex.pp.link")
 
@@ -60,6 +61,7 @@ class Stage0Link:
             td[FINISHED] = fin
         corr = self.t.new_step_id()
         self._sent[corr] = td
+        tr("s0_send", corr)
         self.t.send_step(td, corr)
         self.stats["steps"] += 1
         return corr
@@ -77,8 +79,10 @@ class Stage0Link:
                 self._sent.pop(corr, None)
                 raise StepFailed(f"step {corr:x}: no reply after {attempts} attempts")
             self.stats["retries"] += 1
+            tr("s0_resend", corr)
             self.t.send_step(self._sent[corr], corr)
             self._resend_stale(corr)
+        tr("s0_reply", corr)
         self._sent.pop(corr, None)
         missing = reply.pop(CX_MISSING, None)
         if missing:
@@ -131,6 +135,8 @@ class StageWorker:
 
     def serve(self, td: dict, ctx) -> None:
         """Process one received step (``recv_forward`` output) and send it on."""
+        seq = ctx[0] if isinstance(ctx, tuple) and ctx else 0
+        tr(f"s{getattr(self.t, 'stage_idx', 'x')}_recv", seq)
         self.stats["steps"] += 1
         rids = td.get(REQUEST_IDS) or []
         fin = td.get(FINISHED)
@@ -156,4 +162,5 @@ class StageWorker:
             for k in (REQUEST_IDS, CX_CTX, FINISHED):
                 if k in td and k not in out:
                     out[k] = td[k]
+        tr(f"s{getattr(self.t, 'stage_idx', 'x')}_send", seq)
         self.t.send_reply(out, ctx)

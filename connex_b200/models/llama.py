@@ -26,6 +26,7 @@ from typing import Callable, List, Optional, Sequence
 import torch
 
 from connex_b200 import ops
+from connex_b200.utils import nvtx
 
 
 @dataclass(frozen=True)
@@ -294,9 +295,11 @@ class LlamaModel:
         l's K/V are in the paged cache: the PD path launches its push there."""
         cfg, T = self.cfg, ids.numel()
         assert T <= self.max_tokens
+        nvtx.push(f"prefill T={T}")
         ops.embedding(ids, self.w.embed, self.x[:T], status=self.status)
         ops.rmsnorm(self.x[:T], self.w.layers[0].attn_norm, cfg.eps, out=self.h[:T])
         for l, lw in enumerate(self.w.layers):
+            nvtx.push(f"layer {l}")
             qkv = self.qkv[:T]
             ops.gemm(self.h[:T], lw.wqkv, qkv, status=self.status)
             ops.rope_cache(qkv, positions, self.cos_sin, cfg.heads, cfg.kv_heads, slots,
@@ -305,13 +308,17 @@ class LlamaModel:
                 layer_hook(l)
             ops.prefill_attention(qkv, tile_info, cfg.heads, cfg.kv_heads, out=self.attn[:T])
             self._layer_tail(l, T)
-        return self._head(last_rows, len(seq_lens))
+            nvtx.pop()
+        out = self._head(last_rows, len(seq_lens))
+        nvtx.pop()
+        return out
 
     def decode(self, ids: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor,
                block_tables: torch.Tensor, ctx_lens: torch.Tensor, max_ctx: int,
                workspace: torch.Tensor, rows: torch.Tensor) -> torch.Tensor:
         """One decode step for B sequences (ctx_lens include the new token)."""
         cfg, B = self.cfg, ids.numel()
+        nvtx.push(f"decode B={B}")
         ops.embedding(ids, self.w.embed, self.x[:B], status=self.status)
         ops.rmsnorm(self.x[:B], self.w.layers[0].attn_norm, cfg.eps, out=self.h[:B])
         for l, lw in enumerate(self.w.layers):
@@ -322,7 +329,9 @@ class LlamaModel:
             ops.decode_attention(qkv, self.cache.k(l), self.cache.v(l), block_tables, ctx_lens,
                                  cfg.heads, max_ctx, workspace, out=self.attn[:B])
             self._layer_tail(l, B)
-        return self._head(rows, B)
+        out = self._head(rows, B)
+        nvtx.pop()
+        return out
 
 
 # ------------------------------------------------------------- oracle

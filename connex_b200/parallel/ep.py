@@ -25,6 +25,7 @@ from typing import List, Optional
 import torch
 
 from connex_b200 import _C, ops
+from connex_b200.utils.nvtx import nvtx_range
 
 FLAG_COUNT, FLAG_DATA, FLAG_COMB, FLAG_EXPECT = 0, 4, 8, 12  # int32 offsets (16 B apart)
 
@@ -169,11 +170,16 @@ class EPMoE:
     def forward(self, x, topk_idx, topk_w, l2p, l2p_cnt, out: Optional[torch.Tensor] = None):
         T = x.shape[0]
         out = torch.empty_like(x) if out is None else out
-        self.phase_count(topk_idx, l2p, l2p_cnt)
-        self.phase_dispatch(x, topk_w)
-        self.phase_gate_up()
-        self.phase_down()
-        return self.phase_combine(T, out)
+        with nvtx_range("ep count"):
+            self.phase_count(topk_idx, l2p, l2p_cnt)
+        with nvtx_range("ep dispatch"):
+            self.phase_dispatch(x, topk_w)
+        with nvtx_range("ep gate_up"):
+            self.phase_gate_up()
+        with nvtx_range("ep down"):
+            self.phase_down()
+        with nvtx_range("ep combine"):
+            return self.phase_combine(T, out)
 
 
 def emulated_group(cfg: EPConfig, w13_all: torch.Tensor, w2_all: torch.Tensor, device) -> List[EPMoE]:

@@ -30,6 +30,7 @@ import torch
 
 from connex.rl.weights import WeightManifest
 from connex_b200 import ops
+from connex_b200.utils.nvtx import nvtx_range
 from connex_b200.models.llama import LlamaConfig, LlamaWeights
 
 WS_COLS = 12
@@ -175,6 +176,10 @@ class WeightBroadcast:
         return jobs, jobs.to(self.device), n_tasks, srcs
 
     def sync(self, named: Optional[Dict[str, torch.Tensor]] = None, n_tasks: Optional[int] = None) -> None:
+        with nvtx_range("weight broadcast"):
+            self._sync(named, n_tasks)
+
+    def _sync(self, named: Optional[Dict[str, torch.Tensor]] = None, n_tasks: Optional[int] = None) -> None:
         """Broadcast ``named`` (src rank) into every rank's arena.
 
         ``n_tasks`` is the plan's task count (:func:`plan_jobs`); pass it on

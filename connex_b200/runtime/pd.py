@@ -27,6 +27,7 @@ from typing import List, Optional, Sequence
 import torch
 
 from connex_b200 import ops
+from connex_b200.utils.nvtx import nvtx_range
 from connex_b200.models.llama import LlamaModel, PagedKVCache, slot_mapping
 
 
@@ -92,7 +93,7 @@ class LayerwiseKVPusher:
         ev.record(cur)
         self.stream.wait_event(ev)
         d, c = self._dst, self.src
-        with torch.cuda.stream(self.stream):
+        with torch.cuda.stream(self.stream), nvtx_range(f"kv push {layer}"):
             if self.timing:
                 e0 = torch.cuda.Event(enable_timing=True)
                 e0.record(self.stream)

@@ -253,3 +253,20 @@ def test_trace_and_profile_hooks(tmp_path, monkeypatch, caplog):
     assert events.count("send_called") == 4 and events.count("recv_done") == 4
     assert (tmp_path / "tr.stage1.txt").read_text().count("arrived") == 4
     assert any("phases" in r.getMessage() for r in caplog.records)
+
+
+def test_engine_and_process_stats_are_logged(monkeypatch, caplog):
+    import logging
+    import connex.pp.endpoint as E
+
+    class Eng:
+        def stats(self):
+            return {"live_peers": 1}
+    monkeypatch.setattr(E, "RS_STATS_S", 0.05)
+    st = E.process_stats()
+    assert st["fds"] > 0 and st["rss_mb"] > 0
+    with caplog.at_level(logging.INFO, logger="connex.pp.endpoint"):
+        ep = PipelineEndpoint("m", 1, 2, membership=StaticMembership(0, 0), data="inline", engine=Eng())
+        time.sleep(0.4)
+        ep.close()
+    assert any("live_peers" in r.getMessage() and "rss_mb" in r.getMessage() for r in caplog.records)
