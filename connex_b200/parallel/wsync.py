@@ -60,13 +60,37 @@ def _targets(cfg: LlamaConfig, name: str):
     return name, None, 0, 0
 
 
+def shard_dim0(named: Dict[str, torch.Tensor], rank: int, world: int,
+               align: int = ops.GATE_UP_TILE // 2) -> Tuple[Dict[str, torch.Tensor], Dict[str, int]]:
+    """Per-parameter dim-0 shards of ``named`` (FSDP2 ``Shard(0)``) held by
+    trainer ``rank`` of ``world``: ``(local views, global start of each)``.
+    Row boundaries are multiples of ``align`` rows (1-D tensors: of 8
+    elements), so every shard starts on a gate/up block and a 16-byte column."""
+    local, start = {}, {}
+    for name, t in named.items():
+        n = t.shape[0]
+        unit = 8 if t.dim() == 1 else align
+        per = -(-n // (world * unit)) * unit
+        a, b = min(n, rank * per), min(n, (rank + 1) * per)
+        if a < b:
+            local[name], start[name] = t[a:b], a
+    return local, start
+
+
 def plan_jobs(cfg: LlamaConfig, manifest: WeightManifest, src: Dict[str, torch.Tensor],
-              task_bytes: int = TASK_BYTES) -> Tuple[torch.Tensor, int, List[torch.Tensor]]:
+              task_bytes: int = TASK_BYTES, starts: Optional[Dict[str, int]] = None
+              ) -> Tuple[torch.Tensor, int, List[torch.Tensor]]:
     """Job table (int64 [n, WS_COLS]) moving every trainer tensor of ``src``
-    into the engine arena layout of ``manifest``; returns (jobs, n_tasks, sources)."""
+    into the engine arena layout of ``manifest``; returns (jobs, n_tasks, sources).
+
+    ``starts`` (sharded trainers): the global first row (1-D: first element)
+    of each local tensor.  The shard's place in the engine tensor is folded
+    into the job's destination offset, so the kernel is the same for a whole
+    tensor and for a shard."""
     rows_out: List[List[int]] = []
     srcs: List[torch.Tensor] = []
     task0 = 0
+    starts = starts or {}
     for name, t in src.items():
         tgt, blk, bstride, boff = _targets(cfg, name)
         e = manifest.entry(tgt)
@@ -77,11 +101,24 @@ def plan_jobs(cfg: LlamaConfig, manifest: WeightManifest, src: Dict[str, torch.T
             raise ValueError(f"{name}: expected a row-major 2-D (or 1-D) tensor")
         rows, cols = t2.shape
         dcols = e.shape[-1] if len(e.shape) == 2 else e.shape[0]
-        if cols != dcols:
-            raise ValueError(f"{name}: {cols} columns, engine tensor {tgt} has {dcols}")
+        s0 = int(starts.get(name, 0))
+        doff = e.offset
+        if t.dim() == 1:
+            if s0 % 8 or s0 + cols > dcols:
+                raise ValueError(f"{name}: shard [{s0}, +{cols}) does not fit {tgt} ({dcols}) on 8-element bounds")
+            doff += 2 * s0
+        else:
+            if cols != dcols:
+                raise ValueError(f"{name}: {cols} columns, engine tensor {tgt} has {dcols}")
+            if blk is not None:
+                if s0 % blk:
+                    raise ValueError(f"{name}: shard start {s0} is not on a {blk}-row block")
+                doff += 2 * (s0 // blk) * bstride * dcols
+            else:
+                doff += 2 * s0 * dcols
         blk = blk or rows
         rpt = max(1, min(rows, task_bytes // (2 * cols)))
-        rows_out.append([t2.data_ptr(), e.offset, rows, cols, t2.stride(0), dcols, blk, bstride, boff,
+        rows_out.append([t2.data_ptr(), doff, rows, cols, t2.stride(0), dcols, blk, bstride, boff,
                          int(t.dtype == torch.float32), task0, rpt])
         srcs.append(t2)
         task0 += -(-rows // rpt)
@@ -132,28 +169,38 @@ def apply_local(jobs_cpu: torch.Tensor, dst: torch.Tensor, flag_addr: int = 0) -
 
 
 class WeightBroadcast:
-    """One symmetric weight arena per GPU of ``group``; rank ``src`` sends.
+    """One symmetric weight arena per GPU of ``group``; the ranks in ``srcs``
+    (trainer shards, or one trainer) send.
 
     Collective: every rank constructs it and calls :meth:`sync` together.
     ``mode``: ``"auto"`` (multicast when the GPUs support it, else peer
     stores), ``"multicast"`` or ``"p2p"``.
+
+    Membership per round (``sync(members=...)``): in multicast mode NVSwitch
+    delivers every round to every GPU bound to the group, so a rank that
+    stopped consuming (left) blocks nobody, and a standby rank that joins
+    already holds the latest version once its flag shows the round; in p2p
+    mode only the round's members are written, and a rank that joins later
+    catches up with :meth:`catch_up` (one ``copy_segments`` launch reading a
+    member's arena over NVLink).  No sender ever waits for a receiver.
     """
 
     def __init__(self, cfg: LlamaConfig, group=None, src: int = 0, device=None, mode: str = "auto",
-                 timeout_s: float = 10.0):
+                 timeout_s: float = 10.0, srcs: Optional[Sequence[int]] = None):
         import torch.distributed as dist
         import torch.distributed._symmetric_memory as symm
         self.cfg = cfg
         self.group = group or dist.group.WORLD
         self.rank = dist.get_rank(self.group)
         self.world = dist.get_world_size(self.group)
-        self.src = src
+        self.srcs = list(srcs) if srcs is not None else [src]
+        self.src = self.srcs[0]
         self.device = torch.device("cuda", torch.cuda.current_device()) if device is None else torch.device(device)
         self.manifest = engine_manifest(cfg)
         self.total = self.manifest.total
         self.timeout_s = timeout_s
         self.arena = symm.empty(self.total + FLAG_BYTES, dtype=torch.uint8, device=self.device)
-        self.arena[self.total:].zero_()
+        self.arena.zero_()          # padding between tensors included: arenas compare bytewise
         torch.cuda.synchronize(self.device)
         self.handle = symm.rendezvous(self.arena, self.group)
         mc = int(getattr(self.handle, "multicast_ptr", 0) or 0)
@@ -164,6 +211,8 @@ class WeightBroadcast:
         self.weights = LlamaWeights.from_arena(cfg, self.arena[:self.total], self.manifest)
         self.status = ops.new_status(self.device)
         self.received = 0          # cumulative flag target on this rank
+        self.rounds_seen = 0       # rounds whose flag increments reached this rank
+        self.round = 0
         self._jobs = None
         dist.barrier(group=self.group)
 
@@ -171,48 +220,72 @@ class WeightBroadcast:
     def flag_addr(self) -> int:
         return self.arena.data_ptr() + self.total
 
-    def _plan(self, named: Dict[str, torch.Tensor]):
-        jobs, n_tasks, srcs = plan_jobs(self.cfg, self.manifest, named)
+    @property
+    def is_src(self) -> bool:
+        return self.rank in self.srcs
+
+    def _plan(self, named: Dict[str, torch.Tensor], starts=None):
+        jobs, n_tasks, srcs = plan_jobs(self.cfg, self.manifest, named, starts=starts)
         return jobs, jobs.to(self.device), n_tasks, srcs
 
-    def sync(self, named: Optional[Dict[str, torch.Tensor]] = None, n_tasks: Optional[int] = None) -> None:
+    def sync(self, named: Optional[Dict[str, torch.Tensor]] = None, n_tasks=None, starts=None,
+             members: Optional[Sequence[int]] = None, wait: bool = True) -> None:
         with nvtx_range("weight broadcast"):
-            self._sync(named, n_tasks)
+            self._sync(named, n_tasks, starts, members, wait)
 
-    def _sync(self, named: Optional[Dict[str, torch.Tensor]] = None, n_tasks: Optional[int] = None) -> None:
-        """Broadcast ``named`` (src rank) into every rank's arena.
+    def _sync(self, named, n_tasks, starts, members, wait) -> None:
+        """Broadcast every source's ``named`` (its shard, placed by
+        ``starts``) into the arenas.
 
-        ``n_tasks`` is the plan's task count (:func:`plan_jobs`); pass it on
-        every rank, or None on every rank to have src broadcast it first.
-        Stream-ordered: returns once the work is enqueued on every rank."""
+        ``n_tasks``: per source (list, or an int with one source) the plan's
+        task count; None on every rank to gather it first.  ``members``: the
+        ranks consuming this round (default: every non-source rank);
+        ``wait=False``: this rank does not wait for the round (it is
+        leaving).  Stream-ordered: returns once the work is enqueued."""
         import torch.distributed as dist
         planned = None
-        if self.rank == self.src:
+        if self.is_src:
             if self._jobs is None or self._jobs[4] is not named:
-                jobs, jobs_dev, nt, srcs = self._plan(named)
+                jobs, jobs_dev, nt, srcs = self._plan(named, starts)
                 self._jobs = (jobs, jobs_dev, nt, srcs, named)
             planned = self._jobs[2]
         if n_tasks is None:
-            box = [planned]
-            dist.broadcast_object_list(box, src=dist.get_global_rank(self.group, self.src), group=self.group)
-            n_tasks = box[0]
-        elif planned is not None and planned != n_tasks:
+            box = [None] * self.world
+            dist.all_gather_object(box, planned, group=self.group)
+            n_tasks = [box[r] for r in self.srcs]
+        elif isinstance(n_tasks, int):
+            n_tasks = [n_tasks]
+        if len(n_tasks) != len(self.srcs):
+            raise ValueError(f"{len(n_tasks)} task counts for {len(self.srcs)} sources")
+        if planned is not None and planned != n_tasks[self.srcs.index(self.rank)]:
             raise ValueError(f"n_tasks {n_tasks} does not match the plan ({planned})")
-        ctas = n_ctas(n_tasks, self.device)
+        ctas = sum(n_ctas(n, self.device) for n in n_tasks)
+        members = [r for r in range(self.world) if r not in self.srcs] if members is None else list(members)
+        self.round += 1
         dist.barrier(group=self.group)      # receivers are off their weights from here on
-        if self.rank == self.src:
+        if self.is_src:
             jobs, jobs_dev = self._jobs[0], self._jobs[1]
             ops._n()
             if self.mc:
                 ops._C.wsync(jobs_dev, jobs, self.total, [], [], self.mc, self.mc + self.total, 0)
             else:
-                dst = [p for r, p in enumerate(self.peers) if r != self.rank]
+                dst = [self.peers[r] for r in members if r != self.rank]
                 ops._C.wsync(jobs_dev, jobs, self.total, dst, [p + self.total for p in dst], 0, 0, 0)
-            if self.mc:
-                self.received += ctas    # the multicast flag store reaches this GPU too
-        else:
+        gets_round = bool(self.mc) or self.rank in members
+        if gets_round:
             self.received += ctas
+            self.rounds_seen = self.round
+        if gets_round and wait and not self.is_src and self.rank in members:
             ops.wait_flag(self.flag_addr, self.received & 0xFFFFFFFF, self.status, self.timeout_s)
+
+    def catch_up(self, from_rank: int, max_ctas: int = 64) -> None:
+        """Copy member ``from_rank``'s arena (the latest version) into this
+        rank's, reading it over NVLink (p2p-mode joiners).  Stream-ordered;
+        the caller orders it after that member's round."""
+        seg = torch.tensor([[self.peers[from_rank], self.arena.data_ptr(), self.total]], dtype=torch.int64,
+                           device=self.device)
+        ops.copy_segments(seg, self.total, max_ctas=max_ctas, status=self.status)
+        self.rounds_seen = self.round
 
     def check(self) -> None:
         ops.check_status(self.status, "weight broadcast")

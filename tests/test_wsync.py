@@ -112,3 +112,35 @@ def test_wsync_broadcast_two_gpus(mode, tmp_path):
     import json
     res = json.loads([ln for ln in r.stdout.splitlines() if ln.startswith("[")][-1])
     assert all(x["ok"] for x in res), res
+
+
+@pytest.mark.parametrize("world", [2, 3])
+def test_sharded_trainers_cover_the_arena_exactly(world):
+    """FSDP dim-0 shards on ``world`` trainer ranks: the union of every
+    rank's jobs writes the same bytes as one unsharded plan."""
+    from connex_b200.parallel.wsync import shard_dim0
+    named = random_trainer_weights(CFG, "cpu", dtype=torch.float32, seed=5)
+    m = engine_manifest(CFG)
+    want = _engine_bytes(CFG, fuse_reference(CFG, named), m)
+    got = torch.zeros(m.total, dtype=torch.uint8)
+    covered = 0
+    for r in range(world):
+        local, starts = shard_dim0(named, r, world)
+        jobs, _, srcs = plan_jobs(CFG, m, local, task_bytes=4096, starts=starts)
+        part = emulate_jobs(jobs, srcs, m.total)
+        written = part != 0
+        got[written] = part[written]
+        covered += sum(t.numel() for t in local.values())
+    assert covered == CFG.num_params()
+    assert torch.equal(got, want)
+
+
+def test_shard_start_must_sit_on_a_block():
+    from connex_b200.parallel.wsync import plan_jobs as pj
+    named = random_trainer_weights(CFG, "cpu")
+    g = "model.layers.0.mlp.gate_proj.weight"
+    with pytest.raises(ValueError, match="block"):
+        pj(CFG, engine_manifest(CFG), {g: named[g][3:]}, starts={g: 3})
+    n = "model.norm.weight"
+    with pytest.raises(ValueError, match="8-element"):
+        pj(CFG, engine_manifest(CFG), {n: named[n][4:]}, starts={n: 4})
