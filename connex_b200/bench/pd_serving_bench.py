@@ -1,0 +1,282 @@
+"""PD-disaggregated serving under Poisson load (Llama-3-8B architecture,
+random-init bf16 weights, random token ids): prefill GPU ``p`` pushes each
+batch's KV layer by layer into decode GPU ``p + N/2`` (the ``kv_push_layer``
+kernel over the peer mapping, overlapped with the remaining prefill layers);
+the decode GPU runs continuous batching until every request has its output
+tokens.  The serving counterpart of the PD measurements the reference
+publishes (TTFT / TPOT at a request rate, reference ``docs/results.md:289-296``).
+
+Control between the two GPUs of a pair is a ZeroMQ PAIR socket:
+
+* the prefill side owns the decode cache's block allocator (the decode side
+  returns blocks with ``FREE`` when a request finishes), so a batch needs no
+  round trip before its push;
+* after a batch's prefill and pushes completed on the device, ``ARRIVE``
+  carries the requests (arrival time, prompt length, decode blocks, first
+  token) and the CTA count the decode side adds to its cumulative ready
+  target; the decode side admits them between two decode steps after a
+  bounded device wait on the ready counter.
+
+Reported (host wall clock; one host, so the clocks of the two processes
+agree): TTFT = arrival -> request admitted on the decode GPU with its KV and
+first token in place (queueing + prefill + KV push + admission); TPOT = mean
+gap between its decode tokens; output tokens/s; and the device-timed push
+bandwidth of the KV kernels.
+
+    torchrun --nproc-per-node 2 -m connex_b200.bench.pd_serving_bench --qps 4 --duration 20
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import os
+import statistics
+import time
+from datetime import timedelta
+from typing import Dict, List
+
+import numpy as np
+import torch
+import torch.distributed as dist
+import zmq
+
+from connex_b200 import ops
+from connex_b200.models.llama import LlamaConfig, LlamaModel, LlamaWeights, PagedKVCache
+from connex_b200.parallel.peer import PeerHandle, PeerMapper, export_tensor
+from connex_b200.runtime.pd import (DecodeBatch, KVDestination, LayerwiseKVPusher, block_pairs,
+                                    build_prefill_batch, decode_step)
+
+PUSH_CTAS = 296
+
+
+def arrivals(seed: int, pair: int, qps: float, duration: float, lo: int, hi: int, vocab: int):
+    """Poisson arrivals in [0, duration): ``[(t, prompt)]``."""
+    rng = np.random.default_rng([seed, pair, 7])
+    out, t = [], 0.0
+    while True:
+        t += rng.exponential(1.0 / qps)
+        if t >= duration:
+            return out
+        n = int(rng.integers(lo, hi + 1))
+        out.append((t, rng.integers(0, vocab, size=n).tolist()))
+
+
+def _pct(xs: List[float], q: float) -> float:
+    return float(np.percentile(np.asarray(xs), q)) if xs else float("nan")
+
+
+def prefill_side(args, cfg, weights, dev, sock, dst, n_dec_blocks: int) -> Dict:
+    cache = PagedKVCache(cfg, args.prefill_blocks, dev)
+    model = LlamaModel(weights, cache, max_tokens=args.token_budget, max_batch=args.max_running)
+    pusher = LayerwiseKVPusher(cache, max_ctas=PUSH_CTAS)
+    free = list(range(n_dec_blocks))                  # the decode cache's free blocks
+    reqs = arrivals(args.seed, args.pair, args.qps, args.duration, args.min_len, args.max_len, cfg.vocab_size)
+    need = [cache.blocks_needed(len(p) + args.out_tokens) for _, p in reqs]
+    warm = build_prefill_batch(cache, [list(range(512))], dev)          # first-launch costs off the clock
+    model.prefill(warm.ids, warm.positions, warm.slots, warm.seq_lens, warm.last_rows, warm.tile_info)
+    torch.cuda.synchronize()
+    cache.free(warm.src_blocks[0])
+    t0 = time.time() + 0.5
+    sock.send_pyobj({"op": "START", "t0": t0, "n": len(reqs)})
+    queue: List[int] = []
+    nxt_i, push_ms, push_bytes, batches = 0, 0.0, 0, 0
+
+    def drain(block_s: float = 0.0):
+        if sock.poll(int(block_s * 1000)):
+            while sock.poll(0):
+                m = sock.recv_pyobj()
+                if m["op"] == "FREE":
+                    free.extend(m["blocks"])
+
+    while nxt_i < len(reqs) or queue:
+        now = time.time()
+        while nxt_i < len(reqs) and t0 + reqs[nxt_i][0] <= now:
+            queue.append(nxt_i)
+            nxt_i += 1
+        drain()
+        if not queue:
+            time.sleep(max(0.0, min(0.002, t0 + reqs[nxt_i][0] - time.time())))
+            continue
+        pick, tokens, blocks = [], 0, 0
+        for i in queue:
+            n = len(reqs[i][1])
+            if pick and (tokens + n > args.token_budget or blocks + need[i] > len(free)):
+                break
+            if blocks + need[i] > len(free):
+                break
+            pick.append(i)
+            tokens += n
+            blocks += need[i]
+        if not pick:
+            drain(0.005)                              # wait for finished requests' blocks
+            continue
+        queue = queue[len(pick):]
+        dblocks = []
+        for i in pick:
+            dblocks.append(free[:need[i]])
+            del free[:need[i]]
+        prompts = [reqs[i][1] for i in pick]
+        batch = build_prefill_batch(cache, prompts, dev)
+        pairs = block_pairs(batch.src_blocks, [d[:len(s)] for d, s in zip(dblocks, batch.src_blocks)], dev)
+        pusher.begin(pairs, dst, timing=True)
+        first = model.prefill(batch.ids, batch.positions, batch.slots, batch.seq_lens, batch.last_rows,
+                              batch.tile_info, layer_hook=pusher.hook)
+        pusher.join()
+        first_host = first[:len(pick)].cpu().tolist()       # synchronizes: prefill and pushes are done
+        ops.check_status(pusher.status, "kv push")
+        push_ms += pusher.push_ms()
+        push_bytes += pusher.bytes
+        batches += 1
+        sock.send_pyobj({"op": "ARRIVE", "ctas": pusher.launched,
+                         "reqs": [{"rid": i, "arrival": t0 + reqs[i][0], "len": len(reqs[i][1]), "blocks": d,
+                                   "first": tok} for i, d, tok in zip(pick, dblocks, first_host)]})
+        for b in batch.src_blocks:
+            cache.free(b)
+    sock.send_pyobj({"op": "DONE"})
+    return {"requests": len(reqs), "batches": batches, "push_ms": push_ms, "push_bytes": push_bytes}
+
+
+def decode_side(args, cfg, weights, dev, sock, cache, ready) -> Dict:
+    model = LlamaModel(weights, cache, max_tokens=args.max_running, max_batch=args.max_running)
+    ws = ops.decode_workspace(args.max_running, cfg.heads, args.max_len + args.out_tokens + 2, dev)
+    status = ops.new_status(dev)
+    ids_host = torch.zeros(args.max_running, dtype=torch.int32).pin_memory()
+    warm = DecodeBatch(cache, [[0]], [0], dev)                         # first-launch costs off the clock
+    decode_step(model, warm, torch.zeros(1, dtype=torch.int32, device=dev), ws)
+    torch.cuda.synchronize()
+    start = sock.recv_pyobj()
+    running: Dict[int, dict] = {}
+    pending: List[dict] = []
+    target, done, steps = 0, False, 0
+    ttft, tpot, finished_tokens = [], [], 0
+    t_first_token = t_last = None
+    while True:
+        while sock.poll(0 if (running or pending) else 2):
+            m = sock.recv_pyobj()
+            if m["op"] == "ARRIVE":
+                target += m["ctas"]
+                ops.wait_flag(ready.data_ptr(), target, status, timeout_s=30.0)   # bounded, stream-ordered
+                pending.extend(m["reqs"])
+            elif m["op"] == "DONE":
+                done = True
+        while pending and len(running) < args.max_running:
+            r = pending.pop(0)
+            now = time.time()
+            r.update(ctx=r["len"], last=r["first"], n_gen=1, t_admit=now)
+            ttft.append((now - r["arrival"]) * 1e3)
+            t_first_token = t_first_token or now
+            running[r["rid"]] = r
+        if not running:
+            if done and not pending:
+                break
+            continue
+        rs = list(running.values())
+        B = len(rs)
+        batch = DecodeBatch(cache, [r["blocks"] for r in rs], [r["ctx"] for r in rs], dev)
+        for j, r in enumerate(rs):
+            ids_host[j] = r["last"]
+        ids = ids_host[:B].to(dev, non_blocking=True)
+        tok = decode_step(model, batch, ids, ws)[:B].cpu().tolist()
+        steps += 1
+        now = time.time()
+        freed = []
+        for r, t in zip(rs, tok):
+            r["ctx"] += 1
+            r["last"] = t
+            r["n_gen"] += 1
+            if r["n_gen"] >= args.out_tokens:
+                tpot.append((now - r["t_admit"]) * 1e3 / max(1, args.out_tokens - 1))
+                finished_tokens += args.out_tokens
+                freed.extend(r["blocks"])
+                del running[r["rid"]]
+        if freed:
+            sock.send_pyobj({"op": "FREE", "blocks": freed})
+        t_last = now
+    ops.check_status(status, "decode ready wait")
+    span = (t_last - start["t0"]) if t_last else float("nan")
+    return {"ttft_ms": ttft, "tpot_ms": tpot, "decode_steps": steps, "output_tokens": finished_tokens,
+            "span_s": span}
+
+
+def main() -> None:
+    p = argparse.ArgumentParser()
+    p.add_argument("--qps", type=float, default=4.0)
+    p.add_argument("--duration", type=float, default=20.0)
+    p.add_argument("--min-len", type=int, default=512)
+    p.add_argument("--max-len", type=int, default=8192)
+    p.add_argument("--out-tokens", type=int, default=128)
+    p.add_argument("--token-budget", type=int, default=16384)
+    p.add_argument("--max-running", type=int, default=64)
+    p.add_argument("--prefill-blocks", type=int, default=2048)
+    p.add_argument("--decode-blocks", type=int, default=16384)
+    p.add_argument("--layers", type=int, default=32)
+    p.add_argument("--seed", type=int, default=0)
+    args = p.parse_args()
+    world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world < 2 or world % 2:
+        raise SystemExit("PD serving needs prefill/decode pairs: an even number of GPUs >= 2")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+    cpu = dist.new_group(backend="gloo", timeout=timedelta(seconds=300))
+    role = "prefill" if rank < world // 2 else "decode"
+    args.pair = rank % (world // 2)
+    cfg = LlamaConfig(layers=args.layers)
+    weights = LlamaWeights.random(cfg, dev, seed=args.seed)
+    ctx = zmq.Context()
+    sock = ctx.socket(zmq.PAIR)
+    port = 29700 + args.pair
+    mine = None
+    if role == "decode":
+        cache = PagedKVCache(cfg, args.decode_blocks, dev)
+        ready = torch.zeros(16, dtype=torch.int32, device=dev)
+        mine = {"kv": export_tensor(cache.kv).to_dict(), "ready": export_tensor(ready).to_dict(),
+                "blocks": args.decode_blocks, "layer_stride": cache.layer_stride_bytes,
+                "kv_stride": cache.kv_stride_bytes}
+    allx = [None] * world
+    dist.all_gather_object(allx, mine, group=cpu)
+    mapper = PeerMapper(local)
+    if role == "prefill":
+        sock.bind(f"tcp://127.0.0.1:{port}")
+        d = allx[rank + world // 2]
+        dst = KVDestination(base=mapper.open(PeerHandle.from_dict(d["kv"])), layer_stride=d["layer_stride"],
+                            kv_stride=d["kv_stride"], heads=cfg.kv_heads, num_blocks=d["blocks"],
+                            ready_addr=mapper.open(PeerHandle.from_dict(d["ready"])))
+    else:
+        sock.connect(f"tcp://127.0.0.1:{port}")
+    dist.barrier(group=cpu)
+    if role == "prefill":
+        res = prefill_side(args, cfg, weights, dev, sock, dst, args.decode_blocks)
+    else:
+        res = decode_side(args, cfg, weights, dev, sock, cache, ready)
+    torch.cuda.synchronize()
+    res["role"] = role
+    allr = [None] * world
+    dist.all_gather_object(allr, res, group=cpu)
+    if rank == 0:
+        dec = [r for r in allr if r["role"] == "decode"]
+        pre = [r for r in allr if r["role"] == "prefill"]
+        ttft = [x for r in dec for x in r["ttft_ms"]]
+        tpot = [x for r in dec for x in r["tpot_ms"]]
+        out_tok = sum(r["output_tokens"] for r in dec)
+        span = max(r["span_s"] for r in dec)
+        print(json.dumps({
+            "bench": "pd_serving", "model": f"Llama-3-8B architecture ({args.layers} layers)",
+            "pairs": world // 2, "qps_per_pair": args.qps, "duration_s": args.duration,
+            "prompt_len": [args.min_len, args.max_len], "out_tokens": args.out_tokens,
+            "requests": sum(r["requests"] for r in pre), "completed": len(tpot),
+            "ttft_p50_ms": round(_pct(ttft, 50), 2), "ttft_p99_ms": round(_pct(ttft, 99), 2),
+            "tpot_p50_ms": round(_pct(tpot, 50), 3), "output_tok_s": round(out_tok / span, 1),
+            "kv_push_gbps": round(sum(r["push_bytes"] for r in pre) / max(1e-9, sum(r["push_ms"] for r in pre)) / 1e6, 1),
+            "prefill_batches": sum(r["batches"] for r in pre),
+            "decode_steps": sum(r["decode_steps"] for r in dec),
+            "data": "synthetic (random token ids, random-init weights)"}), flush=True)
+    sock.close(0)
+    ctx.term()
+    mapper.close()
+    dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()
