@@ -1,6 +1,7 @@
 """RL elastic weight-sync scenario on one box: a Llama-3-8B trainer sharded
-FSDP-style (dim-0 shards, fp32 master) on ranks 0-1 pushes every round into
-the bf16 engine-layout weight arenas of the rollout replicas on ranks 2..N-1
+FSDP-style (dim-0 shards, fp32 master) on ranks 0-1 (``--trainers``) pushes
+every round into the bf16 engine-layout weight arenas of the rollout replicas
+on the other ranks
 (q|k|v and gate/up fused by the broadcast kernel); weights are perturbed
 before every round.  One rollout replica leaves in the middle of a round and
 a standby replica joins in the middle of a later one.
@@ -31,18 +32,16 @@ import torch.distributed as dist
 from connex_b200.models.llama import LlamaConfig, random_trainer_weights
 from connex_b200.parallel.wsync import WeightBroadcast, apply_local, engine_manifest, plan_jobs, shard_dim0
 
-TRAINERS = (0, 1)
-
-
 def _checksum(arena_bytes: torch.Tensor) -> int:
     return int(arena_bytes.view(torch.int32).sum(dtype=torch.int64).item())
 
 
 def run(cfg: LlamaConfig, rounds: int = 10, mode: str = "auto", leave_round: int = 3, join_round: int = 5,
-        verify: bool = True) -> Dict:
+        verify: bool = True, trainers: int = 2) -> Dict:
     world, rank = dist.get_world_size(), dist.get_rank()
-    if world < 4:
-        raise SystemExit("the RL sync scenario needs 2 trainer ranks and at least 2 rollout ranks")
+    TRAINERS = tuple(range(trainers))
+    if world < trainers + 1:
+        raise SystemExit(f"the RL sync scenario needs {trainers} trainer rank(s) and at least one rollout rank")
     dev = torch.device("cuda", torch.cuda.current_device())
     rollouts = list(range(len(TRAINERS), world))
     standby = rollouts[-1]                      # joins at join_round
@@ -143,6 +142,7 @@ def main() -> None:
     p.add_argument("--layers", type=int, default=32)
     p.add_argument("--modes", default="multicast,p2p")
     p.add_argument("--no-verify", action="store_true")
+    p.add_argument("--trainers", type=int, default=2, help="FSDP trainer ranks (the first ones)")
     a = p.parse_args()
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
     torch.cuda.set_device(dev)
@@ -151,7 +151,7 @@ def main() -> None:
     out = {}
     for mode in a.modes.split(","):
         try:
-            out[mode] = run(cfg, a.rounds, mode, verify=not a.no_verify)
+            out[mode] = run(cfg, a.rounds, mode, verify=not a.no_verify, trainers=a.trainers)
         except RuntimeError as ex:
             if "multicast is not available" not in str(ex):
                 raise

@@ -270,7 +270,8 @@ class WeightBroadcast:
                 ops._C.wsync(jobs_dev, jobs, self.total, [], [], self.mc, self.mc + self.total, 0)
             else:
                 dst = [self.peers[r] for r in members if r != self.rank]
-                ops._C.wsync(jobs_dev, jobs, self.total, dst, [p + self.total for p in dst], 0, 0, 0)
+                if dst:                        # a round may have no consuming member
+                    ops._C.wsync(jobs_dev, jobs, self.total, dst, [p + self.total for p in dst], 0, 0, 0)
         gets_round = bool(self.mc) or self.rank in members
         if gets_round:
             self.received += ctas
