@@ -17,6 +17,16 @@ Control between the two GPUs of a pair is a ZeroMQ PAIR socket:
   target; the decode side admits them between two decode steps after a
   bounded device wait on the ready counter.
 
+Decode failure (``--kill-at S``): the prefill side keeps each request's
+prompt KV as a lease until the decode side reports the request finished.
+At ``S`` seconds the decode instance dies: its running and admitted requests
+are lost and it says so (``DEAD``, what its peer learns from the engine's
+peer-failure event); after ``--restart-s`` a replacement serves on the same
+GPU (``READY``) and the prefill side refills it from the held KV (pushes
+only, no prefill compute).  The lost requests decode again from their first
+token; ``resume_stall`` is kill -> decoding again.  Nothing is killed on the
+device: the instance's host state is dropped between two decode steps.
+
 Reported (host wall clock; one host, so the clocks of the two processes
 agree): TTFT = arrival -> request admitted on the decode GPU with its KV and
 first token in place (queueing + prefill + KV push + admission); TPOT = mean
@@ -79,30 +89,79 @@ def prefill_side(args, cfg, weights, dev, sock, dst, n_dec_blocks: int) -> Dict:
     t0 = time.time() + 0.5
     sock.send_pyobj({"op": "START", "t0": t0, "n": len(reqs)})
     queue: List[int] = []
+    # KV leases: a request's prompt KV stays held on the prefill GPU until the
+    # decode side reports it finished, so a decode that dies can be refilled
+    held: Dict[int, dict] = {}
+    lost: List[int] = []
+    state = {"decode_up": True, "bye": False, "done": False, "repushed": 0}
     nxt_i, push_ms, push_bytes, batches = 0, 0.0, 0, 0
+
+    def on_msg(m):
+        if m["op"] == "FREE":
+            for rid in m["rids"]:
+                h = held.pop(rid)
+                free.extend(h["dblocks"])
+                cache.free(h["sblocks"])
+        elif m["op"] == "DEAD":                         # the decode instance is gone
+            state["decode_up"] = False
+            for rid in m["lost"]:
+                free.extend(held[rid]["dblocks"])      # the replacement starts with an empty cache
+                lost.append(rid)
+        elif m["op"] == "READY":                        # its replacement is serving
+            state["decode_up"] = True
+        elif m["op"] == "BYE":
+            state["bye"] = True
 
     def drain(block_s: float = 0.0):
         if sock.poll(int(block_s * 1000)):
             while sock.poll(0):
-                m = sock.recv_pyobj()
-                if m["op"] == "FREE":
-                    free.extend(m["blocks"])
+                on_msg(sock.recv_pyobj())
 
-    while nxt_i < len(reqs) or queue:
+    def take_blocks(n):
+        b = free[:n]
+        del free[:n]
+        return b
+
+    def send(ctas, rids, resumed=False):
+        sock.send_pyobj({"op": "ARRIVE", "ctas": ctas, "resumed": resumed,
+                         "reqs": [{"rid": i, "arrival": t0 + reqs[i][0], "len": len(reqs[i][1]),
+                                   "blocks": held[i]["dblocks"], "first": held[i]["first"]} for i in rids]})
+
+    while not state["bye"]:
         now = time.time()
         while nxt_i < len(reqs) and t0 + reqs[nxt_i][0] <= now:
             queue.append(nxt_i)
             nxt_i += 1
         drain()
-        if not queue:
-            time.sleep(max(0.0, min(0.002, t0 + reqs[nxt_i][0] - time.time())))
+        if lost and state["decode_up"] and sum(need[i] for i in lost) <= len(free):
+            # refill the replacement from the held prompt KV: pushes only, no prefill compute
+            rids, lost[:] = list(lost), []
+            for i in rids:
+                held[i]["dblocks"] = take_blocks(need[i])
+            pairs = block_pairs([held[i]["sblocks"] for i in rids],
+                                [held[i]["dblocks"][:len(held[i]["sblocks"])] for i in rids], dev)
+            pusher.begin(pairs, dst, timing=True)
+            for layer in range(cfg.layers):
+                pusher.hook(layer)
+            pusher.join()
+            torch.cuda.synchronize()
+            ops.check_status(pusher.status, "kv re-push")
+            state["repushed"] += len(rids)
+            send(pusher.launched, rids, resumed=True)
+            continue
+        if not queue or not state["decode_up"]:
+            if nxt_i >= len(reqs) and not queue and not state["done"]:
+                sock.send_pyobj({"op": "DONE"})        # no new requests; re-pushes may still follow
+                state["done"] = True
+            wait = 0.002 if nxt_i >= len(reqs) else max(0.0, min(0.002, t0 + reqs[nxt_i][0] - time.time()))
+            drain(wait)
             continue
         pick, tokens, blocks = [], 0, 0
         for i in queue:
             n = len(reqs[i][1])
-            if pick and (tokens + n > args.token_budget or blocks + need[i] > len(free)):
+            if pick and tokens + n > args.token_budget:
                 break
-            if blocks + need[i] > len(free):
+            if blocks + need[i] > len(free) or cache.free_blocks() < cache.blocks_needed(tokens + n) + len(pick) + 1:
                 break
             pick.append(i)
             tokens += n
@@ -111,12 +170,8 @@ def prefill_side(args, cfg, weights, dev, sock, dst, n_dec_blocks: int) -> Dict:
             drain(0.005)                              # wait for finished requests' blocks
             continue
         queue = queue[len(pick):]
-        dblocks = []
-        for i in pick:
-            dblocks.append(free[:need[i]])
-            del free[:need[i]]
-        prompts = [reqs[i][1] for i in pick]
-        batch = build_prefill_batch(cache, prompts, dev)
+        dblocks = [take_blocks(need[i]) for i in pick]
+        batch = build_prefill_batch(cache, [reqs[i][1] for i in pick], dev)
         pairs = block_pairs(batch.src_blocks, [d[:len(s)] for d, s in zip(dblocks, batch.src_blocks)], dev)
         pusher.begin(pairs, dst, timing=True)
         first = model.prefill(batch.ids, batch.positions, batch.slots, batch.seq_lens, batch.last_rows,
@@ -127,13 +182,11 @@ def prefill_side(args, cfg, weights, dev, sock, dst, n_dec_blocks: int) -> Dict:
         push_ms += pusher.push_ms()
         push_bytes += pusher.bytes
         batches += 1
-        sock.send_pyobj({"op": "ARRIVE", "ctas": pusher.launched,
-                         "reqs": [{"rid": i, "arrival": t0 + reqs[i][0], "len": len(reqs[i][1]), "blocks": d,
-                                   "first": tok} for i, d, tok in zip(pick, dblocks, first_host)]})
-        for b in batch.src_blocks:
-            cache.free(b)
-    sock.send_pyobj({"op": "DONE"})
-    return {"requests": len(reqs), "batches": batches, "push_ms": push_ms, "push_bytes": push_bytes}
+        for i, d, sb, tok in zip(pick, dblocks, batch.src_blocks, first_host):
+            held[i] = {"dblocks": d, "sblocks": sb, "first": tok}
+        send(pusher.launched, pick)
+    return {"requests": len(reqs), "batches": batches, "push_ms": push_ms, "push_bytes": push_bytes,
+            "repushed": state["repushed"]}
 
 
 def decode_side(args, cfg, weights, dev, sock, cache, ready) -> Dict:
@@ -150,24 +203,44 @@ def decode_side(args, cfg, weights, dev, sock, cache, ready) -> Dict:
     target, done, steps = 0, False, 0
     ttft, tpot, finished_tokens = [], [], 0
     t_first_token = t_last = None
+    kill_at = start["t0"] + args.kill_at if args.kill_at > 0 else None
+    t_kill, stalls, lost_n, n_done = None, [], 0, 0
     while True:
         while sock.poll(0 if (running or pending) else 2):
             m = sock.recv_pyobj()
             if m["op"] == "ARRIVE":
                 target += m["ctas"]
                 ops.wait_flag(ready.data_ptr(), target, status, timeout_s=30.0)   # bounded, stream-ordered
+                for r in m["reqs"]:
+                    r["resumed"] = m.get("resumed", False)
                 pending.extend(m["reqs"])
             elif m["op"] == "DONE":
                 done = True
+        if kill_at is not None and time.time() >= kill_at:
+            # this decode instance dies: its running and admitted requests are
+            # lost; a replacement on the same GPU takes over after restart_s
+            kill_at = None
+            t_kill = time.time()
+            lost = [r["rid"] for r in list(running.values()) + pending]
+            lost_n = len(lost)
+            running.clear()
+            pending.clear()
+            sock.send_pyobj({"op": "DEAD", "lost": lost})
+            time.sleep(args.restart_s)
+            sock.send_pyobj({"op": "READY"})
+            continue
         while pending and len(running) < args.max_running:
             r = pending.pop(0)
             now = time.time()
             r.update(ctx=r["len"], last=r["first"], n_gen=1, t_admit=now)
-            ttft.append((now - r["arrival"]) * 1e3)
+            if r["resumed"]:
+                stalls.append((now - t_kill) * 1e3)      # kill -> the request decodes again
+            else:
+                ttft.append((now - r["arrival"]) * 1e3)
             t_first_token = t_first_token or now
             running[r["rid"]] = r
         if not running:
-            if done and not pending:
+            if done and not pending and (t_kill is None or len(stalls) >= lost_n):
                 break
             continue
         rs = list(running.values())
@@ -185,17 +258,20 @@ def decode_side(args, cfg, weights, dev, sock, cache, ready) -> Dict:
             r["last"] = t
             r["n_gen"] += 1
             if r["n_gen"] >= args.out_tokens:
-                tpot.append((now - r["t_admit"]) * 1e3 / max(1, args.out_tokens - 1))
+                if not r["resumed"]:
+                    tpot.append((now - r["t_admit"]) * 1e3 / max(1, args.out_tokens - 1))
                 finished_tokens += args.out_tokens
-                freed.extend(r["blocks"])
+                n_done += 1
+                freed.append(r["rid"])
                 del running[r["rid"]]
         if freed:
-            sock.send_pyobj({"op": "FREE", "blocks": freed})
+            sock.send_pyobj({"op": "FREE", "rids": freed})
         t_last = now
+    sock.send_pyobj({"op": "BYE"})
     ops.check_status(status, "decode ready wait")
     span = (t_last - start["t0"]) if t_last else float("nan")
     return {"ttft_ms": ttft, "tpot_ms": tpot, "decode_steps": steps, "output_tokens": finished_tokens,
-            "span_s": span}
+            "span_s": span, "completed": n_done, "lost": lost_n, "stall_ms": stalls}
 
 
 def main() -> None:
@@ -207,7 +283,9 @@ def main() -> None:
     p.add_argument("--out-tokens", type=int, default=128)
     p.add_argument("--token-budget", type=int, default=16384)
     p.add_argument("--max-running", type=int, default=64)
-    p.add_argument("--prefill-blocks", type=int, default=2048)
+    p.add_argument("--prefill-blocks", type=int, default=8192)
+    p.add_argument("--kill-at", type=float, default=0.0, help="seconds after start: the decode instance dies")
+    p.add_argument("--restart-s", type=float, default=0.5, help="until its replacement serves")
     p.add_argument("--decode-blocks", type=int, default=16384)
     p.add_argument("--layers", type=int, default=32)
     p.add_argument("--seed", type=int, default=0)
@@ -265,11 +343,16 @@ def main() -> None:
             "bench": "pd_serving", "model": f"Llama-3-8B architecture ({args.layers} layers)",
             "pairs": world // 2, "qps_per_pair": args.qps, "duration_s": args.duration,
             "prompt_len": [args.min_len, args.max_len], "out_tokens": args.out_tokens,
-            "requests": sum(r["requests"] for r in pre), "completed": len(tpot),
+            "requests": sum(r["requests"] for r in pre), "completed": sum(r["completed"] for r in dec),
             "ttft_p50_ms": round(_pct(ttft, 50), 2), "ttft_p99_ms": round(_pct(ttft, 99), 2),
             "tpot_p50_ms": round(_pct(tpot, 50), 3), "output_tok_s": round(out_tok / span, 1),
             "kv_push_gbps": round(sum(r["push_bytes"] for r in pre) / max(1e-9, sum(r["push_ms"] for r in pre)) / 1e6, 1),
             "prefill_batches": sum(r["batches"] for r in pre),
+            **({"decode_killed_at_s": args.kill_at, "restart_s": args.restart_s,
+                "lost_requests": sum(r["lost"] for r in dec), "repushed": sum(r["repushed"] for r in pre),
+                "resume_stall_p50_ms": round(_pct([x for r in dec for x in r["stall_ms"]], 50), 1),
+                "resume_stall_max_ms": round(max([x for r in dec for x in r["stall_ms"]] or [float("nan")]), 1)}
+               if args.kill_at > 0 else {}),
             "decode_steps": sum(r["decode_steps"] for r in dec),
             "data": "synthetic (random token ids, random-init weights)"}), flush=True)
     sock.close(0)

@@ -64,6 +64,7 @@ def run(cfg: LlamaConfig, rounds: int = 10, mode: str = "auto", leave_round: int
     per_round: List[float] = []
     events: Dict[str, float] = {}
     checks = 0
+    stale_joiner = False
     for r in range(rounds):
         if rank in TRAINERS:
             with torch.no_grad():
@@ -97,9 +98,11 @@ def run(cfg: LlamaConfig, rounds: int = 10, mode: str = "auto", leave_round: int
             dist.barrier()
             j0, j1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
             j0.record()
-            if rank == standby and not bc.mc:
-                bc.catch_up(members[0])         # read a member's arena over NVLink
-            elif rank == standby:
+            source = next((x for x in members if x != standby), None)
+            stale_joiner = not bc.mc and source is None     # nobody to copy from: the next round fills it
+            if rank == standby and not bc.mc and source is not None:
+                bc.catch_up(source)             # read a member's arena over NVLink
+            elif rank == standby and bc.mc:
                 from connex_b200 import ops    # warm standby: the multicast rounds are all there
                 ops.wait_flag(bc.flag_addr, bc.received & 0xFFFFFFFF, bc.status, 5.0)
             j1.record()
@@ -107,7 +110,7 @@ def run(cfg: LlamaConfig, rounds: int = 10, mode: str = "auto", leave_round: int
             bc.check()
             t = torch.tensor([j0.elapsed_time(j1) if rank == standby else 0.0], dtype=torch.float64, device=dev)
             dist.all_reduce(t, op=dist.ReduceOp.MAX)
-            events["join_catch_up_ms"] = float(t.item())
+            events["join_catch_up_ms"] = None if stale_joiner else float(t.item())
             events["join_round_ms"] = per_round[-1]
             if standby not in members:
                 members = members + [standby]
@@ -122,7 +125,8 @@ def run(cfg: LlamaConfig, rounds: int = 10, mode: str = "auto", leave_round: int
             box = [None] * world
             dist.all_gather_object(box, mine)
             want = sum(box[t] for t in TRAINERS)
-            ok = torch.tensor([1 if (rank not in members or _checksum(bc.arena[:m.total]) == want) else 0],
+            skip = rank not in members or (r == join_round and stale_joiner and rank == standby)
+            ok = torch.tensor([1 if (skip or _checksum(bc.arena[:m.total]) == want) else 0],
                               dtype=torch.int32, device=dev)
             dist.all_reduce(ok, op=dist.ReduceOp.MIN)
             if int(ok.item()) != 1:
@@ -133,7 +137,7 @@ def run(cfg: LlamaConfig, rounds: int = 10, mode: str = "auto", leave_round: int
     return {"mode": "multicast" if bc.mc else "p2p", "rounds": rounds, "trainers": len(TRAINERS),
             "rollouts_start": len(rollouts) - (0 if leaver == standby else 1), "engine_bytes": m.total,
             "round_ms": [round(x, 3) for x in per_round], "median_round_ms": round(statistics.median(steady), 3),
-            **{k: round(v, 3) for k, v in events.items()}, "verified_rounds": checks}
+            **{k: (None if v is None else round(v, 3)) for k, v in events.items()}, "verified_rounds": checks}
 
 
 def main() -> None:
