@@ -161,7 +161,7 @@ def prefill_side(args, cfg, weights, dev, sock, dst, n_dec_blocks: int) -> Dict:
             n = len(reqs[i][1])
             if pick and tokens + n > args.token_budget:
                 break
-            if blocks + need[i] > len(free) or cache.free_blocks() < cache.blocks_needed(tokens + n) + len(pick) + 1:
+            if blocks + need[i] > len(free) or cache.free_blocks < cache.blocks_needed(tokens + n) + len(pick) + 1:
                 break
             pick.append(i)
             tokens += n
