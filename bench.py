@@ -22,7 +22,11 @@ Reported (rank 0, one JSON line):
                    through the public PD API including the H2D copy of the
                    prompt ids from pinned memory and the D2H read of the
                    first tokens;
-* ``p50_ttft_ms``, per-step times, clocks and launch counts.
+* ``p50_ttft_ms``, per-step times, clocks and launch counts;
+* ``sub_metrics`` -- the fused EP MoE layer and the fused weight broadcast
+  (each against its NCCL baseline), the EP failover time, and (N >= 2) a
+  10-second serving run per pair under Poisson load (4 requests/s, 128
+  output tokens): ``serving_ttft_p50_ms``, ``serving_tpot_p50_ms``, ...
 
 Timing: W untimed warm-up steps, then K steps, each bracketed by a barrier
 and ``torch.cuda.synchronize()``; device time by CUDA events; max over ranks.
@@ -145,6 +149,19 @@ def main() -> None:
         from connex_b200.bench.sub_metrics import run_sub_metrics
         dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
         sub = run_sub_metrics(world, rank, dev, layers=args.layers)
+        if world > 1:
+            # serving under load: Poisson arrivals on every prefill/decode pair
+            from datetime import timedelta
+            from connex_b200.bench.pd_serving_bench import parser as serving_parser, run_serving
+            torch.cuda.empty_cache()
+            cpu = dist.new_group(backend="gloo", timeout=timedelta(seconds=300))
+            sargs = serving_parser().parse_args(["--qps", "4", "--duration", "10", "--layers", str(args.layers),
+                                                 "--min-len", str(args.min_len), "--max-len", str(args.max_len)])
+            srv = run_serving(sargs, world, rank, int(os.environ.get("LOCAL_RANK", "0")), cpu)
+            if sub is not None and srv is not None:
+                sub.update({f"serving_{k}": srv[k] for k in ("qps_per_pair", "duration_s", "requests", "completed",
+                                                               "ttft_p50_ms", "ttft_p99_ms", "tpot_p50_ms",
+                                                               "output_tok_s")})
         if res is not None:
             res["sub_metrics"] = sub
     if world > 1 and dist.is_initialized():

@@ -43,7 +43,7 @@ import os
 import statistics
 import time
 from datetime import timedelta
-from typing import Dict, List
+from typing import Dict, List, Optional
 
 import numpy as np
 import torch
@@ -274,7 +274,7 @@ def decode_side(args, cfg, weights, dev, sock, cache, ready) -> Dict:
             "span_s": span, "completed": n_done, "lost": lost_n, "stall_ms": stalls}
 
 
-def main() -> None:
+def parser() -> argparse.ArgumentParser:
     p = argparse.ArgumentParser()
     p.add_argument("--qps", type=float, default=4.0)
     p.add_argument("--duration", type=float, default=20.0)
@@ -289,15 +289,14 @@ def main() -> None:
     p.add_argument("--decode-blocks", type=int, default=16384)
     p.add_argument("--layers", type=int, default=32)
     p.add_argument("--seed", type=int, default=0)
-    args = p.parse_args()
-    world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
-    local = int(os.environ.get("LOCAL_RANK", "0"))
-    if world < 2 or world % 2:
-        raise SystemExit("PD serving needs prefill/decode pairs: an even number of GPUs >= 2")
+    return p
+
+
+def run_serving(args, world: int, rank: int, local: int, cpu) -> Optional[Dict]:
+    """One serving run on every rank (the process group is up, ``cpu`` is a
+    gloo group); rank 0 returns the summary."""
     dev = torch.device("cuda", local)
-    torch.cuda.set_device(dev)
-    dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
-    cpu = dist.new_group(backend="gloo", timeout=timedelta(seconds=300))
+    summary = None
     role = "prefill" if rank < world // 2 else "decode"
     args.pair = rank % (world // 2)
     cfg = LlamaConfig(layers=args.layers)
@@ -339,7 +338,7 @@ def main() -> None:
         tpot = [x for r in dec for x in r["tpot_ms"]]
         out_tok = sum(r["output_tokens"] for r in dec)
         span = max(r["span_s"] for r in dec)
-        print(json.dumps({
+        summary = {
             "bench": "pd_serving", "model": f"Llama-3-8B architecture ({args.layers} layers)",
             "pairs": world // 2, "qps_per_pair": args.qps, "duration_s": args.duration,
             "prompt_len": [args.min_len, args.max_len], "out_tokens": args.out_tokens,
@@ -354,10 +353,28 @@ def main() -> None:
                 "resume_stall_max_ms": round(max([x for r in dec for x in r["stall_ms"]] or [float("nan")]), 1)}
                if args.kill_at > 0 else {}),
             "decode_steps": sum(r["decode_steps"] for r in dec),
-            "data": "synthetic (random token ids, random-init weights)"}), flush=True)
+            "data": "synthetic (random token ids, random-init weights)"}
     sock.close(0)
     ctx.term()
     mapper.close()
+    dist.barrier(group=cpu)          # every peer mapping is closed before the decode caches go
+    return summary if rank == 0 else None
+
+
+
+def main() -> None:
+    args = parser().parse_args()
+    world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world < 2 or world % 2:
+        raise SystemExit("PD serving needs prefill/decode pairs: an even number of GPUs >= 2")
+    dev = torch.device("cuda", local)
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=300))
+    cpu = dist.new_group(backend="gloo", timeout=timedelta(seconds=300))
+    out = run_serving(args, world, rank, local, cpu)
+    if out is not None:
+        print(json.dumps(out), flush=True)
     dist.destroy_process_group()
 
 
