@@ -1,7 +1,9 @@
 """Secondary metrics of the flagship benchmark line, measured in the same job
 right after the PD steps: the fused Llama-3-8B weight broadcast (fp32
 trainer weights -> bf16 engine layout on every other GPU) against an NCCL
-broadcast, the fused EP MoE layer latency (dispatch + expert GEMMs +
+broadcast (and, N >= 4, from two FSDP trainer shards on ranks 0-1 to the
+other GPUs, against NCCL broadcasts of the cast shards), the fused EP MoE
+layer latency (dispatch + expert GEMMs +
 combine, Qwen3-30B-A3B layer geometry, 128 tokens per rank) against the
 NCCL all-to-all baseline, and (N > 1) the EP failover time: the last rank
 leaves, the others route around it and finish their next forward (host
@@ -24,6 +26,11 @@ def run_sub_metrics(world: int, rank: int, dev, layers: int = 32) -> Optional[di
     cpu = dist.new_group(backend="gloo", timeout=timedelta(seconds=180)) if world > 1 else None
     ws = run_wsync(LlamaConfig(layers=layers), iters=3, warmup=2)
     torch.cuda.empty_cache()
+    wsh = None
+    if world >= 4:        # the RL config's shape: FSDP trainer shards on ranks 0-1, rollouts on the rest
+        from connex_b200.bench.wsync_bench import run_sharded
+        wsh = run_sharded(LlamaConfig(layers=layers), trainers=2, iters=3, warmup=2)
+        torch.cuda.empty_cache()
     ep = run_ep_bench(world, rank, dev, cpu, None, tokens=(128,), iters=10, warmup=3, failover=True)
     torch.cuda.empty_cache()
     allr = [ep]
@@ -43,4 +50,8 @@ def run_sub_metrics(world: int, rank: int, dev, layers: int = 32) -> Optional[di
         for k in ("fused_multicast_ms", "fused_p2p_ms", "nccl_ms"):
             if ws.get(k) is not None:
                 out[f"weight_sync_{k}"] = round(ws[k], 3)
+        if wsh is not None:
+            for k in ("fused_multicast_ms", "nccl_ms"):
+                if wsh.get(k) is not None:
+                    out[f"weight_sync_fsdp2_{k}"] = round(wsh[k], 3)
     return out

@@ -105,6 +105,82 @@ def run(cfg: LlamaConfig, iters: int = 5, warmup: int = 3) -> Dict:
     return out
 
 
+def unpack_jobs(jobs: torch.Tensor, packed: torch.Tensor, arena: torch.Tensor) -> None:
+    """Scatter a packed bf16 buffer (the job sources one after another, each
+    ``rows x cols``) into the engine arena at the jobs' destination rows, with
+    PyTorch strided copies (the NCCL baseline's receive side)."""
+    a16 = arena.view(torch.bfloat16)
+    off = 0
+    for _, doff, rows, cols, _, dld, blk, bstride, boff, _, _, _ in jobs.tolist():
+        n = rows * cols
+        seg = packed[off:off + n]
+        off += n
+        nblk = rows // blk
+        dst = a16.as_strided((nblk, blk, cols), (bstride * dld if nblk > 1 else dld * blk, dld, 1),
+                             doff // 2 + boff * dld)
+        dst.copy_(seg.view(nblk, blk, cols))
+
+
+def run_sharded(cfg: LlamaConfig, trainers: int = 2, iters: int = 3, warmup: int = 2) -> Dict:
+    """Trainer sharded FSDP-style (dim-0 shards, fp32) on ranks ``0..trainers-1``
+    -> bf16 engine arenas on the other ranks.  Arms: the fused broadcast with
+    every shard as a multicast source, and NCCL: each trainer casts its shard
+    with PyTorch into a packed bf16 buffer and broadcasts it, every receiver
+    scatters it into the engine layout with PyTorch copies."""
+    from connex_b200.parallel.wsync import shard_dim0
+    world, rank = dist.get_world_size(), dist.get_rank()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    m = engine_manifest(cfg)
+    srcs = list(range(trainers))
+    local = starts = None
+    if rank in srcs:
+        full = random_trainer_weights(cfg, dev, dtype=torch.float32, seed=1)
+        local, starts = shard_dim0(full, rank, trainers)
+        local = {k: v.clone() for k, v in local.items()}
+        del full
+        torch.cuda.empty_cache()
+    jobs_cpu = plan_jobs(cfg, m, local, starts=starts)[0] if local is not None else None
+    tables = [None] * world
+    dist.all_gather_object(tables, (jobs_cpu.tolist(), int(sum(t.numel() for t in local.values())))
+                           if jobs_cpu is not None else None)
+    out: Dict = {"engine_bytes": m.total, "trainers": trainers, "receivers": world - trainers}
+    try:
+        bc = WeightBroadcast(cfg, mode="multicast", srcs=srcs)
+        n_tasks = None
+        bc.sync(local, n_tasks, starts)
+        box = [None] * world
+        dist.all_gather_object(box, bc._jobs[2] if bc.is_src else None)
+        n_tasks = [box[t] for t in srcs]
+        for _ in range(warmup):
+            bc.sync(local, n_tasks, starts)
+        out["fused_multicast_ms"] = _time(lambda: bc.sync(local, n_tasks, starts), iters, world)
+        torch.cuda.synchronize()
+        bc.check()
+        bc.close()
+        del bc
+    except RuntimeError as e:
+        out["fused_multicast_ms"] = None
+        out["fused_multicast_error"] = str(e)[:120]
+    torch.cuda.empty_cache()
+    arena = torch.empty(m.total, dtype=torch.uint8, device=dev) if rank not in srcs else None
+    bufs = {t: torch.empty(tables[t][1], dtype=torch.bfloat16, device=dev) for t in srcs if t != rank}
+    jobs_of = {t: torch.tensor(tables[t][0], dtype=torch.int64) for t in srcs}
+
+    def nccl():
+        for t in srcs:
+            if rank == t:
+                buf = torch.cat([v.to(torch.bfloat16).reshape(-1) for v in local.values()])
+            else:
+                buf = bufs[t]
+            dist.broadcast(buf, src=t)
+            if arena is not None:
+                unpack_jobs(jobs_of[t], buf, arena)
+    for _ in range(warmup):
+        nccl()
+    out["nccl_ms"] = _time(nccl, iters, world)
+    return out
+
+
 def main() -> None:
     import argparse
     p = argparse.ArgumentParser()

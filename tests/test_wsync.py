@@ -144,3 +144,19 @@ def test_shard_start_must_sit_on_a_block():
     n = "model.norm.weight"
     with pytest.raises(ValueError, match="8-element"):
         pj(CFG, engine_manifest(CFG), {n: named[n][4:]}, starts={n: 4})
+
+
+def test_nccl_baseline_unpack_matches_the_kernel_layout():
+    """The sharded NCCL baseline's receive side (packed bf16 -> engine arena
+    with PyTorch strided copies) writes the same bytes as the fused plan."""
+    from connex_b200.bench.wsync_bench import unpack_jobs
+    from connex_b200.parallel.wsync import shard_dim0
+    named = random_trainer_weights(CFG, "cpu", dtype=torch.float32, seed=9)
+    m = engine_manifest(CFG)
+    got = torch.zeros(m.total, dtype=torch.uint8)
+    for r in range(2):
+        local, starts = shard_dim0(named, r, 2)
+        jobs, _, _ = plan_jobs(CFG, m, local, starts=starts)
+        packed = torch.cat([v.to(torch.bfloat16).reshape(-1) for v in local.values()])
+        unpack_jobs(jobs, packed, got)
+    assert torch.equal(got, _engine_bytes(CFG, fuse_reference(CFG, named), m))
