@@ -200,6 +200,8 @@ class PipelineEndpoint:
         self.current: Optional[int] = None            # downstream replica (sticky)
         self.current_addr: Optional[str] = None
         self.deregistered: set = set()
+        self.suspect: set = set()                    # (stage, replica) that missed a lease, being probed
+        self._probe_threads: List[threading.Thread] = []
         self.codec = wire.LayoutCodec()
         self.stats = defaultdict(int)
         self.trace = _Tracer(TRACE_PREFIX, stage_idx)
@@ -434,6 +436,7 @@ class PipelineEndpoint:
 
     def on_peer_dead(self, stage_idx: int, replica_idx: int, reason: str = "") -> bool:
         """A peer is gone; True if it was this endpoint's downstream."""
+        self.suspect.discard((stage_idx, replica_idx))
         self.deregistered.add((stage_idx, replica_idx))
         if self.links is not None and self.membership is not None:
             for r in self.membership.get_stage_peers(stage_idx):
@@ -458,8 +461,8 @@ class PipelineEndpoint:
         self.membership = membership
         if hasattr(membership, "on_event"):
             from connex.front_router import EventType
-            for ev in (EventType.ENDPOINT_DEREGISTERED, EventType.ENDPOINT_UNHEALTHY):
-                membership.on_event(ev, self._on_membership_event)
+            membership.on_event(EventType.ENDPOINT_DEREGISTERED, self._on_membership_event)
+            membership.on_event(EventType.ENDPOINT_UNHEALTHY, self._on_membership_unhealthy)
             membership.on_event(EventType.ENDPOINT_REGISTERED, self._on_membership_join)
 
     def _on_membership_event(self, ev) -> None:
@@ -468,10 +471,37 @@ class PipelineEndpoint:
         if "stage_idx" in lid:
             self.on_peer_dead(lid["stage_idx"], lid.get("replica_idx", 0), payload.get("reason", "event"))
 
+    def _on_membership_unhealthy(self, ev) -> None:
+        """A missed lease makes a peer *suspect*, not dead: only our own
+        downstream matters, and it is probed in the background.  A refused
+        connect confirms the death and fails over now (before the lease's
+        grace ends); a peer that still accepts connects is kept (a busy
+        process can miss a heartbeat)."""
+        payload = getattr(ev, "payload", {}) or {}
+        lid = payload.get("lid") or {}
+        if "stage_idx" not in lid:
+            return
+        key = (lid["stage_idx"], lid.get("replica_idx", 0))
+        if key != (self.stage_idx + 1, self.current):
+            return
+        self.suspect.add(key)
+        addr = self.current_addr
+
+        def probe():
+            alive = probe_tcp(addr)
+            if alive is False and key in self.suspect:
+                self.on_peer_dead(key[0], key[1], "unhealthy, probe refused")
+            else:
+                self.stats["suspect_alive"] += 1
+        t = threading.Thread(target=probe, daemon=True, name="cx-pp-probe")
+        t.start()
+        self._probe_threads.append(t)
+
     def _on_membership_join(self, ev) -> None:
         payload = getattr(ev, "payload", {}) or {}
         lid = payload.get("lid") or {}
         if "stage_idx" in lid:
+            self.suspect.discard((lid["stage_idx"], lid.get("replica_idx", 0)))
             self.on_peer_alive(lid["stage_idx"], lid.get("replica_idx", 0))
             addrs = payload.get("addresses") or []
             if self.auto_warm and self.is_first and lid["stage_idx"] == 1 and addrs:
