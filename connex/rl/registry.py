@@ -102,7 +102,8 @@ class WeightRegistry:
 
     def assign(self, version, member, exclude=()):
         with self.lock:
-            hs = {m: h for m, h in self.holders.get(version, {}).items() if m != member and m not in exclude}
+            hs = {m: h for m, h in self.holders.get(version, {}).items()
+                  if m != member and m not in exclude and not h.get("retiring")}
             if not hs:
                 return None
 
@@ -163,6 +164,9 @@ class WeightRegistry:
 
     def wait_idle(self, version, member=PUBLISHER, timeout=5.0, retire=False):
         with self.cv:
+            h = self.holders.get(version, {}).get(member)
+            if retire and h is not None:
+                h["retiring"] = True       # the copy is about to be overwritten: no new readers
             ok = self.cv.wait_for(lambda: self.holders.get(version, {}).get(member, {"load": 0})["load"] == 0,
                                   timeout=timeout)
             if not ok:
