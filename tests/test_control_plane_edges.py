@@ -1,7 +1,7 @@
 """Edge cases of the control plane and the serving layer on CPU: an aborted
 migration cannot be cut over and a completed one is not replayed; pool admin
 needs loopback or the admin token; a stream that breaks after its last token
-is a success; a stream cut after its finish reason is not resumed; a lapsed
+is a success and is not resumed; a lapsed
 blacklist re-arms the replica without a prober; a stale release from an
 earlier reader does not free a newer reader's KV hold."""
 import asyncio
