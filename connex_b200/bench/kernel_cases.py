@@ -104,9 +104,8 @@ def case_wsync(dev, layers=2):
     return (lambda: apply_local(jobs, arena)), {"bytes": m.total * 3}    # 4 B read + 2 B written per element
 
 
-def case_ep_gemm(dev):
+def case_ep_gemm(dev, T: int = 4096):
     from connex_b200.bench.ep_bench import H, FFN, FusedEP, zipf_routing
-    T = 4096
     fused = FusedEP(1, 0, dev, T)
     idx, w = zipf_routing(T, seed=3, device=dev)
     x = (torch.randn(T, H, device=dev) * 0.5).bfloat16()
@@ -117,7 +116,8 @@ def case_ep_gemm(dev):
 
 CASES = {"gemm": lambda d: case_gemm(d), "gemm_qkv": lambda d: case_gemm(d, 8192, 6144, 4096),
          "gemm_silu": lambda d: case_gemm(d, 8192, 28672, 4096, silu=True), "attn": case_attn,
-         "decode_attn": case_decode_attn, "kv_push": case_kv_push, "wsync": case_wsync, "ep_gemm": case_ep_gemm}
+         "decode_attn": case_decode_attn, "kv_push": case_kv_push, "wsync": case_wsync, "ep_gemm": case_ep_gemm,
+         "ep_t128": lambda d: case_ep_gemm(d, 128)}
 
 
 def main() -> None:

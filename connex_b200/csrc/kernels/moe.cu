@@ -75,20 +75,33 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const __nv_bfloat16* _
                                                           const int* counts, int T, int K, int H, int N, int S, int me,
                                                           int R_max, uint32_t count_target, EpPeers peers,
                                                           int* status) {
-  extern __shared__ int off[];  // [N*S]: first row of (me -> dst, slot) at dst
+  extern __shared__ int off[];  // [N*S]: first row of (me -> dst, slot) at dst; then tot[N*S]
   __shared__ int ok;
   if (threadIdx.x == 0)
     ok = wait_flag_geq(reinterpret_cast<const uint32_t*>(peers.count_flag[me]), count_target, kDefaultWaitNs, status);
   __syncthreads();
   if (!ok) return;
   const int NB = N * S;
+  int* tot = off + NB;  // rows of (dst, slot) from every source
+  // one pass over the count matrix, every thread on its own (dst, slot): N loads each, in parallel
+  for (int i = threadIdx.x; i < NB; i += blockDim.x) {
+    const int d = i / S, s = i - d * S;
+    int all = 0, before_me = 0;
+    for (int src = 0; src < N; ++src) {
+      const int c = (int)ld_acquire_gpu_u32((const uint32_t*)&counts[(src * N + d) * S + s]);
+      all += c;
+      if (src < me) before_me += c;
+    }
+    tot[i] = all;
+    off[i] = before_me;
+  }
+  __syncthreads();
+  // slot s of dst d starts after every source's rows of slots < s (prefix from shared memory)
   for (int i = threadIdx.x; i < NB; i += blockDim.x) {
     const int d = i / S, s = i - d * S;
     int base = 0;
-    for (int s2 = 0; s2 < s; ++s2)
-      for (int src = 0; src < N; ++src) base += ld_acquire_gpu_u32((const uint32_t*)&counts[(src * N + d) * S + s2]);
-    for (int src = 0; src < me; ++src) base += ld_acquire_gpu_u32((const uint32_t*)&counts[(src * N + d) * S + s]);
-    off[i] = base;
+    for (int s2 = 0; s2 < s; ++s2) base += tot[d * S + s2];
+    off[i] += base;
   }
   __syncthreads();
   const int lane = threadIdx.x & 31;
@@ -151,24 +164,30 @@ __global__ void __launch_bounds__(epg::THREADS, 1)
 
   const int warp = warp_id(), lane = lane_id();
   const int n_tiles = n_per_expert / BN;
-  if (threadIdx.x == 0) {
-    ok = wait_flag == nullptr ? 1 : (int)wait_flag_geq(wait_flag, wait_target, kDefaultWaitNs, status);
-    if (ok) {
-      int r = 0, t = 0;
-      for (int e = 0; e < S; ++e) {
-        seg[e] = r;
-        tpre[e] = t;
-        int rows = 0;
-        for (int src = 0; src < N; ++src) rows += ld_acquire_gpu_u32((const uint32_t*)&counts[(src * N + me) * S + e]);
-        r += rows;
-        t += ((rows + BM - 1) / BM) * n_tiles;
-      }
-      seg[S] = r;
-      tpre[S] = t;
-      if (r > R_max) {  // counts beyond the receive capacity: do nothing, report
-        record_status(status, CX_ERR_BOUNDS);
-        ok = 0;
-      }
+  if (threadIdx.x == 0) ok = wait_flag == nullptr ? 1 : (int)wait_flag_geq(wait_flag, wait_target, kDefaultWaitNs, status);
+  __syncthreads();
+  if (ok) {  // rows per local expert, summed over sources by all threads in parallel
+    for (int e = threadIdx.x; e < S; e += blockDim.x) {
+      int rows = 0;
+      for (int src = 0; src < N; ++src) rows += ld_acquire_gpu_u32((const uint32_t*)&counts[(src * N + me) * S + e]);
+      tpre[e] = rows;
+    }
+  }
+  __syncthreads();
+  if (threadIdx.x == 0 && ok) {  // prefixes (in place): row starts and tile starts
+    int r = 0, t = 0;
+    for (int e = 0; e < S; ++e) {
+      const int rows = tpre[e];
+      seg[e] = r;
+      tpre[e] = t;
+      r += rows;
+      t += ((rows + BM - 1) / BM) * n_tiles;
+    }
+    seg[S] = r;
+    tpre[S] = t;
+    if (r > R_max) {  // counts beyond the receive capacity: do nothing, report
+      record_status(status, CX_ERR_BOUNDS);
+      ok = 0;
     }
   }
   if (warp == 0 && lane == 0) {
@@ -397,7 +416,8 @@ void ep_dispatch(const void* x, const float* topk_w, const int* pos, const int* 
                  int T, int K, int H, int N, int S, int me, int R_max, uint32_t count_target, EpPeers peers,
                  int* status, cudaStream_t s) {
   if (H % 8) throw std::runtime_error("cx ep_dispatch: hidden size must be a multiple of 8");
-  ep_dispatch_kernel<<<EP_DISPATCH_CTAS, 256, N * S * sizeof(int), s>>>(
+  if (2L * N * S * sizeof(int) > 48 * 1024) throw std::runtime_error("cx ep_dispatch: too many (rank, slot) pairs");
+  ep_dispatch_kernel<<<EP_DISPATCH_CTAS, 256, 2 * N * S * sizeof(int), s>>>(
       reinterpret_cast<const __nv_bfloat16*>(x), topk_w, pos, slot_of, counts_local, T, K, H, N, S, me, R_max,
       count_target, peers, status);
 }
