@@ -119,7 +119,17 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const __nv_bfloat16* _
     const u128* src = reinterpret_cast<const u128*>(x + (size_t)(i / K) * H);
     u128* dst = reinterpret_cast<u128*>(reinterpret_cast<__nv_bfloat16*>(peers.recv[d]) + (size_t)row * H);
     if (!aligned16(src, 1, status) || !aligned16(dst, 1, status)) continue;
-    for (int v = lane; v < nvec; v += 32) st_cs_v4(dst + v, ld_nc_v4(src + v));
+    // 8 loads per lane in flight before the stores (a 2048-wide bf16 row is exactly 256 vectors)
+    constexpr int ILP = 8;
+    int v0 = 0;
+    for (; v0 + 32 * ILP <= nvec; v0 += 32 * ILP) {
+      u128 buf[ILP];
+#pragma unroll
+      for (int j = 0; j < ILP; ++j) buf[j] = ld_nc_v4(src + v0 + lane + 32 * j);
+#pragma unroll
+      for (int j = 0; j < ILP; ++j) st_cs_v4(dst + v0 + lane + 32 * j, buf[j]);
+    }
+    for (int v = v0 + lane; v < nvec; v += 32) st_cs_v4(dst + v, ld_nc_v4(src + v));
     if (lane == 0) {
       int4 m = make_int4(me, i, __float_as_int(topk_w[i]), 0);
       int4* mp = reinterpret_cast<int4*>(peers.recv_meta[d]) + row;
@@ -161,6 +171,8 @@ __global__ void __launch_bounds__(epg::THREADS, 1)
   int* seg = reinterpret_cast<int*>(smem + STAGES * STAGE_BYTES + 256);  // [S+1] row starts
   int* tpre = seg + (MAXS + 1);                                          // [S+1] tile prefix
   __shared__ int ok;
+  __shared__ unsigned comb_rows[EP_MAX_RANKS];  // mode 1: rows stored into each source's combine buffer
+  for (int i = threadIdx.x; i < EP_MAX_RANKS; i += blockDim.x) comb_rows[i] = 0u;
 
   const int warp = warp_id(), lane = lane_id();
   const int n_tiles = n_per_expert / BN;
@@ -349,21 +361,21 @@ __global__ void __launch_bounds__(epg::THREADS, 1)
           }
         }
         if (valid && !ok_src) record_status(status, CX_ERR_BOUNDS);
-        // one release per distinct source in the warp, counting its rows
-        __threadfence_system();
-        __syncwarp();
+        // count this tile's rows per source; the CTA releases them once, after its last tile
         const int key = ok_src ? src : -1;
         const unsigned peers_mask = __match_any_sync(0xffffffffu, key);
-        if (key >= 0 && lane == __ffs(peers_mask) - 1)
-          red_release_sys_add_u32(reinterpret_cast<uint32_t*>(peers.comb_flag[key]), (uint32_t)__popc(peers_mask));
+        if (key >= 0 && lane == __ffs(peers_mask) - 1) atomicAdd(&comb_rows[key], (unsigned)__popc(peers_mask));
       }
       tc_fence_before();
       mbar_arrive(&tempty[acc]);
       acc ^= 1;
       if (!acc) acc_phase ^= 1;
     }
+    if (mode != 0) __threadfence_system();  // this thread's combine stores, before the CTA's releases
   }
   __syncthreads();
+  if (mode != 0 && threadIdx.x < N && comb_rows[threadIdx.x])
+    red_release_sys_add_u32(reinterpret_cast<uint32_t*>(peers.comb_flag[threadIdx.x]), comb_rows[threadIdx.x]);
   if (warp == 1) {
     tc_fence_after();
     tmem_dealloc(tmem_base, 2 * BN);
@@ -428,6 +440,7 @@ void ep_grouped_gemm(const void* A, int lda, const void* B, int n_per_expert, in
                      cudaStream_t s) {
   using namespace epg;
   if (S > MAXS) throw std::runtime_error("cx ep gemm: too many local experts");
+  if (N > EP_MAX_RANKS) throw std::runtime_error("cx ep gemm: too many EP ranks");
   if (n_per_expert % BN || K % 8) throw std::runtime_error("cx ep gemm: expert width must be a multiple of 256");
   static bool attr[64] = {false};
   int dev;

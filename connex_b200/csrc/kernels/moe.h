@@ -26,6 +26,7 @@ struct EpPeers {
 };
 
 constexpr int EP_DISPATCH_CTAS = 132;
+constexpr int EP_MAX_RANKS = 64;
 
 // Count kernel: one CTA.  pos[T*K] receives each routed row's index in its
 // (dst rank, slot) bucket, slot_of[T*K] its global physical slot (-1: not
