@@ -38,21 +38,43 @@ __global__ void __launch_bounds__(1024) ep_count_kernel(const int* __restrict__ 
   if (threadIdx.x == 0) valid = 0;
   __syncthreads();
   int my_valid = 0;
-  for (int i = threadIdx.x; i < T * K; i += blockDim.x) {
-    const int e = topk_idx[i];
-    int slot = -1;
-    if (e >= 0) {
-      const int c = l2p_cnt[e];
-      if (c > 0) slot = l2p[e * max_rep + ((i / K) % c)];  // spread a token's replicas by token index
+  const int TK = T * K;
+  const int lane = threadIdx.x & 31;
+  constexpr int U = 4;  // routed rows per thread per pass: their dependent loads overlap
+  for (int base = 0; base < TK; base += blockDim.x * U) {  // uniform trip count: whole warps take part
+    int idx[U], e[U], c[U], slot[U];
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      idx[u] = base + u * blockDim.x + threadIdx.x;
+      e[u] = idx[u] < TK ? topk_idx[idx[u]] : -1;
     }
-    if (slot < 0 || slot >= NB) {
-      slot_of[i] = -1;
-      pos[i] = -1;
-      continue;
+#pragma unroll
+    for (int u = 0; u < U; ++u) c[u] = e[u] >= 0 ? l2p_cnt[e[u]] : 0;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      // spread a token's replicas by token index
+      slot[u] = c[u] > 0 ? l2p[e[u] * max_rep + ((idx[u] / K) % c[u])] : -1;
+      if (slot[u] >= NB) slot[u] = -1;
     }
-    slot_of[i] = slot;
-    pos[i] = atomicAdd(&hist[slot], 1);
-    ++my_valid;
+#pragma unroll
+    for (int u = 0; u < U; ++u) {
+      // one shared-memory atomic per distinct slot in the warp (skewed routing hits few slots)
+      const unsigned grp = __match_any_sync(0xffffffffu, slot[u]);
+      const int leader = __ffs(grp) - 1;
+      int b = 0;
+      if (slot[u] >= 0 && lane == leader) b = atomicAdd(&hist[slot[u]], __popc(grp));
+      b = __shfl_sync(0xffffffffu, b, leader);
+      if (idx[u] < TK) {
+        if (slot[u] < 0) {
+          slot_of[idx[u]] = -1;
+          pos[idx[u]] = -1;
+        } else {
+          slot_of[idx[u]] = slot[u];
+          pos[idx[u]] = b + __popc(grp & ((1u << lane) - 1u));
+          ++my_valid;
+        }
+      }
+    }
   }
   atomicAdd(&valid, my_valid);
   __syncthreads();
@@ -107,33 +129,52 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const __nv_bfloat16* _
   const int lane = threadIdx.x & 31;
   const int wpb = blockDim.x >> 5;
   const int nvec = H / 8;  // 16-byte vectors per row
-  for (int i = blockIdx.x * wpb + (threadIdx.x >> 5); i < T * K; i += gridDim.x * wpb) {
-    const int slot = slot_of[i];
-    if (slot < 0) continue;
-    const int d = slot / S;
-    const int row = off[slot] + pos[i];
-    if (row < 0 || row >= R_max) {
-      record_status(status, CX_ERR_BOUNDS);
-      continue;
+  const int TK = T * K;
+  const int n_warps = gridDim.x * wpb;
+  // each warp takes `chunk` consecutive routed rows at a time (up to 32, fewer when there are
+  // few rows, so every warp has work): their slot / position / weight are loaded once
+  // (coalesced) and broadcast, so no row waits on its own metadata loads
+  const int chunk = max(1, min(32, (TK + n_warps - 1) / n_warps));
+  for (int c0 = (blockIdx.x * wpb + (threadIdx.x >> 5)) * chunk; c0 < TK; c0 += n_warps * chunk) {
+    int my_slot = -1, my_pos = 0;
+    float my_w = 0.f;
+    if (lane < chunk && c0 + lane < TK) {
+      my_slot = slot_of[c0 + lane];
+      my_pos = pos[c0 + lane];
+      my_w = topk_w[c0 + lane];
     }
-    const u128* src = reinterpret_cast<const u128*>(x + (size_t)(i / K) * H);
-    u128* dst = reinterpret_cast<u128*>(reinterpret_cast<__nv_bfloat16*>(peers.recv[d]) + (size_t)row * H);
-    if (!aligned16(src, 1, status) || !aligned16(dst, 1, status)) continue;
-    // 8 loads per lane in flight before the stores (a 2048-wide bf16 row is exactly 256 vectors)
-    constexpr int ILP = 8;
-    int v0 = 0;
-    for (; v0 + 32 * ILP <= nvec; v0 += 32 * ILP) {
-      u128 buf[ILP];
+    const int n_rows = min(chunk, TK - c0);
+    for (int j = 0; j < n_rows; ++j) {
+      const int i = c0 + j;
+      const int slot = __shfl_sync(0xffffffffu, my_slot, j);
+      const int p = __shfl_sync(0xffffffffu, my_pos, j);
+      const float wt = __shfl_sync(0xffffffffu, my_w, j);
+      if (slot < 0) continue;
+      const int d = slot / S;
+      const int row = off[slot] + p;
+      if (row < 0 || row >= R_max) {
+        record_status(status, CX_ERR_BOUNDS);
+        continue;
+      }
+      const u128* src = reinterpret_cast<const u128*>(x + (size_t)(i / K) * H);
+      u128* dst = reinterpret_cast<u128*>(reinterpret_cast<__nv_bfloat16*>(peers.recv[d]) + (size_t)row * H);
+      if (!aligned16(src, 1, status) || !aligned16(dst, 1, status)) continue;
+      // 8 loads per lane in flight before the stores (a 2048-wide bf16 row is exactly 256 vectors)
+      constexpr int ILP = 8;
+      int v0 = 0;
+      for (; v0 + 32 * ILP <= nvec; v0 += 32 * ILP) {
+        u128 buf[ILP];
 #pragma unroll
-      for (int j = 0; j < ILP; ++j) buf[j] = ld_nc_v4(src + v0 + lane + 32 * j);
+        for (int q = 0; q < ILP; ++q) buf[q] = ld_nc_v4(src + v0 + lane + 32 * q);
 #pragma unroll
-      for (int j = 0; j < ILP; ++j) st_cs_v4(dst + v0 + lane + 32 * j, buf[j]);
-    }
-    for (int v = v0 + lane; v < nvec; v += 32) st_cs_v4(dst + v, ld_nc_v4(src + v));
-    if (lane == 0) {
-      int4 m = make_int4(me, i, __float_as_int(topk_w[i]), 0);
-      int4* mp = reinterpret_cast<int4*>(peers.recv_meta[d]) + row;
-      if (aligned16(mp, 2, status)) *mp = m;
+        for (int q = 0; q < ILP; ++q) st_cs_v4(dst + v0 + lane + 32 * q, buf[q]);
+      }
+      for (int v = v0 + lane; v < nvec; v += 32) st_cs_v4(dst + v, ld_nc_v4(src + v));
+      if (lane == 0) {
+        int4 m = make_int4(me, i, __float_as_int(wt), 0);
+        int4* mp = reinterpret_cast<int4*>(peers.recv_meta[d]) + row;
+        if (aligned16(mp, 2, status)) *mp = m;
+      }
     }
   }
   __syncthreads();
