@@ -227,15 +227,15 @@ int64_t wsync(const at::Tensor& jobs_dev, const at::Tensor& jobs_cpu, int64_t ds
 
 void chan_copy(std::vector<int64_t> src, std::vector<int64_t> dst, std::vector<int64_t> bytes, int64_t wait_on,
                int64_t wait_target, int64_t timeout_ns, int64_t signal, int64_t value, int64_t mode, int64_t done_ctr,
-               int64_t ctas, const at::Tensor& status) {
+               int64_t ctas, const at::Tensor& status, int64_t abort) {
   TORCH_CHECK(src.size() == dst.size() && dst.size() == bytes.size(), "chan_copy: segment lists differ in length");
   TORCH_CHECK(status.is_cuda() && status.scalar_type() == at::kInt, "chan_copy: status must be an int32 CUDA word");
   const c10::cuda::CUDAGuard g(status.device());
   cx::chan_copy(reinterpret_cast<const uint64_t*>(src.data()), reinterpret_cast<const uint64_t*>(dst.data()),
                 reinterpret_cast<const uint64_t*>(bytes.data()), (int)src.size(),
                 reinterpret_cast<const uint32_t*>(wait_on), (uint32_t)wait_target, (uint64_t)timeout_ns,
-                reinterpret_cast<uint32_t*>(signal), (uint32_t)value, (int)mode, reinterpret_cast<uint32_t*>(done_ctr),
-                (int)ctas, status.data_ptr<int>(), cur_stream(status));
+                reinterpret_cast<const uint32_t*>(abort), reinterpret_cast<uint32_t*>(signal), (uint32_t)value,
+                (int)mode, reinterpret_cast<uint32_t*>(done_ctr), (int)ctas, status.data_ptr<int>(), cur_stream(status));
 }
 
 void wait_flag(int64_t flag, int64_t target, int64_t timeout_ns, const at::Tensor& status) {
@@ -394,7 +394,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("wsync", &wsync);
   m.attr("WS_JOB_COLS") = cx::WS_JOB_COLS;
   m.attr("WS_MAX_DST") = cx::WS_MAX_DST;
-  m.def("chan_copy", &chan_copy);
+  m.def("chan_copy", &chan_copy, py::arg("src"), py::arg("dst"), py::arg("bytes"), py::arg("wait_on"),
+        py::arg("wait_target"), py::arg("timeout_ns"), py::arg("signal"), py::arg("value"), py::arg("mode"),
+        py::arg("done_ctr"), py::arg("ctas"), py::arg("status"), py::arg("abort") = 0);
   m.attr("CH_MAX_SEGS") = cx::CH_MAX_SEGS;
   m.def("wait_flag", &wait_flag);
   m.def("write_flag", &write_flag);

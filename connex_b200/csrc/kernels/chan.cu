@@ -9,7 +9,10 @@
 //          system scope) into the sender's `credit` counter, returning the
 //          ring slot.
 // A wait that runs out records CX_ERR_TIMEOUT in `status`, copies nothing
-// and signals nothing.
+// and signals nothing.  `abort` (optional) is a word in pinned host memory
+// that the host raises when the peer is declared dead: a launch that sees it
+// (before or while waiting) records CX_ERR_PEER and returns at once, touching
+// neither the peer's memory nor its counters.
 #include "common.cuh"
 #include "comm.h"
 
@@ -22,11 +25,40 @@ struct ChanSegs {
   int n;
 };
 
+// Bounded wait on `flag` that also gives up when the host raised `abort`.
+__device__ bool wait_or_abort(const uint32_t* flag, uint32_t target, const uint32_t* abort, uint64_t limit_ns,
+                              int* status) {
+  uint64_t t0 = 0;
+  for (uint32_t it = 0;; ++it) {
+    if (flag == nullptr || counter_reached(ld_acquire_sys_u32(flag), target)) return true;
+    if ((it & 15u) == 0u) {
+      if (abort != nullptr && ld_acquire_sys_u32(abort) != 0u) {
+        record_status(status, CX_ERR_PEER);
+        return false;
+      }
+      const uint64_t now = globaltimer_ns();
+      if (t0 == 0) t0 = now;
+      else if (now - t0 > limit_ns) {
+        record_status(status, CX_ERR_TIMEOUT);
+        return false;
+      }
+    }
+    __nanosleep(64);
+  }
+}
+
 __global__ void __launch_bounds__(256) chan_copy_kernel(ChanSegs segs, const uint32_t* wait_on, uint32_t wait_target,
-                                                        uint64_t timeout_ns, uint32_t* signal, uint32_t value,
-                                                        int mode, uint32_t* done_ctr, int* status) {
+                                                        uint64_t timeout_ns, const uint32_t* abort, uint32_t* signal,
+                                                        uint32_t value, int mode, uint32_t* done_ctr, int* status) {
   __shared__ int ok;
-  if (threadIdx.x == 0) ok = wait_on == nullptr ? 1 : (int)wait_flag_geq(wait_on, wait_target, timeout_ns, status);
+  if (threadIdx.x == 0) {
+    if (abort != nullptr && ld_acquire_sys_u32(abort) != 0u) {  // the peer is gone: leave its memory alone
+      record_status(status, CX_ERR_PEER);
+      ok = 0;
+    } else {
+      ok = (int)wait_or_abort(wait_on, wait_target, abort, timeout_ns, status);
+    }
+  }
   __syncthreads();
   if (!ok) return;
   const int lane = threadIdx.x & 31;
@@ -64,8 +96,8 @@ __global__ void __launch_bounds__(256) chan_copy_kernel(ChanSegs segs, const uin
 }
 
 void chan_copy(const uint64_t* src, const uint64_t* dst, const uint64_t* bytes, int n, const uint32_t* wait_on,
-               uint32_t wait_target, uint64_t timeout_ns, uint32_t* signal, uint32_t value, int mode,
-               uint32_t* done_ctr, int ctas, int* status, cudaStream_t s) {
+               uint32_t wait_target, uint64_t timeout_ns, const uint32_t* abort, uint32_t* signal, uint32_t value,
+               int mode, uint32_t* done_ctr, int ctas, int* status, cudaStream_t s) {
   if (n < 0 || n > CH_MAX_SEGS) throw std::runtime_error("cx chan: 0..8 segments per launch");
   ChanSegs c{};
   for (int i = 0; i < n; ++i) {
@@ -76,8 +108,8 @@ void chan_copy(const uint64_t* src, const uint64_t* dst, const uint64_t* bytes, 
   }
   c.n = n;
   if (mode == 2 && done_ctr == nullptr) throw std::runtime_error("cx chan: receiver mode needs a CTA counter");
-  chan_copy_kernel<<<ctas < 1 ? 1 : ctas, 256, 0, s>>>(c, wait_on, wait_target, timeout_ns, signal, value, mode,
-                                                       done_ctr, status);
+  chan_copy_kernel<<<ctas < 1 ? 1 : ctas, 256, 0, s>>>(c, wait_on, wait_target, timeout_ns, abort, signal, value,
+                                                       mode, done_ctr, status);
 }
 
 }  // namespace cx

@@ -25,10 +25,11 @@ int wsync(const int64_t* jobs_dev, const int64_t* jobs_host, int n_jobs, int64_t
 
 // P2P channel copy (chan.cu): wait, copy up to CH_MAX_SEGS segments, signal
 // (mode 1: +1 per CTA on `signal`; mode 2: the last CTA stores `value`).
+// `abort` (may be null): pinned host word; nonzero = the peer is gone, do nothing.
 constexpr int CH_MAX_SEGS = 8;
 void chan_copy(const uint64_t* src, const uint64_t* dst, const uint64_t* bytes, int n, const uint32_t* wait_on,
-               uint32_t wait_target, uint64_t timeout_ns, uint32_t* signal, uint32_t value, int mode,
-               uint32_t* done_ctr, int ctas, int* status, cudaStream_t s);
+               uint32_t wait_target, uint64_t timeout_ns, const uint32_t* abort, uint32_t* signal, uint32_t value,
+               int mode, uint32_t* done_ctr, int ctas, int* status, cudaStream_t s);
 
 void wait_flag(const uint32_t* flag, uint32_t target, uint64_t timeout_ns, int* status, cudaStream_t s);
 void write_flag(uint32_t* flag, uint32_t value, bool add, cudaStream_t s);

@@ -79,6 +79,15 @@ class _Stream:
         self.device = device
         self.stream = torch.cuda.Stream(device)
         self.status = ops.new_status(device)
+        # raised by the host when the peer is declared dead: queued and waiting
+        # launches of this link return without touching the peer's memory
+        self.abort = torch.zeros(4, dtype=torch.int32).pin_memory()
+
+    def cancel(self) -> None:
+        self.abort[0] = 1
+
+    def idle(self) -> bool:
+        return self.stream.query()
 
     def done_event(self):
         ev = torch.cuda.Event()
@@ -112,7 +121,7 @@ class ChanTx(_Stream):
                     nb = sum(p[3] for p in grp)
                     ops._C.chan_copy([tensors[i].data_ptr() + to for i, to, _, _ in grp], [base + po for _, _, po, _ in grp],
                                      [ln for *_, ln in grp], wait, (self.seq - self.slots) & 0xFFFFFFFF, tmo,
-                                     self.ready, 0, 1, 0, _ctas(nb), self.status)
+                                     self.ready, 0, 1, 0, _ctas(nb), self.status, self.abort.data_ptr())
                     ops._n()
         for t in tensors:
             t.record_stream(self.stream)
@@ -148,7 +157,7 @@ class ChanRx(_Stream):
                     ops._C.chan_copy([base + po for _, _, po, _ in grp], [tensors[i].data_ptr() + to for i, to, _, _ in grp],
                                      [ln for *_, ln in grp], ready, self.expected, tmo,
                                      self.credit_addr if last else 0, self.seq & 0xFFFFFFFF, 2 if last else 0, ctr,
-                                     _ctas(nb), self.status)
+                                     _ctas(nb), self.status, self.abort.data_ptr())
                     ops._n()
         for t in tensors:
             t.record_stream(self.stream)
@@ -166,6 +175,7 @@ class ChanLinks:
         self.timeout_s, self.wait = timeout_s, timedelta(seconds=wait_s)
         self.mapper = PeerMapper(self.device.index)
         self._links: Dict[Tuple[str, bool], object] = {}
+        self._graveyard: List[_Stream] = []    # dropped links whose launches may still be queued
         self._lock = threading.Lock()
 
     @staticmethod
@@ -210,10 +220,18 @@ class ChanLinks:
         return self._links.get((peer, tx))
 
     def drop_peer(self, peer: str, abort: bool = True) -> int:
+        """Forget ``peer``'s links.  With ``abort`` their queued and waiting
+        launches return at once (status CX_ERR_PEER) instead of waiting out
+        their timeout, and store nothing into the peer's memory; the link
+        objects stay alive until their streams have drained (their abort
+        words and buffers are still read by those launches)."""
         with self._lock:
             keys = [k for k in self._links if k[0] == peer]
-            for k in keys:
-                self._links.pop(k)
+            dropped = [self._links.pop(k) for k in keys]
+            self._graveyard = [l for l in self._graveyard if not l.idle()] + dropped
+        if abort:
+            for l in dropped:
+                l.cancel()
         return len(keys)
 
     def check(self) -> None:
@@ -223,4 +241,5 @@ class ChanLinks:
     def close(self) -> None:
         torch.cuda.synchronize(self.device)
         self._links.clear()
+        self._graveyard.clear()
         self.mapper.close()

@@ -56,3 +56,38 @@ def test_channel_two_gpus(tmp_path):
                        capture_output=True, text=True, env=dict(os.environ, PYTHONPATH=root), cwd=root)
     assert r.returncode == 0, r.stderr[-3000:]
     assert "[true, true]" in r.stdout
+
+
+def test_cancelled_channel_launch_returns_at_once():
+    """A launch waiting on a counter that nothing will raise (its peer died)
+    returns as soon as the host raises the link's abort word, long before its
+    timeout, with status peer-abort and nothing copied; a launch queued after
+    the abort does not wait at all."""
+    import time
+    from connex_b200 import ops
+    dev = torch.device("cuda", 0)
+    status = ops.new_status(dev)
+    flag = torch.zeros(4, dtype=torch.int32, device=dev)          # never raised
+    src = torch.randn(4096, device=dev)
+    dst = torch.zeros_like(src)
+    abort = torch.zeros(4, dtype=torch.int32).pin_memory()
+    nbytes = src.numel() * 4
+    torch.cuda.synchronize()
+    t0 = time.monotonic()
+    ops._C.chan_copy([src.data_ptr()], [dst.data_ptr()], [nbytes], flag.data_ptr(), 1, int(20e9), 0, 0, 0, 0, 1,
+                     status, abort.data_ptr())
+    time.sleep(0.3)
+    abort[0] = 1
+    torch.cuda.synchronize()
+    assert time.monotonic() - t0 < 5.0
+    assert int(status.item()) == 3 and int(dst.abs().sum().item()) == 0
+    status.zero_()
+    ops._C.chan_copy([src.data_ptr()], [dst.data_ptr()], [nbytes], 0, 0, int(20e9), 0, 0, 0, 0, 1, status,
+                     abort.data_ptr())
+    torch.cuda.synchronize()
+    assert int(status.item()) == 3 and int(dst.abs().sum().item()) == 0
+    # without an abort word the same launch copies
+    status.zero_()
+    ops._C.chan_copy([src.data_ptr()], [dst.data_ptr()], [nbytes], 0, 0, int(20e9), 0, 0, 0, 0, 1, status)
+    torch.cuda.synchronize()
+    assert int(status.item()) == 0 and torch.equal(dst, src)
