@@ -145,3 +145,71 @@ class PDMember:
 
     def stop(self) -> None:
         self.client.stop()
+
+
+def _healthy(url: str, timeout_s: float = 2.0) -> bool:
+    import urllib.request
+    try:
+        with urllib.request.urlopen(url.rstrip("/") + "/health", timeout=timeout_s) as r:
+            return r.status == 200
+    except Exception:  # noqa: BLE001 - not up yet
+        return False
+
+
+def run_member(front_router: str, model: str, role: str, replica: int, url: str, kv_addr: Optional[str] = None,
+               shard: int = 0, group_size: int = 1, poll_s: float = 2.0, stop=None, healthy=_healthy) -> int:
+    """Sidecar loop for an engine that does not register itself: register
+    once ``url``/health answers 200, deregister when it stops answering (the
+    engine died or is restarting) and register again when it is back.
+    ``stop`` (a ``threading.Event``) ends the loop with a deregistration."""
+    import threading
+    stop = stop or threading.Event()
+    member = None
+    while not stop.is_set():
+        up = healthy(url)
+        if up and member is None:
+            member = PDMember(front_router, model, role, replica, url, kv_addr=kv_addr, shard=shard,
+                              group_size=group_size)
+            if not member.start():
+                member.stop()
+                member = None
+        elif not up and member is not None:
+            log.warning("PD member %s: %s/health stopped answering; deregistering", pd_lid(model, role, replica,
+                                                                                          shard), url)
+            member.stop()
+            member = None
+        stop.wait(poll_s)
+    if member is not None:
+        member.stop()
+    return 0
+
+
+def main(argv=None) -> int:
+    """``python -m connex.pd.membership --front-router tcp://fr:15555 --model M --role prefill
+    --replica 0 --url http://me:8100`` — keeps an engine's PD pool membership
+    while its HTTP server is healthy (a sidecar next to a vLLM server with
+    the ConnexConnector)."""
+    import argparse
+    import signal
+    import threading
+    ap = argparse.ArgumentParser(description="register a PD instance in the front-router pools while it is healthy")
+    ap.add_argument("--front-router", required=True)
+    ap.add_argument("--model", required=True)
+    ap.add_argument("--role", choices=[PDRole.PREFILL, PDRole.DECODE], required=True)
+    ap.add_argument("--replica", type=int, default=0)
+    ap.add_argument("--url", required=True)
+    ap.add_argument("--kv-addr", default=None)
+    ap.add_argument("--shard", type=int, default=0)
+    ap.add_argument("--group-size", type=int, default=1)
+    ap.add_argument("--poll-s", type=float, default=2.0)
+    a = ap.parse_args(argv)
+    logging.basicConfig(level=logging.INFO, format="%(asctime)s [%(levelname)s] %(name)s: %(message)s")
+    stop = threading.Event()
+    signal.signal(signal.SIGTERM, lambda *_: stop.set())
+    signal.signal(signal.SIGINT, lambda *_: stop.set())
+    return run_member(a.front_router, a.model, a.role, a.replica, a.url, a.kv_addr, a.shard, a.group_size,
+                      a.poll_s, stop)
+
+
+if __name__ == "__main__":
+    raise SystemExit(main())
