@@ -42,6 +42,7 @@ class LlamaConfig:
     eps: float = 1e-5
     max_pos: int = 8192 + 512
     block_size: int = 16
+    rope_scaling: Optional[tuple] = None     # (factor, low_freq_factor, high_freq_factor, original_max_pos)
 
     @classmethod
     def llama3_8b(cls) -> "LlamaConfig":
@@ -254,7 +255,7 @@ class LlamaModel:
         cfg = self.cfg
         dev = weights.embed.device
         self.device = dev
-        self.cos_sin = ops.rope_cos_sin(cfg.max_pos, cfg.head_dim, cfg.rope_theta, dev)
+        self.cos_sin = ops.rope_cos_sin(cfg.max_pos, cfg.head_dim, cfg.rope_theta, dev, cfg.rope_scaling)
         self.status = ops.new_status(dev)
         self.max_tokens = max_tokens
         bf = dict(dtype=torch.bfloat16, device=dev)
@@ -339,7 +340,8 @@ def reference_forward(weights: LlamaWeights, seqs: Sequence[Sequence[int]]) -> L
     """fp32 PyTorch forward (no cache) returning last-position logits per sequence."""
     from connex_b200.ops import reference as R
     cfg = weights.cfg
-    cos_sin = ops.rope_cos_sin(cfg.max_pos, cfg.head_dim, cfg.rope_theta, weights.embed.device)
+    cos_sin = ops.rope_cos_sin(cfg.max_pos, cfg.head_dim, cfg.rope_theta, weights.embed.device,
+                               cfg.rope_scaling)
     outs = []
     for seq in seqs:
         ids = torch.tensor(seq, device=weights.embed.device)

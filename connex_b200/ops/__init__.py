@@ -132,9 +132,22 @@ def rope_cache(qkv: torch.Tensor, positions: torch.Tensor, cos_sin: torch.Tensor
     _n()
 
 
-def rope_cos_sin(max_pos: int, head_dim: int, theta: float, device) -> torch.Tensor:
-    """fp32 [max_pos, head_dim] table: cos in the first half, sin in the second."""
+def rope_cos_sin(max_pos: int, head_dim: int, theta: float, device, scaling=None) -> torch.Tensor:
+    """fp32 [max_pos, head_dim] table: cos in the first half, sin in the second.
+
+    ``scaling = (factor, low_freq_factor, high_freq_factor, original_max_pos)``
+    applies the Llama 3.1 long-context frequency rule: wavelengths shorter
+    than ``original_max_pos / high_freq_factor`` keep their frequency, those
+    longer than ``original_max_pos / low_freq_factor`` are divided by
+    ``factor``, and the band between blends the two linearly in
+    ``original_max_pos / wavelength``."""
     inv = 1.0 / (theta ** (torch.arange(0, head_dim, 2, dtype=torch.float64) / head_dim))
+    if scaling is not None:
+        factor, lo, hi, orig = (float(v) for v in scaling)
+        wavelen = 2 * math.pi / inv
+        smooth = ((orig / wavelen - lo) / (hi - lo)).clamp(0.0, 1.0)
+        blended = (1 - smooth) * inv / factor + smooth * inv
+        inv = torch.where(wavelen < orig / hi, inv, torch.where(wavelen > orig / lo, inv / factor, blended))
     ang = torch.arange(max_pos, dtype=torch.float64)[:, None] * inv[None, :]
     return torch.cat([ang.cos(), ang.sin()], dim=1).to(torch.float32).to(device)
 

@@ -121,10 +121,14 @@ class StageRuntime:
     """One stage's compute for the step protocol (``StageWorker`` compute + hooks)."""
 
     def __init__(self, cfg: LlamaConfig, l0: int, l1: int, device, num_blocks: int, max_tokens: int,
-                 max_batch: int = 256, max_ctx: int = 8192, seed: int = 0):
+                 max_batch: int = 256, max_ctx: int = 8192, seed: int = 0, weights: Optional[LlamaWeights] = None):
+        """``weights``: layers ``[l0, l1)`` already on ``device`` (e.g. from
+        :func:`connex_b200.models.hf.load_llama`); random from ``seed`` if absent."""
         self.cfg = cfg
         self.device = torch.device(device)
-        self.weights = stage_weights(cfg, l0, l1, self.device, seed)
+        if weights is not None and len(weights.layers) != l1 - l0:
+            raise ValueError(f"weights hold {len(weights.layers)} layers, the stage owns {l1 - l0}")
+        self.weights = weights if weights is not None else stage_weights(cfg, l0, l1, self.device, seed)
         stage_cfg = LlamaConfig(**{**cfg.__dict__, "layers": l1 - l0})
         self.cache = PagedKVCache(stage_cfg, num_blocks, self.device)
         self.model = StageModel(self.weights, l0, l1, self.cache, max_tokens, max_batch, self.device)
