@@ -1,0 +1,429 @@
+"""Continuous-batching generation over this framework's Llama runtime.
+
+:class:`GenerationEngine` owns one thread that drives a *stepper* (the
+model): each iteration admits waiting requests that fit (batch slots, KV
+blocks reserved for prompt + ``max_tokens``, a per-step prefill token
+budget), prefills them together, then decodes every running request by one
+token, and hands each new token to the request's callback.  A request ends
+at ``max_tokens``, at a stop id, or when it is cancelled (client gone); its
+KV blocks are released at once.
+
+Steppers:
+
+* :class:`ModelStepper` -- one GPU, all layers (:class:`StageRuntime` over
+  ``[0, L)``), weights random or from an HF checkpoint;
+* :class:`PipelineStepper` -- stage 0 of an elastic pipeline: its layers
+  locally, the rest through a :class:`connex.pp.link.Stage0Link`; rows whose
+  KV a failed-over downstream replica does not hold are prefilled again with
+  prompt + generated tokens, which yields the same next token;
+* :class:`RuleStepper` -- a deterministic CPU stand-in (next id = a function
+  of the last two ids), for tests of the scheduler and the HTTP layer.
+
+Reference behaviour served this way: the OpenAI API of a vLLM stage-0
+instance behind the proxy / PD router (``connex/serving/proxy.py``,
+``connex/adapters/vllm/pp``); the engine itself is this framework's own.
+"""
+from __future__ import annotations
+
+import collections
+import itertools
+import logging
+import threading
+import time
+from dataclasses import dataclass, field
+from typing import Callable, Dict, List, Optional, Sequence
+
+log = logging.getLogger("connex_b200.serve")
+
+
+class Stepper:
+    """The model behind a :class:`GenerationEngine`.
+
+    ``prefill(rids, seqs)`` computes every token of each sequence (KV written
+    for all of them) and returns the greedy next id per sequence;
+    ``decode(rids, seqs)`` appends the last id of each sequence (whose
+    earlier ids are already in the KV cache) and returns the next ids;
+    ``release(rids)`` frees their KV."""
+
+    max_batch: int = 64
+    max_ctx: int = 4096
+    max_step_tokens: int = 8192
+    num_blocks: int = 1 << 30
+    block_size: int = 16
+    vocab_size: int = 0
+
+    def prefill(self, rids: List[str], seqs: List[List[int]]) -> List[int]:
+        raise NotImplementedError
+
+    def decode(self, rids: List[str], seqs: List[List[int]]) -> List[int]:
+        raise NotImplementedError
+
+    def release(self, rids: List[str]) -> None:
+        pass
+
+    def close(self) -> None:
+        pass
+
+
+class RuleStepper(Stepper):
+    """Greedy stand-in on the CPU: ``next = (37 a + 11 b + 5) mod (V - 16) + 16``
+    of the last two ids -- the rule of ``connex.serving.fake_backend``, so a
+    continuation from ``prompt + partial output`` equals the uninterrupted one."""
+
+    def __init__(self, vocab_size: int = 1000, max_batch: int = 64, max_ctx: int = 4096, num_blocks: int = 1 << 20,
+                 step_delay_s: float = 0.0, fail_on: Optional[Callable[[str, List[str]], bool]] = None):
+        self.vocab_size, self.max_batch, self.max_ctx, self.num_blocks = vocab_size, max_batch, max_ctx, num_blocks
+        self.step_delay_s = step_delay_s
+        self.fail_on = fail_on
+        self.held: Dict[str, int] = {}
+        self.calls: List[tuple] = []
+
+    def _next(self, seq):
+        a = seq[-1] if seq else 0
+        b = seq[-2] if len(seq) > 1 else 0
+        return (a * 37 + b * 11 + 5) % (self.vocab_size - 16) + 16
+
+    def _step(self, kind, rids, seqs):
+        self.calls.append((kind, list(rids)))
+        if self.fail_on is not None and self.fail_on(kind, rids):
+            raise RuntimeError(f"injected {kind} failure")
+        if self.step_delay_s:
+            time.sleep(self.step_delay_s)
+        for r, s in zip(rids, seqs):
+            self.held[r] = len(s)
+        return [self._next(s) for s in seqs]
+
+    def prefill(self, rids, seqs):
+        return self._step("prefill", rids, seqs)
+
+    def decode(self, rids, seqs):
+        for r, s in zip(rids, seqs):
+            assert self.held.get(r) == len(s) - 1, f"{r}: KV holds {self.held.get(r)}, sequence {len(s)}"
+        return self._step("decode", rids, seqs)
+
+    def release(self, rids):
+        for r in rids:
+            self.held.pop(r, None)
+
+
+class _RuntimeSteps(Stepper):
+    """Step tensors for a :class:`connex_b200.runtime.pp.StageRuntime`."""
+
+    def _td(self, kind, rids, seqs):
+        import torch
+        from connex.pp.handover import CX_CTX, REQUEST_IDS
+        if kind == "prefill":
+            ids, ctx, n_new = [t for s in seqs for t in s], [0] * len(seqs), [len(s) for s in seqs]
+        else:
+            ids, ctx, n_new = [s[-1] for s in seqs], [len(s) - 1 for s in seqs], [1] * len(seqs)
+        t = torch.tensor(ids, dtype=torch.int32).pin_memory().to(self.rt.device, non_blocking=True)
+        return {"kind": kind, REQUEST_IDS: list(rids), CX_CTX: ctx, "n_new": n_new, "ids": t}, ctx, n_new
+
+    def release(self, rids):
+        self.rt.release(list(rids))
+
+
+def _make_runtime(cfg, l0, l1, device, num_blocks, max_batch, max_ctx, max_step_tokens, checkpoint, seed):
+    from connex_b200.runtime.pp import StageRuntime
+    weights = None
+    if checkpoint:
+        from connex_b200.models.hf import load_llama
+        weights = load_llama(checkpoint, device, layers=(l0, l1), cfg=cfg)
+    return StageRuntime(cfg, l0, l1, device, num_blocks=num_blocks, max_tokens=max_step_tokens, max_batch=max_batch,
+                        max_ctx=max_ctx, seed=seed, weights=weights)
+
+
+class ModelStepper(_RuntimeSteps):
+    """All layers on one GPU."""
+
+    def __init__(self, cfg, device, num_blocks: int, max_batch: int = 64, max_ctx: int = 4096,
+                 max_step_tokens: int = 8192, checkpoint: Optional[str] = None, seed: int = 0):
+        self.cfg = cfg
+        self.max_batch, self.max_ctx, self.max_step_tokens = max_batch, max_ctx, max_step_tokens
+        self.num_blocks, self.block_size, self.vocab_size = num_blocks, cfg.block_size, cfg.vocab_size
+        self.rt = _make_runtime(cfg, 0, cfg.layers, device, num_blocks, max_batch, max_ctx, max_step_tokens,
+                                checkpoint, seed)
+
+    def _run(self, kind, rids, seqs):
+        td, _, _ = self._td(kind, rids, seqs)
+        return self.rt.compute(td, [])["next"].tolist()
+
+    def prefill(self, rids, seqs):
+        return self._run("prefill", rids, seqs)
+
+    def decode(self, rids, seqs):
+        return self._run("decode", rids, seqs)
+
+
+class _Stage0Hooks:
+    def __init__(self):
+        self.reprefill_rids: List[str] = []
+
+    def kv_held(self, rid):
+        return 0
+
+    def release(self, rids):
+        pass
+
+    def reprefill(self, rids):
+        self.reprefill_rids = list(rids)
+
+    def abort(self, rids):
+        pass
+
+
+class PipelineStepper(_RuntimeSteps):
+    """Stage 0 of a pipeline: layers ``[0, l1)`` here, the rest downstream
+    through ``endpoint`` (a :class:`connex.pp.endpoint.PipelineEndpoint` with
+    membership attached).  Downstream stages serve the same step protocol
+    with :class:`connex_b200.runtime.pp.StageRuntime` (``python -m
+    connex_b200.serve.stage``)."""
+
+    def __init__(self, cfg, l1: int, device, endpoint, num_blocks: int, max_batch: int = 64, max_ctx: int = 4096,
+                 max_step_tokens: int = 8192, checkpoint: Optional[str] = None, seed: int = 0,
+                 recv_timeout_s: float = 30.0):
+        from connex.pp.link import Stage0Link
+        self.cfg = cfg
+        self.max_batch, self.max_ctx, self.max_step_tokens = max_batch, max_ctx, max_step_tokens
+        self.num_blocks, self.block_size, self.vocab_size = num_blocks, cfg.block_size, cfg.vocab_size
+        self.rt = _make_runtime(cfg, 0, l1, device, num_blocks, max_batch, max_ctx, max_step_tokens, checkpoint, seed)
+        self.ep = endpoint
+        self.hooks = _Stage0Hooks()
+        self.link = Stage0Link(endpoint, self.hooks, recv_timeout_s=recv_timeout_s)
+        self.reprefills = 0
+
+    def _run(self, kind, rids, seqs):
+        td, ctx, n_new = self._td(kind, rids, seqs)
+        x = self.rt.compute(td, [])["x"]
+        self.hooks.reprefill_rids = []
+        out = self.link.step({"x": x, "kind": kind, "n_new": n_new}, request_ids=list(rids), num_computed=ctx)
+        nxt = out["next"].tolist()
+        again = list(self.hooks.reprefill_rids)
+        if again:
+            # the new downstream replica holds no KV for these rows: prefill
+            # prompt + generated tokens through the whole pipeline; its last
+            # position is this step's token, so the result replaces it
+            self.reprefills += len(again)
+            idx = [list(rids).index(r) for r in again]
+            fixed = self._run("prefill", again, [seqs[i] for i in idx])
+            for j, i in enumerate(idx):
+                nxt[i] = fixed[j]
+        return nxt
+
+    def prefill(self, rids, seqs):
+        return self._run("prefill", rids, seqs)
+
+    def decode(self, rids, seqs):
+        return self._run("decode", rids, seqs)
+
+    def release(self, rids):
+        self.rt.release(list(rids))
+        self.link.finished(list(rids))          # downstream stages free them on the next steps
+
+    def close(self):
+        self.ep.close()
+
+
+@dataclass
+class Request:
+    rid: str
+    prompt: List[int]
+    max_tokens: int
+    on_token: Callable[["Request", Optional[int], Optional[str]], None]
+    stop_ids: frozenset = frozenset()
+    gen: List[int] = field(default_factory=list)
+    blocks: int = 0
+    cancelled: bool = False
+    finish_reason: Optional[str] = None
+    error: Optional[str] = None
+    t_submit: float = field(default_factory=time.monotonic)
+    t_first: Optional[float] = None
+
+
+class EngineFull(Exception):
+    """The request can never fit (context or KV capacity)."""
+
+
+class GenerationEngine:
+    """Scheduler thread over a :class:`Stepper` (see the module docstring).
+
+    ``on_token(req, token, finish_reason)`` is called from the engine thread
+    once per generated token (``finish_reason`` set on the last one), or
+    with ``token=None`` and a reason (``"error"`` / ``"abort"``) when the
+    request ends without one."""
+
+    def __init__(self, stepper: Stepper, max_batch: Optional[int] = None, max_step_tokens: Optional[int] = None,
+                 idle_wait_s: float = 0.05):
+        self.s = stepper
+        self.max_batch = max_batch or stepper.max_batch
+        self.max_step_tokens = max_step_tokens or stepper.max_step_tokens
+        self.idle_wait_s = idle_wait_s
+        self.waiting: "collections.deque[Request]" = collections.deque()
+        self.running: Dict[str, Request] = {}
+        self.blocks_reserved = 0
+        self._cv = threading.Condition()
+        self._stop = threading.Event()
+        self._ids = itertools.count()
+        self.stats = collections.Counter()
+        self.error: Optional[str] = None
+        self._thread: Optional[threading.Thread] = None
+
+    # ------------------------------------------------------------ client side
+    def blocks_for(self, n_tokens: int) -> int:
+        return -(-n_tokens // self.s.block_size)
+
+    def submit(self, prompt: Sequence[int], max_tokens: int, on_token, stop_ids=(), rid: Optional[str] = None
+               ) -> Request:
+        prompt = [int(t) for t in prompt]
+        if not prompt:
+            raise ValueError("empty prompt")
+        if max_tokens <= 0:
+            raise ValueError("max_tokens must be positive")
+        if len(prompt) + max_tokens > self.s.max_ctx:
+            raise EngineFull(f"prompt ({len(prompt)}) + max_tokens ({max_tokens}) exceeds the context "
+                             f"({self.s.max_ctx})")
+        if len(prompt) > self.max_step_tokens:
+            raise EngineFull(f"prompt ({len(prompt)}) exceeds the prefill budget ({self.max_step_tokens})")
+        if self.s.vocab_size and any(not 0 <= t < self.s.vocab_size for t in prompt):
+            raise ValueError(f"token ids must lie in [0, {self.s.vocab_size})")
+        blocks = self.blocks_for(len(prompt) + max_tokens)
+        if blocks > self.s.num_blocks:
+            raise EngineFull(f"request needs {blocks} KV blocks, the cache has {self.s.num_blocks}")
+        req = Request(rid or f"r{next(self._ids)}", prompt, int(max_tokens), on_token, frozenset(stop_ids or ()),
+                      blocks=blocks)
+        with self._cv:
+            self.waiting.append(req)
+            self.stats["submitted"] += 1
+            self._cv.notify()
+        return req
+
+    def cancel(self, req: Request) -> None:
+        req.cancelled = True
+        with self._cv:
+            self._cv.notify()
+
+    def start(self) -> "GenerationEngine":
+        self._thread = threading.Thread(target=self._loop, name="cx-serve-engine", daemon=True)
+        self._thread.start()
+        return self
+
+    def stop(self, timeout: float = 10.0) -> None:
+        self._stop.set()
+        with self._cv:
+            self._cv.notify()
+        if self._thread is not None:
+            self._thread.join(timeout)
+
+    @property
+    def alive(self) -> bool:
+        return self._thread is not None and self._thread.is_alive() and self.error is None
+
+    def load(self) -> dict:
+        with self._cv:
+            return {"waiting": len(self.waiting), "running": len(self.running),
+                    "kv_blocks_reserved": self.blocks_reserved, "kv_blocks": self.s.num_blocks}
+
+    # ------------------------------------------------------------ engine thread
+    def _finish(self, reqs: List[Request], reason: str, token_sent: bool = True) -> None:
+        rel = [r.rid for r in reqs if r.rid in self.running]
+        for r in reqs:
+            if self.running.pop(r.rid, None) is not None:
+                self.blocks_reserved -= r.blocks
+            r.finish_reason = reason
+            self.stats["finished_" + reason] += 1
+            if not token_sent:
+                try:
+                    r.on_token(r, None, reason)
+                except Exception:  # noqa: BLE001 - a broken callback must not stop the engine
+                    log.exception("callback of %s", r.rid)
+        if rel:
+            self.s.release(rel)
+
+    def _admit(self) -> List[Request]:
+        new, tokens = [], 0
+        with self._cv:
+            while self.waiting:
+                r = self.waiting[0]
+                if r.cancelled:
+                    self.waiting.popleft()
+                    r.finish_reason = "abort"
+                    self.stats["finished_abort"] += 1
+                    continue
+                if len(self.running) + len(new) >= self.max_batch:
+                    break
+                if new and tokens + len(r.prompt) > self.max_step_tokens:
+                    break
+                if self.blocks_reserved + r.blocks > self.s.num_blocks:
+                    break
+                self.waiting.popleft()
+                self.blocks_reserved += r.blocks
+                tokens += len(r.prompt)
+                new.append(r)
+        return new
+
+    def _emit(self, reqs: List[Request], toks: List[int]) -> None:
+        done = collections.defaultdict(list)
+        now = time.monotonic()
+        for r, t in zip(reqs, toks):
+            r.gen.append(int(t))
+            if r.t_first is None:
+                r.t_first = now
+            reason = None
+            if int(t) in r.stop_ids:
+                reason = "stop"
+            elif len(r.gen) >= r.max_tokens:
+                reason = "length"
+            self.stats["tokens"] += 1
+            try:
+                r.on_token(r, int(t), reason)
+            except Exception:  # noqa: BLE001
+                log.exception("callback of %s", r.rid)
+                reason = reason or "abort"
+            if reason:
+                done[reason].append(r)
+        for reason, rs in done.items():
+            self._finish(rs, reason)
+
+    def _step(self, kind: str, reqs: List[Request]) -> None:
+        rids = [r.rid for r in reqs]
+        seqs = [r.prompt + r.gen for r in reqs]
+        try:
+            toks = (self.s.prefill if kind == "prefill" else self.s.decode)(rids, seqs)
+        except Exception as e:  # noqa: BLE001 - fail the step's requests, keep serving
+            log.exception("%s step of %d requests failed", kind, len(reqs))
+            self.stats["step_errors"] += 1
+            for r in reqs:
+                r.error = f"{type(e).__name__}: {e}"
+            self._finish(reqs, "error", token_sent=False)
+            return
+        self.stats[kind + "_steps"] += 1
+        self._emit(reqs, toks)
+
+    def _loop(self) -> None:
+        try:
+            while not self._stop.is_set():
+                gone = [r for r in self.running.values() if r.cancelled]
+                if gone:
+                    self._finish(gone, "abort", token_sent=False)
+                new = self._admit()
+                if not new and not self.running:
+                    with self._cv:
+                        if not self.waiting and not self._stop.is_set():
+                            self._cv.wait(self.idle_wait_s)
+                    continue
+                decoding = list(self.running.values())
+                if new:
+                    for r in new:
+                        self.running[r.rid] = r
+                    self._step("prefill", new)
+                decoding = [r for r in decoding if r.rid in self.running]
+                if decoding:
+                    self._step("decode", decoding)
+        except Exception as e:  # noqa: BLE001
+            log.exception("engine loop died")
+            self.error = f"{type(e).__name__}: {e}"
+        finally:
+            with self._cv:
+                left = list(self.running.values()) + list(self.waiting)
+                self.waiting.clear()
+            self._finish(left, "abort", token_sent=False)

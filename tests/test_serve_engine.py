@@ -1,0 +1,180 @@
+"""The serving engine and its OpenAI front on CPU (deterministic stand-in
+model): continuous batching admits new requests between decode steps and
+keeps every request's KV consistent, KV reservations bound admission and are
+returned on finish / cancel / error, a failed step fails only its requests,
+the HTTP routes answer like the engine API the proxy drives, and the retry /
+resume proxy in front of two engines turns a failed stream into the
+uninterrupted output."""
+import asyncio
+import threading
+import time
+
+import aiohttp
+import pytest
+
+from connex.serving.fake_backend import reference
+from connex_b200.serve.api import Server, WordCodec
+from connex_b200.serve.engine import EngineFull, GenerationEngine, RuleStepper
+from connex_b200.serve.pipeline import split_layers
+from tests.test_serving import _proxy, _run, _serve, _stream, _text
+
+
+def _collect(engine, prompt, n, **kw):
+    done = threading.Event()
+    out = {"toks": [], "reason": None}
+
+    def cb(r, tok, reason):
+        if tok is not None:
+            out["toks"].append(tok)
+        if reason:
+            out["reason"] = reason
+            done.set()
+    out["req"] = engine.submit(prompt, n, cb, **kw)
+    out["done"] = done
+    return out
+
+
+def test_batching_matches_the_uninterrupted_rule_and_admits_between_steps():
+    st = RuleStepper(step_delay_s=0.002)
+    eng = GenerationEngine(st).start()
+    try:
+        a = _collect(eng, [1, 5, 6], 20)
+        time.sleep(0.01)
+        b = _collect(eng, [1, 7], 8)                    # joins while a is decoding
+        for x in (a, b):
+            assert x["done"].wait(5)
+        assert a["toks"] == reference([1, 5, 6], 20)[0] and a["reason"] == "length"
+        assert b["toks"] == reference([1, 7], 8)[0]
+        kinds = [k for k, _ in st.calls]
+        assert kinds.count("prefill") == 2
+        mixed = [rids for k, rids in st.calls if k == "decode" and len(rids) == 2]
+        assert mixed                                    # a and b decoded in the same step
+        assert not st.held and eng.blocks_reserved == 0
+    finally:
+        eng.stop()
+
+
+def test_stop_ids_cancel_and_kv_reservations():
+    st = RuleStepper(num_blocks=4, step_delay_s=0.002)        # 4 blocks of 16 tokens
+    eng = GenerationEngine(st).start()
+    try:
+        stop_at = reference([1, 5], 6)[0][2]
+        s = _collect(eng, [1, 5], 6, stop_ids=[stop_at])
+        assert s["done"].wait(5) and s["reason"] == "stop" and s["toks"][-1] == stop_at and len(s["toks"]) == 3
+        big = _collect(eng, [1] * 10, 40)                     # 50 tokens: 4 blocks, the whole cache
+        time.sleep(0.02)
+        small = _collect(eng, [1, 2], 3)                      # waits for the blocks
+        time.sleep(0.05)
+        assert small["toks"] == [] and eng.load()["waiting"] == 1
+        eng.cancel(big["req"])
+        assert big["done"].wait(5) and big["reason"] == "abort"
+        assert small["done"].wait(5) and small["toks"] == reference([1, 2], 3)[0]
+        with pytest.raises(EngineFull):
+            eng.submit([1] * 10, 60, lambda *a: None)         # 70 tokens > 4 blocks
+        with pytest.raises(EngineFull):
+            eng.submit([1] * 4000, 200, lambda *a: None)      # beyond the context
+        with pytest.raises(ValueError):
+            eng.submit([1, 5000], 2, lambda *a: None)         # outside the vocabulary
+        time.sleep(0.02)
+        assert eng.blocks_reserved == 0 and not st.held
+    finally:
+        eng.stop()
+
+
+def test_a_failed_step_fails_only_its_requests():
+    boom = {"on": False}
+    st = RuleStepper(step_delay_s=0.002, fail_on=lambda kind, rids: boom["on"] and kind == "decode")
+    eng = GenerationEngine(st).start()
+    try:
+        a = _collect(eng, [1, 3], 50)
+        time.sleep(0.02)
+        boom["on"] = True
+        assert a["done"].wait(5) and a["reason"] == "error" and a["req"].error.startswith("RuntimeError")
+        boom["on"] = False
+        b = _collect(eng, [1, 4], 5)
+        assert b["done"].wait(5) and b["toks"] == reference([1, 4], 5)[0]
+        assert eng.alive and eng.stats["step_errors"] == 1 and not st.held
+    finally:
+        eng.stop()
+
+
+def test_http_routes():
+    async def main():
+        eng = GenerationEngine(RuleStepper(step_delay_s=0.001)).start()
+        srv = Server(eng, "m")
+        runner, url = await _serve(srv.app())
+        try:
+            async with aiohttp.ClientSession() as s:
+                assert (await (await s.get(url + "/health")).json())["status"] == "ok"
+                assert (await (await s.get(url + "/v1/models")).json())["data"][0]["id"] == "m"
+                r = await (await s.post(url + "/v1/completions", json={"prompt": "t5 t6", "max_tokens": 4,
+                                                                       "return_token_ids": True})).json()
+                ids, text = reference("t5 t6", 4)
+                assert r["choices"][0]["text"] == text and r["choices"][0]["token_ids"] == ids
+                assert r["usage"] == {"prompt_tokens": 3, "completion_tokens": 4, "total_tokens": 7}
+                tok = await (await s.post(url + "/tokenize", json={"prompt": "t5 t6"})).json()
+                assert tok["tokens"] == [1, 5, 6]
+                det = await (await s.post(url + "/detokenize", json={"tokens": [5, 6]})).json()
+                assert det["prompt"] == " t5 t6"
+                bad = await s.post(url + "/v1/completions", json={"prompt": "t1", "max_tokens": 5000})
+                assert bad.status == 400
+                bad = await s.post(url + "/v1/completions", json={"prompt": "t1", "n": 2})
+                assert bad.status == 400
+                load = await (await s.get(url + "/load")).json()
+                assert load["running"] == 0 and load["tokens"] == 4
+            chunks, done = await _stream(url, "/v1/completions",
+                                         {"prompt": [1, 9, 9], "max_tokens": 5, "return_token_ids": True,
+                                          "logprobs": 0, "return_tokens_as_token_ids": True,
+                                          "stream_options": {"include_usage": True, "continuous_usage_stats": True}})
+            assert done and _text(chunks) == reference([1, 9, 9], 5)[1]
+            toks = [c["choices"][0]["token_ids"][0] for c in chunks if c["choices"]]
+            assert toks == reference([1, 9, 9], 5)[0]
+            lp = chunks[0]["choices"][0]["logprobs"]
+            assert lp["tokens"] == [f"token_id:{toks[0]}"] and lp["token_logprobs"] == [None]
+            assert chunks[-1]["usage"]["completion_tokens"] == 5 and chunks[-1]["choices"] == []
+            assert chunks[-2]["choices"][0]["finish_reason"] == "length"
+            msgs = [{"role": "user", "content": "t7 t8"}]
+            chunks, done = await _stream(url, "/v1/chat/completions", {"messages": msgs, "max_tokens": 3})
+            ids = WordCodec(1000).chat(msgs)
+            assert done and _text(chunks, chat=True) == reference(ids, 3)[1]
+        finally:
+            await runner.cleanup()
+            eng.stop()
+    _run(main())
+
+
+def test_resume_proxy_turns_a_failed_engine_stream_into_the_full_output():
+    async def main():
+        trip = {"n": 0}
+
+        def fail_once(kind, rids):              # engine A fails its 4th decode step, once
+            if kind == "decode":
+                trip["n"] += 1
+                return trip["n"] == 4
+            return False
+        ea = GenerationEngine(RuleStepper(step_delay_s=0.002, fail_on=fail_once)).start()
+        eb = GenerationEngine(RuleStepper(step_delay_s=0.002)).start()
+        ra, ua = await _serve(Server(ea, "m").app())
+        rb, ub = await _serve(Server(eb, "m").app())
+        p = _proxy([ua, ub])
+        pr, url = await _serve(p.app())
+        try:
+            for _ in range(2):                  # whichever replica the proxy picks first
+                chunks, done = await _stream(url, "/v1/completions", {"model": "m", "prompt": "t3 t4",
+                                                                      "max_tokens": 12})
+                assert done and _text(chunks) == reference("t3 t4", 12)[1]
+            assert trip["n"] >= 4 and p.stats["resumes"] >= 1
+        finally:
+            for r in (pr, ra, rb):
+                await r.cleanup()
+            ea.stop()
+            eb.stop()
+    _run(main())
+
+
+def test_split_layers():
+    assert split_layers(32, 2) == [(0, 16), (16, 32)]
+    assert split_layers(32, 3, "10,20") == [(0, 10), (10, 20), (20, 32)]
+    for bad in ((32, 2, "40"), (32, 3, "20,10"), (32, 2, "4,8")):
+        with pytest.raises(ValueError):
+            split_layers(*bad)
