@@ -6,6 +6,9 @@
         --node gpu-node-1 --model-pvc models > pd.json
     python -m connex.deploy.k8s ep --gpus 8 --model Qwen/Qwen3-30B-A3B --node gpu-node-1 > ep.json
     python -m connex.deploy.k8s proxy --endpoints http://a:8000,http://b:8000 > proxy.json
+    python -m connex.deploy.k8s serve --replicas 4 --model Meta-Llama-3-8B --model-pvc models > serve.json
+    python -m connex.deploy.k8s pipeline --num-stages 2 --stage-replicas 2 --model Meta-Llama-3-8B \
+        --model-pvc models --node gpu-node-1 > pipeline.json
     kubectl apply -f router.json -f pd.json
 
 Output is a ``v1/List`` in JSON (``--yaml`` for YAML).  Options come from the
@@ -46,9 +49,17 @@ DEFAULTS = {
     "serve_port": 8100,
     "proxy_port": 5199,
     "ctrl_port": 17100,
+    "replicas": 1,
+    "num_stages": 2,
+    "stage_replicas": 1,
+    "stage_starts": "",
+    "directory_port": 15500,
+    "store_port": 29600,
+    "max_ctx": 4096,
+    "max_batch": 64,
     "endpoints": "",
 }
-KINDS = ("router", "directory", "pd", "ep", "proxy")
+KINDS = ("router", "directory", "pd", "ep", "proxy", "serve", "pipeline")
 
 
 POD_IP = object()     # env value: the pod's own IP from the downward API
@@ -116,8 +127,10 @@ def router(c) -> List[dict]:
 
 def directory(c) -> List[dict]:
     name = f"{c['prefix']}-directory"
-    return [_deployment(c, name, ["connex-directory", "--bind", "0.0.0.0:15500"], {}, {"dir": 15500}),
-            _service(c, name, {"dir": 15500})]
+    port = c["directory_port"]
+    ports = {"dir": port, "events": port + 1}
+    cmd = ["connex-directory", "--bind", f"0.0.0.0:{port}", "--event-bind", f"0.0.0.0:{port + 1}"]
+    return [_deployment(c, name, cmd, {}, ports), _service(c, name, ports)]
 
 
 def pd(c) -> List[dict]:
@@ -171,6 +184,58 @@ def proxy(c) -> List[dict]:
     return [_deployment(c, name, cmd, {}, {"http": c["proxy_port"]}), _service(c, name, {"http": c["proxy_port"]})]
 
 
+def _engine_args(c) -> List[str]:
+    return ["--checkpoint", _model_arg(c), "--model-name", c["model"], "--max-ctx", str(c["max_ctx"]),
+            "--max-batch", str(c["max_batch"]), "--device", "cuda:0"]
+
+
+def _ready(container: dict, port: int) -> None:
+    container["readinessProbe"] = {"httpGet": {"path": "/health", "port": port}, "periodSeconds": 5,
+                                   "failureThreshold": 3}
+
+
+def serve(c) -> List[dict]:
+    """``--replicas`` one-GPU servers of this framework's own engine
+    (``python -m connex_b200.serve``), each behind its Service; put the
+    ``proxy`` kind in front of them for retries and stream resume."""
+    items: List[dict] = []
+    for r in range(int(c["replicas"])):
+        name = f"{c['prefix']}-serve-{r}"
+        cmd = ["python", "-m", "connex_b200.serve", "--port", str(c["serve_port"])] + _engine_args(c)
+        d = _deployment(c, name, cmd, {}, {"http": c["serve_port"]}, gpus=1)
+        _ready(d["spec"]["template"]["spec"]["containers"][0], c["serve_port"])
+        items += [d, _service(c, name, {"http": c["serve_port"]})]
+    return items
+
+
+def pipeline(c) -> List[dict]:
+    """An elastic serving pipeline of this framework's engine: a directory,
+    stage 0 (OpenAI API; hosts the pair-link rendezvous store) and
+    ``--stage-replicas`` replicas of every later stage, one GPU each.  Stage
+    endpoints register their pod address in the directory; stage 0 fails
+    over to another replica of stage 1.. when one dies."""
+    items = directory(c)
+    ns = c["namespace"]
+    dir_addr = f"{c['prefix']}-directory.{ns}.svc.cluster.local:{c['directory_port']}"
+    s0 = f"{c['prefix']}-s0-r0"
+    store = f"{s0}.{ns}.svc.cluster.local:{c['store_port']}"
+    common = _engine_args(c) + ["--num-stages", str(c["num_stages"]), "--directory", dir_addr, "--store", store]
+    if c["stage_starts"]:
+        common += ["--stage-starts", c["stage_starts"]]
+    env = {"CONNEX_HOST_IP": POD_IP}
+    cmd = ["python", "-m", "connex_b200.serve", "--port", str(c["serve_port"]), "--store-master"] + common
+    ports = {"http": c["serve_port"], "store": c["store_port"]}
+    d = _deployment(c, s0, cmd, env, ports, gpus=1)
+    _ready(d["spec"]["template"]["spec"]["containers"][0], c["serve_port"])
+    items += [d, _service(c, s0, ports)]
+    for k in range(1, int(c["num_stages"])):
+        for r in range(int(c["stage_replicas"])):
+            name = f"{c['prefix']}-s{k}-r{r}"
+            cmd = ["python", "-m", "connex_b200.serve.stage", "--stage", str(k), "--replica", str(r)] + common
+            items.append(_deployment(c, name, cmd, env, {}, gpus=1))
+    return items
+
+
 def _options(argv: Optional[List[str]]) -> dict:
     pre = argparse.ArgumentParser(add_help=False)
     pre.add_argument("--config")
@@ -195,7 +260,8 @@ def _options(argv: Optional[List[str]]) -> dict:
 
 def generate(argv: Optional[List[str]] = None) -> dict:
     c = _options(argv)
-    items = {"router": router, "directory": directory, "pd": pd, "ep": ep, "proxy": proxy}[c["what"]](c)
+    items = {"router": router, "directory": directory, "pd": pd, "ep": ep, "proxy": proxy, "serve": serve,
+             "pipeline": pipeline}[c["what"]](c)
     return {"apiVersion": "v1", "kind": "List", "items": items}
 
 

@@ -9,7 +9,7 @@ Stage 0 of a two-stage pipeline (downstream replicas run
 ``python -m connex_b200.serve.stage``; both register with a directory)::
 
     connex-directory --bind 0.0.0.0:15500 &
-    python -m connex_b200.serve --checkpoint CK --num-stages 2 --directory tcp://127.0.0.1:15500 \\
+    python -m connex_b200.serve --checkpoint CK --num-stages 2 --directory 127.0.0.1:15500 \\
         --store 127.0.0.1:29600 --store-master --port 8100
 
 Without ``--checkpoint`` the weights are random with the geometry of
@@ -43,7 +43,7 @@ def model_args(ap: argparse.ArgumentParser) -> None:
     ap.add_argument("--model-name", default=None)
     ap.add_argument("--num-stages", type=int, default=1)
     ap.add_argument("--stage-starts", default=None, help="first layer of stages 1.. (even split by default)")
-    ap.add_argument("--directory", default=None, help="tcp://host:port of the directory / front router")
+    ap.add_argument("--directory", default=None, help="HOST:PORT of the directory (connex-directory --bind)")
     ap.add_argument("--data", default="link", choices=["link", "inline"])
     ap.add_argument("--store", default=None, help="HOST:PORT of the pair-link rendezvous store")
     ap.add_argument("--store-master", action="store_true", help="host the rendezvous store in this process")

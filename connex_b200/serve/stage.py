@@ -6,7 +6,7 @@ R``) for failover: stage 0 moves to another one when this one dies and
 re-prefills the rows whose KV it lacks.
 
     python -m connex_b200.serve.stage --checkpoint CK --num-stages 2 --stage 1 --replica 0 \\
-        --directory tcp://127.0.0.1:15500 --store 127.0.0.1:29600
+        --directory 127.0.0.1:15500 --store 127.0.0.1:29600
 """
 from __future__ import annotations
 

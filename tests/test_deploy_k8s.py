@@ -119,3 +119,36 @@ def test_sidecar_registers_while_healthy(monkeypatch):
     kinds = [e[0] for e in events]
     assert kinds == ["start", "stop", "start", "stop"]        # up, down, up again, deregistered at exit
     assert events[0] == ("start", "tcp://fr:1", "m", "prefill", 2, "http://p:8100")
+
+
+def test_serve_and_pipeline_kinds_run_the_native_engine():
+    items = _items("serve", "--model", "llama", "--replicas", "2", "--model-pvc", "models")
+    assert [i["metadata"]["name"] for i in items if i["kind"] == "Deployment"] == ["cx-serve-0", "cx-serve-1"]
+    c = _pod(items, "cx-serve-1")["containers"][0]
+    assert c["command"][:3] == ["python", "-m", "connex_b200.serve"] and "/models/llama" in c["command"]
+    assert c["readinessProbe"]["httpGet"]["path"] == "/health"
+    items = _items("pipeline", "--model", "llama", "--num-stages", "3", "--stage-replicas", "2",
+                   "--stage-starts", "10,20", "--namespace", "pp")
+    deps = [i["metadata"]["name"] for i in items if i["kind"] == "Deployment"]
+    assert deps == ["cx-directory", "cx-s0-r0", "cx-s1-r0", "cx-s1-r1", "cx-s2-r0", "cx-s2-r1"]
+    s0 = _pod(items, "cx-s0-r0")["containers"][0]["command"]
+    assert "--store-master" in s0 and s0[s0.index("--num-stages") + 1] == "3"
+    assert s0[s0.index("--directory") + 1] == "cx-directory.pp.svc.cluster.local:15500"
+    s2 = _pod(items, "cx-s2-r1")["containers"][0]["command"]
+    assert s2[:3] == ["python", "-m", "connex_b200.serve.stage"]
+    assert s2[s2.index("--stage") + 1] == "2" and s2[s2.index("--replica") + 1] == "1"
+    assert s2[s2.index("--store") + 1] == "cx-s0-r0.pp.svc.cluster.local:29600"
+    assert s2[s2.index("--stage-starts") + 1] == "10,20"
+    d = _pod(items, "cx-directory")["containers"][0]["command"]
+    assert d == ["connex-directory", "--bind", "0.0.0.0:15500", "--event-bind", "0.0.0.0:15501"]
+    # every flag the manifests pass is one the CLIs accept
+    import argparse
+    from connex_b200.serve.__main__ import model_args
+    ap = argparse.ArgumentParser()
+    model_args(ap)
+    ap.add_argument("--port")
+    ap.add_argument("--stage")
+    a = ap.parse_args(s0[3:])
+    assert a.store_master and a.num_stages == 3
+    a = ap.parse_args(s2[3:])
+    assert a.replica == 1 and a.stage == "2"
