@@ -114,10 +114,52 @@ def case_ep_gemm(dev, T: int = 4096):
     return (lambda: fused.forward(x, idx, w, out)), {"flops": flops}
 
 
+def case_gemm_m(dev, M=1, N=28672, K=4096, silu=False):
+    """A decode-shaped GEMM: M rows against an N x K weight (weight-read bound)."""
+    a = torch.randn(M, K, device=dev).bfloat16()
+    b = torch.randn(N, K, device=dev).bfloat16()
+    out = torch.empty(M, N // 2 if silu else N, dtype=torch.bfloat16, device=dev)
+    return (lambda: ops.gemm(a, b, out, silu_mul=silu)), {"bytes": N * K * 2 + M * K * 2 + M * N * 2}
+
+
+def case_decode_step(dev, B=1, ctx=1024, graphs=True):
+    """One Llama-3-8B decode step for B sequences of ``ctx`` cached tokens,
+    replayed from its CUDA graph (device time of the whole step; bytes =
+    weights + the KV read)."""
+    from connex.pp.handover import CX_CTX, REQUEST_IDS
+    from connex_b200.models.llama import LlamaConfig
+    from connex_b200.runtime.pp import StageRuntime
+    cfg = LlamaConfig.llama3_8b()
+    rt = StageRuntime(cfg, 0, cfg.layers, dev, num_blocks=B * (ctx + 64) // 16 + 64, max_tokens=max(B * ctx, 8192),
+                      max_batch=B, max_ctx=ctx + 64)
+    if graphs:
+        rt.enable_decode_graphs()
+    rids = [f"r{i}" for i in range(B)]
+    ids = torch.randint(16, cfg.vocab_size, (B * ctx,), dtype=torch.int32, device=dev)
+    nxt = rt.compute({"kind": "prefill", REQUEST_IDS: rids, CX_CTX: [0] * B, "n_new": [ctx] * B, "ids": ids},
+                     [])["next"]
+    step = {"kind": "decode", REQUEST_IDS: rids, CX_CTX: [ctx] * B, "n_new": [1] * B, "ids": nxt}
+    rt.compute(step, [])
+    if graphs:
+        fn = rt.graphs[next(b for b in rt.g_buckets if b >= B)][0].replay
+    else:
+        fn = lambda: rt.compute(step, [])          # noqa: E731 - the same step again, launched eagerly
+    weights = sum(t.numel() * 2 for lw in rt.weights.layers for t in (lw.wqkv, lw.wo, lw.w13, lw.w2)) \
+        + rt.weights.lm_head.numel() * 2
+    kv = B * (ctx + 1) * cfg.kv_bytes_per_token
+    return fn, {"bytes": weights + kv}
+
+
 CASES = {"gemm": lambda d: case_gemm(d), "gemm_qkv": lambda d: case_gemm(d, 8192, 6144, 4096),
          "gemm_silu": lambda d: case_gemm(d, 8192, 28672, 4096, silu=True), "attn": case_attn,
          "decode_attn": case_decode_attn, "kv_push": case_kv_push, "wsync": case_wsync, "ep_gemm": case_ep_gemm,
-         "ep_t128": lambda d: case_ep_gemm(d, 128)}
+         "ep_t128": lambda d: case_ep_gemm(d, 128),
+         "gemm_m1_qkv": lambda d: case_gemm_m(d, 1, 6144, 4096), "gemm_m1_o": lambda d: case_gemm_m(d, 1, 4096, 4096),
+         "gemm_m1_gateup": lambda d: case_gemm_m(d, 1, 28672, 4096, silu=True),
+         "gemm_m1_down": lambda d: case_gemm_m(d, 1, 4096, 14336),
+         "gemm_m32_gateup": lambda d: case_gemm_m(d, 32, 28672, 4096, silu=True),
+         "decode_step_b1": lambda d: case_decode_step(d, 1), "decode_step_b32": lambda d: case_decode_step(d, 32),
+         "decode_step_b1_eager": lambda d: case_decode_step(d, 1, graphs=False)}
 
 
 def main() -> None:

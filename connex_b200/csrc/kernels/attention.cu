@@ -5,7 +5,10 @@
 // over the context (512 tokens per CTA), one CTA per (sequence, kv head,
 // split) computing all q heads of the GQA group, then a log-sum-exp merge of
 // the splits.  (Prefill attention runs on tcgen05: attention_tc.cu.)
+#include <algorithm>
+
 #include "common.cuh"
+#include "gemm.h"
 #include "layers.h"
 
 namespace cx {
@@ -20,18 +23,31 @@ constexpr int MAXG = 8;
 
 int decode_attention_splits(int max_ctx) { return (max_ctx + dec::SPLIT - 1) / dec::SPLIT; }
 
+int decode_attention_plan(int B, int Hq, int Hkv, int max_ctx, long ws_floats) {
+  int n = decode_attention_splits(max_ctx);
+  if (ws_floats < 0 || B <= 0) return n;
+  const long want = 2L * num_sms();
+  if ((long)B * Hkv * n < want) {
+    long n2 = (want + (long)B * Hkv - 1) / ((long)B * Hkv);
+    n2 = std::min<long>(n2, (max_ctx + 63) / 64);
+    n2 = std::min<long>(n2, ws_floats / ((long)B * Hq * (dec::D + 2)));
+    if (n2 > n) n = (int)n2;
+  }
+  return n;
+}
+
 template <int G>
 __global__ void __launch_bounds__(dec::THREADS)
     decode_attn_kernel(const __nv_bfloat16* __restrict__ q, int ldq, const __nv_bfloat16* __restrict__ kc,
                        const __nv_bfloat16* __restrict__ vc, const int* __restrict__ block_tables, int max_blocks,
                        const int* __restrict__ ctx_lens, __nv_bfloat16* __restrict__ out, int ldo, int Hq, int Hkv,
-                       int BS, float scale_log2, float* __restrict__ ws, int n_splits) {
+                       int BS, float scale_log2, float* __restrict__ ws, int n_splits, int split_len) {
   using namespace dec;
   const int b = blockIdx.x, g = blockIdx.y, sp = blockIdx.z;
   const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
   const int ctx = ctx_lens[b];
-  const int t0 = sp * SPLIT;
-  const int t1 = min(ctx, t0 + SPLIT);
+  const int t0 = sp * split_len;
+  const int t1 = min(ctx, t0 + split_len);  // split_len <= SPLIT: fits lg[][]
   const int n = t1 - t0;
   __shared__ float qs[G][D];
   __shared__ float lg[G][SPLIT];
@@ -199,10 +215,11 @@ __global__ void decode_merge_kernel(const float* __restrict__ ws, __nv_bfloat16*
 
 void decode_attention(const void* q, int ldq, const void* kc, const void* vc, const int* block_tables,
                       int max_blocks, const int* ctx_lens, void* out, int ldo, int B, int Hq, int Hkv, int BS,
-                      int max_ctx, float scale, float* workspace, cudaStream_t s) {
+                      int max_ctx, float scale, float* workspace, cudaStream_t s, long ws_floats) {
   if (B == 0) return;
   const int G = Hq / Hkv;
-  const int n_splits = decode_attention_splits(max_ctx);
+  const int n_splits = decode_attention_plan(B, Hq, Hkv, max_ctx, ws_floats);
+  const int split_len = (max_ctx + n_splits - 1) / n_splits;
   dim3 grid(B, Hkv, n_splits);
   auto Q = reinterpret_cast<const __nv_bfloat16*>(q);
   auto K = reinterpret_cast<const __nv_bfloat16*>(kc);
@@ -211,16 +228,16 @@ void decode_attention(const void* q, int ldq, const void* kc, const void* vc, co
   const float sl = scale * 1.4426950408889634f;
   if (G == 4)
     decode_attn_kernel<4><<<grid, dec::THREADS, 0, s>>>(Q, ldq, K, V, block_tables, max_blocks, ctx_lens, O, ldo,
-                                                         Hq, Hkv, BS, sl, workspace, n_splits);
+                                                         Hq, Hkv, BS, sl, workspace, n_splits, split_len);
   else if (G == 8)
     decode_attn_kernel<8><<<grid, dec::THREADS, 0, s>>>(Q, ldq, K, V, block_tables, max_blocks, ctx_lens, O, ldo,
-                                                         Hq, Hkv, BS, sl, workspace, n_splits);
+                                                         Hq, Hkv, BS, sl, workspace, n_splits, split_len);
   else if (G == 1)
     decode_attn_kernel<1><<<grid, dec::THREADS, 0, s>>>(Q, ldq, K, V, block_tables, max_blocks, ctx_lens, O, ldo,
-                                                         Hq, Hkv, BS, sl, workspace, n_splits);
+                                                         Hq, Hkv, BS, sl, workspace, n_splits, split_len);
   else if (G == 2)
     decode_attn_kernel<2><<<grid, dec::THREADS, 0, s>>>(Q, ldq, K, V, block_tables, max_blocks, ctx_lens, O, ldo,
-                                                         Hq, Hkv, BS, sl, workspace, n_splits);
+                                                         Hq, Hkv, BS, sl, workspace, n_splits, split_len);
   else
     throw std::runtime_error("cx decode attention: GQA group size must be 1, 2, 4 or 8");
   if (n_splits > 1) decode_merge_kernel<<<dim3(B, Hq), dec::D, 0, s>>>(workspace, O, ldo, Hq, n_splits);

@@ -176,7 +176,12 @@ void decode_attention(const at::Tensor& q, const at::Tensor& kc, const at::Tenso
   TORCH_CHECK(workspace.numel() >= (int64_t)B * Hq * splits * 130, "decode workspace too small");
   cx::decode_attention(q.data_ptr(), row_ld(q), kc.data_ptr(), vc.data_ptr(), block_tables.data_ptr<int>(),
                        (int)block_tables.size(1), ctx_lens.data_ptr<int>(), out.data_ptr(), row_ld(out), B, (int)Hq,
-                       Hkv, BS, (int)max_ctx, (float)scale, workspace.data_ptr<float>(), cur_stream(q));
+                       Hkv, BS, (int)max_ctx, (float)scale, workspace.data_ptr<float>(), cur_stream(q),
+                       (long)workspace.numel());
+}
+
+int64_t decode_attention_plan(int64_t B, int64_t Hq, int64_t Hkv, int64_t max_ctx, int64_t ws_floats) {
+  return cx::decode_attention_plan((int)B, (int)Hq, (int)Hkv, (int)max_ctx, (long)ws_floats);
 }
 
 int64_t decode_workspace_floats(int64_t B, int64_t Hq, int64_t max_ctx) {
@@ -387,6 +392,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gather_rows", &gather_rows);
   m.def("prefill_attention", &prefill_attention_tc);
   m.def("decode_attention", &decode_attention);
+  m.def("decode_attention_plan", &decode_attention_plan);
   m.def("decode_workspace_floats", &decode_workspace_floats);
   m.def("kv_push_layer", &kv_push_layer);
   m.def("gemm_splits", &gemm_splits);

@@ -21,6 +21,13 @@ void gemm_bf16_tn(const void* A, const void* B, void* D, const void* R, int M, i
 // The K split gemm_bf16_tn would profit from (1 = none).
 int gemm_splits(int M, int N, int K, int epi, int bn);
 
+// M <= GEMV_MAX_M rows (decode steps): the weight-streaming CUDA-core kernel
+// (gemv.cu) that gemm_bf16_tn dispatches to when bn, max_ctas and splits are
+// left to it; returns false for shapes it does not take.
+constexpr int GEMV_MAX_M = 8;
+bool gemv_bf16_tn(const void* A, const void* B, void* D, const void* R, int M, int N, int K, int lda, int ldb, int ldd,
+                  int ldr, int epi, cudaStream_t s);
+
 CUtensorMap make_tmap_bf16_2d(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
                               uint32_t box_inner, uint32_t box_outer, bool swizzle128);
 int num_sms();

@@ -408,6 +408,7 @@ static void launch_gemm(const void* A, const void* B, void* D, const void* R, in
 // Work-item split of the K loop: only when the output tiles alone would
 // leave most SMs idle (small-M decode GEMMs) and K is long enough.
 int gemm_splits(int M, int N, int K, int epi, int bn) {
+  if (bn == 0 && M <= GEMV_MAX_M) return 1;  // the skinny kernel takes these
   if (bn == 0) bn = epi == EPI_SILU_MUL ? 256 : 128;
   const long tiles = (long)((M + GEMM_BM - 1) / GEMM_BM) * ((N + bn - 1) / bn);
   const int nk = (K + GEMM_BK - 1) / GEMM_BK;
@@ -429,6 +430,9 @@ void gemm_bf16_tn(const void* A, const void* B, void* D, const void* R, int M, i
   if (((uintptr_t)A | (uintptr_t)B | (uintptr_t)D | (uintptr_t)R) & 15)
     throw std::runtime_error("cx gemm: operands must be 16-byte aligned");
   if (N % 8 != 0) throw std::runtime_error("cx gemm: N must be a multiple of 8");
+  if (bn == 0 && max_ctas == 0 && splits <= 1 && M <= GEMV_MAX_M &&
+      gemv_bf16_tn(A, B, D, R, M, N, K, lda, ldb, ldd, ldr, epi, stream))
+    return;
   if (bn == 0) {
     // Prefer 256-wide tiles unless that leaves most SMs idle.
     const long tiles256 = (long)((M + 127) / 128) * ((N + 255) / 256);

@@ -60,11 +60,20 @@ def check_status(status: torch.Tensor, what: str = "kernel") -> None:
 _SPLIT_WS: dict = {}
 
 
+_SPLIT_WS_RETIRED: list = []
+
+
 def _split_workspace(device, n: int) -> torch.Tensor:
-    """Per-device fp32 split-K workspace; the finalize kernel leaves it zero."""
+    """Per-device fp32 split-K workspace; the finalize kernel leaves it zero.
+
+    A workspace that is outgrown is kept alive, not freed: CUDA graphs that
+    captured GEMMs hold its address (and it stays zero between uses)."""
     ws = _SPLIT_WS.get(device)
     if ws is None or ws.numel() < n:
-        ws = torch.zeros(max(n, 1 << 20), dtype=torch.float32, device=device)
+        if ws is not None:
+            _SPLIT_WS_RETIRED.append(ws)
+        ws = torch.zeros(max(n, 1 << 20, 2 * ws.numel() if ws is not None else 0), dtype=torch.float32,
+                         device=device)
         _SPLIT_WS[device] = ws
     return ws
 
@@ -221,7 +230,8 @@ def decode_attention(q: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tens
         out = torch.empty(q.shape[0], n_q_heads * 128, dtype=q.dtype, device=q.device)
     _C.decode_attention(q, k_cache, v_cache, block_tables, ctx_lens, out, n_q_heads, max_ctx,
                         scale if scale is not None else 1.0 / math.sqrt(128), workspace)
-    _n(1 if max_ctx <= 512 else 2)
+    splits = _C.decode_attention_plan(q.shape[0], n_q_heads, k_cache.shape[1], max_ctx, workspace.numel())
+    _n(1 if splits == 1 else 2)
     return out
 
 

@@ -141,6 +141,99 @@ class StageRuntime:
         self.steps = 0
         self.act: Optional[torch.Tensor] = None      # activation log (non-last stages)
         self.act_slot: Dict[object, int] = {}
+        self.graphs: Optional[Dict[int, tuple]] = None
+
+    # ------------------------------------------------------------ CUDA graphs
+    def enable_decode_graphs(self, buckets: Optional[Sequence[int]] = None) -> None:
+        """Replay the decode step from CUDA graphs, one per batch bucket
+        (captured on first use): ~10 launches per layer become one graph
+        launch, which is what bounds a small-batch decode step.
+
+        The graphs read static device buffers (ids or the residual stream,
+        positions, slots, context lengths, block tables over ``max_ctx``);
+        each step stages them in one pinned host buffer and copies it up.
+        Rows between the batch and its bucket point at a reserved trash KV
+        block, so padding never writes a live request's cache.  The split-K
+        workspace is sized for the largest bucket before any capture, so no
+        captured pointer is ever reallocated."""
+        if self.device.type != "cuda":
+            return
+        mb = self.model.max_batch
+        bk = sorted({b for b in (buckets or (1, 2, 4, 8, 16, 24, 32, 48, 64, 96, 128, 192, 256)) if b <= mb} | {mb})
+        self.g_buckets = bk
+        top = bk[-1]
+        self.g_mb = -(-self.max_ctx // self.bs)
+        n_i32 = 3 * top + top * self.g_mb
+        self.g_i32 = torch.zeros(n_i32, dtype=torch.int32, device=self.device)
+        self.g_slots = torch.zeros(top, dtype=torch.int64, device=self.device)
+        self.g_rows = torch.arange(top, dtype=torch.int32, device=self.device)
+        self.g_x = None if self.model.is_first else torch.zeros(top, self.cfg.hidden, dtype=torch.bfloat16,
+                                                                  device=self.device)
+        self.h_i32 = torch.zeros(n_i32, dtype=torch.int32).pin_memory()
+        self.h_slots = torch.zeros(top, dtype=torch.int64).pin_memory()
+        self.h_done = torch.cuda.Event()
+        self.trash = self.cache.allocate(1)[0]
+        widths = [lw.wqkv.shape[0] for lw in self.weights.layers] + [self.cfg.hidden, 2 * self.cfg.ffn]
+        if self.model.is_last:
+            widths.append(self.weights.lm_head.shape[0])
+        ops._split_workspace(self.device, top * max(widths))
+        self.graphs = {}
+
+    def _g_views(self, Bb: int):
+        top, MB = self.g_buckets[-1], self.g_mb
+        i = self.g_i32
+        return (i[0:Bb], i[top:top + Bb], i[2 * top:2 * top + Bb], i[3 * top:].view(top, MB)[:Bb],
+                self.g_slots[:Bb], self.g_rows[:Bb])
+
+    def _g_body(self, Bb: int) -> torch.Tensor:
+        ids, pos, lens, bt, slots, rows = self._g_views(Bb)
+        inp = ids if self.model.is_first else self.g_x[:Bb]
+        return self.model.run(inp, pos, slots, prefill=False, block_tables=bt, ctx_lens=lens, max_ctx=self.max_ctx,
+                              workspace=self.ws, rows=rows, B=Bb)
+
+    def _g_fill(self, B: int, Bb: int, pos, slots, lens, tables) -> None:
+        """Stage one step's metadata; rows [B, Bb) read and write only the trash block."""
+        top, MB = self.g_buckets[-1], self.g_mb
+        self.h_done.synchronize()            # the previous step's upload has left this buffer
+        h = self.h_i32
+        h[top:top + Bb] = 0
+        h[top:top + B] = torch.tensor(pos, dtype=torch.int32)
+        h[2 * top:2 * top + Bb] = 1
+        h[2 * top:2 * top + B] = torch.tensor(lens, dtype=torch.int32)
+        bt = h[3 * top:].view(top, MB)
+        bt[:Bb] = self.trash
+        for i, t in enumerate(tables):
+            bt[i, :len(t)] = torch.tensor(t, dtype=torch.int32)
+        self.h_slots[:Bb] = self.trash * self.bs
+        self.h_slots[:B] = torch.tensor(slots, dtype=torch.int64)
+        self.g_i32[top:].copy_(h[top:], non_blocking=True)
+        self.g_slots[:Bb].copy_(self.h_slots[:Bb], non_blocking=True)
+        self.h_done.record()
+
+    def _g_decode(self, inp: torch.Tensor, B: int, pos, slots, lens, tables) -> torch.Tensor:
+        Bb = next(b for b in self.g_buckets if b >= B)
+        ids, *_ = self._g_views(Bb)
+        if self.model.is_first:
+            ids[:B].copy_(inp)
+            if Bb > B:
+                ids[B:].zero_()
+        else:
+            self.g_x[:B].copy_(inp)
+        self._g_fill(B, Bb, pos, slots, lens, tables)
+        if Bb not in self.graphs:
+            side = torch.cuda.Stream(self.device)
+            side.wait_stream(torch.cuda.current_stream(self.device))
+            with torch.cuda.stream(side):
+                self._g_body(Bb)                 # warm-up outside the capture
+            torch.cuda.current_stream(self.device).wait_stream(side)
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g):
+                out = self._g_body(Bb)
+            self.graphs[Bb] = (g, out)
+            self._g_fill(B, Bb, pos, slots, lens, tables)   # the warm-up ran on these buffers too
+        g, out = self.graphs[Bb]
+        g.replay()
+        return out[:B]
 
     def enable_activation_log(self, max_requests: int) -> None:
         """Keep every output row of this stage per request ([requests, max_ctx,
@@ -213,10 +306,12 @@ class StageRuntime:
                 slots.append(t[p // self.bs] * self.bs + p % self.bs)
             lens.append(c + n)
         dev = self.device
-        positions = torch.tensor(pos, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
-        slot_t = torch.tensor(slots, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
         B = len(rids)
         inp = td["ids"] if self.model.is_first else td["x"]
+        graph = not prefill and self.graphs is not None and B <= self.g_buckets[-1]
+        if not graph:
+            positions = torch.tensor(pos, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
+            slot_t = torch.tensor(slots, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
         kw = {}
         if prefill:
             rows, start, q0s = [], 0, []
@@ -227,6 +322,9 @@ class StageRuntime:
                 start += n
             kw["tile_info"] = ops.prefill_tile_info(n_new, dev)
             kw["rows"] = torch.tensor(rows, dtype=torch.int32, device=dev)
+        elif graph:
+            out = self._g_decode(inp, B, pos, slots, lens, [self.tables[r] for r in rids])
+            kw = None
         else:
             mb = -(-max(lens) // self.bs)
             bt = torch.zeros(B, mb, dtype=torch.int32)
@@ -237,7 +335,8 @@ class StageRuntime:
                       ctx_lens=torch.tensor(lens, dtype=torch.int32).pin_memory().to(dev, non_blocking=True),
                       max_ctx=max(lens), workspace=self.ws,
                       rows=torch.arange(B, dtype=torch.int32, device=dev))
-        out = self.model.run(inp, positions, slot_t, prefill=prefill, B=B, **kw)
+        if kw is not None:
+            out = self.model.run(inp, positions, slot_t, prefill=prefill, B=B, **kw)
         if self.act is not None:
             self._log(rids, ctx, n_new, out)
         for r, c, n in zip(rids, ctx, n_new):

@@ -51,6 +51,7 @@ def model_args(ap: argparse.ArgumentParser) -> None:
     ap.add_argument("--advertise-host", default=os.getenv("CONNEX_HOST_IP", "127.0.0.1"),
                     help="address the pipeline endpoint binds and advertises")
     ap.add_argument("--recv-timeout-s", type=float, default=30.0)
+    ap.add_argument("--no-graphs", action="store_true", help="launch decode steps eagerly (no CUDA graphs)")
 
 
 def llama_config(a):
@@ -93,7 +94,8 @@ def build_stepper(a):
     torch.cuda.set_device(dev)
     if a.num_stages == 1:
         n = kv_blocks(a, cfg, 0, cfg.layers)
-        return ModelStepper(cfg, dev, n, a.max_batch, a.max_ctx, a.max_step_tokens, a.checkpoint, a.seed), None
+        return ModelStepper(cfg, dev, n, a.max_batch, a.max_ctx, a.max_step_tokens, a.checkpoint, a.seed,
+                            graphs=not a.no_graphs), None
     from connex_b200.serve import pipeline
     ranges = pipeline.split_layers(cfg.layers, a.num_stages, a.stage_starts)
     if not a.directory:
@@ -102,7 +104,7 @@ def build_stepper(a):
     ep, client = pipeline.join(a.model_name or "connex-b200", 0, a.num_stages, a.replica, dev, a.directory, a.data,
                                a.store, a.store_master, a.advertise_host, a.recv_timeout_s)
     st = PipelineStepper(cfg, ranges[0][1], dev, ep, n, a.max_batch, a.max_ctx, a.max_step_tokens, a.checkpoint,
-                         a.seed, a.recv_timeout_s)
+                         a.seed, a.recv_timeout_s, graphs=not a.no_graphs)
     ep.warm_stage(1)
     ep.auto_warm = True
     return st, (ep, client)

@@ -134,15 +134,18 @@ def _make_runtime(cfg, l0, l1, device, num_blocks, max_batch, max_ctx, max_step_
 
 
 class ModelStepper(_RuntimeSteps):
-    """All layers on one GPU."""
+    """All layers on one GPU; decode steps replay CUDA graphs (``graphs``)."""
 
     def __init__(self, cfg, device, num_blocks: int, max_batch: int = 64, max_ctx: int = 4096,
-                 max_step_tokens: int = 8192, checkpoint: Optional[str] = None, seed: int = 0):
+                 max_step_tokens: int = 8192, checkpoint: Optional[str] = None, seed: int = 0, graphs: bool = True):
         self.cfg = cfg
         self.max_batch, self.max_ctx, self.max_step_tokens = max_batch, max_ctx, max_step_tokens
-        self.num_blocks, self.block_size, self.vocab_size = num_blocks, cfg.block_size, cfg.vocab_size
+        self.block_size, self.vocab_size = cfg.block_size, cfg.vocab_size
         self.rt = _make_runtime(cfg, 0, cfg.layers, device, num_blocks, max_batch, max_ctx, max_step_tokens,
                                 checkpoint, seed)
+        if graphs:
+            self.rt.enable_decode_graphs()
+        self.num_blocks = self.rt.cache.free_blocks          # less the graphs' trash block
 
     def _run(self, kind, rids, seqs):
         td, _, _ = self._td(kind, rids, seqs)
@@ -181,12 +184,16 @@ class PipelineStepper(_RuntimeSteps):
 
     def __init__(self, cfg, l1: int, device, endpoint, num_blocks: int, max_batch: int = 64, max_ctx: int = 4096,
                  max_step_tokens: int = 8192, checkpoint: Optional[str] = None, seed: int = 0,
-                 recv_timeout_s: float = 30.0):
+                 recv_timeout_s: float = 30.0, graphs: bool = True):
         from connex.pp.link import Stage0Link
         self.cfg = cfg
         self.max_batch, self.max_ctx, self.max_step_tokens = max_batch, max_ctx, max_step_tokens
-        self.num_blocks, self.block_size, self.vocab_size = num_blocks, cfg.block_size, cfg.vocab_size
+        self.block_size, self.vocab_size = cfg.block_size, cfg.vocab_size
         self.rt = _make_runtime(cfg, 0, l1, device, num_blocks, max_batch, max_ctx, max_step_tokens, checkpoint, seed)
+        if graphs:
+            self.rt.enable_decode_graphs()
+        # downstream stages keep a trash block too when they run graphs
+        self.num_blocks = num_blocks - 1
         self.ep = endpoint
         self.hooks = _Stage0Hooks()
         self.link = Stage0Link(endpoint, self.hooks, recv_timeout_s=recv_timeout_s)

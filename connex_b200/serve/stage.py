@@ -34,6 +34,8 @@ def run_stage(a, stop: threading.Event) -> dict:
     weights = load_llama(a.checkpoint, dev, layers=(l0, l1), cfg=cfg) if a.checkpoint else None
     rt = StageRuntime(cfg, l0, l1, dev, num_blocks=kv_blocks(a, cfg, l0, l1), max_tokens=a.max_step_tokens,
                       max_batch=a.max_batch, max_ctx=a.max_ctx, seed=a.seed, weights=weights)
+    if not a.no_graphs:
+        rt.enable_decode_graphs()
     ep, client = pipeline.join(a.model_name or "connex-b200", a.stage, a.num_stages, a.replica, dev, a.directory,
                                a.data, a.store, a.store_master, a.advertise_host, a.recv_timeout_s)
     worker = StageWorker(ep, rt, rt.compute)

@@ -68,7 +68,32 @@ def test_gemm_silu_mul(dev):
     _close(out, R.silu_mul_gemm(a, w))
 
 
-@pytest.mark.parametrize("M", [1, 64, 130])
+@pytest.mark.parametrize("M", [1, 2, 3, 5, 8])
+def test_gemm_skinny_rows(dev, M):
+    """Decode-sized GEMMs (M <= 8) run the weight-streaming kernel: store,
+    in-place residual on a strided output view and SiLU-mul epilogues vs the
+    fp32 reference, one launch each, and a K that is not a multiple of 256."""
+    from connex_b200 import ops
+    from connex_b200.ops import reference as R
+    assert ops._C.gemm_splits(M, 4096, 4096, ops.EPI_STORE, 0) == 1
+    for K in (4096, 1032):
+        a, b = _rnd(M, K, dev=dev, seed=30 + M), _rnd(1544, K, dev=dev, seed=31)
+        n0 = ops.launch_count()
+        out = ops.gemm(a, b)
+        assert ops.launch_count() == n0 + 1
+        _close(out, R.gemm(a, b))
+    a, b = _rnd(M, 4096, dev=dev, seed=32), _rnd(2048, 4096, dev=dev, seed=33)
+    big = _rnd(M, 4096, dev=dev, seed=34)
+    x = big[:, 1024:3072]                       # row stride 4096, 16-byte aligned
+    ref = R.gemm(a, b, residual=x)
+    ops.gemm(a, b, x, residual=x)
+    _close(x, ref)
+    gate, up = _rnd(1024, 4096, dev=dev, seed=35, std=0.1), _rnd(1024, 4096, dev=dev, seed=36, std=0.1)
+    w = ops.interleave_gate_up(gate, up)
+    _close(ops.gemm(a, w, silu_mul=True), R.silu_mul_gemm(a, w))
+
+
+@pytest.mark.parametrize("M", [16, 64, 130])
 def test_gemm_split_k(dev, M):
     """Small-M (decode) GEMMs split the K loop: plain, residual and SiLU-mul
     epilogues against the fp32 reference; the workspace is left zero."""
@@ -199,6 +224,14 @@ def test_decode_attention(dev, G):
     out = ops.decode_attention(q, kc, vc, bt, cl, Hq, max(ctx), ws)
     ref = R.paged_decode_attention(q[:, :Hq * 128].view(B, Hq, 128), kc, vc, bt, cl)
     _close(out.view(B, Hq, 128), ref)
+    # a workspace sized for a larger batch lets this small batch cut the context finer
+    big = ops.decode_workspace(64, Hq, max(ctx), dev)
+    assert ops._C.decode_attention_plan(B, Hq, Hkv, max(ctx), big.numel()) > \
+        ops._C.decode_attention_plan(B, Hq, Hkv, max(ctx), ws.numel())
+    out2 = ops.decode_attention(q, kc, vc, bt, cl, Hq, max(ctx), big)
+    _close(out2.view(B, Hq, 128), ref)
+    one = ops.decode_attention(q[3:], kc, vc, bt[3:], cl[3:], Hq, max(ctx), big)    # batch 1, 2000 tokens
+    _close(one.view(1, Hq, 128), ref[3:])
 
 
 def test_kv_push_local(dev):

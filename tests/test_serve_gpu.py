@@ -1,9 +1,10 @@
 """The serving engine on the native kernels: every token the engine
 generates (batched prefill + decode with requests joining mid-stream) is the
 (near-)argmax of the fp32 PyTorch forward of prompt + tokens so far, and a
-two-stage pipeline (stage 1 served by a StageWorker over the step protocol)
-generates exactly the single-GPU tokens, also after stage 1 fails over to
-its second replica mid-generation (rows re-prefilled there)."""
+two-stage pipeline (stage 1 served by a StageWorker over the step protocol;
+decode steps replayed from CUDA graphs with padded batch buckets) follows
+the single-GPU greedy path and the fp32 forward, also after stage 1 fails
+over to its second replica mid-generation (rows re-prefilled there)."""
 import threading
 import time
 
@@ -52,6 +53,7 @@ def test_engine_tokens_follow_the_fp32_forward():
         for o in outs:
             assert o["done"].wait(60) and o["reason"] == "length"
         assert eng.stats["decode_steps"] >= 10 and eng.blocks_reserved == 0
+        assert st.rt.graphs and max(st.rt.graphs) >= 2        # batched steps replayed from CUDA graphs
         w = stage_weights(cfg, 0, cfg.layers, dev, seed=0)
         for p, o in zip(prompts, outs):
             for k, tok in enumerate(o["toks"]):
@@ -104,7 +106,13 @@ def test_two_stage_pipeline_matches_one_gpu_and_survives_a_failover():
     try:
         out = _collect(eng, prompt, 24)
         assert out["done"].wait(60)
-        assert out["toks"] == ref["toks"]                      # same kernels, same shapes: identical
+        # split-K GEMMs accumulate with fp32 atomics, so runs agree token for
+        # token only up to near-ties: check every token against the fp32 forward
+        from connex_b200.runtime.pp import stage_weights
+        w = stage_weights(cfg, 0, cfg.layers, dev, seed=0)
+        for k, tok in enumerate(out["toks"]):
+            assert _near_argmax(w, prompt + out["toks"][:k], tok), k
+        assert out["toks"][0] == ref["toks"][0]                # the prefill's token (no split-K there)
         # second request: the serving replica dies after a few steps (between steps)
         first = s0.current
         before = served[first]
@@ -116,8 +124,6 @@ def test_two_stage_pipeline_matches_one_gpu_and_survives_a_failover():
         s0.on_peer_dead(1, first, "killed")
         assert out2["done"].wait(60) and out2["reason"] == "length"
         assert s0.current == 1 - first and st.reprefills >= 1
-        from connex_b200.runtime.pp import stage_weights
-        w = stage_weights(cfg, 0, cfg.layers, dev, seed=0)
         for k, tok in enumerate(out2["toks"]):
             assert _near_argmax(w, prompt + out2["toks"][:k], tok), k
     finally:
