@@ -178,3 +178,41 @@ def test_split_layers():
     for bad in ((32, 2, "40"), (32, 3, "20,10"), (32, 2, "4,8")):
         with pytest.raises(ValueError):
             split_layers(*bad)
+
+
+def test_server_cli_serves_the_rule_model(tmp_path):
+    """``python -m connex_b200.serve --rule`` starts, answers /health and a
+    completion with the uninterrupted rule output, and exits on SIGTERM."""
+    import json as _json
+    import os
+    import signal
+    import subprocess
+    import sys
+    import urllib.request
+
+    from tests.helpers import free_port, wait_until
+    port = free_port()
+    env = dict(os.environ, PYTHONPATH=os.getcwd())
+    p = subprocess.Popen([sys.executable, "-m", "connex_b200.serve", "--rule", "--port", str(port), "--host",
+                          "127.0.0.1", "--max-ctx", "512"], env=env, stdout=subprocess.PIPE,
+                         stderr=subprocess.STDOUT)
+    url = f"http://127.0.0.1:{port}"
+
+    def up():
+        try:
+            return urllib.request.urlopen(url + "/health", timeout=1).status == 200
+        except OSError:
+            return False
+    try:
+        assert wait_until(up, 60), p.stdout.read1(4096) if p.poll() is not None else "no /health"
+        req = urllib.request.Request(url + "/v1/completions", data=_json.dumps(
+            {"prompt": "t5 t6", "max_tokens": 6}).encode(), headers={"Content-Type": "application/json"})
+        body = _json.loads(urllib.request.urlopen(req, timeout=10).read())
+        assert body["choices"][0]["text"] == reference("t5 t6", 6)[1]
+    finally:
+        p.send_signal(signal.SIGTERM)
+        try:
+            assert p.wait(20) == 0
+        finally:
+            if p.poll() is None:
+                p.kill()
