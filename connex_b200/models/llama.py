@@ -248,8 +248,13 @@ LayerHook = Callable[[int], None]
 class LlamaModel:
     """Forward passes of the Llama decoder over a :class:`PagedKVCache`."""
 
-    def __init__(self, weights: LlamaWeights, cache: PagedKVCache, max_tokens: int, max_batch: int = 256):
+    def __init__(self, weights: LlamaWeights, cache: PagedKVCache, max_tokens: int, max_batch: int = 256,
+                 tp=None):
+        """``tp``: a :class:`connex_b200.parallel.tp.TPGroup` when ``weights``
+        are one rank's shard (``shard_llama``); the residual stream is then
+        all-reduced after the o- and down-projections."""
         self.w = weights
+        self.tp = tp
         self.cfg = weights.cfg
         self.cache = cache
         cfg = self.cfg
@@ -270,13 +275,24 @@ class LlamaModel:
         self.max_batch = max_batch
 
     # ------------------------------------------------------------ layers
+    def _residual_gemm(self, a: torch.Tensor, w: torch.Tensor, x: torch.Tensor) -> None:
+        """x += a @ w^T; under tensor parallelism summed over the group: rank 0
+        adds its partial to x in the epilogue, the others store theirs into
+        x, and an all-reduce of x adds them up."""
+        tp = self.tp
+        if tp is None or tp.world == 1:
+            ops.gemm(a, w, x, residual=x, status=self.status)
+            return
+        ops.gemm(a, w, x, residual=x if tp.rank == 0 else None, status=self.status)
+        tp.all_reduce(x)
+
     def _layer_tail(self, l: int, T: int):
         cfg, lw = self.cfg, self.w.layers[l]
         x, h = self.x[:T], self.h[:T]
-        ops.gemm(self.attn[:T], lw.wo, x, residual=x, status=self.status)
+        self._residual_gemm(self.attn[:T], lw.wo, x)
         ops.rmsnorm(x, lw.mlp_norm, cfg.eps, out=h)
         ops.gemm(h, lw.w13, self.mid[:T], silu_mul=True, status=self.status)
-        ops.gemm(self.mid[:T], lw.w2, x, residual=x, status=self.status)
+        self._residual_gemm(self.mid[:T], lw.w2, x)
         nw = self.w.layers[l + 1].attn_norm if l + 1 < cfg.layers else self.w.final_norm
         ops.rmsnorm(x, nw, cfg.eps, out=h)
 

@@ -63,13 +63,13 @@ class StageModel(LlamaModel):
     """Layers ``[l0, l1)`` of the decoder on their own KV cache."""
 
     def __init__(self, weights: LlamaWeights, l0: int, l1: int, cache: PagedKVCache, max_tokens: int,
-                 max_batch: int = 256, device=None):
+                 max_batch: int = 256, device=None, tp=None):
         self.l0, self.l1 = l0, l1
         self.is_first, self.is_last = l0 == 0, l1 == weights.cfg.layers
         dev = torch.device(device) if device is not None else weights.layers[0].wqkv.device
         if weights.embed is None:          # LlamaModel reads the device from the embedding
             weights.embed = torch.empty(0, weights.cfg.hidden, dtype=torch.bfloat16, device=dev)
-        super().__init__(weights, cache, max_tokens, max_batch)
+        super().__init__(weights, cache, max_tokens, max_batch, tp=tp)
 
     def _next_norm(self, i: int):
         if i + 1 < len(self.w.layers):
@@ -79,10 +79,10 @@ class StageModel(LlamaModel):
     def _tail(self, i: int, T: int) -> None:
         cfg, lw = self.cfg, self.w.layers[i]
         x, h = self.x[:T], self.h[:T]
-        ops.gemm(self.attn[:T], lw.wo, x, residual=x, status=self.status)
+        self._residual_gemm(self.attn[:T], lw.wo, x)
         ops.rmsnorm(x, lw.mlp_norm, cfg.eps, out=h)
         ops.gemm(h, lw.w13, self.mid[:T], silu_mul=True, status=self.status)
-        ops.gemm(self.mid[:T], lw.w2, x, residual=x, status=self.status)
+        self._residual_gemm(self.mid[:T], lw.w2, x)
         nw = self._next_norm(i)
         if nw is not None:
             ops.rmsnorm(x, nw, self.cfg.eps, out=h)
