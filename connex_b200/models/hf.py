@@ -101,11 +101,12 @@ class _Shards:
 
 
 def load_llama(path: str, device, dtype=torch.bfloat16, layers: Optional[Tuple[int, int]] = None,
-               cfg: Optional[LlamaConfig] = None) -> LlamaWeights:
+               cfg: Optional[LlamaConfig] = None, tp: Optional[Tuple[int, int]] = None) -> LlamaWeights:
     """Weights of layers ``[l0, l1)`` (all by default) of the checkpoint in
     ``path``, in the kernels' layouts, on ``device``.  Tensors the stage
     does not own (embedding off the first stage, head off the last) are
-    ``None``."""
+    ``None``.  ``tp = (rank, world)`` keeps only that tensor-parallel rank's
+    shard of every layer (cut on the host, so the device never holds more)."""
     cfg = cfg or config_from_hf(path)
     l0, l1 = layers or (0, cfg.layers)
     if not 0 <= l0 < l1 <= cfg.layers:
@@ -119,6 +120,10 @@ def load_llama(path: str, device, dtype=torch.bfloat16, layers: Optional[Tuple[i
     def put(t):
         return t.contiguous().to(dev)
 
+    shard = None
+    if tp is not None and tp[1] > 1:
+        from connex_b200.parallel.tp import shard_layer, tp_config
+        shard = (lambda lw: shard_layer(lw, cfg, tp[0], tp[1]))
     out_layers = []
     for i in range(l0, l1):
         p = f"model.layers.{i}."
@@ -126,13 +131,14 @@ def load_llama(path: str, device, dtype=torch.bfloat16, layers: Optional[Tuple[i
             get(p + "self_attn.v_proj.weight")
         if q.shape != (cfg.heads * HEAD_DIM, cfg.hidden) or k.shape != (cfg.kv_heads * HEAD_DIM, cfg.hidden):
             raise ValueError(f"layer {i}: q/k shapes {tuple(q.shape)} / {tuple(k.shape)} do not match the config")
-        out_layers.append(LayerWeights(
-            attn_norm=put(get(p + "input_layernorm.weight")),
-            wqkv=put(torch.cat([q, k, v], 0)),
-            wo=put(get(p + "self_attn.o_proj.weight")),
-            mlp_norm=put(get(p + "post_attention_layernorm.weight")),
-            w13=put(ops.interleave_gate_up(get(p + "mlp.gate_proj.weight"), get(p + "mlp.up_proj.weight"))),
-            w2=put(get(p + "mlp.down_proj.weight"))))
+        lw = LayerWeights(
+            attn_norm=get(p + "input_layernorm.weight"), wqkv=torch.cat([q, k, v], 0),
+            wo=get(p + "self_attn.o_proj.weight"), mlp_norm=get(p + "post_attention_layernorm.weight"),
+            w13=ops.interleave_gate_up(get(p + "mlp.gate_proj.weight"), get(p + "mlp.up_proj.weight")),
+            w2=get(p + "mlp.down_proj.weight"))
+        if shard is not None:           # cut on the host: the device only ever holds this rank's part
+            lw = shard(lw)
+        out_layers.append(LayerWeights(**{name: put(t) for name, t in lw.__dict__.items()}))
     first, last = l0 == 0, l1 == cfg.layers
     embed = put(get("model.embed_tokens.weight")) if first else None
     head = None
@@ -141,7 +147,7 @@ def load_llama(path: str, device, dtype=torch.bfloat16, layers: Optional[Tuple[i
             head = put(get("lm_head.weight"))
         else:
             head = embed if embed is not None else put(get("model.embed_tokens.weight"))
-    return LlamaWeights(cfg=cfg, embed=embed, layers=out_layers,
+    return LlamaWeights(cfg=tp_config(cfg, tp[1]) if shard is not None else cfg, embed=embed, layers=out_layers,
                         final_norm=put(get("model.norm.weight")) if last else None, lm_head=head)
 
 

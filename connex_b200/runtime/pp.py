@@ -121,7 +121,8 @@ class StageRuntime:
     """One stage's compute for the step protocol (``StageWorker`` compute + hooks)."""
 
     def __init__(self, cfg: LlamaConfig, l0: int, l1: int, device, num_blocks: int, max_tokens: int,
-                 max_batch: int = 256, max_ctx: int = 8192, seed: int = 0, weights: Optional[LlamaWeights] = None):
+                 max_batch: int = 256, max_ctx: int = 8192, seed: int = 0, weights: Optional[LlamaWeights] = None,
+                 tp=None):
         """``weights``: layers ``[l0, l1)`` already on ``device`` (e.g. from
         :func:`connex_b200.models.hf.load_llama`); random from ``seed`` if absent."""
         self.cfg = cfg
@@ -131,7 +132,7 @@ class StageRuntime:
         self.weights = weights if weights is not None else stage_weights(cfg, l0, l1, self.device, seed)
         stage_cfg = LlamaConfig(**{**cfg.__dict__, "layers": l1 - l0})
         self.cache = PagedKVCache(stage_cfg, num_blocks, self.device)
-        self.model = StageModel(self.weights, l0, l1, self.cache, max_tokens, max_batch, self.device)
+        self.model = StageModel(self.weights, l0, l1, self.cache, max_tokens, max_batch, self.device, tp=tp)
         self.model.cfg = cfg
         self.bs = cfg.block_size
         self.max_ctx = max_ctx

@@ -52,6 +52,8 @@ def model_args(ap: argparse.ArgumentParser) -> None:
                     help="address the pipeline endpoint binds and advertises")
     ap.add_argument("--recv-timeout-s", type=float, default=30.0)
     ap.add_argument("--no-graphs", action="store_true", help="launch decode steps eagerly (no CUDA graphs)")
+    ap.add_argument("--tp", type=int, default=1,
+                    help="tensor-parallel ranks (launch with torchrun --nproc-per-node TP; rank 0 serves HTTP)")
 
 
 def llama_config(a):
@@ -90,6 +92,8 @@ def build_stepper(a):
         return RuleStepper(vocab_size=1000, max_batch=a.max_batch, max_ctx=a.max_ctx), None
     import torch
     cfg = llama_config(a)
+    if getattr(a, "tp", 1) > 1:
+        return _tp_stepper(a, cfg)
     dev = torch.device(a.device)
     torch.cuda.set_device(dev)
     if a.num_stages == 1:
@@ -110,6 +114,41 @@ def build_stepper(a):
     return st, (ep, client)
 
 
+def _tp_stepper(a, cfg):
+    """Tensor-parallel serving: one process per GPU (torchrun); rank 0 gets a
+    TPStepper, the other ranks follow rank 0's steps here and return None.
+    Decode CUDA graphs stay off under TP (the all-reduces run eagerly)."""
+    import datetime
+
+    import torch
+    import torch.distributed as dist
+
+    from connex_b200.parallel.tp import TPGroup
+    from connex_b200.serve.engine import ModelStepper, TPStepper, tp_follow
+    if a.num_stages != 1:
+        raise SystemExit("--tp with --num-stages > 1 is not supported")
+    rank, world = int(os.environ["RANK"]), int(os.environ["WORLD_SIZE"])
+    if world != a.tp:
+        raise SystemExit(f"--tp {a.tp} but WORLD_SIZE {world}")
+    dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", rank)))
+    torch.cuda.set_device(dev)
+    dist.init_process_group("nccl", device_id=dev, timeout=datetime.timedelta(seconds=120))
+    cpu = dist.new_group(backend="gloo")
+    from connex_b200.parallel.tp import tp_config
+    blocks = kv_blocks(argparse.Namespace(**{**vars(a), "device": str(dev)}), tp_config(cfg, world), 0, cfg.layers)
+    t = torch.tensor([blocks], device=dev)
+    dist.all_reduce(t, op=dist.ReduceOp.MIN)              # every rank sizes its KV cache alike
+    inner = ModelStepper(cfg, dev, int(t.item()), a.max_batch, a.max_ctx, a.max_step_tokens, a.checkpoint,
+                         a.seed, graphs=False, tp=TPGroup(rank, world))
+    if rank == 0:
+        return TPStepper(inner, cpu), ("tp", cpu)
+    log.info("TP rank %d of %d following rank 0", rank, world)
+    n = tp_follow(inner, cpu)
+    log.info("TP rank %d: rank 0 stopped after %d steps", rank, n)
+    dist.destroy_process_group()
+    return None, None
+
+
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description="OpenAI-compatible server over the sm_100a Llama runtime")
     model_args(ap)
@@ -123,6 +162,8 @@ def main(argv=None) -> int:
     from connex_b200.serve.api import HFCodec, Server, serve
     from connex_b200.serve.engine import GenerationEngine
     stepper, pp = build_stepper(a)
+    if stepper is None:                 # a tensor-parallel follower rank: done
+        return 0
     tok_dir = a.tokenizer or (a.checkpoint if a.checkpoint and os.path.exists(
         os.path.join(a.checkpoint, "tokenizer_config.json")) else None)
     codec = HFCodec(tok_dir) if tok_dir else None
@@ -144,7 +185,11 @@ def main(argv=None) -> int:
         asyncio.run(run())
     finally:
         engine.stop()
-        if pp is not None:
+        if pp is not None and pp[0] == "tp":
+            stepper.close()             # releases the follower ranks
+            import torch.distributed as dist
+            dist.destroy_process_group()
+        elif pp is not None:
             from connex_b200.serve import pipeline
             pipeline.leave(*pp)
     return 0

@@ -123,26 +123,38 @@ class _RuntimeSteps(Stepper):
         self.rt.release(list(rids))
 
 
-def _make_runtime(cfg, l0, l1, device, num_blocks, max_batch, max_ctx, max_step_tokens, checkpoint, seed):
-    from connex_b200.runtime.pp import StageRuntime
-    weights = None
+def _make_runtime(cfg, l0, l1, device, num_blocks, max_batch, max_ctx, max_step_tokens, checkpoint, seed, tp=None):
+    """A StageRuntime for layers [l0, l1); with ``tp`` (a TPGroup) this rank's
+    shard of them (checkpoint shards are cut on the host; random weights are
+    drawn whole and cut, so every TP degree serves the same model)."""
+    from connex_b200.runtime.pp import StageRuntime, stage_weights
+    weights, rcfg = None, cfg
     if checkpoint:
         from connex_b200.models.hf import load_llama
-        weights = load_llama(checkpoint, device, layers=(l0, l1), cfg=cfg)
-    return StageRuntime(cfg, l0, l1, device, num_blocks=num_blocks, max_tokens=max_step_tokens, max_batch=max_batch,
-                        max_ctx=max_ctx, seed=seed, weights=weights)
+        weights = load_llama(checkpoint, device, layers=(l0, l1), cfg=cfg,
+                             tp=(tp.rank, tp.world) if tp is not None else None)
+        rcfg = weights.cfg
+    elif tp is not None and tp.world > 1:
+        from connex_b200.parallel.tp import shard_layer, tp_config
+        full = stage_weights(cfg, l0, l1, device, seed)
+        full.layers = [shard_layer(lw, cfg, tp.rank, tp.world) for lw in full.layers]
+        full.cfg = rcfg = tp_config(cfg, tp.world)
+        weights = full
+    return StageRuntime(rcfg, l0, l1, device, num_blocks=num_blocks, max_tokens=max_step_tokens, max_batch=max_batch,
+                        max_ctx=max_ctx, seed=seed, weights=weights, tp=tp)
 
 
 class ModelStepper(_RuntimeSteps):
     """All layers on one GPU; decode steps replay CUDA graphs (``graphs``)."""
 
     def __init__(self, cfg, device, num_blocks: int, max_batch: int = 64, max_ctx: int = 4096,
-                 max_step_tokens: int = 8192, checkpoint: Optional[str] = None, seed: int = 0, graphs: bool = True):
+                 max_step_tokens: int = 8192, checkpoint: Optional[str] = None, seed: int = 0, graphs: bool = True,
+                 tp=None):
         self.cfg = cfg
         self.max_batch, self.max_ctx, self.max_step_tokens = max_batch, max_ctx, max_step_tokens
         self.block_size, self.vocab_size = cfg.block_size, cfg.vocab_size
         self.rt = _make_runtime(cfg, 0, cfg.layers, device, num_blocks, max_batch, max_ctx, max_step_tokens,
-                                checkpoint, seed)
+                                checkpoint, seed, tp)
         if graphs:
             self.rt.enable_decode_graphs()
         self.num_blocks = self.rt.cache.free_blocks          # less the graphs' trash block
@@ -156,6 +168,59 @@ class ModelStepper(_RuntimeSteps):
 
     def decode(self, rids, seqs):
         return self._run("decode", rids, seqs)
+
+
+class TPStepper(Stepper):
+    """Rank 0 of a tensor-parallel group: every step (and every release) is
+    broadcast to the other ranks over a CPU process group before it runs
+    here, so all ranks launch the same kernels and the same all-reduces in
+    the same order; the other ranks run :func:`tp_follow`.  A rank that
+    fails takes the whole group down (its collectives time out), which the
+    membership layer reports as a group failure."""
+
+    def __init__(self, inner: Stepper, cpu_group=None, src: int = 0):
+        self.inner, self.pg, self.src = inner, cpu_group, src
+        for k in ("max_batch", "max_ctx", "max_step_tokens", "num_blocks", "block_size", "vocab_size"):
+            setattr(self, k, getattr(inner, k))
+
+    def _send(self, msg) -> None:
+        import torch.distributed as dist
+        dist.broadcast_object_list([msg], src=self.src, group=self.pg)
+
+    def prefill(self, rids, seqs):
+        self._send(("prefill", list(rids), [list(x) for x in seqs]))
+        return self.inner.prefill(rids, seqs)
+
+    def decode(self, rids, seqs):
+        self._send(("decode", list(rids), [list(x) for x in seqs]))
+        return self.inner.decode(rids, seqs)
+
+    def release(self, rids):
+        self._send(("release", list(rids)))
+        self.inner.release(rids)
+
+    def close(self):
+        self._send(("stop",))
+        self.inner.close()
+
+
+def tp_follow(inner: Stepper, cpu_group=None, src: int = 0) -> int:
+    """Ranks 1.. of a tensor-parallel group: run rank ``src``'s steps until it
+    stops; returns the number of steps run."""
+    import torch.distributed as dist
+    n = 0
+    while True:
+        box = [None]
+        dist.broadcast_object_list(box, src=src, group=cpu_group)
+        msg = box[0]
+        if msg[0] == "stop":
+            inner.close()
+            return n
+        if msg[0] == "release":
+            inner.release(msg[1])
+        else:
+            getattr(inner, msg[0])(msg[1], msg[2])
+            n += 1
 
 
 class _Stage0Hooks:

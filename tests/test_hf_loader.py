@@ -119,3 +119,16 @@ def test_native_kernels_on_a_loaded_checkpoint(tmp_path):
         lg = _hf_logits(m, s)
         top = lg.max().item()
         assert lg[int(tok)].item() >= top - 0.05 * (abs(top) + 1), (int(tok), int(lg.argmax()))
+
+
+def test_tensor_parallel_load_is_the_shard_of_the_full_load(tmp_path):
+    from connex_b200.parallel.tp import shard_llama
+    _hf_model(tmp_path, vocab_size=1024, hidden_size=512, num_attention_heads=8, num_key_value_heads=2,
+              intermediate_size=1024, tie=True)
+    full = load_llama(str(tmp_path), "cpu")
+    for rank in range(2):
+        part = load_llama(str(tmp_path), "cpu", tp=(rank, 2))
+        ref = shard_llama(full, rank, 2)
+        assert part.cfg == ref.cfg and part.lm_head is part.embed
+        for (n, a), (_, b) in zip(part.named_tensors(), ref.named_tensors()):
+            assert torch.equal(a, b), n

@@ -216,3 +216,47 @@ def test_server_cli_serves_the_rule_model(tmp_path):
         finally:
             if p.poll() is None:
                 p.kill()
+
+
+def _tp_rank(rank, port, q):
+    import os
+    import torch.distributed as dist
+    from connex_b200.serve.engine import GenerationEngine, TPStepper, tp_follow
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=2)
+        inner = RuleStepper(step_delay_s=0.001)
+        if rank == 0:
+            eng = GenerationEngine(TPStepper(inner)).start()
+            outs = [_collect(eng, [1, 5, 6], 12), _collect(eng, [1, 7], 5)]
+            for o in outs:
+                assert o["done"].wait(10)
+            eng.stop()
+            eng.s.close()
+            q.put((0, inner.calls, [o["toks"] for o in outs], dict(inner.held)))
+        else:
+            n = tp_follow(inner)
+            q.put((1, inner.calls, n, dict(inner.held)))
+        dist.destroy_process_group()
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, "error", repr(e), None))
+
+
+def test_tensor_parallel_ranks_follow_rank_zero_step_for_step():
+    import torch.multiprocessing as mp
+    from tests.helpers import free_port
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    ps = [ctx.Process(target=_tp_rank, args=(r, port, q)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = {r[0]: r[1:] for r in (q.get(timeout=120) for _ in range(2))}
+    for p in ps:
+        p.join(30)
+    assert res[0][0] != "error" and res[1][0] != "error", res
+    calls0, toks, held0 = res[0]
+    calls1, n, held1 = res[1]
+    assert calls0 == calls1 and n == len(calls0)             # the same steps, same order, same rows
+    assert toks == [reference([1, 5, 6], 12)[0], reference([1, 7], 5)[0]]
+    assert held0 == held1 == {}                              # releases followed too
