@@ -78,7 +78,7 @@ async def run_level(url, clients, prompt_len, max_tokens, vocab, duration_s, see
 
 def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description=__doc__.split("\n\n")[0])
-    ap.add_argument("--config", default="llama3-8b", choices=["llama3-8b", "tiny"])
+    ap.add_argument("--config", default="llama3-8b", choices=["llama3-8b", "llama3.1-8b", "tiny"])
     ap.add_argument("--checkpoint", default=None)
     ap.add_argument("--clients", default="1,32")
     ap.add_argument("--prompt-len", type=int, default=1024)
@@ -95,10 +95,10 @@ def main(argv=None) -> int:
     from connex_b200.serve.engine import GenerationEngine
     ns = argparse.Namespace(rule=a.rule, checkpoint=a.checkpoint, config=a.config, layers=None, seed=0,
                             device="cuda:0", num_blocks=a.num_blocks, kv_fraction=0.8, max_batch=a.max_batch,
-                            max_ctx=a.prompt_len + a.max_tokens + 64, max_step_tokens=max(8192, a.prompt_len * 4),
+                            max_ctx=a.prompt_len + a.max_tokens + 64, max_step_tokens=max(8192, a.prompt_len + 64),
                             num_stages=1, stage_starts=None, directory=None, data="link", store=None,
                             store_master=False, replica=0, advertise_host="127.0.0.1", recv_timeout_s=30.0,
-                            no_graphs=a.no_graphs)
+                            no_graphs=a.no_graphs, tp=1)
     stepper, _ = build_stepper(ns)
     engine = GenerationEngine(stepper).start()
     server = Server(engine, "bench")

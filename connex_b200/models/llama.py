@@ -49,6 +49,11 @@ class LlamaConfig:
         return cls()
 
     @classmethod
+    def llama31_8b(cls) -> "LlamaConfig":
+        """Llama-3.1-8B: the 8B geometry with 128k positions and Llama 3.1 RoPE scaling."""
+        return cls(max_pos=131072, rope_scaling=(8.0, 1.0, 4.0, 8192))
+
+    @classmethod
     def tiny(cls, layers: int = 2) -> "LlamaConfig":
         """A small config with the same head geometry (for tests / smoke)."""
         return cls(vocab_size=1024, hidden=512, layers=layers, heads=8, kv_heads=2, ffn=1024,

@@ -30,8 +30,9 @@ log = logging.getLogger("connex_b200.serve")
 
 def model_args(ap: argparse.ArgumentParser) -> None:
     ap.add_argument("--checkpoint", default=None, help="HF Llama checkpoint directory (config.json + safetensors)")
-    ap.add_argument("--config", default="llama3-8b", choices=["llama3-8b", "tiny"],
-                    help="geometry of random weights when no checkpoint is given")
+    ap.add_argument("--config", default="llama3-8b", choices=["llama3-8b", "llama3.1-8b", "tiny"],
+                    help="geometry of random weights when no checkpoint is given (llama3.1-8b: 128k positions, "
+                         "Llama 3.1 RoPE scaling)")
     ap.add_argument("--layers", type=int, default=None, help="override the layer count of --config")
     ap.add_argument("--seed", type=int, default=0)
     ap.add_argument("--device", default="cuda:0")
@@ -62,7 +63,7 @@ def llama_config(a):
         from connex_b200.models.hf import config_from_hf
         cfg = config_from_hf(a.checkpoint)
     else:
-        cfg = LlamaConfig.tiny() if a.config == "tiny" else LlamaConfig.llama3_8b()
+        cfg = {"tiny": LlamaConfig.tiny, "llama3.1-8b": LlamaConfig.llama31_8b}.get(a.config, LlamaConfig.llama3_8b)()
     if a.layers:
         cfg = LlamaConfig(**{**cfg.__dict__, "layers": a.layers})
     if a.max_ctx > cfg.max_pos:
