@@ -3,7 +3,8 @@
 Routes: ``/v1/completions`` and ``/v1/chat/completions`` (streamed or
 not; ``stream_options.include_usage`` / ``continuous_usage_stats``;
 ``return_token_ids``; ``return_tokens_as_token_ids``; id prompts; chat
-``add_generation_prompt`` / ``continue_final_message``; ``stop_token_ids``;
+``add_generation_prompt`` / ``continue_final_message``; ``stop`` strings
+(held back while they may still match, never shown); ``stop_token_ids``;
 ``ignore_eos``), ``/tokenize``, ``/detokenize``, ``/v1/models``, ``/health``
 (503 once the engine thread has died) and ``/load`` (queue and KV
 reservation figures).  This is the request surface the retry / resume proxy
@@ -78,6 +79,41 @@ class HFCodec:
     def chat(self, messages, add_generation_prompt=True, continue_final=False) -> List[int]:
         return list(self.tok.apply_chat_template(messages, add_generation_prompt=add_generation_prompt,
                                                  continue_final_message=continue_final, tokenize=True))
+
+
+class StopMatcher:
+    """Text stop sequences (the API's ``stop``): ``feed`` returns the text
+    that may be shown now and whether a stop sequence completed.  Text that
+    could still be the start of a stop sequence is held back until it is not
+    (or until ``flush``); the stop sequence itself is never shown."""
+
+    def __init__(self, stops):
+        if isinstance(stops, str):
+            stops = [stops]
+        self.stops = [x for x in (stops or []) if x]
+        self.held = ""
+
+    def feed(self, text: str):
+        if not self.stops:
+            return text, False
+        buf = self.held + text
+        hits = [(buf.find(x), x) for x in self.stops if x in buf]
+        if hits:
+            at = min(i for i, _ in hits)
+            self.held = ""
+            return buf[:at], True
+        keep = 0
+        for x in self.stops:
+            for n in range(min(len(x) - 1, len(buf)), 0, -1):
+                if buf.endswith(x[:n]):
+                    keep = max(keep, n)
+                    break
+        self.held = buf[len(buf) - keep:] if keep else ""
+        return buf[:len(buf) - keep], False
+
+    def flush(self) -> str:
+        out, self.held = self.held, ""
+        return out
 
 
 def _err(msg: str, status: int = 400) -> web.Response:
@@ -190,19 +226,25 @@ class Server:
                 return {"content": [{"token": tok, "logprob": None, "top_logprobs": []}]}
             return {"tokens": [tok], "token_logprobs": [None], "top_logprobs": None, "text_offset": [0]}
 
+        sm = StopMatcher(b.get("stop"))
         if not b.get("stream"):
-            toks, reason = [], None
+            toks, reason, parts = [], None, []
             try:
                 while reason is None:
                     tok, reason = await q.get()
                     if tok is not None:
                         toks.append(tok)
+                        shown, hit = sm.feed(self.codec.decode_one(tok))
+                        parts.append(shown)
+                        if hit:
+                            self.engine.cancel(r)
+                            reason = "stop"
             except asyncio.CancelledError:
                 self.engine.cancel(r)
                 raise
             if reason in ("error", "abort"):
                 return _err(f"generation failed: {r.error or reason}", 500)
-            text = "".join(self.codec.decode_one(t) for t in toks)
+            text = "".join(parts) + sm.flush()
             if chat:
                 choice = {"index": 0, "message": {"role": "assistant", "content": text}, "finish_reason": reason}
             else:
@@ -237,11 +279,17 @@ class Server:
                         req.transport.abort()
                     return resp
                 k += 1
+                shown, hit = sm.feed(self.codec.decode_one(tok))
+                if hit:
+                    self.engine.cancel(r)
+                    reason = "stop"
+                elif reason is not None:
+                    shown += sm.flush()
                 if chat:
-                    ch = {"index": 0, "delta": {"content": self.codec.decode_one(tok)},
+                    ch = {"index": 0, "delta": {"content": shown},
                           "logprobs": lp(tok) if want_lp else None, "finish_reason": reason}
                 else:
-                    ch = {"index": 0, "text": self.codec.decode_one(tok), "logprobs": lp(tok) if want_lp else None,
+                    ch = {"index": 0, "text": shown, "logprobs": lp(tok) if want_lp else None,
                           "finish_reason": reason, "stop_reason": None}
                 if want_ids:
                     ch["token_ids"] = [tok]

@@ -260,3 +260,35 @@ def test_tensor_parallel_ranks_follow_rank_zero_step_for_step():
     assert calls0 == calls1 and n == len(calls0)             # the same steps, same order, same rows
     assert toks == [reference([1, 5, 6], 12)[0], reference([1, 7], 5)[0]]
     assert held0 == held1 == {}                              # releases followed too
+
+
+def test_stop_strings_end_generation_and_are_not_shown():
+    from connex_b200.serve.api import StopMatcher
+    m = StopMatcher(["END", "xyz"])
+    assert m.feed("abc E") == ("abc ", False)              # "E" may start "END": held back
+    assert m.feed("N") == ("", False)
+    assert m.feed("Dmore") == ("", True)                    # stop completed; nothing after it shown
+    m = StopMatcher("xyz")
+    assert m.feed("ab x") == ("ab ", False) and m.flush() == "x"
+
+    async def main():
+        eng = GenerationEngine(RuleStepper(step_delay_s=0.001)).start()
+        runner, url = await _serve(Server(eng, "m").app())
+        try:
+            ids, _ = reference("t5 t6", 12)
+            stop = f" t{ids[3]} t{ids[4]}"                     # spans two tokens
+            want = "".join(f" t{t}" for t in ids[:3])
+            async with aiohttp.ClientSession() as s:
+                r = await (await s.post(url + "/v1/completions", json={"prompt": "t5 t6", "max_tokens": 12,
+                                                                       "stop": stop})).json()
+            assert r["choices"][0]["text"] == want and r["choices"][0]["finish_reason"] == "stop"
+            chunks, done = await _stream(url, "/v1/completions", {"prompt": "t5 t6", "max_tokens": 12,
+                                                                   "stop": [stop]})
+            assert done and _text(chunks) == want
+            assert chunks[-1]["choices"][0]["finish_reason"] == "stop"
+            await asyncio.sleep(0.05)
+            assert eng.stats["finished_abort"] >= 2 and eng.blocks_reserved == 0     # generation was cut short
+        finally:
+            await runner.cleanup()
+            eng.stop()
+    _run(main())
