@@ -50,6 +50,7 @@ DEFAULTS = {
     "proxy_port": 5199,
     "ctrl_port": 17100,
     "replicas": 1,
+    "tp": 1,
     "num_stages": 2,
     "stage_replicas": 1,
     "stage_starts": "",
@@ -195,14 +196,20 @@ def _ready(container: dict, port: int) -> None:
 
 
 def serve(c) -> List[dict]:
-    """``--replicas`` one-GPU servers of this framework's own engine
-    (``python -m connex_b200.serve``), each behind its Service; put the
-    ``proxy`` kind in front of them for retries and stream resume."""
+    """``--replicas`` servers of this framework's own engine (``python -m
+    connex_b200.serve``; ``--tp N`` GPUs each, tensor-parallel under
+    torchrun), each behind its Service; put the ``proxy`` kind in front of
+    them for retries and stream resume."""
     items: List[dict] = []
+    tp = int(c["tp"])
     for r in range(int(c["replicas"])):
         name = f"{c['prefix']}-serve-{r}"
-        cmd = ["python", "-m", "connex_b200.serve", "--port", str(c["serve_port"])] + _engine_args(c)
-        d = _deployment(c, name, cmd, {}, {"http": c["serve_port"]}, gpus=1)
+        if tp > 1:          # one process per GPU; rank 0 serves HTTP
+            cmd = ["torchrun", "--nproc-per-node", str(tp), "--master-addr", "127.0.0.1", "-m", "connex_b200.serve",
+                   "--tp", str(tp), "--port", str(c["serve_port"])] + _engine_args(c)
+        else:
+            cmd = ["python", "-m", "connex_b200.serve", "--port", str(c["serve_port"])] + _engine_args(c)
+        d = _deployment(c, name, cmd, {}, {"http": c["serve_port"]}, gpus=tp)
         _ready(d["spec"]["template"]["spec"]["containers"][0], c["serve_port"])
         items += [d, _service(c, name, {"http": c["serve_port"]})]
     return items

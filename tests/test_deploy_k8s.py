@@ -152,3 +152,10 @@ def test_serve_and_pipeline_kinds_run_the_native_engine():
     assert a.store_master and a.num_stages == 3
     a = ap.parse_args(s2[3:])
     assert a.replica == 1 and a.stage == "2"
+
+
+def test_tensor_parallel_serve_replicas():
+    c = _pod(_items("serve", "--model", "llama", "--tp", "4"), "cx-serve-0")["containers"][0]
+    assert c["command"][:4] == ["torchrun", "--nproc-per-node", "4", "--master-addr"]
+    assert c["command"][c["command"].index("--tp") + 1] == "4"
+    assert c["resources"]["limits"] == {"nvidia.com/gpu": 4}
