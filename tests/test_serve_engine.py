@@ -292,3 +292,43 @@ def test_stop_strings_end_generation_and_are_not_shown():
             await runner.cleanup()
             eng.stop()
     _run(main())
+
+
+def test_agent_sessions_stick_migrate_and_fail_over_across_engines():
+    """The session proxy in front of two engines: turns stick to one engine,
+    a migration re-prefills the conversation on the other (a 1-token chat
+    continuation), and when the placement dies the next turn fails over."""
+    from connex.agents import SessionProxy
+    from connex.serving.proxy import Pool
+
+    async def main():
+        engines = [GenerationEngine(RuleStepper(step_delay_s=0.001)).start() for _ in range(2)]
+        served = [await _serve(Server(e, "m").app()) for e in engines]
+        urls = [u for _, u in served]
+        sp = SessionProxy(Pool(urls), probe_interval=0, idle_timeout=0.5)
+        pr, url = await _serve(sp.app())
+        try:
+            msgs = [{"role": "user", "content": "t1 t2"}]
+            outs = []
+            for _ in range(2):
+                chunks, done = await _stream(url, "/v1/chat/completions",
+                                             {"messages": msgs, "max_tokens": 3, "session_id": "s1"})
+                assert done
+                outs.append(_text(chunks, chat=True))
+            assert outs[0] == outs[1] == reference(WordCodec(1000).chat(msgs), 3)[1]
+            first = urls.index(sp.sessions["s1"].url)
+            assert engines[first].stats["submitted"] == 2 and engines[1 - first].stats["submitted"] == 0
+            rec = await sp.migrate("s1", urls[1 - first])
+            assert rec["mode"] == "reprefill" and sp.sessions["s1"].url == urls[1 - first]
+            assert engines[1 - first].stats["submitted"] == 1                   # the re-prefill
+            await served[1 - first][0].cleanup()                                 # the new placement dies
+            engines[1 - first].stop()
+            chunks, done = await _stream(url, "/v1/chat/completions", {"messages": msgs, "max_tokens": 3},
+                                         headers={"X-Connex-Session": "s1"})
+            assert done and sp.stats["failovers"] == 1 and sp.sessions["s1"].url == urls[first]
+        finally:
+            await pr.cleanup()
+            await served[first][0].cleanup()
+            for e in engines:
+                e.stop()
+    _run(main())
