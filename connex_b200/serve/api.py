@@ -6,8 +6,9 @@ not; ``stream_options.include_usage`` / ``continuous_usage_stats``;
 ``add_generation_prompt`` / ``continue_final_message``; ``stop`` strings
 (held back while they may still match, never shown); ``stop_token_ids``;
 ``ignore_eos``), ``/tokenize``, ``/detokenize``, ``/v1/models``, ``/health``
-(503 once the engine thread has died) and ``/load`` (queue and KV
-reservation figures).  This is the request surface the retry / resume proxy
+(503 once the engine thread has died), ``/load`` (queue and KV reservation
+figures) and ``/metrics`` (Prometheus: requests by finish reason, tokens,
+TTFT / TPOT histograms, queue and KV gauges).  This is the request surface the retry / resume proxy
 and the PD router drive, so both can front this engine directly.
 
 Decoding is greedy (the device argmax); ``temperature`` and friends are
@@ -121,12 +122,45 @@ def _err(msg: str, status: int = 400) -> web.Response:
                              status=status)
 
 
+class _Metrics:
+    """Prometheus collectors of one server (own registry, so several servers
+    can live in one process): requests by outcome, generated tokens, TTFT
+    and TPOT histograms, and the engine's queue / KV gauges read at scrape."""
+
+    def __init__(self, engine: GenerationEngine):
+        from prometheus_client import CollectorRegistry, Counter, Gauge, Histogram
+        self.registry = r = CollectorRegistry()
+        self.requests = Counter("connex_serve_requests", "finished requests", ["finish_reason"], registry=r)
+        self.tokens = Counter("connex_serve_generated_tokens", "generated tokens", registry=r)
+        self.ttft = Histogram("connex_serve_ttft_seconds", "arrival to first token", registry=r,
+                              buckets=(.005, .01, .025, .05, .1, .25, .5, 1, 2.5, 5, 10))
+        self.tpot = Histogram("connex_serve_tpot_seconds", "mean time per output token after the first",
+                              registry=r, buckets=(.001, .0025, .005, .01, .02, .05, .1, .25))
+        for name, key in (("waiting", "waiting"), ("running", "running"), ("kv_blocks_reserved", "kv_blocks_reserved"),
+                          ("kv_blocks", "kv_blocks")):
+            g = Gauge(f"connex_serve_{name}", name.replace("_", " "), registry=r)
+            g.set_function(lambda key=key: engine.load()[key])
+
+    def finished(self, req, reason: str) -> None:
+        self.requests.labels(reason or "unknown").inc()
+        self.tokens.inc(len(req.gen))
+        if req.t_first is not None:
+            self.ttft.observe(req.t_first - req.t_submit)
+            if len(req.gen) > 1:
+                import time as _t
+                self.tpot.observe((_t.monotonic() - req.t_first) / (len(req.gen) - 1))
+
+
 class Server:
     def __init__(self, engine: GenerationEngine, model: str = "connex-b200", codec=None):
         self.engine = engine
         self.model = model
         self.codec = codec or WordCodec(engine.s.vocab_size or 1000)
         self._n = 0
+        try:
+            self.metrics = _Metrics(engine)
+        except ImportError:          # prometheus_client is optional
+            self.metrics = None
 
     def app(self) -> web.Application:
         app = web.Application(client_max_size=64 << 20)
@@ -137,7 +171,15 @@ class Server:
         app.router.add_get("/v1/models", self._models)
         app.router.add_get("/health", self._health)
         app.router.add_get("/load", self._load)
+        app.router.add_get("/metrics", self._metrics)
         return app
+
+    async def _metrics(self, req):
+        if self.metrics is None:
+            return web.Response(status=404, text="prometheus_client is not installed")
+        from prometheus_client import CONTENT_TYPE_LATEST, generate_latest
+        return web.Response(body=generate_latest(self.metrics.registry),
+                            headers={"Content-Type": CONTENT_TYPE_LATEST})
 
     async def _models(self, req):
         return web.json_response({"object": "list", "data": [{"id": self.model, "object": "model",
@@ -202,7 +244,11 @@ class Server:
         loop = asyncio.get_running_loop()
         q: asyncio.Queue = asyncio.Queue()
 
+        metrics = self.metrics
+
         def on_token(r, tok, reason):
+            if reason is not None and metrics is not None:
+                metrics.finished(r, reason)
             loop.call_soon_threadsafe(q.put_nowait, (tok, reason))
         try:
             r = self.engine.submit(ids, n_max, on_token, stop_ids=stop)

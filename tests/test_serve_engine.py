@@ -122,6 +122,10 @@ def test_http_routes():
                 assert bad.status == 400
                 load = await (await s.get(url + "/load")).json()
                 assert load["running"] == 0 and load["tokens"] == 4
+                m = await (await s.get(url + "/metrics")).text()
+                assert 'connex_serve_requests_total{finish_reason="length"} 1.0' in m
+                assert "connex_serve_generated_tokens_total 4.0" in m and "connex_serve_ttft_seconds_count 1.0" in m
+                assert "connex_serve_waiting 0.0" in m
             chunks, done = await _stream(url, "/v1/completions",
                                          {"prompt": [1, 9, 9], "max_tokens": 5, "return_token_ids": True,
                                           "logprobs": 0, "return_tokens_as_token_ids": True,
