@@ -25,7 +25,7 @@ from __future__ import annotations
 import asyncio
 import json
 import time
-from typing import List, Optional
+from typing import List
 
 from aiohttp import web
 
