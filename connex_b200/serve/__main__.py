@@ -89,6 +89,8 @@ def kv_blocks(a, cfg, l0: int, l1: int) -> int:
 
 def build_stepper(a):
     from connex_b200.serve.engine import ModelStepper, PipelineStepper, RuleStepper
+    if getattr(a, "rule", False) and a.num_stages > 1:
+        return _rule_pipeline(a)
     if getattr(a, "rule", False):
         return RuleStepper(vocab_size=1000, max_batch=a.max_batch, max_ctx=a.max_ctx), None
     import torch
@@ -110,6 +112,25 @@ def build_stepper(a):
                                a.store, a.store_master, a.advertise_host, a.recv_timeout_s)
     st = PipelineStepper(cfg, ranges[0][1], dev, ep, n, a.max_batch, a.max_ctx, a.max_step_tokens, a.checkpoint,
                          a.seed, a.recv_timeout_s, graphs=not a.no_graphs)
+    ep.warm_stage(1)
+    ep.auto_warm = True
+    return st, (ep, client)
+
+
+def _rule_pipeline(a):
+    """Stage 0 of a pipeline of CPU stand-in stages (``--rule``: every stage
+    runs :class:`RuleStageRuntime`; ``--data inline``), to check the CLIs,
+    the directory and failover without a GPU."""
+    from connex_b200.models.llama import LlamaConfig
+    from connex_b200.serve import pipeline
+    from connex_b200.serve.engine import PipelineStepper, RuleStageRuntime
+    if not a.directory:
+        raise SystemExit("--num-stages > 1 needs --directory")
+    cfg = LlamaConfig(vocab_size=1000)
+    ep, client = pipeline.join(a.model_name or "connex-b200", 0, a.num_stages, a.replica, "cpu", a.directory, "inline",
+                               None, False, a.advertise_host, a.recv_timeout_s)
+    st = PipelineStepper(cfg, 1, "cpu", ep, 1 << 20, a.max_batch, a.max_ctx, a.max_step_tokens,
+                         recv_timeout_s=a.recv_timeout_s, rt=RuleStageRuntime(True, False, 1000))
     ep.warm_stage(1)
     ep.auto_warm = True
     return st, (ep, client)
@@ -156,7 +177,8 @@ def main(argv=None) -> int:
     ap.add_argument("--host", default="0.0.0.0")
     ap.add_argument("--port", type=int, default=8100)
     ap.add_argument("--tokenizer", default=None, help="HF tokenizer directory (default: the checkpoint's, if any)")
-    ap.add_argument("--rule", action="store_true", help="serve the deterministic CPU stand-in model")
+    ap.add_argument("--rule", action="store_true", help="serve the deterministic CPU stand-in model (with "
+                    "--num-stages: stage 0 of a pipeline of stand-in stages)")
     ap.add_argument("--log-level", default="INFO")
     a = ap.parse_args(argv)
     logging.basicConfig(level=getattr(logging, a.log_level), format="%(asctime)s [%(levelname)s] %(name)s: %(message)s")

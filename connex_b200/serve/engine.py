@@ -106,6 +106,61 @@ class RuleStepper(Stepper):
             self.held.pop(r, None)
 
 
+class RuleStageRuntime:
+    """CPU stand-in for one pipeline stage's compute (the step protocol of
+    :class:`connex_b200.runtime.pp.StageRuntime`): the "activations" are the
+    token ids themselves, every stage keeps each request's ids as its "KV"
+    (so a replica that never saw a request lacks it and the rows come back
+    missing), and the last stage answers the :class:`RuleStepper` rule.
+    ``delay_s`` slows each step, to kill a replica mid-stream in tests."""
+
+    def __init__(self, first: bool, last: bool, vocab_size: int = 1000, delay_s: float = 0.0):
+        import torch
+        self.first, self.last, self.vocab, self.delay_s = first, last, vocab_size, delay_s
+        self.device = torch.device("cpu")
+        self.seqs: Dict[str, List[int]] = {}
+        self.steps = 0
+
+    def kv_held(self, rid) -> int:
+        return len(self.seqs.get(rid, ()))
+
+    def release(self, rids) -> None:
+        for r in rids:
+            self.seqs.pop(r, None)
+
+    def reprefill(self, rids) -> None:
+        pass
+
+    def abort(self, rids) -> None:
+        self.release(rids)
+
+    def compute(self, td: dict, missing) -> dict:
+        import torch
+        from connex.pp.handover import CX_CTX, REQUEST_IDS
+        if td.get("kind") == "warmup":
+            return {"kind": "warmup", "w": td["w"].clone()}
+        if self.delay_s:
+            time.sleep(self.delay_s)
+        rids, ctx, n_new = list(td[REQUEST_IDS]), list(td[CX_CTX]), list(td["n_new"])
+        x = (td["ids"] if self.first else td["x"]).to(torch.int64).tolist()
+        i, nxt = 0, []
+        for r, c, n in zip(rids, ctx, n_new):
+            seq = [] if (td["kind"] == "prefill" or r in missing) else self.seqs.get(r, [])[:c]
+            seq = seq + x[i:i + n]
+            i += n
+            if r not in missing:
+                self.seqs[r] = seq
+            a, b = seq[-1], seq[-2] if len(seq) > 1 else 0
+            nxt.append((a * 37 + b * 11 + 5) % (self.vocab - 16) + 16)
+        self.steps += 1
+        out = {"kind": td["kind"], "n_new": n_new}
+        if self.last:
+            out["next"] = torch.tensor(nxt, dtype=torch.int64)
+        else:
+            out["x"] = torch.tensor(x, dtype=torch.int64)
+        return out
+
+
 class _RuntimeSteps(Stepper):
     """Step tensors for a :class:`connex_b200.runtime.pp.StageRuntime`."""
 
@@ -116,7 +171,9 @@ class _RuntimeSteps(Stepper):
             ids, ctx, n_new = [t for s in seqs for t in s], [0] * len(seqs), [len(s) for s in seqs]
         else:
             ids, ctx, n_new = [s[-1] for s in seqs], [len(s) - 1 for s in seqs], [1] * len(seqs)
-        t = torch.tensor(ids, dtype=torch.int32).pin_memory().to(self.rt.device, non_blocking=True)
+        t = torch.tensor(ids, dtype=torch.int32)
+        if self.rt.device.type == "cuda":
+            t = t.pin_memory().to(self.rt.device, non_blocking=True)
         return {"kind": kind, REQUEST_IDS: list(rids), CX_CTX: ctx, "n_new": n_new, "ids": t}, ctx, n_new
 
     def release(self, rids):
@@ -249,13 +306,16 @@ class PipelineStepper(_RuntimeSteps):
 
     def __init__(self, cfg, l1: int, device, endpoint, num_blocks: int, max_batch: int = 64, max_ctx: int = 4096,
                  max_step_tokens: int = 8192, checkpoint: Optional[str] = None, seed: int = 0,
-                 recv_timeout_s: float = 30.0, graphs: bool = True):
+                 recv_timeout_s: float = 30.0, graphs: bool = True, rt=None):
+        """``rt``: stage 0's compute when not the Llama runtime (the CPU
+        stand-in :class:`RuleStageRuntime`)."""
         from connex.pp.link import Stage0Link
         self.cfg = cfg
         self.max_batch, self.max_ctx, self.max_step_tokens = max_batch, max_ctx, max_step_tokens
         self.block_size, self.vocab_size = cfg.block_size, cfg.vocab_size
-        self.rt = _make_runtime(cfg, 0, l1, device, num_blocks, max_batch, max_ctx, max_step_tokens, checkpoint, seed)
-        if graphs:
+        self.rt = rt if rt is not None else _make_runtime(cfg, 0, l1, device, num_blocks, max_batch, max_ctx,
+                                                          max_step_tokens, checkpoint, seed)
+        if graphs and rt is None:
             self.rt.enable_decode_graphs()
         # downstream stages keep a trash block too when they run graphs
         self.num_blocks = num_blocks - 1

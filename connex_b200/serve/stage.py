@@ -24,6 +24,13 @@ def run_stage(a, stop: threading.Event) -> dict:
     import torch
 
     from connex.pp.link import StageWorker
+    if a.rule:                 # CPU stand-in stage (no GPU): ids as activations, ids as KV
+        from connex_b200.serve import pipeline
+        from connex_b200.serve.engine import RuleStageRuntime
+        rt = RuleStageRuntime(False, a.stage == a.num_stages - 1, 1000, a.rule_delay_ms / 1e3)
+        ep, client = pipeline.join(a.model_name or "connex-b200", a.stage, a.num_stages, a.replica, "cpu",
+                                   a.directory, "inline", None, False, a.advertise_host, a.recv_timeout_s)
+        return _serve_loop(ep, client, StageWorker(ep, rt, rt.compute), stop, a, (a.stage, a.stage + 1))
     from connex_b200.models.hf import load_llama
     from connex_b200.runtime.pp import StageRuntime
     from connex_b200.serve import pipeline
@@ -38,8 +45,13 @@ def run_stage(a, stop: threading.Event) -> dict:
         rt.enable_decode_graphs()
     ep, client = pipeline.join(a.model_name or "connex-b200", a.stage, a.num_stages, a.replica, dev, a.directory,
                                a.data, a.store, a.store_master, a.advertise_host, a.recv_timeout_s)
-    worker = StageWorker(ep, rt, rt.compute)
-    log.info("stage %d replica %d: layers [%d, %d) serving at %s", a.stage, a.replica, l0, l1, ep.address)
+    return _serve_loop(ep, client, StageWorker(ep, rt, rt.compute), stop, a, (l0, l1))
+
+
+def _serve_loop(ep, client, worker, stop: threading.Event, a, layers) -> dict:
+    from connex_b200.serve import pipeline
+    log.info("stage %d replica %d: layers [%d, %d) serving at %s", a.stage, a.replica, layers[0], layers[1],
+             ep.address)
     try:
         while not stop.is_set():
             td, ctx = ep.recv_forward(timeout_s=0.2)
@@ -54,6 +66,8 @@ def main(argv=None) -> int:
     ap = argparse.ArgumentParser(description="downstream stage of a serving pipeline")
     model_args(ap)
     ap.add_argument("--stage", type=int, required=True)
+    ap.add_argument("--rule", action="store_true", help="CPU stand-in stage (with a --rule stage 0)")
+    ap.add_argument("--rule-delay-ms", type=float, default=0.0, help="stand-in stage: sleep per step")
     ap.add_argument("--log-level", default="INFO")
     a = ap.parse_args(argv)
     if not 0 < a.stage < a.num_stages or not a.directory:
