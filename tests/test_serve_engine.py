@@ -16,6 +16,7 @@ from connex.serving.fake_backend import reference
 from connex_b200.serve.api import Server, WordCodec
 from connex_b200.serve.engine import EngineFull, GenerationEngine, RuleStepper
 from connex_b200.serve.pipeline import split_layers
+from tests.helpers import wait_until
 from tests.test_serving import _proxy, _run, _serve, _stream, _text
 
 
@@ -38,18 +39,18 @@ def test_batching_matches_the_uninterrupted_rule_and_admits_between_steps():
     st = RuleStepper(step_delay_s=0.002)
     eng = GenerationEngine(st).start()
     try:
-        a = _collect(eng, [1, 5, 6], 20)
-        time.sleep(0.01)
+        a = _collect(eng, [1, 5, 6], 60)
+        assert wait_until(lambda: len(a["toks"]) >= 2, 5)
         b = _collect(eng, [1, 7], 8)                    # joins while a is decoding
         for x in (a, b):
             assert x["done"].wait(5)
-        assert a["toks"] == reference([1, 5, 6], 20)[0] and a["reason"] == "length"
+        assert a["toks"] == reference([1, 5, 6], 60)[0] and a["reason"] == "length"
         assert b["toks"] == reference([1, 7], 8)[0]
         kinds = [k for k, _ in st.calls]
         assert kinds.count("prefill") == 2
         mixed = [rids for k, rids in st.calls if k == "decode" and len(rids) == 2]
         assert mixed                                    # a and b decoded in the same step
-        assert not st.held and eng.blocks_reserved == 0
+        assert wait_until(lambda: not st.held and eng.blocks_reserved == 0, 5)
     finally:
         eng.stop()
 
@@ -62,7 +63,7 @@ def test_stop_ids_cancel_and_kv_reservations():
         s = _collect(eng, [1, 5], 6, stop_ids=[stop_at])
         assert s["done"].wait(5) and s["reason"] == "stop" and s["toks"][-1] == stop_at and len(s["toks"]) == 3
         big = _collect(eng, [1] * 10, 40)                     # 50 tokens: 4 blocks, the whole cache
-        time.sleep(0.02)
+        assert wait_until(lambda: len(big["toks"]) >= 1, 5)
         small = _collect(eng, [1, 2], 3)                      # waits for the blocks
         time.sleep(0.05)
         assert small["toks"] == [] and eng.load()["waiting"] == 1
@@ -75,8 +76,7 @@ def test_stop_ids_cancel_and_kv_reservations():
             eng.submit([1] * 4000, 200, lambda *a: None)      # beyond the context
         with pytest.raises(ValueError):
             eng.submit([1, 5000], 2, lambda *a: None)         # outside the vocabulary
-        time.sleep(0.02)
-        assert eng.blocks_reserved == 0 and not st.held
+        assert wait_until(lambda: eng.blocks_reserved == 0 and not st.held, 5)   # released right after the callback
     finally:
         eng.stop()
 
@@ -93,7 +93,7 @@ def test_a_failed_step_fails_only_its_requests():
         boom["on"] = False
         b = _collect(eng, [1, 4], 5)
         assert b["done"].wait(5) and b["toks"] == reference([1, 4], 5)[0]
-        assert eng.alive and eng.stats["step_errors"] == 1 and not st.held
+        assert wait_until(lambda: eng.alive and eng.stats["step_errors"] == 1 and not st.held, 5)
     finally:
         eng.stop()
 
@@ -290,7 +290,10 @@ def test_stop_strings_end_generation_and_are_not_shown():
                                                                    "stop": [stop]})
             assert done and _text(chunks) == want
             assert chunks[-1]["choices"][0]["finish_reason"] == "stop"
-            await asyncio.sleep(0.05)
+            for _ in range(100):
+                if eng.stats["finished_abort"] >= 2 and eng.blocks_reserved == 0:
+                    break
+                await asyncio.sleep(0.05)
             assert eng.stats["finished_abort"] >= 2 and eng.blocks_reserved == 0     # generation was cut short
         finally:
             await runner.cleanup()
