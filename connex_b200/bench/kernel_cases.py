@@ -11,7 +11,10 @@ capture of the case runs.
 Cases: gemm (8192^3), gemm_qkv (T=8192 Llama-3-8B QKV), gemm_silu (T=8192
 gate/up + SiLU-mul), attn (8 x 2048-token causal prefill, 32/8 heads),
 decode_attn (64 x 4096-token paged decode), kv_push (one layer of a 64k-token
-KV push, local), wsync (Llama-3-8B 2-layer slice, fp32 -> bf16 fused
+KV push, local), kv_push_nvlink (the same layer pushed from GPU 0 into GPU 1's
+memory over NVLink, one process, peer access; ``--ctas`` sets the grid,
+``--pull`` runs the kernel on GPU 1 reading GPU 0's memory instead, ``--ce``
+times a copy-engine peer copy of the same bytes for comparison), wsync (Llama-3-8B 2-layer slice, fp32 -> bf16 fused
 re-layout), ep_gemm (grouped expert GEMM, 1 GPU).
 """
 from __future__ import annotations
@@ -37,17 +40,18 @@ def _peaks():
         return 6650.0, 1590.0, "fallback"
 
 
-def _time(fn, iters: int, warmup: int = 3) -> float:
-    for _ in range(warmup):
-        fn()
-    torch.cuda.synchronize()
-    a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
-    a.record()
-    for _ in range(iters):
-        fn()
-    b.record()
-    torch.cuda.synchronize()
-    return a.elapsed_time(b) / iters
+def _time(fn, iters: int, warmup: int = 3, device=None) -> float:
+    with torch.cuda.device(device if device is not None else torch.cuda.current_device()):
+        for _ in range(warmup):
+            fn()
+        torch.cuda.synchronize()
+        a, b = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        a.record()
+        for _ in range(iters):
+            fn()
+        b.record()
+        torch.cuda.synchronize()
+        return a.elapsed_time(b) / iters
 
 
 def case_gemm(dev, M=8192, N=8192, K=8192, silu=False):
@@ -91,6 +95,44 @@ def case_kv_push(dev, tokens=65536, hkv=8):
         ops.kv_push_layer(src[0].data_ptr(), src[1].data_ptr(), dst[0].data_ptr(), dst[1].data_ptr(), pairs,
                           src_heads=hkv, dst_heads=hkv, chunk_bytes=chunk, src_blocks=nb, dst_blocks=nb)
     return run, {"bytes": 2 * src.numel() * 2}   # read + write
+
+
+def case_kv_push_nvlink(dev, tokens=65536, hkv=8, ctas=0, pull=False, ce=False):
+    """One layer's KV (64k tokens, 256 MB) from GPU 0's cache into GPU 1's over
+    NVLink.  Push: the kernel runs on GPU 0 and stores into GPU 1's memory;
+    pull: it runs on GPU 1 and loads GPU 0's memory.  Bytes counted once (the
+    bytes that cross the link)."""
+    if torch.cuda.device_count() < 2:
+        raise SystemExit("kv_push_nvlink needs 2 GPUs")
+    bs = 16
+    nb = tokens // bs
+    d0, d1 = torch.device("cuda", 0), torch.device("cuda", 1)
+    ops.enable_peer_access(0, 1)
+    ops.enable_peer_access(1, 0)
+    src = torch.randn(2, nb, hkv, bs, 128, device=d0).bfloat16()
+    dst = torch.empty_like(src, device=d1)
+    run_dev = d1 if pull else d0
+    perm = torch.randperm(nb)
+    pairs = torch.stack([torch.arange(nb), perm], 1).int().to(run_dev)
+    chunk = bs * 128 * 2
+    status = ops.new_status(run_dev)
+    if ce:
+        def run():
+            dst.copy_(src, non_blocking=True)
+    else:
+        def run():
+            ops.kv_push_layer(src[0].data_ptr(), src[1].data_ptr(), dst[0].data_ptr(), dst[1].data_ptr(), pairs,
+                              src_heads=hkv, dst_heads=hkv, chunk_bytes=chunk, src_blocks=nb, dst_blocks=nb,
+                              max_ctas=ctas, status=status)
+
+    def check():
+        torch.cuda.synchronize(d0)
+        torch.cuda.synchronize(d1)
+        if not ce:
+            ops.check_status(status, "kv push nvlink")
+            got = dst[:, perm.to(d1).long()].float().cpu()
+            assert torch.equal(got, src.float().cpu()), "kv_push_nvlink: destination differs from source"
+    return run, {"bytes": src.numel() * 2, "device": run_dev, "check": check, "link": True}
 
 
 def case_wsync(dev, layers=2):
@@ -160,24 +202,39 @@ CASES = {"gemm": lambda d: case_gemm(d), "gemm_qkv": lambda d: case_gemm(d, 8192
          "gemm_m32_gateup": lambda d: case_gemm_m(d, 32, 28672, 4096, silu=True),
          "decode_step_b1": lambda d: case_decode_step(d, 1), "decode_step_b32": lambda d: case_decode_step(d, 32),
          "decode_step_b1_eager": lambda d: case_decode_step(d, 1, graphs=False)}
+NEEDS_ARGS = {"kv_push_nvlink": case_kv_push_nvlink}
 
 
 def main() -> None:
     p = argparse.ArgumentParser()
-    p.add_argument("case", choices=sorted(CASES))
+    p.add_argument("case", choices=sorted(CASES) + sorted(NEEDS_ARGS))
     p.add_argument("--iters", type=int, default=20)
+    p.add_argument("--ctas", type=int, default=0, help="kv_push_nvlink: grid size (0 = the launcher's default)")
+    p.add_argument("--pull", action="store_true", help="kv_push_nvlink: run on GPU 1, loading GPU 0's memory")
+    p.add_argument("--ce", action="store_true", help="kv_push_nvlink: copy-engine peer copy instead of the kernel")
     a = p.parse_args()
     dev = torch.device("cuda", 0)
-    fn, work = CASES[a.case](dev)
-    ms = _time(fn, a.iters)
+    if a.case in NEEDS_ARGS:
+        fn, work = NEEDS_ARGS[a.case](dev, ctas=a.ctas, pull=a.pull, ce=a.ce)
+    else:
+        fn, work = CASES[a.case](dev)
+    ms = _time(fn, a.iters, device=work.get("device"))
+    if "check" in work:
+        work["check"]()
     hbm, tf, src = _peaks()
     res = {"case": a.case, "ms": round(ms, 4)}
+    if a.case in NEEDS_ARGS:
+        res.update({"ctas": a.ctas, "pull": a.pull, "ce": a.ce})
     if "flops" in work:
         res["tflops"] = round(work["flops"] / ms / 1e9, 1)
         res[f"frac_of_{src}_bf16"] = round(res["tflops"] / tf, 3)
     if "bytes" in work:
         res["gbps"] = round(work["bytes"] / ms / 1e6, 1)
-        res[f"frac_of_{src}_hbm"] = round(res["gbps"] / hbm, 3)
+        if work.get("link"):
+            # NVLink 5: 770 GB/s measured peer copy per direction on this machine type, 900 nominal
+            res["frac_of_770_peer_copy"] = round(res["gbps"] / 770.0, 3)
+        else:
+            res[f"frac_of_{src}_hbm"] = round(res["gbps"] / hbm, 3)
     print(json.dumps(res), flush=True)
 
 

@@ -7,8 +7,8 @@ from __future__ import annotations
 
 import os
 import statistics
-import time
 from datetime import timedelta
+from typing import Sequence
 
 import numpy as np
 import torch
@@ -20,7 +20,8 @@ from connex_b200.parallel.peer import PeerHandle, PeerMapper, export_tensor
 from connex_b200.runtime.pd import (DecodeBatch, KVDestination, LayerwiseKVPusher, block_pairs,
                                     build_prefill_batch, decode_step)
 
-PUSH_CTAS = 296          # CTAs per layer push (2 per SM): leaves the prefill GEMMs most SMs
+PUSH_CTAS = int(os.environ.get("CX_PD_PUSH_CTAS", "296"))   # CTAs per layer push (2 per SM by default)
+PUSH_AFTER_ATTENTION = os.environ.get("CX_PD_PUSH_AFTER", "kv") == "attention"
 TOKEN_BYTES = 64         # first-token inbox copy (16 int32)
 
 
@@ -30,10 +31,50 @@ def push_ctas(n_pairs: int, n_heads: int) -> int:
     return min((warps + 7) // 8, PUSH_CTAS)
 
 
-def _prompts(seed: int, step: int, pair: int, batch: int, lo: int, hi: int, vocab: int):
-    rng = np.random.default_rng([seed, step, pair])
+def _prompts(seed: int, step: int, batch: int, lo: int, hi: int, vocab: int):
+    """The step's prompts.  Every prefill/decode pair draws the same lengths in
+    a step, so the max-over-ranks step time measures the transfer, not the
+    slowest random draw."""
+    rng = np.random.default_rng([seed, step])
     lens = rng.integers(lo, hi + 1, size=batch)
     return [rng.integers(0, vocab, size=int(n)).tolist() for n in lens]
+
+
+def _runs(src: Sequence[int], dst: Sequence[int]):
+    """(src0, dst0, n) runs where both block lists advance by one."""
+    out = []
+    for s, d in zip(src, dst):
+        if out and out[-1][0] + out[-1][2] == s and out[-1][1] + out[-1][2] == d:
+            out[-1][2] += 1
+        else:
+            out.append([s, d, 1])
+    return [tuple(r) for r in out]
+
+
+def kv_checksum(cache: PagedKVCache, blocks: Sequence[Sequence[int]], lens: Sequence[int]) -> list:
+    """Order-sensitive checksums of each request's first ``n`` cached tokens
+    over all layers: the sum and the token-position-weighted sum in fp64."""
+    out = []
+    for b, n in zip(blocks, lens):
+        nb = (n + cache.cfg.block_size - 1) // cache.cfg.block_size
+        idx = torch.tensor(list(b[:nb]), dtype=torch.long, device=cache.kv.device)
+        x = cache.kv.index_select(2, idx)                             # [L, 2, nb, H, BS, D]
+        L, two, _, H, BS, D = x.shape
+        x = x.permute(0, 1, 3, 2, 4, 5).reshape(L, two, H, nb * BS, D)[:, :, :, :n].double()
+        w = torch.arange(1, n + 1, dtype=torch.float64, device=x.device).view(1, 1, 1, -1, 1)
+        out.append((round(float(x.sum()), 6), round(float((x * w).sum()), 6)))
+    return out
+
+
+def _job_gpu_uuids(world: int, cpu, dev) -> list:
+    """UUIDs of the GPUs this job's ranks drive (nvidia-smi ``uuid`` form)."""
+    mine = str(torch.cuda.get_device_properties(dev).uuid)
+    mine = mine if mine.startswith("GPU-") else "GPU-" + mine
+    if world == 1:
+        return [mine]
+    allu = [None] * world
+    dist.all_gather_object(allu, mine, group=cpu)
+    return allu
 
 
 def run_pd_bench(args, ClockSampler, finalize: bool = True):
@@ -103,9 +144,14 @@ def run_pd_bench(args, ClockSampler, finalize: bool = True):
     ready_target = 0
     tok_seg = None
 
-    def run_step(step: int, timed: bool):
+    def run_step(step: int, timed: bool, check: bool = False, bulk: bool = False):
+        """One step.  ``bulk``: the reference's design instead of the layerwise
+        push -- prefill every layer, then copy the whole KV with one copy-engine
+        peer copy per (layer, K/V, run of consecutive blocks).  ``check``:
+        after the step, compare checksums of the prefill side's source blocks
+        and the decode side's destination blocks (outside any timed region)."""
         nonlocal ready_target, tok_seg
-        prompts = _prompts(args.seed, step, pair, B, args.min_len, args.max_len, cfg.vocab_size)
+        prompts = _prompts(args.seed, step, B, args.min_len, args.max_len, cfg.vocab_size)
         lens = [len(p) for p in prompts]
         n_pairs_total = sum((n + cfg.block_size - 1) // cfg.block_size for n in lens)
         # destination blocks: allocated by the decode instance, sent to its prefill peer
@@ -130,20 +176,25 @@ def run_pd_bench(args, ClockSampler, finalize: bool = True):
             ids = ids_host.to(dev, non_blocking=True)                      # H2D from pinned memory
             batch = build_prefill_batch(pre.cache, prompts, dev, ids=ids)
             pairs = block_pairs(batch.src_blocks, [d[:len(s)] for d, s in zip(dblocks, batch.src_blocks)], dev)
-            pusher.begin(pairs, dst, timing=True)
+            if not bulk:
+                pusher.begin(pairs, dst, timing=True)
             nxt = pre.prefill(batch.ids, batch.positions, batch.slots, batch.seq_lens, batch.last_rows,
-                              batch.tile_info, layer_hook=pusher.hook)
+                              batch.tile_info, layer_hook=None if bulk else pusher.hook,
+                              hook_after_attention=PUSH_AFTER_ATTENTION)
             # first tokens -> decode inbox, on the push stream after the prefill's head
             pusher.stream.wait_stream(torch.cuda.current_stream(dev))
             if tok_seg is None:
                 tok_seg = torch.tensor([[pre.next_ids.data_ptr(), inbox_addr, TOKEN_BYTES]],
                                        dtype=torch.int64, device=dev)
             with torch.cuda.stream(pusher.stream):
+                if bulk:
+                    kv_bytes = bulk_copy(batch.src_blocks, dblocks)
                 ops.copy_segments(tok_seg, TOKEN_BYTES, ready=dst.ready_addr, max_ctas=1, status=pusher.status)
             pusher.join()
-            kv_bytes = pusher.bytes  # summed over all layers
+            if not bulk:
+                kv_bytes = pusher.bytes  # summed over all layers
         if role in ("decode", "both"):
-            ready_target += cfg.layers * push_ctas(n_pairs_total, cfg.kv_heads) + 1
+            ready_target += (0 if bulk else cfg.layers * push_ctas(n_pairs_total, cfg.kv_heads)) + 1
             ops.wait_flag(ready.data_ptr(), ready_target, dstatus, timeout_s=30.0)
             db = DecodeBatch(dec_cache, dblocks, lens, dev)
             tok = decode_step(dec, db, inbox[:B], ws)
@@ -152,8 +203,15 @@ def run_pd_bench(args, ClockSampler, finalize: bool = True):
         torch.cuda.synchronize(dev)
         launches = ops.launch_count() - l0
         step_ms = e0.elapsed_time(e1)
+        sums = None
+        if check:
+            sums = {}
+            if role in ("prefill", "both"):
+                sums["src"] = kv_checksum(pre.cache, batch.src_blocks, lens)
+            if role in ("decode", "both"):
+                sums["dst"] = kv_checksum(dec_cache, dblocks, lens)
         if role in ("prefill", "both"):
-            push_ms = pusher.push_ms()
+            push_ms = 0.0 if bulk else pusher.push_ms()
             ops.check_status(pusher.status, "kv push")
             for b in batch.src_blocks:
                 pre.cache.free(b)
@@ -162,21 +220,44 @@ def run_pd_bench(args, ClockSampler, finalize: bool = True):
             for b in dblocks:
                 dec_cache.free(b)
         return {"step_ms": step_ms, "push_ms": push_ms, "kv_bytes": kv_bytes, "tokens": sum(lens),
-                "launches": launches, "lens": lens}
+                "launches": launches, "lens": lens, "sums": sums}
+
+    def bulk_copy(src_blocks, dst_blocks) -> int:
+        """The reference's design: after the whole prefill, copy every layer's
+        K and V block runs with the copy engine (one memcpy per run)."""
+        nbytes = 0
+        hs = pre.cache.head_slice_bytes * cfg.kv_heads          # one block of one layer's K (or V)
+        for sb, db in zip(src_blocks, dst_blocks):
+            for s0, d0, n in _runs(sb, db[:len(sb)]):
+                for layer in range(cfg.layers):
+                    for kv in range(2):
+                        src = pre.cache.kv[layer, kv, s0:s0 + n]
+                        dptr = dst.base + layer * dst.layer_stride + kv * dst.kv_stride + d0 * hs
+                        ops.from_ptr(dptr, list(src.shape), src.dtype, dev.index).copy_(src, non_blocking=True)
+                        nbytes += n * hs
+        return nbytes
 
     for w in range(args.warmup):
         run_step(10_000 + w, False)
-    clocks = ClockSampler(range(torch.cuda.device_count())) if local == 0 else None
+    sampled = _job_gpu_uuids(world, cpu, dev)
+    clocks = ClockSampler(sampled) if local == 0 else None
     if clocks:
         clocks.start()
     recs = [run_step(s, True) for s in range(args.steps)]
     clk = clocks.stop() if clocks else None
+    # outside the timed region: KV checksum of one layerwise-push step, then
+    # the bulk-copy design on the same prompts (TTFT comparison)
+    chk = run_step(20_000, False, check=True)
+    n_bulk = max(3, min(args.steps, 8))
+    run_step(30_000, False, bulk=True)
+    bulk = [run_step(s, False, bulk=True) for s in range(n_bulk)]
 
     gathered = [None] * world
+    mine = {"role": role, "recs": recs, "clk": clk, "sums": chk["sums"], "bulk": bulk}
     if world > 1:
-        dist.all_gather_object(gathered, {"role": role, "recs": recs, "clk": clk}, group=cpu)
+        dist.all_gather_object(gathered, mine, group=cpu)
     else:
-        gathered = [{"role": role, "recs": recs, "clk": clk}]
+        gathered = [mine]
     result = None
     if rank == 0:
         K = args.steps
@@ -192,6 +273,12 @@ def run_pd_bench(args, ClockSampler, finalize: bool = True):
         tokens = sum(g["recs"][s]["tokens"] for g in prod for s in range(K))
         launches = sum(g["recs"][s]["launches"] for g in gathered for s in range(K))
         clk0 = gathered[0]["clk"] or {}
+        # KV check: every pair's decode-side blocks equal its prefill-side blocks
+        if world == 1:
+            ok = gathered[0]["sums"]["src"] == gathered[0]["sums"]["dst"]
+        else:
+            ok = all(gathered[r]["sums"]["src"] == gathered[r + world // 2]["sums"]["dst"] for r in range(world // 2))
+        bulk_max = [max(g["bulk"][s]["step_ms"] for g in gathered) for s in range(n_bulk)]
         result = {
             "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": K, "warmup": args.warmup,
             "ms_per_step": round(statistics.mean(step_max), 3),
@@ -199,7 +286,11 @@ def run_pd_bench(args, ClockSampler, finalize: bool = True):
             "kv_bytes_per_step": kv_total // K,
             "push_ms_per_step_max": round(statistics.mean(push_max), 3),
             "prefill_tokens_per_s": round(tokens / (sum(step_max) * 1e-3), 1),
-            "e2e": {"value": round(e2e, 3), "unit": "GB/s KV delivered (whole step, public PD API)",
+            "kv_check": "ok" if ok else "MISMATCH",
+            "p50_ttft_ms_bulk_copy_after_prefill": round(statistics.median(bulk_max), 3),
+            "e2e": {"value": round(e2e, 3),
+                    "unit": ("GB/s of KV delivered per second of the whole step through connex_b200.runtime.pd "
+                             "(H2D of prompt ids, prefill with the layerwise push, decode first token, D2H)"),
                     "h2d_bytes_per_step": 4 * tokens // K, "d2h_bytes_per_step": 4 * B * len(prod)},
             "gpu_launches": launches,
             "clocks": {"sm_mhz": clk0.get("sm_mhz"), "sm_max_mhz": clk0.get("sm_max_mhz"),
@@ -208,8 +299,11 @@ def run_pd_bench(args, ClockSampler, finalize: bool = True):
             "config": {"model": f"Llama-3-8B architecture ({cfg.layers} layers)", "global_batch": B * len(prod),
                        "seq_len": f"uniform {args.min_len}-{args.max_len}",
                        "parallelism": "colocated 1P1D" if world == 1 else f"pd {world // 2}P{world // 2}D (TP1)",
-                       "kv_block_tokens": cfg.block_size, "l2": "inputs larger than L2 (16 GB weights, GB-scale KV)"},
+                       "kv_block_tokens": cfg.block_size, "l2": "inputs larger than L2 (16 GB weights, GB-scale KV)",
+                       "push_ctas": PUSH_CTAS, "push_after": "attention" if PUSH_AFTER_ATTENTION else "kv write"},
         }
+    if rank == 0 and result is not None and result["kv_check"] != "ok":
+        raise SystemExit("kv_check failed: decode-side KV differs from the prefill side")
     if world > 1:
         barrier()
         mapper.close()

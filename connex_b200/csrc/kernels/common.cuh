@@ -2,7 +2,7 @@
 //
 // Everything here is written against the public PTX ISA for sm_100a:
 //   * mbarrier arrive / expect_tx / try_wait (bounded by %globaltimer),
-//   * TMA tiled loads (cp.async.bulk.tensor, never with .multicast::cluster),
+//   * TMA tiled loads of local memory only (cp.async.bulk.tensor, no cluster multicast),
 //   * tcgen05 alloc / mma / commit / ld for the 5th-generation tensor cores,
 //   * system-scope acquire / release accesses for flags in peer memory.
 //

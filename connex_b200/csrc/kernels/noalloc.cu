@@ -71,8 +71,11 @@ extern "C" __attribute__((visibility("default"))) int cx_decode_attention_noallo
   const int rc = scratch_for_current_device(&scratch);
   if (rc != CX_NOALLOC_OK) return rc;
   try {
+    // The whole array is this call's workspace, so small batches get the
+    // finer split plan (more CTAs) the allocating path uses when its
+    // workspace has room; the plan never asks for more than it is given.
     cx::decode_attention(q, ldq, k_cache, v_cache, block_tables, max_blocks, ctx_lens, out, ldo, B, Hq, Hkv, BS,
-                         max_ctx, scale, scratch, stream);
+                         max_ctx, scale, scratch, stream, (long)CX_NOALLOC_SCRATCH_FLOATS);
   } catch (const std::exception&) {
     return CX_NOALLOC_ERR_ARGS;
   }

@@ -310,11 +310,14 @@ class LlamaModel:
 
     def prefill(self, ids: torch.Tensor, positions: torch.Tensor, slots: torch.Tensor,
                 seq_lens: Sequence[int], last_rows: torch.Tensor, tile_info: torch.Tensor,
-                layer_hook: Optional[LayerHook] = None) -> torch.Tensor:
+                layer_hook: Optional[LayerHook] = None, hook_after_attention: bool = False) -> torch.Tensor:
         """Prefill a packed batch; returns the greedy next token of each sequence.
 
         ``layer_hook(l)`` runs (on the host, in stream order) right after layer
-        l's K/V are in the paged cache: the PD path launches its push there."""
+        l's K/V are in the paged cache: the PD path launches its push there.
+        With ``hook_after_attention`` it runs after layer l's attention has
+        been enqueued instead (the push then overlaps the layer's GEMMs rather
+        than its attention kernel)."""
         cfg, T = self.cfg, ids.numel()
         assert T <= self.max_tokens
         nvtx.push(f"prefill T={T}")
@@ -326,9 +329,11 @@ class LlamaModel:
             ops.gemm(self.h[:T], lw.wqkv, qkv, status=self.status)
             ops.rope_cache(qkv, positions, self.cos_sin, cfg.heads, cfg.kv_heads, slots,
                            self.cache.k(l), self.cache.v(l), status=self.status)
-            if layer_hook is not None:
+            if layer_hook is not None and not hook_after_attention:
                 layer_hook(l)
             ops.prefill_attention(qkv, tile_info, cfg.heads, cfg.kv_heads, out=self.attn[:T])
+            if layer_hook is not None and hook_after_attention:
+                layer_hook(l)
             self._layer_tail(l, T)
             nvtx.pop()
         out = self._head(last_rows, len(seq_lens))

@@ -52,6 +52,12 @@ class WordCodec:
     def decode_one(self, t: int) -> str:
         return f" t{t}"
 
+    def decode(self, ids) -> str:
+        return "".join(self.decode_one(int(t)) for t in ids)
+
+    def stream(self) -> "_WordStream":
+        return _WordStream(self)
+
     def chat(self, messages, add_generation_prompt=True, continue_final=False) -> List[int]:
         ids = [BOS]
         for i, m in enumerate(messages):
@@ -75,11 +81,76 @@ class HFCodec:
         return list(self.tok.encode(text, add_special_tokens=add_special))
 
     def decode_one(self, t: int) -> str:
-        return self.tok.decode([t])
+        return self.tok.decode([t], skip_special_tokens=True)
+
+    def decode(self, ids) -> str:
+        return self.tok.decode(list(ids), skip_special_tokens=True)
+
+    def stream(self) -> "IncrementalDetokenizer":
+        return IncrementalDetokenizer(self.tok)
 
     def chat(self, messages, add_generation_prompt=True, continue_final=False) -> List[int]:
-        return list(self.tok.apply_chat_template(messages, add_generation_prompt=add_generation_prompt,
-                                                 continue_final_message=continue_final, tokenize=True))
+        out = self.tok.apply_chat_template(messages, add_generation_prompt=add_generation_prompt,
+                                           continue_final_message=continue_final, tokenize=True)
+        if hasattr(out, "keys"):          # newer transformers return a BatchEncoding
+            out = out["input_ids"]
+        return [int(t) for t in out]
+
+
+class _WordStream:
+    """Per-request text of the word codec: every id is a whole word."""
+
+    def __init__(self, codec: WordCodec):
+        self.codec = codec
+
+    def feed(self, t: int) -> str:
+        return self.codec.decode_one(t)
+
+    def flush(self) -> str:
+        return ""
+
+
+class IncrementalDetokenizer:
+    """Streaming text of one request's generated ids for a subword tokenizer.
+
+    Decoding each id on its own breaks two things: a byte-level BPE splits a
+    multi-byte UTF-8 character across ids (each piece alone decodes to
+    U+FFFD), and word-initial spaces depend on the previous piece.  So each
+    ``feed`` decodes a short window -- the ids already shown since the last
+    stable point plus the new ones -- and emits only the text beyond what
+    the window's shown part decodes to.  While the window's text ends in an
+    incomplete character (U+FFFD) nothing is emitted; the bytes come out
+    with the id that completes them.  Special tokens (EOS and the like) are
+    skipped."""
+
+    def __init__(self, tok):
+        self.tok = tok
+        self.ids: List[int] = []
+        self.start = 0        # first id of the decoding window (left context)
+        self.shown = 0        # ids [start, shown) are already emitted as text
+
+    def _text(self, a: int, b: int) -> str:
+        return self.tok.decode(self.ids[a:b], skip_special_tokens=True)
+
+    def feed(self, t: int) -> str:
+        self.ids.append(int(t))
+        before = self._text(self.start, self.shown)
+        now = self._text(self.start, len(self.ids))
+        if now.endswith("\ufffd") or len(now) < len(before) or not now.startswith(before):
+            return ""                                  # an incomplete character: wait for its next byte
+        new = now[len(before):]
+        # the ids just shown become the next window's left context
+        self.start, self.shown = self.shown, len(self.ids)
+        return new
+
+    def flush(self) -> str:
+        """Whatever is still held back (an unfinished character at the end)."""
+        if self.shown == len(self.ids):
+            return ""
+        before = self._text(self.start, self.shown)
+        now = self._text(self.start, len(self.ids))
+        self.shown = len(self.ids)
+        return now[len(before):] if now.startswith(before) else now
 
 
 class StopMatcher:
@@ -204,7 +275,7 @@ class Server:
 
     async def _detokenize(self, req):
         b = await req.json()
-        return web.json_response({"prompt": "".join(self.codec.decode_one(int(t)) for t in b["tokens"])})
+        return web.json_response({"prompt": self.codec.decode([int(t) for t in b["tokens"]])})
 
     async def _completions(self, req):
         try:
@@ -273,6 +344,13 @@ class Server:
             return {"tokens": [tok], "token_logprobs": [None], "top_logprobs": None, "text_offset": [0]}
 
         sm = StopMatcher(b.get("stop"))
+        dt = self.codec.stream()
+
+        def text_of(tok, reason):
+            """New text of a generated id; a stop id ends the output without text."""
+            if reason == "stop" and tok in stop:
+                return dt.flush()
+            return dt.feed(tok) + (dt.flush() if reason is not None else "")
         if not b.get("stream"):
             toks, reason, parts = [], None, []
             try:
@@ -280,7 +358,7 @@ class Server:
                     tok, reason = await q.get()
                     if tok is not None:
                         toks.append(tok)
-                        shown, hit = sm.feed(self.codec.decode_one(tok))
+                        shown, hit = sm.feed(text_of(tok, reason))
                         parts.append(shown)
                         if hit:
                             self.engine.cancel(r)
@@ -325,7 +403,7 @@ class Server:
                         req.transport.abort()
                     return resp
                 k += 1
-                shown, hit = sm.feed(self.codec.decode_one(tok))
+                shown, hit = sm.feed(text_of(tok, reason))
                 if hit:
                     self.engine.cancel(r)
                     reason = "stop"

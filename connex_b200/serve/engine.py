@@ -227,43 +227,92 @@ class ModelStepper(_RuntimeSteps):
         return self._run("decode", rids, seqs)
 
 
+class GroupStepError(RuntimeError):
+    """A step failed on one rank of a tensor-parallel group.  The ranks no
+    longer issue matching collectives, so the whole group must stop: the
+    engine treats this error as fatal (it fails every request and stops
+    admitting new ones) instead of failing only the step's requests."""
+
+
 class TPStepper(Stepper):
     """Rank 0 of a tensor-parallel group: every step (and every release) is
     broadcast to the other ranks over a CPU process group before it runs
     here, so all ranks launch the same kernels and the same all-reduces in
-    the same order; the other ranks run :func:`tp_follow`.  A rank that
-    fails takes the whole group down (its collectives time out), which the
-    membership layer reports as a group failure."""
+    the same order; the other ranks run :func:`tp_follow`.
+
+    A failure anywhere is fatal to the group.  If this rank's step raises,
+    the followers may be inside that step's all-reduces (or past them), so no
+    later step can pair its collectives correctly: the stepper turns broken,
+    tells the followers to exit (best effort, from a daemon thread so a
+    follower stuck in a collective cannot block this rank) and raises
+    :class:`GroupStepError`, which stops the engine.  If a follower's step
+    raises, it exits; this rank's next collective then fails with the
+    process group's timeout, which lands here the same way."""
 
     def __init__(self, inner: Stepper, cpu_group=None, src: int = 0):
         self.inner, self.pg, self.src = inner, cpu_group, src
+        self.broken: Optional[str] = None
         for k in ("max_batch", "max_ctx", "max_step_tokens", "num_blocks", "block_size", "vocab_size"):
             setattr(self, k, getattr(inner, k))
 
     def _send(self, msg) -> None:
         import torch.distributed as dist
+        if self.broken is not None:
+            raise GroupStepError(f"tensor-parallel group is down: {self.broken}")
         dist.broadcast_object_list([msg], src=self.src, group=self.pg)
 
+    def _fail(self, e: BaseException) -> GroupStepError:
+        import threading as _th
+
+        import torch.distributed as dist
+        self.broken = f"{type(e).__name__}: {e}"
+
+        def tell():
+            try:
+                dist.broadcast_object_list([("abort", self.broken)], src=self.src, group=self.pg)
+            except Exception:  # noqa: BLE001 - the followers may be gone or stuck; nothing more to do
+                pass
+        _th.Thread(target=tell, name="cx-tp-abort", daemon=True).start()
+        return GroupStepError(f"step failed on rank {self.src}; the tensor-parallel group stops: {self.broken}")
+
+    def _run(self, kind, rids, seqs):
+        if self.broken is not None:
+            raise GroupStepError(f"tensor-parallel group is down: {self.broken}")
+        try:
+            self._send((kind, list(rids), [list(x) for x in seqs]))
+            return getattr(self.inner, kind)(rids, seqs)
+        except Exception as e:  # noqa: BLE001 - any failure breaks collective matching
+            raise self._fail(e) from e
+
     def prefill(self, rids, seqs):
-        self._send(("prefill", list(rids), [list(x) for x in seqs]))
-        return self.inner.prefill(rids, seqs)
+        return self._run("prefill", rids, seqs)
 
     def decode(self, rids, seqs):
-        self._send(("decode", list(rids), [list(x) for x in seqs]))
-        return self.inner.decode(rids, seqs)
+        return self._run("decode", rids, seqs)
 
     def release(self, rids):
-        self._send(("release", list(rids)))
+        if self.broken is not None:
+            return
+        try:
+            self._send(("release", list(rids)))
+        except Exception as e:  # noqa: BLE001
+            raise self._fail(e) from e
         self.inner.release(rids)
 
     def close(self):
-        self._send(("stop",))
+        if self.broken is None:
+            try:
+                self._send(("stop",))
+            except Exception:  # noqa: BLE001 - the followers are gone; close this rank anyway
+                pass
         self.inner.close()
 
 
 def tp_follow(inner: Stepper, cpu_group=None, src: int = 0) -> int:
     """Ranks 1.. of a tensor-parallel group: run rank ``src``'s steps until it
-    stops; returns the number of steps run."""
+    stops; returns the number of steps run.  Raises :class:`GroupStepError`
+    when rank ``src`` reports a failed step; a step failing here propagates
+    (the caller exits, and rank ``src``'s next collective fails)."""
     import torch.distributed as dist
     n = 0
     while True:
@@ -273,6 +322,9 @@ def tp_follow(inner: Stepper, cpu_group=None, src: int = 0) -> int:
         if msg[0] == "stop":
             inner.close()
             return n
+        if msg[0] == "abort":
+            inner.close()
+            raise GroupStepError(f"rank {src} failed a step: {msg[1]}")
         if msg[0] == "release":
             inner.release(msg[1])
         else:
@@ -411,6 +463,8 @@ class GenerationEngine:
             raise ValueError("empty prompt")
         if max_tokens <= 0:
             raise ValueError("max_tokens must be positive")
+        if self.error is not None:
+            raise EngineFull(f"engine stopped: {self.error}")
         if len(prompt) + max_tokens > self.s.max_ctx:
             raise EngineFull(f"prompt ({len(prompt)}) + max_tokens ({max_tokens}) exceeds the context "
                              f"({self.s.max_ctx})")
@@ -521,6 +575,8 @@ class GenerationEngine:
         seqs = [r.prompt + r.gen for r in reqs]
         try:
             toks = (self.s.prefill if kind == "prefill" else self.s.decode)(rids, seqs)
+        except GroupStepError:
+            raise                       # fatal: the loop ends and fails every request
         except Exception as e:  # noqa: BLE001 - fail the step's requests, keep serving
             log.exception("%s step of %d requests failed", kind, len(reqs))
             self.stats["step_errors"] += 1

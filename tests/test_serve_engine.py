@@ -266,6 +266,85 @@ def test_tensor_parallel_ranks_follow_rank_zero_step_for_step():
     assert held0 == held1 == {}                              # releases followed too
 
 
+def _tp_rank_failing(rank, port, q, failing_rank):
+    """Rank ``failing_rank``'s inner stepper raises on its 3rd decode step."""
+    import os
+    from datetime import timedelta
+    import torch.distributed as dist
+    from connex_b200.serve.engine import EngineFull, GenerationEngine, GroupStepError, TPStepper, tp_follow
+    try:
+        os.environ.update(MASTER_ADDR="127.0.0.1", MASTER_PORT=str(port))
+        dist.init_process_group("gloo", rank=rank, world_size=2, timeout=timedelta(seconds=10))
+        seen = {"decode": 0}
+
+        def fail_on(kind, rids):
+            seen[kind] = seen.get(kind, 0) + 1
+            return rank == failing_rank and kind == "decode" and seen["decode"] == 3
+        inner = RuleStepper(step_delay_s=0.001, fail_on=fail_on)
+        if rank == 0:
+            eng = GenerationEngine(TPStepper(inner)).start()
+            out = _collect(eng, [1, 5, 6], 12)
+            assert out["done"].wait(30)
+            assert wait_until(lambda: not eng.alive, 30)
+            try:
+                eng.submit([1, 2], 3, lambda *a: None)
+                refused = False
+            except EngineFull:
+                refused = True
+            q.put((0, eng.error, out["reason"], len(out["toks"]), refused))
+            eng.stop()
+        else:
+            try:
+                tp_follow(inner)
+                q.put((1, "returned", None, None, None))
+            except GroupStepError as e:
+                q.put((1, "GroupStepError", str(e), None, None))
+            except Exception as e:  # noqa: BLE001 - its own injected failure
+                q.put((1, type(e).__name__, str(e), None, None))
+                q.close()
+                q.join_thread()        # the result is flushed; now die like a crashed rank
+                os._exit(0)
+        try:
+            dist.destroy_process_group()
+        except Exception:  # noqa: BLE001
+            pass
+    except Exception as e:  # noqa: BLE001
+        q.put((rank, "error", repr(e), None, None))
+
+
+def _run_tp_failing(failing_rank):
+    import torch.multiprocessing as mp
+    from tests.helpers import free_port
+    ctx = mp.get_context("spawn")
+    q = ctx.Queue()
+    port = free_port()
+    ps = [ctx.Process(target=_tp_rank_failing, args=(r, port, q, failing_rank)) for r in range(2)]
+    for p in ps:
+        p.start()
+    res = {r[0]: r[1:] for r in (q.get(timeout=120) for _ in range(2))}
+    for p in ps:
+        p.join(30)
+        if p.is_alive():
+            p.kill()
+    return res
+
+
+def test_tensor_parallel_step_failure_on_rank_zero_stops_the_whole_group():
+    res = _run_tp_failing(0)
+    err, reason, n_toks, refused = res[0]
+    assert err is not None and "GroupStepError" in err, res    # fatal, not a per-request failure
+    assert reason == "abort" and n_toks < 12 and refused
+    assert res[1][0] == "GroupStepError" and "injected decode failure" in res[1][1]   # the follower was told
+
+
+def test_tensor_parallel_step_failure_on_a_follower_stops_rank_zero():
+    res = _run_tp_failing(1)
+    assert res[1][0] == "RuntimeError"                          # the follower's own step failed; it exited
+    err, reason, n_toks, refused = res[0]
+    assert err is not None and "GroupStepError" in err, res    # rank 0's next collective failed: fatal
+    assert reason == "abort" and n_toks < 12 and refused
+
+
 def test_stop_strings_end_generation_and_are_not_shown():
     from connex_b200.serve.api import StopMatcher
     m = StopMatcher(["END", "xyz"])
@@ -339,3 +418,84 @@ def test_agent_sessions_stick_migrate_and_fail_over_across_engines():
             for e in engines:
                 e.stop()
     _run(main())
+
+
+def _tiny_bpe_dir(tmp_path):
+    """A byte-level BPE tokenizer trained here on a few lines (no network),
+    saved as an HF tokenizer directory with an EOS special token."""
+    from tokenizers import Tokenizer, decoders, models, pre_tokenizers, trainers
+    from transformers import PreTrainedTokenizerFast
+    tk = Tokenizer(models.BPE())
+    tk.pre_tokenizer = pre_tokenizers.ByteLevel(add_prefix_space=False)
+    tk.decoder = decoders.ByteLevel()
+    trainer = trainers.BpeTrainer(vocab_size=300, special_tokens=["<|bos|>", "<|eot|>"],
+                                  initial_alphabet=pre_tokenizers.ByteLevel.alphabet())
+    tk.train_from_iterator(["hello world", "the cat sat", "ok ok ok"], trainer)
+    fast = PreTrainedTokenizerFast(tokenizer_object=tk, bos_token="<|bos|>", eos_token="<|eot|>")
+    fast.chat_template = ("{% for m in messages %}{{ m['role'] }}: {{ m['content'] }}<|eot|>{% endfor %}"
+                          "{% if add_generation_prompt %}assistant: {% endif %}")
+    fast.save_pretrained(str(tmp_path))
+    return str(tmp_path)
+
+
+class _ScriptStepper(RuleStepper):
+    """Emits a fixed continuation, whatever the prompt."""
+
+    def __init__(self, script):
+        super().__init__(vocab_size=100000)
+        self.script = list(script)
+        self.pos = {}
+
+    def _step(self, kind, rids, seqs):
+        out = []
+        for r, s in zip(rids, seqs):
+            i = self.pos.get(r, 0)
+            self.pos[r] = i + 1
+            self.held[r] = len(s)
+            out.append(self.script[min(i, len(self.script) - 1)])
+        return out
+
+
+def test_streamed_text_keeps_multibyte_characters_whole_and_drops_eos(tmp_path):
+    from connex_b200.serve.api import HFCodec
+    codec = HFCodec(_tiny_bpe_dir(tmp_path))
+    want = "héllo ✓ wörld ok"
+    ids = codec.encode(want, add_special=False)
+    # the characters outside the training text are split over several byte ids
+    assert any("�" in codec.tok.decode([t]) for t in ids)
+    script = ids + [codec.eos_id]
+
+    async def main():
+        eng = GenerationEngine(_ScriptStepper(script)).start()
+        runner, url = await _serve(Server(eng, "m", codec=codec).app())
+        try:
+            async with aiohttp.ClientSession() as s:
+                async with s.post(url + "/v1/completions", json={"prompt": "the cat", "max_tokens": 64}) as r:
+                    body = await r.json()
+                chunks, done = await _stream(url, "/v1/completions", {"prompt": "the cat", "max_tokens": 64})
+                assert done
+                async with s.post(url + "/v1/chat/completions", json={
+                        "messages": [{"role": "user", "content": "hello"}], "max_tokens": 64}) as r:
+                    chat = await r.json()
+        finally:
+            await runner.cleanup()
+            eng.stop()
+        return body, chunks, chat
+    body, chunks, chat = asyncio.run(main())
+    assert body["choices"][0]["text"] == want and body["choices"][0]["finish_reason"] == "stop"
+    streamed = [c["choices"][0]["text"] for c in chunks if c.get("choices")]
+    assert "".join(streamed) == want
+    assert all("�" not in t for t in streamed)
+    assert chunks[-1]["choices"][0]["finish_reason"] == "stop"
+    assert chat["choices"][0]["message"]["content"] == want and "<|eot|>" not in chat["choices"][0]["message"]["content"]
+
+
+def test_incremental_detokenizer_matches_a_whole_decode(tmp_path):
+    from connex_b200.serve.api import HFCodec
+    codec = HFCodec(_tiny_bpe_dir(tmp_path))
+    text = "a ✓✓ é b — the cat sat 漢字 ok"
+    ids = codec.encode(text, add_special=False)
+    dt = codec.stream()
+    parts = [dt.feed(t) for t in ids] + [dt.flush()]
+    assert "".join(parts) == codec.decode(ids) == text
+    assert all("�" not in p for p in parts)

@@ -14,6 +14,8 @@ import torch
 
 pytestmark = pytest.mark.gpu
 
+ERR_TOO_LARGE, ERR_ARGS = -1, -3
+
 
 def _lib():
     from connex_b200 import _C
@@ -50,23 +52,43 @@ def _call(lib, q, kc, vc, bt, cl, Hq, Hkv, BS, out, max_ctx):
                                            Hq, Hkv, BS, max_ctx, 1.0 / 128 ** 0.5, stream)
 
 
-def test_noalloc_matches_allocating_entry_point_twice():
+def _check(lib, dev, seed, ctx, G, max_ctx=None):
+    """One call of the allocation-free entry point against the allocating
+    entry point and the fp32 oracle."""
     from connex_b200 import ops
+    from connex_b200.ops.reference import paged_decode_attention
+    q, kc, vc, bt, cl, Hq, Hkv, BS = _case(dev, seed, ctx, G)
+    max_ctx = max_ctx or max(ctx)
+    ws = ops.decode_workspace(len(ctx), Hq, max_ctx, dev)
+    ref = ops.decode_attention(q, kc, vc, bt, cl, Hq, max_ctx, ws)
+    out = torch.full((len(ctx), Hq * 128), float("nan"), dtype=torch.bfloat16, device=dev)
+    rc = _call(lib, q, kc, vc, bt, cl, Hq, Hkv, BS, out, max_ctx)
+    assert rc == 0, lib.cx_noalloc_error_string(rc).decode()
+    torch.cuda.synchronize(dev)
+    err = (out.float() - ref.float()).abs().max().item()
+    scale = ref.float().abs().max().item() + 1e-6
+    assert err <= 2e-2 + 2e-2 * scale, f"vs allocating path: max err {err} vs scale {scale}"
+    oracle = paged_decode_attention(q[:, :Hq * 128].float().view(len(ctx), Hq, 128), kc.float(), vc.float(),
+                                    bt.long(), cl.long())
+    err32 = (out.float().view_as(oracle) - oracle).abs().max().item()
+    assert err32 <= 2e-2 + 2e-2 * oracle.abs().max().item(), f"vs fp32 oracle: max err {err32}"
+
+
+def test_noalloc_matches_allocating_entry_point_twice():
     dev = torch.device("cuda", 0)
     lib = _lib()
     # two calls in a row, different sizes: the second reuses the scratch the first left behind
     for seed, ctx, G in [(1, [5, 700, 3000, 1200], 4), (2, [2100, 33], 8)]:
-        q, kc, vc, bt, cl, Hq, Hkv, BS = _case(dev, seed, ctx, G)
-        max_ctx = max(ctx)
-        ws = ops.decode_workspace(len(ctx), Hq, max_ctx, dev)
-        ref = ops.decode_attention(q, kc, vc, bt, cl, Hq, max_ctx, ws)
-        out = torch.full((len(ctx), Hq * 128), float("nan"), dtype=torch.bfloat16, device=dev)
-        rc = _call(lib, q, kc, vc, bt, cl, Hq, Hkv, BS, out, max_ctx)
-        assert rc == 0, lib.cx_noalloc_error_string(rc).decode()
-        torch.cuda.synchronize()
-        err = (out.float() - ref.float()).abs().max().item()
-        scale = ref.float().abs().max().item() + 1e-6
-        assert err <= 2e-2 + 2e-2 * scale, f"max err {err} vs scale {scale}"
+        _check(lib, dev, seed, ctx, G)
+
+
+@pytest.mark.parametrize("G", [1, 2, 4, 8])
+def test_noalloc_every_gqa_group(G):
+    lib = _lib()
+    dev = torch.device("cuda", 0)
+    _check(lib, dev, 10 + G, [1, 17, 900], G)                  # one sequence per split regime
+    # every sequence shorter than max_ctx: each split holds fewer live keys than its length
+    _check(lib, dev, 20 + G, [40, 300, 129], G, max_ctx=2048)
 
 
 def test_noalloc_rejects_sizes_beyond_its_scratch():
@@ -77,5 +99,25 @@ def test_noalloc_rejects_sizes_beyond_its_scratch():
     huge_ctx = 1 << 22  # needs far more than the built-in scratch
     assert lib.cx_decode_attention_noalloc_scratch_floats(2, Hq, huge_ctx) > (1 << 20)
     rc = _call(lib, q, kc, vc, bt, cl, Hq, Hkv, BS, out, huge_ctx)
-    assert rc == -1
+    assert rc == ERR_TOO_LARGE
     assert b"scratch" in lib.cx_noalloc_error_string(rc)
+
+
+def test_noalloc_rejects_unsupported_head_layouts():
+    lib = _lib()
+    dev = torch.device("cuda", 0)
+    q, kc, vc, bt, cl, Hq, Hkv, BS = _case(dev, 4, [64, 64], 4)
+    out = torch.empty(2, Hq * 128, dtype=torch.bfloat16, device=dev)
+    assert _call(lib, q, kc, vc, bt, cl, 6, 4, BS, out, 64) == ERR_ARGS        # Hq not a multiple of Hkv
+    assert _call(lib, q, kc, vc, bt, cl, 32, 2, BS, out, 64) == ERR_ARGS       # GQA group 16
+    assert b"GQA" in lib.cx_noalloc_error_string(ERR_ARGS)
+
+
+def test_noalloc_second_device_has_its_own_scratch():
+    if torch.cuda.device_count() < 2:
+        pytest.skip("needs a second GPU")
+    lib = _lib()
+    _check(lib, torch.device("cuda", 0), 5, [300, 40], 4)
+    with torch.cuda.device(1):
+        _check(lib, torch.device("cuda", 1), 6, [1000, 7], 8)     # resolves device 1's copy of the array
+    _check(lib, torch.device("cuda", 0), 7, [64], 2)
