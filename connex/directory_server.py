@@ -1,21 +1,33 @@
 """In-memory directory service: ZeroMQ ROUTER for requests, PUB for events.
 
-Speaks the :mod:`connex.directory` msgpack protocol (the reference's
-``connex/directory_server.py:48-241``): a global epoch is bumped on every
-membership change and returned in replies; every change is published as
-``{"event", "endpoint", "epoch", "reason"}`` with reasons ``deregister``,
-``reported`` or ``expired``.  Leases (``lease_s``) apply only to members that
-have heartbeated at least once.
+It speaks the msgpack protocol of :mod:`connex.directory` (wire parity with
+``connex/directory_server.py:8-22`` of the reference):
+
+* requests ``{"type": ...}`` -- ``register`` (event JOIN / MIGRATE / LEAVE),
+  ``heartbeat``, ``report_failure``, ``lookup``, ``list_stage``,
+  ``request_assignment``, ``info``; every reply carries ``status`` and the
+  directory ``epoch``;
+* events ``{"event", "endpoint", "epoch", "reason"}`` on the PUB socket, one
+  per membership change, with reasons ``deregister`` / ``reported`` /
+  ``expired`` for removals.
+
+The membership itself is :class:`MembershipTable`, a plain object without
+sockets: one epoch counter bumped by every change, the events not yet
+published, and leases kept as a deadline heap (only members that have
+heartbeated at least once hold a lease; each heartbeat pushes a new
+deadline and older heap entries of that member are skipped when they
+surface).  :class:`DirectoryServer` runs the table behind the two sockets.
 
     python -m connex.directory_server --bind 127.0.0.1:5555
 """
 from __future__ import annotations
 
 import argparse
+import heapq
 import logging
 import threading
 import time
-from typing import Any, Optional
+from typing import Callable, Dict, List, Optional, Tuple
 
 import msgpack
 import zmq
@@ -23,6 +35,70 @@ import zmq
 from connex.directory import MembershipEvent
 
 logger = logging.getLogger("connex.directory_server")
+
+Key = Tuple
+
+
+class MembershipTable:
+    """Members by LID tuple, the directory epoch and the outgoing events."""
+
+    def __init__(self, lease_s: float, clock: Callable[[], float] = time.monotonic):
+        self.lease_s = lease_s
+        self.clock = clock
+        self.epoch = 0
+        self.members: Dict[Key, dict] = {}
+        self._deadline: Dict[Key, float] = {}          # current lease per heartbeating member
+        self._heap: List[Tuple[float, Key]] = []
+        self.pending: List[dict] = []
+
+    # -------------------------------------------------------------- changes
+    def _changed(self, event: str, endpoint: dict, reason: str) -> None:
+        self.epoch += 1
+        self.pending.append({"event": event, "endpoint": endpoint, "epoch": self.epoch, "reason": reason})
+
+    def _renew(self, key: Key) -> None:
+        due = self.clock() + self.lease_s
+        self._deadline[key] = due
+        heapq.heappush(self._heap, (due, key))
+
+    def put(self, endpoint: dict, event: str) -> None:
+        key = tuple(endpoint["lid"])
+        self.members[key] = endpoint
+        if key in self._deadline:           # re-registration of a heartbeating member renews its lease
+            self._renew(key)
+        self._changed(event, endpoint, "")
+
+    def drop(self, key: Key, reason: str) -> bool:
+        self._deadline.pop(key, None)
+        endpoint = self.members.pop(key, None)
+        if endpoint is None:
+            return False
+        self._changed(MembershipEvent.LEAVE.value, endpoint, reason)
+        logger.info("LEAVE %s (%s, epoch %d)", key, reason, self.epoch)
+        return True
+
+    def heartbeat(self, key: Key) -> bool:
+        if key not in self.members:
+            return False
+        self._renew(key)
+        return True
+
+    def expire(self) -> int:
+        """Remove members whose lease ran out; returns how many."""
+        now, n = self.clock(), 0
+        while self._heap and self._heap[0][0] < now:
+            due, key = heapq.heappop(self._heap)
+            if self._deadline.get(key) == due:      # not renewed since this entry was pushed
+                n += self.drop(key, "expired")
+        return n
+
+    def take_events(self) -> List[dict]:
+        out, self.pending = self.pending, []
+        return out
+
+    # -------------------------------------------------------------- queries
+    def stage(self, model: str, stage: int) -> List[Tuple[Key, dict]]:
+        return sorted((k, ep) for k, ep in self.members.items() if k[0] == model and k[1] == stage)
 
 
 class DirectoryServer:
@@ -32,17 +108,22 @@ class DirectoryServer:
         host, port = bind_addr.rsplit(":", 1)
         self.event_bind_addr = event_bind_addr or f"{host}:{int(port) + 1}"
         self.lease_s = lease_s
-        self.epoch = 0
-        self._endpoints: dict = {}
-        self._last_seen: dict = {}
-        self._outbox: list = []
+        self.table = MembershipTable(lease_s)
         self._lock = threading.Lock()
         self._stop = threading.Event()
         self._ready = threading.Event()
         self._thread: Optional[threading.Thread] = None
         self._bind_error: Optional[BaseException] = None
+        self._ops = {"register": self._op_register, "heartbeat": self._op_heartbeat,
+                     "report_failure": self._op_report_failure, "lookup": self._op_lookup,
+                     "list_stage": self._op_list_stage, "request_assignment": self._op_assignment,
+                     "info": self._op_info}
 
-    # ------------------------------------------------------------ control
+    @property
+    def epoch(self) -> int:
+        return self.table.epoch
+
+    # ------------------------------------------------------------- lifecycle
     def start(self) -> None:
         self._thread = threading.Thread(target=self.serve_forever, daemon=True, name="connex-directory")
         self._thread.start()
@@ -57,124 +138,99 @@ class DirectoryServer:
 
     def members(self) -> dict:
         with self._lock:
-            return dict(self._endpoints)
+            return dict(self.table.members)
 
-    def serve_forever(self) -> None:
+    def _open(self):
         ctx = zmq.Context.instance()
-        sock, pub = ctx.socket(zmq.ROUTER), ctx.socket(zmq.PUB)
-        for s in (sock, pub):
+        router, pub = ctx.socket(zmq.ROUTER), ctx.socket(zmq.PUB)
+        for s in (router, pub):
             s.setsockopt(zmq.LINGER, 0)
         try:
-            sock.bind(f"tcp://{self.bind_addr}")
+            router.bind(f"tcp://{self.bind_addr}")
             pub.bind(f"tcp://{self.event_bind_addr}")
+        except zmq.ZMQError as e:
+            router.close()
+            pub.close()
+            raise e
+        return router, pub
+
+    def _answer(self, frames) -> bytes:
+        try:
+            reply = self.handle(msgpack.unpackb(frames[-1], raw=False))
+        except Exception as e:  # noqa: BLE001 - a malformed request gets an error reply
+            reply = {"status": "error", "error": str(e)}
+        return msgpack.packb(reply, use_bin_type=True)
+
+    def serve_forever(self) -> None:
+        try:
+            router, pub = self._open()
         except zmq.ZMQError as e:
             self._bind_error = e
             self._ready.set()
-            sock.close()
-            pub.close()
             return
         self._ready.set()
-        tick_ms = int(1000 * min(0.05, self.lease_s / 4))
+        poll_ms = int(1000 * min(0.05, self.lease_s / 4))
         try:
             while not self._stop.is_set():
-                if sock.poll(tick_ms):
-                    while True:  # drain the burst before publishing
+                if router.poll(poll_ms):
+                    # answer the whole burst, then publish its events together
+                    while True:
                         try:
-                            frames = sock.recv_multipart(zmq.NOBLOCK)
+                            frames = router.recv_multipart(zmq.NOBLOCK)
                         except zmq.Again:
                             break
-                        try:
-                            resp = self.handle(msgpack.unpackb(frames[-1], raw=False))
-                        except Exception as e:
-                            resp = {"status": "error", "error": str(e)}
-                        sock.send_multipart([frames[0], msgpack.packb(resp, use_bin_type=True)])
-                self._expire_leases()
+                        router.send_multipart([frames[0], self._answer(frames)])
                 with self._lock:
-                    out, self._outbox = self._outbox, []
-                for ev in out:
+                    self.table.expire()
+                    events = self.table.take_events()
+                for ev in events:
                     pub.send(msgpack.packb(ev, use_bin_type=True))
         finally:
-            sock.close()
+            router.close()
             pub.close()
 
-    # ----------------------------------------------------------- handlers
+    # -------------------------------------------------------------- requests
     def handle(self, req: dict) -> dict:
-        kind = req.get("type")
-        if kind == "register":
-            return self._register(req)
-        if kind == "heartbeat":
-            return self._heartbeat(tuple(req["lid"]))
-        if kind == "report_failure":
-            with self._lock:
-                ok = self._remove(tuple(req["lid"]), "reported")
-                return {"status": "ok" if ok else "not_found", "epoch": self.epoch}
-        if kind == "lookup":
-            with self._lock:
-                ep = self._endpoints.get(tuple(req["lid"]))
-                if ep is None:
-                    return {"status": "not_found", "epoch": self.epoch}
-                return {"status": "ok", "endpoint": ep, "epoch": self.epoch}
-        if kind == "list_stage":
-            with self._lock:
-                eps = [ep for lid, ep in sorted(self._endpoints.items())
-                       if lid[0] == req["model"] and lid[1] == req["stage"]]
-                return {"status": "ok", "endpoints": eps, "epoch": self.epoch}
-        if kind == "request_assignment":
-            return self._assignment(req)
-        if kind == "info":
-            return {"status": "ok", "event_address": self.event_bind_addr, "lease_s": self.lease_s,
-                    "epoch": self.epoch}
-        return {"status": "error", "error": f"unknown request type {kind!r}"}
+        op = self._ops.get(req.get("type"))
+        if op is None:
+            return {"status": "error", "error": f"unknown request type {req.get('type')!r}"}
+        with self._lock:
+            return op(req)
 
-    def _publish(self, event: str, ep: dict, reason: str) -> None:
-        self.epoch += 1
-        self._outbox.append({"event": event, "endpoint": ep, "epoch": self.epoch, "reason": reason})
+    def _reply(self, ok: bool, **extra) -> dict:
+        return {"status": "ok" if ok else "not_found", "epoch": self.table.epoch, **extra}
 
-    def _remove(self, lid: tuple, reason: str) -> bool:  # lock held
-        ep = self._endpoints.pop(lid, None)
-        self._last_seen.pop(lid, None)
-        if ep is None:
-            return False
-        self._publish(MembershipEvent.LEAVE.value, ep, reason)
-        logger.info("LEAVE %s (%s, epoch %d)", lid, reason, self.epoch)
-        return True
-
-    def _register(self, req: dict) -> dict:
+    def _op_register(self, req: dict) -> dict:
         ep = req["endpoint"]
-        lid = tuple(ep["lid"])
         event = req.get("event", MembershipEvent.JOIN.value)
-        with self._lock:
-            if event == MembershipEvent.LEAVE.value:
-                ok = self._remove(lid, "deregister")
-                return {"status": "ok" if ok else "not_found", "epoch": self.epoch}
-            self._endpoints[lid] = ep
-            if lid in self._last_seen:
-                self._last_seen[lid] = time.monotonic()
-            self._publish(event, ep, "")
-            return {"status": "ok", "epoch": self.epoch}
+        if event == MembershipEvent.LEAVE.value:
+            return self._reply(self.table.drop(tuple(ep["lid"]), "deregister"))
+        self.table.put(ep, event)
+        return self._reply(True)
 
-    def _heartbeat(self, lid: tuple) -> dict:
-        with self._lock:
-            if lid not in self._endpoints:
-                return {"status": "not_found", "epoch": self.epoch}
-            self._last_seen[lid] = time.monotonic()
-            return {"status": "ok", "epoch": self.epoch}
+    def _op_heartbeat(self, req: dict) -> dict:
+        return self._reply(self.table.heartbeat(tuple(req["lid"])))
 
-    def _expire_leases(self) -> None:
-        now = time.monotonic()
-        with self._lock:
-            for lid in [l for l, t in self._last_seen.items() if now - t > self.lease_s]:
-                self._remove(lid, "expired")
+    def _op_report_failure(self, req: dict) -> dict:
+        return self._reply(self.table.drop(tuple(req["lid"]), "reported"))
 
-    def _assignment(self, req: dict) -> dict:
-        model, stage = req.get("model"), req.get("target_stage")
-        with self._lock:
-            cands = sorted(l for l in self._endpoints if l[0] == model and l[1] == stage)
-            if not cands:
-                return {"status": "not_found", "epoch": self.epoch}
-            ep = self._endpoints[cands[0]]
-            return {"status": "ok", "endpoint": ep["addresses"][0] if ep["addresses"] else "",
-                    "routing_key": "-".join(str(x) for x in cands[0]), "epoch": self.epoch}
+    def _op_lookup(self, req: dict) -> dict:
+        ep = self.table.members.get(tuple(req["lid"]))
+        return self._reply(True, endpoint=ep) if ep is not None else self._reply(False)
+
+    def _op_list_stage(self, req: dict) -> dict:
+        return self._reply(True, endpoints=[ep for _, ep in self.table.stage(req["model"], req["stage"])])
+
+    def _op_assignment(self, req: dict) -> dict:
+        found = self.table.stage(req.get("model"), req.get("target_stage"))
+        if not found:
+            return self._reply(False)
+        key, ep = found[0]
+        return self._reply(True, endpoint=ep["addresses"][0] if ep["addresses"] else "",
+                           routing_key="-".join(str(x) for x in key))
+
+    def _op_info(self, req: dict) -> dict:
+        return self._reply(True, event_address=self.event_bind_addr, lease_s=self.lease_s)
 
 
 def main() -> None:

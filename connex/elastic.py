@@ -1,35 +1,89 @@
 """ElasticPeerSet: directory membership turned into connected, routable peers.
 
-Semantics (the reference's ``connex/elastic.py:49-261``):
+Every LID of the watched stage has one :class:`_Peer` record holding the
+address the directory lists for it, the endpoint currently connected (and
+its address), and a *generation* number.  Every change of the listed
+address and every removal bumps the generation; a connect attempt carries
+the generation it was started for and its result is kept only if that is
+still current, so a connect that completes after the LID left or moved
+again is closed instead of routed (the stale-connect guard).
 
-* JOIN / MIGRATE -- the new address is connected on a background pool and
-  becomes routable only once connected; a connect that finishes after the
-  LID left or moved again is discarded (stale-connect guard); a migrated
-  LID's old endpoint is drained, then closed.
-* LEAVE (deregister / lease expiry / reported failure) -- unroutable at once;
-  the endpoint closes after ``drain_grace_s`` unless the same endpoint is in
-  use again (transports cache endpoints per address, so a same-address
-  rejoin can share it).
-* send failure -- ``mark_failed``: drop locally, ``report_failure`` to the
-  directory (which tells every other sender), close.
-* membership comes from directory push events, else from polling
-  ``list_stage`` every ``poll_s`` on a private client.
+* JOIN / MIGRATE: the new address is connected on a worker pool; the LID
+  becomes routable (or switches endpoint) only once connected.  An endpoint
+  replaced by a migration is drained for ``drain_grace_s``, then closed.
+* LEAVE (deregister, lease expiry, reported failure): unroutable at once;
+  its endpoint is drained, then closed -- unless it is in use again by then
+  (transports cache endpoints per address, so a same-address rejoin may
+  share it).
+* A failed send calls :meth:`ElasticPeerSet.mark_failed`: the peer is
+  dropped here and reported to the directory, which tells every other
+  sender.
+* Membership arrives as directory push events; without them a private
+  client polls ``list_stage`` every ``poll_s``.
 
-``transport`` needs ``connect_sync(host, port)``, ``send_sync(ep, data, tag)``
-and ``close_endpoint(ep)``; :class:`ZmqTransport` is the CPU one and
-:class:`connex_b200.engine.CxEngineTransport` the native one.
+Draining endpoints sit in one deadline queue served by a single reaper
+thread.  ``transport`` needs ``connect_sync(host, port)``, ``send_sync(ep,
+data, tag)`` and ``close_endpoint(ep)``: :class:`ZmqTransport` is the CPU
+one, :class:`connex_b200.engine.CxEngineTransport` the native one.
+Behavioural parity: ``connex/elastic.py:49-327`` of the reference.
 """
 from __future__ import annotations
 
+import heapq
+import itertools
 import logging
 import threading
 import time
 from concurrent.futures import ThreadPoolExecutor
-from typing import Any, Optional
+from dataclasses import dataclass
+from typing import Any, Dict, List, Optional, Tuple
 
 from connex.directory import DirectoryClient, EndpointInfo, MembershipEvent
 
 logger = logging.getLogger("connex.elastic")
+
+
+@dataclass
+class _Peer:
+    listed: Optional[str] = None       # the address the directory lists
+    generation: int = 0
+    endpoint: Any = None               # connected endpoint (routable when set)
+    connected_to: Optional[str] = None
+
+
+class _Reaper:
+    """Closes endpoints once their drain deadline passes, unless ``keep(ep)``
+    says they are in use again by then."""
+
+    def __init__(self, close, keep):
+        self._close, self._keep = close, keep
+        self._heap: List[Tuple[float, int, Any]] = []
+        self._cv = threading.Condition()
+        self._seq = itertools.count()
+        self._done = False
+        self._thread = threading.Thread(target=self._run, daemon=True, name="connex-peer-drain")
+        self._thread.start()
+
+    def later(self, ep: Any, delay_s: float) -> None:
+        with self._cv:
+            heapq.heappush(self._heap, (time.monotonic() + delay_s, next(self._seq), ep))
+            self._cv.notify()
+
+    def stop(self) -> None:
+        with self._cv:
+            self._done = True
+            self._cv.notify()
+
+    def _run(self) -> None:
+        while True:
+            with self._cv:
+                while not self._done and (not self._heap or self._heap[0][0] > time.monotonic()):
+                    self._cv.wait(None if not self._heap else max(0.0, self._heap[0][0] - time.monotonic()))
+                if self._done:
+                    return
+                _, _, ep = heapq.heappop(self._heap)
+            if not self._keep(ep):
+                self._close(ep)
 
 
 class ElasticPeerSet:
@@ -40,67 +94,70 @@ class ElasticPeerSet:
         self.stage_idx = stage_idx
         self.drain_grace_s = drain_grace_s
         self.poll_s = poll_s
-        self._lock = threading.Lock()
-        self._cv = threading.Condition(self._lock)
-        self._ready: dict = {}    # lid -> (endpoint, address)
-        self._wanted: dict = {}   # lid -> address we should be connected to
-        self._order: list = []    # routable lids, sorted
-        self._rr = 0
+        self._cv = threading.Condition()
+        self._peers: Dict[tuple, _Peer] = {}
+        self._gen = itertools.count(1)
+        self._turn = itertools.count()
         self._pool = ThreadPoolExecutor(max_workers=connect_workers, thread_name_prefix="connex-peer")
-        self._stop = threading.Event()
-        self._push = False
-        self._closed_on_stop: list = []
+        self._stopped = threading.Event()
+        self._retired: List[Any] = []           # endpoints closed by stop()
+        self._reaper = _Reaper(self._close, self._in_use)
         self.stats = {"connects": 0, "connect_ms_total": 0.0, "failures": 0, "leaves": 0}
 
-    # ---------------------------------------------------------- lifecycle
+    # ------------------------------------------------------------ lifecycle
     def start(self) -> None:
         self.directory.subscribe_events(self._on_event)
-        self._push = self.directory.start_event_listener()
-        self._sync(self.directory.list_stage(self.stage_idx))  # snapshot after subscribing
-        if not self._push:
-            threading.Thread(target=self._poll_loop, daemon=True, name="connex-peer-poll").start()
+        pushed = self.directory.start_event_listener()
+        self._reconcile(self.directory.list_stage(self.stage_idx))   # snapshot after subscribing
+        if not pushed:
+            threading.Thread(target=self._poll, daemon=True, name="connex-peer-poll").start()
 
     def stop(self) -> None:
-        self._stop.set()
-        with self._lock:
-            eps = [ep for ep, _ in self._ready.values()]
-            self._ready.clear()
-            self._wanted.clear()
-            self._order = []
-            self._closed_on_stop = eps
+        self._stopped.set()
+        with self._cv:
+            eps = [p.endpoint for p in self._peers.values() if p.endpoint is not None]
+            self._peers.clear()
+            self._retired = eps
+            self._cv.notify_all()
         for ep in eps:
             self._close(ep)
+        self._reaper.stop()
         self._pool.shutdown(wait=False)
 
-    # -------------------------------------------------------------- query
+    # ---------------------------------------------------------------- views
+    def _routable(self) -> List[tuple]:          # lock held
+        return sorted(lid for lid, p in self._peers.items() if p.endpoint is not None)
+
     def peers(self) -> list:
-        with self._lock:
-            return list(self._order)
+        with self._cv:
+            return self._routable()
 
     def wait_ready(self, n: int = 1, timeout: float = 30.0) -> bool:
-        deadline = time.monotonic() + timeout
         with self._cv:
-            while len(self._order) < n:
-                left = deadline - time.monotonic()
-                if left <= 0:
-                    return False
-                self._cv.wait(left)
-            return True
+            return self._cv.wait_for(lambda: len(self._routable()) >= n, timeout)
 
     def pick(self) -> Optional[tuple]:
-        with self._lock:
-            if not self._order:
-                return None
-            lid = self._order[self._rr % len(self._order)]
-            self._rr += 1
-            return lid
+        """Round-robin over the routable peers."""
+        with self._cv:
+            ready = self._routable()
+            return ready[next(self._turn) % len(ready)] if ready else None
 
     def endpoint(self, lid: tuple) -> Optional[Any]:
-        with self._lock:
-            e = self._ready.get(lid)
-            return e[0] if e else None
+        with self._cv:
+            p = self._peers.get(lid)
+            return p.endpoint if p is not None else None
 
-    # --------------------------------------------------------------- data
+    def address(self, lid: tuple) -> Optional[str]:
+        """The address ``lid``'s routable endpoint is connected to, or None."""
+        with self._cv:
+            p = self._peers.get(lid)
+            return p.connected_to if p is not None and p.endpoint is not None else None
+
+    def _in_use(self, ep: Any) -> bool:
+        with self._cv:
+            return any(p.endpoint is ep for p in self._peers.values()) or any(e is ep for e in self._retired)
+
+    # ----------------------------------------------------------------- data
     def send(self, lid: tuple, data: Any, tag: int = 0) -> None:
         ep = self.endpoint(lid)
         if ep is None:
@@ -112,126 +169,113 @@ class ElasticPeerSet:
             raise
 
     def mark_failed(self, lid: tuple) -> None:
-        with self._lock:
-            entry = self._ready.pop(lid, None)
-            self._wanted.pop(lid, None)
-            self._reorder()
+        """Drop a peer a send failed on and report it to the directory."""
+        with self._cv:
+            p = self._peers.pop(lid, None)
+            self._cv.notify_all()
         self.stats["failures"] += 1
         logger.warning("peer %s failed: removed and reported", lid)
         self.directory.report_failure(lid)
-        if entry is not None:
+        if p is not None and p.endpoint is not None:
             try:
-                self._pool.submit(self._close, entry[0])
-            except RuntimeError:
-                self._close(entry[0])
+                self._pool.submit(self._close, p.endpoint)
+            except RuntimeError:          # pool already shut down
+                self._close(p.endpoint)
 
-    # ----------------------------------------------------------- internal
-    def _reorder(self) -> None:  # lock held
-        self._order = sorted(self._ready)
-        self._cv.notify_all()
-
+    # ----------------------------------------------------------- membership
     def _on_event(self, event: MembershipEvent, info: EndpointInfo) -> None:
         if info.stage != self.stage_idx or info.model != self.directory.model_name:
             return
         if event == MembershipEvent.LEAVE:
-            self._remove(info.lid)
+            self._forget(info.lid)
         elif info.addresses:
-            self._want(info.lid, info.primary_address)
+            self._track(info.lid, info.primary_address)
 
-    def _sync(self, members: list) -> None:
-        current = {m.lid: m.primary_address for m in members if m.addresses}
-        with self._lock:
-            gone = [l for l in self._wanted if l not in current]
+    def _reconcile(self, members: list) -> None:
+        listed = {m.lid: m.primary_address for m in members if m.addresses}
+        with self._cv:
+            gone = [lid for lid in self._peers if lid not in listed]
         for lid in gone:
-            self._remove(lid)
-        for lid, addr in current.items():
-            self._want(lid, addr)
+            self._forget(lid)
+        for lid, addr in listed.items():
+            self._track(lid, addr)
 
-    def _poll_loop(self) -> None:
+    def _poll(self) -> None:
         client = DirectoryClient(self.directory.front_router_addr, self.directory.model_name,
                                  stage_idx=-1, replica_idx=id(self) & 0xFFFF)
         client.start()
         try:
-            while not self._stop.wait(self.poll_s):
-                self._sync(client.list_stage(self.stage_idx))
+            while not self._stopped.wait(self.poll_s):
+                self._reconcile(client.list_stage(self.stage_idx))
         finally:
             client.stop()
 
-    def _want(self, lid: tuple, addr: str) -> None:
-        with self._lock:
-            if self._stop.is_set() or self._wanted.get(lid) == addr:
+    def _track(self, lid: tuple, addr: str) -> None:
+        """The directory lists ``lid`` at ``addr``: connect unless already there."""
+        with self._cv:
+            if self._stopped.is_set():
                 return
-            self._wanted[lid] = addr
+            p = self._peers.setdefault(lid, _Peer())
+            if p.listed == addr:
+                return
+            p.listed, p.generation = addr, next(self._gen)
+            gen = p.generation
         try:
-            self._pool.submit(self._connect, lid, addr)
+            self._pool.submit(self._dial, lid, addr, gen)
         except RuntimeError:
-            with self._lock:
-                if self._wanted.get(lid) == addr:
-                    del self._wanted[lid]
+            pass                              # stopping
 
-    def _connect(self, lid: tuple, addr: str) -> None:
+    def _forget(self, lid: tuple) -> None:
+        with self._cv:
+            p = self._peers.pop(lid, None)
+            self._cv.notify_all()
+        if p is not None and p.endpoint is not None:
+            self.stats["leaves"] += 1
+            self._reaper.later(p.endpoint, self.drain_grace_s)
+
+    def _dial(self, lid: tuple, addr: str, gen: int) -> None:
         host, port = addr.rsplit(":", 1)
         t0 = time.monotonic()
         try:
             ep = self.transport.connect_sync(host, int(port))
-        except Exception as e:
+        except Exception as e:  # noqa: BLE001 - retried on the next listing of this address
             logger.warning("connect to %s at %s failed: %s", lid, addr, e)
-            with self._lock:
-                if self._wanted.get(lid) == addr:
-                    del self._wanted[lid]
+            with self._cv:
+                p = self._peers.get(lid)
+                if p is not None and p.generation == gen:
+                    p.listed = None
             return
-        old = None
-        with self._lock:
-            stale = self._wanted.get(lid) != addr
-            if not stale:
-                old = self._ready.get(lid)
-                self._ready[lid] = (ep, addr)
-                self._reorder()
-        if stale:
-            self._close(ep)
+        with self._cv:
+            p = self._peers.get(lid)
+            current = p is not None and p.generation == gen
+            if current:
+                replaced, p.endpoint, p.connected_to = p.endpoint, ep, addr
+                self._cv.notify_all()
+        if not current:
+            self._close(ep)                    # the LID left or moved while we dialled
             return
-        dt = (time.monotonic() - t0) * 1000
         self.stats["connects"] += 1
-        self.stats["connect_ms_total"] += dt
-        if old is not None and old[0] is not ep:
-            self._close_later(old[0])
-
-    def _remove(self, lid: tuple) -> None:
-        with self._lock:
-            self._wanted.pop(lid, None)
-            entry = self._ready.pop(lid, None)
-            self._reorder()
-        if entry is not None:
-            self.stats["leaves"] += 1
-            self._close_later(entry[0])
-
-    def _close_later(self, ep: Any) -> None:
-        def run():
-            with self._lock:
-                in_use = any(e is ep for e, _ in self._ready.values())
-                closed = any(e is ep for e in self._closed_on_stop)
-            if not in_use and not closed:
-                self._close(ep)
-        t = threading.Timer(self.drain_grace_s, run)
-        t.daemon = True
-        t.start()
+        self.stats["connect_ms_total"] += (time.monotonic() - t0) * 1000
+        if replaced is not None and replaced is not ep:
+            self._reaper.later(replaced, self.drain_grace_s)
 
     def _close(self, ep: Any) -> None:
         try:
             self.transport.close_endpoint(ep)
-        except Exception as e:
+        except Exception as e:  # noqa: BLE001
             logger.debug("close_endpoint failed: %s", e)
 
 
 class ZmqTransport:
-    """CPU PUSH/PULL transport with endpoints cached by address."""
+    """CPU transport: one PULL socket to receive on, one PUSH socket per
+    destination address (shared by every LID at that address)."""
 
     def __init__(self, host: str = "127.0.0.1", port: int = 0):
         import zmq
         self._zmq = zmq
         self._ctx = zmq.Context.instance()
         self._lock = threading.Lock()
-        self._eps: dict = {}
+        self._by_addr: Dict[Tuple[str, int], Any] = {}
         self._rx = self._ctx.socket(zmq.PULL)
         self._rx.setsockopt(zmq.LINGER, 0)
         if port:
@@ -241,37 +285,37 @@ class ZmqTransport:
             self.local_port = self._rx.bind_to_random_port(f"tcp://{host}")
 
     def start_sync(self) -> None:
-        pass
+        return None
 
     def connect_sync(self, host: str, port: int) -> Any:
         with self._lock:
-            ep = self._eps.get((host, port))
-            if ep is None:
-                ep = self._ctx.socket(self._zmq.PUSH)
-                ep.setsockopt(self._zmq.LINGER, 0)
-                ep.setsockopt(self._zmq.SNDTIMEO, 2000)
-                ep.connect(f"tcp://{host}:{port}")
-                self._eps[(host, port)] = ep
-            return ep
+            sock = self._by_addr.get((host, port))
+            if sock is None:
+                sock = self._ctx.socket(self._zmq.PUSH)
+                sock.setsockopt(self._zmq.LINGER, 0)
+                sock.setsockopt(self._zmq.SNDTIMEO, 2000)
+                sock.connect(f"tcp://{host}:{port}")
+                self._by_addr[(host, port)] = sock
+            return sock
 
     def send_sync(self, ep: Any, data: bytes, tag: int = 0) -> None:
         with self._lock:
             ep.send(data)
 
     def recv_sync(self, timeout_ms: int = 1000) -> Optional[bytes]:
-        return self._rx.recv() if self._rx.poll(timeout_ms) else None
+        if not self._rx.poll(timeout_ms):
+            return None
+        return self._rx.recv()
 
     def close_endpoint(self, ep: Any) -> bool:
         with self._lock:
-            for k, v in list(self._eps.items()):
-                if v is ep:
-                    del self._eps[k]
+            self._by_addr = {k: s for k, s in self._by_addr.items() if s is not ep}
         ep.close(0)
         return True
 
     def stop_sync(self) -> None:
         with self._lock:
-            for ep in self._eps.values():
-                ep.close(0)
-            self._eps.clear()
+            socks, self._by_addr = list(self._by_addr.values()), {}
+        for s in socks:
+            s.close(0)
         self._rx.close(0)

@@ -183,7 +183,7 @@ def run(steps: int = 1000, seed: int = 0, payload_bytes: int = 64, fail_at: int 
             addr = replicas[0].migrate()
             # wait until the sender routes replica 0 to its new address
             deadline = time.monotonic() + 10
-            while time.monotonic() < deadline and peers._ready.get((MODEL, 1, 0, 0), (None, ""))[1] != addr:
+            while time.monotonic() < deadline and peers.address((MODEL, 1, 0, 0)) != addr:
                 time.sleep(0.005)
             replicas[0].close_old()
             events.append({"step": i, "event": "migrate", "replica": 0, "address": addr})

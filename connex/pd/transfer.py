@@ -1,25 +1,37 @@
 """Pull-based KV block transfer between a prefill and a decode instance.
 
-Prefill side :class:`KVProducer`: after a request's prefill it *holds* the
-KV blocks under a transfer id (a lease renewed by every acquire, freed after
-``retain_s`` without one) and serves a ZeroMQ ROUTER control channel with
-msgpack ops (the reference's ``connex/pd/transfer.py:148-195``):
+Prefill side -- :class:`KVProducer`
+    After a request's prefill the engine *holds* its KV blocks under a
+    transfer id.  Holds live in a :class:`LeaseTable`: every ``acquire``
+    renews a hold's lease, a hold nobody acquires for ``retain_s`` expires,
+    and a ``release`` frees it (after all ``of`` readers of a multi-reader
+    TP pull released; a single-reader release from anyone but the last
+    acquirer is ignored as stale -- a replacement decode instance may be
+    re-pulling).  A release that arrives before its hold leaves a tombstone
+    so the late hold is freed at once.  Freed and expired requests are handed
+    back to the engine by :meth:`KVProducer.take_finished`.
 
-* ``{"op": "meta"}``    -> incarnation, data-plane URL / backend, engine id,
-  block size, device, KV layouts (and, for the NVLink plane, the IPC spans);
-* ``{"op": "acquire", "tid", "who"}`` -> the held block ids (renews the lease);
-* ``{"op": "release", "tid", "who", ["of"]}`` -> frees once all ``of`` readers
-  released (stale-owner guard for single-reader releases);
-* ``{"op": "ping"}``.
+    The control channel is a ZeroMQ ROUTER speaking msgpack ``{"op": ...}``:
+    ``meta`` (incarnation, data-plane URL / backend, engine id, block size,
+    device, KV layouts), ``acquire`` (the held block ids), ``release``,
+    ``ping``.  A reply that refers to a host-staging copy still in flight is
+    sent only once that copy has completed.
 
-Decode side :class:`KVConsumer`: acquires (retrying while the hold is still
-unknown), fetches / caches the producer's meta by incarnation, builds the
-fewest one-sided reads (``read_ops`` / ``head_read_ops`` for heterogeneous
-TP), checks that every destination lies in its registered KV memory, reads
-through its data plane, and reports a per-request :class:`PullResult` --
-failures are reported, never raised.  Holding until release (not freeing
-after the first read) lets a replacement decode instance re-pull the prompt
-KV after a decode death instead of re-running prefill.
+Decode side -- :class:`KVConsumer`
+    A pull is a :class:`_PullJob`: acquire (retrying while the producer does
+    not know the transfer yet), pick the remote blocks, fetch the producer's
+    meta (cached per address, refreshed when the producer's incarnation
+    changes), plan the fewest one-sided reads (whole blocks, or a head range
+    for a heterogeneous-TP source), check that every destination lies in the
+    registered KV memory, read, optionally release.  Results come back from
+    :meth:`KVConsumer.take_done` as :class:`PullResult` objects -- a failed
+    pull is reported, never raised.
+
+Keeping a hold until it is released (not freeing it after the first read)
+lets a replacement decode instance re-pull the prompt's KV after a decode
+death instead of re-running the prefill.  Wire parity:
+``connex/pd/transfer.py:148-195`` of the reference (op names, fields and
+reply keys); the decomposition here is this module's own.
 """
 from __future__ import annotations
 
@@ -29,17 +41,17 @@ import threading
 import time
 from concurrent.futures import ThreadPoolExecutor
 from dataclasses import dataclass, field
-from typing import List, Optional, Sequence, Tuple
+from typing import Any, Dict, List, Optional, Sequence, Set, Tuple
 
 import msgpack
 import zmq
 
-from connex.pd.dataplane import ZCOPY_THRESH
 from connex.pd.host_staging import block_ranges, register_with_staging
 from connex.pd.kv_layout import TPSource, TensorLayout, head_read_ops, read_ops, register_spans
 
 log = logging.getLogger("connex.pd")
 PROTO_VERSION = 1
+_TOMBSTONE_CAP = 100_000
 
 
 def _pack(o) -> bytes:
@@ -50,15 +62,135 @@ def _unpack(b: bytes):
     return msgpack.unpackb(b, raw=False)
 
 
+# =========================================================== prefill side
 @dataclass
-class _Hold:
+class Lease:
+    """One held transfer."""
+
     req_id: str
     blocks: List[int]
-    deadline: float
-    acquired: int = 0
-    released_by: set = field(default_factory=set)
-    ready: object = None
-    owner: object = None
+    expires: float
+    staged: Any = None                    # host-staging completion event, if any
+    acquires: int = 0
+    owner: Optional[str] = None           # last acquirer
+    releasers: Set[str] = field(default_factory=set)
+
+
+class LeaseTable:
+    """Held transfers by transfer id, with lease expiry and release rules."""
+
+    def __init__(self, retain_s: float, clock=time.monotonic):
+        self.retain_s = retain_s
+        self.clock = clock
+        self.leases: Dict[str, Lease] = {}
+        self.tombstones: Set[str] = set()       # released before their hold arrived
+        self.freed: Set[str] = set()            # request ids the engine may free
+        self.counts = {"holds": 0, "acquires": 0, "releases": 0, "expired": 0, "unknown": 0}
+
+    def hold(self, tid: str, req_id: str, blocks: Sequence[int], staged=None) -> bool:
+        """False (and the request is freed at once) when already released."""
+        if tid in self.tombstones:
+            self.tombstones.discard(tid)
+            self.freed.add(req_id)
+            return False
+        self.leases[tid] = Lease(req_id, list(blocks), self.clock() + self.retain_s, staged)
+        self.counts["holds"] += 1
+        return True
+
+    def acquire(self, tid: str, who: Optional[str]) -> Optional[Lease]:
+        lease = self.leases.get(tid)
+        if lease is None:
+            self.counts["unknown"] += 1
+            return None
+        lease.acquires += 1
+        lease.owner = who or lease.owner
+        lease.expires = self.clock() + self.retain_s
+        self.counts["acquires"] += 1
+        return lease
+
+    def release(self, tid: str, who: Optional[str], of: int) -> dict:
+        self.counts["releases"] += 1
+        lease = self.leases.get(tid)
+        if lease is None:
+            if len(self.tombstones) >= _TOMBSTONE_CAP:
+                self.tombstones.clear()
+            self.tombstones.add(tid)
+            return {"ok": True}
+        if of <= 1:
+            if who and lease.owner and who != lease.owner:
+                self.counts["stale_releases"] = self.counts.get("stale_releases", 0) + 1
+                return {"ok": True, "stale": True}
+        else:
+            lease.releasers.add(who)
+            if len(lease.releasers) < of:
+                return {"ok": True, "pending": of - len(lease.releasers)}
+        self._free(tid)
+        return {"ok": True}
+
+    def _free(self, tid: str) -> None:
+        self.freed.add(self.leases.pop(tid).req_id)
+
+    def drop(self, tid: str) -> None:
+        self.leases.pop(tid, None)
+
+    def expire(self) -> None:
+        now = self.clock()
+        for tid in [t for t, l in self.leases.items() if l.expires < now]:
+            self._free(tid)
+            self.counts["expired"] += 1
+
+    def take_freed(self) -> Set[str]:
+        out, self.freed = self.freed, set()
+        return out
+
+
+def _event_done(ev) -> bool:
+    try:
+        return bool(ev.query())
+    except Exception:  # noqa: BLE001 - an event without query(): wait for it
+        ev.synchronize()
+        return True
+
+
+class _ControlServer:
+    """ROUTER loop: ``answer(msg) -> (reply, wait_event)``; replies whose
+    event has not completed are held back and sent once it has."""
+
+    def __init__(self, answer, bind_ip: str, port: int):
+        self._answer = answer
+        self.sock = zmq.Context.instance().socket(zmq.ROUTER)
+        self.sock.setsockopt(zmq.LINGER, 0)
+        if port:
+            self.sock.bind(f"tcp://{bind_ip}:{port}")
+            self.port = port
+        else:
+            self.port = self.sock.bind_to_random_port(f"tcp://{bind_ip}")
+        self._stop = threading.Event()
+        self._thread = threading.Thread(target=self._loop, name="connex-pd-producer", daemon=True)
+        self._thread.start()
+
+    def _loop(self) -> None:
+        deferred: List[Tuple[Any, list, dict]] = []
+        while not self._stop.is_set():
+            if self.sock.poll(1 if deferred else 100):
+                *route, body = self.sock.recv_multipart()
+                try:
+                    reply, ev = self._answer(_unpack(body))
+                except Exception as e:  # noqa: BLE001 - a bad request gets an error reply
+                    reply, ev = {"ok": False, "why": f"error: {e}"}, None
+                deferred.append((ev, route, reply))
+            keep = []
+            for ev, route, reply in deferred:
+                if ev is None or _event_done(ev):
+                    self.sock.send_multipart(route + [_pack(reply)])
+                else:
+                    keep.append((ev, route, reply))
+            deferred = keep
+
+    def close(self) -> None:
+        self._stop.set()
+        self._thread.join(timeout=2)
+        self.sock.close(0)
 
 
 class KVProducer:
@@ -72,146 +204,79 @@ class KVProducer:
         self.inc = os.urandom(8).hex()
         self.block_size = block_size
         self.device = device
-        self._holds: dict = {}
-        self._released: set = set()
-        self._finished: set = set()
+        self.table = LeaseTable(retain_s)
         self._lock = threading.Lock()
-        self.stats = {"holds": 0, "acquires": 0, "releases": 0, "expired": 0, "unknown": 0}
         self._staging = register_with_staging(plane, register_spans(self.layouts), "KV producer") if register \
             else getattr(plane, "_connex_staging", None)
-        self._sock = zmq.Context.instance().socket(zmq.ROUTER)
-        self._sock.setsockopt(zmq.LINGER, 0)
-        if port:
-            self._sock.bind(f"tcp://{bind_ip}:{port}")
-            self.port = port
-        else:
-            self.port = self._sock.bind_to_random_port(f"tcp://{bind_ip}")
-        self._stop = threading.Event()
-        self._thread = threading.Thread(target=self._serve, name="connex-pd-producer", daemon=True)
-        self._thread.start()
+        self._server = _ControlServer(self._answer, bind_ip, port)
+        self.port = self._server.port
 
-    # ------------------------------------------------------------- engine
+    @property
+    def stats(self) -> dict:
+        return self.table.counts
+
+    # ----------------------------------------------------------- engine side
     def hold(self, req_id: str, transfer_id: str, blocks: Sequence[int]) -> None:
         with self._lock:
-            if transfer_id in self._released:  # released before the hold arrived
-                self._released.discard(transfer_id)
-                self._finished.add(req_id)
+            if transfer_id in self.table.tombstones:
+                self.table.hold(transfer_id, req_id, blocks)       # frees it at once
                 return
-        ready = self._staging.stage_out(block_ranges(self.layouts, blocks)) if self._staging is not None else None
+        staged = None
+        if self._staging is not None:
+            staged = self._staging.stage_out(block_ranges(self.layouts, blocks))
         with self._lock:
-            self._holds[transfer_id] = _Hold(req_id, list(blocks), time.monotonic() + self.retain_s, ready=ready)
-            self.stats["holds"] += 1
+            self.table.hold(transfer_id, req_id, blocks, staged)
 
     def drop(self, transfer_id: str) -> None:
         with self._lock:
-            self._holds.pop(transfer_id, None)
+            self.table.drop(transfer_id)
 
     def take_finished(self) -> set:
-        """Request ids whose blocks may be freed now (released or lease expired)."""
-        now = time.monotonic()
+        """Request ids whose blocks the engine may free now (released or expired)."""
         with self._lock:
-            for tid, h in list(self._holds.items()):
-                if h.deadline < now:
-                    del self._holds[tid]
-                    self._finished.add(h.req_id)
-                    self.stats["expired"] += 1
-            out, self._finished = self._finished, set()
-        return out
+            self.table.expire()
+            return self.table.take_freed()
 
     def held(self) -> int:
         with self._lock:
-            return len(self._holds)
+            return len(self.table.leases)
 
-    # ----------------------------------------------------------- control
-    def _meta(self) -> dict:
+    # ---------------------------------------------------------- control side
+    def meta(self) -> dict:
+        layouts = [self._staging.translate(lo) if self._staging else lo for lo in self.layouts]
         d = {"ok": True, "v": PROTO_VERSION, "inc": self.inc, "url": self.plane.local_url,
              "backend": self.plane.name, "engine_id": self.engine_id, "block_size": self.block_size,
-             "device": self.device,
-             "layouts": [(self._staging.translate(lo) if self._staging else lo).to_dict() for lo in self.layouts]}
+             "device": self.device, "layouts": [lo.to_dict() for lo in layouts]}
         describe = getattr(self.plane, "describe", None)
         if describe is not None and self._staging is None:
             d["spans"] = describe()
         return d
 
-    def _handle(self, m: dict) -> dict:
+    def _answer(self, m: dict):
         op = m.get("op")
         if op == "meta":
-            return self._meta()
-        tid = m.get("tid")
+            return self.meta(), None
         with self._lock:
-            h = self._holds.get(tid)
             if op == "acquire":
-                if h is None:
-                    self.stats["unknown"] += 1
-                    return {"ok": False, "why": "unknown"}
-                h.acquired += 1
-                if m.get("who"):
-                    h.owner = m.get("who")
-                h.deadline = time.monotonic() + self.retain_s
-                self.stats["acquires"] += 1
-                return {"ok": True, "blocks": h.blocks, "inc": self.inc, "_wait": h.ready}
+                lease = self.table.acquire(m.get("tid"), m.get("who"))
+                if lease is None:
+                    return {"ok": False, "why": "unknown"}, None
+                return {"ok": True, "blocks": lease.blocks, "inc": self.inc}, lease.staged
             if op == "release":
-                self.stats["releases"] += 1
-                of, who = int(m.get("of") or 1), m.get("who")
-                if h is not None and of <= 1 and who and h.owner and who != h.owner:
-                    self.stats["stale_releases"] = self.stats.get("stale_releases", 0) + 1
-                    return {"ok": True, "stale": True}
-                if h is not None and of > 1:
-                    h.released_by.add(who)
-                    if len(h.released_by) < of:
-                        return {"ok": True, "pending": of - len(h.released_by)}
-                if h is None:
-                    self._released.add(tid)
-                    if len(self._released) > 100000:
-                        self._released.clear()
-                else:
-                    del self._holds[tid]
-                    self._finished.add(h.req_id)
-                return {"ok": True}
+                return self.table.release(m.get("tid"), m.get("who"), int(m.get("of") or 1)), None
             if op == "ping":
-                return {"ok": True, "held": len(self._holds)}
-        return {"ok": False, "why": f"bad op {op!r}"}
+                return {"ok": True, "held": len(self.table.leases)}, None
+        return {"ok": False, "why": f"bad op {op!r}"}, None
 
-    @staticmethod
-    def _ready(ev) -> bool:
-        try:
-            return bool(ev.query())
-        except Exception:
-            ev.synchronize()
-            return True
-
-    def _serve(self) -> None:
-        poller = zmq.Poller()
-        poller.register(self._sock, zmq.POLLIN)
-        waiting: list = []  # replies whose staged copy has not finished
-        while not self._stop.is_set():
-            if poller.poll(1 if waiting else 100):
-                frames = self._sock.recv_multipart()
-                env, body = frames[:-1], frames[-1]
-                try:
-                    rep = self._handle(_unpack(body))
-                    ev = rep.pop("_wait", None)
-                except Exception as e:
-                    rep, ev = {"ok": False, "why": f"error: {e}"}, None
-                if ev is not None and not self._ready(ev):
-                    waiting.append((ev, env, rep))
-                else:
-                    self._sock.send_multipart(env + [_pack(rep)])
-            if waiting:
-                still = []
-                for ev, env, rep in waiting:
-                    if self._ready(ev):
-                        self._sock.send_multipart(env + [_pack(rep)])
-                    else:
-                        still.append((ev, env, rep))
-                waiting = still
+    def answer(self, m: dict) -> dict:
+        """Handle one control message in-process (no staging wait)."""
+        return self._answer(m)[0]
 
     def close(self) -> None:
-        self._stop.set()
-        self._thread.join(timeout=2)
-        self._sock.close(0)
+        self._server.close()
 
 
+# ============================================================ decode side
 @dataclass
 class PullResult:
     req_id: str
@@ -223,6 +288,8 @@ class PullResult:
 
 
 class _PeerMeta:
+    """A producer's ``meta`` reply."""
+
     def __init__(self, d: dict):
         self.url = d["url"]
         self.backend = d.get("backend")
@@ -232,6 +299,144 @@ class _PeerMeta:
         self.device = d.get("device", "")
         self.layouts = [TensorLayout.from_dict(x) for x in d["layouts"]]
         self.spans = d.get("spans")
+
+
+class _ControlPool:
+    """REQ sockets per producer address, reused between calls; a socket that
+    timed out or failed is closed (a REQ socket cannot be reused then)."""
+
+    def __init__(self, timeout_ms: int):
+        self.timeout_ms = timeout_ms
+        self._ctx = zmq.Context.instance()
+        self._idle: Dict[str, List[Any]] = {}
+        self._lock = threading.Lock()
+        self._closed = False
+
+    def _socket(self, addr: str):
+        with self._lock:
+            idle = self._idle.get(addr)
+            if idle:
+                return idle.pop()
+        s = self._ctx.socket(zmq.REQ)
+        for opt in (zmq.RCVTIMEO, zmq.SNDTIMEO):
+            s.setsockopt(opt, self.timeout_ms)
+        s.setsockopt(zmq.LINGER, 0)
+        s.connect(f"tcp://{addr}")
+        return s
+
+    def call(self, addr: str, msg: dict) -> Optional[dict]:
+        s = self._socket(addr)
+        try:
+            s.send(_pack(msg))
+            reply = _unpack(s.recv())
+        except zmq.ZMQError:
+            s.close(0)
+            return None
+        except Exception as e:  # noqa: BLE001 - undecodable reply
+            log.warning("PD: bad control reply from %s: %s", addr, e)
+            s.close(0)
+            return None
+        with self._lock:
+            if not self._closed:
+                self._idle.setdefault(addr, []).append(s)
+                return reply
+        s.close(0)
+        return reply
+
+    def forget(self, addr: str) -> None:
+        with self._lock:
+            socks = self._idle.pop(addr, [])
+        for s in socks:
+            s.close(0)
+
+    def close(self) -> None:
+        with self._lock:
+            self._closed = True
+            idle, self._idle = self._idle, {}
+        for socks in idle.values():
+            for s in socks:
+                s.close(0)
+
+
+class _PullFailed(Exception):
+    pass
+
+
+class _PullJob:
+    """One pull from one producer (one TP source when ``src`` is given)."""
+
+    def __init__(self, consumer: "KVConsumer", req_id: str, addr: str, tid: str, local: List[int], first: int,
+                 t0: float, src: Optional[TPSource]):
+        self.c, self.req_id, self.addr, self.tid = consumer, req_id, addr, tid
+        self.local, self.first, self.t0, self.src = local, first, t0, src
+
+    def _acquire(self) -> dict:
+        pause = 0.002
+        while True:
+            r = self.c.control(self.addr, {"op": "acquire", "tid": self.tid, "who": self.c.who})
+            unknown = r is not None and not r.get("ok") and r.get("why") == "unknown"
+            if not unknown or time.monotonic() - self.t0 > self.c.acquire_wait_s:
+                break
+            time.sleep(pause)                 # the hold may not have reached the producer yet
+            pause = min(2 * pause, 0.05)
+        if r is None:
+            self.c.forget_peer(self.addr)
+            raise _PullFailed("producer unreachable")
+        if not r.get("ok"):
+            raise _PullFailed(f"producer: {r.get('why')}")
+        return r
+
+    def _meta(self, inc: Optional[str]) -> _PeerMeta:
+        meta = self.c.peer_meta(self.addr)
+        if meta is not None and inc and meta.inc != inc:
+            meta = self.c.peer_meta(self.addr, refresh=True)     # restarted at the same address
+        if meta is None:
+            raise _PullFailed("producer meta unavailable")
+        if self.c.block_size and meta.block_size and meta.block_size != self.c.block_size:
+            raise _PullFailed(f"block size {meta.block_size} != {self.c.block_size}")
+        return meta
+
+    def _plan(self, meta: _PeerMeta, remote: List[int]) -> list:
+        s = self.src
+        mine, theirs = self.c.layouts[0], meta.layouts[0]
+        partial = s is not None and not (s.nheads == mine.heads == theirs.heads and mine.seg_bytes == theirs.seg_bytes
+                                         and mine.head_stride == theirs.head_stride
+                                         and mine.token_stride == theirs.token_stride)
+        if partial:
+            return head_read_ops(self.c.layouts, meta.layouts, self.local, remote, s.local_head0, s.remote_head0,
+                                 s.nheads)
+        return read_ops(self.c.layouts, meta.layouts, self.local, remote)
+
+    def _read(self, meta: _PeerMeta, ops: list) -> None:
+        st = self.c.staging
+        rc = self.c.plane.read(meta.url, st.mirror_ops(ops) if st is not None else ops)
+        if rc != 0:
+            self.c.forget_peer(self.addr)
+            raise _PullFailed(f"{self.c.plane.name} read returned {rc}")
+        if st is not None:
+            st.stage_in([(d, n) for d, _, n in ops])
+
+    def run(self) -> PullResult:
+        try:
+            r = self._acquire()
+            if not self.local:
+                return PullResult(self.req_id, True)
+            held = r["blocks"]
+            remote = held[self.first:self.first + len(self.local)]
+            if len(remote) < len(self.local):
+                raise _PullFailed(f"producer holds {len(held)} blocks, need {self.first + len(self.local)}")
+            meta = self._meta(r.get("inc"))
+            ops = self._plan(meta, remote)
+            outside = self.c.outside(ops)
+            if outside:
+                raise _PullFailed(f"read outside registered KV memory: {outside}")
+            self._read(meta, ops)
+            if self.c.release_after_pull:
+                self.c.control(self.addr, self.c.release_msg(self.tid, self.src))
+            return PullResult(self.req_id, True, nbytes=sum(n for _, _, n in ops),
+                              seconds=time.monotonic() - self.t0)
+        except _PullFailed as e:
+            return PullResult(self.req_id, False, str(e))
 
 
 class KVConsumer:
@@ -245,194 +450,107 @@ class KVConsumer:
         self.acquire_wait_s = acquire_wait_s
         self.layouts = list(layouts)
         self.block_size = block_size
-        self.ctrl_timeout_ms = ctrl_timeout_ms
         self.release_after_pull = release_after_pull
-        self._spans = register_spans(self.layouts)
-        self._staging = register_with_staging(plane, self._spans, "KV consumer") if register \
+        self.spans = register_spans(self.layouts)
+        self.staging = register_with_staging(plane, self.spans, "KV consumer") if register \
             else getattr(plane, "_connex_staging", None)
-        self._pool = ThreadPoolExecutor(max_workers=workers, thread_name_prefix="connex-pd-pull")
-        self._src_pool = ThreadPoolExecutor(max_workers=max(8, 2 * workers), thread_name_prefix="connex-pd-src")
-        self._meta: dict = {}
+        self._ctrl = _ControlPool(ctrl_timeout_ms)
+        self._jobs = ThreadPoolExecutor(max_workers=workers, thread_name_prefix="connex-pd-pull")
+        self._sources = ThreadPoolExecutor(max_workers=max(8, 2 * workers), thread_name_prefix="connex-pd-src")
+        self._metas: Dict[str, _PeerMeta] = {}
         self._lock = threading.Lock()
-        self._done: List[PullResult] = []
-        self._ctx = zmq.Context.instance()
-        self._socks: dict = {}
-        self._closed = False
+        self._results: List[PullResult] = []
         self.stats = {"pulls": 0, "failed": 0, "bytes": 0, "seconds": 0.0}
 
-    # ------------------------------------------------------------ control
-    def _call(self, addr: str, msg: dict) -> Optional[dict]:
-        with self._lock:
-            idle = self._socks.get(addr)
-            s = idle.pop() if idle else None
-        if s is None:
-            s = self._ctx.socket(zmq.REQ)
-            s.setsockopt(zmq.LINGER, 0)
-            s.setsockopt(zmq.RCVTIMEO, self.ctrl_timeout_ms)
-            s.setsockopt(zmq.SNDTIMEO, self.ctrl_timeout_ms)
-            s.connect(f"tcp://{addr}")
-        try:
-            s.send(_pack(msg))
-            rep = _unpack(s.recv())
-        except Exception as e:
-            s.close(0)
-            if not isinstance(e, zmq.ZMQError):
-                log.warning("PD: bad control reply from %s: %s", addr, e)
-            return None
-        with self._lock:
-            if not self._closed:
-                self._socks.setdefault(addr, []).append(s)
-                s = None
-        if s is not None:
-            s.close(0)
-        return rep
+    # ------------------------------------------------------------- control
+    def control(self, addr: str, msg: dict) -> Optional[dict]:
+        """One control request to the producer at ``addr`` (None on failure)."""
+        return self._ctrl.call(addr, msg)
 
     def peer_meta(self, addr: str, refresh: bool = False) -> Optional[_PeerMeta]:
         with self._lock:
-            m = self._meta.get(addr)
-        if m is not None and not refresh:
-            return m
-        r = self._call(addr, {"op": "meta"})
+            cached = self._metas.get(addr)
+        if cached is not None and not refresh:
+            return cached
+        r = self.control(addr, {"op": "meta"})
         if not r or not r.get("ok"):
             return None
-        m = _PeerMeta(r)
-        if m.spans is not None and hasattr(self.plane, "add_peer"):
-            self.plane.add_peer(m.url, m.spans)
+        meta = _PeerMeta(r)
+        if meta.spans is not None and hasattr(self.plane, "add_peer"):
+            self.plane.add_peer(meta.url, meta.spans)
         with self._lock:
-            self._meta[addr] = m
-        return m
+            self._metas[addr] = meta
+        return meta
 
     def forget_peer(self, addr: str) -> None:
         with self._lock:
-            self._meta.pop(addr, None)
-            socks = self._socks.pop(addr, [])
-        for s in socks:
-            s.close(0)
+            self._metas.pop(addr, None)
+        self._ctrl.forget(addr)
 
-    # --------------------------------------------------------------- pull
-    def pull(self, req_id: str, addr: str, transfer_id: str, local_blocks: Sequence[int], first_block: int = 0,
-             sources: Optional[Sequence[Tuple[str, TPSource]]] = None) -> None:
-        """Start pulling remote blocks [first_block, +len(local)) of
-        ``transfer_id`` into ``local_blocks``; the result shows up in ``take_done``."""
-        self._pool.submit(self._pull, req_id, addr, transfer_id, list(local_blocks), first_block,
-                          list(sources) if sources else None)
-
-    def _pull(self, req_id, addr, tid, local, first, sources=None) -> None:
-        t0 = time.monotonic()
-        res = PullResult(req_id, False, failed_blocks=local)
-        try:
-            res = self._pull_sources(req_id, sources, tid, local, first, t0) if sources else \
-                self._pull_inner(req_id, addr, tid, local, first, t0)
-        except Exception as e:
-            res.why = f"error: {e}"
-            log.exception("KV pull of %s failed", req_id)
-        if not res.ok:
-            res.failed_blocks = list(local)
-        with self._lock:
-            self.stats["pulls"] += 1
-            self.stats["failed"] += 0 if res.ok else 1
-            self.stats["bytes"] += res.nbytes
-            self.stats["seconds"] += res.seconds
-            self._done.append(res)
-
-    def _pull_sources(self, req_id, sources, tid, local, first, t0) -> PullResult:
-        if self.inject_delay_s:
-            time.sleep(self.inject_delay_s)
-        futs = [self._src_pool.submit(self._pull_inner, req_id, a, tid, local, first, t0, src=s, delay=False)
-                for a, s in sources]
-        nbytes = 0
-        for (a, s), f in zip(sources, futs):
-            r = f.result()
-            if not r.ok:
-                r.why = f"TP rank {s.remote_rank} ({a}): {r.why}"
-                return r
-            nbytes += r.nbytes
-        return PullResult(req_id, True, nbytes=nbytes, seconds=time.monotonic() - t0)
-
-    def _pull_inner(self, req_id, addr, tid, local, first, t0, src: Optional[TPSource] = None,
-                    delay: bool = True) -> PullResult:
-        if self.inject_delay_s and delay:
-            time.sleep(self.inject_delay_s)
-        backoff = 0.002
-        while True:
-            r = self._call(addr, {"op": "acquire", "tid": tid, "who": self.who})
-            if r is None or r.get("ok") or r.get("why") != "unknown" or time.monotonic() - t0 > self.acquire_wait_s:
-                break
-            time.sleep(backoff)
-            backoff = min(backoff * 2, 0.05)
-        if r is None:
-            self.forget_peer(addr)
-            return PullResult(req_id, False, "producer unreachable")
-        if not r.get("ok"):
-            return PullResult(req_id, False, f"producer: {r.get('why')}")
-        if not local:
-            return PullResult(req_id, True)
-        remote = r["blocks"][first:first + len(local)]
-        if len(remote) < len(local):
-            return PullResult(req_id, False, f"producer holds {len(r['blocks'])} blocks, need {first + len(local)}")
-        meta = self.peer_meta(addr)
-        if meta is not None and r.get("inc") and meta.inc != r["inc"]:
-            meta = self.peer_meta(addr, refresh=True)  # restarted at the same address
-        if meta is None:
-            return PullResult(req_id, False, "producer meta unavailable")
-        if self.block_size and meta.block_size and meta.block_size != self.block_size:
-            return PullResult(req_id, False, f"block size {meta.block_size} != {self.block_size}")
-        ops = self._ops(meta, local, remote, src)
-        if self.plane.name == "cxengine" and self._staging is None and ops and \
-                min(n for _, _, n in ops) < ZCOPY_THRESH:
-            log.debug("KV segment below %d B: small reads", ZCOPY_THRESH)
-        bad = self._outside(ops)
-        if bad:
-            return PullResult(req_id, False, f"read outside registered KV memory: {bad}")
-        if self._staging is not None:
-            rc = self.plane.read(meta.url, self._staging.mirror_ops(ops))
-            if rc == 0:
-                self._staging.stage_in([(d, n) for d, _, n in ops])
-        else:
-            rc = self.plane.read(meta.url, ops)
-        if rc != 0:
-            self.forget_peer(addr)
-            return PullResult(req_id, False, f"{self.plane.name} read returned {rc}")
-        if self.release_after_pull:
-            self._call(addr, self._release_msg(tid, src))
-        return PullResult(req_id, True, nbytes=sum(n for _, _, n in ops), seconds=time.monotonic() - t0)
-
-    def _ops(self, meta: _PeerMeta, local, remote, src: Optional[TPSource]):
-        if src is not None:
-            lo, ro = self.layouts[0], meta.layouts[0]
-            whole = (src.nheads == lo.heads == ro.heads and lo.seg_bytes == ro.seg_bytes
-                     and lo.head_stride == ro.head_stride and lo.token_stride == ro.token_stride)
-            if not whole:
-                return head_read_ops(self.layouts, meta.layouts, local, remote, src.local_head0, src.remote_head0,
-                                     src.nheads)
-        return read_ops(self.layouts, meta.layouts, local, remote)
-
-    def _release_msg(self, tid: str, src: Optional[TPSource] = None) -> dict:
+    def release_msg(self, tid: str, src: Optional[TPSource] = None) -> dict:
         m = {"op": "release", "tid": tid, "who": self.who}
         if src is not None and src.readers > 1:
             m["of"] = src.readers
         return m
 
-    def _outside(self, ops) -> Optional[tuple]:
+    def outside(self, ops) -> Optional[tuple]:
+        """The first destination not inside the registered KV memory, if any."""
         for dst, _, n in ops:
-            if not any(s <= dst and dst + n <= s + ln for s, ln in self._spans):
-                return (hex(dst), n)
+            if not any(s <= dst and dst + n <= s + ln for s, ln in self.spans):
+                return hex(dst), n
         return None
 
+    # ---------------------------------------------------------------- pulls
+    def pull(self, req_id: str, addr: str, transfer_id: str, local_blocks: Sequence[int], first_block: int = 0,
+             sources: Optional[Sequence[Tuple[str, TPSource]]] = None) -> None:
+        """Start pulling remote blocks ``[first_block, +len(local_blocks))`` of
+        ``transfer_id`` into ``local_blocks``; the outcome appears in
+        :meth:`take_done`.  ``sources``: (address, TPSource) per remote TP rank."""
+        self._jobs.submit(self._run, req_id, addr, transfer_id, list(local_blocks), first_block,
+                          list(sources) if sources else None)
+
+    def _run(self, req_id, addr, tid, local, first, sources) -> None:
+        t0 = time.monotonic()
+        try:
+            if self.inject_delay_s:
+                time.sleep(self.inject_delay_s)
+            if sources:
+                res = self._run_sources(req_id, sources, tid, local, first, t0)
+            else:
+                res = _PullJob(self, req_id, addr, tid, local, first, t0, None).run()
+        except Exception as e:  # noqa: BLE001 - reported, never raised
+            log.exception("KV pull of %s failed", req_id)
+            res = PullResult(req_id, False, f"error: {e}")
+        if not res.ok:
+            res.failed_blocks = list(local)
+        with self._lock:
+            self.stats["pulls"] += 1
+            self.stats["failed"] += not res.ok
+            self.stats["bytes"] += res.nbytes
+            self.stats["seconds"] += res.seconds
+            self._results.append(res)
+
+    def _run_sources(self, req_id, sources, tid, local, first, t0) -> PullResult:
+        futs = [(a, s, self._sources.submit(_PullJob(self, req_id, a, tid, local, first, t0, s).run))
+                for a, s in sources]
+        total = 0
+        for a, s, f in futs:
+            r = f.result()
+            if not r.ok:
+                r.why = f"TP rank {s.remote_rank} ({a}): {r.why}"
+                return r
+            total += r.nbytes
+        return PullResult(req_id, True, nbytes=total, seconds=time.monotonic() - t0)
+
     def release(self, addr: str, transfer_id: str, src: Optional[TPSource] = None) -> None:
-        self._pool.submit(self._call, addr, self._release_msg(transfer_id, src))
+        self._jobs.submit(self.control, addr, self.release_msg(transfer_id, src))
 
     def take_done(self) -> List[PullResult]:
         with self._lock:
-            out, self._done = self._done, []
+            out, self._results = self._results, []
         return out
 
     def close(self) -> None:
-        self._pool.shutdown(wait=True)
-        self._src_pool.shutdown(wait=True)
-        with self._lock:
-            self._closed = True
-            socks, self._socks = self._socks, {}
-        for lst in socks.values():
-            for s in lst:
-                s.close(0)
+        self._jobs.shutdown(wait=True)
+        self._sources.shutdown(wait=True)
+        self._ctrl.close()

@@ -1,12 +1,18 @@
-"""Engine-facing protocols of the pipeline step protocol, metrics sinks and
-network helpers (reference ``connex/pp/hooks.py:31-223``).
+"""What the pipeline step protocol needs from an engine, metrics sinks, and
+address helpers.
 
-* :class:`EngineHooks` -- what an engine provides: ``kv_held`` / ``release``
-  (stages 1..), ``reprefill`` / ``abort`` (stage 0).
+* :class:`EngineHooks` -- the engine side of the protocol: ``kv_held`` and
+  ``release`` on stages 1.., ``reprefill`` and ``abort`` on stage 0.
 * :class:`StepTransport` -- the step-level API of a pipeline endpoint that
-  :mod:`connex.pp.link` drives.
-* :class:`MetricsSink` with :data:`METRIC_NAMES`, :class:`NullMetrics` and
-  :class:`PrefixedPrometheusSink`.
+  :mod:`connex.pp.link` drives (K steps in flight, per-step ids).
+* Metrics: the :class:`MetricsSink` protocol and the metric names the PP
+  data plane reports (:data:`METRIC_NAMES`), a null sink, an in-memory sink
+  and a Prometheus binding (:class:`PrefixedPrometheusSink`).
+* Address helpers for IPv4 / IPv6 ``host:port`` strings and ZeroMQ URIs,
+  and this host's routable address (``CONNEX_HOST_IP``).
+
+Interface parity: ``connex/pp/hooks.py:31-223`` of the reference (protocol
+method names and metric names are part of the public contract).
 """
 from __future__ import annotations
 
@@ -14,58 +20,68 @@ import ipaddress
 import logging
 import os
 import socket
-from typing import Any, Iterable, Optional, Protocol, Sequence, runtime_checkable
+from typing import Any, Callable, Dict, Iterable, Optional, Protocol, Sequence, Tuple, runtime_checkable
+
+_log = logging.getLogger("connex.pp")
 
 
-# ---- network helpers ------------------------------------------------------------
-def _is_ipv6(host: str) -> bool:
+# ---------------------------------------------------------------- addresses
+def _ipv6(host: str) -> bool:
     try:
-        return isinstance(ipaddress.ip_address(host), ipaddress.IPv6Address)
+        return ipaddress.ip_address(host).version == 6
     except ValueError:
         return False
 
 
+def _bracket(host: str) -> str:
+    return f"[{host}]" if _ipv6(host) else host
+
+
 def get_ip() -> str:
-    """This host's address: ``CONNEX_HOST_IP`` / ``VLLM_HOST_IP`` or the
-    interface of the default route (a UDP connect sends no packet)."""
-    env = os.getenv("CONNEX_HOST_IP") or os.getenv("VLLM_HOST_IP")
-    if env:
-        return env
-    for fam, probe in ((socket.AF_INET, ("8.8.8.8", 80)), (socket.AF_INET6, ("2001:4860:4860::8888", 80))):
+    """This host's address for peers to dial: ``CONNEX_HOST_IP`` (or
+    ``VLLM_HOST_IP``) when set, else the source address of the default route
+    (found with a connected UDP socket, which sends nothing)."""
+    for var in ("CONNEX_HOST_IP", "VLLM_HOST_IP"):
+        if os.getenv(var):
+            return os.environ[var]
+    probes = ((socket.AF_INET, "8.8.8.8"), (socket.AF_INET6, "2001:4860:4860::8888"))
+    for family, target in probes:
         try:
-            with socket.socket(fam, socket.SOCK_DGRAM) as s:
-                s.connect(probe)
+            with socket.socket(family, socket.SOCK_DGRAM) as s:
+                s.connect((target, 80))
                 return s.getsockname()[0]
         except OSError:
-            pass
-    logging.getLogger("connex.pp").warning("no routable address found; using 0.0.0.0 (set CONNEX_HOST_IP)")
+            continue
+    _log.warning("no routable address found; using 0.0.0.0 (set CONNEX_HOST_IP)")
     return "0.0.0.0"
 
 
 def get_tcp_uri(ip: str, port: int) -> str:
-    return f"tcp://[{ip}]:{port}" if _is_ipv6(ip) else f"tcp://{ip}:{port}"
+    return f"tcp://{_bracket(ip)}:{port}"
 
 
 def join_host_port(host: str, port: int) -> str:
-    return f"[{host}]:{port}" if _is_ipv6(host) else f"{host}:{port}"
+    return f"{_bracket(host)}:{port}"
 
 
-def split_host_port(host_port: str) -> tuple:
-    if host_port.startswith("["):
-        host, rest = host_port[1:].split("]", 1)
-        return host, int(rest.lstrip(":"))
-    host, port = host_port.rsplit(":", 1)
-    return host, int(port)
+def split_host_port(host_port: str) -> Tuple[str, int]:
+    """``"h:p"`` or ``"[v6]:p"`` -> (host, port)."""
+    host, sep, port = host_port.rpartition(":")
+    if not sep:
+        raise ValueError(f"no port in {host_port!r}")
+    return host.strip("[]"), int(port)
 
 
 class NetUtils:
+    """The address helpers as one namespace (injectable in tests)."""
+
     get_ip = staticmethod(get_ip)
     get_tcp_uri = staticmethod(get_tcp_uri)
     join_host_port = staticmethod(join_host_port)
     split_host_port = staticmethod(split_host_port)
 
 
-# ---- metrics ----------------------------------------------------------------------
+# ------------------------------------------------------------------ metrics
 METRIC_NAMES = (
     "bytes_sent", "bytes_received", "messages_sent", "messages_received",
     "send_latency", "recv_latency", "enqueue_latency", "delivery_latency",
@@ -88,96 +104,108 @@ class MetricsSink(Protocol):
 
 
 class NullMetrics:
+    """Discards everything (the default sink)."""
+
     enabled = False
 
     def observe(self, name, value, **labels):
-        pass
+        return None
 
     def inc(self, name, value=1.0, **labels):
-        pass
+        return None
 
     def set(self, name, value, **labels):
-        pass
+        return None
 
 
 NULL_METRICS = NullMetrics()
 
 
 class RecordingMetrics:
-    """In-memory sink (tests, local debugging): ``values[name]`` lists observations."""
+    """Keeps every call in memory: ``values[name]`` is a list of
+    ``(value, labels)`` in call order (tests, local debugging)."""
 
     enabled = True
 
     def __init__(self):
-        self.values: dict = {}
+        self.values: Dict[str, list] = {}
 
-    def observe(self, name, value, **labels):
+    def _record(self, name, value, **labels):
         self.values.setdefault(name, []).append((value, labels))
 
-    inc = observe
-    set = observe
+    def observe(self, name, value, **labels):
+        self._record(name, value, **labels)
+
+    def inc(self, name, value=1.0, **labels):
+        self._record(name, value, **labels)
+
+    def set(self, name, value, **labels):
+        self._record(name, value, **labels)
 
 
 class PrefixedPrometheusSink:
-    """Binds metric names to prometheus collectors ``<prefix>comm_<name>`` (or
-    ``<prefix><name>``) of ``module`` with labels backend / stage_idx + the
-    call's labels; children are bound once per label set."""
+    """Forwards metric calls to Prometheus collectors that an engine defines
+    in ``module`` as ``<prefix>comm_<name>`` (or ``<prefix><name>``), labelled
+    with ``backend`` and ``stage_idx`` plus the call's own labels.  A name
+    without a collector is ignored.  The labelled child of each (name,
+    labels) pair is resolved once and reused."""
 
     enabled = True
 
     def __init__(self, module: Any, prefix: str, backend: str, stage_idx: int):
         self.module, self.prefix = module, prefix
         self.base = {"backend": backend, "stage_idx": stage_idx}
-        self._children: dict = {}
+        self._bound: Dict[tuple, Any] = {}
 
-    def _child(self, name: str, labels: dict):
-        key = (name, tuple(sorted(labels.items())))
-        ch = self._children.get(key)
-        if ch is None:
-            m = getattr(self.module, f"{self.prefix}comm_{name}", None) or \
-                getattr(self.module, f"{self.prefix}{name}", None)
-            ch = m.labels(**self.base, **labels) if m is not None else False
-            self._children[key] = ch
-        return ch
+    def _collector(self, name: str):
+        for attr in (f"{self.prefix}comm_{name}", f"{self.prefix}{name}"):
+            c = getattr(self.module, attr, None)
+            if c is not None:
+                return c
+        return None
+
+    def _apply(self, op: str, name: str, value: float, labels: dict) -> None:
+        key = (name, frozenset(labels.items()))
+        child = self._bound.get(key)
+        if child is None:
+            coll = self._collector(name)
+            child = coll.labels(**self.base, **labels) if coll is not None else False
+            self._bound[key] = child
+        if child is not False:
+            getattr(child, op)(value)
 
     def observe(self, name, value, **labels):
-        ch = self._child(name, labels)
-        if ch:
-            ch.observe(value)
+        self._apply("observe", name, value, labels)
 
     def inc(self, name, value=1.0, **labels):
-        ch = self._child(name, labels)
-        if ch:
-            ch.inc(value)
+        self._apply("inc", name, value, labels)
 
     def set(self, name, value, **labels):
-        ch = self._child(name, labels)
-        if ch:
-            ch.set(value)
+        self._apply("set", name, value, labels)
 
 
-# ---- engine contract ------------------------------------------------------------
+# -------------------------------------------------------- engine contract
 RequestId = Any
 
 
 @runtime_checkable
 class EngineHooks(Protocol):
     def kv_held(self, request_id: RequestId) -> int:
-        """Stages 1..: leading tokens of the request whose KV this stage itself
-        computed and still holds (a fresh replica after failover holds 0)."""
+        """Stages 1..: how many leading tokens of the request this stage has
+        computed itself and still holds (0 on a replica new to it)."""
         ...
 
     def release(self, request_ids: Iterable[RequestId]) -> None:
-        """Drop all per-request state (KV blocks) of these requests."""
+        """Drop every per-request state (KV blocks) of these requests."""
         ...
 
     def reprefill(self, request_ids: Sequence[RequestId]) -> None:
-        """Stage 0: discard this step's token for them and recompute them
-        (prompt + generated tokens) on the current chain."""
+        """Stage 0: discard this step's token of each and recompute them
+        (prompt plus generated tokens) on the current chain."""
         ...
 
     def abort(self, request_ids: Sequence[RequestId]) -> None:
-        """Stage 0: finish them with an error (re-prefill budget exhausted)."""
+        """Stage 0: finish them with an error (re-prefill budget used up)."""
         ...
 
 
@@ -203,3 +231,6 @@ class StepTransport(Protocol):
     def send_reply(self, tensor_dict: dict, ctx: Optional[tuple]) -> None: ...
 
     def downstream_healthy(self) -> bool: ...
+
+
+MetricsFactory = Callable[[int], MetricsSink]

@@ -1,47 +1,65 @@
 """Step-protocol bookkeeping that never touches a transport.
 
-Stage 0 stamps every pipeline step with ``corr = incarnation << 32 | seq``
-and re-sends a step under the same id; later stages echo it.  That yields
-reply matching with K steps in flight, idempotent retries (a duplicate is
-answered from :class:`ReplyCache`), and stale suppression
-(:class:`CorrFilter`: an id K or more behind the newest id of the same
-incarnation is dropped).  Reference: ``connex/pp/steps.py:21-91``.
+A pipeline step carries a correlation id ``corr = incarnation << 32 | seq``
+chosen by stage 0 (a random 32-bit incarnation per stage-0 process and a
+running sequence number).  A re-sent step keeps its id and later stages echo
+it, which gives three properties:
+
+* replies can be matched to steps while K steps are in flight;
+* a retried step is answered from the stage's reply cache, not recomputed;
+* a step that is K or more sequence numbers behind the newest one seen from
+  the same incarnation is stale and dropped.
+
+Behavioural parity: ``connex/pp/steps.py:21-91`` of the reference (same
+class names and semantics; the data structures here are this module's own).
 """
 from __future__ import annotations
 
 import os
-from collections import OrderedDict
-from typing import Any, Callable, Optional
+from typing import Any, Callable, Dict, Optional
+
+_SEQ_MASK = (1 << 32) - 1
+
+
+def _split(corr: int):
+    return corr >> 32, corr & _SEQ_MASK
 
 
 class CorrFilter:
-    """Newest seq seen per stage-0 incarnation; ``accept`` drops ids that are
-    ``window`` or more behind it (``window`` = steps the sender keeps in flight)."""
+    """Admission test for incoming step ids.
+
+    For each stage-0 incarnation the filter remembers the newest sequence
+    number seen.  ``window`` is how many steps that sender keeps in flight:
+    ids inside the window may arrive out of order (a per-step retry routed
+    around a failed replica), ids ``window`` or more behind the newest are
+    stale.  At most ``cap`` incarnations are remembered; the one heard from
+    least recently is forgotten first (dict order is kept as recency)."""
 
     def __init__(self, cap: int = 64, window: int = 1):
-        self.cap = cap
+        self.cap = int(cap)
         self.window = max(1, int(window))
-        self.hi: "OrderedDict[int, int]" = OrderedDict()
+        self._newest: Dict[int, int] = {}
 
     def accept(self, corr: Optional[int]) -> bool:
         if not corr:
-            return True
-        inc, seq = corr >> 32, corr & 0xFFFFFFFF
-        newest = self.hi.get(inc)
-        if newest is not None and seq + self.window <= newest:
-            return False
-        self.hi[inc] = seq if newest is None else max(newest, seq)
-        self.hi.move_to_end(inc)
-        while len(self.hi) > self.cap:
-            self.hi.popitem(last=False)
-        return True
+            return True                      # a sender without ids: nothing to judge
+        inc, seq = _split(corr)
+        newest = self._newest.pop(inc, None)  # re-inserted below, as the most recent
+        stale = newest is not None and newest - seq >= self.window
+        self._newest[inc] = seq if newest is None else max(newest, seq)
+        if len(self._newest) > self.cap:
+            del self._newest[next(iter(self._newest))]
+        return not stale
 
 
 class StepIds:
-    """Correlation-id allocator of a stage-0 process (random 32-bit incarnation)."""
+    """Correlation ids of one stage-0 process: ``base + 1``, ``base + 2``, ...
+    where ``base`` holds a random 32-bit incarnation in its high half."""
 
     def __init__(self, base: Optional[int] = None):
-        self.base = (int.from_bytes(os.urandom(4), "big") << 32) if base is None else base
+        if base is None:
+            base = int.from_bytes(os.urandom(4), "big") << 32
+        self.base = base
         self.seq = 0
 
     def next(self) -> int:
@@ -50,23 +68,30 @@ class StepIds:
 
 
 class ReplyCache:
-    """Last ``k`` replies by correlation id; ``on_evict`` runs for every
-    evicted or replaced entry (e.g. to unpin its send-ring region)."""
+    """The newest ``k`` replies of a stage, keyed by correlation id, so a
+    duplicate step is answered again instead of recomputed.
+
+    ``on_evict(entry)`` is called for every entry that leaves the cache,
+    whether pushed out by newer replies or replaced under the same id (the
+    PP endpoint unpins the entry's send-ring region there)."""
 
     def __init__(self, k: int = 1, on_evict: Optional[Callable[[Any], None]] = None):
         self.k = max(1, int(k))
         self.on_evict = on_evict
-        self.entries: "OrderedDict[int, Any]" = OrderedDict()
+        self.entries: Dict[int, Any] = {}    # insertion order = age
+
+    def _drop(self, entry) -> None:
+        if self.on_evict is not None:
+            self.on_evict(entry)
 
     def put(self, corr: int, entry: Any) -> None:
-        old = self.entries.pop(corr, None)
-        if old is not None and self.on_evict:
-            self.on_evict(old)
+        if corr in self.entries:
+            self._drop(self.entries.pop(corr))
         self.entries[corr] = entry
-        while len(self.entries) > self.k:
-            _, e = self.entries.popitem(last=False)
-            if self.on_evict:
-                self.on_evict(e)
+        overflow = len(self.entries) - self.k
+        if overflow > 0:
+            for old in list(self.entries)[:overflow]:
+                self._drop(self.entries.pop(old))
 
     def get(self, corr):
         return self.entries.get(corr)

@@ -91,11 +91,11 @@ def test_stale_release_does_not_free_a_newer_readers_hold():
     prod = KVProducer(LoopbackPlane(), [lo], bind_ip="127.0.0.1", retain_s=30)
     try:
         prod.hold("r", "t", [1, 2])
-        assert prod._handle({"op": "acquire", "tid": "t", "who": "old"})["ok"]
-        assert prod._handle({"op": "acquire", "tid": "t", "who": "new"})["ok"]    # a re-pull by a new decode
-        assert prod._handle({"op": "release", "tid": "t", "who": "old"}).get("stale") is True
+        assert prod.answer({"op": "acquire", "tid": "t", "who": "old"})["ok"]
+        assert prod.answer({"op": "acquire", "tid": "t", "who": "new"})["ok"]    # a re-pull by a new decode
+        assert prod.answer({"op": "release", "tid": "t", "who": "old"}).get("stale") is True
         assert prod.held() == 1
-        assert prod._handle({"op": "release", "tid": "t", "who": "new"}) == {"ok": True}
+        assert prod.answer({"op": "release", "tid": "t", "who": "new"}) == {"ok": True}
         assert prod.held() == 0 and "r" in prod.take_finished()
     finally:
         prod.close()

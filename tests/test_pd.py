@@ -137,20 +137,20 @@ def test_lease_expiry_unknown_retry_and_stale_release():
         prod.hold("r", "t", [1])
         assert _wait_done(cons)[0].ok
         # stale release from another owner is ignored (single reader)
-        assert cons._call(addr, {"op": "release", "tid": "t", "who": "someone-else"})["stale"]
+        assert cons.control(addr, {"op": "release", "tid": "t", "who": "someone-else"})["stale"]
         assert prod.held() == 1
         time.sleep(0.3)
         assert "r" in prod.take_finished() and prod.stats["expired"] == 1
         # release before hold: the hold is dropped on arrival
-        cons._call(addr, {"op": "release", "tid": "t2", "who": "x"})
+        cons.control(addr, {"op": "release", "tid": "t2", "who": "x"})
         prod.hold("r2", "t2", [2])
         assert prod.held() == 0 and "r2" in prod.take_finished()
         # multi-reader release (heterogeneous TP): freed after all readers
         prod.hold("r3", "t3", [3])
-        assert cons._call(addr, {"op": "release", "tid": "t3", "who": "a", "of": 2})["pending"] == 1
-        assert cons._call(addr, {"op": "release", "tid": "t3", "who": "b", "of": 2}) == {"ok": True}
+        assert cons.control(addr, {"op": "release", "tid": "t3", "who": "a", "of": 2})["pending"] == 1
+        assert cons.control(addr, {"op": "release", "tid": "t3", "who": "b", "of": 2}) == {"ok": True}
         assert prod.held() == 0
-        assert cons._call(addr, {"op": "ping"})["ok"]
+        assert cons.control(addr, {"op": "ping"})["ok"]
     finally:
         cons.close()
         prod.close()
