@@ -135,6 +135,9 @@ def main() -> None:
     p.add_argument("--max-len", type=int, default=8192)
     p.add_argument("--layers", type=int, default=32, help="model depth (32 = Llama-3-8B)")
     p.add_argument("--seed", type=int, default=0)
+    p.add_argument("--kv-mode", default="auto", choices=["auto", "push", "pull"],
+                   help="layerwise KV transfer between GPUs: the prefill GPU pushes, or the decode GPU pulls "
+                        "(auto: pull for N >= 2; one GPU always pushes into its local decode cache)")
     p.add_argument("--no-sub-metrics", action="store_true",
                    help="skip the EP layer and weight-sync measurements after the PD steps")
     args = p.parse_args()

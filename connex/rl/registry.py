@@ -1,33 +1,66 @@
-"""Weight registry: the control plane of elastic weight sync (reference
-``connex/rl/registry.py:24-284``).
+"""Weight registry: the control plane of elastic weight sync.
 
-Knows the latest published version and its manifest, which members
-(rollout engines) are alive (TTL) and at which version, and who holds a
-full copy of each version (the last two versions are kept).  ``assign``
-hands a reader a source with spare fan-out, so the broadcast becomes a tree
-that grows as members finish (the publisher serves only when it has spare
-fan-out too).  ``retract`` / ``wait_idle`` guard a holder that is about to
-overwrite its copy: readers still assigned to it when the bounded wait
-expires are told on ``release`` that their bytes may be torn (``stale``).
+The registry knows
 
-:class:`RegistryServer` serves the same method set over stdlib HTTP/JSON
-(``POST /<method>`` with keyword arguments; reply ``{"result": ...}`` or
-``{"error": ...}``) and :class:`RegistryClient` calls it.
+* the latest published version and its manifest;
+* the members (rollout engines): alive while they heartbeat within the TTL,
+  and the version each has applied;
+* for each of the last two versions, the *copies*: who holds a full copy
+  (the publisher's arena, and members that keep theirs as relays), where to
+  read it, and which readers are reading it right now.
+
+``assign`` picks a copy for a reader: a copy below the fan-out limit if one
+exists -- relays before the publisher, then the least busy -- else the least
+busy copy, so the broadcast grows into a tree as members finish.
+``retract`` / ``wait_idle`` protect a holder about to overwrite its copy: it
+gets no new readers, and readers still on it when the bounded wait ends are
+told on ``release`` that their bytes may be torn (``stale``) so they re-read.
+
+:class:`RegistryServer` serves the method set over stdlib HTTP/JSON
+(``POST /<method>`` with keyword arguments, reply ``{"result": ...}`` or
+``{"error": ...}``); :class:`RegistryClient` is the matching client.
+Method names, arguments and replies follow ``connex/rl/registry.py:24-284``
+of the reference, so trainers and rollouts of either implementation
+interoperate; the bookkeeping here is this module's own.
 """
 from __future__ import annotations
 
+import collections
 import json
 import threading
 import time
 import urllib.error
 import urllib.request
+from dataclasses import dataclass, field
 from http.server import BaseHTTPRequestHandler, ThreadingHTTPServer
-from typing import Optional
+from typing import Dict, List, Optional, Set, Tuple
 
 PUBLISHER = "trainer"
 
-_METHODS = {"join", "heartbeat", "leave", "expire", "publish", "get_latest", "assign", "release", "report_failure",
-            "retract", "wait_idle", "done", "status", "wait_all"}
+_METHODS = ("join", "heartbeat", "leave", "expire", "publish", "get_latest", "assign", "release",
+            "report_failure", "retract", "wait_idle", "done", "status", "wait_all")
+
+
+@dataclass
+class _Copy:
+    """A full copy of one version that readers may pull from."""
+
+    url: str
+    addr: int
+    publisher: bool = False
+    retiring: bool = False                  # about to be overwritten: no new readers
+    readers: collections.Counter = field(default_factory=collections.Counter)
+
+    @property
+    def load(self) -> int:
+        return sum(self.readers.values())
+
+
+@dataclass
+class _Member:
+    url: str
+    version: Optional[int] = None
+    seen: float = field(default_factory=time.time)
 
 
 class WeightRegistry:
@@ -37,49 +70,50 @@ class WeightRegistry:
         self.lock = threading.Lock()
         self.cv = threading.Condition(self.lock)
         self.latest: Optional[dict] = None
-        self.holders: dict = {}    # version -> {member: {url, addr, load, publisher}}
-        self.members: dict = {}    # member -> {url, version, last_seen}
-        self.events: list = []
-        self.reading: dict = {}    # reader -> [(version, source)]
-        self.stale: set = set()    # (reader, version, source)
+        self.members: Dict[str, _Member] = {}
+        self.holders: Dict[int, Dict[str, _Copy]] = {}      # version -> holder -> copy
+        self.stale: Set[Tuple[str, int, str]] = set()       # (reader, version, source) with torn bytes
+        self.events: collections.deque = collections.deque(maxlen=1000)
 
-    def _ev(self, kind, member, detail=None):
+    def _log(self, kind, member, detail=None) -> None:
         self.events.append((time.time(), kind, member, detail))
-        del self.events[:-1000]
 
-    # ---------------------------------------------------------- membership
+    def _changed(self) -> None:
+        self.cv.notify_all()
+
+    # ------------------------------------------------------------- members
     def join(self, member, url=""):
-        with self.lock:
-            self.members[member] = {"url": url, "version": None, "last_seen": time.time()}
-            self._ev("join", member)
+        with self.cv:
+            self.members[member] = _Member(url)
+            self._log("join", member)
             return {"latest": self.latest["version"] if self.latest else None}
 
     def heartbeat(self, member):
-        with self.lock:
-            if member in self.members:
-                self.members[member]["last_seen"] = time.time()
-                return {"ok": True}
-            return {"ok": False}
+        with self.cv:
+            m = self.members.get(member)
+            if m is not None:
+                m.seen = time.time()
+            return {"ok": m is not None}
 
     def leave(self, member, reason="leave"):
         with self.cv:
             self.members.pop(member, None)
-            for version, source in self.reading.pop(member, []):  # give its load back
-                self._release(version, source)
-            self.stale = {x for x in self.stale if x[0] != member}
-            for hs in self.holders.values():
-                hs.pop(member, None)
-            self._ev(reason, member)
-            self.cv.notify_all()
+            for copies in self.holders.values():
+                copies.pop(member, None)                     # its copy is gone
+                for c in copies.values():
+                    c.readers.pop(member, None)              # its reads give their load back
+            self.stale = {s for s in self.stale if s[0] != member}
+            self._log(reason, member)
+            self._changed()
             return {"ok": True}
 
     def expire(self):
-        now = time.time()
-        with self.lock:
-            dead = [m for m, i in self.members.items() if now - i["last_seen"] > self.ttl]
-        for m in dead:
-            self.leave(m, "expired")
-        return dead
+        cutoff = time.time() - self.ttl
+        with self.cv:
+            gone = [name for name, m in self.members.items() if m.seen < cutoff]
+        for name in gone:
+            self.leave(name, "expired")
+        return gone
 
     # ------------------------------------------------------------ versions
     def publish(self, version, manifest, url, addr):
@@ -87,151 +121,166 @@ class WeightRegistry:
             if self.latest and version <= self.latest["version"]:
                 raise ValueError(f"version {version} <= latest {self.latest['version']}")
             self.latest = {"version": version, "manifest": manifest}
-            self.holders[version] = {PUBLISHER: {"url": url, "addr": addr, "load": 0, "publisher": True}}
-            for v in [v for v in self.holders if v < version - 1]:
-                del self.holders[v]
-            self._ev("publish", PUBLISHER, version)
-            self.cv.notify_all()
+            self.holders[version] = {PUBLISHER: _Copy(url, addr, publisher=True)}
+            for old in [v for v in self.holders if v < version - 1]:
+                del self.holders[old]                        # keep the last two versions
+            self._log("publish", PUBLISHER, version)
+            self._changed()
             return {"ok": True}
 
     def get_latest(self, wait_newer_than=None, timeout=0.0):
         with self.cv:
             if wait_newer_than is not None:
-                self.cv.wait_for(lambda: self.latest and self.latest["version"] > wait_newer_than, timeout=timeout)
+                self.cv.wait_for(lambda: self.latest is not None and self.latest["version"] > wait_newer_than,
+                                 timeout=timeout)
             return self.latest
 
+    def _preference(self, copy: _Copy):
+        """Sort key of a copy for a new reader (smaller is better)."""
+        load = copy.load
+        if load < self.fanout:
+            return 0, 0, copy.publisher, load
+        return 1, load, copy.publisher, load
+
     def assign(self, version, member, exclude=()):
-        with self.lock:
-            hs = {m: h for m, h in self.holders.get(version, {}).items()
-                  if m != member and m not in exclude and not h.get("retiring")}
-            if not hs:
+        with self.cv:
+            options = [(name, c) for name, c in self.holders.get(version, {}).items()
+                       if name != member and name not in exclude and not c.retiring]
+            if not options:
                 return None
-
-            def key(item):
-                _, h = item
-                full = h["load"] >= self.fanout
-                return (full, h["load"] if full else 0, h["publisher"], h["load"])
-            m, h = min(hs.items(), key=key)
-            h["load"] += 1
-            self.reading.setdefault(member, []).append((version, m))
-            return {"member": m, "url": h["url"], "addr": h["addr"]}
-
-    def _release(self, version, source):
-        h = self.holders.get(version, {}).get(source)
-        if h and h["load"] > 0:
-            h["load"] -= 1
+            name, copy = min(options, key=lambda nc: self._preference(nc[1]))
+            copy.readers[member] += 1
+            return {"member": name, "url": copy.url, "addr": copy.addr}
 
     def release(self, version, source, member=None):
         with self.cv:
-            if member is not None:
-                rs = self.reading.get(member, [])
-                if (version, source) not in rs:
-                    return {"ok": True}
-                rs.remove((version, source))
-                if not rs:
-                    self.reading.pop(member, None)
-            self._release(version, source)
-            self.cv.notify_all()
-            if member is not None and (member, version, source) in self.stale:
+            copy = self.holders.get(version, {}).get(source)
+            if member is None:
+                # an anonymous release: give back one unit of load
+                if copy is not None and copy.readers:
+                    reader = next(iter(copy.readers))
+                    copy.readers[reader] -= 1
+                    if copy.readers[reader] <= 0:
+                        del copy.readers[reader]
+                self._changed()
+                return {"ok": True}
+            if copy is not None and copy.readers.get(member, 0) > 0:
+                copy.readers[member] -= 1
+                if copy.readers[member] <= 0:
+                    del copy.readers[member]
+                self._changed()
+            # the copy may be gone already (retired / older than the last two
+            # versions): a reader it was invalidated under still learns so
+            if (member, version, source) in self.stale:
                 self.stale.discard((member, version, source))
                 return {"ok": True, "stale": True}
             return {"ok": True}
 
-    def _invalidate(self, version, source):
-        for reader, rs in self.reading.items():
-            for v, src in rs:
-                if src == source and (version is None or v == version):
-                    self.stale.add((reader, v, src))
+    def invalidate(self, version, source) -> None:
+        """Readers now on ``source`` (of ``version``, or any version when None)
+        will hear on release that their bytes may be torn.  Lock held."""
+        for v, copies in self.holders.items():
+            copy = copies.get(source)
+            if copy is None or (version is not None and v != version):
+                continue
+            self.stale.update((reader, v, source) for reader in copy.readers)
 
     def report_failure(self, version, source, reporter):
         with self.cv:
-            h = self.holders.get(version, {})
-            if source in h and not h[source]["publisher"]:
-                del h[source]
-            self._ev("source_failed", source, {"version": version, "by": reporter})
-            self.cv.notify_all()
+            copies = self.holders.get(version, {})
+            if source in copies and not copies[source].publisher:
+                del copies[source]
+            self._log("source_failed", source, {"version": version, "by": reporter})
+            self._changed()
             return {"ok": True}
 
+    def _busy(self, member, version=None) -> int:
+        return sum(c[member].load for v, c in self.holders.items()
+                   if member in c and (version is None or v == version))
+
     def retract(self, member, timeout=5.0):
+        """``member`` is about to overwrite its copies: wait (bounded) for its
+        readers, mark the rest stale, and drop the copies."""
         with self.cv:
-            def busy():
-                return sum(h[member]["load"] for h in self.holders.values() if member in h)
-            if not self.cv.wait_for(lambda: busy() == 0, timeout=timeout):
-                self._invalidate(None, member)
-            for hs in self.holders.values():
-                hs.pop(member, None)
+            if not self.cv.wait_for(lambda: self._busy(member) == 0, timeout=timeout):
+                self.invalidate(None, member)
+            for copies in self.holders.values():
+                copies.pop(member, None)
             return {"ok": True}
 
     def wait_idle(self, version, member=PUBLISHER, timeout=5.0, retire=False):
         with self.cv:
-            h = self.holders.get(version, {}).get(member)
-            if retire and h is not None:
-                h["retiring"] = True       # the copy is about to be overwritten: no new readers
-            ok = self.cv.wait_for(lambda: self.holders.get(version, {}).get(member, {"load": 0})["load"] == 0,
-                                  timeout=timeout)
-            if not ok:
-                self._invalidate(version, member)
+            copy = self.holders.get(version, {}).get(member)
+            if retire and copy is not None:
+                copy.retiring = True
+            idle = self.cv.wait_for(lambda: self._busy(member, version) == 0, timeout=timeout)
+            if not idle:
+                self.invalidate(version, member)
             if retire:
                 self.holders.get(version, {}).pop(member, None)
-            return {"ok": bool(ok)}
+            return {"ok": bool(idle)}
 
     def done(self, version, member, url, addr, hold=True):
+        """``member`` applied ``version``; with ``hold`` it keeps the copy as a relay."""
         with self.cv:
-            if member not in self.members:
-                self.members[member] = {"url": url, "version": None, "last_seen": time.time()}
-            self.members[member].update(version=version, last_seen=time.time())
+            m = self.members.setdefault(member, _Member(url))
+            m.version, m.seen = version, time.time()
             if hold and version in self.holders:
-                self.holders[version][member] = {"url": url, "addr": addr, "load": 0, "publisher": False}
-            self._ev("applied", member, version)
-            self.cv.notify_all()
+                self.holders[version][member] = _Copy(url, addr)
+            self._log("applied", member, version)
+            self._changed()
             return {"ok": True}
 
     def status(self):
-        with self.lock:
+        with self.cv:
             return {"latest": self.latest["version"] if self.latest else None,
-                    "members": {m: i["version"] for m, i in self.members.items()},
-                    "holders": {str(v): {m: h["load"] for m, h in hs.items()} for v, hs in self.holders.items()}}
+                    "members": {name: m.version for name, m in self.members.items()},
+                    "holders": {str(v): {name: c.load for name, c in copies.items()}
+                                for v, copies in self.holders.items()}}
 
     def wait_all(self, version, timeout=60.0):
         with self.cv:
-            return self.cv.wait_for(lambda: all(i["version"] == version for i in self.members.values()),
+            return self.cv.wait_for(lambda: all(m.version == version for m in self.members.values()),
                                     timeout=timeout)
 
 
+class _Handler(BaseHTTPRequestHandler):
+    registry: WeightRegistry
+
+    def log_message(self, *args):
+        return None
+
+    def _reply(self, code: int, body: dict) -> None:
+        data = json.dumps(body).encode()
+        self.send_response(code)
+        self.send_header("Content-Length", str(len(data)))
+        self.end_headers()
+        self.wfile.write(data)
+
+    def do_POST(self):
+        method = self.path.strip("/")
+        try:
+            kwargs = json.loads(self.rfile.read(int(self.headers.get("Content-Length") or 0)) or b"{}")
+            if method not in _METHODS:
+                raise KeyError(method)
+            self._reply(200, {"result": getattr(self.registry, method)(**kwargs)})
+        except Exception as e:  # noqa: BLE001 - reported to the caller
+            self._reply(400, {"error": f"{type(e).__name__}: {e}"})
+
+
 class RegistryServer:
+    """Serves a :class:`WeightRegistry` over HTTP and expires silent members."""
+
     def __init__(self, registry: Optional[WeightRegistry] = None, host: str = "0.0.0.0", port: int = 0,
                  expire_interval: float = 1.0):
         self.reg = registry or WeightRegistry()
-        reg = self.reg
-
-        class Handler(BaseHTTPRequestHandler):
-            def log_message(self, *a):
-                pass
-
-            def do_POST(self):
-                name = self.path.strip("/")
-                n = int(self.headers.get("Content-Length") or 0)
-                try:
-                    body = json.loads(self.rfile.read(n) or b"{}")
-                    if name not in _METHODS:
-                        raise KeyError(name)
-                    out, code = {"result": getattr(reg, name)(**body)}, 200
-                except Exception as e:
-                    out, code = {"error": f"{type(e).__name__}: {e}"}, 400
-                data = json.dumps(out).encode()
-                self.send_response(code)
-                self.send_header("Content-Length", str(len(data)))
-                self.end_headers()
-                self.wfile.write(data)
-
-        self.httpd = ThreadingHTTPServer((host, port), Handler)
+        handler = type("RegistryHandler", (_Handler,), {"registry": self.reg})
+        self.httpd = ThreadingHTTPServer((host, port), handler)
         self.httpd.daemon_threads = True
         self.port = self.httpd.server_address[1]
         self._stop = threading.Event()
-        self._threads = [threading.Thread(target=self.httpd.serve_forever, daemon=True),
-                         threading.Thread(target=self._expire_loop, args=(expire_interval,), daemon=True)]
-        for t in self._threads:
-            t.start()
+        for target in (self.httpd.serve_forever, lambda: self._expire_loop(expire_interval)):
+            threading.Thread(target=target, daemon=True).start()
 
     def _expire_loop(self, every: float) -> None:
         while not self._stop.wait(every):
@@ -244,28 +293,36 @@ class RegistryServer:
 
 
 class RegistryClient:
-    """Same methods as :class:`WeightRegistry`, over HTTP (no env proxies)."""
+    """The :class:`WeightRegistry` methods over HTTP (environment proxies ignored)."""
 
     def __init__(self, url: str, timeout: float = 120.0):
         self.url = url.rstrip("/")
         self.timeout = timeout
-        self._open = urllib.request.build_opener(urllib.request.ProxyHandler({})).open
+        self._opener = urllib.request.build_opener(urllib.request.ProxyHandler({}))
 
-    def __getattr__(self, name):
-        if name not in _METHODS:
-            raise AttributeError(name)
-
-        def call(**kw):
-            req = urllib.request.Request(f"{self.url}/{name}", data=json.dumps(kw).encode(),
-                                         headers={"Content-Type": "application/json"})
+    def _post(self, method: str, kwargs: dict):
+        req = urllib.request.Request(f"{self.url}/{method}", data=json.dumps(kwargs).encode(),
+                                     headers={"Content-Type": "application/json"})
+        try:
+            with self._opener.open(req, timeout=self.timeout) as r:
+                return json.loads(r.read())["result"]
+        except urllib.error.HTTPError as e:
+            raw = e.read()
             try:
-                with self._open(req, timeout=self.timeout) as r:
-                    return json.loads(r.read())["result"]
-            except urllib.error.HTTPError as e:
-                body = e.read()
-                try:
-                    msg = json.loads(body).get("error")
-                except ValueError:
-                    msg = f"HTTP {e.code}: {body[:200]!r}"
-                raise RuntimeError(msg) from None
-        return call
+                message = json.loads(raw).get("error")
+            except ValueError:
+                message = f"HTTP {e.code}: {raw[:200]!r}"
+            raise RuntimeError(message) from None
+
+
+def _remote(method: str):
+    def call(self, **kwargs):
+        return self._post(method, kwargs)
+    call.__name__ = method
+    call.__doc__ = f"``WeightRegistry.{method}`` on the server."
+    return call
+
+
+for _m in _METHODS:
+    setattr(RegistryClient, _m, _remote(_m))
+del _m

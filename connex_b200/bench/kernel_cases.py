@@ -14,7 +14,9 @@ decode_attn (64 x 4096-token paged decode), kv_push (one layer of a 64k-token
 KV push, local), kv_push_nvlink (the same layer pushed from GPU 0 into GPU 1's
 memory over NVLink, one process, peer access; ``--ctas`` sets the grid,
 ``--pull`` runs the kernel on GPU 1 reading GPU 0's memory instead, ``--ce``
-times a copy-engine peer copy of the same bytes for comparison), wsync (Llama-3-8B 2-layer slice, fp32 -> bf16 fused
+times a copy-engine peer copy of the same bytes for comparison),
+kv_push_beside (the push of one 8k-token layer alone or next to a running
+GEMM / attention kernel, ``--co``, ``--ctas``), wsync (Llama-3-8B 2-layer slice, fp32 -> bf16 fused
 re-layout), ep_gemm (grouped expert GEMM, 1 GPU).
 """
 from __future__ import annotations
@@ -135,6 +137,61 @@ def case_kv_push_nvlink(dev, tokens=65536, hkv=8, ctas=0, pull=False, ce=False):
     return run, {"bytes": src.numel() * 2, "device": run_dev, "check": check, "link": True}
 
 
+def push_beside(dev, co: str = "gemm", ctas: int = 296, tokens: int = 8192, iters: int = 20) -> dict:
+    """The KV push of one layer (``tokens`` tokens, local destination) timed
+    alone and while another kernel runs on a second stream: ``co`` = gemm
+    (the gate/up GEMM of ``tokens`` rows), attn (causal prefill attention of
+    4 x ``tokens/4``), or none.  The push runs on a high-priority stream, as
+    in the PD prefill; returns per-launch push times (CUDA events)."""
+    bs, hkv = 16, 8
+    nb = tokens // bs
+    src = torch.randn(2, nb, hkv, bs, 128, device=dev).bfloat16()
+    dst = torch.empty_like(src)
+    pairs = torch.stack([torch.arange(nb), torch.randperm(nb)], 1).int().to(dev)
+    status = ops.new_status(dev)
+    push_stream = torch.cuda.Stream(device=dev, priority=-1)
+    co_stream = torch.cuda.Stream(device=dev)
+    if co == "gemm":
+        a = torch.randn(tokens, 4096, device=dev).bfloat16()
+        w = torch.randn(28672, 4096, device=dev).bfloat16()
+        out = torch.empty(tokens, 14336, dtype=torch.bfloat16, device=dev)
+        co_fn = lambda: ops.gemm(a, w, out, silu_mul=True)           # noqa: E731
+    elif co == "attn":
+        qkv = (torch.randn(tokens, 6144, device=dev) * 0.5).bfloat16()
+        ti = ops.prefill_tile_info([tokens // 4] * 4, dev)
+        ao = torch.empty(tokens, 4096, dtype=torch.bfloat16, device=dev)
+        co_fn = lambda: ops.prefill_attention(qkv, ti, 32, 8, ao)     # noqa: E731
+    else:
+        co_fn = None
+
+    def push():
+        ops.kv_push_layer(src[0].data_ptr(), src[1].data_ptr(), dst[0].data_ptr(), dst[1].data_ptr(), pairs,
+                          src_heads=hkv, dst_heads=hkv, chunk_bytes=bs * 256, src_blocks=nb, dst_blocks=nb,
+                          max_ctas=ctas, status=status)
+    times = []
+    for i in range(iters + 3):
+        torch.cuda.synchronize(dev)
+        if co_fn is not None:
+            started = torch.cuda.Event()
+            with torch.cuda.stream(co_stream):
+                co_fn()
+                started.record(co_stream)      # the second co-runner launch begins as the push does
+                co_fn()
+            push_stream.wait_event(started)
+        with torch.cuda.stream(push_stream):
+            e0, e1 = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+            e0.record(push_stream)
+            push()
+            e1.record(push_stream)
+        torch.cuda.synchronize(dev)
+        if i >= 3:
+            times.append(e0.elapsed_time(e1))
+    ops.check_status(status, "push beside")
+    ms = sorted(times)[len(times) // 2]
+    return {"case": "kv_push_beside", "co": co, "ctas": ctas, "tokens": tokens, "ms_p50": round(ms, 4),
+            "gbps": round(src.numel() * 2 * 2 / ms / 1e6, 1)}
+
+
 def case_wsync(dev, layers=2):
     from connex_b200.models.llama import LlamaConfig, random_trainer_weights
     from connex_b200.parallel.wsync import apply_local, engine_manifest, plan_jobs
@@ -207,13 +264,17 @@ NEEDS_ARGS = {"kv_push_nvlink": case_kv_push_nvlink}
 
 def main() -> None:
     p = argparse.ArgumentParser()
-    p.add_argument("case", choices=sorted(CASES) + sorted(NEEDS_ARGS))
+    p.add_argument("case", choices=sorted(CASES) + sorted(NEEDS_ARGS) + ["kv_push_beside"])
     p.add_argument("--iters", type=int, default=20)
     p.add_argument("--ctas", type=int, default=0, help="kv_push_nvlink: grid size (0 = the launcher's default)")
     p.add_argument("--pull", action="store_true", help="kv_push_nvlink: run on GPU 1, loading GPU 0's memory")
     p.add_argument("--ce", action="store_true", help="kv_push_nvlink: copy-engine peer copy instead of the kernel")
+    p.add_argument("--co", default="gemm", help="kv_push_beside: co-running kernel (gemm, attn, none)")
     a = p.parse_args()
     dev = torch.device("cuda", 0)
+    if a.case == "kv_push_beside":
+        print(json.dumps(push_beside(dev, a.co, a.ctas or 296)), flush=True)
+        return
     if a.case in NEEDS_ARGS:
         fn, work = NEEDS_ARGS[a.case](dev, ctas=a.ctas, pull=a.pull, ce=a.ce)
     else:

@@ -17,11 +17,12 @@ import torch.distributed as dist
 from connex_b200 import ops
 from connex_b200.models.llama import LlamaConfig, LlamaModel, LlamaWeights, PagedKVCache
 from connex_b200.parallel.peer import PeerHandle, PeerMapper, export_tensor
-from connex_b200.runtime.pd import (DecodeBatch, KVDestination, LayerwiseKVPusher, block_pairs,
-                                    build_prefill_batch, decode_step)
+from connex_b200.runtime.pd import (DecodeBatch, KVDestination, LayerReadySignal, LayerwiseKVPuller,
+                                    LayerwiseKVPusher, block_pairs, build_prefill_batch, decode_step)
 
 PUSH_CTAS = int(os.environ.get("CX_PD_PUSH_CTAS", "296"))   # CTAs per layer push (2 per SM by default)
 PUSH_AFTER_ATTENTION = os.environ.get("CX_PD_PUSH_AFTER", "kv") == "attention"
+PULL_CTAS = int(os.environ.get("CX_PD_PULL_CTAS", "592"))   # the decode GPU is otherwise idle during prefill
 TOKEN_BYTES = 64         # first-token inbox copy (16 int32)
 
 
@@ -77,6 +78,28 @@ def _job_gpu_uuids(world: int, cpu, dev) -> list:
     return allu
 
 
+def kv_mode(args, world: int) -> str:
+    """The layerwise transfer the timed steps use: ``--kv-mode`` (or
+    ``CX_PD_KV_MODE``); by default pull between GPUs, push on one GPU."""
+    m = getattr(args, "kv_mode", None) or os.environ.get("CX_PD_KV_MODE") or "auto"
+    if m == "auto":
+        m = "pull" if world > 1 else "push"
+    if m not in ("push", "pull"):
+        raise SystemExit(f"kv mode must be push, pull or auto, got {m!r}")
+    return "push" if world == 1 else m
+
+
+def _pair_rate(ranks: list, key: str, n: int, field: str) -> float:
+    """Aggregate GB/s: sum over the transferring ranks of bytes / summed time."""
+    total = 0.0
+    for g in ranks:
+        b = sum(g[key][s]["kv_bytes"] for s in range(n))
+        t = sum(g[key][s][field] for s in range(n))
+        if t > 0:
+            total += b / (t * 1e-3)
+    return total / 1e9
+
+
 def run_pd_bench(args, ClockSampler, finalize: bool = True):
     """The PD steps; with ``finalize=False`` the process group stays up for
     further collective measurements (the caller destroys it)."""
@@ -120,9 +143,12 @@ def run_pd_bench(args, ClockSampler, finalize: bool = True):
         dstatus = ops.new_status(dev)
         ws = ops.decode_workspace(B, cfg.heads, args.max_len + 2, dev)
         tok_host = torch.zeros(B, dtype=torch.int32).pin_memory()
+        layer_ctr = torch.zeros(4, dtype=torch.int32, device=dev)      # pull mode: prefill's per-layer counter
+        puller = LayerwiseKVPuller(dec_cache, max_ctas=PULL_CTAS)
 
     # ---- peer mapping of the decode caches (control plane: object gather) ----
     mapper = PeerMapper(local)
+    signal = None
     if world == 1:
         dst = KVDestination.of_cache(dec_cache, ready)
         inbox_addr = inbox.data_ptr()
@@ -130,27 +156,41 @@ def run_pd_bench(args, ClockSampler, finalize: bool = True):
         mine = None
         if role == "decode":
             mine = {"kv": export_tensor(dec_cache.kv).to_dict(), "ready": export_tensor(ready).to_dict(),
-                    "inbox": export_tensor(inbox).to_dict(), "blocks": n_blocks,
-                    "layer_stride": dec_cache.layer_stride_bytes, "kv_stride": dec_cache.kv_stride_bytes}
+                    "inbox": export_tensor(inbox).to_dict(), "layer_ctr": export_tensor(layer_ctr).to_dict(),
+                    "blocks": n_blocks, "layer_stride": dec_cache.layer_stride_bytes,
+                    "kv_stride": dec_cache.kv_stride_bytes}
+        else:
+            mine = {"kv": export_tensor(pre_cache.kv).to_dict(), "blocks": n_blocks,
+                    "layer_stride": pre_cache.layer_stride_bytes, "kv_stride": pre_cache.kv_stride_bytes}
         allx = [None] * world
         dist.all_gather_object(allx, mine, group=cpu)
+        d = allx[peer]
         if role == "prefill":
-            d = allx[peer]
             base = mapper.open(PeerHandle.from_dict(d["kv"]))
             dst = KVDestination(base=base, layer_stride=d["layer_stride"], kv_stride=d["kv_stride"],
                                 heads=cfg.kv_heads, num_blocks=d["blocks"],
                                 ready_addr=mapper.open(PeerHandle.from_dict(d["ready"])))
             inbox_addr = mapper.open(PeerHandle.from_dict(d["inbox"]))
+            signal = LayerReadySignal(mapper.open(PeerHandle.from_dict(d["layer_ctr"])), dev, cfg.layers)
+        else:
+            src_view = {"base": mapper.open(PeerHandle.from_dict(d["kv"])), "blocks": d["blocks"],
+                        "layer_stride": d["layer_stride"], "kv_stride": d["kv_stride"]}
     ready_target = 0
+    pull_base = 0
     tok_seg = None
 
-    def run_step(step: int, timed: bool, check: bool = False, bulk: bool = False):
-        """One step.  ``bulk``: the reference's design instead of the layerwise
-        push -- prefill every layer, then copy the whole KV with one copy-engine
-        peer copy per (layer, K/V, run of consecutive blocks).  ``check``:
-        after the step, compare checksums of the prefill side's source blocks
-        and the decode side's destination blocks (outside any timed region)."""
-        nonlocal ready_target, tok_seg
+    def run_step(step: int, timed: bool, check: bool = False, mode: str = "push"):
+        """One step.  ``mode``: ``push`` (the prefill GPU's kernel stores each
+        layer into the decode cache), ``pull`` (the decode GPU's kernel
+        gathers each layer as soon as the prefill publishes it), or ``bulk``
+        (the reference's design: prefill every layer, then copy the whole KV
+        with one copy-engine peer copy per (layer, K/V, run of consecutive
+        blocks)).  ``check``: after the step, compare checksums of the
+        prefill side's source blocks and the decode side's destination blocks
+        (outside any timed region)."""
+        nonlocal ready_target, tok_seg, pull_base
+        bulk = mode == "bulk"
+        pull = mode == "pull" and world > 1
         prompts = _prompts(args.seed, step, B, args.min_len, args.max_len, cfg.vocab_size)
         lens = [len(p) for p in prompts]
         n_pairs_total = sum((n + cfg.block_size - 1) // cfg.block_size for n in lens)
@@ -158,12 +198,21 @@ def run_pd_bench(args, ClockSampler, finalize: bool = True):
         dblocks = None
         if role in ("decode", "both"):
             dblocks = [dec_cache.allocate(dec_cache.blocks_needed(n + 1)) for n in lens]
+        sblocks = None
+        if pull and role == "prefill":       # source blocks are allocated up front so the puller knows them
+            sblocks = [pre.cache.allocate(pre.cache.blocks_needed(n)) for n in lens]
         if role == "decode":
             dist.send_object_list([dblocks], dst=peer, group=cpu)
+            if pull:
+                box = [None]
+                dist.recv_object_list(box, src=peer, group=cpu)
+                sblocks = box[0]
         elif role == "prefill":
             box = [None]
             dist.recv_object_list(box, src=peer, group=cpu)
             dblocks = box[0]
+            if pull:
+                dist.send_object_list([sblocks], dst=peer, group=cpu)
         ids_host = torch.tensor([t for p in prompts for t in p], dtype=torch.int32).pin_memory()
         barrier()
         torch.cuda.synchronize(dev)
@@ -174,13 +223,18 @@ def run_pd_bench(args, ClockSampler, finalize: bool = True):
         kv_bytes = 0
         if role in ("prefill", "both"):
             ids = ids_host.to(dev, non_blocking=True)                      # H2D from pinned memory
-            batch = build_prefill_batch(pre.cache, prompts, dev, ids=ids)
+            batch = build_prefill_batch(pre.cache, prompts, dev, ids=ids, blocks=sblocks)
             pairs = block_pairs(batch.src_blocks, [d[:len(s)] for d, s in zip(dblocks, batch.src_blocks)], dev)
-            if not bulk:
+            hook = None
+            if pull:
+                hook = signal.hook
+            elif not bulk:
                 pusher.begin(pairs, dst, timing=True)
+                hook = pusher.hook
             nxt = pre.prefill(batch.ids, batch.positions, batch.slots, batch.seq_lens, batch.last_rows,
-                              batch.tile_info, layer_hook=None if bulk else pusher.hook,
-                              hook_after_attention=PUSH_AFTER_ATTENTION)
+                              batch.tile_info, layer_hook=hook, hook_after_attention=PUSH_AFTER_ATTENTION)
+            if pull:
+                signal.end()
             # first tokens -> decode inbox, on the push stream after the prefill's head
             pusher.stream.wait_stream(torch.cuda.current_stream(dev))
             if tok_seg is None:
@@ -191,10 +245,16 @@ def run_pd_bench(args, ClockSampler, finalize: bool = True):
                     kv_bytes = bulk_copy(batch.src_blocks, dblocks)
                 ops.copy_segments(tok_seg, TOKEN_BYTES, ready=dst.ready_addr, max_ctas=1, status=pusher.status)
             pusher.join()
-            if not bulk:
+            if mode == "push":
                 kv_bytes = pusher.bytes  # summed over all layers
         if role in ("decode", "both"):
-            ready_target += (0 if bulk else cfg.layers * push_ctas(n_pairs_total, cfg.kv_heads)) + 1
+            if pull:
+                pairs_d = block_pairs(sblocks, [d[:len(s)] for d, s in zip(dblocks, sblocks)], dev)
+                puller.pull(src_view["base"], src_view["layer_stride"], src_view["kv_stride"], cfg.kv_heads,
+                            src_view["blocks"], pairs_d, layer_ctr.data_ptr(), pull_base, timing=True)
+                pull_base += cfg.layers
+                kv_bytes = puller.bytes
+            ready_target += (cfg.layers * push_ctas(n_pairs_total, cfg.kv_heads) if mode == "push" else 0) + 1
             ops.wait_flag(ready.data_ptr(), ready_target, dstatus, timeout_s=30.0)
             db = DecodeBatch(dec_cache, dblocks, lens, dev)
             tok = decode_step(dec, db, inbox[:B], ws)
@@ -210,17 +270,25 @@ def run_pd_bench(args, ClockSampler, finalize: bool = True):
                 sums["src"] = kv_checksum(pre.cache, batch.src_blocks, lens)
             if role in ("decode", "both"):
                 sums["dst"] = kv_checksum(dec_cache, dblocks, lens)
+        kernel_ms = 0.0
         if role in ("prefill", "both"):
-            push_ms = 0.0 if bulk else pusher.push_ms()
+            if mode == "push":
+                push_ms, kernel_ms = pusher.push_ms(), pusher.kernel_ms()
             ops.check_status(pusher.status, "kv push")
             for b in batch.src_blocks:
                 pre.cache.free(b)
         if role in ("decode", "both"):
+            if pull:
+                push_ms, kernel_ms = puller.pull_ms(), puller.kernel_ms()
+                ops.check_status(puller.status, "kv pull")
             ops.check_status(dstatus, "decode wait")
             for b in dblocks:
                 dec_cache.free(b)
-        return {"step_ms": step_ms, "push_ms": push_ms, "kv_bytes": kv_bytes, "tokens": sum(lens),
-                "launches": launches, "lens": lens, "sums": sums}
+        # the rank that ran the transfer kernels reports their bytes and times
+        mover = (role == "decode") if pull else (role in ("prefill", "both"))
+        return {"step_ms": step_ms, "push_ms": push_ms if mover else 0.0, "kernel_ms": kernel_ms if mover else 0.0,
+                "kv_bytes": kv_bytes if mover else 0, "tokens": sum(lens) if role != "decode" else 0,
+                "launches": launches, "lens": lens, "sums": sums, "mover": mover}
 
     def bulk_copy(src_blocks, dst_blocks) -> int:
         """The reference's design: after the whole prefill, copy every layer's
@@ -237,23 +305,29 @@ def run_pd_bench(args, ClockSampler, finalize: bool = True):
                         nbytes += n * hs
         return nbytes
 
+    mode = kv_mode(args, world)
+    other = "push" if mode == "pull" else None
     for w in range(args.warmup):
-        run_step(10_000 + w, False)
+        run_step(10_000 + w, False, mode=mode)
     sampled = _job_gpu_uuids(world, cpu, dev)
     clocks = ClockSampler(sampled) if local == 0 else None
     if clocks:
         clocks.start()
-    recs = [run_step(s, True) for s in range(args.steps)]
+    recs = [run_step(s, True, mode=mode) for s in range(args.steps)]
     clk = clocks.stop() if clocks else None
-    # outside the timed region: KV checksum of one layerwise-push step, then
-    # the bulk-copy design on the same prompts (TTFT comparison)
-    chk = run_step(20_000, False, check=True)
-    n_bulk = max(3, min(args.steps, 8))
-    run_step(30_000, False, bulk=True)
-    bulk = [run_step(s, False, bulk=True) for s in range(n_bulk)]
+    # outside the timed region: KV checksum of one step, the other layerwise
+    # mode on the same prompts, and the bulk-copy design (TTFT comparison)
+    chk = run_step(20_000, False, check=True, mode=mode)
+    n_cmp = max(3, min(args.steps, 8))
+    alt = []
+    if other is not None:
+        run_step(40_000, False, mode=other)
+        alt = [run_step(s, False, mode=other) for s in range(n_cmp)]
+    run_step(30_000, False, mode="bulk")
+    bulk = [run_step(s, False, mode="bulk") for s in range(n_cmp)]
 
     gathered = [None] * world
-    mine = {"role": role, "recs": recs, "clk": clk, "sums": chk["sums"], "bulk": bulk}
+    mine = {"role": role, "recs": recs, "clk": clk, "sums": chk["sums"], "bulk": bulk, "alt": alt}
     if world > 1:
         dist.all_gather_object(gathered, mine, group=cpu)
     else:
@@ -263,14 +337,13 @@ def run_pd_bench(args, ClockSampler, finalize: bool = True):
         K = args.steps
         step_max = [max(g["recs"][s]["step_ms"] for g in gathered) for s in range(K)]
         prod = [g for g in gathered if g["role"] in ("prefill", "both")]
-        kv_total = sum(g["recs"][s]["kv_bytes"] for g in prod for s in range(K))
-        push_max = [max(g["recs"][s]["push_ms"] for g in prod) for s in range(K)]
-        push_sum_by_pair = [sum(g["recs"][s]["push_ms"] for s in range(K)) for g in prod]
-        kv_by_pair = [sum(g["recs"][s]["kv_bytes"] for s in range(K)) for g in prod]
-        # aggregate bandwidth of the push kernels: sum over pairs of bytes / device time
-        value = sum(b / (t * 1e-3) for b, t in zip(kv_by_pair, push_sum_by_pair)) / 1e9
+        movers = [g for g in gathered if g["recs"][0]["mover"]]      # the ranks that ran the KV kernels
+        kv_total = sum(g["recs"][s]["kv_bytes"] for g in movers for s in range(K))
+        push_max = [max(g["recs"][s]["push_ms"] for g in movers) for s in range(K)]
+        value = _pair_rate(movers, "recs", K, "push_ms")
+        window_gbps = _pair_rate(movers, "recs", K, "kernel_ms")
         e2e = kv_total / (sum(step_max) * 1e-3) / 1e9
-        tokens = sum(g["recs"][s]["tokens"] for g in prod for s in range(K))
+        tokens = sum(g["recs"][s]["tokens"] for g in gathered for s in range(K))
         launches = sum(g["recs"][s]["launches"] for g in gathered for s in range(K))
         clk0 = gathered[0]["clk"] or {}
         # KV check: every pair's decode-side blocks equal its prefill-side blocks
@@ -278,15 +351,31 @@ def run_pd_bench(args, ClockSampler, finalize: bool = True):
             ok = gathered[0]["sums"]["src"] == gathered[0]["sums"]["dst"]
         else:
             ok = all(gathered[r]["sums"]["src"] == gathered[r + world // 2]["sums"]["dst"] for r in range(world // 2))
-        bulk_max = [max(g["bulk"][s]["step_ms"] for g in gathered) for s in range(n_bulk)]
+        bulk_max = [max(g["bulk"][s]["step_ms"] for g in gathered) for s in range(n_cmp)]
+        alt_stats = {}
+        if alt:
+            alt_movers = [g for g in gathered if g["alt"][0]["mover"]]
+            alt_max = [max(g["alt"][s]["step_ms"] for g in gathered) for s in range(n_cmp)]
+            alt_stats = {f"kv_{other}_gbps": round(_pair_rate(alt_movers, "alt", n_cmp, "push_ms"), 2),
+                         f"kv_{other}_kernel_window_gbps": round(_pair_rate(alt_movers, "alt", n_cmp, "kernel_ms"), 2),
+                         f"p50_ttft_ms_{other}": round(statistics.median(alt_max), 3)}
         result = {
             "value": round(value, 2), "unit": "GB/s", "n_gpus": world, "steps": K, "warmup": args.warmup,
             "ms_per_step": round(statistics.mean(step_max), 3),
             "p50_ttft_ms": round(statistics.median(step_max), 3),
             "kv_bytes_per_step": kv_total // K,
             "push_ms_per_step_max": round(statistics.mean(push_max), 3),
+            # the same bytes over the push kernels' own execution windows
+            # (%globaltimer, first CTA start to last CTA end): launch and
+            # queueing delays on the push stream excluded
+            "push_kernel_window_gbps": round(window_gbps, 2),
             "prefill_tokens_per_s": round(tokens / (sum(step_max) * 1e-3), 1),
             "kv_check": "ok" if ok else "MISMATCH",
+            "kv_transfer": ("pull: the decode GPU's kernel gathers each layer from the prefill GPU's cache over "
+                            "NVLink as soon as the prefill publishes it" if mode == "pull" else
+                            "push: the prefill GPU's kernel stores each layer into the decode cache right after "
+                            "the layer's KV write"),
+            **alt_stats,
             "p50_ttft_ms_bulk_copy_after_prefill": round(statistics.median(bulk_max), 3),
             "e2e": {"value": round(e2e, 3),
                     "unit": ("GB/s of KV delivered per second of the whole step through connex_b200.runtime.pd "

@@ -37,7 +37,11 @@ __global__ void __launch_bounds__(256) kv_push_kernel(const uint8_t* __restrict_
                                                       uint8_t* dk, uint8_t* dv, const int* __restrict__ pairs,
                                                       int n_pairs, int sH, int dH, int sh0, int dh0, int nh,
                                                       int chunk_bytes, int src_blocks, int dst_blocks,
-                                                      uint32_t* ready, int* status) {
+                                                      uint32_t* ready, int* status,
+                                                      unsigned long long* span) {
+  // span (optional): [first CTA start, last CTA end] in %globaltimer ns -- the
+  // kernel's own execution window, free of launch and queueing delays
+  if (span != nullptr && threadIdx.x == 0) atomicMin(&span[0], (unsigned long long)globaltimer_ns());
   const int lane = threadIdx.x & 31;
   const int wpb = blockDim.x >> 5;
   const long total = (long)n_pairs * 2 * nh;
@@ -65,11 +69,12 @@ __global__ void __launch_bounds__(256) kv_push_kernel(const uint8_t* __restrict_
     }
   }
   signal_done(ready);
+  if (span != nullptr && threadIdx.x == 0) atomicMax(&span[1], (unsigned long long)globaltimer_ns());
 }
 
 int kv_push_layer(const void* src_k, const void* src_v, void* dst_k, void* dst_v, const int* pairs, int n_pairs,
                   int src_heads, int dst_heads, int src_h0, int dst_h0, int n_heads, int chunk_bytes, int src_blocks,
-                  int dst_blocks, uint32_t* ready, int max_ctas, int* status, cudaStream_t s) {
+                  int dst_blocks, uint32_t* ready, int max_ctas, int* status, cudaStream_t s, uint64_t* span) {
   if (n_pairs <= 0) return 0;
   if (chunk_bytes % 16 != 0) throw std::runtime_error("cx kv_push: head slice must be a multiple of 16 bytes");
   const long warps = (long)n_pairs * 2 * n_heads;
@@ -79,7 +84,8 @@ int kv_push_layer(const void* src_k, const void* src_v, void* dst_k, void* dst_v
   kv_push_kernel<<<(int)ctas, 256, 0, s>>>(
       reinterpret_cast<const uint8_t*>(src_k), reinterpret_cast<const uint8_t*>(src_v),
       reinterpret_cast<uint8_t*>(dst_k), reinterpret_cast<uint8_t*>(dst_v), pairs, n_pairs, src_heads, dst_heads,
-      src_h0, dst_h0, n_heads, chunk_bytes, src_blocks, dst_blocks, ready, status);
+      src_h0, dst_h0, n_heads, chunk_bytes, src_blocks, dst_blocks, ready, status,
+      reinterpret_cast<unsigned long long*>(span));
   return (int)ctas;
 }
 

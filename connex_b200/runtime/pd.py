@@ -15,6 +15,15 @@ prefill instance pushes instead, one kernel per layer:
 * the decode stream acquire-waits (bounded, status word on timeout) for the
   counter to reach the value the prefill side announced, then decodes.
 
+The same kernel also runs on the *decode* GPU (:class:`LayerwiseKVPuller`):
+the prefill stream then only publishes a per-layer ready counter in the
+decode GPU's memory (:class:`LayerReadySignal`, one release store per
+layer), and the decode stream acquire-waits for layer l and gathers layer
+l's blocks from the prefill GPU's cache over NVLink into its own block
+table.  The bytes and the overlap with the remaining prefill layers are the
+same; the copy then uses the decode GPU's SMs, which sit idle while a
+request is in prefill, instead of competing with the prefill's kernels.
+
 Hold / acquire / release leases of :mod:`connex.pd.transfer` stay on the
 host, so a decode instance that dies can still re-pull (the KV remains held
 on the prefill side until released).
@@ -75,6 +84,7 @@ class LayerwiseKVPusher:
         self.bytes = 0
         self.timing = False
         self._ev: List[tuple] = []
+        self._span: Optional[torch.Tensor] = None
 
     def begin(self, pairs: torch.Tensor, dst: KVDestination, n_heads: Optional[int] = None,
               src_h0: int = 0, timing: bool = False) -> None:
@@ -85,6 +95,12 @@ class LayerwiseKVPusher:
         self.bytes = 0
         self.timing = timing
         self._ev = []
+        if timing:
+            L = self.src.cfg.layers
+            if self._span is None or self._span.shape[0] < L:
+                self._span = torch.empty(L, 2, dtype=torch.int64, device=self.src.kv.device)
+            self._span[:, 0] = -1          # u64 max: the kernels lower it to their first start
+            self._span[:, 1] = 0
 
     def hook(self, layer: int) -> None:
         """Called on the host right after layer ``layer``'s KV write was enqueued."""
@@ -102,7 +118,8 @@ class LayerwiseKVPusher:
                                   src_h0=self._sh0, dst_h0=d.head_offset, n_heads=self._nh,
                                   chunk_bytes=c.head_slice_bytes, src_blocks=c.num_blocks,
                                   dst_blocks=d.num_blocks, ready=d.ready_addr, max_ctas=self.max_ctas,
-                                  status=self.status)
+                                  status=self.status,
+                                  span=self._span[layer].data_ptr() if self.timing else 0)
             if self.timing:
                 e1 = torch.cuda.Event(enable_timing=True)
                 e1.record(self.stream)
@@ -111,14 +128,106 @@ class LayerwiseKVPusher:
         self.bytes += self._pairs.shape[0] * 2 * self._nh * c.head_slice_bytes
 
     def push_ms(self) -> float:
-        """Summed device time of this batch's push kernels (needs timing=True, synced)."""
+        """Summed time of this batch's push launches from their stream's point
+        of view (CUDA events around each launch; needs timing=True, synced)."""
         return sum(a.elapsed_time(b) for a, b in self._ev)
+
+    def kernel_ms(self) -> float:
+        """Summed execution windows of this batch's push kernels as the
+        kernels themselves saw them (first CTA start to last CTA end)."""
+        if not self._ev:
+            return 0.0
+        sp = self._span[:len(self._ev)].cpu()
+        return float((sp[:, 1] - sp[:, 0]).clamp(min=0).sum()) * 1e-6
 
     def span_events(self):
         return (self._ev[0][0], self._ev[-1][1]) if self._ev else (None, None)
 
     def join(self) -> None:
         torch.cuda.current_stream(self.src.kv.device).wait_stream(self.stream)
+
+
+class LayerReadySignal:
+    """Prefill side of the pull design: right after layer l's KV write the
+    compute stream stores ``base + l + 1`` (release, system scope) into the
+    decode GPU's layer counter (a peer-mapped u32).  Use ``hook`` as the
+    prefill's ``layer_hook``."""
+
+    def __init__(self, counter_addr: int, device, layers: int):
+        self.addr, self.layers = counter_addr, layers
+        self.like = torch.empty(1, device=device)
+        self.base = 0
+
+    def begin(self) -> int:
+        """Start a batch; returns the counter base the decode side waits from."""
+        return self.base
+
+    def hook(self, layer: int) -> None:
+        ops.write_flag(self.addr, self.base + layer + 1, self.like)
+
+    def end(self) -> None:
+        self.base += self.layers
+
+
+class LayerwiseKVPuller:
+    """Decode side of the pull design: for every layer, a bounded
+    acquire-wait on the layer counter, then one ``kv_push_layer`` launch that
+    gathers the layer's (src block, dst block) pairs from the prefill GPU's
+    peer-mapped cache into the local cache.  Everything is enqueued up front
+    on the decode stream; the waits hold the pulls back until the prefill
+    publishes each layer."""
+
+    def __init__(self, dst: PagedKVCache, max_ctas: int = 0, timeout_s: float = 30.0):
+        self.dst = dst
+        self.max_ctas = max_ctas
+        self.timeout_s = timeout_s
+        self.status = ops.new_status(dst.kv.device)
+        self.bytes = 0
+        self._ev: List[tuple] = []
+        self._span: Optional[torch.Tensor] = None
+
+    def pull(self, src_base: int, src_layer_stride: int, src_kv_stride: int, src_heads: int, src_blocks: int,
+             pairs: torch.Tensor, counter_addr: int, base: int, timing: bool = False, src_h0: int = 0,
+             dst_h0: int = 0, n_heads: Optional[int] = None) -> None:
+        """Enqueue the whole batch's pulls on the current stream."""
+        c = self.dst
+        L = c.cfg.layers
+        nh = n_heads if n_heads is not None else c.cfg.kv_heads
+        self._ev = []
+        self.bytes = 0
+        if timing:
+            if self._span is None or self._span.shape[0] < L:
+                self._span = torch.empty(L, 2, dtype=torch.int64, device=c.kv.device)
+            self._span[:, 0] = -1
+            self._span[:, 1] = 0
+        stream = torch.cuda.current_stream(c.kv.device)
+        for layer in range(L):
+            ops.wait_flag(counter_addr, base + layer + 1, self.status, timeout_s=self.timeout_s)
+            with nvtx_range(f"kv pull {layer}"):
+                if timing:
+                    e0 = torch.cuda.Event(enable_timing=True)
+                    e0.record(stream)
+                sk = src_base + layer * src_layer_stride
+                ops.kv_push_layer(sk, sk + src_kv_stride, c.k(layer).data_ptr(), c.v(layer).data_ptr(), pairs,
+                                  src_heads=src_heads, dst_heads=c.cfg.kv_heads, src_h0=src_h0, dst_h0=dst_h0,
+                                  n_heads=nh, chunk_bytes=c.head_slice_bytes, src_blocks=src_blocks,
+                                  dst_blocks=c.num_blocks, max_ctas=self.max_ctas, status=self.status,
+                                  span=self._span[layer].data_ptr() if timing else 0)
+                if timing:
+                    e1 = torch.cuda.Event(enable_timing=True)
+                    e1.record(stream)
+                    self._ev.append((e0, e1))
+            self.bytes += pairs.shape[0] * 2 * nh * c.head_slice_bytes
+
+    def pull_ms(self) -> float:
+        """Summed device time of the pull launches (CUDA events; waits excluded)."""
+        return sum(a.elapsed_time(b) for a, b in self._ev)
+
+    def kernel_ms(self) -> float:
+        if not self._ev:
+            return 0.0
+        sp = self._span[:len(self._ev)].cpu()
+        return float((sp[:, 1] - sp[:, 0]).clamp(min=0).sum()) * 1e-6
 
 
 @dataclass
@@ -139,15 +248,18 @@ class PrefillBatch:
 
 
 def build_prefill_batch(cache: PagedKVCache, prompts: Sequence[Sequence[int]], device,
-                        ids: Optional[torch.Tensor] = None) -> PrefillBatch:
-    """Allocate source blocks and build positions / slots / tile metadata.
-    ``ids`` may be given already on the device (e.g. copied from pinned memory)."""
+                        ids: Optional[torch.Tensor] = None,
+                        blocks: Optional[Sequence[Sequence[int]]] = None) -> PrefillBatch:
+    """Allocate source blocks (or use ``blocks``, allocated earlier) and build
+    positions / slots / tile metadata.  ``ids`` may be given already on the
+    device (e.g. copied from pinned memory)."""
     bs = cache.cfg.block_size
     seq_lens = [len(p) for p in prompts]
+    given = list(blocks) if blocks is not None else None
     blocks, pos, slots, rows = [], [], [], []
     r = 0
-    for n in seq_lens:
-        b = cache.allocate(cache.blocks_needed(n))
+    for i, n in enumerate(seq_lens):
+        b = list(given[i]) if given is not None else cache.allocate(cache.blocks_needed(n))
         blocks.append(b)
         pos.extend(range(n))
         slots.extend(slot_mapping(b, 0, n, bs))

@@ -67,7 +67,7 @@ def test_source_dies_mid_move_is_replanned_from_another_replica():
     eng = _engine(table)
     ctl = EPController(table, eng)
     ctl.push(force=True)
-    src0 = table._pick_src(0, 0, 8)
+    src0 = table.best_source(0, 0, 8, None)
     real_move = eng.move
     calls = {"n": 0}
 

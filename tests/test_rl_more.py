@@ -56,7 +56,7 @@ def test_subscriber_rereads_when_its_source_was_overwritten():
         out = real(url, ops, dst, window, timeout_ms)
         if reads["n"] == 1:                                   # the publisher overwrote its copy meanwhile
             with reg.cv:
-                reg._invalidate(1, PUBLISHER)
+                reg.invalidate(1, PUBLISHER)
         return out
     st.read_window = read_window
     m = sub.pull()
