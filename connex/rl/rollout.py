@@ -1,18 +1,23 @@
 """Rollout pool: route rollouts over elastic engine instances so that no
-request ever mixes two weight versions (reference ``connex/rl/rollout.py:63-237``).
+request ever mixes two weight versions.
 
-A request takes the pool's version when admitted and runs only on an
-instance at exactly that version.  Instances change version only with no
-request in flight (drained, or aborted and re-queued), so:
+Invariant: a request is bound to the pool's version when admitted and runs
+only on an instance at exactly that version, and an instance changes
+version only while no request is in flight on it.  Hence:
 
-* ``add``: the instance catches up to the pool version before serving;
-* ``update(v, rolling=k)``: new requests wait for an instance at ``v``;
-  ``k`` instances at a time stop admitting, drain (or abort past
-  ``drain_timeout``; aborted requests restart at ``v``) and update;
-* an instance that dies mid-request: the request re-runs on another
-  instance of the same version (resuming from the tokens so far when the
-  instance ``supports_resume``), else restarts at the pool version; an
-  instance that fails its update is removed.
+* ``add``: a new instance first catches up to the pool's version;
+* ``update(v, rolling=k)``: the pool moves to ``v`` at once (new requests
+  wait for an instance at ``v``), then updates ``k`` instances at a time --
+  each stops admitting, drains (or, past ``drain_timeout``, has its
+  requests aborted; they restart at ``v``), updates and serves again;
+* an instance that dies mid-request is dropped; the request continues on
+  another instance of the same version (from the tokens so far when the
+  instance ``supports_resume``), or restarts at the pool's version when
+  that version is gone; an instance that fails its update is dropped.
+
+Each request is a small state machine (:class:`_Rollout`): bound version,
+tokens produced so far, instances tried, attempts.
+Behavioural parity: ``connex/rl/rollout.py:32-237`` of the reference.
 """
 from __future__ import annotations
 
@@ -20,6 +25,7 @@ import asyncio
 import enum
 import logging
 import time
+from dataclasses import dataclass, field
 from typing import Dict, List, Optional
 
 log = logging.getLogger("connex.rl.rollout")
@@ -33,7 +39,7 @@ class InstanceState(enum.Enum):
 
 
 class InstanceDead(Exception):
-    """The instance's engine died; ``partial`` = tokens generated so far."""
+    """The instance's engine died; ``partial`` holds the tokens generated so far."""
 
     def __init__(self, msg: str = "", partial=None):
         super().__init__(msg)
@@ -45,7 +51,7 @@ class Aborted(Exception):
 
 
 class RolloutInstance:
-    """What the pool drives (``FakeInstance`` for tests, HTTP engines in
+    """What the pool drives (``FakeInstance`` in tests, HTTP engines in
     :mod:`connex.rl.engines`)."""
 
     name = "instance"
@@ -65,22 +71,40 @@ class RolloutInstance:
         pass
 
 
-class _Member:
+class _Seat:
+    """The pool's view of one instance: its state and its requests in flight."""
+
     def __init__(self, inst: RolloutInstance):
         self.inst = inst
         self.state = InstanceState.JOINING
-        self.inflight: Dict = {}
-        self.idle = asyncio.Event()
-        self.idle.set()
+        self.running: set = set()
+        self.quiet = asyncio.Event()
+        self.quiet.set()
 
-    def enter(self, task, req) -> None:
-        self.inflight[task] = req
-        self.idle.clear()
+    @property
+    def load(self) -> int:
+        return len(self.running)
 
-    def leave(self, task) -> None:
-        self.inflight.pop(task, None)
-        if not self.inflight:
-            self.idle.set()
+    def admit(self, key) -> None:
+        self.running.add(key)
+        self.quiet.clear()
+
+    def finish(self, key) -> None:
+        self.running.discard(key)
+        if not self.running:
+            self.quiet.set()
+
+
+@dataclass
+class _Rollout:
+    version: int
+    tokens: List[int] = field(default_factory=list)      # produced before a death, for resume
+    tried: List[str] = field(default_factory=list)
+    attempts: int = 0
+
+    def rebind(self, version: int) -> None:
+        """Start over at ``version`` (nothing carried over)."""
+        self.version, self.tokens, self.tried = version, [], []
 
 
 class RolloutPool:
@@ -88,23 +112,22 @@ class RolloutPool:
         self.version = version
         self.drain_timeout = drain_timeout
         self.max_attempts = max_attempts
-        self.slots: Dict[str, _Member] = {}
+        self.slots: Dict[str, _Seat] = {}
         self.changed = asyncio.Condition()
         self.stats = {"requests": 0, "completed": 0, "restarted": 0, "resumed": 0, "aborted_for_update": 0,
                       "instance_failures": 0, "failed": 0, "tokens": 0, "updates": []}
 
-    async def _notify(self) -> None:
+    async def _wake(self) -> None:
         async with self.changed:
             self.changed.notify_all()
 
-    async def _set(self, m: _Member, state: InstanceState) -> None:
-        m.state = state
-        await self._notify()
+    async def _move(self, seat: _Seat, state: InstanceState) -> None:
+        seat.state = state
+        await self._wake()
 
-    # ---------------------------------------------------------- membership
+    # ------------------------------------------------------------ instances
     async def add(self, inst: RolloutInstance) -> None:
-        m = _Member(inst)
-        self.slots[inst.name] = m
+        seat = self.slots[inst.name] = _Seat(inst)
         if inst.version != self.version:
             try:
                 await inst.update(self.version)
@@ -112,119 +135,129 @@ class RolloutPool:
                 log.warning("%s could not catch up to v%s: %s", inst.name, self.version, e)
                 self.slots.pop(inst.name, None)
                 raise
-        # came up ahead of the pool (next version already published): park it
-        await self._set(m, InstanceState.SERVING if inst.version == self.version else InstanceState.JOINING)
+        # an instance that came up ahead of the pool waits until the pool moves there
+        await self._move(seat, InstanceState.SERVING if inst.version == self.version else InstanceState.JOINING)
 
     async def remove(self, name: str, drain: bool = True) -> None:
-        m = self.slots.get(name)
-        if m is None:
+        seat = self.slots.get(name)
+        if seat is None:
             return
-        await self._set(m, InstanceState.UPDATING)
+        await self._move(seat, InstanceState.UPDATING)
         if drain:
-            await m.idle.wait()
+            await seat.quiet.wait()
         else:
-            await self._abort(m)
+            await self._abort(seat)
         self.slots.pop(name, None)
-        await m.inst.close()
-        await self._notify()
+        await seat.inst.close()
+        await self._wake()
 
     def mark_dead(self, name: str) -> None:
-        m = self.slots.pop(name, None)
-        if m is not None:
-            m.state = InstanceState.DEAD
+        seat = self.slots.pop(name, None)
+        if seat is not None:
+            seat.state = InstanceState.DEAD
             self.stats["instance_failures"] += 1
 
-    def serving(self, version=None) -> List[_Member]:
-        v = self.version if version is None else version
-        return [m for m in self.slots.values() if m.state is InstanceState.SERVING and m.inst.version == v]
+    def serving(self, version=None) -> List[_Seat]:
+        want = self.version if version is None else version
+        return [s for s in self.slots.values() if s.state is InstanceState.SERVING and s.inst.version == want]
 
-    # ------------------------------------------------------------ requests
-    async def _pick(self, version, exclude=()):
+    # -------------------------------------------------------------- requests
+    async def _seat_for(self, ro: _Rollout) -> Optional[_Seat]:
+        """The least loaded instance serving ``ro.version`` (one not tried yet
+        if possible); waits for one; None when that version is gone."""
         async with self.changed:
             while True:
-                ok = self.serving(version)
-                pref = [m for m in ok if m.inst.name not in exclude] or ok
-                if pref:
-                    return min(pref, key=lambda m: len(m.inflight))
-                if version != self.version:
-                    return None          # the old version is gone
+                ready = self.serving(ro.version)
+                fresh = [s for s in ready if s.inst.name not in ro.tried] or ready
+                if fresh:
+                    return min(fresh, key=lambda s: s.load)
+                if ro.version != self.version:
+                    return None
                 await self.changed.wait()
+
+    async def _attempt(self, seat: _Seat, req, ro: _Rollout) -> List[int]:
+        resume = ro.tokens if ro.tokens and seat.inst.supports_resume else None
+        if resume is None:
+            ro.tokens = []
+        out = await seat.inst.generate(req, partial=resume)
+        return list(resume or []) + list(out["tokens"])
 
     async def generate(self, req) -> dict:
         """One rollout -> ``{"tokens", "version", "instance", "attempts"}``."""
         self.stats["requests"] += 1
-        version, partial, tried, attempts = self.version, [], [], 0
-        task = asyncio.current_task()
-        while attempts < self.max_attempts:
-            m = await self._pick(version, tried)
-            if m is None:
-                version, partial, tried = self.version, [], []
+        ro = _Rollout(self.version)
+        key = object()
+        while ro.attempts < self.max_attempts:
+            seat = await self._seat_for(ro)
+            if seat is None:                       # its version is gone: restart at the pool's
+                ro.rebind(self.version)
                 self.stats["restarted"] += 1
                 continue
-            attempts += 1
-            m.enter(task, req)
+            ro.attempts += 1
+            seat.admit(key)
             try:
-                resume = partial if (partial and m.inst.supports_resume) else None
-                if partial and resume is None:
-                    partial = []
-                out = await m.inst.generate(req, partial=resume)
-                toks = list(resume or []) + list(out["tokens"])
+                tokens = await self._attempt(seat, req, ro)
                 self.stats["completed"] += 1
-                self.stats["tokens"] += len(toks)
-                return {"tokens": toks, "version": version, "instance": m.inst.name, "attempts": attempts}
+                self.stats["tokens"] += len(tokens)
+                return {"tokens": tokens, "version": ro.version, "instance": seat.inst.name, "attempts": ro.attempts}
             except Aborted:
                 self.stats["aborted_for_update"] += 1
-                version, partial, tried = self.version, [], []
+                ro.rebind(self.version)
             except InstanceDead as e:
-                log.warning("instance %s died during a request", m.inst.name)
-                self.mark_dead(m.inst.name)
-                tried.append(m.inst.name)
-                if m.inst.supports_resume and e.partial:
-                    partial = list(partial) + e.partial
+                log.warning("instance %s died during a request", seat.inst.name)
+                self.mark_dead(seat.inst.name)
+                ro.tried.append(seat.inst.name)
+                if seat.inst.supports_resume and e.partial:
+                    ro.tokens = list(ro.tokens) + e.partial
                     self.stats["resumed"] += 1
             finally:
-                m.leave(task)
+                seat.finish(key)
         self.stats["failed"] += 1
-        raise RuntimeError(f"request failed after {attempts} attempts")
+        raise RuntimeError(f"request failed after {ro.attempts} attempts")
 
-    # ------------------------------------------------------------- updates
-    async def _abort(self, m: _Member) -> None:
-        if m.inflight:
-            await m.inst.abort_all()
-            await m.idle.wait()
+    # --------------------------------------------------------------- updates
+    async def _abort(self, seat: _Seat) -> None:
+        if seat.running:
+            await seat.inst.abort_all()
+            await seat.quiet.wait()
 
-    async def _update_one(self, m: _Member, version) -> bool:
-        await self._set(m, InstanceState.UPDATING)
+    async def _quiesce(self, seat: _Seat) -> None:
+        """No request in flight on ``seat`` any more (drained, or aborted after the timeout)."""
         if self.drain_timeout is None:
-            await m.idle.wait()
-        else:
-            try:
-                await asyncio.wait_for(m.idle.wait(), self.drain_timeout)
-            except asyncio.TimeoutError:
-                await self._abort(m)
+            await seat.quiet.wait()
+            return
         try:
-            if m.inst.version != version:
-                await m.inst.update(version)
-            if m.inst.version != version:
-                raise RuntimeError(f"came up at v{m.inst.version}, wanted v{version}")
-        except Exception as e:  # noqa: BLE001
-            log.warning("%s failed to update to v%s: %s; removing it", m.inst.name, version, e)
-            self.mark_dead(m.inst.name)
-            await self._notify()
+            await asyncio.wait_for(seat.quiet.wait(), self.drain_timeout)
+        except asyncio.TimeoutError:
+            await self._abort(seat)
+
+    async def _update_one(self, seat: _Seat, version) -> bool:
+        await self._move(seat, InstanceState.UPDATING)
+        await self._quiesce(seat)
+        try:
+            if seat.inst.version != version:
+                await seat.inst.update(version)
+            if seat.inst.version != version:
+                raise RuntimeError(f"came up at v{seat.inst.version}, wanted v{version}")
+        except Exception as e:  # noqa: BLE001 - the instance is dropped
+            log.warning("%s failed to update to v%s: %s; removing it", seat.inst.name, version, e)
+            self.mark_dead(seat.inst.name)
+            await self._wake()
             return False
-        await self._set(m, InstanceState.SERVING)
+        await self._move(seat, InstanceState.SERVING)
         return True
 
     async def update(self, version, rolling: Optional[int] = None) -> int:
         """Move the pool to ``version``; returns how many instances updated."""
         t0 = time.perf_counter()
         self.version = version
-        await self._notify()
-        members = list(self.slots.values())
-        k = rolling or len(members) or 1
-        ok = 0
-        for i in range(0, len(members), k):
-            ok += sum(await asyncio.gather(*(self._update_one(m, version) for m in members[i:i + k])))
-        self.stats["updates"].append({"version": version, "s": time.perf_counter() - t0, "instances": ok,
-                                      "of": len(members)})
-        return ok
+        await self._wake()
+        seats = list(self.slots.values())
+        width = rolling or len(seats) or 1
+        updated = 0
+        for start in range(0, len(seats), width):
+            wave = seats[start:start + width]
+            updated += sum(await asyncio.gather(*(self._update_one(s, version) for s in wave)))
+        self.stats["updates"].append({"version": version, "s": time.perf_counter() - t0, "instances": updated,
+                                      "of": len(seats)})
+        return updated

@@ -1,17 +1,22 @@
-"""Trainer-side publisher and engine-side subscriber (reference
-``connex/rl/sync.py:41-259``).
+"""Trainer-side publisher and engine-side subscriber of elastic weight sync.
 
-Publisher: pack version ``v`` into one of ``buffers`` registered arenas (the
-slot of the oldest version is reused only after its readers drained, or
-after ``idle_timeout``, in which case those readers are told their copy is
-stale and read again), then announce ``v`` and its manifest.
+:class:`WeightPublisher`
+    Packs version ``v`` into one of ``buffers`` registered arenas and
+    announces it with its manifest.  The arena slot of the oldest version is
+    reused only after its readers drained -- or after ``idle_timeout``, in
+    which case the registry tells those readers their copy is stale and they
+    read again.
 
-Subscriber: ask the registry for a source of the latest version, pull the
-arena in ``chunk_bytes`` pieces (``window`` in flight), and on a failed read
-report the source, take another one and continue from the first chunk that
-did not arrive.  The publisher always holds ``v``, so the pull ends while it
-lives.  ``apply`` gets the whole version in one call; ``commit`` then offers
-the copy to later pullers (tree fan-out) unless ``relay`` is off.
+:class:`WeightSubscriber`
+    Asks the registry for a source of the latest version and pulls the arena
+    as a :class:`_Download`: fixed-size chunks read through a rolling window;
+    when a read fails the source is reported, another one is taken and the
+    download resumes at the first chunk that did not arrive.  The publisher
+    always holds the version, so a download finishes while it lives.  After
+    ``apply`` (the whole version in one call) ``commit`` offers the copy to
+    later readers (tree fan-out) unless ``relay`` is off.
+
+Behavioural parity: ``connex/rl/sync.py:29-259`` of the reference.
 """
 from __future__ import annotations
 
@@ -19,7 +24,8 @@ import logging
 import os
 import threading
 import time
-from typing import Callable, Iterable, List, Optional, Tuple
+from dataclasses import dataclass, field
+from typing import Callable, Iterable, List, Optional, Set, Tuple
 
 import torch
 
@@ -46,43 +52,77 @@ class WeightPublisher:
         self.t = transport
         self.device = torch.device(device)
         self.nbuf = max(1, buffers)
-        self.arenas: List[list] = []       # [tensor, version]
+        self.arenas: List[list] = []       # [tensor, version held]
         self.manifest: Optional[WeightManifest] = None
         self.version = 0
         self.idle_timeout = idle_timeout
 
+    def _new_arena(self, nbytes: int) -> torch.Tensor:
+        a = torch.empty(nbytes, dtype=torch.uint8, device=self.device)
+        self.t.register(a)
+        return a
+
+    def _retire(self, version: int) -> None:
+        """Wait (bounded) until nobody reads ``version`` from us any more."""
+        r = self.reg.wait_idle(version=version, member=PUBLISHER, timeout=self.idle_timeout, retire=True)
+        if not (r or {}).get("ok", True):
+            log.warning("publisher: v%s still read after %.0fs; overwriting (readers re-read)", version,
+                        self.idle_timeout)
+
     def _slot(self, need: int) -> int:
+        """An arena slot of at least ``need`` bytes for the next version."""
         if len(self.arenas) < self.nbuf:
-            a = torch.empty(need, dtype=torch.uint8, device=self.device)
-            self.t.register(a)
-            self.arenas.append([a, None])
+            self.arenas.append([self._new_arena(need), None])
             return len(self.arenas) - 1
         slot = min(range(self.nbuf), key=lambda i: self.arenas[i][1])
-        a, old = self.arenas[slot]
-        if old is not None:
-            r = self.reg.wait_idle(version=old, member=PUBLISHER, timeout=self.idle_timeout, retire=True)
-            if not (r or {}).get("ok", True):
-                log.warning("publisher: v%s still read after %.0fs; overwriting (readers re-read)",
-                            old, self.idle_timeout)
-        if a.numel() < need:
-            self.t.unregister(a)
-            a = torch.empty(need, dtype=torch.uint8, device=self.device)
-            self.t.register(a)
-            self.arenas[slot][0] = a
+        arena, held = self.arenas[slot]
+        if held is not None:
+            self._retire(held)
+        if arena.numel() < need:
+            self.t.unregister(arena)
+            self.arenas[slot][0] = self._new_arena(need)
         return slot
 
     def publish(self, named: Iterable[Tuple[str, torch.Tensor]], version: Optional[int] = None) -> int:
         named = list(named)
         v = self.version + 1 if version is None else version
-        m = WeightManifest.build(v, named)
-        slot = self._slot(m.total)
-        a = self.arenas[slot][0]
-        pack_into(a, m, named)
-        _stream_sync(a)
+        manifest = WeightManifest.build(v, named)
+        slot = self._slot(manifest.total)
+        arena = self.arenas[slot][0]
+        pack_into(arena, manifest, named)
+        _stream_sync(arena)
         self.arenas[slot][1] = v
-        self.reg.publish(version=v, manifest=m.to_dict(), url=self.t.url, addr=a.data_ptr())
-        self.version, self.manifest = v, m
+        self.reg.publish(version=v, manifest=manifest.to_dict(), url=self.t.url, addr=arena.data_ptr())
+        self.version, self.manifest = v, manifest
         return v
+
+
+@dataclass
+class _Download:
+    """One version's arena, fetched chunk by chunk from changing sources."""
+
+    version: int
+    total: int
+    chunk: int
+    next_chunk: int = 0                       # first chunk not yet read
+    failures: int = 0
+    stale: bool = False                       # some source overwrote its copy while we read it
+    excluded: Set[str] = field(default_factory=set)
+    sources: List[str] = field(default_factory=list)
+    source: Optional[dict] = None             # the current assignment
+
+    @property
+    def offsets(self) -> List[int]:
+        return list(range(0, self.total, self.chunk))
+
+    @property
+    def finished(self) -> bool:
+        return self.next_chunk >= len(self.offsets)
+
+    def remaining_ops(self) -> list:
+        """(remote address, local offset, bytes) of every chunk still missing."""
+        base = self.source["addr"]
+        return [(base + o, o, min(self.chunk, self.total - o)) for o in self.offsets[self.next_chunk:]]
 
 
 class WeightSubscriber:
@@ -90,8 +130,7 @@ class WeightSubscriber:
 
     ``arena``: ``"device"`` (default) or ``"host"`` (pinned host memory, no
     second device copy; env ``CONNEX_RL_ARENA``).  ``relay=False`` (env
-    ``CONNEX_RL_RELAY=0``) frees the copy after apply instead of serving it.
-    """
+    ``CONNEX_RL_RELAY=0``) frees the copy after apply instead of serving it."""
 
     def __init__(self, registry, transport, member: str, device="cpu", chunk_bytes: int = DEFAULT_CHUNK,
                  max_source_failures: int = 16, heartbeat_s: float = 2.0, window: int = 16,
@@ -123,7 +162,7 @@ class WeightSubscriber:
         while not self._stop.wait(every):
             try:
                 if not self.reg.heartbeat(member=self.member)["ok"]:
-                    self.reg.join(member=self.member, url=self.t.url)
+                    self.reg.join(member=self.member, url=self.t.url)     # expired meanwhile: rejoin
             except Exception:  # noqa: BLE001 - the registry may be restarting
                 pass
 
@@ -131,8 +170,7 @@ class WeightSubscriber:
         lt = self.reg.get_latest()
         return None if lt is None else lt["version"]
 
-    def pull(self, version: Optional[int] = None) -> WeightManifest:
-        """Fetch the latest version (at least ``version``) into the arena."""
+    def _target(self, version: Optional[int]) -> dict:
         lt = self.reg.get_latest()
         if lt is None:
             raise RuntimeError("no weight version published yet")
@@ -140,26 +178,27 @@ class WeightSubscriber:
             lt = self.reg.get_latest(wait_newer_than=version - 1, timeout=60.0)
             if lt is None or lt["version"] < version:
                 raise RuntimeError(f"version {version} not published")
-        v, m = lt["version"], WeightManifest.from_dict(lt["manifest"])
+        return lt
+
+    def pull(self, version: Optional[int] = None) -> WeightManifest:
+        """Fetch the latest version (at least ``version``) into the arena."""
+        lt = self._target(version)
+        v, manifest = lt["version"], WeightManifest.from_dict(lt["manifest"])
         t0 = time.perf_counter()
         if self.arena is not None:
-            self.reg.retract(member=self.member)   # stop serving the copy about to be overwritten
+            self.reg.retract(member=self.member)     # stop serving the copy we are about to overwrite
         self.manifest = None
         for _ in range(3):
-            stale, failures, sources = self._read(v, m)
-            if not stale:
+            dl = self._download(v, manifest)
+            if not dl.stale:
                 break
             log.warning("%s: a source of v%d overwrote its copy mid-read; reading again", self.member, v)
         else:
             raise RuntimeError(f"v{v}: sources kept changing during the read")
-        self.manifest = m
-        self.stats = {"version": v, "bytes": m.total, "pull_s": time.perf_counter() - t0,
-                      "sources": sources, "source_failures": failures}
-        return m
-
-    def _release(self, version: int, source: str) -> bool:
-        r = self.reg.release(version=version, source=source, member=self.member)
-        return bool((r or {}).get("stale"))
+        self.manifest = manifest
+        self.stats = {"version": v, "bytes": manifest.total, "pull_s": time.perf_counter() - t0,
+                      "sources": dl.sources, "source_failures": dl.failures}
+        return manifest
 
     def _ensure_arena(self, total: int) -> None:
         if self.arena is not None and self.arena.numel() >= total:
@@ -167,48 +206,55 @@ class WeightSubscriber:
         if self.arena is not None:
             self.t.unregister(self.arena)
         self.arena = torch.empty(total, dtype=torch.uint8, device=self.device, pin_memory=self.pin)
-        _stream_sync(self.arena)   # the previous user of this memory must be done
+        _stream_sync(self.arena)                    # the previous user of this memory must be done
         self.t.register(self.arena)
 
-    def _read(self, version: int, m: WeightManifest):
-        self._ensure_arena(m.total)
-        offs = list(range(0, m.total, self.chunk))
-        stale, failures, bad, sources = False, 0, set(), []
-        src = None
-        i = 0
+    def _let_go(self, dl: _Download) -> None:
+        """Release the current assignment; a stale answer marks the download."""
+        if dl.source is None:
+            return
+        r = self.reg.release(version=dl.version, source=dl.source["member"], member=self.member)
+        dl.stale |= bool((r or {}).get("stale"))
+        dl.source = None
+
+    def _take_source(self, dl: _Download) -> None:
+        dl.source = self.reg.assign(version=dl.version, member=self.member, exclude=sorted(dl.excluded))
+        if dl.source is None:
+            raise RuntimeError(f"no source holds version {dl.version}")
+        dl.sources.append(dl.source["member"])
+
+    def _source_failed(self, dl: _Download, err: TransferError) -> None:
+        name = dl.source["member"]
+        dl.next_chunk += getattr(err, "done", 0)        # the chunks before the failure did arrive
+        dl.failures += 1
+        log.warning("%s: read of v%d from %s failed (%s); switching source", self.member, dl.version, name, err)
+        self.reg.report_failure(version=dl.version, source=name, reporter=self.member)
+        self._let_go(dl)
+        if name != PUBLISHER:
+            dl.excluded.add(name)
+        if dl.failures > self.max_fail:
+            raise err
+
+    def _download(self, version: int, manifest: WeightManifest) -> _Download:
+        self._ensure_arena(manifest.total)
+        dl = _Download(version, manifest.total, self.chunk)
         try:
-            while i < len(offs):
-                if src is None:
-                    src = self.reg.assign(version=version, member=self.member, exclude=sorted(bad))
-                    if src is None:
-                        raise RuntimeError(f"no source holds version {version}")
-                    sources.append(src["member"])
-                ops = [(src["addr"] + o, o, min(self.chunk, m.total - o)) for o in offs[i:]]
+            while not dl.finished:
+                if dl.source is None:
+                    self._take_source(dl)
                 try:
-                    self.t.read_window(src["url"], ops, self.arena, self.window)
-                    i = len(offs)
+                    self.t.read_window(dl.source["url"], dl.remaining_ops(), self.arena, self.window)
+                    dl.next_chunk = len(dl.offsets)
                 except TransferError as e:
-                    i += getattr(e, "done", 0)
-                    failures += 1
-                    log.warning("%s: read of v%d from %s failed (%s); switching source",
-                                self.member, version, src["member"], e)
-                    self.reg.report_failure(version=version, source=src["member"], reporter=self.member)
-                    stale |= self._release(version, src["member"])
-                    if src["member"] != PUBLISHER:
-                        bad.add(src["member"])
-                    src = None
-                    if failures > self.max_fail:
-                        raise
+                    self._source_failed(dl, e)
         except BaseException:
-            if src is not None:
-                try:
-                    self._release(version, src["member"])
-                except Exception:  # noqa: BLE001
-                    pass
+            try:
+                self._let_go(dl)
+            except Exception:  # noqa: BLE001
+                pass
             raise
-        if src is not None:
-            stale |= self._release(version, src["member"])
-        return stale, failures, sources
+        self._let_go(dl)
+        return dl
 
     def tensors(self):
         return unpack(self.arena, self.manifest)
@@ -224,12 +270,12 @@ class WeightSubscriber:
 
     def sync(self, apply: Callable, version: Optional[int] = None) -> dict:
         """pull + ``apply(iterable of (name, tensor))`` + commit; returns stats."""
-        m = self.pull(version)
+        manifest = self.pull(version)
         t0 = time.perf_counter()
         apply(self.tensors())
         _stream_sync(self.arena)
         self.stats["apply_s"] = time.perf_counter() - t0
-        self.commit(m.version)
+        self.commit(manifest.version)
         return self.stats
 
     def close(self, leave: bool = True) -> None:

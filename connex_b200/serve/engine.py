@@ -66,9 +66,10 @@ class Stepper:
 
 
 class RuleStepper(Stepper):
-    """Greedy stand-in on the CPU: ``next = (37 a + 11 b + 5) mod (V - 16) + 16``
-    of the last two ids -- the rule of ``connex.serving.fake_backend``, so a
-    continuation from ``prompt + partial output`` equals the uninterrupted one."""
+    """Greedy stand-in on the CPU: the next id is
+    :func:`connex.serving.fake_backend.next_token` of the last two ids (the
+    fake HTTP backend's rule), so a continuation from ``prompt + partial
+    output`` equals the uninterrupted one."""
 
     def __init__(self, vocab_size: int = 1000, max_batch: int = 64, max_ctx: int = 4096, num_blocks: int = 1 << 20,
                  step_delay_s: float = 0.0, fail_on: Optional[Callable[[str, List[str]], bool]] = None):
@@ -79,9 +80,8 @@ class RuleStepper(Stepper):
         self.calls: List[tuple] = []
 
     def _next(self, seq):
-        a = seq[-1] if seq else 0
-        b = seq[-2] if len(seq) > 1 else 0
-        return (a * 37 + b * 11 + 5) % (self.vocab_size - 16) + 16
+        from connex.serving.fake_backend import next_token
+        return next_token(seq, self.vocab_size)
 
     def _step(self, kind, rids, seqs):
         self.calls.append((kind, list(rids)))
@@ -141,6 +141,7 @@ class RuleStageRuntime:
             return {"kind": "warmup", "w": td["w"].clone()}
         if self.delay_s:
             time.sleep(self.delay_s)
+        from connex.serving.fake_backend import next_token
         rids, ctx, n_new = list(td[REQUEST_IDS]), list(td[CX_CTX]), list(td["n_new"])
         x = (td["ids"] if self.first else td["x"]).to(torch.int64).tolist()
         i, nxt = 0, []
@@ -150,8 +151,7 @@ class RuleStageRuntime:
             i += n
             if r not in missing:
                 self.seqs[r] = seq
-            a, b = seq[-1], seq[-2] if len(seq) > 1 else 0
-            nxt.append((a * 37 + b * 11 + 5) % (self.vocab - 16) + 16)
+            nxt.append(next_token(seq, self.vocab))
         self.steps += 1
         out = {"kind": td["kind"], "n_new": n_new}
         if self.last:

@@ -250,14 +250,14 @@ def test_sglang_control_payload_and_loader(monkeypatch):
             def load_weights(self, named):
                 self.got = dict(named)
         monkeypatch.setenv("CONNEX_RL_DEVICE", "cpu")
-        monkeypatch.setattr(sglang_ext, "_sub", None)
+        sglang_ext.reset_subscriber()
         m = Model()
         sglang_ext.connex_load(m, payload)
         assert torch.equal(m.got["b"], weights_for(4)[1][1]) and sglang_ext.last_stats["version"] == 4
         m2 = Model()
         sglang_ext.connex_load(m2, [("x", torch.ones(2))])   # plain tensors pass through
         assert torch.equal(m2.got["x"], torch.ones(2))
-        sglang_ext._sub.close()
+        sglang_ext.reset_subscriber()
     finally:
         srv.close()
 
