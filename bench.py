@@ -51,26 +51,94 @@ METRIC = "PD KV GB/s + p50 TTFT; EP dispatch+combine µs; weight-sync s; failove
 
 
 def reference_arm(args) -> None:
+    """The reference's own PD KV hand-off on this machine (see
+    ``connex_b200/bench/reference_pd.py``): its ``KVProducer.hold`` /
+    ``KVConsumer.pull`` with the data plane its stock selection takes here
+    (pinned host staging over the in-process loopback plane; connex-rs and
+    Mooncake are not installed).  One pair per prefill rank: rank r's
+    process drives GPU r (prefill cache) and GPU r + N/2 (decode cache);
+    N = 1 keeps both caches on GPU 0.  Host clock around each hand-off
+    (the reference's data plane here is host code), max over pairs."""
+    world, rank = int(os.environ.get("WORLD_SIZE", "1")), int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
     ref = os.path.join(ROOT, "baseline", "_ref")
-    reason = None
+
+    def say(obj):
+        if rank == 0:
+            print(json.dumps(obj), flush=True)
     if not os.path.isdir(os.path.join(ref, "connex")):
-        reason = "reference not installed under baseline/_ref"
-    else:
-        # Probe the reference's stock PD data-plane selection in a clean interpreter
-        # (our own `connex` package must not shadow it).
-        code = ("import sys; sys.path.insert(0, %r); import importlib.util as u;"
-                "print('connex_rs' if u.find_spec('connex_rs') else '',"
-                " 'mooncake' if u.find_spec('mooncake') else '')") % ref
-        out = subprocess.run([sys.executable, "-I", "-c", code], capture_output=True, text=True,
-                             cwd="/", timeout=120).stdout.strip()
-        if not out:
-            reason = ("reference PD KV data plane needs connex-rs (empty git submodule, no Rust "
-                      "toolchain) or Mooncake/UCX (not installed); its stock path cannot move GPU KV offline")
-    if reason is not None:
-        if int(os.environ.get("RANK", "0")) == 0:
-            print(json.dumps({"impl": "reference", "unavailable": reason}), flush=True)
+        say({"impl": "reference", "unavailable": "reference not installed under baseline/_ref"})
         return
-    raise SystemExit("reference data plane present but no driver for it is implemented")
+    if world > 1 and world % 2:
+        say({"impl": "reference", "unavailable": "needs an even number of GPUs (prefill/decode pairs)"})
+        return
+    import torch
+    cpu = None
+    if world > 1:
+        import torch.distributed as dist
+        from datetime import timedelta
+        dist.init_process_group("gloo", timeout=timedelta(seconds=900))
+        cpu = dist.group.WORLD
+    mover = world == 1 or rank < world // 2
+    src, dst = (local, local if world == 1 else local + world // 2)
+    uuids = []
+    for d in sorted({src, dst}):
+        u = str(torch.cuda.get_device_properties(d).uuid)
+        uuids.append(u if u.startswith("GPU-") else "GPU-" + u)
+    out, err, clk = None, None, None
+    if mover:
+        cmd = [sys.executable, "-I", os.path.join(ROOT, "connex_b200", "bench", "reference_pd.py"), "--ref", ref,
+               "--src-device", str(src), "--dst-device", str(dst), "--steps", str(args.steps),
+               "--warmup", str(args.warmup), "--batch", str(args.batch), "--min-len", str(args.min_len),
+               "--max-len", str(args.max_len), "--layers", str(args.layers), "--seed", str(args.seed)]
+        clocks = ClockSampler(uuids)
+        clocks.start()
+        r = subprocess.run(cmd, capture_output=True, text=True, cwd="/tmp", timeout=1800)
+        clk = clocks.stop()
+        lines = [x for x in r.stdout.splitlines() if x.startswith("{")]
+        if r.returncode != 0 or not lines:
+            err = (r.stderr.strip().splitlines() or ["no output"])[-1][:300]
+        else:
+            out = json.loads(lines[-1])
+    allr = [{"out": out, "err": err, "clk": clk, "mover": mover}]
+    if world > 1:
+        import torch.distributed as dist
+        allr = [None] * world
+        dist.all_gather_object(allr, {"out": out, "err": err, "clk": clk, "mover": mover}, group=cpu)
+        dist.destroy_process_group()
+    if rank != 0:
+        return
+    errs = [x["err"] for x in allr if x["mover"] and x["err"]]
+    if errs:
+        say({"impl": "reference", "unavailable": f"reference PD hand-off failed on this machine: {errs[0]}"})
+        return
+    runs = [x["out"] for x in allr if x["mover"]]
+    K = args.steps
+    value = sum(sum(r["bytes"] for r in o["recs"]) / sum(r["pull_s"] for r in o["recs"]) for o in runs) / 1e9
+    step_max = [max(o["recs"][s]["step_s"] for o in runs) for s in range(K)]
+    kv_total = sum(r["bytes"] for o in runs for r in o["recs"])
+    clk0 = allr[0]["clk"] or {}
+    say({"impl": "reference", "metric": METRIC, "value": round(value, 3), "unit": "GB/s", "n_gpus": world,
+         "steps": K, "warmup": args.warmup, "ms_per_step": round(1e3 * statistics.mean(step_max), 3),
+         "higher_is_better": True, "scaling": "weak",
+         "vs_baseline": round(value / PUBLISHED_KV_GBPS, 3),
+         "e2e": {"value": round(kv_total / sum(step_max) / 1e9, 3),
+                 "unit": "GB/s of KV delivered per second of hand-off (hold incl. device->host staging, "
+                         "until every pull is back on the decode GPU)",
+                 "h2d_bytes_per_step": kv_total // K, "d2h_bytes_per_step": kv_total // K},
+         "kv_check": "ok" if all(o["kv_check"] for o in runs) else "MISMATCH",
+         "kv_bytes_per_step": kv_total // K,
+         "gpu_launches": 0,
+         "clocks": {"sm_mhz": clk0.get("sm_mhz"), "sm_max_mhz": clk0.get("sm_max_mhz"),
+                    "reasons": clk0.get("reasons", [])},
+         "dtype": "bf16", "data": "synthetic (random KV contents; prompt lengths drawn as in the flagship, seed 0)",
+         "timing": "host clock (the reference's data plane on this machine is host code); max over pairs",
+         "config": {"model": f"Llama-3-8B KV geometry ({args.layers} layers x 8 KV heads x 128, 16-token blocks)",
+                    "global_batch": args.batch * len(runs), "seq_len": f"uniform {args.min_len}-{args.max_len}",
+                    "parallelism": "colocated 1P1D" if world == 1 else f"pd {world // 2}P{world // 2}D (TP1)",
+                    "data_plane": "reference KVProducer/KVConsumer, host staging + in-process loopback plane "
+                                  "(connex-rs / Mooncake not installed, no GPUDirect peer-memory driver)",
+                    "l2": "inputs larger than L2 (GB-scale KV)"}})
 
 
 class ClockSampler:

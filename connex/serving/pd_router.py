@@ -1,26 +1,30 @@
-"""PD router: prefill, then decode, over elastic prefill and decode pools
-(reference ``connex/serving/pd_router.py:68-559``).
+"""PD router: prefill, then decode, over elastic prefill and decode pools.
 
-Per request (vLLM mode): the prompt goes to a prefill instance with
+vLLM mode, per request: the prompt goes to a prefill instance with
 ``max_tokens=1`` and ``kv_transfer_params={"do_remote_decode": true,
-"transfer_id": ...}``; the response's ``kv_transfer_params`` then go with the
-streamed request to a decode instance, which pulls the prompt KV.  SGLang
-mode sends prefill and decode together, paired by a ``bootstrap_room``.
+"transfer_id": ...}``; the ``kv_transfer_params`` of its answer then go with
+the streamed request to a decode instance, which pulls the prompt's KV.
+SGLang mode sends prefill and decode together, paired by a
+``bootstrap_room``; the prefill's outcome guards the decode's first token.
 
-Pools are the union of static URLs, files re-read every second and the
-front-router's PD registrations; a new member serves once a probe succeeds;
-``POST /pd/drain`` (loopback or bearer token) stops new traffic to a member.
+Pools (:class:`ElasticPool`) are the union of static URLs, a file re-read
+every second and the front router's PD registrations; a new member takes
+traffic once a probe succeeded; ``POST /pd/drain`` / ``/pd/undrain``
+(loopback or a bearer token) stop / resume new traffic to a member.
 
-Failures, on top of the resume proxy:
+Failures, on top of the resume proxy (:mod:`connex.serving.proxy`):
 
 * a failed prefill is retried on another prefill instance;
-* a decode that fails before its first token while it is alive (its KV pull
-  failed) triggers a fresh prefill elsewhere;
+* a decode that fails before its first token while it still answers probes
+  failed its KV hand-off: prefill again elsewhere, without blaming it;
 * a decode that dies after k tokens resumes on another decode instance with
-  prompt + k ids and ``max_tokens - k``, re-pulling the held KV when the
-  prefill still holds it, else prefilling again;
+  prompt + k ids and ``max_tokens - k``, re-pulling the held KV when its
+  prefill instance still holds it, else prefilling the extended prompt;
 * a front-router failure event (``connex.endpoint_deregistered`` with a
   failure reason) cuts the member's streams at once.
+
+Behavioural parity: ``connex/serving/pd_router.py:68-559`` of the reference
+(routes, flags, request fields); the structure here is this module's own.
 """
 from __future__ import annotations
 
@@ -42,10 +46,14 @@ from connex.serving.proxy import RETRYABLE, Endpoint, Pool, Proxy, Resumer, Stre
 log = logging.getLogger("connex.pd_router")
 
 UNPROBED = 1e18      # bad_until of a member that has not answered a probe yet
+_NOT_FOR_PREFILL = ("stream_options", "logprobs", "top_logprobs", "return_tokens_as_token_ids", "min_tokens",
+                    "kv_transfer_params")
 
 
 class ElasticPool(Pool):
-    """Static URLs + endpoints file + a dynamic source; new members wait for a probe."""
+    """Members from three sources -- static URLs, an endpoints file, a dynamic
+    list (the front router's registrations) -- minus drained members; a new
+    member starts unprobed (no traffic) unless ``probe_new`` is off."""
 
     def __init__(self, urls=(), endpoints_file=None, blacklist_s: float = 5.0, probe_new: bool = True):
         self.static = [u.strip().rstrip("/") for u in urls if u.strip()]
@@ -55,25 +63,24 @@ class ElasticPool(Pool):
         super().__init__(self.static, endpoints_file, blacklist_s)
 
     def set_urls(self, urls) -> None:
-        urls = [u.strip().rstrip("/") for u in urls if u.strip()]
-        for u in urls:
+        merged = list(dict.fromkeys(u.strip().rstrip("/") for u in urls if u.strip()))
+        for u in merged:
             if u not in self.eps:
-                ep = Endpoint(u)
+                ep = self.eps[u] = Endpoint(u)
                 if self.probe_new:
                     ep.bad_until = UNPROBED
-                self.eps[u] = ep
-        order = [u for u in dict.fromkeys(urls) if u not in self.drained]
-        if order != self.order:
-            log.info("pool: +%s -%s", sorted(set(order) - set(self.order)), sorted(set(self.order) - set(order)))
-        self.order = order
+        listed = [u for u in merged if u not in self.drained]
+        if listed != self.order:
+            log.info("pool: +%s -%s", sorted(set(listed) - set(self.order)), sorted(set(self.order) - set(listed)))
+        self.order = listed
+
+    def refresh(self) -> None:
+        from_file = (self._file_urls() or []) if self.file else []
+        self.set_urls(self.static + from_file + self.dynamic)
 
     def set_dynamic(self, urls) -> None:
         self.dynamic = list(urls)
         self.refresh()
-
-    def refresh(self) -> None:
-        file_urls = (self._file_urls() or []) if self.file else []
-        self.set_urls(self.static + file_urls + self.dynamic)
 
     def reload(self) -> None:
         self.refresh()
@@ -97,16 +104,26 @@ class PrefillFailed(UpstreamFailed):
 
 
 class PDResumer(Resumer):
+    """A request with its prompt KV: ``kv`` (the ``kv_transfer_params`` the
+    decode pulls with), the prefill instance holding it (``kv_ep``) and the
+    completion tokens already out when it was made (``kv_tokens``)."""
+
     def __init__(self, proxy, kind, body):
         super().__init__(proxy, kind, body)
         self.kv: Optional[dict] = None
         self.kv_ep: Optional[Endpoint] = None
-        self.kv_tokens = 0            # completion tokens already out when the KV was made
+        self.kv_tokens = 0
         self.prefills = 0
-        self.avoid_prefill: Optional[Endpoint] = None
-        self.spare_endpoint = False
-        self.prefill_task = None
-        self.abort_first = None
+        self.avoid_prefill: Optional[Endpoint] = None   # the next prefill goes elsewhere
+        self.prefill_task: Optional[asyncio.Future] = None  # SGLang: the paired prefill request
+        self._guard = None
+
+    def _kv_reusable(self) -> bool:
+        """The held prompt KV serves the next decode attempt only while its
+        holder lives and the new prompt extends it id for id."""
+        if self.kv_ep is None or not self.kv_ep.healthy(time.monotonic()):
+            return False
+        return self.k == self.kv_tokens or (self.use_ids and not self.chat)
 
     async def build(self, ep):
         b = await super().build(ep)
@@ -114,11 +131,7 @@ class PDResumer(Resumer):
             await self.p.sglang_dispatch(self, b)
             return b
         if self.kv is not None:
-            reuse = self.kv_ep is not None and self.kv_ep.healthy(time.monotonic())
-            # the held prompt KV is reusable only if the new prompt extends it id for id
-            if self.k != self.kv_tokens and not (self.use_ids and not self.chat):
-                reuse = False
-            if not reuse:
+            if not self._kv_reusable():
                 self.kv = None
             elif self.k > 0:
                 self.p.stats["kv_repulls"] += 1
@@ -127,6 +140,9 @@ class PDResumer(Resumer):
             self.kv_tokens = self.k
         b["kv_transfer_params"] = dict(self.kv)
         return b
+
+    def first_token_guard(self):
+        return self._guard
 
 
 class PDRouter(Proxy):
@@ -151,7 +167,7 @@ class PDRouter(Proxy):
             front_router_events = front_router.rsplit(":", 1)[0] + ":15560"
         self.front_router_events = front_router_events
         self.admin_token = os.getenv("CONNEX_PD_ADMIN_TOKEN") or None
-        self._members: Dict[Tuple[str, int], str] = {}
+        self._members: Dict[Tuple[str, int], str] = {}      # (role, replica) -> URL
         self.stats.update({"prefills": 0, "prefill_retries": 0, "kv_reprefills": 0, "kv_repulls": 0,
                            "membership_errors": 0, "failure_events": 0})
 
@@ -165,34 +181,44 @@ class PDRouter(Proxy):
     async def _startup(self, app=None):
         await super()._startup(app)
         if self.prefill_pool.file:
-            self._bg.append(asyncio.create_task(self._every(1.0, self.prefill_pool.reload)))
+            self._background(self._every(1.0, self.prefill_pool.reload))
         if self.front_router:
-            self._bg.append(asyncio.create_task(self._membership_loop()))
+            self._background(self._membership_loop())
             if self.front_router_events:
-                self._bg.append(asyncio.create_task(self._failure_events_loop()))
+                self._background(self._failure_events_loop())
+
+    def _pool_of(self, role_or_ep) -> ElasticPool:
+        if isinstance(role_or_ep, Endpoint):
+            return self.prefill_pool if role_or_ep.url in self.prefill_pool.eps else self.pool
+        return self.prefill_pool if role_or_ep == "prefill" else self.pool
+
+    # ------------------------------------------------------------ membership
+    def _apply_membership(self, pools) -> None:
+        from connex.protocol import PDRole
+        for m in pools[PDRole.PREFILL]:
+            if m.kv_addr:
+                self.bootstrap[m.url] = m.kv_addr
+        for role in (PDRole.PREFILL, PDRole.DECODE):
+            for m in pools[role]:
+                self._members[(role, m.replica)] = m.url
+        self.prefill_pool.set_dynamic([m.url for m in pools[PDRole.PREFILL]])
+        self.pool.set_dynamic([m.url for m in pools[PDRole.DECODE]])
 
     async def _membership_loop(self):
         from connex.pd.membership import fetch_pools
-        from connex.protocol import PDRole
         loop = asyncio.get_running_loop()
         while True:
             pools = await loop.run_in_executor(None, fetch_pools, self.front_router, self.model)
             if pools is None:
                 self.stats["membership_errors"] += 1
             else:
-                for m in pools[PDRole.PREFILL]:
-                    if m.kv_addr:
-                        self.bootstrap[m.url] = m.kv_addr
-                for role in (PDRole.PREFILL, PDRole.DECODE):
-                    for m in pools[role]:
-                        self._members[(role, m.replica)] = m.url
-                self.prefill_pool.set_dynamic([m.url for m in pools[PDRole.PREFILL]])
-                self.pool.set_dynamic([m.url for m in pools[PDRole.DECODE]])
+                self._apply_membership(pools)
             await asyncio.sleep(self.membership_interval)
 
     def on_failure_event(self, ev: dict) -> bool:
-        """A front-router event; True if it cut a member.  Only deregistrations
-        with a failure reason count (a graceful leave lets requests finish)."""
+        """A front-router event; True when it cut a member.  Only
+        deregistrations with a failure reason count (a graceful leave lets
+        in-flight requests finish)."""
         from connex.pd.membership import STAGE_ROLE
         payload = ev.get("payload") or {}
         reason = payload.get("reason")
@@ -201,10 +227,8 @@ class PDRouter(Proxy):
         lid = payload.get("lid") or {}
         role = STAGE_ROLE.get(lid.get("stage_idx"))
         url = self._members.get((role, lid.get("replica_idx")))
-        if url is None:
-            return False
-        pool = self.prefill_pool if role == "prefill" else self.pool
-        ep = pool.eps.get(url)
+        pool = self._pool_of(role)
+        ep = pool.eps.get(url) if url is not None else None
         if ep is None or not ep.healthy(time.monotonic()):
             return False
         self.stats["failure_events"] += 1
@@ -228,74 +252,84 @@ class PDRouter(Proxy):
         finally:
             sub.close(0)
 
+    # ---------------------------------------------------------------- probes
+    def _probe_targets(self) -> List[tuple]:
+        return [(e, p) for p in (self.pool, self.prefill_pool) for e in list(p.eps.values()) if e.url in p.order]
+
     async def _probe_loop(self):
-        while True:
-            eps = [e for p in (self.pool, self.prefill_pool) for e in list(p.eps.values()) if e.url in p.order]
-            await asyncio.gather(*(self._probe_any(e) for e in eps), return_exceptions=True)
+        while True:         # probe right away: new members wait for their first probe
+            await asyncio.gather(*(self._probe(e, p) for e, p in self._probe_targets()), return_exceptions=True)
             await asyncio.sleep(self.probe_interval)
 
-    async def _probe_any(self, ep: Endpoint):
-        pool = self.prefill_pool if ep.url in self.prefill_pool.eps else self.pool
-        if ep.bad_until >= UNPROBED:          # a new member: one success admits it
+    async def _probe(self, ep: Endpoint, pool: Optional[Pool] = None) -> None:
+        pool = pool or self._pool_of(ep)
+        if ep.bad_until >= UNPROBED:          # a new member: one answer admits it
             if await self._alive(ep):
                 log.info("member %s is up", ep.url)
                 pool.mark_good(ep)
             return
-        if await self._alive(ep) or await self._alive(ep):
-            pool.mark_good(ep)
-        else:
-            pool.mark_bad(ep, "probe failed twice")
+        await super()._probe(ep, pool)
 
-    # ------------------------------------------------------------- prefill
-    async def prefill(self, st: PDResumer, body: dict):
-        """Prefill ``body`` somewhere; returns (kv_transfer_params, endpoint)."""
-        path = "/v1/chat/completions" if st.chat else "/v1/completions"
-        drop = ("stream_options", "logprobs", "top_logprobs", "return_tokens_as_token_ids", "min_tokens",
-                "kv_transfer_params")
-        req = {k: v for k, v in body.items() if k not in drop}
+    # --------------------------------------------------------------- prefill
+    def _prefill_body(self, body: dict) -> dict:
+        req = {k: v for k, v in body.items() if k not in _NOT_FOR_PREFILL}
         req["stream"] = False
         req["max_tokens"] = 1
         if "max_completion_tokens" in req:
             req["max_completion_tokens"] = 1
+        return req
+
+    async def _post_json(self, url: str, body: dict):
+        async with self.session.post(url, json=body, timeout=aiohttp.ClientTimeout(total=self.prefill_timeout)) as r:
+            try:
+                return r.status, await r.json(content_type=None)
+            except ValueError:
+                return r.status, None
+
+    async def _prefill_on(self, st: PDResumer, ep: Endpoint, req: dict) -> dict:
+        """One prefill attempt; its ``kv_transfer_params`` or StreamBroken.
+        A member declared dead meanwhile ends the attempt at once."""
+        call = asyncio.ensure_future(self._post_json(ep.url + self._path(st), req))
+        watch = {call}
+        if ep.healthy(time.monotonic()):
+            watch.add(asyncio.ensure_future(ep.dead.wait()))
+        try:
+            done, _ = await asyncio.wait(watch, return_when=asyncio.FIRST_COMPLETED)
+        finally:
+            for t in watch - {call}:
+                t.cancel()
+        if call not in done:
+            call.cancel()
+            raise StreamBroken("prefill instance died")
+        status, data = call.result()
+        if status != 200:
+            raise StreamBroken(f"prefill HTTP {status}: {str(data)[:200]}")
+        kv = (data or {}).get("kv_transfer_params")
+        if not kv:
+            raise StreamBroken("prefill response without kv_transfer_params (not a KV producer?)")
+        if st.prompt_tokens is None:
+            st.prompt_tokens = (data.get("usage") or {}).get("prompt_tokens")
+        return kv
+
+    async def prefill(self, st: PDResumer, body: dict):
+        """Prefill ``body`` somewhere; returns (kv_transfer_params, endpoint)."""
+        req = self._prefill_body(body)
         tried = [st.avoid_prefill.url] if st.avoid_prefill is not None else []
         st.avoid_prefill = None
-        last = "no prefill instances"
-        pool = self.prefill_pool
-        for attempt in range(max(self.max_attempts, len(pool.order) + 1)):
+        pool, last = self.prefill_pool, "no prefill instances"
+        for n in range(max(self.max_attempts, len(pool.order) + 1)):
             ep = pool.pick(exclude=tried) or pool.pick()
             if ep is None:
                 break
-            if attempt:
-                self.stats["prefill_retries"] += 1
+            self.stats["prefill_retries"] += n > 0
             req["kv_transfer_params"] = {"do_remote_decode": True, "do_remote_prefill": False,
                                          "transfer_id": uuid.uuid4().hex}
             ep.inflight += 1
             st.prefills += 1
             try:
-                post = self.session.post(ep.url + path, json=req,
-                                         timeout=aiohttp.ClientTimeout(total=self.prefill_timeout))
-                rtask = asyncio.ensure_future(self._post_json(post))
-                watch = {rtask}
-                if ep.healthy(time.monotonic()):     # cut short if it is declared dead meanwhile
-                    watch.add(asyncio.ensure_future(ep.dead.wait()))
-                try:
-                    done, _ = await asyncio.wait(watch, return_when=asyncio.FIRST_COMPLETED)
-                finally:
-                    for t in watch - {rtask}:
-                        t.cancel()
-                if rtask not in done:
-                    rtask.cancel()
-                    raise StreamBroken("prefill instance died")
-                status, data = rtask.result()
-                if status != 200:
-                    raise StreamBroken(f"prefill HTTP {status}: {str(data)[:200]}")
-                kv = (data or {}).get("kv_transfer_params")
-                if not kv:
-                    raise StreamBroken("prefill response without kv_transfer_params (not a KV producer?)")
+                kv = await self._prefill_on(st, ep, req)
                 self.stats["prefills"] += 1
                 pool.mark_good(ep)      # it just answered: a blacklisted last resort is back
-                if st.prompt_tokens is None:
-                    st.prompt_tokens = (data.get("usage") or {}).get("prompt_tokens")
                 return kv, ep
             except (StreamBroken, ValueError, *RETRYABLE) as e:
                 last = f"{type(e).__name__}: {e}"
@@ -306,95 +340,84 @@ class PDRouter(Proxy):
                 ep.inflight -= 1
         raise PrefillFailed(f"prefill failed: {last}", st)
 
-    async def _post_json(self, post):
-        async with post as r:
-            try:
-                return r.status, await r.json(content_type=None)
-            except ValueError:
-                return r.status, None
-
-    # -------------------------------------------------------------- SGLang
+    # ---------------------------------------------------------------- SGLang
     def _bootstrap_of(self, url: str):
         addr = self.bootstrap.get(url)
         if addr:
-            h, p = addr.rsplit(":", 1)
-            return h, int(p)
+            host, port = addr.rsplit(":", 1)
+            return host, int(port)
         from urllib.parse import urlparse
         return urlparse(url).hostname, self.bootstrap_port
 
+    async def _sglang_prefill(self, pep: Endpoint, path: str, body: dict) -> Optional[str]:
+        """The paired prefill request; None when it succeeded, else why not."""
+        pep.inflight += 1
+        try:
+            async with self.session.post(pep.url + path, json=body,
+                                         timeout=aiohttp.ClientTimeout(total=self.prefill_timeout)) as r:
+                await r.read()
+                return None if r.status == 200 else f"prefill HTTP {r.status}"
+        except RETRYABLE as e:
+            self.prefill_pool.mark_bad(pep, f"{type(e).__name__}: {e}")
+            return f"prefill {type(e).__name__}"
+        finally:
+            pep.inflight -= 1
+
     async def sglang_dispatch(self, st: PDResumer, b: dict) -> None:
-        pool = self.prefill_pool
+        """Pick a prefill, pair it with this decode attempt by a bootstrap
+        room, start the prefill and guard the decode's first token with it."""
         avoid = [st.avoid_prefill.url] if st.avoid_prefill is not None else []
         st.avoid_prefill = None
-        pep = pool.pick(exclude=avoid) or pool.pick()
+        pep = self.prefill_pool.pick(exclude=avoid) or self.prefill_pool.pick()
         if pep is None:
             raise PrefillFailed("no prefill instances", st)
         host, port = self._bootstrap_of(pep.url)
         b.update(bootstrap_host=host, bootstrap_port=port, bootstrap_room=uuid.uuid4().int & ((1 << 63) - 1))
-        path = "/v1/chat/completions" if st.chat else "/v1/completions"
-        pb = {k: v for k, v in b.items() if k != "stream_options"}
-        pb["stream"] = False
+        prefill_body = {k: v for k, v in b.items() if k != "stream_options"}
+        prefill_body["stream"] = False
         st.kv_ep = pep
         st.prefills += 1
         self.stats["prefills"] += 1
+        st.prefill_task = asyncio.ensure_future(self._sglang_prefill(pep, self._path(st), prefill_body))
+        task = st.prefill_task
 
-        async def run():
-            pep.inflight += 1
-            try:
-                async with self.session.post(pep.url + path, json=pb,
-                                             timeout=aiohttp.ClientTimeout(total=self.prefill_timeout)) as r:
-                    await r.read()
-                    return None if r.status == 200 else f"prefill HTTP {r.status}"
-            except RETRYABLE as e:
-                pool.mark_bad(pep, f"{type(e).__name__}: {e}")
-                return f"prefill {type(e).__name__}"
-            finally:
-                pep.inflight -= 1
+        async def guard():
+            why = await asyncio.shield(task)
+            if why is None:
+                await asyncio.Event().wait()     # the prefill succeeded: never abort the decode
+            return why
+        st._guard = guard
 
-        st.prefill_task = asyncio.ensure_future(run())
-
-        async def abort():
-            err = await asyncio.shield(st.prefill_task)
-            if err is None:
-                await asyncio.Event().wait()       # prefill fine: never abort the decode
-            return err
-        st.abort_first = abort
-
-    # -------------------------------------------------------------- decode
-    async def _attempt(self, st: PDResumer, ep, path):
-        k0 = st.k
-        try:
-            async for c in super()._attempt(st, ep, path):
-                yield c
-        except (StreamBroken, ValueError, KeyError, *RETRYABLE):
+    # ---------------------------------------------------------------- decode
+    async def on_attempt_failed(self, st: PDResumer, ep: Endpoint, err: BaseException, produced: int) -> bool:
+        if self.engine == "sglang":
             pt = st.prefill_task
-            if self.engine == "sglang":
-                if pt is not None and pt.done() and not pt.cancelled() and pt.result():
-                    st.avoid_prefill = st.kv_ep       # the paired prefill failed, not the decode
-                    st.spare_endpoint = st.k == k0
-                    self.stats["prefill_retries"] += 1
-                elif st.k > k0:
-                    self.stats["kv_reprefills"] += 1
-                raise
-            if st.k == k0 and st.kv is not None and await self._alive(ep):
-                # decode alive, nothing generated: the KV hand-off failed; prefill again
-                st.avoid_prefill = st.kv_ep
-                st.kv = None
-                st.spare_endpoint = True
+            if pt is not None and pt.done() and not pt.cancelled() and pt.result():
+                st.avoid_prefill = st.kv_ep           # the paired prefill failed, not the decode
+                self.stats["prefill_retries"] += 1
+                if produced == 0:
+                    return False
+            elif produced > 0:
                 self.stats["kv_reprefills"] += 1
-                log.warning("decode %s failed before its first token; re-prefilling", ep.url)
-            raise
+        elif produced == 0 and st.kv is not None and await self._alive(ep):
+            # the decode answers and produced nothing: its KV hand-off failed; prefill again
+            st.avoid_prefill = st.kv_ep
+            st.kv = None
+            self.stats["kv_reprefills"] += 1
+            log.warning("decode %s failed before its first token; re-prefilling", ep.url)
+            return False
+        return await super().on_attempt_failed(st, ep, err, produced)
 
-    # --------------------------------------------------------------- admin
+    # ----------------------------------------------------------------- admin
     async def handle_pools(self, request):
         now = time.monotonic()
 
-        def desc(p: ElasticPool):
-            live = [{"url": u, "healthy": p.eps[u].healthy(now), "probed": p.eps[u].bad_until < UNPROBED,
-                     "inflight": p.eps[u].inflight} for u in p.order]
-            return live + [{"url": u, "drained": True, "inflight": p.eps[u].inflight} for u in p.drained
-                           if u in p.eps]
-        return web.json_response({"prefill": desc(self.prefill_pool), "decode": desc(self.pool)})
+        def describe(p: ElasticPool):
+            listed = [{"url": u, "healthy": p.eps[u].healthy(now), "probed": p.eps[u].bad_until < UNPROBED,
+                       "inflight": p.eps[u].inflight} for u in p.order]
+            return listed + [{"url": u, "drained": True, "inflight": p.eps[u].inflight}
+                             for u in p.drained if u in p.eps]
+        return web.json_response({"prefill": describe(self.prefill_pool), "decode": describe(self.pool)})
 
     def _admin_allowed(self, request) -> bool:
         """Pool changes: loopback clients, or ``Authorization: Bearer <token>``
@@ -406,25 +429,21 @@ class PDRouter(Proxy):
         remote = (request.remote or "").split("%", 1)[0]
         return remote in ("127.0.0.1", "::1", "localhost") or remote.startswith("::ffff:127.")
 
-    async def _drain_target(self, request):
+    async def _admin(self, request, action: str):
         if not self._admin_allowed(request):
             raise web.HTTPForbidden(text="pool admin needs loopback or an admin token")
         body = await request.json()
-        return body.get("url", ""), body.get("role")
+        url, role = body.get("url", ""), body.get("role")
+        for name, p in (("prefill", self.prefill_pool), ("decode", self.pool)):
+            if role in (None, name):
+                getattr(p, action)(url)
+        return web.json_response({"ok": True})
 
     async def handle_drain(self, request):
-        url, role = await self._drain_target(request)
-        for name, p in (("prefill", self.prefill_pool), ("decode", self.pool)):
-            if role in (None, name):
-                p.drain(url)
-        return web.json_response({"ok": True})
+        return await self._admin(request, "drain")
 
     async def handle_undrain(self, request):
-        url, role = await self._drain_target(request)
-        for name, p in (("prefill", self.prefill_pool), ("decode", self.pool)):
-            if role in (None, name):
-                p.undrain(url)
-        return web.json_response({"ok": True})
+        return await self._admin(request, "undrain")
 
 
 def main() -> None:

@@ -1,25 +1,36 @@
-"""Resume proxy: an OpenAI-API front that hides replica deaths from clients
-(reference ``connex/serving/proxy.py:84-764``).
+"""Resume proxy: an OpenAI-API front that hides replica deaths from clients.
 
-* **Replicas** come from ``--endpoints`` and/or an endpoints file (re-read
-  every ``--reload-interval`` s; an URL removed from the file counts as
-  dead).  A prober GETs ``/v1/models`` on fresh connections; two failed
-  probes, a connect error or a broken stream blacklist a replica for
-  ``--blacklist-s``.  The least-loaded healthy replica is picked.
-* **Before the first token** a failed attempt (refused, reset, 5xx, the
-  replica declared dead while we wait) is retried elsewhere.  No idle timer
-  runs before the first token, so a long prefill is never cut; the wait ends
-  only when the replica is declared dead (or an optional first-token cap).
-* **After k tokens** (reset, EOF without ``[DONE]``, no chunk for
-  ``--idle-timeout`` s) the request resumes on another replica: completions
-  from token ids (``prompt_ids + generated_ids``; the proxy asks for
-  ``return_token_ids`` / id logprobs and strips them again), chat through
-  ``continue_final_message``; ``max_tokens``/``min_tokens`` shrink by k.  The
-  client sees one stream with one ``id`` and a usage block counting the
-  original prompt and all completion tokens.
+Replicas
+    come from ``--endpoints`` and/or an endpoints file (re-read every
+    ``--reload-interval`` s; a URL removed from the file counts as dead).  A
+    prober GETs ``/v1/models`` on fresh connections; two failed probes in a
+    row, a refused connect or a broken stream blacklist a replica for
+    ``--blacklist-s``.  Requests go to the least loaded healthy replica.
 
-Every backend call streams; non-streaming clients get the aggregate.
-:meth:`Proxy.move` cuts a request over on purpose (planned migration).
+One client request is a :class:`Resumer`: the body of the next backend
+attempt, and a ledger of what the client has been sent (text, token ids,
+completion-token count, id / created / model of the first attempt).  Every
+attempt streams, whatever the client asked for; :class:`_Lines` reads the
+backend's lines under two regimes:
+
+* **before the first token** there is no idle limit -- a long prefill is
+  never cut; the wait ends only when the replica is declared dead, an
+  optional first-token cap passes, or the request's own guard fires (the
+  PD router's SGLang prefill);
+* **after a token**, ``--idle-timeout`` without a line, or the replica's
+  death, ends the attempt.
+
+A failed attempt before the first token is retried elsewhere; after k
+tokens the request *resumes* elsewhere: completions from token ids (prompt
+ids + generated ids: the proxy asks for ``return_token_ids`` / id logprobs
+and strips what the client did not ask for), chat through
+``continue_final_message``; ``max_tokens`` / ``min_tokens`` shrink by k.  The
+client sees one stream with one ``id`` and a usage block counting the
+original prompt and every completion token.  :meth:`Proxy.move` cuts a
+request over on purpose (planned migration; no blame, no attempt used).
+
+Behavioural parity: ``connex/serving/proxy.py:84-764`` of the reference
+(routes, flags, resume semantics); the structure here is this module's own.
 
     python -m connex.serving.proxy --port 5199 --endpoints http://a:5100,http://b:5101
 """
@@ -30,7 +41,7 @@ import asyncio
 import json
 import logging
 import time
-from typing import Dict, List, Optional
+from typing import AsyncIterator, Callable, Dict, List, Optional
 
 import aiohttp
 from aiohttp import web
@@ -38,10 +49,7 @@ from aiohttp import web
 log = logging.getLogger("connex.proxy")
 
 RETRYABLE = (aiohttp.ClientError, asyncio.TimeoutError, ConnectionError, OSError)
-
-
-def _loads(b):
-    return json.loads(b)
+_ID_PREFIX = "token_id:"
 
 
 def _sse(obj) -> bytes:
@@ -49,7 +57,7 @@ def _sse(obj) -> bytes:
 
 
 class StreamBroken(Exception):
-    pass
+    """The backend stream ended or failed before ``[DONE]``."""
 
 
 class HTTPPassthrough(Exception):
@@ -66,18 +74,25 @@ class UpstreamFailed(Exception):
         self.st = st
 
 
-# ------------------------------------------------------------------ pool
+# ================================================================ replicas
 class Endpoint:
+    """One replica: health (blacklisted until ``bad_until``), load, and an
+    event that is set while it is blacklisted (waiters on it wake up)."""
+
     __slots__ = ("url", "bad_until", "inflight", "dead")
 
     def __init__(self, url: str):
         self.url = url.rstrip("/")
         self.bad_until = 0.0
         self.inflight = 0
-        self.dead = asyncio.Event()     # set while blacklisted: wakes its waiters
+        self.dead = asyncio.Event()
 
     def healthy(self, now: float) -> bool:
         return now >= self.bad_until
+
+
+def _clean(urls) -> List[str]:
+    return [u.strip().rstrip("/") for u in urls if u.strip()]
 
 
 class Pool:
@@ -86,37 +101,38 @@ class Pool:
         self.order: List[str] = []
         self.file = endpoints_file
         self.blacklist_s = blacklist_s
-        self._rr = 0
+        self._turn = 0
         self.set_urls(urls)
 
     def set_urls(self, urls) -> None:
-        urls = [u.strip().rstrip("/") for u in urls if u.strip()]
+        urls = _clean(urls)
         for u in urls:
-            self.eps.setdefault(u, Endpoint(u))
+            if u not in self.eps:
+                self.eps[u] = Endpoint(u)
         self.order = urls
 
     def _file_urls(self) -> Optional[List[str]]:
         try:
             with open(self.file) as f:
-                return [x.strip().rstrip("/") for x in f if x.strip()]
+                return _clean(f)
         except OSError:
             return None
 
     def reload(self) -> None:
-        if not self.file:
+        """Re-read the endpoints file; a URL that left it is dead now."""
+        listed = self._file_urls() if self.file else None
+        if not listed:
             return
-        urls = self._file_urls()
-        if not urls:
-            return
-        gone = [u for u in self.order if u not in urls]
-        self.set_urls(urls)
-        for u in gone:      # removed (e.g. by a supervisor that saw it die): dead now
+        removed = [u for u in self.order if u not in listed]
+        self.set_urls(listed)
+        for u in removed:
             self.mark_bad(self.eps[u], "removed from endpoints file")
 
     def mark_bad(self, ep: Endpoint, why: str = "") -> None:
-        if ep.healthy(time.monotonic()):
+        now = time.monotonic()
+        if ep.healthy(now):
             log.warning("blacklisting %s for %.1fs: %s", ep.url, self.blacklist_s, why)
-        ep.bad_until = time.monotonic() + self.blacklist_s
+        ep.bad_until = now + self.blacklist_s
         ep.dead.set()
 
     def mark_good(self, ep: Endpoint) -> None:
@@ -125,38 +141,43 @@ class Pool:
             ep.dead = asyncio.Event()
 
     def pick(self, exclude=()) -> Optional[Endpoint]:
-        now = time.monotonic()
-        cands = [self.eps[u] for u in self.order if u not in exclude]
-        if not cands:
+        """The least loaded healthy replica outside ``exclude`` (ties broken by
+        rotation); with none healthy, the one whose blacklist ends first."""
+        options = [self.eps[u] for u in self.order if u not in exclude]
+        if not options:
             return None
-        ok = [e for e in cands if e.healthy(now)]
-        if not ok:          # last resort: the one whose blacklist ends first
-            return min(cands, key=lambda e: e.bad_until)
-        for e in ok:
-            if e.bad_until:     # blacklist lapsed without a probe: re-arm
+        now = time.monotonic()
+        healthy = [e for e in options if e.healthy(now)]
+        if not healthy:
+            return min(options, key=lambda e: e.bad_until)
+        for e in healthy:
+            if e.bad_until:              # its blacklist lapsed without a probe: re-arm it
                 self.mark_good(e)
-        self._rr += 1
-        rot = ok[self._rr % len(ok):] + ok[:self._rr % len(ok)]
-        return min(rot, key=lambda e: e.inflight)
+        self._turn += 1
+        start = self._turn % len(healthy)
+        rotated = healthy[start:] + healthy[:start]
+        return min(rotated, key=lambda e: e.inflight)
 
 
-def _ids_from_logprobs(lp, chat: bool):
+# ================================================================ requests
+def _ids_in_logprobs(lp, chat: bool) -> Optional[List[int]]:
+    """Token ids carried as ``token_id:<n>`` strings in a logprobs block."""
     if not lp:
         return None
-    toks = [c.get("token") for c in lp.get("content") or []] if chat else lp.get("tokens")
-    if not toks:
+    names = [c.get("token") for c in lp.get("content") or []] if chat else lp.get("tokens")
+    if not names or not all(isinstance(n, str) and n.startswith(_ID_PREFIX) for n in names):
         return None
-    out = []
-    for t in toks:
-        if not isinstance(t, str) or not t.startswith("token_id:"):
-            return None
-        out.append(int(t[len("token_id:"):]))
-    return out
+    return [int(n[len(_ID_PREFIX):]) for n in names]
 
 
-# --------------------------------------------------------------- resumer
 class Resumer:
-    """One client request across its backend attempts."""
+    """One client request across its backend attempts.
+
+    What the client has received so far: ``text`` (pieces), ``ids`` (when
+    the backend reports token ids), ``k`` (completion tokens), the id /
+    created / model of the first attempt, ``finish`` / ``stop_reason``.
+    ``build(ep)`` turns that into the body of the next attempt;
+    ``on_chunk`` accounts one backend chunk and rewrites it for the client."""
 
     def __init__(self, proxy: "Proxy", kind: str, body: dict):
         self.p = proxy
@@ -167,30 +188,33 @@ class Resumer:
         self.client_usage = bool(so.get("include_usage"))
         self.client_cont_usage = bool(so.get("continuous_usage_stats"))
         prompt = body.get("prompt")
-        single = body.get("n") in (None, 1) and body.get("best_of") in (None, 1)
-        text_or_ids = isinstance(prompt, str) or (isinstance(prompt, list) and bool(prompt)
-                                                  and isinstance(prompt[0], int))
-        self.resumable = single and (self.chat or text_or_ids)
+        one_choice = body.get("n") in (None, 1) and body.get("best_of") in (None, 1)
+        single_prompt = isinstance(prompt, str) or (isinstance(prompt, list) and bool(prompt)
+                                                    and isinstance(prompt[0], int))
+        self.resumable = one_choice and (self.chat or single_prompt)
         lp = body.get("logprobs")
-        self.client_lp = lp is not None and lp is not False      # logprobs=0 asks for them too
+        self.client_lp = lp is not None and lp is not False     # logprobs=0 asks for them too
         self.use_ids = (self.resumable and not self.chat and proxy.token_ids
                         and (not self.client_lp or bool(body.get("return_tokens_as_token_ids"))))
         self.inject_lp = self.use_ids and not self.client_lp
+        self.prompt_ids: Optional[List[int]] = prompt if isinstance(prompt, list) else None
+        self.model = body.get("model")
+        # the ledger
         self.ids: List[int] = []
         self.text: List[str] = []
         self.k = 0
         self.prompt_tokens = None
-        self.prompt_ids = prompt if isinstance(prompt, list) else None
         self.rid = self.created = None
-        self.model = body.get("model")
         self.finish = self.stop_reason = None
-        self.attempts = 0
         self.sent_role = False
+        # the current attempt
+        self.attempts = 0
         self.resp = None
-        self.ep = None
+        self.ep: Optional[Endpoint] = None
         self.moved = False
 
-    async def build(self, ep: Endpoint) -> dict:
+    # ------------------------------------------------------------ next body
+    def _common(self) -> dict:
         b = dict(self.body)
         b["stream"] = True
         b["stream_options"] = {"include_usage": True, "continuous_usage_stats": True}
@@ -199,22 +223,26 @@ class Resumer:
             b["return_tokens_as_token_ids"] = True
         if self.use_ids:
             b["return_token_ids"] = True
-        if self.k == 0:
-            return b
+        return b
+
+    def _shrink(self, b: dict) -> None:
         for key in ("max_tokens", "max_completion_tokens"):
             if b.get(key) is not None:
                 b[key] -= self.k
         if b.get("min_tokens"):
             b["min_tokens"] = max(0, b["min_tokens"] - self.k)
-        done_text = "".join(self.text)
-        if self.chat:
-            msgs = [dict(m) for m in b["messages"]]
-            if b.get("continue_final_message") and msgs and msgs[-1].get("role") == "assistant":
-                msgs[-1]["content"] = (msgs[-1].get("content") or "") + done_text
-            else:
-                msgs.append({"role": "assistant", "content": done_text})
-            b.update(messages=msgs, add_generation_prompt=False, continue_final_message=True)
-            return b
+
+    def _chat_continuation(self, b: dict) -> dict:
+        done = "".join(self.text)
+        msgs = [dict(m) for m in b["messages"]]
+        if b.get("continue_final_message") and msgs and msgs[-1].get("role") == "assistant":
+            msgs[-1]["content"] = (msgs[-1].get("content") or "") + done
+        else:
+            msgs.append({"role": "assistant", "content": done})
+        b.update(messages=msgs, add_generation_prompt=False, continue_final_message=True)
+        return b
+
+    async def _completion_continuation(self, b: dict, ep: Endpoint) -> dict:
         b["echo"] = False
         if self.use_ids and len(self.ids) == self.k:
             if self.prompt_ids is None:
@@ -223,9 +251,24 @@ class Resumer:
                 b["prompt"] = list(self.prompt_ids) + self.ids
                 return b
         if isinstance(b["prompt"], str):
-            b["prompt"] += done_text
+            b["prompt"] += "".join(self.text)
             return b
         raise StreamBroken("cannot resume a token-id prompt without the generated ids")
+
+    async def build(self, ep: Endpoint) -> dict:
+        """The backend body of the next attempt (on ``ep``)."""
+        b = self._common()
+        if self.k == 0:
+            return b
+        self._shrink(b)
+        if self.chat:
+            return self._chat_continuation(b)
+        return await self._completion_continuation(b, ep)
+
+    def first_token_guard(self) -> Optional[Callable]:
+        """An awaitable factory whose completion before the first token ends
+        the attempt (its result is the reason); None for no guard."""
+        return None
 
     def can_resume(self) -> bool:
         return self.k == 0 or self.resumable
@@ -236,13 +279,46 @@ class Resumer:
             m = self.body.get("max_completion_tokens")
         return None if m is None else m - self.k
 
-    def on_chunk(self, c: dict, base_k: int):
-        """Account one backend chunk; returns the chunk for the client or None."""
+    def complete_already(self) -> bool:
+        """The stream broke after its last token (before ``[DONE]``)."""
+        rem = self.remaining()
+        return self.k > 0 and (self.finish is not None or (rem is not None and rem <= 0))
+
+    # -------------------------------------------------------------- ledger
+    def _count(self, ch: dict, usage: Optional[dict], base_k: int, piece: str) -> None:
+        ids = ch.get("token_ids")
+        if not ids and self.use_ids:
+            ids = _ids_in_logprobs(ch.get("logprobs"), self.chat)
+        if usage and usage.get("completion_tokens") is not None:
+            self.k = base_k + usage["completion_tokens"]
+        elif ids:
+            self.k += len(ids)
+        elif piece:
+            self.k += 1
+        if self.use_ids:
+            self.ids.extend(ids or [])
+            if len(self.ids) != self.k:
+                self.use_ids = False            # lost count: resume from text instead
+
+    def _for_client(self, c: dict, ch: dict) -> dict:
+        c["id"], c["created"], c["model"] = self.rid, self.created, self.model
+        if self.inject_lp:
+            ch["logprobs"] = None
+        if "token_ids" in ch and not self.body.get("return_token_ids"):
+            del ch["token_ids"]
+        if self.client_cont_usage:
+            c["usage"] = self.usage()
+        elif "usage" in c:
+            c["usage"] = None
+        return c
+
+    def on_chunk(self, c: dict, base_k: int) -> Optional[dict]:
+        """Account one backend chunk; returns the chunk for the client, or None."""
         usage = c.get("usage")
         choices = c.get("choices") or []
         if usage and base_k == 0 and self.prompt_tokens is None:
             self.prompt_tokens = usage.get("prompt_tokens")
-        if not choices:             # trailing usage-only chunk: ours replaces it
+        if not choices:                         # a usage-only chunk: ours replaces it at the end
             if usage and usage.get("completion_tokens") is not None:
                 self.k = max(self.k, base_k + usage["completion_tokens"])
             return None
@@ -257,35 +333,15 @@ class Resumer:
             piece = delta.get("content") or ""
             if not piece and ch.get("finish_reason") is None and "role" in delta:
                 if self.sent_role:
-                    return None     # role preamble of a retried / resumed stream
+                    return None                 # the role preamble of a retried / resumed stream
                 self.sent_role = True
         else:
             piece = ch.get("text") or ""
-        ids = ch.get("token_ids") or (_ids_from_logprobs(ch.get("logprobs"), self.chat) if self.use_ids else None)
-        if usage and usage.get("completion_tokens") is not None:
-            self.k = base_k + usage["completion_tokens"]
-        elif ids:
-            self.k += len(ids)
-        elif piece:
-            self.k += 1
-        if self.use_ids:
-            if ids:
-                self.ids.extend(ids)
-            if len(self.ids) != self.k:
-                self.use_ids = False    # lost count: resume from text instead
+        self._count(ch, usage, base_k, piece)
         self.text.append(piece)
         if ch.get("finish_reason") is not None:
             self.finish, self.stop_reason = ch["finish_reason"], ch.get("stop_reason")
-        c["id"], c["created"], c["model"] = self.rid, self.created, self.model
-        if self.inject_lp:
-            ch["logprobs"] = None
-        if "token_ids" in ch and not self.body.get("return_token_ids"):
-            del ch["token_ids"]
-        if self.client_cont_usage:
-            c["usage"] = self.usage()
-        elif "usage" in c:
-            c["usage"] = None
-        return c
+        return self._for_client(c, ch)
 
     def usage(self) -> dict:
         pt = self.prompt_tokens
@@ -294,7 +350,44 @@ class Resumer:
         return {"prompt_tokens": pt, "completion_tokens": self.k, "total_tokens": (pt or 0) + self.k}
 
 
-# ----------------------------------------------------------------- proxy
+class _Lines:
+    """The lines of one backend response under the proxy's timing rules."""
+
+    def __init__(self, resp, ep: Endpoint, idle_timeout: Optional[float], first_token_timeout: Optional[float],
+                 guard: Optional[Callable]):
+        self.resp, self.ep = resp, ep
+        self.idle, self.first_cap = idle_timeout, first_token_timeout
+        self.guard_task = asyncio.ensure_future(guard()) if guard is not None else None
+
+    async def next(self, started: bool) -> bytes:
+        read = asyncio.ensure_future(self.resp.content.readline())
+        death = asyncio.ensure_future(self.ep.dead.wait())
+        waits = {read, death}
+        if not started and self.guard_task is not None:
+            waits.add(self.guard_task)
+        limit = self.idle if started else self.first_cap
+        try:
+            done, _ = await asyncio.wait(waits, timeout=limit or None, return_when=asyncio.FIRST_COMPLETED)
+        finally:
+            death.cancel()
+        if read in done:
+            return read.result()
+        read.cancel()
+        self.resp.close()
+        if self.guard_task is not None and self.guard_task in done:
+            raise StreamBroken(f"aborted before first token: {self.guard_task.result()}")
+        if death in done:
+            raise StreamBroken("replica died" + ("" if started else " before first token"))
+        if started:
+            raise asyncio.TimeoutError()        # idle: the caller checks whether the replica lives
+        raise StreamBroken("first-token timeout")
+
+    def close(self) -> None:
+        if self.guard_task is not None and not self.guard_task.done():
+            self.guard_task.cancel()
+
+
+# ================================================================== proxy
 class Proxy:
     resumer_cls = Resumer
 
@@ -310,9 +403,10 @@ class Proxy:
         self.reload_interval = 1.0
         self.session: Optional[aiohttp.ClientSession] = None
         self.probe_session: Optional[aiohttp.ClientSession] = None
-        self.stats = {"requests": 0, "retries": 0, "resumes": 0, "failed": 0}
+        self.stats = {"requests": 0, "retries": 0, "resumes": 0, "failed": 0, "moves": 0}
         self._bg: List[asyncio.Task] = []
 
+    # -------------------------------------------------------------- lifecycle
     def app(self) -> web.Application:
         app = web.Application(client_max_size=64 << 20)
         app.router.add_post("/v1/completions", self.handle_completions)
@@ -333,9 +427,12 @@ class Proxy:
                                                    trust_env=False)
         if self.pool.file:
             self.pool.reload()
-            self._bg.append(asyncio.create_task(self._every(self.reload_interval, self.pool.reload)))
+            self._background(self._every(self.reload_interval, self.pool.reload))
         if self.probe_interval:
-            self._bg.append(asyncio.create_task(self._probe_loop()))
+            self._background(self._probe_loop())
+
+    def _background(self, coro) -> None:
+        self._bg.append(asyncio.create_task(coro))
 
     async def _cleanup(self, app=None):
         for t in self._bg:
@@ -343,16 +440,20 @@ class Proxy:
         await self.session.close()
         await self.probe_session.close()
 
-    async def _every(self, s: float, fn) -> None:
+    async def _every(self, period: float, fn) -> None:
         while True:
-            await asyncio.sleep(s)
+            await asyncio.sleep(period)
             fn()
+
+    # ---------------------------------------------------------------- probes
+    def _probe_targets(self) -> List[tuple]:
+        """(endpoint, its pool) of every listed replica."""
+        return [(e, self.pool) for e in list(self.pool.eps.values()) if e.url in self.pool.order]
 
     async def _probe_loop(self):
         while True:
             await asyncio.sleep(self.probe_interval)
-            eps = [e for e in list(self.pool.eps.values()) if e.url in self.pool.order]
-            await asyncio.gather(*(self._probe(e) for e in eps), return_exceptions=True)
+            await asyncio.gather(*(self._probe(e, p) for e, p in self._probe_targets()), return_exceptions=True)
 
     async def _alive(self, ep: Endpoint, timeout: float = 2.0) -> bool:
         try:
@@ -362,12 +463,13 @@ class Proxy:
         except RETRYABLE:
             return False
 
-    async def _probe(self, ep: Endpoint) -> None:
+    async def _probe(self, ep: Endpoint, pool: Optional[Pool] = None) -> None:
         # two failures in a row: a busy but alive server keeps its prefills
+        pool = pool or self.pool
         if await self._alive(ep) or await self._alive(ep):
-            self.pool.mark_good(ep)
+            pool.mark_good(ep)
         else:
-            self.pool.mark_bad(ep, "probe failed twice")
+            pool.mark_bad(ep, "probe failed twice")
 
     async def tokenize(self, ep: Endpoint, model, prompt):
         try:
@@ -379,114 +481,68 @@ class Proxy:
             pass
         return None
 
-    # ---------------------------------------------------------------- core
-    async def _attempt(self, st: Resumer, ep: Endpoint, path: str):
-        """Stream one backend attempt, yielding client chunks; raises if the
-        stream ends without ``[DONE]``."""
-        req = await st.build(ep)
+    # ------------------------------------------------------------- attempts
+    @staticmethod
+    def _path(st: Resumer) -> str:
+        return "/v1/chat/completions" if st.chat else "/v1/completions"
+
+    async def _attempt(self, st: Resumer, ep: Endpoint) -> AsyncIterator[dict]:
+        """Stream one backend attempt, yielding client chunks; returns at
+        ``[DONE]``, raises otherwise."""
+        body = await st.build(ep)
         base_k = st.k
         ep.inflight += 1
+        lines = None
         try:
-            async with self.session.post(ep.url + path, json=req) as r:
+            async with self.session.post(ep.url + self._path(st), json=body) as r:
                 st.resp, st.ep = r, ep
                 if r.status != 200:
                     payload = await r.read()
                     if r.status >= 500 or r.status in (404, 408, 429) or base_k > 0:
                         raise StreamBroken(f"HTTP {r.status}")
                     raise HTTPPassthrough(r.status, payload, r.content_type)
-                loop = asyncio.get_running_loop()
-                last = [loop.time()]
-                fired = [False]
-                dog = None
-                started = base_k > 0
-                try:
-                    while True:
-                        if started:
-                            if dog is None and self.idle_timeout:
-                                dog = asyncio.ensure_future(self._watchdog(r, last, fired, ep.dead))
-                            try:
-                                line = await r.content.readline()
-                            except RETRYABLE:
-                                if fired[0]:
-                                    raise asyncio.TimeoutError()
-                                raise
-                            if fired[0]:
-                                raise asyncio.TimeoutError()
-                            last[0] = loop.time()
-                        else:
-                            line = await self._wait_first(r.content, ep, getattr(st, "abort_first", None))
-                        if not line:
-                            raise StreamBroken("EOF before [DONE]")
-                        if not line.startswith(b"data:"):
-                            continue
-                        data = line[5:].strip()
-                        if data == b"[DONE]":
-                            return
-                        obj = _loads(data)
-                        if isinstance(obj, dict) and obj.get("error") and not obj.get("choices"):
-                            raise StreamBroken(f"backend error: {str(obj['error'])[:200]}")
-                        out = st.on_chunk(obj, base_k)
-                        started = started or st.k > base_k
-                        if out is not None:
-                            yield out
-                finally:
-                    if dog is not None:
-                        dog.cancel()
+                lines = _Lines(r, ep, self.idle_timeout, self.first_token_timeout, st.first_token_guard())
+                while True:
+                    line = await lines.next(started=st.k > base_k or base_k > 0)
+                    if not line:
+                        raise StreamBroken("EOF before [DONE]")
+                    if not line.startswith(b"data:"):
+                        continue
+                    data = line[5:].strip()
+                    if data == b"[DONE]":
+                        return
+                    obj = json.loads(data)
+                    if isinstance(obj, dict) and obj.get("error") and not obj.get("choices"):
+                        raise StreamBroken(f"backend error: {str(obj['error'])[:200]}")
+                    out = st.on_chunk(obj, base_k)
+                    if out is not None:
+                        yield out
         finally:
+            if lines is not None:
+                lines.close()
             st.resp = None
             ep.inflight -= 1
 
-    async def _watchdog(self, r, last, fired, dead: Optional[asyncio.Event] = None):
-        """Close ``r`` after ``idle_timeout`` without a line, or as soon as
-        the replica is declared dead, so the pending read fails over."""
-        loop = asyncio.get_running_loop()
-        dw = asyncio.ensure_future(dead.wait()) if dead is not None else None
-        try:
-            while True:
-                left = last[0] + self.idle_timeout - loop.time()
-                if left <= 0 or (dw is not None and dw.done()):
-                    fired[0] = True
-                    r.close()
-                    return
-                if dw is not None:
-                    await asyncio.wait({dw}, timeout=max(left, 0.01))
-                else:
-                    await asyncio.sleep(max(left, 0.01))
-        finally:
-            if dw is not None and not dw.done():
-                dw.cancel()
+    async def on_attempt_failed(self, st: Resumer, ep: Endpoint, err: BaseException, produced: int) -> bool:
+        """Whether to blacklist ``ep`` after a failed attempt that produced
+        ``produced`` tokens.  An idle stream on a replica that still answers
+        is not its death."""
+        if isinstance(err, asyncio.TimeoutError) and await self._alive(ep):
+            log.info("%s idle but alive: resuming elsewhere without blacklisting", ep.url)
+            return False
+        return True
 
-    async def _wait_first(self, content, ep: Endpoint, abort=None):
-        """Next line before the first token: no idle limit; ends early only if
-        the replica is declared dead or ``abort()`` (a coroutine factory)
-        finishes first."""
-        read = asyncio.ensure_future(content.readline())
-        dead = asyncio.ensure_future(ep.dead.wait())
-        waits = {read, dead}
-        ab = asyncio.ensure_future(abort()) if abort is not None else None
-        if ab is not None:
-            waits.add(ab)
-        try:
-            done, _ = await asyncio.wait(waits, timeout=self.first_token_timeout, return_when=asyncio.FIRST_COMPLETED)
-            if read in done:
-                return read.result()
-            if ab is not None and ab in done:
-                raise StreamBroken(f"aborted before first token: {ab.result()}")
-            raise StreamBroken("replica died before first token" if done else "first-token timeout")
-        finally:
-            for t in (dead, ab):
-                if t is not None:
-                    t.cancel()
-            if not read.done():
-                read.cancel()
+    # ------------------------------------------------------------- requests
+    def make_request(self, kind: str, body: dict) -> Resumer:
+        return self.resumer_cls(self, kind, body)
 
     async def generate(self, kind: str, body: dict):
         """Client chunks of one request (retry / resume inside); the final
         item is the :class:`Resumer` itself."""
-        st = self.resumer_cls(self, kind, body)
+        st = self.make_request(kind, body)
         self.begin(st)
         try:
-            async for c in self._generate(st):
+            async for c in self._drive(st):
                 yield c
         finally:
             self.end(st)
@@ -497,15 +553,16 @@ class Proxy:
     def end(self, st: Resumer) -> None:
         """Hook: ``st`` finished, failed or was cancelled."""
 
-    async def _generate(self, st: Resumer):
-        path = "/v1/chat/completions" if st.chat else "/v1/completions"
+    def pick(self, st: Resumer, tried) -> Optional[Endpoint]:
+        """Replica for the next attempt (session-aware routers override)."""
+        return self.pool.pick(exclude=tried) or self.pool.pick()
+
+    async def _drive(self, st: Resumer):
         self.stats["requests"] += 1
         tried: List[str] = []
-        last_err = "no endpoints"
+        reason = "no endpoints"
         while st.attempts < self.max_attempts:
-            rem = st.remaining()
-            if st.k > 0 and (st.finish is not None or (rem is not None and rem <= 0)):
-                # broke after its last token but before [DONE]: complete already
+            if st.complete_already():
                 st.finish = st.finish or "length"
                 yield st
                 return
@@ -515,41 +572,33 @@ class Proxy:
             st.attempts += 1
             if st.attempts > 1:
                 self.stats["resumes" if st.k else "retries"] += 1
-            k0 = st.k
+            k_before = st.k
             try:
-                async for c in self._attempt(st, ep, path):
+                async for c in self._attempt(st, ep):
                     yield c
                 yield st
                 return
             except HTTPPassthrough:
                 raise
             except (StreamBroken, ValueError, KeyError, *RETRYABLE) as e:
-                if st.moved:        # planned cut-over: no blame, no attempt used
+                if st.moved:                    # planned cut-over: no blame, no attempt used
                     st.moved = False
                     st.attempts -= 1
-                    self.stats["moves"] = self.stats.get("moves", 0) + 1
+                    self.stats["moves"] += 1
                     continue
-                last_err = f"idle > {self.idle_timeout}s" if isinstance(e, asyncio.TimeoutError) \
+                reason = f"idle > {self.idle_timeout}s" if isinstance(e, asyncio.TimeoutError) \
                     else f"{type(e).__name__}: {e}"
-                if getattr(st, "spare_endpoint", False):
-                    st.spare_endpoint = False       # not this replica's fault
-                elif isinstance(e, asyncio.TimeoutError) and await self._alive(ep):
-                    log.info("%s idle but alive: resuming elsewhere without blacklisting", ep.url)
-                else:
-                    self.pool.mark_bad(ep, last_err)
+                if await self.on_attempt_failed(st, ep, e, st.k - k_before):
+                    self.pool.mark_bad(ep, reason)
                 tried.append(ep.url)
                 if len(tried) >= len(self.pool.order):
                     tried = tried[-1:]
                 log.warning("attempt %d on %s failed after %d tokens (%d here): %s", st.attempts, ep.url, st.k,
-                            st.k - k0, last_err)
+                            st.k - k_before, reason)
                 if not st.can_resume():
                     break
         self.stats["failed"] += 1
-        raise UpstreamFailed(last_err, st)
-
-    def pick(self, st: Resumer, tried) -> Optional[Endpoint]:
-        """Replica for the next attempt (session-aware routers override)."""
-        return self.pool.pick(exclude=tried) or self.pool.pick()
+        raise UpstreamFailed(reason, st)
 
     def move(self, st: Resumer) -> bool:
         """Cut ``st`` over: close its backend stream and resume it elsewhere."""
@@ -559,7 +608,7 @@ class Proxy:
         st.resp.close()
         return True
 
-    # ------------------------------------------------------------ handlers
+    # -------------------------------------------------------------- handlers
     async def handle_completions(self, request):
         return await self._handle(request, "completions")
 
@@ -568,6 +617,9 @@ class Proxy:
 
     async def _handle(self, request, kind: str):
         body = await request.json()
+        return await self.respond(request, kind, body)
+
+    async def respond(self, request, kind: str, body: dict):
         gen = self.generate(kind, body)
         if body.get("stream"):
             return await self._stream(request, gen)
@@ -575,22 +627,23 @@ class Proxy:
 
     async def _stream(self, request, gen):
         resp = None
+
+        async def opened():
+            nonlocal resp
+            if resp is None:
+                resp = web.StreamResponse(headers={"Content-Type": "text/event-stream", "Cache-Control": "no-cache"})
+                await resp.prepare(request)
+            return resp
         try:
             async for c in gen:
                 if isinstance(c, Resumer):
-                    if resp is None:
-                        resp = web.StreamResponse(headers={"Content-Type": "text/event-stream"})
-                        await resp.prepare(request)
+                    out = await opened()
                     if c.client_usage:
-                        await resp.write(_sse({"id": c.rid, "object": _obj(c.chat), "created": c.created,
-                                               "model": c.model, "choices": [], "usage": c.usage()}))
-                    await resp.write(b"data: [DONE]\n\n")
+                        await out.write(_sse({"id": c.rid, "object": _obj(c.chat), "created": c.created,
+                                              "model": c.model, "choices": [], "usage": c.usage()}))
+                    await out.write(b"data: [DONE]\n\n")
                     break
-                if resp is None:
-                    resp = web.StreamResponse(headers={"Content-Type": "text/event-stream",
-                                                       "Cache-Control": "no-cache"})
-                    await resp.prepare(request)
-                await resp.write(_sse(c))
+                await (await opened()).write(_sse(c))
         except HTTPPassthrough as e:
             if resp is None:
                 return web.Response(status=e.status, body=e.payload, content_type=e.ctype)
@@ -606,14 +659,15 @@ class Proxy:
         return resp
 
     async def _aggregate(self, gen, kind: str):
-        text, lps, st = [], [], None
+        pieces, lps, st = [], [], None
         try:
             async for c in gen:
                 if isinstance(c, Resumer):
                     st = c
                     break
                 ch = c["choices"][0]
-                text.append(((ch.get("delta") or {}).get("content") or "") if kind == "chat" else (ch.get("text") or ""))
+                pieces.append(((ch.get("delta") or {}).get("content") or "") if kind == "chat"
+                              else (ch.get("text") or ""))
                 if ch.get("logprobs"):
                     lps.append(ch["logprobs"])
         except HTTPPassthrough as e:
@@ -621,14 +675,11 @@ class Proxy:
         except UpstreamFailed as e:
             return web.json_response({"error": {"message": f"all replicas failed: {e}", "type": "upstream_failed"}},
                                      status=502)
-        content = "".join(text)
+        content = "".join(pieces)
         lp = _merge_lp(lps, kind == "chat")
-        if kind == "chat":
-            choice = {"index": 0, "message": {"role": "assistant", "content": content}, "logprobs": lp,
-                      "finish_reason": st.finish, "stop_reason": st.stop_reason}
-        else:
-            choice = {"index": 0, "text": content, "logprobs": lp, "finish_reason": st.finish,
-                      "stop_reason": st.stop_reason}
+        base = {"index": 0, "logprobs": lp, "finish_reason": st.finish, "stop_reason": st.stop_reason}
+        choice = {**base, "message": {"role": "assistant", "content": content}} if kind == "chat" \
+            else {**base, "text": content}
         return web.json_response({"id": st.rid, "object": "chat.completion" if kind == "chat" else "text_completion",
                                   "created": st.created, "model": st.model, "choices": [choice], "usage": st.usage()})
 
@@ -661,15 +712,13 @@ def _obj(chat: bool) -> str:
 
 
 def _merge_lp(lps, chat: bool):
+    """One logprobs block from the per-chunk blocks."""
     if not lps:
         return None
     if chat:
         return {"content": [x for lp in lps for x in lp.get("content") or []]}
-    out = {"tokens": [], "token_logprobs": [], "top_logprobs": [], "text_offset": []}
-    for lp in lps:
-        for k in out:
-            out[k].extend(lp.get(k) or [])
-    return out
+    keys = ("tokens", "token_logprobs", "top_logprobs", "text_offset")
+    return {k: [x for lp in lps for x in (lp.get(k) or [])] for k in keys}
 
 
 def main() -> None:
