@@ -85,8 +85,7 @@ def test_sequence_gap_forces_a_full_refresh(fr):
         assert wait_until(a.cache_in_sync, 3)
         b = _client(fr, 1)
         assert wait_until(lambda: len(a.get_stage_peers(1, refresh="never")) == 1, 3)
-        with a._sync_lock:                                 # pretend events were lost
-            a._last_seq -= 5
+        a.route_table.seq -= 5                             # pretend events were lost
         c = _client(fr, 1, 1)
         assert wait_until(lambda: a.stats["seq_gaps"] >= 1 and len(a.get_stage_peers(1, refresh="never")) == 2, 3)
         assert a.stats["full_refreshes"] >= 1 and wait_until(a.cache_in_sync, 3)
@@ -129,17 +128,17 @@ def test_migration_prepare_shadow_cutover(fr):
     try:
         b = _client(fr, 1, addr="tcp://10.0.0.1:5000")
         assert wait_until(lambda: len(a.get_stage_peers(1, refresh="never")) == 1, 3)
-        e0 = a._call_api("get_epoch", {})["epoch"]
-        r = a._call_api("prepare_migration", {"lid": _lid(1).to_dict(), "new_address": "tcp://10.0.0.9:6000"})
+        e0 = a.call("get_epoch", {})["epoch"]
+        r = a.call("prepare_migration", {"lid": _lid(1).to_dict(), "new_address": "tcp://10.0.0.9:6000"})
         assert r["success"] and r["new_epoch"] > e0
         mid = r["migration_id"]
         # clients got PREPARE_MIGRATION and answered shadow_ready on their own
         assert wait_until(lambda: fr.migration_orchestrator.get(mid) is not None and
                           len(fr.migration_orchestrator.get(mid).shadows_ready) >= 1, 3)
-        assert a._call_api("execute_cutover", {"migration_id": mid})["success"]
+        assert a.call("execute_cutover", {"migration_id": mid})["success"]
         assert wait_until(lambda: bool(done), 3)
         assert wait_until(lambda: a.get_peer_address(_lid(1)) == "tcp://10.0.0.9:6000", 3)
-        assert a._call_api("get_epoch", {})["epoch"] >= r["new_epoch"]
+        assert a.call("get_epoch", {})["epoch"] >= r["new_epoch"]
         b.stop()
     finally:
         a.stop()
@@ -152,9 +151,9 @@ def test_address_update_and_fallback_route(fr):
         assert b0.update_my_address(["tcp://10.1.1.1:7000"])
         assert wait_until(lambda: a.get_peer_address(_lid(1, 0)) == "tcp://10.1.1.1:7000", 3)
         fr.route_manager.update_route_state(_lid(1, 0), RouteState.DRAINING)
-        got = a._call_api("get_route", {"lid": _lid(1, 0).to_dict()})
+        got = a.call("get_route", {"lid": _lid(1, 0).to_dict()})
         assert got["is_fallback"] and got["fallback_replica"] == 1
-        strict = a._call_api("get_route", {"lid": _lid(1, 0).to_dict(), "allow_fallback": False})
+        strict = a.call("get_route", {"lid": _lid(1, 0).to_dict(), "allow_fallback": False})
         assert strict["route"]["lid"]["replica_idx"] == 0
         assert "error" in fr._handle_request({"method": "no_such_method"})
         b0.stop()
