@@ -34,6 +34,7 @@ re-sends them to the newly selected replica (sticky routing,
 """
 from __future__ import annotations
 
+import json
 import logging
 import os
 import pickle
@@ -140,6 +141,9 @@ def process_stats() -> dict:
     return {"fds": fds, "rss_mb": round(rss_mb, 1)}
 
 
+CONTROL_MAGIC = b"CXCTL"     # liveness-protocol messages (JSON) share the endpoint's sockets
+
+
 class ChainFailed(RuntimeError):
     """Raised by the K=1 receive when the downstream chain failed over."""
 
@@ -213,6 +217,15 @@ class PipelineEndpoint:
         self._send_lock = threading.Lock()      # a signal and its link sends stay together, per process
         self.auto_warm = False
         self._warm_threads: List[threading.Thread] = []
+        # liveness protocol (connex.pp.liveness) and the transport peer watch
+        self.control_handlers: List[Any] = []        # called with each control message (I/O thread)
+        self.route_listeners: List[Any] = []         # called with (stage, replica, address) on a new downstream
+        self.failure_veto = None                      # (stage, replica) -> True: ignore a failure report
+        self.last_step_from: Dict[str, float] = {}    # stage-0 address -> time of its last step here
+        self.done_seq = -1                            # the last step this stage answered
+        self._watch_pump = None
+        self._transport_up: set = set()
+        self.last_transport_failover: Optional[dict] = None
         if membership is not None:
             self.attach_membership(membership)
         self._io = threading.Thread(target=self._io_loop, name=f"cx-pp-io-{stage_idx}", daemon=True)
@@ -341,12 +354,27 @@ class PipelineEndpoint:
         self.trace("signaled", corr)
         self.prof.add("send", time.perf_counter() - t0)
 
+    def send_control(self, address: str, msg: dict) -> None:
+        """A liveness-protocol message (:mod:`connex.pp.liveness`) to the
+        endpoint at ``address``; it carries this endpoint's identity."""
+        body = dict(msg, **{"from": self.address, "stage": self.stage_idx, "replica": self.replica_idx})
+        self._post(address, [CONTROL_MAGIC + json.dumps(body).encode()])
+
+    def _on_control(self, body: bytes) -> None:
+        msg = json.loads(body[len(CONTROL_MAGIC):])
+        self.stats["control_" + str(msg.get("kind", "?")).lower()] += 1
+        for handler in list(self.control_handlers):
+            handler(msg)
+
     def _peer_name(self, address: str) -> str:
         """Link identity of the endpoint at ``address`` (carried after '#')."""
         return address.split("#", 1)[1] if "#" in address else address
 
     def _on_message(self, frames: List[bytes]) -> None:
         body = frames[0]
+        if body.startswith(CONTROL_MAGIC):
+            self._on_control(body)
+            return
         tok = wire.decode_ack(body)
         if tok is not None:
             if self._ring is not None:
@@ -405,6 +433,7 @@ class PipelineEndpoint:
                 else:
                     self.stats["late_replies"] += 1
             return
+        self.last_step_from[m.origin] = time.monotonic()
         cached = self.replies.get(m.corr)
         if cached is not None:          # duplicate of an answered step: answer again
             self.stats["dedup_replies"] += 1
@@ -426,13 +455,24 @@ class PipelineEndpoint:
             if self.current is not None and rep != self.current:
                 self.chain_epoch += 1
             self.current, self.current_addr = rep, addr
+            self._announce_route()
         return addr
+
+    def _announce_route(self) -> None:
+        for listener in list(self.route_listeners):
+            try:
+                listener(self.stage_idx + 1, self.current, self.current_addr)
+            except Exception:  # noqa: BLE001
+                log.exception("route listener")
 
     def set_downstream(self, address: str, replica_idx: int = 0) -> None:
         """Fixed downstream (no membership)."""
         if self.current_addr is not None and address != self.current_addr:
             self.chain_epoch += 1
+        changed = address != self.current_addr
         self.current, self.current_addr = replica_idx, address
+        if changed:
+            self._announce_route()
 
     def on_peer_dead(self, stage_idx: int, replica_idx: int, reason: str = "") -> bool:
         """A peer is gone; True if it was this endpoint's downstream."""
@@ -455,6 +495,53 @@ class PipelineEndpoint:
 
     def on_peer_alive(self, stage_idx: int, replica_idx: int) -> None:
         self.deregistered.discard((stage_idx, replica_idx))
+
+    # ---------------------------------------------------- transport watch
+    def watch_peers(self, engine, urls: Optional[Dict[Tuple[int, int], str]] = None) -> None:
+        """First tier of failure detection: follow ``engine``'s peer events
+        (the native engine reports a peer's socket reset or heartbeat loss
+        within milliseconds).  ``urls``: (stage, replica) -> engine URL of
+        downstream replicas to connect to (more with :meth:`watch_peer`).
+
+        A ``failed`` event about a downstream replica whose link was up
+        fails it over at once -- unless :attr:`failure_veto` says the report
+        is about an earlier incarnation; a failure by heartbeat timeout only
+        makes it suspect (the TCP probe decides)."""
+        from connex.pd.group import EventPump
+        self._watch_engine = engine
+        for (stage, replica), url in (urls or {}).items():
+            self.watch_peer(stage, replica, url)
+        self._watch_pump = EventPump(engine, self._on_transport_event, name=f"cx-pp-watch-{self.stage_idx}").start()
+
+    def watch_peer(self, stage_idx: int, replica_idx: int, url: str) -> None:
+        self._watch_engine.connect(url)
+
+    def _on_transport_event(self, ev: dict) -> None:
+        from connex.pd.group import is_timeout, peer_key
+        key = peer_key(ev)
+        if key is None or key[0] != self.model or key[1] != self.stage_idx + 1:
+            return
+        peer = (key[1], key[3])
+        if ev.get("type") in ("up", "joined"):
+            self._transport_up.add(peer)
+            return
+        if ev.get("type") != "failed" or peer not in self._transport_up:
+            return
+        self._transport_up.discard(peer)
+        t_event = time.monotonic()
+        if is_timeout(ev):
+            self.stats["transport_suspects"] += 1
+            if peer == (self.stage_idx + 1, self.current) and self.current_addr is not None:
+                alive = probe_tcp(self.current_addr)
+                if alive is False:
+                    self.on_peer_dead(peer[0], peer[1], "heartbeat lost, probe refused")
+            return
+        if self.failure_veto is not None and self.failure_veto(*peer):
+            return
+        self.stats["transport_failovers"] += 1
+        self.on_peer_dead(peer[0], peer[1], f"transport: {ev.get('reason', 'failed')}")
+        self.last_transport_failover = {"peer": peer, "event_t": t_event, "failover_t": time.monotonic(),
+                                        "reason": ev.get("reason")}
 
     def attach_membership(self, membership) -> None:
         """Route with ``membership`` and follow its deregister / register events."""
@@ -617,6 +704,7 @@ class PipelineEndpoint:
 
     def send_reply(self, td: dict, ctx: Tuple[int, str]) -> None:
         corr, origin = ctx
+        self.done_seq = corr
         self.replies.put(corr, (td, origin))
         self._send_reply_now(td, corr, origin)
 
@@ -645,6 +733,8 @@ class PipelineEndpoint:
 
     def close(self) -> None:
         self._stop.set()
+        if self._watch_pump is not None:
+            self._watch_pump.stop()
         self._io.join(timeout=2)
         self.trace.close()
         for s in list(self._dealers.values()) + [self.router, self._wake_rx, self._wake_tx]:

@@ -48,6 +48,15 @@ class _Pending:
     payload: dict
     sent_at: float = field(default_factory=time.monotonic)
     resends: int = 0
+    first_sent: float = field(default_factory=time.monotonic)
+
+    @property
+    def size(self) -> int:
+        """Scheduled tokens (``n_new``) or rows of the step, for comparing step times."""
+        n_new = self.payload.get("n_new")
+        if isinstance(n_new, (list, tuple)):
+            return int(sum(int(x) for x in n_new))
+        return len(self.payload.get(REQUEST_IDS) or ())
 
 
 class Stage0Link:
@@ -64,6 +73,7 @@ class Stage0Link:
         self.outbox = FinishedOutbox(finished_repeat)
         self.log = log
         self._pending: Dict[int, _Pending] = {}
+        self.step_listeners: List[Callable[[float, int], None]] = []    # (seconds, size) per completed step
         self.stats = {"steps": 0, "retries": 0, "reprefilled": 0, "aborted": 0}
 
     @property
@@ -73,6 +83,10 @@ class Stage0Link:
     def outstanding(self) -> List[int]:
         """Correlation ids of the steps awaiting a reply, oldest first."""
         return sorted(self._pending)
+
+    def pending_steps(self) -> List[tuple]:
+        """(corr, first sent at, size) of every step awaiting its reply."""
+        return [(c, p.first_sent, p.size) for c, p in list(self._pending.items())]
 
     def finished(self, request_ids: Sequence) -> None:
         """Requests stage 0 finished: tell the downstream stages, forget their budget."""
@@ -150,7 +164,10 @@ class Stage0Link:
             self._hand_over_others(corr)
             reply = self.t.recv_step(corr, self.recv_timeout_s)
         tr("s0_reply", corr)
-        self._pending.pop(corr, None)
+        done = self._pending.pop(corr, None)
+        if done is not None:
+            for listener in list(self.step_listeners):
+                listener(time.monotonic() - done.first_sent, done.size)
         self._settle_missing(reply)
         return reply
 
