@@ -142,6 +142,7 @@ def process_stats() -> dict:
 
 
 CONTROL_MAGIC = b"CXCTL"     # liveness-protocol messages (JSON) share the endpoint's sockets
+ENGINE_ADDRESS_PREFIX = "cx="  # a listed address "cx=<url>": the replica's transfer engine (peer events)
 
 
 class ChainFailed(RuntimeError):
@@ -224,6 +225,8 @@ class PipelineEndpoint:
         self.last_step_from: Dict[str, float] = {}    # stage-0 address -> time of its last step here
         self.done_seq = -1                            # the last step this stage answered
         self._watch_pump = None
+        self._watch_engine = None
+        self._watched: dict = {}            # (stage, replica) -> engine URL connected for peer events
         self._transport_up: set = set()
         self.last_transport_failover: Optional[dict] = None
         if membership is not None:
@@ -511,10 +514,31 @@ class PipelineEndpoint:
         self._watch_engine = engine
         for (stage, replica), url in (urls or {}).items():
             self.watch_peer(stage, replica, url)
+        if self.membership is not None:
+            for r in self.membership.get_stage_peers(self.stage_idx + 1):
+                self._watch_listed(r.lid.stage_idx, r.lid.replica_idx, r.addresses)
         self._watch_pump = EventPump(engine, self._on_transport_event, name=f"cx-pp-watch-{self.stage_idx}").start()
 
-    def watch_peer(self, stage_idx: int, replica_idx: int, url: str) -> None:
-        self._watch_engine.connect(url)
+    def watch_peer(self, stage_idx: int, replica_idx: int, url: str) -> bool:
+        """Connect the watch engine to a downstream replica's engine (once per
+        incarnation: a failed peer is connected again when it is listed again)."""
+        if self._watch_engine is None or self._watched.get((stage_idx, replica_idx)) == url:
+            return False
+        self._watched[(stage_idx, replica_idx)] = url
+        try:
+            return bool(self._watch_engine.connect(url))
+        except Exception as e:  # noqa: BLE001 - the lease tier still covers this peer
+            log.warning("stage %s: cannot watch %s: %s", self.stage_idx, url, e)
+            return False
+
+    def _watch_listed(self, stage_idx: int, replica_idx: int, addresses) -> None:
+        """Watch a listed downstream replica that advertises an engine
+        (an address ``cx=<engine url>`` beside its step address)."""
+        if stage_idx != self.stage_idx + 1:
+            return
+        for a in addresses or ():
+            if isinstance(a, str) and a.startswith(ENGINE_ADDRESS_PREFIX):
+                self.watch_peer(stage_idx, replica_idx, a[len(ENGINE_ADDRESS_PREFIX):])
 
     def _on_transport_event(self, ev: dict) -> None:
         from connex.pd.group import is_timeout, peer_key
@@ -528,6 +552,7 @@ class PipelineEndpoint:
         if ev.get("type") != "failed" or peer not in self._transport_up:
             return
         self._transport_up.discard(peer)
+        self._watched.pop(peer, None)
         t_event = time.monotonic()
         if is_timeout(ev):
             self.stats["transport_suspects"] += 1
@@ -591,6 +616,8 @@ class PipelineEndpoint:
             self.suspect.discard((lid["stage_idx"], lid.get("replica_idx", 0)))
             self.on_peer_alive(lid["stage_idx"], lid.get("replica_idx", 0))
             addrs = payload.get("addresses") or []
+            if self._watch_engine is not None:
+                self._watch_listed(lid["stage_idx"], lid.get("replica_idx", 0), addrs)
             if self.auto_warm and self.is_first and lid["stage_idx"] == 1 and addrs:
                 t = threading.Thread(target=self.warm, args=(addrs[0],), daemon=True, name="cx-pp-warm")
                 t.start()

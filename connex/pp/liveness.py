@@ -53,7 +53,7 @@ import os
 import threading
 import time
 from dataclasses import dataclass
-from typing import Deque, Dict, List, Optional, Sequence, Tuple
+from typing import Callable, Deque, Dict, List, Optional, Sequence, Tuple
 
 log = logging.getLogger("connex.pp.liveness")
 
@@ -181,6 +181,9 @@ class ChainWatchdog:
     """Stage 0's side of the protocol: HELLO to every downstream it routes to,
     reacts to HELLO_OK / BUSY / READY / DYING, and finds hung stages.
 
+    A hung replica further down than our own downstream is failed over by
+    its upstream replica (FAILOVER) and reported through ``report``.
+
     Step timeout: the fixed ``step_timeout`` until ``min_samples`` steps came
     back; then ``factor`` x the slowest measured step at least as large as the
     late one (clamped to [``min_timeout``, ``step_timeout``]) -- after many
@@ -189,12 +192,13 @@ class ChainWatchdog:
     the whole route (each PONG names the next hop), then :func:`pick_stuck`."""
 
     def __init__(self, ep, link, step_timeout: float = 60.0, min_timeout: float = 2.0, factor: float = 20.0,
-                 min_samples: int = 32, ping_wait_s: float = 1.0, period_s: float = 0.5, membership=None):
+                 min_samples: int = 32, ping_wait_s: float = 1.0, period_s: float = 0.5,
+                 report: Optional[Callable[[int, int, str], None]] = None):
         self.ep, self.link = ep, link
         self.step_timeout, self.min_timeout, self.factor = step_timeout, min_timeout, factor
         self.min_samples = min_samples
         self.ping_wait_s, self.period_s = ping_wait_s, period_s
-        self.membership = membership
+        self.report = report           # (stage, replica, reason) -> tell the membership service
         self.hops: Dict[Tuple[int, int], Hop] = {}
         self.samples: Deque[Tuple[float, int]] = collections.deque(maxlen=512)
         self.events: List[dict] = []
@@ -311,9 +315,8 @@ class ChainWatchdog:
         if upstream is not None:
             self.ep.send_control(upstream.address, {"kind": FAILOVER, "target_stage": hop.stage,
                                                     "target_replica": hop.replica, "reason": reason})
-        if self.membership is not None and hasattr(self.membership, "report_failure"):
-            from connex.front_router import LogicalEndpointID
-            self.membership.report_failure(LogicalEndpointID(self.ep.model, hop.stage, 0, hop.replica), reason)
+        if self.report is not None:
+            self.report(hop.stage, hop.replica, reason)
 
     def check_once(self) -> Optional[Hop]:
         """One watchdog round; returns the replica it failed over, if any."""

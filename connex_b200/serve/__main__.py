@@ -52,6 +52,8 @@ def model_args(ap: argparse.ArgumentParser) -> None:
     ap.add_argument("--advertise-host", default=os.getenv("CONNEX_HOST_IP", "127.0.0.1"),
                     help="address the pipeline endpoint binds and advertises")
     ap.add_argument("--recv-timeout-s", type=float, default=30.0)
+    ap.add_argument("--step-timeout-s", type=float, default=60.0,
+                    help="stage 0: the step watchdog's fixed timeout (until enough steps were measured)")
     ap.add_argument("--no-graphs", action="store_true", help="launch decode steps eagerly (no CUDA graphs)")
     ap.add_argument("--tp", type=int, default=1,
                     help="tensor-parallel ranks (launch with torchrun --nproc-per-node TP; rank 0 serves HTTP)")
@@ -114,6 +116,7 @@ def build_stepper(a):
                          a.seed, a.recv_timeout_s, graphs=not a.no_graphs)
     ep.warm_stage(1)
     ep.auto_warm = True
+    ep.watchdog = pipeline.watchdog(ep, st.link, client, step_timeout=a.step_timeout_s)
     return st, (ep, client)
 
 
@@ -133,6 +136,7 @@ def _rule_pipeline(a):
                          recv_timeout_s=a.recv_timeout_s, rt=RuleStageRuntime(True, False, 1000))
     ep.warm_stage(1)
     ep.auto_warm = True
+    ep.watchdog = pipeline.watchdog(ep, st.link, client, step_timeout=a.step_timeout_s)
     return st, (ep, client)
 
 

@@ -82,6 +82,8 @@ def test_pipeline_cli_failover_keeps_the_stream_exact(tmp_path):
         assert done and _text(chunks) == reference("t7 t8", 60)[1]
         log1 = (tmp_path / "s1r1.log").read_text()
         assert "no KV here" in log1, log1[-2000:]                               # re-prefilled on replica 1
+        log0 = (tmp_path / "s0.log").read_text()
+        assert "transport:" in log0, log0[-3000:]                               # the engine's peer event moved it
     finally:
         for p, f in procs.values():
             if p.poll() is None:
