@@ -5,7 +5,18 @@
 managed / registered memory, ``transfer_sync_read/write``, ``get_async`` /
 ``put_async`` / ``put_signal`` handles, messages, peer events
 (``up`` / ``joined`` / ``failed``) and counters.  Error codes:
-``PEER_FAILED`` (-2), ``TIMEOUT`` (-3), ``INVALID`` (-4).
+``PEER_FAILED`` (-2), ``TIMEOUT`` (-3), ``INVALID`` (-4), ``CANCELLED`` (-5).
+
+Device memory: ``allocate_device_buffer(size, device)`` gives a GPU range
+(a VMM allocation) that peers on the same machine map and reach with the
+copy engines; any other registered device range (a torch tensor) is exported
+through its legacy IPC handle.  Device ranges are never served over the
+socket path (a peer on another machine gets ``INVALID``).  ``put_chain`` is
+the doorbell -> gate -> payload -> flag chain of a ring channel.  A dead
+peer's mappings are released once the copies that touched them have passed
+(``reap``; also run by the heartbeat thread).  :class:`DeviceBuffer` /
+:class:`Mapping` are the same export / import for buffers shared without an
+engine (:mod:`connex_b200.parallel.peer`).
 
 :class:`CxEngineTransport` adapts it to the ``ElasticPeerSet`` transport duck
 type, and :func:`url_identity` parses identities out of engine URLs.
@@ -14,7 +25,8 @@ from __future__ import annotations
 
 from typing import Any, Optional, Tuple
 
-from connex_b200._cxengine import INVALID, OK, PEER_FAILED, TIMEOUT, Engine, Handle  # noqa: F401
+from connex_b200._cxengine import (CANCELLED, INVALID, OK, PEER_FAILED, TIMEOUT, DeviceBuffer, Engine,  # noqa: F401
+                                   Handle, Mapping, boot_id, device_memory_info, device_plane)
 
 
 def url_identity(url: str) -> Optional[Tuple[str, int, int, int]]:

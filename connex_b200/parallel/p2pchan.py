@@ -33,7 +33,7 @@ import torch
 import torch.distributed as dist
 
 from connex_b200 import ops
-from connex_b200.parallel.peer import PeerHandle, PeerMapper, export_tensor
+from connex_b200.parallel.peer import PeerHandle, PeerMapper, export_tensor, shared_empty
 
 ALIGN = 256
 CHAN_CTAS = 64
@@ -132,8 +132,10 @@ class ChanRx(_Stream):
     def __init__(self, device, slots: int, slot_bytes: int, timeout_s: float):
         super().__init__(device)
         self.slots, self.slot_bytes = slots, slot_bytes
-        self.ring = torch.empty(slots, slot_bytes, dtype=torch.uint8, device=device)
-        self.ready = torch.zeros(4, dtype=torch.int32, device=device)      # [0] ready, [1] CTA counter
+        # VMM allocations (zero-filled): the sender's mappings of them are
+        # released deterministically when either side goes away
+        self.ring = shared_empty((slots, slot_bytes), torch.uint8, device)
+        self.ready = shared_empty((4,), torch.int32, device)      # [0] ready, [1] CTA counter
         self.credit_addr = 0            # the sender's credit counter (peer mapping)
         self.seq = 0
         self.expected = 0
@@ -191,11 +193,11 @@ class ChanLinks:
             hit = self._links.get((peer, True))
         if hit is not None:
             return hit
-        credit = torch.zeros(4, dtype=torch.int32, device=self.device)
+        credit = shared_empty((4,), torch.int32, self.device)
         self.store.set(self._key(self.me, peer, "tx"), pickle.dumps(export_tensor(credit).to_dict()))
         rx = self._get(self._key(self.me, peer, "rx"))
-        ring = self.mapper.open(PeerHandle.from_dict(rx["ring"]))
-        ready = self.mapper.open(PeerHandle.from_dict(rx["ready"]))
+        ring = self.mapper.open(PeerHandle.from_dict(rx["ring"]), owner=peer)
+        ready = self.mapper.open(PeerHandle.from_dict(rx["ready"]), owner=peer)
         link = ChanTx(self.device, ring, ready, rx["slots"], rx["slot_bytes"], credit, self.timeout_s)
         with self._lock:
             self._links[(peer, True)] = link
@@ -211,7 +213,7 @@ class ChanLinks:
             "ring": export_tensor(link.ring).to_dict(), "ready": export_tensor(link.ready).to_dict(),
             "slots": self.slots, "slot_bytes": self.slot_bytes}))
         tx = self._get(self._key(peer, self.me, "tx"))
-        link.credit_addr = self.mapper.open(PeerHandle.from_dict(tx))
+        link.credit_addr = self.mapper.open(PeerHandle.from_dict(tx), owner=peer)
         with self._lock:
             self._links[(peer, False)] = link
         return link
@@ -224,7 +226,9 @@ class ChanLinks:
         launches return at once (status CX_ERR_PEER) instead of waiting out
         their timeout, and store nothing into the peer's memory; the link
         objects stay alive until their streams have drained (their abort
-        words and buffers are still read by those launches)."""
+        words and buffers are still read by those launches), and so do the
+        mappings of the peer's memory: they are released once those streams
+        have passed (:meth:`reap`, also run by :meth:`check`)."""
         with self._lock:
             keys = [k for k in self._links if k[0] == peer]
             dropped = [self._links.pop(k) for k in keys]
@@ -232,9 +236,17 @@ class ChanLinks:
         if abort:
             for l in dropped:
                 l.cancel()
+        self.mapper.forget(peer, [l.stream for l in dropped])
+        self.mapper.reap()
         return len(keys)
 
+    def reap(self) -> int:
+        """Release dropped peers' mappings whose streams have passed; returns
+        how many are still held."""
+        return self.mapper.reap()
+
     def check(self) -> None:
+        self.mapper.reap()
         for l in list(self._links.values()):
             ops.check_status(l.status, "p2p channel")
 

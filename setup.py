@@ -6,9 +6,11 @@ Two native modules are built in-tree (``python setup.py build_ext --inplace``):
                                fused KV push, EP dispatch/combine, weight sync)
                                and the CUDA IPC plumbing, bound with pybind11.
 * ``connex_b200._cxengine`` -- the C++17 transfer engine (identity-keyed
-                               endpoints, registered regions, one-sided
-                               read/write, events, heartbeats) that provides the
-                               data-plane surface of the control plane.
+                               endpoints, host and GPU regions, one-sided
+                               read/write, put_chain, events, heartbeats, VMM
+                               export and the dead-peer graveyard) that
+                               provides the data-plane surface of the control
+                               plane.
 
 Every CUDA file is compiled for exactly one target: sm_100a (B200).
 """
@@ -16,7 +18,7 @@ import os
 import glob
 
 from setuptools import Extension, setup, find_packages
-from torch.utils.cpp_extension import BuildExtension, CUDAExtension, CppExtension
+from torch.utils.cpp_extension import CUDA_HOME, BuildExtension, CUDAExtension, CppExtension
 
 ROOT = os.path.dirname(os.path.abspath(__file__))
 KDIR = os.path.join("connex_b200", "csrc", "kernels")
@@ -42,15 +44,17 @@ ext_modules = [
     ),
 ]
 if engine_sources:
-    # plain pybind11 module: importing the engine does not load libtorch
+    # plain pybind11 module: importing the engine loads neither libtorch nor
+    # libcuda (the driver API is resolved at run time; cuda.h gives the types)
     import pybind11
     ext_modules.append(
         Extension(
             name="connex_b200._cxengine",
             sources=engine_sources,
-            include_dirs=[os.path.join(ROOT, EDIR), pybind11.get_include()],
+            include_dirs=[os.path.join(ROOT, EDIR), pybind11.get_include(),
+                          os.path.join(CUDA_HOME or "/usr/local/cuda", "include")],
             extra_compile_args=CXX_FLAGS + ["-pthread", "-fvisibility=hidden"],
-            extra_link_args=["-pthread"],
+            extra_link_args=["-pthread", "-ldl"],
             language="c++",
         )
     )
