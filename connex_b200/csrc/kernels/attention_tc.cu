@@ -18,6 +18,15 @@
 //               when the running max grew by more than 2^8); P is written
 //               into the 128-byte-swizzled K-major layout the MMA reads.
 // All waits are bounded (status word on timeout); no cluster multicast.
+//
+// Paged variant (chunked prefill): the chunk's queries come from the QKV
+// buffer, while K and V of the whole context -- earlier chunks and this
+// one, already written by rope_cache -- stream from the paged cache through
+// the sequence's block table: each 64-key tile is four 16-token blocks, each
+// loaded as [16 rows x 64 dims] boxes into the same swizzled tile layout
+// (a box lands at a 2 KB offset, so the 1 KB swizzle pattern is unchanged).
+// Query i of a chunk with context c sits at position c + i and sees keys
+// [0, c + i].
 #include "common.cuh"
 #include "gemm.h"
 #include "layers.h"
@@ -62,10 +71,12 @@ __device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t smem_addr, uint3
 }
 }  // namespace fatc
 
+template <bool PAGED>
 __global__ void __launch_bounds__(fatc::THREADS, 2)
-    prefill_attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmkv,
-                           __nv_bfloat16* __restrict__ out, int ldo, const int* __restrict__ tile_info, int n_tiles,
-                           int Hq, int Hkv, float scale_log2, int* status) {
+    prefill_attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                           const __grid_constant__ CUtensorMap tmv, __nv_bfloat16* __restrict__ out, int ldo,
+                           const int* __restrict__ tile_info, int n_tiles, int Hq, int Hkv, float scale_log2,
+                           const int* __restrict__ block_tables, int bt_stride, int* status) {
   using namespace fatc;
   extern __shared__ __align__(1024) uint8_t smem[];
   if ((smem_u32(smem) & 1023u) != 0) {  // swizzled operands need a 1 KB-aligned base
@@ -87,11 +98,15 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
 
   const int tile = n_tiles - 1 - (int)blockIdx.x;  // heaviest (latest) tiles first
   const int h = blockIdx.y;
-  const int seq_start = tile_info[tile * 3 + 0];
-  const int seq_len = tile_info[tile * 3 + 1];
-  const int q0 = tile_info[tile * 3 + 2];
+  const int* ti = tile_info + tile * (PAGED ? 5 : 3);
+  const int seq_start = ti[0];                    // first row of the sequence's new tokens in QKV
+  const int seq_len = ti[1];                      // its new tokens
+  const int q0 = ti[2];                           // first query of this tile (among the new tokens)
+  const int ctx = PAGED ? ti[3] : 0;              // tokens already in the cache before them
+  const int* bt = PAGED ? block_tables + (size_t)ti[4] * bt_stride : nullptr;
+  const int total = ctx + seq_len;
   const int g = h / (Hq / Hkv);
-  const int kv_len = min(seq_len, q0 + BM);
+  const int kv_len = min(total, ctx + q0 + BM);
   const int nkv = (kv_len + BN - 1) / BN;
   const int qcol = h * D, kcol = (Hq + g) * D, vcol = (Hq + Hkv + g) * D;
 
@@ -111,7 +126,8 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
     mbar_init(drain, 1);
     fence_barrier_init();
     prefetch_tmap(&tmq);
-    prefetch_tmap(&tmkv);
+    prefetch_tmap(&tmk);
+    if (PAGED) prefetch_tmap(&tmv);
   }
   if (warp == 1) {
     tmem_alloc(tmem_slot, TMEM_COLS);
@@ -129,31 +145,58 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
       mbar_arrive_expect_tx(q_full, 2 * Q_HALF);
       tma_load_2d(smem + OFF_Q, &tmq, q_full, qcol, row0);
       tma_load_2d(smem + OFF_Q + Q_HALF, &tmq, q_full, qcol + 64, row0);
+      // paged: cache rows of the four 16-token blocks of a key tile (tile j's
+      // block ids are fetched one tile ahead so their loads are in flight)
+      constexpr int BPT = BN / 16;
+      const int nblk = (total + 15) / 16;
+      auto rows_of = [&](int j, int (&r)[BPT]) {
+#pragma unroll
+        for (int i = 0; i < BPT; ++i) {
+          const int b = j * BPT + i;
+          r[i] = (bt[b < nblk ? b : 0] * Hkv + g) * 16;  // past the end: any valid block (masked)
+        }
+      };
+      auto load_tile = [&](const CUtensorMap* map, uint8_t* buf, uint64_t* bar, int col, int j, const int (&r)[BPT]) {
+        if constexpr (PAGED) {
+#pragma unroll
+          for (int i = 0; i < BPT; ++i) {
+            tma_load_2d(buf + i * 2048, map, bar, 0, r[i]);
+            tma_load_2d(buf + KV_HALF + i * 2048, map, bar, 64, r[i]);
+          }
+        } else {
+          tma_load_2d(buf, map, bar, col, seq_start + j * BN);
+          tma_load_2d(buf + KV_HALF, map, bar, col + 64, seq_start + j * BN);
+        }
+      };
+      int r_cur[BPT] = {}, r_prev[BPT] = {}, r_next[BPT] = {};
+      if (PAGED) rows_of(0, r_cur);
       // K_j goes out before V_{j-1}: K stages free up earlier (after Q.K^T)
       auto load_k = [&](int j) -> bool {
         const int s = j & 1;
         if (!mbar_wait(&k_empty[s], ((j >> 1) & 1) ^ 1, status)) return false;
         mbar_arrive_expect_tx(&k_full[s], KV_TILE);
-        uint8_t* kb = smem + OFF_K + s * KV_TILE;
-        tma_load_2d(kb, &tmkv, &k_full[s], kcol, seq_start + j * BN);
-        tma_load_2d(kb + KV_HALF, &tmkv, &k_full[s], kcol + 64, seq_start + j * BN);
+        load_tile(&tmk, smem + OFF_K + s * KV_TILE, &k_full[s], kcol, j, r_cur);
         return true;
       };
-      auto load_v = [&](int j) -> bool {
+      auto load_v = [&](int j, const int (&r)[BPT]) -> bool {
         const int s = j & 1;
         if (!mbar_wait(&v_empty[s], ((j >> 1) & 1) ^ 1, status)) return false;
         mbar_arrive_expect_tx(&v_full[s], KV_TILE);
-        uint8_t* vb = smem + OFF_V + s * KV_TILE;
-        tma_load_2d(vb, &tmkv, &v_full[s], vcol, seq_start + j * BN);
-        tma_load_2d(vb + KV_HALF, &tmkv, &v_full[s], vcol + 64, seq_start + j * BN);
+        load_tile(&tmv, smem + OFF_V + s * KV_TILE, &v_full[s], vcol, j, r);
         return true;
       };
       bool good = true;
       for (int j = 0; j < nkv && good; ++j) {
         good = load_k(j);
-        if (good && j >= 1) good = load_v(j - 1);
+        if (PAGED && j + 1 < nkv) rows_of(j + 1, r_next);
+        if (good && j >= 1) good = load_v(j - 1, r_prev);
+#pragma unroll
+        for (int i = 0; i < BPT; ++i) {
+          r_prev[i] = r_cur[i];
+          r_cur[i] = r_next[i];
+        }
       }
-      if (good) load_v(nkv - 1);
+      if (good) load_v(nkv - 1, r_prev);
     }
     __syncwarp();
   } else if (warp == 1) {
@@ -203,7 +246,7 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
   } else {
     const int q = warp & 3;
     const int row = q * 32 + lane;
-    const int qpos = q0 + row;
+    const int qpos = ctx + q0 + row;  // position in the sequence
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     uint8_t* prow = smem + OFF_P + row * 128;
     const uint32_t swz = (uint32_t)(row & 7);
@@ -225,14 +268,14 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
       tc_fence_before();
       mbar_arrive(&s_free[s]);  // S[s] is in registers now
       const int key0 = j * BN;
-      const bool mask = (key0 + BN - 1 > q0) || (key0 + BN > seq_len);
+      const bool mask = (key0 + BN - 1 > ctx + q0) || (key0 + BN > total);
       // raw scores stay unscaled: the scale is folded into one FFMA per
       // element below (scale > 0, so the max commutes with it)
       float mx_raw = -INFINITY;
 #pragma unroll
       for (int e = 0; e < BN; ++e) {
         float v = __uint_as_float(r[e]);
-        if (mask && (key0 + e > qpos || key0 + e >= seq_len)) {
+        if (mask && (key0 + e > qpos || key0 + e >= total)) {
           v = -INFINITY;
           r[e] = __float_as_uint(v);
         }
@@ -287,8 +330,8 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
     if (ok && mbar_wait(pv_done, (nkv - 1) & 1, status)) {
       tc_fence_after();
       const float inv = l > 0.f ? 1.f / l : 0.f;
-      const bool valid = qpos < seq_len;
-      __nv_bfloat16* orow = out + (size_t)(seq_start + qpos) * ldo + (size_t)h * D;
+      const bool valid = q0 + row < seq_len;
+      __nv_bfloat16* orow = out + (size_t)(seq_start + q0 + row) * ldo + (size_t)h * D;
 #pragma unroll 1
       for (int c = 0; c < D / 32; ++c) {
         uint32_t o[32];
@@ -315,22 +358,43 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
   }
 }
 
-void prefill_attention_tc(const void* qkv, int ldq, int qkv_cols, int T, void* out, int ldo, const int* tile_info,
-                          int n_tiles, int Hq, int Hkv, float scale, int* status, cudaStream_t s) {
-  if (n_tiles == 0) return;
+template <bool PAGED>
+static void set_smem_once() {
   static bool attr[64] = {false};
   int dev;
   cudaGetDevice(&dev);
   if (!attr[dev & 63]) {
-    cudaFuncSetAttribute(prefill_attn_tc_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, fatc::SMEM);
+    cudaFuncSetAttribute(prefill_attn_tc_kernel<PAGED>, cudaFuncAttributeMaxDynamicSharedMemorySize, fatc::SMEM);
     attr[dev & 63] = true;
   }
+}
+
+void prefill_attention_tc(const void* qkv, int ldq, int qkv_cols, int T, void* out, int ldo, const int* tile_info,
+                          int n_tiles, int Hq, int Hkv, float scale, int* status, cudaStream_t s) {
+  if (n_tiles == 0) return;
+  set_smem_once<false>();
   const CUtensorMap tq = make_tmap_bf16_2d(qkv, (uint64_t)qkv_cols, (uint64_t)T, (uint64_t)ldq * 2, 64, 128, true);
   const CUtensorMap tkv = make_tmap_bf16_2d(qkv, (uint64_t)qkv_cols, (uint64_t)T, (uint64_t)ldq * 2, 64, 64, true);
   dim3 grid(n_tiles, Hq);
-  prefill_attn_tc_kernel<<<grid, fatc::THREADS, fatc::SMEM, s>>>(tq, tkv, reinterpret_cast<__nv_bfloat16*>(out),
-                                                                  ldo, tile_info, n_tiles, Hq, Hkv,
-                                                                  scale * 1.4426950408889634f, status);
+  prefill_attn_tc_kernel<false><<<grid, fatc::THREADS, fatc::SMEM, s>>>(
+      tq, tkv, tkv, reinterpret_cast<__nv_bfloat16*>(out), ldo, tile_info, n_tiles, Hq, Hkv,
+      scale * 1.4426950408889634f, nullptr, 0, status);
+}
+
+void prefill_attention_paged_tc(const void* qkv, int ldq, int qkv_cols, int T, const void* kc, const void* vc,
+                                int64_t cache_rows, const int* block_tables, int bt_stride, void* out, int ldo,
+                                const int* tile_info, int n_tiles, int Hq, int Hkv, float scale, int* status,
+                                cudaStream_t s) {
+  if (n_tiles == 0) return;
+  set_smem_once<true>();
+  const CUtensorMap tq = make_tmap_bf16_2d(qkv, (uint64_t)qkv_cols, (uint64_t)T, (uint64_t)ldq * 2, 64, 128, true);
+  // caches as [blocks * Hkv * 16 rows, 128 dims]: one row per (block, head, token)
+  const CUtensorMap tk = make_tmap_bf16_2d(kc, 128, (uint64_t)cache_rows, 256, 64, 16, true);
+  const CUtensorMap tv = make_tmap_bf16_2d(vc, 128, (uint64_t)cache_rows, 256, 64, 16, true);
+  dim3 grid(n_tiles, Hq);
+  prefill_attn_tc_kernel<true><<<grid, fatc::THREADS, fatc::SMEM, s>>>(
+      tq, tk, tv, reinterpret_cast<__nv_bfloat16*>(out), ldo, tile_info, n_tiles, Hq, Hkv,
+      scale * 1.4426950408889634f, block_tables, bt_stride, status);
 }
 
 }  // namespace cx

@@ -162,6 +162,29 @@ void prefill_attention_tc(const at::Tensor& qkv, at::Tensor& out, const at::Tens
                            (float)scale, status_ptr(status), cur_stream(qkv));
 }
 
+void prefill_attention_paged(const at::Tensor& qkv, const at::Tensor& kc, const at::Tensor& vc,
+                             const at::Tensor& block_tables, at::Tensor& out, const at::Tensor& tile_info, int64_t Hq,
+                             int64_t Hkv, double scale, const c10::optional<at::Tensor>& status) {
+  CHECK_BF16(qkv);
+  CHECK_BF16(kc);
+  CHECK_BF16(vc);
+  CHECK_BF16(out);
+  TORCH_CHECK(tile_info.scalar_type() == at::kInt && tile_info.dim() == 2 && tile_info.size(1) == 5,
+              "tile_info must be int32 [n, 5]");
+  TORCH_CHECK(block_tables.scalar_type() == at::kInt && block_tables.dim() == 2 && block_tables.is_contiguous(),
+              "block_tables must be contiguous int32 [B, max_blocks]");
+  TORCH_CHECK(qkv.size(1) == (Hq + 2 * Hkv) * 128, "qkv must hold exactly (Hq + 2 Hkv) heads of 128");
+  TORCH_CHECK(kc.dim() == 4 && kc.size(1) == Hkv && kc.size(2) == 16 && kc.size(3) == 128 && kc.is_contiguous() &&
+                  vc.is_contiguous() && vc.sizes() == kc.sizes(),
+              "caches must be contiguous [blocks, Hkv, 16, 128]");
+  const c10::cuda::CUDAGuard g(qkv.device());
+  cx::prefill_attention_paged_tc(qkv.data_ptr(), row_ld(qkv), (int)qkv.size(1), (int)qkv.size(0), kc.data_ptr(),
+                                 vc.data_ptr(), kc.size(0) * Hkv * 16, block_tables.data_ptr<int>(),
+                                 (int)block_tables.size(1), out.data_ptr(), row_ld(out), tile_info.data_ptr<int>(),
+                                 (int)tile_info.size(0), (int)Hq, (int)Hkv, (float)scale, status_ptr(status),
+                                 cur_stream(qkv));
+}
+
 void decode_attention(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc, const at::Tensor& block_tables,
                       const at::Tensor& ctx_lens, at::Tensor& out, int64_t Hq, int64_t max_ctx, double scale,
                       at::Tensor& workspace) {
@@ -391,6 +414,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("argmax", &argmax);
   m.def("gather_rows", &gather_rows);
   m.def("prefill_attention", &prefill_attention_tc);
+  m.def("prefill_attention_paged", &prefill_attention_paged);
   m.def("decode_attention", &decode_attention);
   m.def("decode_attention_plan", &decode_attention_plan);
   m.def("decode_workspace_floats", &decode_workspace_floats);

@@ -21,6 +21,15 @@ void gather_rows(const void* src, int lds, const int* idx, void* out, int ldo, i
 // the 128-row tile).  qkv_cols = (Hq+2Hkv)*128, T = rows of qkv.
 void prefill_attention_tc(const void* qkv, int ldq, int qkv_cols, int T, void* out, int ldo, const int* tile_info,
                           int n_tiles, int Hq, int Hkv, float scale, int* status, cudaStream_t s);
+// The same over a paged cache (chunked prefill): q rows from QKV; K/V of the
+// whole context from the caches [blocks, Hkv, 16, 128] (cache_rows =
+// blocks * Hkv * 16) through block_tables [B, bt_stride]; tile_info: [n_tiles,
+// 5] int32 of (seq start row, new tokens, first query, context length,
+// sequence index).
+void prefill_attention_paged_tc(const void* qkv, int ldq, int qkv_cols, int T, const void* kc, const void* vc,
+                                int64_t cache_rows, const int* block_tables, int bt_stride, void* out, int ldo,
+                                const int* tile_info, int n_tiles, int Hq, int Hkv, float scale, int* status,
+                                cudaStream_t s);
 
 // Paged decode attention.  q: [B, *] rows (ld ldq, q heads first).
 // Caches [blocks, Hkv, BS, 128]; block_tables [B, max_blocks]; ctx_lens [B].

@@ -190,15 +190,18 @@ def gather_rows(src: torch.Tensor, idx: torch.Tensor, out: Optional[torch.Tensor
 PREFILL_TILE = 128
 
 
-def prefill_tile_info(seq_lens, device) -> torch.Tensor:
-    """[n_tiles, 3] int32 (seq start row, seq length, first query of the 128-row tile)."""
+def prefill_tile_info(seq_lens, device, ctx=None) -> torch.Tensor:
+    """[n_tiles, 3] int32 (seq start row, seq length, first query of the 128-row tile);
+    with ``ctx`` (tokens already in the cache per sequence, chunked prefill)
+    [n_tiles, 5] adding (context length, sequence index) for the paged kernel."""
     rows = []
     start = 0
-    for n in seq_lens:
+    for i, n in enumerate(seq_lens):
         for q0 in range(0, n, PREFILL_TILE):
-            rows.append((start, n, q0))
+            rows.append((start, n, q0) if ctx is None else (start, n, q0, int(ctx[i]), i))
         start += n
-    t = torch.tensor(rows if rows else [(0, 0, 0)], dtype=torch.int32)
+    width = 3 if ctx is None else 5
+    t = torch.tensor(rows if rows else [(0,) * width], dtype=torch.int32)
     if not rows:
         return t[:0].to(device)
     return t.pin_memory().to(device, non_blocking=True) if torch.cuda.is_available() else t.to(device)
@@ -213,6 +216,24 @@ def prefill_attention(qkv: torch.Tensor, tile_info: torch.Tensor, n_q_heads: int
         out = torch.empty(qkv.shape[0], n_q_heads * 128, dtype=qkv.dtype, device=qkv.device)
     _C.prefill_attention(qkv, out, tile_info, n_q_heads, n_kv_heads,
                          scale if scale is not None else 1.0 / math.sqrt(128), status)
+    _n()
+    return out
+
+
+def prefill_attention_paged(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
+                            block_tables: torch.Tensor, tile_info: torch.Tensor, n_q_heads: int, n_kv_heads: int,
+                            out: Optional[torch.Tensor] = None, scale: Optional[float] = None,
+                            status: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """Causal prefill attention of chunks that continue cached sequences (the
+    tcgen05 kernel's paged variant): queries from ``qkv``, keys and values of
+    the whole context -- this chunk's included, already written to the cache
+    -- from ``k_cache`` / ``v_cache`` [blocks, Hkv, 16, 128] through
+    ``block_tables`` [B, max_blocks]; ``tile_info`` from
+    ``prefill_tile_info(n_new, device, ctx)``."""
+    if out is None:
+        out = torch.empty(qkv.shape[0], n_q_heads * 128, dtype=qkv.dtype, device=qkv.device)
+    _C.prefill_attention_paged(qkv, k_cache, v_cache, block_tables, out, tile_info, n_q_heads, n_kv_heads,
+                               scale if scale is not None else 1.0 / math.sqrt(128), status)
     _n()
     return out
 

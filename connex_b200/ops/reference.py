@@ -80,6 +80,34 @@ def paged_decode_attention(q, k_cache, v_cache, block_tables, ctx_lens, scale=No
     return out
 
 
+def paged_prefill_attention(q, k_cache, v_cache, block_tables, ctx, n_new, scale=None):
+    """Chunks that continue cached sequences: q [T, Hq, D] packed by sequence
+    (``n_new[i]`` rows each); K/V of positions [0, ctx[i] + n_new[i]) from the
+    caches [blocks, Hkv, BS, D] through ``block_tables``; query j of sequence
+    i sits at position ctx[i] + j -> [T, Hq, D] fp32."""
+    T, Hq, D = q.shape
+    Hkv, BS = k_cache.shape[1], k_cache.shape[2]
+    scale = scale if scale is not None else 1.0 / math.sqrt(D)
+    out = torch.empty(T, Hq, D, dtype=torch.float32, device=q.device)
+    s = 0
+    for b, (c, n) in enumerate(zip(ctx, n_new)):
+        tot = c + n
+        nb = (tot + BS - 1) // BS
+        blocks = block_tables[b, :nb].long()
+        k = k_cache[blocks].float().permute(1, 0, 2, 3).reshape(Hkv, nb * BS, D)[:, :tot]
+        v = v_cache[blocks].float().permute(1, 0, 2, 3).reshape(Hkv, nb * BS, D)[:, :tot]
+        k = k.repeat_interleave(Hq // Hkv, 0)
+        v = v.repeat_interleave(Hq // Hkv, 0)
+        qs = q[s:s + n].float().transpose(0, 1)                        # [Hq, n, D]
+        att = (qs @ k.transpose(1, 2)) * scale                         # [Hq, n, tot]
+        keys = torch.arange(tot, device=q.device)[None, :]
+        pos = (c + torch.arange(n, device=q.device))[:, None]
+        att = att.masked_fill(keys > pos, float("-inf")).softmax(-1)
+        out[s:s + n] = (att @ v).transpose(0, 1)
+        s += n
+    return out
+
+
 def kv_push(src_k, src_v, dst_k, dst_v, pairs, src_h0=0, dst_h0=0, n_heads=None):
     """In-place reference of kv_push_layer on plain tensors."""
     nh = n_heads if n_heads is not None else src_k.shape[1]

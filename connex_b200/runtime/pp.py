@@ -95,9 +95,15 @@ class StageModel(LlamaModel):
         ops.rmsnorm(self.x[:T], self.w.layers[0].attn_norm, self.cfg.eps, out=self.h[:T])
 
     def run(self, inp: torch.Tensor, positions, slots, *, prefill: bool, tile_info=None, block_tables=None,
-            ctx_lens=None, max_ctx: int = 0, workspace=None, rows=None, B: int = 0):
+            ctx_lens=None, max_ctx: int = 0, workspace=None, rows=None, B: int = 0, n_dec: Optional[int] = None):
         """Ids (first stage) or the residual stream in; the residual stream
-        (``x[:T]``) or, on the last stage, the greedy next ids of ``rows`` out."""
+        (``x[:T]``) or, on the last stage, the greedy next ids of ``rows`` out.
+
+        ``n_dec`` set: a mixed step -- the first ``n_dec`` rows are decode
+        rows (paged decode attention over ``block_tables[:n_dec]`` /
+        ``ctx_lens``), the rest are prefill chunks that continue cached
+        sequences (the paged prefill kernel over ``block_tables[n_dec:]`` and
+        ``tile_info`` of width 5); every GEMM runs once over all rows."""
         cfg, T = self.cfg, inp.shape[0]
         assert T <= self.max_tokens
         self._enter(inp, T)
@@ -106,7 +112,15 @@ class StageModel(LlamaModel):
             ops.gemm(self.h[:T], lw.wqkv, qkv, status=self.status)
             ops.rope_cache(qkv, positions, self.cos_sin, cfg.heads, cfg.kv_heads, slots, self.cache.k(i),
                            self.cache.v(i), status=self.status)
-            if prefill:
+            if n_dec is not None:
+                if n_dec:
+                    ops.decode_attention(qkv[:n_dec], self.cache.k(i), self.cache.v(i), block_tables[:n_dec],
+                                         ctx_lens, cfg.heads, max_ctx, workspace, out=self.attn[:n_dec])
+                if T > n_dec:
+                    ops.prefill_attention_paged(qkv[n_dec:], self.cache.k(i), self.cache.v(i), block_tables[n_dec:],
+                                                tile_info, cfg.heads, cfg.kv_heads, out=self.attn[n_dec:T],
+                                                status=self.status)
+            elif prefill:
                 ops.prefill_attention(qkv, tile_info, cfg.heads, cfg.kv_heads, out=self.attn[:T])
             else:
                 ops.decode_attention(qkv, self.cache.k(i), self.cache.v(i), block_tables, ctx_lens, cfg.heads,
@@ -295,7 +309,11 @@ class StageRuntime:
         rids = list(td[REQUEST_IDS])
         ctx = list(td[CX_CTX])
         n_new = list(td["n_new"])
-        prefill = td["kind"] == "prefill"
+        kind = td["kind"]
+        if kind == "prefill" and any(ctx):      # chunks that continue cached sequences
+            kind = "mixed"
+        n_dec = int(td.get("n_dec", 0)) if kind == "mixed" else None
+        prefill = kind == "prefill"
         miss = set(missing)
         pos, slots, lens = [], [], []
         for r, c, n in zip(rids, ctx, n_new):
@@ -309,20 +327,32 @@ class StageRuntime:
         dev = self.device
         B = len(rids)
         inp = td["ids"] if self.model.is_first else td["x"]
-        graph = not prefill and self.graphs is not None and B <= self.g_buckets[-1]
+        graph = kind == "decode" and self.graphs is not None and B <= self.g_buckets[-1]
         if not graph:
             positions = torch.tensor(pos, dtype=torch.int32).pin_memory().to(dev, non_blocking=True)
             slot_t = torch.tensor(slots, dtype=torch.int64).pin_memory().to(dev, non_blocking=True)
         kw = {}
+        last_rows, start = [], 0
+        for n in n_new:                 # each row's last token: its next id comes from there
+            start += n
+            last_rows.append(start - 1)
         if prefill:
-            rows, start, q0s = [], 0, []
-            for r, c, n in zip(rids, ctx, n_new):
-                if c:
-                    raise NotImplementedError("prefill continuation (chunked prefill) is not supported")
-                rows.append(start + n - 1)
-                start += n
             kw["tile_info"] = ops.prefill_tile_info(n_new, dev)
-            kw["rows"] = torch.tensor(rows, dtype=torch.int32, device=dev)
+            kw["rows"] = torch.tensor(last_rows, dtype=torch.int32, device=dev)
+        elif n_dec is not None:
+            if any(n != 1 for n in n_new[:n_dec]):
+                raise ValueError("a mixed step's decode rows carry one token each")
+            mb = -(-max(lens) // self.bs)
+            bt = torch.zeros(B, mb, dtype=torch.int32)
+            for i, r in enumerate(rids):
+                t = self.tables[r]
+                bt[i, :len(t)] = torch.tensor(t[:mb], dtype=torch.int32)
+            kw.update(n_dec=n_dec, block_tables=bt.pin_memory().to(dev, non_blocking=True),
+                      tile_info=ops.prefill_tile_info(n_new[n_dec:], dev, ctx=ctx[n_dec:]),
+                      rows=torch.tensor(last_rows, dtype=torch.int32).pin_memory().to(dev, non_blocking=True))
+            if n_dec:
+                kw.update(ctx_lens=torch.tensor(lens[:n_dec], dtype=torch.int32).pin_memory().to(dev, non_blocking=True),
+                          max_ctx=max(lens[:n_dec]), workspace=self.ws)
         elif graph:
             out = self._g_decode(inp, B, pos, slots, lens, [self.tables[r] for r in rids])
             kw = None
@@ -347,6 +377,8 @@ class StageRuntime:
                 self.held[r] = c + n
         self.steps += 1
         res = {"kind": td["kind"], "n_new": n_new}
+        if n_dec is not None:
+            res["n_dec"] = n_dec
         # a copy: the model's buffers are rewritten by the next step while the
         # link may still be sending this one
         res["next" if self.model.is_last else "x"] = out.clone()

@@ -2,11 +2,21 @@
 
 :class:`GenerationEngine` owns one thread that drives a *stepper* (the
 model): each iteration admits waiting requests that fit (batch slots, KV
-blocks reserved for prompt + ``max_tokens``, a per-step prefill token
-budget), prefills them together, then decodes every running request by one
-token, and hands each new token to the request's callback.  A request ends
-at ``max_tokens``, at a stop id, or when it is cancelled (client gone); its
-KV blocks are released at once.
+blocks reserved for prompt + ``max_tokens``), then runs one step and hands
+each new token to the request's callback.  A request ends at
+``max_tokens``, at a stop id, or when it is cancelled (client gone); its KV
+blocks are released at once.
+
+Chunked prefill (steppers with ``supports_mixed``): every step is one
+*mixed* batch -- a decode row (one token) for each request that is
+generating, plus prefill chunks of the prompts still being read, up to the
+step's token budget (``max_step_tokens``) in admission order.  A prompt
+longer than the budget is read over several steps while the others keep
+decoding (a 30k-token prompt no longer stalls every stream for its whole
+prefill); its first token comes from the step with its last chunk.  Every
+GEMM of a step runs once over all its rows.  Steppers without mixed steps
+get a prefill step for the admitted prompts (whole, within the budget) and a
+decode step per iteration.
 
 Steppers:
 
@@ -33,6 +43,8 @@ import time
 from dataclasses import dataclass, field
 from typing import Callable, Dict, List, Optional, Sequence
 
+from connex.pp.handover import CX_CTX, REQUEST_IDS
+
 log = logging.getLogger("connex_b200.serve")
 
 
@@ -51,8 +63,16 @@ class Stepper:
     num_blocks: int = 1 << 30
     block_size: int = 16
     vocab_size: int = 0
+    supports_mixed: bool = False
 
     def prefill(self, rids: List[str], seqs: List[List[int]]) -> List[int]:
+        raise NotImplementedError
+
+    def mixed(self, rids: List[str], seqs: List[List[int]], ctx: List[int], n_new: List[int]) -> List[int]:
+        """One step over rows that each add ``seq[ctx:ctx + n_new]`` to a
+        sequence whose first ``ctx`` ids are already in the KV cache (decode
+        rows and prefill chunks together); returns each row's greedy next id
+        (the one after ``seq[ctx + n_new - 1]``)."""
         raise NotImplementedError
 
     def decode(self, rids: List[str], seqs: List[List[int]]) -> List[int]:
@@ -93,6 +113,8 @@ class RuleStepper(Stepper):
             self.held[r] = len(s)
         return [self._next(s) for s in seqs]
 
+    supports_mixed = True
+
     def prefill(self, rids, seqs):
         return self._step("prefill", rids, seqs)
 
@@ -100,6 +122,15 @@ class RuleStepper(Stepper):
         for r, s in zip(rids, seqs):
             assert self.held.get(r) == len(s) - 1, f"{r}: KV holds {self.held.get(r)}, sequence {len(s)}"
         return self._step("decode", rids, seqs)
+
+    def mixed(self, rids, seqs, ctx, n_new):
+        for r, c in zip(rids, ctx):
+            assert self.held.get(r, 0) == c, f"{r}: KV holds {self.held.get(r)}, step continues at {c}"
+        # named like the runtime's step kinds: all one-token rows run as a
+        # decode step, fresh whole prompts as a prefill step
+        kind = ("decode" if all(n == 1 for n in n_new) else
+                "prefill" if not any(ctx) and all(n != 1 for n in n_new) else "mixed")
+        return self._step(kind, rids, [s[:c + n] for s, c, n in zip(seqs, ctx, n_new)])
 
     def release(self, rids):
         for r in rids:
@@ -146,7 +177,7 @@ class RuleStageRuntime:
         x = (td["ids"] if self.first else td["x"]).to(torch.int64).tolist()
         i, nxt = 0, []
         for r, c, n in zip(rids, ctx, n_new):
-            seq = [] if (td["kind"] == "prefill" or r in missing) else self.seqs.get(r, [])[:c]
+            seq = [] if (c == 0 or r in missing) else self.seqs.get(r, [])[:c]
             seq = seq + x[i:i + n]
             i += n
             if r not in missing:
@@ -154,6 +185,8 @@ class RuleStageRuntime:
             nxt.append(next_token(seq, self.vocab))
         self.steps += 1
         out = {"kind": td["kind"], "n_new": n_new}
+        if "n_dec" in td:
+            out["n_dec"] = td["n_dec"]
         if self.last:
             out["next"] = torch.tensor(nxt, dtype=torch.int64)
         else:
@@ -163,6 +196,40 @@ class RuleStageRuntime:
 
 class _RuntimeSteps(Stepper):
     """Step tensors for a :class:`connex_b200.runtime.pp.StageRuntime`."""
+
+    supports_mixed = True
+
+    def _td_rows(self, rids, seqs, ctx, n_new):
+        """A mixed step: one-token rows first (decode attention), chunks after
+        (the paged prefill kernel); pure decode / fresh prefill steps keep
+        their own kinds (decode graphs, the contiguous prefill kernel).
+        Returns (td, order) -- ``order[i]``: the caller's row at position i."""
+        import torch
+        from connex.pp.handover import CX_CTX, REQUEST_IDS
+        order = sorted(range(len(rids)), key=lambda i: n_new[i] != 1)
+        n_dec = sum(1 for n in n_new if n == 1)
+        if n_dec == len(rids):
+            kind = "decode"
+        elif n_dec == 0 and not any(ctx):
+            kind = "prefill"
+        else:
+            kind = "mixed"
+        ids = [t for i in order for t in seqs[i][ctx[i]:ctx[i] + n_new[i]]]
+        t = torch.tensor(ids, dtype=torch.int32)
+        if self.rt.device.type == "cuda":
+            t = t.pin_memory().to(self.rt.device, non_blocking=True)
+        td = {"kind": kind, REQUEST_IDS: [rids[i] for i in order], CX_CTX: [ctx[i] for i in order],
+              "n_new": [n_new[i] for i in order], "ids": t}
+        if kind == "mixed":
+            td["n_dec"] = n_dec
+        return td, order
+
+    @staticmethod
+    def _unorder(order, vals):
+        out = [0] * len(order)
+        for pos, i in enumerate(order):
+            out[i] = vals[pos]
+        return out
 
     def _td(self, kind, rids, seqs):
         import torch
@@ -226,6 +293,10 @@ class ModelStepper(_RuntimeSteps):
     def decode(self, rids, seqs):
         return self._run("decode", rids, seqs)
 
+    def mixed(self, rids, seqs, ctx, n_new):
+        td, order = self._td_rows(rids, seqs, ctx, n_new)
+        return self._unorder(order, self.rt.compute(td, [])["next"].tolist())
+
 
 class GroupStepError(RuntimeError):
     """A step failed on one rank of a tensor-parallel group.  The ranks no
@@ -252,7 +323,8 @@ class TPStepper(Stepper):
     def __init__(self, inner: Stepper, cpu_group=None, src: int = 0):
         self.inner, self.pg, self.src = inner, cpu_group, src
         self.broken: Optional[str] = None
-        for k in ("max_batch", "max_ctx", "max_step_tokens", "num_blocks", "block_size", "vocab_size"):
+        for k in ("max_batch", "max_ctx", "max_step_tokens", "num_blocks", "block_size", "vocab_size",
+                  "supports_mixed"):
             setattr(self, k, getattr(inner, k))
 
     def _send(self, msg) -> None:
@@ -275,12 +347,12 @@ class TPStepper(Stepper):
         _th.Thread(target=tell, name="cx-tp-abort", daemon=True).start()
         return GroupStepError(f"step failed on rank {self.src}; the tensor-parallel group stops: {self.broken}")
 
-    def _run(self, kind, rids, seqs):
+    def _run(self, kind, rids, seqs, *extra):
         if self.broken is not None:
             raise GroupStepError(f"tensor-parallel group is down: {self.broken}")
         try:
-            self._send((kind, list(rids), [list(x) for x in seqs]))
-            return getattr(self.inner, kind)(rids, seqs)
+            self._send((kind, list(rids), [list(x) for x in seqs]) + tuple(list(e) for e in extra))
+            return getattr(self.inner, kind)(rids, seqs, *extra)
         except Exception as e:  # noqa: BLE001 - any failure breaks collective matching
             raise self._fail(e) from e
 
@@ -289,6 +361,9 @@ class TPStepper(Stepper):
 
     def decode(self, rids, seqs):
         return self._run("decode", rids, seqs)
+
+    def mixed(self, rids, seqs, ctx, n_new):
+        return self._run("mixed", rids, seqs, ctx, n_new)
 
     def release(self, rids):
         if self.broken is not None:
@@ -328,7 +403,7 @@ def tp_follow(inner: Stepper, cpu_group=None, src: int = 0) -> int:
         if msg[0] == "release":
             inner.release(msg[1])
         else:
-            getattr(inner, msg[0])(msg[1], msg[2])
+            getattr(inner, msg[0])(*msg[1:])
             n += 1
 
 
@@ -376,29 +451,63 @@ class PipelineStepper(_RuntimeSteps):
         self.link = Stage0Link(endpoint, self.hooks, recv_timeout_s=recv_timeout_s)
         self.reprefills = 0
 
-    def _run(self, kind, rids, seqs):
-        td, ctx, n_new = self._td(kind, rids, seqs)
+    def _through(self, td, rids, ctx, n_new):
+        """This stage's layers, then the rest of the pipeline; the next ids."""
         x = self.rt.compute(td, [])["x"]
         self.hooks.reprefill_rids = []
-        out = self.link.step({"x": x, "kind": kind, "n_new": n_new}, request_ids=list(rids), num_computed=ctx)
-        nxt = out["next"].tolist()
+        step = {"x": x, "kind": td["kind"], "n_new": n_new}
+        if "n_dec" in td:
+            step["n_dec"] = td["n_dec"]
+        return self.link.step(step, request_ids=list(rids), num_computed=ctx)["next"].tolist()
+
+    def _repair(self, rids, seqs, upto, nxt):
+        """Rows whose KV the new downstream replica lacks: read their
+        sequences up to ``upto`` again through the whole pipeline (in chunks
+        of the step budget); the last position's id replaces this step's."""
         again = list(self.hooks.reprefill_rids)
-        if again:
-            # the new downstream replica holds no KV for these rows: prefill
-            # prompt + generated tokens through the whole pipeline; its last
-            # position is this step's token, so the result replaces it
-            self.reprefills += len(again)
-            idx = [list(rids).index(r) for r in again]
-            fixed = self._run("prefill", again, [seqs[i] for i in idx])
-            for j, i in enumerate(idx):
-                nxt[i] = fixed[j]
-        return nxt
+        if not again:
+            return nxt
+        self.reprefills += len(again)
+        idx = [list(rids).index(r) for r in again]
+        self.rt.release(again)
+        done = [0] * len(idx)
+        while True:
+            rows = [j for j, i in enumerate(idx) if done[j] < upto[i]]
+            if not rows:
+                return nxt
+            budget, take = self.max_step_tokens, []
+            for j in rows:
+                n = min(upto[idx[j]] - done[j], budget)
+                if n <= 0:
+                    break
+                take.append((j, n))
+                budget -= n
+            sub_r = [again[j] for j, _ in take]
+            sub_s = [seqs[idx[j]] for j, _ in take]
+            sub_c = [done[j] for j, _ in take]
+            sub_n = [n for _, n in take]
+            td, order = self._td_rows(sub_r, sub_s, sub_c, sub_n)
+            got = self._unorder(order, self._through(td, td[REQUEST_IDS], td[CX_CTX], td["n_new"]))
+            for (j, n), tok in zip(take, got):
+                done[j] += n
+                if done[j] == upto[idx[j]]:
+                    nxt[idx[j]] = tok
+
+    def _run(self, kind, rids, seqs):
+        td, ctx, n_new = self._td(kind, rids, seqs)
+        nxt = self._through(td, rids, ctx, n_new)
+        return self._repair(rids, seqs, [len(s) for s in seqs], nxt)
 
     def prefill(self, rids, seqs):
         return self._run("prefill", rids, seqs)
 
     def decode(self, rids, seqs):
         return self._run("decode", rids, seqs)
+
+    def mixed(self, rids, seqs, ctx, n_new):
+        td, order = self._td_rows(rids, seqs, ctx, n_new)
+        nxt = self._unorder(order, self._through(td, td[REQUEST_IDS], td[CX_CTX], td["n_new"]))
+        return self._repair(rids, seqs, [c + n for c, n in zip(ctx, n_new)], nxt)
 
     def release(self, rids):
         self.rt.release(list(rids))
@@ -416,6 +525,7 @@ class Request:
     on_token: Callable[["Request", Optional[int], Optional[str]], None]
     stop_ids: frozenset = frozenset()
     gen: List[int] = field(default_factory=list)
+    done: int = 0                  # prompt tokens already in the KV cache (chunked prefill)
     blocks: int = 0
     cancelled: bool = False
     finish_reason: Optional[str] = None
@@ -437,10 +547,11 @@ class GenerationEngine:
     request ends without one."""
 
     def __init__(self, stepper: Stepper, max_batch: Optional[int] = None, max_step_tokens: Optional[int] = None,
-                 idle_wait_s: float = 0.05):
+                 idle_wait_s: float = 0.05, chunked: Optional[bool] = None):
         self.s = stepper
         self.max_batch = max_batch or stepper.max_batch
         self.max_step_tokens = max_step_tokens or stepper.max_step_tokens
+        self.chunked = bool(getattr(stepper, "supports_mixed", False)) if chunked is None else chunked
         self.idle_wait_s = idle_wait_s
         self.waiting: "collections.deque[Request]" = collections.deque()
         self.running: Dict[str, Request] = {}
@@ -468,7 +579,7 @@ class GenerationEngine:
         if len(prompt) + max_tokens > self.s.max_ctx:
             raise EngineFull(f"prompt ({len(prompt)}) + max_tokens ({max_tokens}) exceeds the context "
                              f"({self.s.max_ctx})")
-        if len(prompt) > self.max_step_tokens:
+        if len(prompt) > self.max_step_tokens and not self.chunked:
             raise EngineFull(f"prompt ({len(prompt)}) exceeds the prefill budget ({self.max_step_tokens})")
         if self.s.vocab_size and any(not 0 <= t < self.s.vocab_size for t in prompt):
             raise ValueError(f"token ids must lie in [0, {self.s.vocab_size})")
@@ -537,7 +648,7 @@ class GenerationEngine:
                     continue
                 if len(self.running) + len(new) >= self.max_batch:
                     break
-                if new and tokens + len(r.prompt) > self.max_step_tokens:
+                if not self.chunked and new and tokens + len(r.prompt) > self.max_step_tokens:
                     break
                 if self.blocks_reserved + r.blocks > self.s.num_blocks:
                     break
@@ -587,6 +698,44 @@ class GenerationEngine:
         self.stats[kind + "_steps"] += 1
         self._emit(reqs, toks)
 
+    def _step_mixed(self) -> None:
+        """One mixed step: a decode row per generating request, then prefill
+        chunks of the prompts still being read, in admission order, within
+        the step's token budget."""
+        decode = [r for r in self.running.values() if r.done == len(r.prompt)]
+        budget = max(0, self.max_step_tokens - len(decode))
+        chunks = []
+        for r in self.running.values():
+            if r.done < len(r.prompt) and budget > 0:
+                n = min(len(r.prompt) - r.done, budget)
+                chunks.append((r, n))
+                budget -= n
+        reqs = decode + [r for r, _ in chunks]
+        if not reqs:
+            return
+        seqs = [r.prompt + r.gen for r in decode] + [r.prompt for r, _ in chunks]
+        ctx = [len(s) - 1 for s in seqs[:len(decode)]] + [r.done for r, _ in chunks]
+        n_new = [1] * len(decode) + [n for _, n in chunks]
+        try:
+            toks = self.s.mixed([r.rid for r in reqs], seqs, ctx, n_new)
+        except GroupStepError:
+            raise
+        except Exception as e:  # noqa: BLE001 - fail the step's requests, keep serving
+            log.exception("mixed step of %d rows failed", len(reqs))
+            self.stats["step_errors"] += 1
+            for r in reqs:
+                r.error = f"{type(e).__name__}: {e}"
+            self._finish(reqs, "error", token_sent=False)
+            return
+        self.stats["mixed_steps"] += 1
+        self.stats["chunks"] += len(chunks)
+        first = []
+        for (r, n), tok in zip(chunks, toks[len(decode):]):
+            r.done += n
+            if r.done == len(r.prompt):
+                first.append((r, tok))       # its last chunk: the first generated token
+        self._emit(decode + [r for r, _ in first], toks[:len(decode)] + [t for _, t in first])
+
     def _loop(self) -> None:
         try:
             while not self._stop.is_set():
@@ -598,6 +747,11 @@ class GenerationEngine:
                     with self._cv:
                         if not self.waiting and not self._stop.is_set():
                             self._cv.wait(self.idle_wait_s)
+                    continue
+                if self.chunked:
+                    for r in new:
+                        self.running[r.rid] = r
+                    self._step_mixed()
                     continue
                 decoding = list(self.running.values())
                 if new:

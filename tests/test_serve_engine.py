@@ -37,7 +37,7 @@ def _collect(engine, prompt, n, **kw):
 
 def test_batching_matches_the_uninterrupted_rule_and_admits_between_steps():
     st = RuleStepper(step_delay_s=0.002)
-    eng = GenerationEngine(st).start()
+    eng = GenerationEngine(st, chunked=False).start()        # separate prefill and decode steps
     try:
         a = _collect(eng, [1, 5, 6], 60)
         assert wait_until(lambda: len(a["toks"]) >= 2, 5)
@@ -51,6 +51,54 @@ def test_batching_matches_the_uninterrupted_rule_and_admits_between_steps():
         mixed = [rids for k, rids in st.calls if k == "decode" and len(rids) == 2]
         assert mixed                                    # a and b decoded in the same step
         assert wait_until(lambda: not st.held and eng.blocks_reserved == 0, 5)
+    finally:
+        eng.stop()
+
+
+def test_chunked_prefill_reads_long_prompts_while_others_decode():
+    st = RuleStepper(step_delay_s=0.001)
+    eng = GenerationEngine(st, max_step_tokens=64).start()
+    try:
+        a = _collect(eng, [1, 5, 6], 40)
+        assert wait_until(lambda: len(a["toks"]) >= 2, 5)
+        long = [1] + [(7 * i) % 900 + 3 for i in range(299)]  # 300 tokens: five chunks of <= 64
+        b = _collect(eng, long, 6)
+        for x in (a, b):
+            assert x["done"].wait(10)
+        assert a["toks"] == reference([1, 5, 6], 40)[0]
+        assert b["toks"] == reference(long, 6)[0]                 # the same as one whole prefill
+        steps = [(k, rids) for k, rids in st.calls]
+        with_b = [i for i, (k, rids) in enumerate(steps) if b["req"].rid in rids]
+        chunk_steps = with_b[:5]
+        assert all(steps[i][0] == "mixed" and a["req"].rid in steps[i][1] for i in chunk_steps[:4])
+        assert eng.stats["chunks"] >= 5 and b["req"].t_first is not None
+        # a kept decoding: one token per step while b's prompt was read
+        assert all(a["req"].rid in steps[i][1] for i in chunk_steps[:4])
+        assert wait_until(lambda: not st.held and eng.blocks_reserved == 0, 5)
+        # the budget is shared: two long prompts never exceed it in one step
+        st.calls.clear()
+        c, d = _collect(eng, long, 3), _collect(eng, long[::-1], 3)
+        for x in (c, d):
+            assert x["done"].wait(10)
+        assert c["toks"] == reference(long, 3)[0] and d["toks"] == reference(long[::-1], 3)[0]
+    finally:
+        eng.stop()
+
+
+def test_chunked_steps_never_exceed_the_budget():
+    seen = []
+
+    class Spy(RuleStepper):
+        def mixed(self, rids, seqs, ctx, n_new):
+            seen.append(sum(n_new))
+            return super().mixed(rids, seqs, ctx, n_new)
+    st = Spy(step_delay_s=0.0005)
+    eng = GenerationEngine(st, max_step_tokens=50).start()
+    try:
+        outs = [_collect(eng, [1] + [3 + k % 7] * (30 + 17 * k), 5) for k in range(6)]
+        for o in outs:
+            assert o["done"].wait(10)
+        assert max(seen) <= 50 and len(seen) > 6
     finally:
         eng.stop()
 
