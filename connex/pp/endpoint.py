@@ -663,8 +663,8 @@ class PipelineEndpoint:
 
     # --------------------------------------------------------- stage-0 API
     def new_step_id(self) -> int:
-        c = self.ids.next()
-        with self._cv:
+        with self._cv:                   # several threads may start steps (K > 1)
+            c = self.ids.next()
             self._outstanding.add(c)
         return c
 

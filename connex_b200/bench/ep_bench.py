@@ -6,9 +6,17 @@ logits ~ N(0, 1) plus a Zipf(1.2) popularity bias over experts (seeded),
 T tokens per rank.  Measures one full MoE layer (dispatch + expert GEMMs +
 combine) per step:
 
-* ``cx``   -- this package's five kernels over NVLink peer memory (no NCCL),
-* ``nccl`` -- ``all_to_all_single`` of counts, tokens and results (NCCL) with
-  per-expert torch matmuls, the conventional EP implementation.
+* ``cx``   -- this package's five kernels over NVLink peer memory (no NCCL);
+  the per-phase split (count, dispatch, gate/up, down + combine stores,
+  combine) comes from CUDA events between the phases on the rank's stream
+  (each phase's time includes its wait for the peers);
+* ``nccl`` -- the conventional EP layer on NCCL, without host syncs in the
+  expert math: per-(rank, expert) counts by ``all_to_all_single``, one host
+  read of the split sizes (``all_to_all_single`` with uneven splits needs
+  them), tokens sorted by expert and sent with one ``all_to_all_single``,
+  the experts as two grouped GEMMs (``torch._grouped_mm`` over per-expert
+  offsets on the device), one ``all_to_all_single`` back and a weighted
+  ``index_add`` combine.
 
 Device time by CUDA events around ``iters`` steps after warm-up, max over
 ranks.  Both paths are checked against each other before timing.
@@ -51,8 +59,83 @@ def make_weights(S: int, rank: int, device):
     return w13, w2
 
 
+_GROUPED_MM: Optional[bool] = None
+
+
+def _grouped_mm_ok(device) -> bool:
+    """Whether ``torch._grouped_mm`` runs here (bf16, jagged M, 3-D weights)."""
+    global _GROUPED_MM
+    if _GROUPED_MM is None:
+        try:
+            a = torch.randn(64, 256, device=device).bfloat16()
+            b = torch.randn(2, 128, 256, device=device).bfloat16()
+            offs = torch.tensor([16, 64], dtype=torch.int32, device=device)
+            out = torch._grouped_mm(a, b.transpose(1, 2), offs=offs)
+            ref = torch.cat([a[:16].float() @ b[0].float().t(), a[16:].float() @ b[1].float().t()])
+            _GROUPED_MM = bool((out.float() - ref).abs().max() < 0.5)
+        except (AttributeError, RuntimeError, TypeError):
+            _GROUPED_MM = False
+    return _GROUPED_MM
+
+
+def _swiglu(gu: torch.Tensor) -> torch.Tensor:
+    """gate/up interleaved per 128 rows of the fused weight -> SiLU(g) * u."""
+    v = gu.view(-1, 2 * FFN // 256, 2, 128)
+    return F.silu(v[:, :, 0].reshape(-1, FFN)) * v[:, :, 1].reshape(-1, FFN)
+
+
+def a2a_moe(x, idx, w, w13, w2, N: int, S: int, group=None):
+    """Fair baseline: the conventional NCCL EP layer with grouped expert GEMMs
+    and one host read (the split sizes) per layer."""
+    T, K = idx.shape
+    H_ = x.shape[1]
+    flat = idx.flatten().long()                        # global expert = dst * S + local expert
+    order = torch.argsort(flat, stable=True)           # by destination rank, then local expert
+    send_ec = torch.bincount(flat, minlength=N * S).view(N, S)
+    recv_ec = torch.empty_like(send_ec)                # [src, local expert]: rows arriving here
+    if N > 1:
+        dist.all_to_all_single(recv_ec, send_ec, group=group)
+    else:
+        recv_ec.copy_(send_ec)
+    sizes = torch.cat([send_ec.sum(1), recv_ec.sum(1), recv_ec.sum(0)]).cpu()   # the one host sync
+    sc, rc, per_e = sizes[:N].tolist(), sizes[N:2 * N].tolist(), sizes[2 * N:]
+    R = sum(rc)
+    send_x = x[order // K]
+    recv_x = torch.empty(R, H_, dtype=x.dtype, device=x.device)
+    if N > 1:
+        dist.all_to_all_single(recv_x, send_x, rc, sc, group=group)
+    else:
+        recv_x.copy_(send_x)
+    # rows arrive by source, each source's rows by local expert: regroup by expert
+    e_of_row = torch.repeat_interleave(torch.arange(S, device=x.device).repeat(N), recv_ec.flatten(), output_size=R)
+    perm = torch.argsort(e_of_row, stable=True)
+    xe = recv_x[perm]
+    if _grouped_mm_ok(x.device):
+        offs = torch.cumsum(recv_ec.sum(0), 0).to(torch.int32)
+        h = _swiglu(torch._grouped_mm(xe, w13.transpose(1, 2), offs=offs))
+        ye = torch._grouped_mm(h, w2.transpose(1, 2), offs=offs)
+    else:                                              # per-expert matmuls on host offsets (no further sync)
+        ye = torch.empty_like(xe)
+        start = 0
+        for e, n in enumerate(per_e.tolist()):
+            if n:
+                ye[start:start + n] = _swiglu(xe[start:start + n] @ w13[e].t()) @ w2[e].t()
+            start += n
+    out = torch.empty_like(ye)
+    out[perm] = ye
+    back = torch.empty_like(send_x)
+    if N > 1:
+        dist.all_to_all_single(back, out, sc, rc, group=group)
+    else:
+        back.copy_(out)
+    y = torch.zeros(T, H_, dtype=torch.float32, device=x.device)
+    y.index_add_(0, order // K, back.float() * w.flatten()[order][:, None])
+    return y.to(x.dtype)
+
+
 def nccl_moe(x, idx, w, w13, w2, N: int, S: int, group=None):
-    """Baseline: NCCL all_to_all_single dispatch/combine + torch matmuls."""
+    """The naive per-expert loop (host syncs per expert); kept as a reference
+    implementation for tests, not as the timed baseline."""
     T, K = idx.shape
     flat = idx.flatten().long()
     dst = flat // S
@@ -123,6 +206,30 @@ class FusedEP:
         self.mapper.close()
 
 
+PHASES = ("count", "dispatch", "gate_up", "down", "combine")
+
+
+def _phase_times(fused: "FusedEP", x, idx, w, out, iters: int, warmup: int, barrier) -> Dict[str, float]:
+    """Mean device time of each phase of the fused layer (events between the
+    phases on this rank's stream; a phase's time includes its peer waits)."""
+    L, T = fused.layer, x.shape[0]
+    steps = [lambda: L.phase_count(idx, fused.l2p, fused.cnt), lambda: L.phase_dispatch(x, w), L.phase_gate_up,
+             L.phase_down, lambda: L.phase_combine(T, out)]
+    for _ in range(warmup):
+        for f in steps:
+            f()
+    barrier()
+    torch.cuda.synchronize()
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(steps) + 1)] for _ in range(iters)]
+    for it in range(iters):
+        ev[it][0].record()
+        for k, f in enumerate(steps):
+            f()
+            ev[it][k + 1].record()
+    torch.cuda.synchronize()
+    return {name: 1000.0 * sum(e[k].elapsed_time(e[k + 1]) for e in ev) / iters for k, name in enumerate(PHASES)}
+
+
 def _time(fn, iters: int, warmup: int, barrier) -> float:
     for _ in range(warmup):
         fn()
@@ -153,12 +260,16 @@ def run_ep_bench(world: int, rank: int, device, cpu_group=None, nccl_group=None,
         ops.check_status(fused.bufs.status, "ep")
         err = (y_cx.float() - y_ref.float()).abs().max().item()
         scale = y_ref.float().abs().max().item() + 1e-6
+        y_a2a = a2a_moe(x, idx, w, fused.w13, fused.w2, world, E // world, nccl_group)
+        err_a2a = (y_a2a.float() - y_ref.float()).abs().max().item()
         out = torch.empty_like(x)
         t_cx = _time(lambda: fused.forward(x, idx, w, out), iters, warmup, barrier)
-        t_nccl = _time(lambda: nccl_moe(x, idx, w, fused.w13, fused.w2, world, E // world, nccl_group),
+        phases = _phase_times(fused, x, idx, w, out, iters, warmup, barrier)
+        t_nccl = _time(lambda: a2a_moe(x, idx, w, fused.w13, fused.w2, world, E // world, nccl_group),
                        iters, warmup, barrier)
         ops.check_status(fused.bufs.status, "ep")
-        res[T] = {"cx_us": t_cx, "nccl_us": t_nccl, "max_err": err, "scale": scale}
+        res[T] = {"cx_us": t_cx, "nccl_us": t_nccl, "max_err": max(err, err_a2a), "scale": scale,
+                  **{f"phase_{k}_us": v for k, v in phases.items()}}
     if failover and world > 1:
         res["failover_ms"] = ep_failover_ms(fused, world, rank, device, barrier, x, idx, w)
     fused.close()
@@ -193,7 +304,8 @@ def ep_failover_ms(fused: "FusedEP", world: int, rank: int, device, barrier, x, 
 def reduce_max(per_rank: List[Dict]) -> Dict:
     out = {}
     for T in [k for k in per_rank[0] if k != "failover_ms"]:
-        out[str(T)] = {k: max(r[T][k] for r in per_rank) for k in ("cx_us", "nccl_us", "max_err", "scale")}
+        keys = ("cx_us", "nccl_us", "max_err", "scale") + tuple(f"phase_{p}_us" for p in PHASES)
+        out[str(T)] = {k: max(r[T][k] for r in per_rank) for k in keys if k in per_rank[0][T]}
         out[str(T)]["speedup_vs_nccl"] = round(out[str(T)]["nccl_us"] / out[str(T)]["cx_us"], 2)
         out[str(T)] = {k: (float(f"{v:.4g}") if isinstance(v, float) else v) for k, v in out[str(T)].items()}
     return out

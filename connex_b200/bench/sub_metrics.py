@@ -4,8 +4,9 @@ trainer weights -> bf16 engine layout on every other GPU) against an NCCL
 broadcast (and, N >= 4, from two FSDP trainer shards on ranks 0-1 to the
 other GPUs, against NCCL broadcasts of the cast shards), the fused EP MoE
 layer latency (dispatch + expert GEMMs +
-combine, Qwen3-30B-A3B layer geometry, 128 tokens per rank) against the
-NCCL all-to-all baseline, and (N > 1) the EP failover time: the last rank
+combine, Qwen3-30B-A3B layer geometry, 128 tokens per rank) with its
+per-phase split, against the NCCL all-to-all baseline with grouped expert
+GEMMs, and (N > 1) the EP failover time: the last rank
 leaves, the others route around it and finish their next forward (host
 clock of the box).  The rest are device-timed, max over ranks.  Every rank
 must call :func:`run_sub_metrics` (it is collective when N > 1).
@@ -41,6 +42,8 @@ def run_sub_metrics(world: int, rank: int, dev, layers: int = 32) -> Optional[di
         return None
     e = reduce_max(allr)["128"]
     out = {"ep_layer_us_t128": e["cx_us"], "ep_layer_us_t128_nccl_baseline": e["nccl_us"],
+           "ep_layer_phases_us_t128": {p: e.get(f"phase_{p}_us") for p in ("count", "dispatch", "gate_up", "down",
+                                                                           "combine")},
            "weight_sync_bytes": ws["engine_bytes"]}
     if world > 1:
         out["ep_failover_ms"] = round(max(r.get("failover_ms", 0.0) for r in allr), 2)

@@ -181,11 +181,104 @@ def run_sharded(cfg: LlamaConfig, trainers: int = 2, iters: int = 3, warmup: int
     return out
 
 
+def probe(cfg: LlamaConfig, iters: int = 3, warmup: int = 2) -> Dict:
+    """Where a broadcast's time goes at this N (bf16 engine-layout source, so
+    no cast): ``mc_copy`` multicast from rank 0 to everyone; ``scatter``
+    rank 0 unicasts slice j of the arena to receiver j only (the sender's
+    egress is the model once); ``fwd_mc`` / ``fwd_p2p`` every receiver sends
+    its slice to all others through the multicast address / with unicast
+    peer stores (the all-gather half).  Device time, max over ranks."""
+    from connex_b200 import ops
+    world, rank = dist.get_world_size(), dist.get_rank()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    m = engine_manifest(cfg)
+    bc = WeightBroadcast(cfg, mode="multicast")
+    total = m.total
+    recv = list(range(1, world))
+    R = len(recv)
+    sl = -(-total // (R * 16)) * 16                    # slice bytes (16-byte aligned)
+    named = {e.name: torch.randn(e.shape, device=dev).to(torch.bfloat16) for e in m.entries} if rank == 0 else None
+    out: Dict = {"engine_bytes": total, "receivers": R, "slice_bytes": sl}
+    n_tasks = [plan_jobs(cfg, m, named)[1] if rank == 0 else None]
+    dist.broadcast_object_list(n_tasks, src=0)
+    for _ in range(warmup):
+        bc.sync(named, n_tasks[0])
+    out["mc_copy_ms"] = _time(lambda: bc.sync(named, n_tasks[0]), iters, world)
+    torch.cuda.synchronize()
+    bc.check()
+    jobs = plan_jobs(cfg, m, named)[0] if rank == 0 else None
+    jobs_dev = jobs.to(dev) if jobs is not None else None
+    state = {"target": bc.received}
+
+    def scatter():
+        dist.barrier()
+        ctas = 0
+        if rank == 0:
+            ctas = ops._C.wsync(jobs_dev, jobs, total, [bc.peers[r] for r in recv],
+                                [bc.peers[r] + total for r in recv], 0, 0, 0, sl)
+        box = torch.tensor([ctas], device=dev)
+        dist.broadcast(box, src=0)
+        state["target"] += int(box.item())
+        if rank != 0:
+            ops.wait_flag(bc.flag_addr, state["target"] & 0xFFFFFFFF, bc.status, 10.0)
+    for _ in range(warmup):
+        scatter()
+    out["scatter_ms"] = _time(scatter, iters, world)
+
+    def my_slice_jobs():
+        j = recv.index(rank)
+        a, b = j * sl, min(total, (j + 1) * sl)
+        cols = 4096                                    # 8 KB rows; the tail row separately
+        full = (b - a) // (2 * cols)
+        rows_ = []
+        if full:
+            rows_.append([bc.arena.data_ptr() + a, a, full, cols, cols, cols, full, 0, 0, 0, 0, full])
+        tail = (b - a) - full * 2 * cols
+        if tail:
+            t0 = a + full * 2 * cols
+            rows_.append([bc.arena.data_ptr() + t0, t0, 1, tail // 2, tail // 2, tail // 2, 1, 0, 0, 0,
+                          1 if full else 0, 1])
+        for r_ in rows_:                               # one task per 64 KB of output
+            r_[11] = max(1, min(r_[2], (64 << 10) // (2 * r_[3])))
+        t = 0
+        for r_ in rows_:
+            r_[10] = t
+            t += -(-r_[2] // r_[11])
+        return torch.tensor(rows_, dtype=torch.int64)
+    if rank != 0:
+        sj = my_slice_jobs()
+        sj_dev = sj.to(dev)
+        j = recv.index(rank)
+        a, b = j * sl, min(total, (j + 1) * sl)
+        segs = torch.tensor([[bc.arena.data_ptr() + a, bc.peers[r] + a, b - a] for r in recv if r != rank],
+                            dtype=torch.int64, device=dev)
+
+    def fwd_mc():
+        dist.barrier()
+        if rank != 0:
+            ops._C.wsync(sj_dev, sj, total, [], [], bc.mc, 0, 0, 0)
+    def fwd_p2p():
+        dist.barrier()
+        if rank != 0 and segs.shape[0]:
+            ops.copy_segments(segs, int(segs[:, 2].sum().item()), status=bc.status)
+    for name, fn in (("fwd_mc_ms", fwd_mc), ("fwd_p2p_ms", fwd_p2p)):
+        if name == "fwd_mc_ms" and not bc.mc:
+            continue
+        for _ in range(warmup):
+            fn()
+        out[name] = _time(fn, iters, world)
+    torch.cuda.synchronize()
+    bc.check()
+    bc.close()
+    return out
+
+
 def main() -> None:
     import argparse
     p = argparse.ArgumentParser()
     p.add_argument("--iters", type=int, default=5)
     p.add_argument("--layers", type=int, default=32)
+    p.add_argument("--probe", action="store_true", help="time multicast / scatter / all-gather halves instead")
     a = p.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
@@ -193,6 +286,13 @@ def main() -> None:
     if world > 1:
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
     cfg = LlamaConfig(layers=a.layers)
+    if a.probe:
+        res = probe(cfg, a.iters)
+        if dist.get_rank() == 0:
+            print(json.dumps({"wsync_probe": res, "n_gpus": world}), flush=True)
+        dist.barrier()
+        dist.destroy_process_group()
+        return
     res = run(cfg, a.iters)
     if (dist.get_rank() if world > 1 else 0) == 0:
         gb = res["engine_bytes"] / 1e9

@@ -323,7 +323,20 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
         uint8_t* dst = prow + ((((uint32_t)c) ^ swz) << 4);
         *reinterpret_cast<uint4*>(dst) = make_uint4(pk[4 * c], pk[4 * c + 1], pk[4 * c + 2], pk[4 * c + 3]);
       }
-      fence_proxy_async_smem();  // P stores -> visible to the tensor core
+      if (PAGED && j == nkv - 1 && total - j * BN < BN) {
+        // the last tile's keys past the sequence end are cache slots nobody
+        // wrote: their P is 0, but 0 x NaN would still poison O -- zero those
+        // V rows (whole 128-byte rows, so the swizzle does not matter)
+        if (!mbar_wait(&v_full[s], (j >> 1) & 1, status)) { ok = false; break; }
+        uint8_t* vb = smem + OFF_V + s * KV_TILE;
+        const int tail = total - j * BN, nz = (BN - tail) * 8;   // 16-byte chunks per half
+        for (int t = (int)threadIdx.x - 64; t < 2 * nz; t += 128) {
+          const int half = t / nz, rem = t - half * nz;
+          *reinterpret_cast<uint4*>(vb + half * KV_HALF + (tail + rem / 8) * 128 + (rem % 8) * 16) =
+              make_uint4(0u, 0u, 0u, 0u);
+        }
+      }
+      fence_proxy_async_smem();  // P (and zeroed V) stores -> visible to the tensor core
       tc_fence_before();
       mbar_arrive(p_full);
     }

@@ -238,7 +238,7 @@ int64_t copy_segments(const at::Tensor& segs, int64_t total_bytes, int64_t ready
 // (validated here); destinations are a multicast address or up to
 // WS_MAX_DST plain bases (with optional flag words).
 int64_t wsync(const at::Tensor& jobs_dev, const at::Tensor& jobs_cpu, int64_t dst_bytes, std::vector<int64_t> bases,
-              std::vector<int64_t> flags, int64_t mc_base, int64_t mc_flag, int64_t max_ctas) {
+              std::vector<int64_t> flags, int64_t mc_base, int64_t mc_flag, int64_t max_ctas, int64_t scatter_bytes) {
   TORCH_CHECK(jobs_dev.is_cuda() && jobs_dev.scalar_type() == at::kLong && jobs_dev.is_contiguous() &&
                   jobs_dev.dim() == 2 && jobs_dev.size(1) == cx::WS_JOB_COLS,
               "jobs_dev must be contiguous int64 CUDA [n, ", cx::WS_JOB_COLS, "]");
@@ -250,7 +250,7 @@ int64_t wsync(const at::Tensor& jobs_dev, const at::Tensor& jobs_cpu, int64_t ds
   return cx::wsync(jobs_dev.data_ptr<int64_t>(), jobs_cpu.data_ptr<int64_t>(), (int)jobs_dev.size(0), dst_bytes,
                    reinterpret_cast<const uint64_t*>(bases.data()),
                    flags.empty() ? nullptr : reinterpret_cast<const uint64_t*>(flags.data()), (int)bases.size(),
-                   (uint64_t)mc_base, (uint64_t)mc_flag, (int)max_ctas, cur_stream(jobs_dev));
+                   (uint64_t)mc_base, (uint64_t)mc_flag, (int)max_ctas, scatter_bytes, cur_stream(jobs_dev));
 }
 
 void chan_copy(std::vector<int64_t> src, std::vector<int64_t> dst, std::vector<int64_t> bytes, int64_t wait_on,
@@ -421,7 +421,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("kv_push_layer", &kv_push_layer);
   m.def("gemm_splits", &gemm_splits);
   m.def("copy_segments", &copy_segments);
-  m.def("wsync", &wsync);
+  m.def("wsync", &wsync, py::arg("jobs_dev"), py::arg("jobs_cpu"), py::arg("dst_bytes"), py::arg("bases"),
+        py::arg("flags"), py::arg("mc_base"), py::arg("mc_flag"), py::arg("max_ctas"), py::arg("scatter_bytes") = 0);
   m.attr("WS_JOB_COLS") = cx::WS_JOB_COLS;
   m.attr("WS_MAX_DST") = cx::WS_MAX_DST;
   m.def("chan_copy", &chan_copy, py::arg("src"), py::arg("dst"), py::arg("bytes"), py::arg("wait_on"),

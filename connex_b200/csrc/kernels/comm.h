@@ -24,7 +24,7 @@ int copy_segments(const int64_t* segs, int n, int64_t total_bytes, uint32_t* rea
 constexpr int WS_JOB_COLS = 12;
 constexpr int WS_MAX_DST = 8;
 int wsync(const int64_t* jobs_dev, const int64_t* jobs_host, int n_jobs, int64_t dst_bytes, const uint64_t* dst_bases,
-          const uint64_t* dst_flags, int n_dst, uint64_t mc_base, uint64_t mc_flag, int max_ctas, cudaStream_t s);
+          const uint64_t* dst_flags, int n_dst, uint64_t mc_base, uint64_t mc_flag, int max_ctas, int64_t scatter_bytes, cudaStream_t s);
 
 // P2P channel copy (chan.cu): wait, copy up to CH_MAX_SEGS segments, signal
 // (mode 1: +1 per CTA on `signal`; mode 2: the last CTA stores `value`).

@@ -7,7 +7,11 @@
 //     trainer's egress is the model size once, whatever the receiver count),
 //   * or to each of up to WS_MAX_DST destination bases with plain stores
 //     (peer-push fallback, or a local fused cast+re-layout copy when the
-//     source is another GPU's buffer mapped through CUDA IPC).
+//     source is another GPU's buffer mapped through CUDA IPC),
+//   * or, scattered, each 16 bytes to ONE destination chosen by its arena
+//     offset (destination p owns [p * scatter_bytes, (p + 1) * scatter_bytes)):
+//     the first half of a scatter + all-gather broadcast, whose sender
+//     egress is the model size once without multicast.
 // When every CTA is done it releases (system scope) +1 on the receivers'
 // flag words -- through the multicast address, or on each destination -- so a
 // receiver's stream waits on that flag instead of a host barrier.
@@ -33,6 +37,7 @@ struct WsDst {
   int n;
   uint64_t mc_base;  // nonzero: multicast destination (base[] unused)
   uint64_t mc_flag;
+  int64_t scatter;   // nonzero: each store goes to base[offset / scatter] only
 };
 
 __device__ __forceinline__ void multimem_st_v4(uint64_t addr, const u128& v) {
@@ -97,6 +102,10 @@ __global__ void __launch_bounds__(WS_THREADS) wsync_kernel(const int64_t* __rest
         if (i0 + (int64_t)u * WS_THREADS < total) {
           if (dst.mc_base) {
             multimem_st_v4(dst.mc_base + d[u], v[u]);
+          } else if (dst.scatter) {
+            const int64_t q = d[u] / dst.scatter;
+            const int p = q < dst.n - 1 ? (int)q : dst.n - 1;
+            st_v4(reinterpret_cast<void*>(dst.base[p] + d[u]), v[u]);
           } else {
             for (int p = 0; p < dst.n; ++p) st_v4(reinterpret_cast<void*>(dst.base[p] + d[u]), v[u]);
           }
@@ -120,10 +129,13 @@ __global__ void __launch_bounds__(WS_THREADS) wsync_kernel(const int64_t* __rest
 }  // namespace
 
 int wsync(const int64_t* jobs_dev, const int64_t* jobs_host, int n_jobs, int64_t dst_bytes, const uint64_t* dst_bases,
-          const uint64_t* dst_flags, int n_dst, uint64_t mc_base, uint64_t mc_flag, int max_ctas, cudaStream_t s) {
+          const uint64_t* dst_flags, int n_dst, uint64_t mc_base, uint64_t mc_flag, int max_ctas, int64_t scatter_bytes,
+          cudaStream_t s) {
   if (n_jobs <= 0) return 0;
   if (!mc_base && (n_dst <= 0 || n_dst > WS_MAX_DST)) throw std::runtime_error("cx wsync: bad destination count");
   if (mc_base % 16) throw std::runtime_error("cx wsync: multicast base not 16-byte aligned");
+  if (scatter_bytes < 0 || scatter_bytes % 16 || (scatter_bytes && mc_base))
+    throw std::runtime_error("cx wsync: scatter size must be a multiple of 16 bytes, without multicast");
   int64_t n_tasks = 0;
   for (int j = 0; j < n_jobs; ++j) {
     const int64_t* q = jobs_host + (int64_t)j * WS_JOB_COLS;
@@ -153,6 +165,7 @@ int wsync(const int64_t* jobs_dev, const int64_t* jobs_host, int n_jobs, int64_t
   }
   d.mc_base = mc_base;
   d.mc_flag = mc_flag;
+  d.scatter = scatter_bytes;
   const int sms = num_sms_comm();
   int ctas = (int)std::min<int64_t>(n_tasks, (int64_t)sms * 4);
   if (max_ctas > 0) ctas = std::min(ctas, max_ctas);

