@@ -10,7 +10,7 @@ capture of the case runs.
 
 Cases: gemm (8192^3), gemm_qkv (T=8192 Llama-3-8B QKV), gemm_silu (T=8192
 gate/up + SiLU-mul), attn (8 x 2048-token causal prefill, 32/8 heads),
-decode_attn (64 x 4096-token paged decode), kv_push (one layer of a 64k-token
+attn_paged (the paged variant: 8 chunks of 2048 queries over 2048 cached tokens), decode_attn (64 x 4096-token paged decode), kv_push (one layer of a 64k-token
 KV push, local), kv_push_nvlink (the same layer pushed from GPU 0 into GPU 1's
 memory over NVLink, one process, peer access; ``--ctas`` sets the grid,
 ``--pull`` runs the kernel on GPU 1 reading GPU 0's memory instead, ``--ce``
@@ -70,6 +70,23 @@ def case_attn(dev, n_seq=8, L=2048, hq=32, hkv=8):
     out = torch.empty(T, hq * 128, dtype=torch.bfloat16, device=dev)
     flops = n_seq * hq * 2 * 2 * 128 * L * L / 2   # causal: half of QK^T and PV
     return (lambda: ops.prefill_attention(qkv, ti, hq, hkv, out)), {"flops": flops}
+
+
+def case_attn_paged(dev, n_seq=8, ctx=2048, L=2048, hq=32, hkv=8):
+    """Chunked prefill: 8 chunks of 2048 queries continuing 2048 cached tokens
+    each, K/V of the whole context read from the paged cache."""
+    bs = 16
+    T = n_seq * L
+    per = (ctx + L) // bs
+    nb = n_seq * per
+    kc = (torch.randn(nb, hkv, bs, 128, device=dev) * 0.5).bfloat16()
+    vc = (torch.randn(nb, hkv, bs, 128, device=dev) * 0.5).bfloat16()
+    bt = torch.randperm(nb, device=dev).to(torch.int32).view(n_seq, per).contiguous()
+    qkv = (torch.randn(T, (hq + 2 * hkv) * 128, device=dev) * 0.5).bfloat16()
+    ti = ops.prefill_tile_info([L] * n_seq, dev, ctx=[ctx] * n_seq)
+    out = torch.empty(T, hq * 128, dtype=torch.bfloat16, device=dev)
+    flops = n_seq * hq * 4 * 128 * (L * ctx + L * L / 2)
+    return (lambda: ops.prefill_attention_paged(qkv, kc, vc, bt, ti, hq, hkv, out)), {"flops": flops}
 
 
 def case_decode_attn(dev, B=64, ctx=4096, hq=32, hkv=8):
@@ -251,6 +268,7 @@ def case_decode_step(dev, B=1, ctx=1024, graphs=True):
 
 CASES = {"gemm": lambda d: case_gemm(d), "gemm_qkv": lambda d: case_gemm(d, 8192, 6144, 4096),
          "gemm_silu": lambda d: case_gemm(d, 8192, 28672, 4096, silu=True), "attn": case_attn,
+         "attn_paged": case_attn_paged,
          "decode_attn": case_decode_attn, "kv_push": case_kv_push, "wsync": case_wsync, "ep_gemm": case_ep_gemm,
          "ep_t128": lambda d: case_ep_gemm(d, 128),
          "gemm_m1_qkv": lambda d: case_gemm_m(d, 1, 6144, 4096), "gemm_m1_o": lambda d: case_gemm_m(d, 1, 4096, 4096),

@@ -364,11 +364,11 @@ def run_pd_bench(args, ClockSampler, finalize: bool = True):
             "ms_per_step": round(statistics.mean(step_max), 3),
             "p50_ttft_ms": round(statistics.median(step_max), 3),
             "kv_bytes_per_step": kv_total // K,
-            "push_ms_per_step_max": round(statistics.mean(push_max), 3),
-            # the same bytes over the push kernels' own execution windows
+            "kv_ms_per_step_max": round(statistics.mean(push_max), 3),
+            # the same bytes over the transfer kernels' own execution windows
             # (%globaltimer, first CTA start to last CTA end): launch and
-            # queueing delays on the push stream excluded
-            "push_kernel_window_gbps": round(window_gbps, 2),
+            # queueing delays on the transfer stream excluded
+            "kv_kernel_window_gbps": round(window_gbps, 2),
             "prefill_tokens_per_s": round(tokens / (sum(step_max) * 1e-3), 1),
             "kv_check": "ok" if ok else "MISMATCH",
             "kv_transfer": ("pull: the decode GPU's kernel gathers each layer from the prefill GPU's cache over "
@@ -379,7 +379,7 @@ def run_pd_bench(args, ClockSampler, finalize: bool = True):
             "p50_ttft_ms_bulk_copy_after_prefill": round(statistics.median(bulk_max), 3),
             "e2e": {"value": round(e2e, 3),
                     "unit": ("GB/s of KV delivered per second of the whole step through connex_b200.runtime.pd "
-                             "(H2D of prompt ids, prefill with the layerwise push, decode first token, D2H)"),
+                             f"(H2D of prompt ids, prefill with the layerwise {mode}, decode first token, D2H)"),
                     "h2d_bytes_per_step": 4 * tokens // K, "d2h_bytes_per_step": 4 * B * len(prod)},
             "gpu_launches": launches,
             "clocks": {"sm_mhz": clk0.get("sm_mhz"), "sm_max_mhz": clk0.get("sm_max_mhz"),
@@ -389,7 +389,8 @@ def run_pd_bench(args, ClockSampler, finalize: bool = True):
                        "seq_len": f"uniform {args.min_len}-{args.max_len}",
                        "parallelism": "colocated 1P1D" if world == 1 else f"pd {world // 2}P{world // 2}D (TP1)",
                        "kv_block_tokens": cfg.block_size, "l2": "inputs larger than L2 (16 GB weights, GB-scale KV)",
-                       "push_ctas": PUSH_CTAS, "push_after": "attention" if PUSH_AFTER_ATTENTION else "kv write"},
+                       "kv_ctas": PULL_CTAS if mode == "pull" else PUSH_CTAS,
+                       "push_after": "attention" if PUSH_AFTER_ATTENTION else "kv write"},
         }
     if rank == 0 and result is not None and result["kv_check"] != "ok":
         raise SystemExit("kv_check failed: decode-side KV differs from the prefill side")

@@ -56,6 +56,28 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
+// 2^x for x <= 0 on the FMA pipe, to take part of the softmax's exponentials
+// off the special-function unit (which a 128 x 64 tile keeps as busy as its
+// MMAs): x = i + f with i = floor(x), f in [0, 1); 2^f from a cubic fitted
+// here to 2^f on [0, 1) by least squares on the relative error (max relative
+// error 7.5e-5, far below the bf16 rounding of P); i added to the exponent
+// field.  -inf (masked) and anything below 2^-126 give 0.
+constexpr float EXP2_C0 = 0.99992520f, EXP2_C1 = 0.69583350f, EXP2_C2 = 0.22606719f, EXP2_C3 = 0.07802450f;
+__device__ __forceinline__ float poly_exp2(float x) {
+  const float xc = fmaxf(x, -126.0f);
+  const float fi = floorf(xc);
+  const float f = xc - fi;
+  const float p = fmaf(fmaf(fmaf(EXP2_C3, f, EXP2_C2), f, EXP2_C1), f, EXP2_C0);
+  const float r = __int_as_float(__float_as_int(p) + (__float2int_rz(fi) << 23));
+  return x < -126.0f ? 0.0f : r;
+}
+// elements of a row whose exponential runs on the FMA pipe: EMU_OF_8 of every 8
+constexpr int EMU_OF_8 = 2;
+template <int E>
+__device__ __forceinline__ float exp2_mixed(float x) {
+  return (E % 8) >= 8 - EMU_OF_8 ? poly_exp2(x) : fast_exp2(x);
+}
+
 
 // MN-major, 128-byte-swizzled operand (V as the B operand of P.V): 64
 // contiguous elements per 128-byte row (rows = K index), 8-row groups 1024 B
@@ -271,7 +293,11 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
       const bool mask = (key0 + BN - 1 > ctx + q0) || (key0 + BN > total);
       // raw scores stay unscaled: the scale is folded into one FFMA per
       // element below (scale > 0, so the max commutes with it)
-      float mx_raw = -INFINITY;
+      // eight independent running maxima (a 64-long dependent chain of
+      // FMNMX would leave the special-function unit idle), then a tree
+      float mx8[8];
+#pragma unroll
+      for (int q8 = 0; q8 < 8; ++q8) mx8[q8] = -INFINITY;
 #pragma unroll
       for (int e = 0; e < BN; ++e) {
         float v = __uint_as_float(r[e]);
@@ -279,8 +305,10 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
           v = -INFINITY;
           r[e] = __float_as_uint(v);
         }
-        mx_raw = fmaxf(mx_raw, v);
+        mx8[e & 7] = fmaxf(mx8[e & 7], v);
       }
+      const float mx_raw = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
+                                 fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
       const float mx = mx_raw * scale_log2;
       float m_new = m;
       bool resc = false;
@@ -289,15 +317,27 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
         resc = (j > 0);
       }
       const float base = (m_new == -INFINITY) ? 0.f : m_new;
-      float sum = 0.f;
+      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
       uint32_t pk[BN / 2];
 #pragma unroll
       for (int e = 0; e < BN; e += 2) {
-        const float p0 = fast_exp2(fmaf(__uint_as_float(r[e]), scale_log2, -base));
-        const float p1 = fast_exp2(fmaf(__uint_as_float(r[e + 1]), scale_log2, -base));
-        sum += p0 + p1;
+        float p0, p1;
+        // the element index is a compile-time constant after unrolling: each
+        // one is statically on the special-function unit or the FMA pipe
+        switch (e & 7) {
+          case 0: p0 = exp2_mixed<0>(fmaf(__uint_as_float(r[e]), scale_log2, -base));
+                  p1 = exp2_mixed<1>(fmaf(__uint_as_float(r[e + 1]), scale_log2, -base)); break;
+          case 2: p0 = exp2_mixed<2>(fmaf(__uint_as_float(r[e]), scale_log2, -base));
+                  p1 = exp2_mixed<3>(fmaf(__uint_as_float(r[e + 1]), scale_log2, -base)); break;
+          case 4: p0 = exp2_mixed<4>(fmaf(__uint_as_float(r[e]), scale_log2, -base));
+                  p1 = exp2_mixed<5>(fmaf(__uint_as_float(r[e + 1]), scale_log2, -base)); break;
+          default: p0 = exp2_mixed<6>(fmaf(__uint_as_float(r[e]), scale_log2, -base));
+                   p1 = exp2_mixed<7>(fmaf(__uint_as_float(r[e + 1]), scale_log2, -base)); break;
+        }
+        sum4[(e >> 1) & 3] += p0 + p1;
         pk[e >> 1] = pack_bf16x2(p0, p1);
       }
+      const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
       const float alpha = resc ? fast_exp2(m - m_new) : 1.f;
       l = l * alpha + sum;
       m = m_new;
