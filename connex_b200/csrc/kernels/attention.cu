@@ -2,9 +2,18 @@
 //
 // One query token per sequence against its paged KV cache ([blocks, Hkv, 16,
 // 128] per layer, i.e. one head of one block is 4 KB contiguous).  Split-K
-// over the context (512 tokens per CTA), one CTA per (sequence, kv head,
-// split) computing all q heads of the GQA group, then a log-sum-exp merge of
-// the splits.  (Prefill attention runs on tcgen05: attention_tc.cu.)
+// over the context (up to 512 tokens per CTA), one CTA per (sequence, kv
+// head, split) computing all q heads of the GQA group, then a log-sum-exp
+// merge of the splits.  (Prefill attention runs on tcgen05: attention_tc.cu.)
+//
+// The 16-token-block path is one pass per split: a producer warp streams the
+// K and V head slices of two blocks per stage into a 3-stage shared-memory
+// ring with bulk async copies (cp.async.bulk, 4 KB each, completing on an
+// mbarrier; local memory only, no multicast), so a CTA keeps 48 KB of cache
+// reads in flight with one thread; four consumer warps compute the stage's
+// logits (q of the thread's dims held in registers), update the online
+// softmax (one warp per head) and accumulate P.V, then release the stage.  Every wait is bounded and the consumers agree on
+// a timeout with a barrier reduction, so none is left at a barrier.
 #include <algorithm>
 
 #include "common.cuh"
@@ -34,6 +43,279 @@ int decode_attention_plan(int B, int Hq, int Hkv, int max_ctx, long ws_floats) {
     if (n2 > n) n = (int)n2;
   }
   return n;
+}
+
+// ------------------------------------------- pipelined path (16-token blocks)
+namespace decb {
+constexpr int D = 128, BS = 16, BPS = 2, TOK = BS * BPS, NS = 3;
+constexpr int SLICE = BS * D * 2;            // one head of one block: 4 KB
+constexpr int STAGE = 2 * BPS * SLICE;       // K and V of BPS blocks: 16 KB
+constexpr int CONS = 128, THREADS = CONS + 32;
+constexpr int MAXB = 64;                     // block ids of a split staged in shared memory (splits <= 1024 tokens)
+template <int G>
+constexpr int smem_bytes() {  // the token quarters' partial sums reuse the ring once it is drained
+  return NS * STAGE + (G * D + 2 * G * TOK + 2 * 8 + 2 * 8 + MAXB) * 4 + 2 * NS * 8 + 16;
+}
+static_assert(3 * 8 * D * 4 <= NS * STAGE, "partial sums fit in the drained ring");
+}  // namespace decb
+
+__device__ __forceinline__ void bulk_load(void* smem_dst, const void* src, uint32_t bytes, uint64_t* bar) {
+  asm volatile("cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
+                   smem_u32(smem_dst)),
+               "l"(src), "r"(bytes), "r"(smem_u32(bar))
+               : "memory");
+}
+__device__ __forceinline__ void consumers_sync() { asm volatile("bar.sync 1, 128;" ::: "memory"); }
+// every consumer thread's `ok`, AND-ed (a barrier of the 128 consumer threads)
+__device__ __forceinline__ bool consumers_all(bool ok) {
+  uint32_t r;
+  asm volatile(
+      "{\n\t.reg .pred p, q;\n\tsetp.ne.u32 p, %1, 0;\n\t"
+      "bar.red.and.pred q, 1, 128, p;\n\tselp.u32 %0, 1, 0, q;\n\t}"
+      : "=r"(r)
+      : "r"((uint32_t)ok)
+      : "memory");
+  return r != 0;
+}
+
+template <int G>
+__global__ void __launch_bounds__(decb::THREADS, G >= 8 ? 2 : G >= 4 ? 3 : 4)
+    decode_attn_bulk_kernel(const __nv_bfloat16* __restrict__ q, int ldq, const __nv_bfloat16* __restrict__ kc,
+                            const __nv_bfloat16* __restrict__ vc, const int* __restrict__ block_tables,
+                            int max_blocks, const int* __restrict__ ctx_lens, __nv_bfloat16* __restrict__ out,
+                            int ldo, int Hq, int Hkv, float scale_log2, float* __restrict__ ws, int n_splits,
+                            int split_len, int* status) {
+  using namespace decb;
+  extern __shared__ __align__(128) uint8_t smem[];
+  float* qs = reinterpret_cast<float*>(smem + NS * STAGE);  // [G][D], scaled to log2 units
+  float* ps = qs + G * D;                                    // [2][G][TOK]: logits, then probabilities
+  float* ml = ps + 2 * G * TOK;                              // [8] running max, [8] running sum
+  float* al = ml + 16;                                       // [2][8] rescale factor of the stage
+  float* part = reinterpret_cast<float*>(smem);             // [3][G][D]: quarters 1-3's sums, after the ring
+  int* bids = reinterpret_cast<int*>(al + 16);               // [MAXB] the split's block ids
+  uint64_t* full = reinterpret_cast<uint64_t*>(bids + MAXB);
+  uint64_t* empty = full + NS;
+  const int b = blockIdx.x, g = blockIdx.y, sp = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int ctx = ctx_lens[b];
+  const int t0 = sp * split_len;                             // split_len is a multiple of BS
+  const int n = min(ctx, t0 + split_len) - t0;
+  if (n <= 0) {
+    if (n_splits > 1 && tid < G) {
+      float* o = ws + (size_t)b * Hq * n_splits * (D + 2) + (size_t)((g * G + tid) * n_splits + sp) * (D + 2);
+      o[D] = -INFINITY;
+      o[D + 1] = 0.f;
+    }
+    return;
+  }
+  const int nblk = (n + BS - 1) / BS, n_it = (nblk + BPS - 1) / BPS;
+  const int* bt = block_tables + (size_t)b * max_blocks + t0 / BS;
+  if (nblk > MAXB) {  // the host sizes splits so this never happens
+    record_status(status, CX_ERR_BOUNDS);
+    return;
+  }
+  // all block ids of the split in one parallel load: the producer then issues
+  // its copies without a dependent global load in front of each
+  for (int i = tid; i < nblk; i += THREADS) bids[i] = bt[i];
+  if (tid == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], CONS);
+    }
+    fence_barrier_init();
+  }
+  for (int i = tid; i < G * D; i += THREADS) {
+    const int h = i / D, d = i - h * D;
+    qs[i] = __bfloat162float(q[(size_t)b * ldq + (size_t)(g * G + h) * D + d]) * scale_log2;
+  }
+  if (tid < 8) {
+    ml[tid] = -INFINITY;
+    ml[8 + tid] = 0.f;
+  }
+  __syncthreads();
+
+  if (warp == CONS / 32) {  // producer
+    if (lane == 0) {
+      int it = 0;
+      for (; it < n_it; ++it) {
+        const int s = it % NS;
+        if (it >= NS && !mbar_wait(&empty[s], ((it / NS) - 1) & 1, status)) break;
+        const int nb = min(BPS, nblk - it * BPS);
+        mbar_arrive_expect_tx(&full[s], (uint32_t)(nb * 2 * SLICE));
+        uint8_t* stg = smem + s * STAGE;
+        for (int bb = 0; bb < nb; ++bb) {
+          const size_t off = ((size_t)bids[it * BPS + bb] * Hkv + g) * BS * D;
+          bulk_load(stg + bb * SLICE, kc + off, SLICE, &full[s]);
+          bulk_load(stg + (BPS + bb) * SLICE, vc + off, SLICE, &full[s]);
+        }
+      }
+      // the CTA's shared memory must outlive every copy issued into it
+      for (int j = max(0, it - NS); j < it; ++j) mbar_wait(&full[j % NS], (j / NS) & 1, status);
+    }
+    return;
+  }
+
+  // consumers.  Logits: TPT = 2G threads per token, each owning DPT = 64 / G
+  // dims of q for all G heads in registers (64 values whatever G is).  P.V:
+  // thread (dim quad dq, token quarter qt) accumulates 4 dims of all G heads
+  // over 8 tokens of each stage.
+  // threads per token: 2G (measured: 16 threads for G = 4 fit four CTAs per
+  // SM but their longer shuffle reductions cost the time the occupancy won)
+  constexpr int TPT = 2 * G, DPT = D / TPT, NCH = DPT / 8, TPP = CONS / TPT;
+  const int sub = tid % TPT, tk = tid / TPT;
+  const int dq = tid & 31, qt = tid >> 5;
+  uint64_t qr2[G][DPT / 2];  // q of the thread's dims, as packed pairs
+  // the thread's dims: 16-byte chunks sub, sub + TPT, ... of the 256-byte row,
+  // so the TPT threads of a token read one contiguous span per load
+  // (conflict-free for G >= 4) and every q register is indexed statically
+#pragma unroll
+  for (int h = 0; h < G; ++h)
+#pragma unroll
+    for (int j = 0; j < NCH; ++j)
+#pragma unroll
+      for (int e = 0; e < 4; ++e) {
+        const float* qp = qs + h * D + (sub + j * TPT) * 8 + 2 * e;
+        qr2[h][j * 4 + e] = f32x2(qp[0], qp[1]);
+      }
+  uint64_t acc[G][2];  // dims (4dq, 4dq+1) and (4dq+2, 4dq+3) of each head, packed
+#pragma unroll
+  for (int h = 0; h < G; ++h) acc[h][0] = acc[h][1] = 0ull;
+  bool ok = true;
+  for (int it = 0; it < n_it; ++it) {
+    const int s = it % NS;
+    ok = consumers_all(mbar_wait(&full[s], (it / NS) & 1, status));
+    if (!ok) break;
+    const uint8_t* stg = smem + s * STAGE;
+    float* pb = ps + (it & 1) * G * TOK;
+    float* ab = al + (it & 1) * 8;
+#pragma unroll
+    for (int pass = 0; pass * TPP < TOK; ++pass) {
+      const int tt = pass * TPP + tk;
+      float a[G];
+      if (tt < TOK) {
+        // two dims per packed f32x2 FMA: (k0, k1) x (q0, q1) + (s0, s1), the lanes summed at the end
+        uint64_t a2[G];
+#pragma unroll
+        for (int h = 0; h < G; ++h) a2[h] = 0ull;
+        const uint8_t* krow = stg + (tt / BS) * SLICE + (tt % BS) * (D * 2);
+#pragma unroll
+        for (int j = 0; j < NCH; ++j) {
+          const u128 kv = *reinterpret_cast<const u128*>(krow + (sub + j * TPT) * 16);
+          const uint32_t* pk = reinterpret_cast<const uint32_t*>(&kv);
+#pragma unroll
+          for (int w = 0; w < 4; ++w) {
+            const uint64_t k2 = f32x2(bf16_lo(pk[w]), bf16_hi(pk[w]));
+#pragma unroll
+            for (int h = 0; h < G; ++h) a2[h] = fma_f32x2(k2, qr2[h][j * 4 + w], a2[h]);
+          }
+        }
+#pragma unroll
+        for (int h = 0; h < G; ++h) a[h] = lo_f32(a2[h]) + hi_f32(a2[h]);
+      } else {
+#pragma unroll
+        for (int h = 0; h < G; ++h) a[h] = 0.f;
+      }
+#pragma unroll
+      for (int off = 1; off < TPT; off <<= 1)
+#pragma unroll
+        for (int h = 0; h < G; ++h) a[h] += __shfl_xor_sync(0xffffffffu, a[h], off);
+      if (sub == 0 && tt < TOK) {
+        const int tok = it * TOK + tt;
+#pragma unroll
+        for (int h = 0; h < G; ++h) pb[h * TOK + tt] = tok < n ? a[h] : -INFINITY;
+      }
+    }
+    consumers_sync();
+    for (int h = warp; h < G; h += 4) {  // online softmax, one warp per head, one lane per token
+      const float x = pb[h * TOK + lane];
+      const float mx = warp_max(x);
+      const float m_old = ml[h], m_new = fmaxf(m_old, mx);
+      const float p = x == -INFINITY ? 0.f : exp2f(x - m_new);
+      const float sum = warp_sum(p);
+      const float alpha = m_old == -INFINITY ? 0.f : exp2f(m_old - m_new);
+      pb[h * TOK + lane] = p;
+      __syncwarp();
+      if (lane == 0) {
+        ml[h] = m_new;
+        ml[8 + h] = ml[8 + h] * alpha + sum;
+        ab[h] = alpha;
+      }
+    }
+    consumers_sync();
+    {  // P.V over this thread's quarter of the stage (8 tokens, 4 dims, all heads)
+      const int base = it * TOK + qt * 8;
+      const int cnt = min(8, n - base);
+#pragma unroll
+      for (int h = 0; h < G; ++h) {
+        const uint64_t a2 = f32x2(ab[h], ab[h]);
+        acc[h][0] = mul_f32x2(acc[h][0], a2);
+        acc[h][1] = mul_f32x2(acc[h][1], a2);
+      }
+#pragma unroll
+      for (int j4 = 0; j4 < 8; j4 += 4) {  // four tokens at a time: one float4 of p per head
+        if (j4 < cnt) {
+          float pr[G][4];
+#pragma unroll
+          for (int h = 0; h < G; ++h) {
+            const float4 p4 = *reinterpret_cast<const float4*>(pb + h * TOK + qt * 8 + j4);
+            pr[h][0] = p4.x; pr[h][1] = p4.y; pr[h][2] = p4.z; pr[h][3] = p4.w;
+          }
+#pragma unroll
+          for (int j = 0; j < 4; ++j) {
+            if (j4 + j < cnt) {  // past the end: p is 0, but the slot's V may be NaN
+              const int t = qt * 8 + j4 + j;
+              const uint2 v4 = *reinterpret_cast<const uint2*>(stg + (BPS + t / BS) * SLICE + (t % BS) * (D * 2) +
+                                                               dq * 8);
+              const uint64_t v01 = f32x2(bf16_lo(v4.x), bf16_hi(v4.x)), v23 = f32x2(bf16_lo(v4.y), bf16_hi(v4.y));
+#pragma unroll
+              for (int h = 0; h < G; ++h) {
+                const uint64_t pp = f32x2(pr[h][j], pr[h][j]);
+                acc[h][0] = fma_f32x2(pp, v01, acc[h][0]);
+                acc[h][1] = fma_f32x2(pp, v23, acc[h][1]);
+              }
+            }
+          }
+        }
+      }
+    }
+    mbar_arrive(&empty[s]);
+  }
+  if (!ok) return;
+  consumers_sync();  // every stage is consumed: the ring is free for the partial sums
+  // quarters 1-3 hand their sums to quarter 0 through shared memory
+  if (qt > 0) {
+#pragma unroll
+    for (int h = 0; h < G; ++h)
+      *reinterpret_cast<float4*>(part + ((qt - 1) * G + h) * D + 4 * dq) =
+          make_float4(lo_f32(acc[h][0]), hi_f32(acc[h][0]), lo_f32(acc[h][1]), hi_f32(acc[h][1]));
+  }
+  consumers_sync();
+  if (qt == 0) {
+#pragma unroll
+    for (int h = 0; h < G; ++h) {
+      float o[4] = {lo_f32(acc[h][0]), hi_f32(acc[h][0]), lo_f32(acc[h][1]), hi_f32(acc[h][1])};
+#pragma unroll
+      for (int k = 0; k < 3; ++k) {
+        const float4 x = *reinterpret_cast<const float4*>(part + (k * G + h) * D + 4 * dq);
+        o[0] += x.x; o[1] += x.y; o[2] += x.z; o[3] += x.w;
+      }
+      if (n_splits == 1) {
+        const float inv = 1.f / ml[8 + h];
+        uint2 w;
+        w.x = pack_bf16x2(o[0] * inv, o[1] * inv);
+        w.y = pack_bf16x2(o[2] * inv, o[3] * inv);
+        *reinterpret_cast<uint2*>(out + (size_t)b * ldo + (size_t)(g * G + h) * D + 4 * dq) = w;
+      } else {
+        float* op = ws + (size_t)b * Hq * n_splits * (D + 2) + (size_t)((g * G + h) * n_splits + sp) * (D + 2);
+#pragma unroll
+        for (int e = 0; e < 4; ++e) op[4 * dq + e] = o[e];
+        if (dq == 0) {
+          op[D] = ml[h];
+          op[D + 1] = ml[8 + h];
+        }
+      }
+    }
+  }
 }
 
 template <int G>
@@ -215,17 +497,40 @@ __global__ void decode_merge_kernel(const float* __restrict__ ws, __nv_bfloat16*
 
 void decode_attention(const void* q, int ldq, const void* kc, const void* vc, const int* block_tables,
                       int max_blocks, const int* ctx_lens, void* out, int ldo, int B, int Hq, int Hkv, int BS,
-                      int max_ctx, float scale, float* workspace, cudaStream_t s, long ws_floats) {
+                      int max_ctx, float scale, float* workspace, cudaStream_t s, long ws_floats, int* status) {
   if (B == 0) return;
   const int G = Hq / Hkv;
   const int n_splits = decode_attention_plan(B, Hq, Hkv, max_ctx, ws_floats);
-  const int split_len = (max_ctx + n_splits - 1) / n_splits;
   dim3 grid(B, Hkv, n_splits);
   auto Q = reinterpret_cast<const __nv_bfloat16*>(q);
   auto K = reinterpret_cast<const __nv_bfloat16*>(kc);
   auto V = reinterpret_cast<const __nv_bfloat16*>(vc);
   auto O = reinterpret_cast<__nv_bfloat16*>(out);
   const float sl = scale * 1.4426950408889634f;
+  if (BS == decb::BS && (G == 1 || G == 2 || G == 4 || G == 8)) {
+    // splits start on block boundaries; n_splits * split_len still covers max_ctx
+    const int split_len = ((max_ctx + n_splits - 1) / n_splits + decb::BS - 1) / decb::BS * decb::BS;
+    auto launch = [&](auto kern, int smem) {
+      static bool attr[64][4] = {};
+      int dev;
+      cudaGetDevice(&dev);
+      const int gi = G == 1 ? 0 : G == 2 ? 1 : G == 4 ? 2 : 3;
+      if (!attr[dev & 63][gi]) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+        cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);   // 4 CTAs per SM
+        attr[dev & 63][gi] = true;
+      }
+      kern<<<grid, decb::THREADS, smem, s>>>(Q, ldq, K, V, block_tables, max_blocks, ctx_lens, O, ldo, Hq, Hkv, sl,
+                                             workspace, n_splits, split_len, status);
+    };
+    if (G == 4) launch(decode_attn_bulk_kernel<4>, decb::smem_bytes<4>());
+    else if (G == 8) launch(decode_attn_bulk_kernel<8>, decb::smem_bytes<8>());
+    else if (G == 2) launch(decode_attn_bulk_kernel<2>, decb::smem_bytes<2>());
+    else launch(decode_attn_bulk_kernel<1>, decb::smem_bytes<1>());
+    if (n_splits > 1) decode_merge_kernel<<<dim3(B, Hq), dec::D, 0, s>>>(workspace, O, ldo, Hq, n_splits);
+    return;
+  }
+  const int split_len = (max_ctx + n_splits - 1) / n_splits;
   if (G == 4)
     decode_attn_kernel<4><<<grid, dec::THREADS, 0, s>>>(Q, ldq, K, V, block_tables, max_blocks, ctx_lens, O, ldo,
                                                          Hq, Hkv, BS, sl, workspace, n_splits, split_len);

@@ -71,8 +71,11 @@ __device__ __forceinline__ float poly_exp2(float x) {
   const float r = __int_as_float(__float_as_int(p) + (__float2int_rz(fi) << 23));
   return x < -126.0f ? 0.0f : r;
 }
-// elements of a row whose exponential runs on the FMA pipe: EMU_OF_8 of every 8
-constexpr int EMU_OF_8 = 2;
+// elements of a row whose exponential runs on the FMA pipe: EMU_OF_8 of every
+// 8.  Measured: with the softmax warps issue-bound (57 % issue-active, the
+// special-function unit 36 % busy) the polynomial's extra instructions cost
+// more than the unit time they free, so it is off.
+constexpr int EMU_OF_8 = 0;
 template <int E>
 __device__ __forceinline__ float exp2_mixed(float x) {
   return (E % 8) >= 8 - EMU_OF_8 ? poly_exp2(x) : fast_exp2(x);
@@ -317,27 +320,29 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
         resc = (j > 0);
       }
       const float base = (m_new == -INFINITY) ? 0.f : m_new;
-      float sum4[4] = {0.f, 0.f, 0.f, 0.f};
+      // pairs of elements through packed f32x2 FMA / add (one instruction per
+      // two scores); four independent partial sums
+      uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
       uint32_t pk[BN / 2];
+      const uint64_t sc2 = f32x2(scale_log2, scale_log2), nb2 = f32x2(-base, -base);
 #pragma unroll
       for (int e = 0; e < BN; e += 2) {
+        const uint64_t t2 = fma_f32x2(f32x2(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), sc2, nb2);
         float p0, p1;
         // the element index is a compile-time constant after unrolling: each
         // one is statically on the special-function unit or the FMA pipe
         switch (e & 7) {
-          case 0: p0 = exp2_mixed<0>(fmaf(__uint_as_float(r[e]), scale_log2, -base));
-                  p1 = exp2_mixed<1>(fmaf(__uint_as_float(r[e + 1]), scale_log2, -base)); break;
-          case 2: p0 = exp2_mixed<2>(fmaf(__uint_as_float(r[e]), scale_log2, -base));
-                  p1 = exp2_mixed<3>(fmaf(__uint_as_float(r[e + 1]), scale_log2, -base)); break;
-          case 4: p0 = exp2_mixed<4>(fmaf(__uint_as_float(r[e]), scale_log2, -base));
-                  p1 = exp2_mixed<5>(fmaf(__uint_as_float(r[e + 1]), scale_log2, -base)); break;
-          default: p0 = exp2_mixed<6>(fmaf(__uint_as_float(r[e]), scale_log2, -base));
-                   p1 = exp2_mixed<7>(fmaf(__uint_as_float(r[e + 1]), scale_log2, -base)); break;
+          case 0: p0 = exp2_mixed<0>(lo_f32(t2)); p1 = exp2_mixed<1>(hi_f32(t2)); break;
+          case 2: p0 = exp2_mixed<2>(lo_f32(t2)); p1 = exp2_mixed<3>(hi_f32(t2)); break;
+          case 4: p0 = exp2_mixed<4>(lo_f32(t2)); p1 = exp2_mixed<5>(hi_f32(t2)); break;
+          default: p0 = exp2_mixed<6>(lo_f32(t2)); p1 = exp2_mixed<7>(hi_f32(t2)); break;
         }
-        sum4[(e >> 1) & 3] += p0 + p1;
+        sum2[(e >> 1) & 3] = add_f32x2(sum2[(e >> 1) & 3], f32x2(p0, p1));
         pk[e >> 1] = pack_bf16x2(p0, p1);
       }
-      const float sum = (sum4[0] + sum4[1]) + (sum4[2] + sum4[3]);
+      const uint64_t s01 = add_f32x2(sum2[0], sum2[1]), s23 = add_f32x2(sum2[2], sum2[3]);
+      const uint64_t s4 = add_f32x2(s01, s23);
+      const float sum = lo_f32(s4) + hi_f32(s4);
       const float alpha = resc ? fast_exp2(m - m_new) : 1.f;
       l = l * alpha + sum;
       m = m_new;

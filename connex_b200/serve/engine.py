@@ -727,7 +727,8 @@ class GenerationEngine:
                 r.error = f"{type(e).__name__}: {e}"
             self._finish(reqs, "error", token_sent=False)
             return
-        self.stats["mixed_steps"] += 1
+        # steps named like the runtime's kinds: one-token rows only, chunks only, or both
+        self.stats["decode_steps" if not chunks else "prefill_steps" if not decode else "mixed_steps"] += 1
         self.stats["chunks"] += len(chunks)
         first = []
         for (r, n), tok in zip(chunks, toks[len(decode):]):

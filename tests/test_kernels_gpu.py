@@ -234,6 +234,34 @@ def test_decode_attention(dev, G):
     _close(one.view(1, Hq, 128), ref[3:])
 
 
+@pytest.mark.parametrize("G", [1, 2])
+def test_decode_attention_small_groups_and_unwritten_slots(dev, G):
+    """GQA groups of 1 and 2, and cache slots past each sequence's end that
+    hold NaN (never written): they must not reach the output."""
+    from connex_b200 import ops
+    from connex_b200.ops import reference as R
+    Hkv, BS, NB = 4, 16, 700
+    Hq = Hkv * G
+    ctx = [5, 16, 33, 1000, 2047]
+    B = len(ctx)
+    kc, vc = _rnd(NB, Hkv, BS, 128, dev=dev, seed=21), _rnd(NB, Hkv, BS, 128, dev=dev, seed=22)
+    maxb = (max(ctx) + BS - 1) // BS
+    perm = torch.randperm(NB, device=dev).to(torch.int32)
+    bt = perm[:B * maxb].view(B, maxb).contiguous()
+    for b, n in enumerate(ctx):                      # poison the tail of each last block
+        if n % BS:
+            last = int(bt[b, (n - 1) // BS])
+            kc[last, :, n % BS:].view(torch.int16).fill_(-1)
+            vc[last, :, n % BS:].view(torch.int16).fill_(-1)
+    cl = torch.tensor(ctx, dtype=torch.int32, device=dev)
+    q = _rnd(B, Hq * 128, dev=dev, seed=23)
+    ref = R.paged_decode_attention(q.reshape(B, Hq, 128), kc, vc, bt, cl)
+    for ws in (ops.decode_workspace(B, Hq, max(ctx), dev), ops.decode_workspace(64, Hq, max(ctx), dev)):
+        out = ops.decode_attention(q, kc, vc, bt, cl, Hq, max(ctx), ws)
+        assert torch.isfinite(out.float()).all()
+        _close(out.reshape(B, Hq, 128), ref)
+
+
 def test_kv_push_local(dev):
     from connex_b200 import ops
     from connex_b200.ops import reference as R
