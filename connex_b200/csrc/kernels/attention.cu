@@ -318,6 +318,244 @@ __global__ void __launch_bounds__(decb::THREADS, G >= 8 ? 2 : G >= 4 ? 3 : 4)
   }
 }
 
+// ------------------------------------- tensor-core path (16-token blocks)
+// QK^T and P.V on mma.sync (bf16 in, fp32 accumulate): the kernel is memory
+// bound, so the point is the instruction count -- a warp's logits for 8
+// tokens x 128 dims are 8 MMAs instead of ~600 CUDA-core instructions.  K and
+// V stream in by TMA (128-byte swizzle: the ldmatrix reads are conflict-free)
+// into a 3-stage ring; warp w takes tokens [8w, 8w + 8) of every 32-token
+// stage with its own online softmax (no barrier per stage) and the warps
+// merge at the end.  S^T = q.K^T puts the heads on the M dimension (rows
+// 0..7; rows 8..15 are zero padding); its C fragment (head, token pair) is
+// exactly the B fragment of O^T = V^T.P^T (m16n8k8: dims on M, heads on N),
+// so P never leaves the registers and O needs no padded rows.
+namespace decm {
+constexpr int D = 128, BS = 16, TOK = 32, NS = 3, SLICE = BS * D * 2, STAGE = 4 * SLICE;  // K0 K1 V0 V1
+constexpr int CONS = 128, THREADS = CONS + 32, MAXB = 64;
+// ring (1 KB aligned for the swizzle) | q [8][D] fp32 | per-warp (m, l) [4][8][2] | block ids | barriers
+constexpr int SMEM = 1024 + NS * STAGE + 8 * D * 4 + 4 * 8 * 2 * 4 + MAXB * 4 + 2 * NS * 8;
+}  // namespace decm
+
+__device__ __forceinline__ void ldsm_x4(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+__device__ __forceinline__ void ldsm_x4_t(uint32_t addr, uint32_t& r0, uint32_t& r1, uint32_t& r2, uint32_t& r3) {
+  asm volatile("ldmatrix.sync.aligned.m8n8.x4.trans.shared.b16 {%0, %1, %2, %3}, [%4];"
+               : "=r"(r0), "=r"(r1), "=r"(r2), "=r"(r3)
+               : "r"(addr));
+}
+// D (16x8 fp32) += A (16x16 bf16, rows 8..15 zero) . B (16x8 bf16)
+__device__ __forceinline__ void mma16816(float (&d)[4], uint32_t a0, uint32_t a2, uint32_t b0, uint32_t b1) {
+  const uint32_t z = 0u;
+  asm volatile("mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5, %6, %7}, {%8, %9}, "
+               "{%0, %1, %2, %3};"
+               : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+               : "r"(a0), "r"(z), "r"(a2), "r"(z), "r"(b0), "r"(b1));
+}
+// D (16x8 fp32) += A (16x8 bf16) . B (8x8 bf16)
+__device__ __forceinline__ void mma1688(float (&d)[4], uint32_t a0, uint32_t a1, uint32_t b0) {
+  asm volatile("mma.sync.aligned.m16n8k8.row.col.f32.bf16.bf16.f32 {%0, %1, %2, %3}, {%4, %5}, {%6}, "
+               "{%0, %1, %2, %3};"
+               : "+f"(d[0]), "+f"(d[1]), "+f"(d[2]), "+f"(d[3])
+               : "r"(a0), "r"(a1), "r"(b0));
+}
+
+template <int G>
+__global__ void __launch_bounds__(decm::THREADS, 3)
+    decode_attn_mma_kernel(const __grid_constant__ CUtensorMap tmk, const __grid_constant__ CUtensorMap tmv,
+                           const __nv_bfloat16* __restrict__ q, int ldq, const int* __restrict__ block_tables,
+                           int max_blocks, const int* __restrict__ ctx_lens, __nv_bfloat16* __restrict__ out, int ldo,
+                           int Hq, int Hkv, float scale_log2, float* __restrict__ ws, int n_splits, int split_len,
+                           int* status) {
+  using namespace decm;
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* ring = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  float* qs = reinterpret_cast<float*>(ring + NS * STAGE);  // [8][D]
+  float* mlw = qs + 8 * D;                                  // [4 warps][8 heads][m, l]
+  int* bids = reinterpret_cast<int*>(mlw + 4 * 8 * 2);
+  uint64_t* full = reinterpret_cast<uint64_t*>(bids + MAXB);
+  uint64_t* empty = full + NS;
+  const int b = blockIdx.x, g = blockIdx.y, sp = blockIdx.z;
+  const int tid = threadIdx.x, lane = tid & 31, warp = tid >> 5;
+  const int ctx = ctx_lens[b];
+  const int t0 = sp * split_len;
+  const int n = min(ctx, t0 + split_len) - t0;
+  if (n <= 0) {
+    if (n_splits > 1 && tid < G) {
+      float* o = ws + (size_t)b * Hq * n_splits * (D + 2) + (size_t)((g * G + tid) * n_splits + sp) * (D + 2);
+      o[D] = -INFINITY;
+      o[D + 1] = 0.f;
+    }
+    return;
+  }
+  const int nblk = (n + BS - 1) / BS, n_it = (nblk + 1) / 2;
+  if (nblk > MAXB) {
+    record_status(status, CX_ERR_BOUNDS);
+    return;
+  }
+  const int* bt = block_tables + (size_t)b * max_blocks + t0 / BS;
+  for (int i = tid; i < nblk; i += THREADS) bids[i] = bt[i];
+  for (int i = tid; i < 8 * D; i += THREADS) {
+    const int h = i / D, d = i - h * D;
+    qs[i] = h < G ? __bfloat162float(q[(size_t)b * ldq + (size_t)(g * G + h) * D + d]) * scale_log2 : 0.f;
+  }
+  if (tid == 0) {
+    for (int s = 0; s < NS; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], CONS / 32);
+    }
+    fence_barrier_init();
+    prefetch_tmap(&tmk);
+    prefetch_tmap(&tmv);
+  }
+  __syncthreads();
+
+  if (warp == CONS / 32) {  // producer: TMA of two blocks' K and V head slices per stage
+    if (lane == 0) {
+      int it = 0;
+      for (; it < n_it; ++it) {
+        const int s = it % NS;
+        if (it >= NS && !mbar_wait(&empty[s], ((it / NS) - 1) & 1, status)) break;
+        const int nb = min(2, nblk - it * 2);
+        mbar_arrive_expect_tx(&full[s], (uint32_t)(nb * 2 * SLICE));
+        uint8_t* stg = ring + s * STAGE;
+        for (int bb = 0; bb < nb; ++bb) {
+          const int row = (bids[it * 2 + bb] * Hkv + g) * BS;  // cache row of (block, head, token 0)
+          for (int h = 0; h < 2; ++h) {
+            tma_load_2d(stg + bb * SLICE + h * 2048, &tmk, &full[s], h * 64, row);
+            tma_load_2d(stg + (2 + bb) * SLICE + h * 2048, &tmv, &full[s], h * 64, row);
+          }
+        }
+      }
+      for (int j = max(0, it - NS); j < it; ++j) mbar_wait(&full[j % NS], (j / NS) & 1, status);
+    }
+    return;
+  }
+
+  const int gq = lane >> 2, qd = lane & 3;  // fragment row (head) / column pair
+  // q as the A operand of S^T = q.K^T: 8 k-steps of 16 dims, rows 0..7
+  uint32_t qa[8][2];
+#pragma unroll
+  for (int kk = 0; kk < 8; ++kk) {
+    const float* qp = qs + gq * D + kk * 16 + 2 * qd;
+    qa[kk][0] = pack_bf16x2(qp[0], qp[1]);
+    qa[kk][1] = pack_bf16x2(qp[8], qp[9]);
+  }
+  float o[8][4];  // O^T: m-tile mt = dims [16 mt, 16 mt + 16); (dim gq | gq + 8, heads 2qd, 2qd + 1)
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) o[mt][0] = o[mt][1] = o[mt][2] = o[mt][3] = 0.f;
+  float m_run = -INFINITY, l_run = 0.f;  // row gq's running max / this thread's partial sum
+  const int blk = warp >> 1, rib0 = (warp & 1) * 8;  // this warp's 8 tokens: rows rib0.. of block blk
+  const int lrow = rib0 + (lane & 7), lmat = lane >> 3;  // ldmatrix: the row this lane addresses
+  bool ok = true;
+  for (int it = 0; it < n_it; ++it) {
+    const int s = it % NS;
+    if (!mbar_wait(&full[s], (it / NS) & 1, status)) { ok = false; break; }
+    const uint8_t* stg = ring + s * STAGE;
+    const int tok0 = it * TOK + warp * 8;  // first of this warp's tokens in the split
+    if (tok0 < n) {
+      const uint32_t kb = smem_u32(stg + blk * SLICE), vb = smem_u32(stg + (2 + blk) * SLICE);
+      if (tok0 + 8 > n) {  // past the end: V rows are cache slots nobody wrote (NaN would survive P = 0)
+        for (int i = lane; i < 8 * 16; i += 32) {
+          const int r = i >> 4, c = i & 15;
+          if (tok0 + r >= n)
+            *reinterpret_cast<uint4*>(const_cast<uint8_t*>(stg) + (2 + blk) * SLICE + (c >> 3) * 2048 +
+                                      (rib0 + r) * 128 + (((c & 7) ^ ((rib0 + r) & 7)) << 4)) = make_uint4(0, 0, 0, 0);
+        }
+        __syncwarp();
+      }
+      float sc[4] = {0.f, 0.f, 0.f, 0.f};  // S^T: (head gq, tokens 2qd, 2qd + 1); rows 8.. unused
+#pragma unroll
+      for (int kk = 0; kk < 8; kk += 2) {  // one ldmatrix.x4 = two k-steps of K^T
+        const int chunk = kk * 2 + lmat;   // 16-byte chunk of the row: dims [8 chunk, 8 chunk + 8)
+        const uint32_t addr = kb + (chunk >> 3) * 2048 + lrow * 128 + (((chunk & 7) ^ (lrow & 7)) << 4);
+        uint32_t b0, b1, b2, b3;
+        ldsm_x4(addr, b0, b1, b2, b3);
+        mma16816(sc, qa[kk][0], qa[kk][1], b0, b1);
+        mma16816(sc, qa[kk + 1][0], qa[kk + 1][1], b2, b3);
+      }
+      const float s0 = tok0 + 2 * qd < n ? sc[0] : -INFINITY;
+      const float s1 = tok0 + 2 * qd + 1 < n ? sc[1] : -INFINITY;
+      float mx = fmaxf(s0, s1);
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 1));
+      mx = fmaxf(mx, __shfl_xor_sync(0xffffffffu, mx, 2));
+      const float m_new = fmaxf(m_run, mx);
+      const float alpha = m_run == -INFINITY ? 0.f : exp2f(m_run - m_new);
+      const float p0 = s0 == -INFINITY ? 0.f : exp2f(s0 - m_new), p1 = s1 == -INFINITY ? 0.f : exp2f(s1 - m_new);
+      l_run = l_run * alpha + p0 + p1;
+      m_run = m_new;
+      const uint32_t pb = pack_bf16x2(p0, p1);  // B fragment of P^T: (tokens 2qd, 2qd + 1; head gq)
+      // O^T's columns are heads 2qd, 2qd + 1: their rescale factors live in rows 2qd, 2qd + 1
+      const float a_lo = __shfl_sync(0xffffffffu, alpha, 8 * qd), a_hi = __shfl_sync(0xffffffffu, alpha, 8 * qd + 4);
+#pragma unroll
+      for (int mt = 0; mt < 8; ++mt) {
+        o[mt][0] *= a_lo;
+        o[mt][1] *= a_hi;
+        o[mt][2] *= a_lo;
+        o[mt][3] *= a_hi;
+      }
+#pragma unroll
+      for (int mt = 0; mt < 8; mt += 2) {  // one ldmatrix.x4.trans = V^T of 32 dims (two m-tiles)
+        const int chunk = 2 * mt + lmat;   // dims [8 chunk, 8 chunk + 8)
+        const uint32_t addr = vb + (chunk >> 3) * 2048 + lrow * 128 + (((chunk & 7) ^ (lrow & 7)) << 4);
+        uint32_t v0, v1, v2, v3;
+        ldsm_x4_t(addr, v0, v1, v2, v3);
+        mma1688(o[mt], v0, v1, pb);
+        mma1688(o[mt + 1], v2, v3, pb);
+      }
+    }
+    __syncwarp();
+    if (lane == 0) mbar_arrive(&empty[s]);
+  }
+  ok = consumers_all(ok);
+  if (!ok) return;
+  // merge the four warps: (m, l) per head, then the weighted sums of O
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 1);
+  l_run += __shfl_xor_sync(0xffffffffu, l_run, 2);
+  if (qd == 0) {
+    mlw[(warp * 8 + gq) * 2] = m_run;
+    mlw[(warp * 8 + gq) * 2 + 1] = l_run;
+  }
+  consumers_sync();  // the ring is drained: reuse it for the warps' O
+  float* ow = reinterpret_cast<float*>(ring);  // [4 warps][8 heads][D]
+#pragma unroll
+  for (int mt = 0; mt < 8; ++mt) {
+    const int d0 = mt * 16 + gq;
+    ow[(warp * 8 + 2 * qd) * D + d0] = o[mt][0];
+    ow[(warp * 8 + 2 * qd + 1) * D + d0] = o[mt][1];
+    ow[(warp * 8 + 2 * qd) * D + d0 + 8] = o[mt][2];
+    ow[(warp * 8 + 2 * qd + 1) * D + d0 + 8] = o[mt][3];
+  }
+  consumers_sync();
+  for (int i = tid; i < G * D; i += CONS) {
+    const int h = i / D, d = i - h * D;
+    float M = -INFINITY;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) M = fmaxf(M, mlw[(w * 8 + h) * 2]);
+    float num = 0.f, den = 0.f;
+#pragma unroll
+    for (int w = 0; w < 4; ++w) {
+      const float mw = mlw[(w * 8 + h) * 2];
+      if (mw == -INFINITY) continue;
+      const float f = exp2f(mw - M);
+      num += ow[(w * 8 + h) * D + d] * f;
+      den += mlw[(w * 8 + h) * 2 + 1] * f;
+    }
+    if (n_splits == 1) {
+      out[(size_t)b * ldo + (size_t)(g * G + h) * D + d] = __float2bfloat16(den > 0.f ? num / den : 0.f);
+    } else {
+      float* op = ws + (size_t)b * Hq * n_splits * (D + 2) + (size_t)((g * G + h) * n_splits + sp) * (D + 2);
+      op[d] = num;
+      if (d == 0) {
+        op[D] = M;
+        op[D + 1] = den;
+      }
+    }
+  }
+}
+
 template <int G>
 __global__ void __launch_bounds__(dec::THREADS)
     decode_attn_kernel(const __nv_bfloat16* __restrict__ q, int ldq, const __nv_bfloat16* __restrict__ kc,
@@ -497,7 +735,8 @@ __global__ void decode_merge_kernel(const float* __restrict__ ws, __nv_bfloat16*
 
 void decode_attention(const void* q, int ldq, const void* kc, const void* vc, const int* block_tables,
                       int max_blocks, const int* ctx_lens, void* out, int ldo, int B, int Hq, int Hkv, int BS,
-                      int max_ctx, float scale, float* workspace, cudaStream_t s, long ws_floats, int* status) {
+                      int max_ctx, float scale, float* workspace, cudaStream_t s, long ws_floats, int* status,
+                      long cache_blocks) {
   if (B == 0) return;
   const int G = Hq / Hkv;
   const int n_splits = decode_attention_plan(B, Hq, Hkv, max_ctx, ws_floats);
@@ -507,6 +746,31 @@ void decode_attention(const void* q, int ldq, const void* kc, const void* vc, co
   auto V = reinterpret_cast<const __nv_bfloat16*>(vc);
   auto O = reinterpret_cast<__nv_bfloat16*>(out);
   const float sl = scale * 1.4426950408889634f;
+  if (BS == decm::BS && (G == 1 || G == 2 || G == 4 || G == 8)) {
+    const int split_len = ((max_ctx + n_splits - 1) / n_splits + decm::BS - 1) / decm::BS * decm::BS;
+    const uint64_t rows = cache_blocks > 0 ? (uint64_t)cache_blocks * Hkv * decm::BS : (1ull << 31);
+    const CUtensorMap tk = make_tmap_bf16_2d(kc, decm::D, rows, decm::D * 2, 64, 16, true);
+    const CUtensorMap tv = make_tmap_bf16_2d(vc, decm::D, rows, decm::D * 2, 64, 16, true);
+    auto launch = [&](auto kern) {
+      static bool attr[64][4] = {};
+      int dev;
+      cudaGetDevice(&dev);
+      const int gi = G == 1 ? 0 : G == 2 ? 1 : G == 4 ? 2 : 3;
+      if (!attr[dev & 63][gi]) {
+        cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, decm::SMEM);
+        cudaFuncSetAttribute(kern, cudaFuncAttributePreferredSharedMemoryCarveout, 100);
+        attr[dev & 63][gi] = true;
+      }
+      kern<<<grid, decm::THREADS, decm::SMEM, s>>>(tk, tv, Q, ldq, block_tables, max_blocks, ctx_lens, O, ldo, Hq,
+                                                    Hkv, sl, workspace, n_splits, split_len, status);
+    };
+    if (G == 4) launch(decode_attn_mma_kernel<4>);
+    else if (G == 8) launch(decode_attn_mma_kernel<8>);
+    else if (G == 2) launch(decode_attn_mma_kernel<2>);
+    else launch(decode_attn_mma_kernel<1>);
+    if (n_splits > 1) decode_merge_kernel<<<dim3(B, Hq), dec::D, 0, s>>>(workspace, O, ldo, Hq, n_splits);
+    return;
+  }
   if (BS == decb::BS && (G == 1 || G == 2 || G == 4 || G == 8)) {
     // splits start on block boundaries; n_splits * split_len still covers max_ctx
     const int split_len = ((max_ctx + n_splits - 1) / n_splits + decb::BS - 1) / decb::BS * decb::BS;

@@ -296,22 +296,21 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
       const bool mask = (key0 + BN - 1 > ctx + q0) || (key0 + BN > total);
       // raw scores stay unscaled: the scale is folded into one FFMA per
       // element below (scale > 0, so the max commutes with it)
-      // eight independent running maxima (a 64-long dependent chain of
-      // FMNMX would leave the special-function unit idle), then a tree
-      float mx8[8];
+      // four independent running maxima, each folding two scores per step
+      // (three-input max); only the tiles that cross the diagonal or the
+      // sequence end pay for the mask (one compare per score against the
+      // row's last valid key), the others take a separate, compare-free loop
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+      if (mask) {
+        const int lim = min(qpos + 1, total) - key0;  // keys [0, lim) of the tile are valid for this row
 #pragma unroll
-      for (int q8 = 0; q8 < 8; ++q8) mx8[q8] = -INFINITY;
-#pragma unroll
-      for (int e = 0; e < BN; ++e) {
-        float v = __uint_as_float(r[e]);
-        if (mask && (key0 + e > qpos || key0 + e >= total)) {
-          v = -INFINITY;
-          r[e] = __float_as_uint(v);
-        }
-        mx8[e & 7] = fmaxf(mx8[e & 7], v);
+        for (int e = 0; e < BN; ++e)
+          if (e >= lim) r[e] = __float_as_uint(-INFINITY);
       }
-      const float mx_raw = fmaxf(fmaxf(fmaxf(mx8[0], mx8[1]), fmaxf(mx8[2], mx8[3])),
-                                 fmaxf(fmaxf(mx8[4], mx8[5]), fmaxf(mx8[6], mx8[7])));
+#pragma unroll
+      for (int e = 0; e < BN; e += 2)
+        mx4[(e >> 1) & 3] = fmaxf(mx4[(e >> 1) & 3], fmaxf(__uint_as_float(r[e]), __uint_as_float(r[e + 1])));
+      const float mx_raw = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3]));
       const float mx = mx_raw * scale_log2;
       float m_new = m;
       bool resc = false;

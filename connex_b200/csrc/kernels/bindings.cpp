@@ -195,12 +195,14 @@ void decode_attention(const at::Tensor& q, const at::Tensor& kc, const at::Tenso
   const c10::cuda::CUDAGuard g(q.device());
   const int B = (int)q.size(0);
   const int Hkv = (int)kc.size(1), BS = (int)kc.size(2);
+  TORCH_CHECK(kc.dim() == 4 && kc.size(3) == 128 && kc.is_contiguous() && vc.is_contiguous() && vc.sizes() == kc.sizes(),
+              "caches must be contiguous [blocks, Hkv, BS, 128]");
   const int splits = cx::decode_attention_splits((int)max_ctx);
   TORCH_CHECK(workspace.numel() >= (int64_t)B * Hq * splits * 130, "decode workspace too small");
   cx::decode_attention(q.data_ptr(), row_ld(q), kc.data_ptr(), vc.data_ptr(), block_tables.data_ptr<int>(),
                        (int)block_tables.size(1), ctx_lens.data_ptr<int>(), out.data_ptr(), row_ld(out), B, (int)Hq,
                        Hkv, BS, (int)max_ctx, (float)scale, workspace.data_ptr<float>(), cur_stream(q),
-                       (long)workspace.numel());
+                       (long)workspace.numel(), nullptr, (long)kc.size(0));
 }
 
 int64_t decode_attention_plan(int64_t B, int64_t Hq, int64_t Hkv, int64_t max_ctx, int64_t ws_floats) {

@@ -38,7 +38,7 @@ void prefill_attention_paged_tc(const void* qkv, int ldq, int qkv_cols, int T, c
 void decode_attention(const void* q, int ldq, const void* kc, const void* vc, const int* block_tables,
                       int max_blocks, const int* ctx_lens, void* out, int ldo, int B, int Hq, int Hkv, int BS,
                       int max_ctx, float scale, float* workspace, cudaStream_t s, long ws_floats = -1,
-                      int* status = nullptr);
+                      int* status = nullptr, long cache_blocks = -1);
 int decode_attention_splits(int max_ctx);
 // Splits a launch uses (>= decode_attention_splits; more for small batches when ws_floats allows).
 int decode_attention_plan(int B, int Hq, int Hkv, int max_ctx, long ws_floats);
