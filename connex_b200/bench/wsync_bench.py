@@ -8,6 +8,9 @@ weight arena):
 * ``fused_mc``  -- :class:`WeightBroadcast` over NVLink multicast (one
   kernel reads fp32, casts, re-lays out and stores through the multicast
   address; receivers wait on a device flag);
+* ``fused_relay`` -- the same kernel scattering each round of pieces to the
+  receiver that owns their arena slice; each receiver multicasts its share
+  of the round on to every arena as soon as it lands;
 * ``fused_p2p`` -- the same kernel storing to each receiver's peer address;
 * ``nccl``      -- conventional: PyTorch cast + cat + interleave on the
   trainer into a bf16 staging arena, then ``dist.broadcast`` (NCCL).
@@ -71,7 +74,7 @@ def run(cfg: LlamaConfig, iters: int = 5, warmup: int = 3) -> Dict:
             apply_local(jobs, arena)
         out["local_ms"] = _time(lambda: apply_local(jobs, arena), iters, 1)
         return out
-    for mode in ("multicast", "p2p"):
+    for mode in ("multicast", "relay", "p2p"):
         try:
             bc = WeightBroadcast(cfg, mode=mode)
         except RuntimeError as e:

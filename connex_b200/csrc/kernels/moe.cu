@@ -83,11 +83,12 @@ __global__ void __launch_bounds__(1024) ep_count_kernel(const int* __restrict__ 
     for (int i = threadIdx.x; i < NB; i += blockDim.x) cm[me * NB + i] = hist[i];
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    atomicAdd(comb_expect, (uint32_t)valid * arrivals_per_row);
-    __threadfence_system();
-    for (int d = 0; d < N; ++d) red_release_sys_add_u32(reinterpret_cast<uint32_t*>(peers.count_flag[d]), 1u);
-  }
+  if (threadIdx.x == 0) atomicAdd(comb_expect, (uint32_t)valid * arrivals_per_row);
+  // one release per destination, each from its own thread: they run in
+  // parallel (a release from one thread to N flags would be N system fences
+  // in a row); the barrier above makes every thread's peer stores part of
+  // what each release publishes
+  if (threadIdx.x < N) red_release_sys_add_u32(reinterpret_cast<uint32_t*>(peers.count_flag[threadIdx.x]), 1u);
 }
 
 // --------------------------------------------------------------- dispatch
@@ -178,10 +179,8 @@ __global__ void __launch_bounds__(256) ep_dispatch_kernel(const __nv_bfloat16* _
     }
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    __threadfence_system();
-    for (int d = 0; d < N; ++d) red_release_sys_add_u32(reinterpret_cast<uint32_t*>(peers.data_flag[d]), 1u);
-  }
+  // the rows are stored: one release per destination, in parallel threads
+  if (threadIdx.x < N) red_release_sys_add_u32(reinterpret_cast<uint32_t*>(peers.data_flag[threadIdx.x]), 1u);
 }
 
 // ------------------------------------------------------- grouped GEMM

@@ -115,14 +115,14 @@ __global__ void __launch_bounds__(WS_THREADS) wsync_kernel(const int64_t* __rest
     __syncthreads();  // job[] is rewritten by the next task
   }
   __syncthreads();
-  if (threadIdx.x == 0) {
-    asm volatile("fence.acq_rel.sys;" ::: "memory");
-    if (dst.mc_flag) {
+  if (dst.mc_flag) {
+    if (threadIdx.x == 0) {
+      asm volatile("fence.acq_rel.sys;" ::: "memory");
       multimem_red_release_add(dst.mc_flag, 1u);
-    } else {
-      for (int p = 0; p < dst.n; ++p)
-        if (dst.flag[p]) red_release_sys_add_u32(reinterpret_cast<uint32_t*>(dst.flag[p]), 1u);
     }
+  } else if (threadIdx.x < dst.n && dst.flag[threadIdx.x]) {
+    // one release per destination, each from its own thread (in parallel)
+    red_release_sys_add_u32(reinterpret_cast<uint32_t*>(dst.flag[threadIdx.x]), 1u);
   }
 }
 

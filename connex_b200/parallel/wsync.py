@@ -35,7 +35,9 @@ from connex_b200.models.llama import LlamaConfig, LlamaWeights
 
 WS_COLS = 12
 TASK_BYTES = 64 << 10       # output bytes per task (one CTA iteration)
-FLAG_BYTES = 4096           # tail of the arena holding the receive flag
+FLAG_BYTES = 4096           # tail of the arena holding the receive flags
+RELAY_FLAG = 64             # byte offset (in that tail) of the relay-round flag
+RELAY_ROUNDS = 16           # rounds a relayed broadcast is cut into
 
 
 def engine_manifest(cfg: LlamaConfig) -> WeightManifest:
@@ -156,6 +158,90 @@ def fuse_reference(cfg: LlamaConfig, named: Dict[str, torch.Tensor]) -> Dict[str
     return out
 
 
+# ------------------------------------------------------------- relay plans
+def job_intervals(jobs_cpu: torch.Tensor) -> List[Tuple[int, int]]:
+    """Destination byte intervals ``(offset, nbytes)`` the job rows write,
+    sorted and merged (a job whose rows are interleaved in blocks writes one
+    interval per block)."""
+    out = []
+    for _, doff, rows, cols, _, dld, blk, bstride, boff, _, _, _ in jobs_cpu.tolist():
+        if cols != dld:
+            raise ValueError("relay plans need jobs that write whole destination rows")
+        row_b = 2 * dld
+        if blk >= rows:
+            out.append((doff + boff * row_b, rows * row_b))
+        else:
+            for i in range(0, rows, blk):
+                out.append((doff + ((i // blk) * bstride + boff) * row_b, min(blk, rows - i) * row_b))
+    out.sort()
+    merged: List[Tuple[int, int]] = []
+    for off, n in out:
+        if merged and merged[-1][0] + merged[-1][1] == off:
+            merged[-1] = (merged[-1][0], merged[-1][1] + n)
+        else:
+            merged.append((off, n))
+    return merged
+
+
+def split_intervals(intervals: Sequence[Tuple[int, int]], slice_bytes: int, n: int) -> List[List[Tuple[int, int]]]:
+    """The intervals cut at slice boundaries: per slice owner (the last owner
+    takes everything past ``(n - 1) * slice_bytes``)."""
+    per: List[List[Tuple[int, int]]] = [[] for _ in range(n)]
+    for off, ln in intervals:
+        end = off + ln
+        while off < end:
+            k = min(off // slice_bytes, n - 1)
+            stop = end if k == n - 1 else min(end, (k + 1) * slice_bytes)
+            per[k].append((off, stop - off))
+            off = stop
+    return per
+
+
+def copy_jobs(intervals: Sequence[Tuple[int, int]], base: int, task_bytes: int = TASK_BYTES
+              ) -> Tuple[torch.Tensor, int]:
+    """Identity bf16 copy jobs reading ``base + offset`` for each interval and
+    writing the same offsets (the relay's forward of its slice)."""
+    rows_out, task0 = [], 0
+    for off, n in intervals:
+        el = n // 2
+        cols = next(c for c in (4096, 2048, 1024, 512, 256, 128, 64, 32, 16, 8) if el % c == 0)
+        rows = el // cols
+        rpt = max(1, min(rows, task_bytes // (2 * cols)))
+        rows_out.append([base + off, off, rows, cols, cols, cols, rows, 0, 0, 0, task0, rpt])
+        task0 += -(-rows // rpt)
+    if not rows_out:
+        return torch.zeros(0, WS_COLS, dtype=torch.int64), 0
+    return torch.tensor(rows_out, dtype=torch.int64), task0
+
+
+def split_rounds(jobs_cpu: torch.Tensor, rounds: int) -> List[torch.Tensor]:
+    """Whole job rows grouped into ``rounds`` consecutive groups of about equal
+    output bytes, each with its own running task prefix."""
+    rows = jobs_cpu.tolist()
+    total = sum(r[2] * r[3] * 2 for r in rows)
+    groups, cur, acc = [], [], 0
+    for r in rows:
+        cur.append(list(r))
+        acc += r[2] * r[3] * 2
+        if acc >= total * (len(groups) + 1) / rounds and len(groups) < rounds - 1:
+            groups.append(cur)
+            cur = []
+    if cur:
+        groups.append(cur)
+    out = []
+    for g in groups:
+        t = 0
+        for r in g:
+            r[10] = t
+            t += -(-r[2] // r[11])
+        out.append(torch.tensor(g, dtype=torch.int64))
+    return out
+
+
+def _tasks(jobs_cpu: torch.Tensor) -> int:
+    return sum(-(-r[2] // r[11]) for r in jobs_cpu.tolist())
+
+
 def n_ctas(n_tasks: int, device) -> int:
     sms = torch.cuda.get_device_properties(device).multi_processor_count
     return min(n_tasks, 4 * sms)
@@ -175,6 +261,16 @@ class WeightBroadcast:
     Collective: every rank constructs it and calls :meth:`sync` together.
     ``mode``: ``"auto"`` (multicast when the GPUs support it, else peer
     stores), ``"multicast"`` or ``"p2p"``.
+
+    ``"relay"`` (one trainer, every other rank a member): the trainer stores
+    each 16-byte piece only into the receiver that owns its slice of the
+    arena (its egress is the model size once, at the unicast link rate), in
+    ``RELAY_ROUNDS`` rounds; as soon as a round has landed, each receiver
+    multicasts its share of that round to every arena.  Measured on 8 B200:
+    one trainer multicasting to 7 receivers is limited by the switch's
+    replication (16 GB in 39 ms), while the scatter alone takes 23 ms and the
+    receivers' concurrent multicasts of their slices 25 ms -- pipelined, the
+    two halves overlap.
 
     Membership per round (``sync(members=...)``): in multicast mode NVSwitch
     delivers every round to every GPU bound to the group, so a rank that
@@ -204,13 +300,19 @@ class WeightBroadcast:
         torch.cuda.synchronize(self.device)
         self.handle = symm.rendezvous(self.arena, self.group)
         mc = int(getattr(self.handle, "multicast_ptr", 0) or 0)
-        if mode == "multicast" and not mc:
+        if mode in ("multicast", "relay") and not mc:
             raise RuntimeError("NVLink multicast is not available on this group")
-        self.mc = mc if mode in ("auto", "multicast") else 0
+        if mode == "relay" and len(self.srcs) != 1:
+            raise ValueError("relay mode has one source")
+        self.relay = mode == "relay"
+        self.mc = mc if mode in ("auto", "multicast", "relay") else 0
         self.peers = [int(p) for p in self.handle.buffer_ptrs]
         self.weights = LlamaWeights.from_arena(cfg, self.arena[:self.total], self.manifest)
         self.status = ops.new_status(self.device)
         self.received = 0          # cumulative flag target on this rank
+        self.relay_received = 0    # cumulative target of the relay-round flag
+        self._relay = None         # (plan version, per-rank relay state)
+        self._plan_version = 0
         self.rounds_seen = 0       # rounds whose flag increments reached this rank
         self.round = 0
         self._jobs = None
@@ -219,6 +321,10 @@ class WeightBroadcast:
     @property
     def flag_addr(self) -> int:
         return self.arena.data_ptr() + self.total
+
+    @property
+    def relay_flag_addr(self) -> int:
+        return self.arena.data_ptr() + self.total + RELAY_FLAG
 
     @property
     def is_src(self) -> bool:
@@ -248,7 +354,12 @@ class WeightBroadcast:
             if self._jobs is None or self._jobs[4] is not named:
                 jobs, jobs_dev, nt, srcs = self._plan(named, starts)
                 self._jobs = (jobs, jobs_dev, nt, srcs, named)
+                self._plan_version += 1
             planned = self._jobs[2]
+        recv_all = [r for r in range(self.world) if r not in self.srcs]
+        if self.relay and (members is None or sorted(members) == recv_all) and recv_all:
+            self._sync_relay(planned, wait)
+            return
         if n_tasks is None:
             box = [None] * self.world
             dist.all_gather_object(box, planned, group=self.group)
@@ -278,6 +389,65 @@ class WeightBroadcast:
             self.rounds_seen = self.round
         if gets_round and wait and not self.is_src and self.rank in members:
             ops.wait_flag(self.flag_addr, self.received & 0xFFFFFFFF, self.status, self.timeout_s)
+
+    def _relay_state(self, planned) -> dict:
+        """This rank's part of the relay plan: the trainer's round tables, each
+        receiver's forward tables, and the flag arrivals to wait for.  Planned
+        on the trainer, shipped once per plan version."""
+        import torch.distributed as dist
+        box = [None] * self.world
+        dist.all_gather_object(box, (planned, self._plan_version) if self.is_src else None, group=self.group)
+        planned, version = box[self.src]
+        if self._relay is not None and self._relay[0] == version:
+            return self._relay[1]
+        recv = [r for r in range(self.world) if r != self.src]
+        slice_bytes = -(-self.total // (len(recv) * 16)) * 16
+        meta = [None]
+        if self.is_src:
+            rounds = split_rounds(self._jobs[0], RELAY_ROUNDS)
+            per_round = [split_intervals(job_intervals(j), slice_bytes, len(recv)) for j in rounds]
+            meta = [([_tasks(j) for j in rounds], per_round)]
+        dist.broadcast_object_list(meta, src=self.src, group=self.group)
+        src_tasks, per_round = meta[0]
+        st = {"slice": slice_bytes, "recv": recv, "src_ctas": [n_ctas(t, self.device) for t in src_tasks]}
+        fwd_ctas = 0
+        for ivs in per_round:
+            for k in range(len(recv)):
+                fwd_ctas += n_ctas(copy_jobs(ivs[k], 0)[1], self.device) if ivs[k] else 0
+        st["fwd_ctas_total"] = fwd_ctas
+        if self.is_src:
+            st["rounds"] = [(j, j.to(self.device)) for j in split_rounds(self._jobs[0], RELAY_ROUNDS)]
+        else:
+            j = recv.index(self.rank)
+            fw = []
+            for ivs in per_round:
+                jobs, nt = copy_jobs(ivs[j], self.arena.data_ptr())
+                fw.append((jobs, jobs.to(self.device) if nt else None))
+            st["fwd"] = fw
+        self._relay = (version, st)
+        return st
+
+    def _sync_relay(self, planned, wait: bool) -> None:
+        import torch.distributed as dist
+        st = self._relay_state(planned)
+        self.round += 1
+        dist.barrier(group=self.group)      # receivers are off their weights from here on
+        ops._n()
+        if self.is_src:
+            dst = [self.peers[r] for r in st["recv"]]
+            for jobs, jobs_dev in st["rounds"]:
+                ops._C.wsync(jobs_dev, jobs, self.total, dst, [p + self.total for p in dst], 0, 0, 0, st["slice"])
+            self.relay_received += st["fwd_ctas_total"]      # the forwards land in this arena too
+            return
+        for (jobs, jobs_dev), ctas in zip(st["fwd"], st["src_ctas"]):
+            self.received += ctas                            # this round's scatter has landed here...
+            ops.wait_flag(self.flag_addr, self.received & 0xFFFFFFFF, self.status, self.timeout_s)
+            if jobs_dev is not None:                         # ...so pass this rank's share on to every arena
+                ops._C.wsync(jobs_dev, jobs, self.total, [], [], self.mc, self.mc + self.total + RELAY_FLAG, 0)
+        self.relay_received += st["fwd_ctas_total"]
+        self.rounds_seen = self.round
+        if wait:
+            ops.wait_flag(self.relay_flag_addr, self.relay_received & 0xFFFFFFFF, self.status, self.timeout_s)
 
     def catch_up(self, from_rank: int, max_ctas: int = 64) -> None:
         """Copy member ``from_rank``'s arena (the latest version) into this

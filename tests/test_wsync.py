@@ -34,6 +34,29 @@ def test_plan_matches_pytorch_fusion(dtype):
     assert w.layers[1].w13.shape == (2 * CFG.ffn, CFG.hidden)
 
 
+def test_relay_plan_covers_the_arena_once():
+    """The relay's forward intervals, over all rounds and slice owners, are
+    exactly the bytes the broadcast writes, each owned by one receiver."""
+    from connex_b200.parallel.wsync import copy_jobs, job_intervals, split_intervals, split_rounds
+    named = random_trainer_weights(CFG, "cpu", dtype=torch.float32, seed=2)
+    m = engine_manifest(CFG)
+    jobs, _, _ = plan_jobs(CFG, m, named)
+    want = set()
+    for off, n in job_intervals(jobs):
+        want |= set(range(off, off + n, 16))
+    for receivers in (1, 3, 7):
+        sl = -(-m.total // (receivers * 16)) * 16
+        got = []
+        for r in split_rounds(jobs, 16):
+            for k, ivs in enumerate(split_intervals(job_intervals(r), sl, receivers)):
+                for off, n in ivs:
+                    assert off >= k * sl and (k == receivers - 1 or off + n <= (k + 1) * sl)
+                    got += list(range(off, off + n, 16))
+                cj, nt = copy_jobs(ivs, 0)
+                assert sum(row[2] * row[3] * 2 for row in cj.tolist()) == sum(n for _, n in ivs)
+        assert len(got) == len(set(got)) and set(got) == want
+
+
 def test_plan_rejects_bad_shapes():
     named = random_trainer_weights(CFG, "cpu")
     named["model.norm.weight"] = torch.ones(CFG.hidden + 8)
@@ -97,7 +120,7 @@ dist.destroy_process_group()
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("mode", ["auto", "p2p"])
+@pytest.mark.parametrize("mode", ["auto", "p2p", "relay"])
 def test_wsync_broadcast_two_gpus(mode, tmp_path):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
