@@ -56,11 +56,19 @@ def _time(fn, iters: int, warmup: int = 3, device=None) -> float:
         return a.elapsed_time(b) / iters
 
 
+def _status_check(status, what):
+    """A timed case's kernels record timeouts and bad arguments in a status
+    word; a case whose kernels gave up is an error, not a slow number."""
+    return lambda: ops.check_status(status, what)
+
+
 def case_gemm(dev, M=8192, N=8192, K=8192, silu=False):
     a = torch.randn(M, K, device=dev).bfloat16()
     b = torch.randn(N, K, device=dev).bfloat16()
     out = torch.empty(M, N // 2 if silu else N, dtype=torch.bfloat16, device=dev)
-    return (lambda: ops.gemm(a, b, out, silu_mul=silu)), {"flops": 2 * M * N * K}
+    st = ops.new_status(dev)
+    return (lambda: ops.gemm(a, b, out, silu_mul=silu, status=st)), {"flops": 2 * M * N * K,
+                                                                      "check": _status_check(st, "gemm")}
 
 
 def case_attn(dev, n_seq=8, L=2048, hq=32, hkv=8):
@@ -69,7 +77,9 @@ def case_attn(dev, n_seq=8, L=2048, hq=32, hkv=8):
     ti = ops.prefill_tile_info([L] * n_seq, dev)
     out = torch.empty(T, hq * 128, dtype=torch.bfloat16, device=dev)
     flops = n_seq * hq * 2 * 2 * 128 * L * L / 2   # causal: half of QK^T and PV
-    return (lambda: ops.prefill_attention(qkv, ti, hq, hkv, out)), {"flops": flops}
+    st = ops.new_status(dev)
+    return (lambda: ops.prefill_attention(qkv, ti, hq, hkv, out, status=st)), {
+        "flops": flops, "check": _status_check(st, "prefill attention")}
 
 
 def case_attn_paged(dev, n_seq=8, ctx=2048, L=2048, hq=32, hkv=8):
@@ -86,7 +96,9 @@ def case_attn_paged(dev, n_seq=8, ctx=2048, L=2048, hq=32, hkv=8):
     ti = ops.prefill_tile_info([L] * n_seq, dev, ctx=[ctx] * n_seq)
     out = torch.empty(T, hq * 128, dtype=torch.bfloat16, device=dev)
     flops = n_seq * hq * 4 * 128 * (L * ctx + L * L / 2)
-    return (lambda: ops.prefill_attention_paged(qkv, kc, vc, bt, ti, hq, hkv, out)), {"flops": flops}
+    st = ops.new_status(dev)
+    return (lambda: ops.prefill_attention_paged(qkv, kc, vc, bt, ti, hq, hkv, out, status=st)), {
+        "flops": flops, "check": _status_check(st, "paged prefill attention")}
 
 
 def case_decode_attn(dev, B=64, ctx=4096, hq=32, hkv=8):
@@ -288,7 +300,11 @@ def main() -> None:
     p.add_argument("--pull", action="store_true", help="kv_push_nvlink: run on GPU 1, loading GPU 0's memory")
     p.add_argument("--ce", action="store_true", help="kv_push_nvlink: copy-engine peer copy instead of the kernel")
     p.add_argument("--co", default="gemm", help="kv_push_beside: co-running kernel (gemm, attn, none)")
+    p.add_argument("--exp-split", type=int, default=None,
+                   help="attn cases: softmax exponentials of every 8 on the FMA pipe (0, 2, 3)")
     a = p.parse_args()
+    if a.exp_split is not None:
+        ops._C.attention_exp_split(a.exp_split)
     dev = torch.device("cuda", 0)
     if a.case == "kv_push_beside":
         print(json.dumps(push_beside(dev, a.co, a.ctas or 296)), flush=True)

@@ -71,14 +71,14 @@ __device__ __forceinline__ float poly_exp2(float x) {
   const float r = __int_as_float(__float_as_int(p) + (__float2int_rz(fi) << 23));
   return x < -126.0f ? 0.0f : r;
 }
-// elements of a row whose exponential runs on the FMA pipe: EMU_OF_8 of every
-// 8.  Measured: with the softmax warps issue-bound (57 % issue-active, the
+// elements of a row whose exponential runs on the FMA pipe: EMU of every 8
+// (a template parameter of the kernel, chosen by attention_exp_split).
+// Measured: with the softmax warps issue-bound (57 % issue-active, the
 // special-function unit 36 % busy) the polynomial's extra instructions cost
-// more than the unit time they free, so it is off.
-constexpr int EMU_OF_8 = 0;
-template <int E>
+// more than the unit time they free, so the default is 0.
+template <int EMU, int E>
 __device__ __forceinline__ float exp2_mixed(float x) {
-  return (E % 8) >= 8 - EMU_OF_8 ? poly_exp2(x) : fast_exp2(x);
+  return (E % 8) >= 8 - EMU ? poly_exp2(x) : fast_exp2(x);
 }
 
 
@@ -96,7 +96,7 @@ __device__ __forceinline__ uint64_t umma_desc_sw128_mn(uint32_t smem_addr, uint3
 }
 }  // namespace fatc
 
-template <bool PAGED>
+template <bool PAGED, int EMU>
 __global__ void __launch_bounds__(fatc::THREADS, 2)
     prefill_attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                            const __grid_constant__ CUtensorMap tmv, __nv_bfloat16* __restrict__ out, int ldo,
@@ -331,10 +331,10 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
         // the element index is a compile-time constant after unrolling: each
         // one is statically on the special-function unit or the FMA pipe
         switch (e & 7) {
-          case 0: p0 = exp2_mixed<0>(lo_f32(t2)); p1 = exp2_mixed<1>(hi_f32(t2)); break;
-          case 2: p0 = exp2_mixed<2>(lo_f32(t2)); p1 = exp2_mixed<3>(hi_f32(t2)); break;
-          case 4: p0 = exp2_mixed<4>(lo_f32(t2)); p1 = exp2_mixed<5>(hi_f32(t2)); break;
-          default: p0 = exp2_mixed<6>(lo_f32(t2)); p1 = exp2_mixed<7>(hi_f32(t2)); break;
+          case 0: p0 = exp2_mixed<EMU, 0>(lo_f32(t2)); p1 = exp2_mixed<EMU, 1>(hi_f32(t2)); break;
+          case 2: p0 = exp2_mixed<EMU, 2>(lo_f32(t2)); p1 = exp2_mixed<EMU, 3>(hi_f32(t2)); break;
+          case 4: p0 = exp2_mixed<EMU, 4>(lo_f32(t2)); p1 = exp2_mixed<EMU, 5>(hi_f32(t2)); break;
+          default: p0 = exp2_mixed<EMU, 6>(lo_f32(t2)); p1 = exp2_mixed<EMU, 7>(hi_f32(t2)); break;
         }
         sum2[(e >> 1) & 3] = add_f32x2(sum2[(e >> 1) & 3], f32x2(p0, p1));
         pk[e >> 1] = pack_bf16x2(p0, p1);
@@ -415,27 +415,50 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
   }
 }
 
-template <bool PAGED>
+// How many of every 8 softmax exponentials run on the FMA pipe (0, 2 or 3).
+static int g_exp_split = 0;
+void attention_exp_split(int n) { g_exp_split = n == 2 || n == 3 ? n : 0; }
+
+template <bool PAGED, int EMU>
 static void set_smem_once() {
   static bool attr[64] = {false};
   int dev;
   cudaGetDevice(&dev);
   if (!attr[dev & 63]) {
-    cudaFuncSetAttribute(prefill_attn_tc_kernel<PAGED>, cudaFuncAttributeMaxDynamicSharedMemorySize, fatc::SMEM);
+    cudaFuncSetAttribute(prefill_attn_tc_kernel<PAGED, EMU>, cudaFuncAttributeMaxDynamicSharedMemorySize, fatc::SMEM);
     attr[dev & 63] = true;
   }
+}
+
+template <bool PAGED, int EMU>
+static void launch_attn(dim3 grid, cudaStream_t s, const CUtensorMap& tq, const CUtensorMap& tk,
+                        const CUtensorMap& tv, void* out, int ldo, const int* tile_info, int n_tiles, int Hq,
+                        int Hkv, float scale, const int* bt, int bt_stride, int* status) {
+  set_smem_once<PAGED, EMU>();
+  prefill_attn_tc_kernel<PAGED, EMU><<<grid, fatc::THREADS, fatc::SMEM, s>>>(
+      tq, tk, tv, reinterpret_cast<__nv_bfloat16*>(out), ldo, tile_info, n_tiles, Hq, Hkv,
+      scale * 1.4426950408889634f, bt, bt_stride, status);
+}
+
+template <bool PAGED>
+static void launch_attn_split(dim3 grid, cudaStream_t s, const CUtensorMap& tq, const CUtensorMap& tk,
+                              const CUtensorMap& tv, void* out, int ldo, const int* tile_info, int n_tiles, int Hq,
+                              int Hkv, float scale, const int* bt, int bt_stride, int* status) {
+  if (g_exp_split == 2)
+    launch_attn<PAGED, 2>(grid, s, tq, tk, tv, out, ldo, tile_info, n_tiles, Hq, Hkv, scale, bt, bt_stride, status);
+  else if (g_exp_split == 3)
+    launch_attn<PAGED, 3>(grid, s, tq, tk, tv, out, ldo, tile_info, n_tiles, Hq, Hkv, scale, bt, bt_stride, status);
+  else
+    launch_attn<PAGED, 0>(grid, s, tq, tk, tv, out, ldo, tile_info, n_tiles, Hq, Hkv, scale, bt, bt_stride, status);
 }
 
 void prefill_attention_tc(const void* qkv, int ldq, int qkv_cols, int T, void* out, int ldo, const int* tile_info,
                           int n_tiles, int Hq, int Hkv, float scale, int* status, cudaStream_t s) {
   if (n_tiles == 0) return;
-  set_smem_once<false>();
   const CUtensorMap tq = make_tmap_bf16_2d(qkv, (uint64_t)qkv_cols, (uint64_t)T, (uint64_t)ldq * 2, 64, 128, true);
   const CUtensorMap tkv = make_tmap_bf16_2d(qkv, (uint64_t)qkv_cols, (uint64_t)T, (uint64_t)ldq * 2, 64, 64, true);
   dim3 grid(n_tiles, Hq);
-  prefill_attn_tc_kernel<false><<<grid, fatc::THREADS, fatc::SMEM, s>>>(
-      tq, tkv, tkv, reinterpret_cast<__nv_bfloat16*>(out), ldo, tile_info, n_tiles, Hq, Hkv,
-      scale * 1.4426950408889634f, nullptr, 0, status);
+  launch_attn_split<false>(grid, s, tq, tkv, tkv, out, ldo, tile_info, n_tiles, Hq, Hkv, scale, nullptr, 0, status);
 }
 
 void prefill_attention_paged_tc(const void* qkv, int ldq, int qkv_cols, int T, const void* kc, const void* vc,
@@ -443,15 +466,13 @@ void prefill_attention_paged_tc(const void* qkv, int ldq, int qkv_cols, int T, c
                                 const int* tile_info, int n_tiles, int Hq, int Hkv, float scale, int* status,
                                 cudaStream_t s) {
   if (n_tiles == 0) return;
-  set_smem_once<true>();
   const CUtensorMap tq = make_tmap_bf16_2d(qkv, (uint64_t)qkv_cols, (uint64_t)T, (uint64_t)ldq * 2, 64, 128, true);
   // caches as [blocks * Hkv * 16 rows, 128 dims]: one row per (block, head, token)
   const CUtensorMap tk = make_tmap_bf16_2d(kc, 128, (uint64_t)cache_rows, 256, 64, 16, true);
   const CUtensorMap tv = make_tmap_bf16_2d(vc, 128, (uint64_t)cache_rows, 256, 64, 16, true);
   dim3 grid(n_tiles, Hq);
-  prefill_attn_tc_kernel<true><<<grid, fatc::THREADS, fatc::SMEM, s>>>(
-      tq, tk, tv, reinterpret_cast<__nv_bfloat16*>(out), ldo, tile_info, n_tiles, Hq, Hkv,
-      scale * 1.4426950408889634f, block_tables, bt_stride, status);
+  launch_attn_split<true>(grid, s, tq, tk, tv, out, ldo, tile_info, n_tiles, Hq, Hkv, scale, block_tables, bt_stride,
+                          status);
 }
 
 }  // namespace cx

@@ -21,6 +21,10 @@ void gather_rows(const void* src, int lds, const int* idx, void* out, int ldo, i
 // the 128-row tile).  qkv_cols = (Hq+2Hkv)*128, T = rows of qkv.
 void prefill_attention_tc(const void* qkv, int ldq, int qkv_cols, int T, void* out, int ldo, const int* tile_info,
                           int n_tiles, int Hq, int Hkv, float scale, int* status, cudaStream_t s);
+// How many of every 8 softmax exponentials of the prefill attention run on
+// the FMA pipe instead of the special-function unit: 0 (default), 2 or 3.
+void attention_exp_split(int n);
+
 // The same over a paged cache (chunked prefill): q rows from QKV; K/V of the
 // whole context from the caches [blocks, Hkv, 16, 128] (cache_rows =
 // blocks * Hkv * 16) through block_tables [B, bt_stride]; tile_info: [n_tiles,

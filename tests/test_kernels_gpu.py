@@ -206,6 +206,28 @@ def test_prefill_attention(dev, lens, G):
     _close(out.view(T, Hq, 128), R.causal_attention(q, k, v, lens))
 
 
+@pytest.mark.parametrize("split", [2, 3])
+def test_prefill_attention_with_fma_pipe_exponentials(dev, split):
+    """Part of the softmax's 2^x on the FMA pipe (own cubic for 2^f): the
+    output stays within the fp32 reference's tolerance."""
+    from connex_b200 import ops
+    from connex_b200.ops import reference as R
+    lens, Hkv, G = [513, 130, 7], 2, 4
+    Hq, T = Hkv * G, sum(lens)
+    qkv = _rnd(T, (Hq + 2 * Hkv) * 128, dev=dev, seed=41)
+    ti = ops.prefill_tile_info(lens, dev)
+    try:
+        ops._C.attention_exp_split(split)
+        out = ops.prefill_attention(qkv, ti, Hq, Hkv)
+        torch.cuda.synchronize()
+    finally:
+        ops._C.attention_exp_split(0)
+    q = qkv[:, :Hq * 128].view(T, Hq, 128)
+    k = qkv[:, Hq * 128:(Hq + Hkv) * 128].view(T, Hkv, 128)
+    v = qkv[:, (Hq + Hkv) * 128:].view(T, Hkv, 128)
+    _close(out.view(T, Hq, 128), R.causal_attention(q, k, v, lens))
+
+
 @pytest.mark.parametrize("G", [4, 8])
 def test_decode_attention(dev, G):
     from connex_b200 import ops
