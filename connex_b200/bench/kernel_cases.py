@@ -71,18 +71,38 @@ def case_gemm(dev, M=8192, N=8192, K=8192, silu=False):
                                                                       "check": _status_check(st, "gemm")}
 
 
-def case_attn(dev, n_seq=8, L=2048, hq=32, hkv=8):
+def case_attn(dev, n_seq=8, L=2048, hq=32, hkv=8, tile=None):
     T = n_seq * L
     qkv = (torch.randn(T, (hq + 2 * hkv) * 128, device=dev) * 0.5).bfloat16()
-    ti = ops.prefill_tile_info([L] * n_seq, dev)
+    ti = ops.prefill_tile_info([L] * n_seq, dev, tile_rows=tile)
     out = torch.empty(T, hq * 128, dtype=torch.bfloat16, device=dev)
     flops = n_seq * hq * 2 * 2 * 128 * L * L / 2   # causal: half of QK^T and PV
     st = ops.new_status(dev)
-    return (lambda: ops.prefill_attention(qkv, ti, hq, hkv, out, status=st)), {
+    return (lambda: ops.prefill_attention(qkv, ti, hq, hkv, out, status=st, tile_rows=tile)), {
         "flops": flops, "check": _status_check(st, "prefill attention")}
 
 
-def case_attn_paged(dev, n_seq=8, ctx=2048, L=2048, hq=32, hkv=8):
+def case_attn_library(dev, backend="cudnn", n_seq=8, L=2048, hq=32, hkv=8):
+    """The same causal prefill (8 x 2048, 32 q / 8 kv heads, d=128) through
+    torch's scaled_dot_product_attention on one of its library backends
+    (cuDNN or torch's flash-attention kernels): a reference point for the
+    tcgen05 kernel above.  K/V are expanded to the query heads outside the
+    timed region."""
+    import torch.nn.functional as F
+    from torch.nn.attention import SDPBackend, sdpa_kernel
+    q = (torch.randn(n_seq, hq, L, 128, device=dev) * 0.5).bfloat16()
+    k = (torch.randn(n_seq, hkv, L, 128, device=dev) * 0.5).bfloat16().repeat_interleave(hq // hkv, dim=1)
+    v = (torch.randn(n_seq, hkv, L, 128, device=dev) * 0.5).bfloat16().repeat_interleave(hq // hkv, dim=1)
+    be = {"cudnn": SDPBackend.CUDNN_ATTENTION, "flash": SDPBackend.FLASH_ATTENTION}[backend]
+    flops = n_seq * hq * 2 * 2 * 128 * L * L / 2
+
+    def run():
+        with sdpa_kernel(be):
+            F.scaled_dot_product_attention(q, k, v, is_causal=True)
+    return run, {"flops": flops}
+
+
+def case_attn_paged(dev, n_seq=8, ctx=2048, L=2048, hq=32, hkv=8, tile=None):
     """Chunked prefill: 8 chunks of 2048 queries continuing 2048 cached tokens
     each, K/V of the whole context read from the paged cache."""
     bs = 16
@@ -93,11 +113,11 @@ def case_attn_paged(dev, n_seq=8, ctx=2048, L=2048, hq=32, hkv=8):
     vc = (torch.randn(nb, hkv, bs, 128, device=dev) * 0.5).bfloat16()
     bt = torch.randperm(nb, device=dev).to(torch.int32).view(n_seq, per).contiguous()
     qkv = (torch.randn(T, (hq + 2 * hkv) * 128, device=dev) * 0.5).bfloat16()
-    ti = ops.prefill_tile_info([L] * n_seq, dev, ctx=[ctx] * n_seq)
+    ti = ops.prefill_tile_info([L] * n_seq, dev, ctx=[ctx] * n_seq, tile_rows=tile)
     out = torch.empty(T, hq * 128, dtype=torch.bfloat16, device=dev)
     flops = n_seq * hq * 4 * 128 * (L * ctx + L * L / 2)
     st = ops.new_status(dev)
-    return (lambda: ops.prefill_attention_paged(qkv, kc, vc, bt, ti, hq, hkv, out, status=st)), {
+    return (lambda: ops.prefill_attention_paged(qkv, kc, vc, bt, ti, hq, hkv, out, status=st, tile_rows=tile)), {
         "flops": flops, "check": _status_check(st, "paged prefill attention")}
 
 
@@ -280,7 +300,12 @@ def case_decode_step(dev, B=1, ctx=1024, graphs=True):
 
 CASES = {"gemm": lambda d: case_gemm(d), "gemm_qkv": lambda d: case_gemm(d, 8192, 6144, 4096),
          "gemm_silu": lambda d: case_gemm(d, 8192, 28672, 4096, silu=True), "attn": case_attn,
-         "attn_paged": case_attn_paged,
+         "attn_paged": case_attn_paged, "attn_t128": lambda d: case_attn(d, tile=128),
+         "attn_paged_t128": lambda d: case_attn_paged(d, tile=128),
+         "attn_2x8192": lambda d: case_attn(d, n_seq=2, L=8192),
+         "attn_2x8192_t128": lambda d: case_attn(d, n_seq=2, L=8192, tile=128),
+         "attn_cudnn_2x8192": lambda d: case_attn_library(d, "cudnn", n_seq=2, L=8192), "attn_cudnn": lambda d: case_attn_library(d, "cudnn"),
+         "attn_torch_flash": lambda d: case_attn_library(d, "flash"),
          "decode_attn": case_decode_attn, "kv_push": case_kv_push, "wsync": case_wsync, "ep_gemm": case_ep_gemm,
          "ep_t128": lambda d: case_ep_gemm(d, 128),
          "gemm_m1_qkv": lambda d: case_gemm_m(d, 1, 6144, 4096), "gemm_m1_o": lambda d: case_gemm_m(d, 1, 4096, 4096),
@@ -301,7 +326,7 @@ def main() -> None:
     p.add_argument("--ce", action="store_true", help="kv_push_nvlink: copy-engine peer copy instead of the kernel")
     p.add_argument("--co", default="gemm", help="kv_push_beside: co-running kernel (gemm, attn, none)")
     p.add_argument("--exp-split", type=int, default=None,
-                   help="attn cases: softmax exponentials of every 8 on the FMA pipe (0, 2, 3)")
+                   help="attn cases: softmax exponentials of every 8 on the FMA pipe (0, 2, 4)")
     a = p.parse_args()
     if a.exp_split is not None:
         ops._C.attention_exp_split(a.exp_split)

@@ -56,29 +56,40 @@ __device__ __forceinline__ float fast_exp2(float x) {
   return y;
 }
 
-// 2^x for x <= 0 on the FMA pipe, to take part of the softmax's exponentials
-// off the special-function unit (which a 128 x 64 tile keeps as busy as its
-// MMAs): x = i + f with i = floor(x), f in [0, 1); 2^f from a cubic fitted
-// here to 2^f on [0, 1) by least squares on the relative error (max relative
-// error 7.5e-5, far below the bf16 rounding of P); i added to the exponent
-// field.  -inf (masked) and anything below 2^-126 give 0.
-constexpr float EXP2_C0 = 0.99992520f, EXP2_C1 = 0.69583350f, EXP2_C2 = 0.22606719f, EXP2_C3 = 0.07802450f;
-__device__ __forceinline__ float poly_exp2(float x) {
-  const float xc = fmaxf(x, -126.0f);
-  const float fi = floorf(xc);
-  const float f = xc - fi;
-  const float p = fmaf(fmaf(fmaf(EXP2_C3, f, EXP2_C2), f, EXP2_C1), f, EXP2_C0);
-  const float r = __int_as_float(__float_as_int(p) + (__float2int_rz(fi) << 23));
-  return x < -126.0f ? 0.0f : r;
+// 2^x of a pair on the FMA and integer pipes only (no special-function or
+// conversion instruction), to take part of the softmax's exponentials off
+// the special-function unit.  x = n + f with n = round(x) and f in
+// [-0.5, 0.5]: adding 1.5 * 2^23 rounds x to an integer held in the low
+// mantissa bits of the sum, so n is read from those bits and f = x - n is
+// exact; 2^f comes from a cubic fitted here to 2^f on [-0.5, 0.5] as the
+// minimax of the relative error (linear program over 4001 points; 7.5e-5 in
+// fp32 Horner form, far below the bf16 rounding of P), and n is added to its
+// exponent field.  Inputs are clamped to >= -125 (the result stays a normal
+// float; 2^-125 next to the row's largest term, >= 2^-8, is as good as 0),
+// which also maps the mask's -inf to that value.
+constexpr float EXP2_C0 = 0.999928057f, EXP2_C1 = 0.693260968f, EXP2_C2 = 0.242611125f, EXP2_C3 = 0.0551716685f;
+__device__ __forceinline__ uint64_t poly_exp2_x2(uint64_t x2) {
+  const uint64_t x = f32x2(fmaxf(lo_f32(x2), -125.0f), fmaxf(hi_f32(x2), -125.0f));
+  const uint64_t t = add_f32x2(x, f32x2(12582912.0f, 12582912.0f));
+  const uint64_t n = add_f32x2(t, f32x2(-12582912.0f, -12582912.0f));
+  const uint64_t f = fma_f32x2(n, f32x2(-1.0f, -1.0f), x);
+  uint64_t p = fma_f32x2(f32x2(EXP2_C3, EXP2_C3), f, f32x2(EXP2_C2, EXP2_C2));
+  p = fma_f32x2(p, f, f32x2(EXP2_C1, EXP2_C1));
+  p = fma_f32x2(p, f, f32x2(EXP2_C0, EXP2_C0));
+  const uint32_t lo = __float_as_uint(lo_f32(p)) + (__float_as_uint(lo_f32(t)) << 23);
+  const uint32_t hi = __float_as_uint(hi_f32(p)) + (__float_as_uint(hi_f32(t)) << 23);
+  return f32x2(__uint_as_float(lo), __uint_as_float(hi));
 }
-// elements of a row whose exponential runs on the FMA pipe: EMU of every 8
-// (a template parameter of the kernel, chosen by attention_exp_split).
-// Measured: with the softmax warps issue-bound (57 % issue-active, the
-// special-function unit 36 % busy) the polynomial's extra instructions cost
-// more than the unit time they free, so the default is 0.
-template <int EMU, int E>
-__device__ __forceinline__ float exp2_mixed(float x) {
-  return (E % 8) >= 8 - EMU ? poly_exp2(x) : fast_exp2(x);
+// pair P of a row (elements 2P, 2P+1): EMU of every 8 elements (EMU / 2 of
+// every 4 pairs) go to the polynomial, the rest to ex2.approx.  EMU is a
+// template parameter of the kernel, chosen by attention_exp_split.
+template <int EMU, int P>
+__device__ __forceinline__ uint64_t exp2_pair(uint64_t t2) {
+  if constexpr ((P % 4) >= 4 - EMU / 2) {
+    return poly_exp2_x2(t2);
+  } else {
+    return f32x2(fast_exp2(lo_f32(t2)), fast_exp2(hi_f32(t2)));
+  }
 }
 
 
@@ -327,17 +338,17 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
 #pragma unroll
       for (int e = 0; e < BN; e += 2) {
         const uint64_t t2 = fma_f32x2(f32x2(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), sc2, nb2);
-        float p0, p1;
-        // the element index is a compile-time constant after unrolling: each
-        // one is statically on the special-function unit or the FMA pipe
-        switch (e & 7) {
-          case 0: p0 = exp2_mixed<EMU, 0>(lo_f32(t2)); p1 = exp2_mixed<EMU, 1>(hi_f32(t2)); break;
-          case 2: p0 = exp2_mixed<EMU, 2>(lo_f32(t2)); p1 = exp2_mixed<EMU, 3>(hi_f32(t2)); break;
-          case 4: p0 = exp2_mixed<EMU, 4>(lo_f32(t2)); p1 = exp2_mixed<EMU, 5>(hi_f32(t2)); break;
-          default: p0 = exp2_mixed<EMU, 6>(lo_f32(t2)); p1 = exp2_mixed<EMU, 7>(hi_f32(t2)); break;
+        // the pair index is a compile-time constant after unrolling: each
+        // pair is statically on the special-function unit or the FMA pipe
+        uint64_t p2;
+        switch ((e >> 1) & 3) {
+          case 0: p2 = exp2_pair<EMU, 0>(t2); break;
+          case 1: p2 = exp2_pair<EMU, 1>(t2); break;
+          case 2: p2 = exp2_pair<EMU, 2>(t2); break;
+          default: p2 = exp2_pair<EMU, 3>(t2); break;
         }
-        sum2[(e >> 1) & 3] = add_f32x2(sum2[(e >> 1) & 3], f32x2(p0, p1));
-        pk[e >> 1] = pack_bf16x2(p0, p1);
+        sum2[(e >> 1) & 3] = add_f32x2(sum2[(e >> 1) & 3], p2);
+        pk[e >> 1] = pack_bf16x2(lo_f32(p2), hi_f32(p2));
       }
       const uint64_t s01 = add_f32x2(sum2[0], sum2[1]), s23 = add_f32x2(sum2[2], sum2[3]);
       const uint64_t s4 = add_f32x2(s01, s23);
@@ -415,64 +426,455 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
   }
 }
 
-// How many of every 8 softmax exponentials run on the FMA pipe (0, 2 or 3).
-static int g_exp_split = 0;
-void attention_exp_split(int n) { g_exp_split = n == 2 || n == 3 ? n : 0; }
+// ---------------------------------------------------------------------------
+// Two Q tiles per CTA.  One CTA per SM holds 256 query rows of one head as two
+// 128-row tiles X = 0, 1 that share every 128-key K/V tile, and the whole
+// tensor memory: S_X = Q_X.K_j^T (128 f32 columns each) and O_X (128 each).
+// P_X is written back over the first 64 columns of S_X as bf16 pairs and the
+// P.V MMA reads it from there (A operand in tensor memory), so the softmax
+// stores nothing to shared memory.  The MMA thread issues, per key tile j:
+//   P_0.V_j, Q_0.K_{j+1}^T   once softmax 0 has written P_0(j),
+//   P_1.V_j, Q_1.K_{j+1}^T   once softmax 1 has written P_1(j),
+// so the tensor core runs one tile's P.V and next scores while the other
+// tile's softmax runs (the two softmax warpgroups alternate).  The MMAs of
+// one thread execute in issue order: Q_X.K_{j+1}^T overwrites S_X only after
+// P_X(j).V_j has read it, and the commit of S_X(j+1) also marks P_X(j).V_j
+// complete, so the softmax may rescale O_X as soon as it sees S_X(j+1).
+// Warps: 0 TMA producer, 1 MMA issuer, 2-5 softmax of tile 0, 6-9 of tile 1
+// (warp w reaches tensor-memory lanes 32 (w % 4) .. + 31).
+namespace fap {
+constexpr int D = 128;
+constexpr int BM = 128;                      // rows of one Q tile
+constexpr int BN = 128;                      // keys of one K/V tile
+constexpr int ROWS = 2 * BM;                 // query rows of a CTA
+constexpr int THREADS = 320;
+constexpr int HALF_Q = BM * 64 * 2;          // [128 rows x 64 dims]: 16 KB
+constexpr int HALF_KV = BN * 64 * 2;         // [128 keys x 64 dims]: 16 KB
+constexpr int TILE_Q = 2 * HALF_Q;
+constexpr int TILE_KV = 2 * HALF_KV;
+constexpr int OFF_Q = 0;                     // Q_0, Q_1
+constexpr int OFF_K = OFF_Q + 2 * TILE_Q;    // 2 stages
+constexpr int OFF_V = OFF_K + 2 * TILE_KV;   // 2 stages
+constexpr int OFF_BAR = OFF_V + 2 * TILE_KV;
+constexpr int SMEM = OFF_BAR + 256;          // 192.25 KB
+constexpr int TMEM_COLS = 512;
+constexpr int BPT = BN / 16;                 // paged: 16-token cache blocks per key tile
+static_assert(SMEM <= 227 * 1024, "shared memory");
+}  // namespace fap
 
 template <bool PAGED, int EMU>
-static void set_smem_once() {
-  static bool attr[64] = {false};
-  int dev;
-  cudaGetDevice(&dev);
-  if (!attr[dev & 63]) {
-    cudaFuncSetAttribute(prefill_attn_tc_kernel<PAGED, EMU>, cudaFuncAttributeMaxDynamicSharedMemorySize, fatc::SMEM);
-    attr[dev & 63] = true;
+__global__ void __launch_bounds__(fap::THREADS, 1)
+    prefill_attn_pair_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
+                             const __grid_constant__ CUtensorMap tmv, __nv_bfloat16* __restrict__ out, int ldo,
+                             const int* __restrict__ tile_info, int n_tiles, int Hq, int Hkv, float scale_log2,
+                             const int* __restrict__ block_tables, int bt_stride, int* status) {
+  using namespace fap;
+  using fatc::RESCALE_THRESHOLD;
+  extern __shared__ __align__(1024) uint8_t smem[];
+  if ((smem_u32(smem) & 1023u) != 0) {  // swizzled operands need a 1 KB-aligned base
+    if (threadIdx.x == 0) record_status(status, CX_ERR_BOUNDS);
+    return;
+  }
+  uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
+  uint64_t* q_full = bars + 0;
+  uint64_t* k_full = bars + 1;    // [2 stages]
+  uint64_t* k_empty = bars + 3;   // [2]  committed once both tiles' Q.K^T of the stage are done
+  uint64_t* v_full = bars + 5;    // [2]
+  uint64_t* v_empty = bars + 7;   // [2]  committed once both tiles' P.V of the stage are done
+  uint64_t* s_full = bars + 9;    // [tile]  S_X(j) ready; after the tile's last P.V: O_X final
+  uint64_t* p_full = bars + 11;   // [tile]  P_X(j) in tensor memory, O_X rescaled (128 arrivals)
+  uint64_t* drain = bars + 13;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
+
+  const int tile = n_tiles - 1 - (int)blockIdx.x;  // heaviest (latest) tiles first
+  const int h = blockIdx.y;
+  const int* ti = tile_info + tile * (PAGED ? 5 : 3);
+  const int seq_start = ti[0];                    // first row of the sequence's new tokens in QKV
+  const int seq_len = ti[1];                      // its new tokens
+  const int q0 = ti[2];                           // first query of this CTA (among the new tokens)
+  const int ctx = PAGED ? ti[3] : 0;              // tokens already in the cache before them
+  const int* bt = PAGED ? block_tables + (size_t)ti[4] * bt_stride : nullptr;
+  const int total = ctx + seq_len;
+  const int g = h / (Hq / Hkv);
+  // key tiles that Q tile X takes part in (none for a tile past the sequence end)
+  int nt[2];
+#pragma unroll
+  for (int x = 0; x < 2; ++x) {
+    const int r0 = q0 + x * BM;
+    nt[x] = r0 < seq_len ? (min(total, ctx + r0 + BM) + BN - 1) / BN : 0;
+  }
+  const int nkv = max(nt[0], nt[1]);
+  const int qcol = h * D, kcol = (Hq + g) * D, vcol = (Hq + Hkv + g) * D;
+
+  const int warp = warp_id(), lane = lane_id();
+  if (warp == 0 && lane == 0) {
+    mbar_init(q_full, 1);
+    for (int s = 0; s < 2; ++s) {
+      mbar_init(&k_full[s], 1);
+      mbar_init(&k_empty[s], 1);
+      mbar_init(&v_full[s], 1);
+      mbar_init(&v_empty[s], 1);
+      mbar_init(&s_full[s], 1);
+      mbar_init(&p_full[s], 128);
+    }
+    mbar_init(drain, 1);
+    fence_barrier_init();
+    prefetch_tmap(&tmq);
+    if (PAGED) {
+      prefetch_tmap(&tmk);
+      prefetch_tmap(&tmv);
+    }
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+    tc_fence_before();
+  }
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem = *tmem_slot;
+
+  if (warp == 0) {
+    if (lane == 0) {
+      mbar_arrive_expect_tx(q_full, 2 * TILE_Q);
+#pragma unroll
+      for (int x = 0; x < 2; ++x) {   // rows past the tensor end are zero-filled, past the sequence unused
+        tma_load_2d(smem + OFF_Q + x * TILE_Q, &tmq, q_full, qcol, seq_start + q0 + x * BM);
+        tma_load_2d(smem + OFF_Q + x * TILE_Q + HALF_Q, &tmq, q_full, qcol + 64, seq_start + q0 + x * BM);
+      }
+      // paged: cache rows of the eight 16-token blocks of a key tile (tile j's
+      // block ids are fetched one tile ahead so their loads are in flight)
+      const int nblk = (total + 15) / 16;
+      auto rows_of = [&](int j, int (&r)[BPT]) {
+#pragma unroll
+        for (int i = 0; i < BPT; ++i) {
+          const int b = j * BPT + i;
+          r[i] = (bt[b < nblk ? b : 0] * Hkv + g) * 16;  // past the end: any valid block (masked)
+        }
+      };
+      auto load_tile = [&](const CUtensorMap* map, uint8_t* buf, uint64_t* bar, int col, int j, const int (&r)[BPT]) {
+        if constexpr (PAGED) {
+#pragma unroll
+          for (int i = 0; i < BPT; ++i) {
+            tma_load_2d(buf + i * 2048, map, bar, 0, r[i]);
+            tma_load_2d(buf + HALF_KV + i * 2048, map, bar, 64, r[i]);
+          }
+        } else {
+          tma_load_2d(buf, map, bar, col, seq_start + j * BN);
+          tma_load_2d(buf + HALF_KV, map, bar, col + 64, seq_start + j * BN);
+        }
+      };
+      int r_cur[BPT] = {}, r_prev[BPT] = {}, r_next[BPT] = {};
+      if (PAGED) rows_of(0, r_cur);
+      auto load_k = [&](int j) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait(&k_empty[s], ((j >> 1) & 1) ^ 1, status)) return false;
+        mbar_arrive_expect_tx(&k_full[s], TILE_KV);
+        load_tile(&tmk, smem + OFF_K + s * TILE_KV, &k_full[s], kcol, j, r_cur);
+        return true;
+      };
+      auto load_v = [&](int j, const int (&r)[BPT]) -> bool {
+        const int s = j & 1;
+        if (!mbar_wait(&v_empty[s], ((j >> 1) & 1) ^ 1, status)) return false;
+        mbar_arrive_expect_tx(&v_full[s], TILE_KV);
+        load_tile(&tmv, smem + OFF_V + s * TILE_KV, &v_full[s], vcol, j, r);
+        return true;
+      };
+      bool good = true;
+      for (int j = 0; j < nkv && good; ++j) {   // K_j goes out before V_{j-1}
+        good = load_k(j);
+        if (PAGED && j + 1 < nkv) rows_of(j + 1, r_next);
+        if (good && j >= 1) good = load_v(j - 1, r_prev);
+#pragma unroll
+        for (int i = 0; i < BPT; ++i) {
+          r_prev[i] = r_cur[i];
+          r_cur[i] = r_next[i];
+        }
+      }
+      if (good && nkv > 0) load_v(nkv - 1, r_prev);
+    }
+    __syncwarp();
+  } else if (warp == 1) {
+    if (lane == 0) {
+      constexpr uint32_t IDESC_QK = umma_idesc_bf16(BM, BN);
+      constexpr uint32_t IDESC_PV = umma_idesc_bf16_bmn(BM, D);
+      bool ok = mbar_wait(q_full, 0, status);
+      bool issued = false;
+      auto qk = [&](int x, int j) {  // S_x = Q_x.K_j^T, then S_x(j) is signalled
+        const uint32_t sQ = smem_u32(smem + OFF_Q + x * TILE_Q);
+        const uint32_t sK = smem_u32(smem + OFF_K + (j & 1) * TILE_KV);
+#pragma unroll
+        for (int k = 0; k < D / 16; ++k) {
+          umma_bf16(tmem + x * BN, umma_desc_sw128(sQ + (k >> 2) * HALF_Q + (k & 3) * 32),
+                    umma_desc_sw128(sK + (k >> 2) * HALF_KV + (k & 3) * 32), IDESC_QK, k > 0 ? 1u : 0u);
+        }
+        umma_commit(&s_full[x]);
+      };
+      auto pv = [&](int x, int j) {  // O_x += P_x.V_j, P_x in the first 64 columns of S_x
+        const uint32_t sV = smem_u32(smem + OFF_V + (j & 1) * TILE_KV);
+#pragma unroll
+        for (int kk = 0; kk < BN / 16; ++kk) {
+          umma_bf16_ts(tmem + 2 * BN + x * D, tmem + x * BN + kk * 8,
+                       fatc::umma_desc_sw128_mn(sV + kk * 2048, HALF_KV), IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+        }
+      };
+      if (ok && nkv > 0) {
+        ok = mbar_wait(&k_full[0], 0, status);
+        if (ok) {
+          tc_fence_after();
+          for (int x = 0; x < 2; ++x)
+            if (nt[x] > 0) qk(x, 0);
+          issued = true;
+          umma_commit(&k_empty[0]);
+        }
+      }
+      for (int j = 0; j < nkv && ok; ++j) {
+        const int s = j & 1;
+        if (!mbar_wait(&v_full[s], (j >> 1) & 1, status)) { ok = false; break; }
+        for (int x = 0; x < 2 && ok; ++x) {
+          if (j >= nt[x]) continue;
+          if (!mbar_wait(&p_full[x], j & 1, status)) { ok = false; break; }
+          tc_fence_after();
+          pv(x, j);
+          if (j + 1 < nt[x]) {
+            if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, status)) { ok = false; break; }
+            tc_fence_after();
+            qk(x, j + 1);
+          } else {
+            umma_commit(&s_full[x]);   // O_x final
+          }
+        }
+        if (!ok) break;
+        umma_commit(&v_empty[s]);                                // both tiles' P.V_j
+        if (j + 1 < nkv) umma_commit(&k_empty[(j + 1) & 1]);     // both tiles' Q.K_{j+1}^T
+      }
+      if (!ok && issued) {
+        umma_commit(drain);
+        mbar_wait(drain, 0, nullptr, 100000000ull);
+      }
+    }
+    __syncwarp();
+  } else {
+    const int x = (warp - 2) >> 2;        // Q tile of this warpgroup
+    const int q = warp & 3;               // its tensor-memory lane quadrant
+    const int row = q * 32 + lane;
+    const int r0 = q0 + x * BM;           // first query of the tile
+    const int qpos = ctx + r0 + row;      // position in the sequence
+    const uint32_t lane_off = (uint32_t)(q * 32) << 16;
+    const uint32_t tS = tmem + x * BN + lane_off, tO = tmem + 2 * BN + x * D + lane_off;
+    const int n = nt[x];
+    const int zero_x = nt[0] == nkv ? 0 : 1;   // the tile whose P.V reads the last V tile first
+    float m = -INFINITY, l = 0.f;
+    bool ok = true;
+    for (int j = 0; j < n; ++j) {
+      if (!mbar_wait(&s_full[x], j & 1, status)) { ok = false; break; }
+      tc_fence_after();
+      uint32_t r[BN];
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
+      tmem_ld_wait();
+      const int key0 = j * BN;
+      // only tiles that cross the diagonal or the sequence end pay for the
+      // mask (one compare per score against the row's last valid key)
+      const bool mask = (key0 + BN - 1 > ctx + r0) || (key0 + BN > total);
+      if (mask) {
+        const int lim = min(qpos + 1, total) - key0;  // keys [0, lim) of the tile are valid for this row
+#pragma unroll
+        for (int e = 0; e < BN; ++e)
+          if (e >= lim) r[e] = __float_as_uint(-INFINITY);
+      }
+      // raw scores stay unscaled (scale > 0 commutes with the max); four
+      // independent running maxima, two scores per three-input max
+      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+      for (int e = 0; e < BN; e += 2)
+        mx4[(e >> 1) & 3] = fmaxf(mx4[(e >> 1) & 3], fmaxf(__uint_as_float(r[e]), __uint_as_float(r[e + 1])));
+      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * scale_log2;
+      float m_new = m;
+      bool resc = false;
+      if (j == 0 || mx > m + RESCALE_THRESHOLD) {  // lazy rescale
+        m_new = fmaxf(m, mx);
+        resc = (j > 0);
+      }
+      const float base = (m_new == -INFINITY) ? 0.f : m_new;
+      uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
+      const uint64_t sc2 = f32x2(scale_log2, scale_log2), nb2 = f32x2(-base, -base);
+#pragma unroll
+      for (int c = 0; c < BN / 32; ++c) {   // 32 keys -> 16 bf16 pairs -> 16 columns of S_x
+        uint32_t pk[16];
+#pragma unroll
+        for (int e2 = 0; e2 < 16; ++e2) {
+          const int e = c * 32 + 2 * e2;
+          const uint64_t t2 = fma_f32x2(f32x2(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), sc2, nb2);
+          uint64_t p2;
+          switch (e2 & 3) {   // compile-time after unrolling: each pair's unit is fixed
+            case 0: p2 = fatc::exp2_pair<EMU, 0>(t2); break;
+            case 1: p2 = fatc::exp2_pair<EMU, 1>(t2); break;
+            case 2: p2 = fatc::exp2_pair<EMU, 2>(t2); break;
+            default: p2 = fatc::exp2_pair<EMU, 3>(t2); break;
+          }
+          sum2[e2 & 3] = add_f32x2(sum2[e2 & 3], p2);
+          pk[e2] = pack_bf16x2(lo_f32(p2), hi_f32(p2));
+        }
+        tmem_st16(tS + c * 16, pk);
+      }
+      const uint64_t s4 = add_f32x2(add_f32x2(sum2[0], sum2[1]), add_f32x2(sum2[2], sum2[3]));
+      const float sum = lo_f32(s4) + hi_f32(s4);
+      const float alpha = resc ? fatc::fast_exp2(m - m_new) : 1.f;
+      l = l * alpha + sum;
+      m = m_new;
+      if (j >= 1 && __any_sync(0xffffffffu, resc)) {
+        // S_x(j) was committed after P_x(j-1).V_{j-1}: O_x is complete here
+#pragma unroll 1
+        for (int c = 0; c < D / 32; ++c) {
+          uint32_t o[32];
+          tmem_ld32(tO + c * 32, o);
+          tmem_ld_wait();
+#pragma unroll
+          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+          tmem_st32(tO + c * 32, o);
+        }
+      }
+      if (PAGED && x == zero_x && j == nkv - 1 && total - key0 < BN) {
+        // the last tile's keys past the sequence end are cache slots nobody
+        // wrote: their P is 0, but 0 x NaN would still poison O -- zero those
+        // V rows (whole 128-byte rows, so the swizzle does not matter)
+        if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1, status)) { ok = false; break; }
+        uint8_t* vb = smem + OFF_V + (j & 1) * TILE_KV;
+        const int tail = total - key0, nz = (BN - tail) * 8;   // 16-byte chunks per half
+        for (int t = q * 32 + lane; t < 2 * nz; t += 128) {
+          const int half = t / nz, rem = t - half * nz;
+          *reinterpret_cast<uint4*>(vb + half * HALF_KV + (tail + rem / 8) * 128 + (rem % 8) * 16) =
+              make_uint4(0u, 0u, 0u, 0u);
+        }
+        fence_proxy_async_smem();
+      }
+      tmem_st_wait();
+      tc_fence_before();
+      mbar_arrive(&p_full[x]);
+    }
+    if (ok && n > 0 && mbar_wait(&s_full[x], n & 1, status)) {
+      tc_fence_after();
+      const float inv = l > 0.f ? 1.f / l : 0.f;
+      const bool valid = r0 + row < seq_len;
+      __nv_bfloat16* orow = out + (size_t)(seq_start + r0 + row) * ldo + (size_t)h * D;
+#pragma unroll 1
+      for (int c = 0; c < D / 32; ++c) {
+        uint32_t o[32];
+        tmem_ld32(tO + c * 32, o);
+        tmem_ld_wait();
+        if (valid) {
+#pragma unroll
+          for (int v = 0; v < 4; ++v) {
+            u128 w;
+            w.x = pack_bf16x2(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
+            w.y = pack_bf16x2(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
+            w.z = pack_bf16x2(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
+            w.w = pack_bf16x2(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
+            st_v4(orow + c * 32 + v * 8, w);
+          }
+        }
+      }
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem, TMEM_COLS);
   }
 }
 
-template <bool PAGED, int EMU>
-static void launch_attn(dim3 grid, cudaStream_t s, const CUtensorMap& tq, const CUtensorMap& tk,
-                        const CUtensorMap& tv, void* out, int ldo, const int* tile_info, int n_tiles, int Hq,
-                        int Hkv, float scale, const int* bt, int bt_stride, int* status) {
-  set_smem_once<PAGED, EMU>();
-  prefill_attn_tc_kernel<PAGED, EMU><<<grid, fatc::THREADS, fatc::SMEM, s>>>(
-      tq, tk, tv, reinterpret_cast<__nv_bfloat16*>(out), ldo, tile_info, n_tiles, Hq, Hkv,
-      scale * 1.4426950408889634f, bt, bt_stride, status);
+// How many of every 8 softmax exponentials run on the FMA pipe (0, 2 or 4).
+static int g_exp_split = 0;
+void attention_exp_split(int n) { g_exp_split = n == 2 || n == 4 ? n : 0; }
+
+struct AttnArgs {
+  CUtensorMap tq, tk, tv;
+  void* out;
+  int ldo;
+  const int* tile_info;
+  int n_tiles, Hq, Hkv;
+  float scale_log2;
+  const int* bt;
+  int bt_stride;
+  int* status;
+};
+
+// PAIR: the two-tile kernel (256 query rows per CTA, one CTA per SM);
+// otherwise the one-tile kernel (128 rows, two CTAs per SM).
+template <bool PAIR, bool PAGED, int EMU>
+static void launch_attn(const AttnArgs& a, cudaStream_t s) {
+  static bool attr[64] = {false};
+  int dev;
+  cudaGetDevice(&dev);
+  auto* kern = PAIR ? prefill_attn_pair_kernel<PAGED, EMU> : prefill_attn_tc_kernel<PAGED, EMU>;
+  const int smem = PAIR ? fap::SMEM : fatc::SMEM;
+  if (!attr[dev & 63]) {
+    cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
+    attr[dev & 63] = true;
+  }
+  kern<<<dim3(a.n_tiles, a.Hq), PAIR ? fap::THREADS : fatc::THREADS, smem, s>>>(
+      a.tq, a.tk, a.tv, reinterpret_cast<__nv_bfloat16*>(a.out), a.ldo, a.tile_info, a.n_tiles, a.Hq, a.Hkv,
+      a.scale_log2, a.bt, a.bt_stride, a.status);
 }
 
-template <bool PAGED>
-static void launch_attn_split(dim3 grid, cudaStream_t s, const CUtensorMap& tq, const CUtensorMap& tk,
-                              const CUtensorMap& tv, void* out, int ldo, const int* tile_info, int n_tiles, int Hq,
-                              int Hkv, float scale, const int* bt, int bt_stride, int* status) {
+template <bool PAIR, bool PAGED>
+static void launch_attn_split(const AttnArgs& a, cudaStream_t s) {
   if (g_exp_split == 2)
-    launch_attn<PAGED, 2>(grid, s, tq, tk, tv, out, ldo, tile_info, n_tiles, Hq, Hkv, scale, bt, bt_stride, status);
-  else if (g_exp_split == 3)
-    launch_attn<PAGED, 3>(grid, s, tq, tk, tv, out, ldo, tile_info, n_tiles, Hq, Hkv, scale, bt, bt_stride, status);
+    launch_attn<PAIR, PAGED, 2>(a, s);
+  else if (g_exp_split == 4)
+    launch_attn<PAIR, PAGED, 4>(a, s);
   else
-    launch_attn<PAGED, 0>(grid, s, tq, tk, tv, out, ldo, tile_info, n_tiles, Hq, Hkv, scale, bt, bt_stride, status);
+    launch_attn<PAIR, PAGED, 0>(a, s);
 }
 
 void prefill_attention_tc(const void* qkv, int ldq, int qkv_cols, int T, void* out, int ldo, const int* tile_info,
-                          int n_tiles, int Hq, int Hkv, float scale, int* status, cudaStream_t s) {
+                          int n_tiles, int Hq, int Hkv, float scale, int* status, cudaStream_t s, int tile_rows) {
   if (n_tiles == 0) return;
-  const CUtensorMap tq = make_tmap_bf16_2d(qkv, (uint64_t)qkv_cols, (uint64_t)T, (uint64_t)ldq * 2, 64, 128, true);
-  const CUtensorMap tkv = make_tmap_bf16_2d(qkv, (uint64_t)qkv_cols, (uint64_t)T, (uint64_t)ldq * 2, 64, 64, true);
-  dim3 grid(n_tiles, Hq);
-  launch_attn_split<false>(grid, s, tq, tkv, tkv, out, ldo, tile_info, n_tiles, Hq, Hkv, scale, nullptr, 0, status);
+  const bool pair = tile_rows == fap::ROWS;
+  AttnArgs a;
+  a.tq = make_tmap_bf16_2d(qkv, (uint64_t)qkv_cols, (uint64_t)T, (uint64_t)ldq * 2, 64, 128, true);
+  a.tk = a.tv = pair ? a.tq : make_tmap_bf16_2d(qkv, (uint64_t)qkv_cols, (uint64_t)T, (uint64_t)ldq * 2, 64, 64, true);
+  a.out = out;
+  a.ldo = ldo;
+  a.tile_info = tile_info;
+  a.n_tiles = n_tiles;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.bt = nullptr;
+  a.bt_stride = 0;
+  a.status = status;
+  if (pair)
+    launch_attn_split<true, false>(a, s);
+  else
+    launch_attn_split<false, false>(a, s);
 }
 
 void prefill_attention_paged_tc(const void* qkv, int ldq, int qkv_cols, int T, const void* kc, const void* vc,
                                 int64_t cache_rows, const int* block_tables, int bt_stride, void* out, int ldo,
                                 const int* tile_info, int n_tiles, int Hq, int Hkv, float scale, int* status,
-                                cudaStream_t s) {
+                                cudaStream_t s, int tile_rows) {
   if (n_tiles == 0) return;
-  const CUtensorMap tq = make_tmap_bf16_2d(qkv, (uint64_t)qkv_cols, (uint64_t)T, (uint64_t)ldq * 2, 64, 128, true);
+  AttnArgs a;
+  a.tq = make_tmap_bf16_2d(qkv, (uint64_t)qkv_cols, (uint64_t)T, (uint64_t)ldq * 2, 64, 128, true);
   // caches as [blocks * Hkv * 16 rows, 128 dims]: one row per (block, head, token)
-  const CUtensorMap tk = make_tmap_bf16_2d(kc, 128, (uint64_t)cache_rows, 256, 64, 16, true);
-  const CUtensorMap tv = make_tmap_bf16_2d(vc, 128, (uint64_t)cache_rows, 256, 64, 16, true);
-  dim3 grid(n_tiles, Hq);
-  launch_attn_split<true>(grid, s, tq, tk, tv, out, ldo, tile_info, n_tiles, Hq, Hkv, scale, block_tables, bt_stride,
-                          status);
+  a.tk = make_tmap_bf16_2d(kc, 128, (uint64_t)cache_rows, 256, 64, 16, true);
+  a.tv = make_tmap_bf16_2d(vc, 128, (uint64_t)cache_rows, 256, 64, 16, true);
+  a.out = out;
+  a.ldo = ldo;
+  a.tile_info = tile_info;
+  a.n_tiles = n_tiles;
+  a.Hq = Hq;
+  a.Hkv = Hkv;
+  a.scale_log2 = scale * 1.4426950408889634f;
+  a.bt = block_tables;
+  a.bt_stride = bt_stride;
+  a.status = status;
+  if (tile_rows == fap::ROWS)
+    launch_attn_split<true, true>(a, s);
+  else
+    launch_attn_split<false, true>(a, s);
 }
 
 }  // namespace cx

@@ -150,21 +150,24 @@ void gather_rows(const at::Tensor& src, const at::Tensor& idx, at::Tensor& out) 
 }
 
 void prefill_attention_tc(const at::Tensor& qkv, at::Tensor& out, const at::Tensor& tile_info, int64_t Hq,
-                          int64_t Hkv, double scale, const c10::optional<at::Tensor>& status) {
+                          int64_t Hkv, double scale, const c10::optional<at::Tensor>& status, int64_t tile_rows) {
   CHECK_BF16(qkv);
   CHECK_BF16(out);
+  TORCH_CHECK(tile_rows == 128 || tile_rows == 256, "tile_rows must be 128 or 256");
   TORCH_CHECK(tile_info.scalar_type() == at::kInt && tile_info.dim() == 2 && tile_info.size(1) == 3,
               "tile_info must be int32 [n, 3]");
   TORCH_CHECK(qkv.size(1) == (Hq + 2 * Hkv) * 128, "qkv must hold exactly (Hq + 2 Hkv) heads of 128");
   const c10::cuda::CUDAGuard g(qkv.device());
   cx::prefill_attention_tc(qkv.data_ptr(), row_ld(qkv), (int)qkv.size(1), (int)qkv.size(0), out.data_ptr(),
                            row_ld(out), tile_info.data_ptr<int>(), (int)tile_info.size(0), (int)Hq, (int)Hkv,
-                           (float)scale, status_ptr(status), cur_stream(qkv));
+                           (float)scale, status_ptr(status), cur_stream(qkv), (int)tile_rows);
 }
 
 void prefill_attention_paged(const at::Tensor& qkv, const at::Tensor& kc, const at::Tensor& vc,
                              const at::Tensor& block_tables, at::Tensor& out, const at::Tensor& tile_info, int64_t Hq,
-                             int64_t Hkv, double scale, const c10::optional<at::Tensor>& status) {
+                             int64_t Hkv, double scale, const c10::optional<at::Tensor>& status,
+                             int64_t tile_rows) {
+  TORCH_CHECK(tile_rows == 128 || tile_rows == 256, "tile_rows must be 128 or 256");
   CHECK_BF16(qkv);
   CHECK_BF16(kc);
   CHECK_BF16(vc);
@@ -182,7 +185,7 @@ void prefill_attention_paged(const at::Tensor& qkv, const at::Tensor& kc, const 
                                  vc.data_ptr(), kc.size(0) * Hkv * 16, block_tables.data_ptr<int>(),
                                  (int)block_tables.size(1), out.data_ptr(), row_ld(out), tile_info.data_ptr<int>(),
                                  (int)tile_info.size(0), (int)Hq, (int)Hkv, (float)scale, status_ptr(status),
-                                 cur_stream(qkv));
+                                 cur_stream(qkv), (int)tile_rows);
 }
 
 void decode_attention(const at::Tensor& q, const at::Tensor& kc, const at::Tensor& vc, const at::Tensor& block_tables,

@@ -18,11 +18,12 @@ void gather_rows(const void* src, int lds, const int* idx, void* out, int ldo, i
 // Causal varlen prefill attention (GQA, head_dim 128) on the tcgen05 tensor
 // cores.  q/k/v rows live in the fused QKV buffer [T, (Hq+2Hkv)*128];
 // tile_info: [n_tiles, 3] int32 of (seq start row, seq length, first query of
-// the 128-row tile).  qkv_cols = (Hq+2Hkv)*128, T = rows of qkv.
+// the tile); tile_rows: 256 (two 128-row Q tiles per CTA) or 128 (one).
+// qkv_cols = (Hq+2Hkv)*128, T = rows of qkv.
 void prefill_attention_tc(const void* qkv, int ldq, int qkv_cols, int T, void* out, int ldo, const int* tile_info,
-                          int n_tiles, int Hq, int Hkv, float scale, int* status, cudaStream_t s);
+                          int n_tiles, int Hq, int Hkv, float scale, int* status, cudaStream_t s, int tile_rows);
 // How many of every 8 softmax exponentials of the prefill attention run on
-// the FMA pipe instead of the special-function unit: 0 (default), 2 or 3.
+// the FMA pipe instead of the special-function unit: 0 (default), 2 or 4.
 void attention_exp_split(int n);
 
 // The same over a paged cache (chunked prefill): q rows from QKV; K/V of the
@@ -33,7 +34,7 @@ void attention_exp_split(int n);
 void prefill_attention_paged_tc(const void* qkv, int ldq, int qkv_cols, int T, const void* kc, const void* vc,
                                 int64_t cache_rows, const int* block_tables, int bt_stride, void* out, int ldo,
                                 const int* tile_info, int n_tiles, int Hq, int Hkv, float scale, int* status,
-                                cudaStream_t s);
+                                cudaStream_t s, int tile_rows);
 
 // Paged decode attention.  q: [B, *] rows (ld ldq, q heads first).
 // Caches [blocks, Hkv, BS, 128]; block_tables [B, max_blocks]; ctx_lens [B].

@@ -187,17 +187,22 @@ def gather_rows(src: torch.Tensor, idx: torch.Tensor, out: Optional[torch.Tensor
 
 
 # ---------------------------------------------------------- attention
+# Query rows per CTA of the prefill attention: 256 runs two 128-row tiles per
+# CTA (one CTA per SM), 128 the one-tile kernel (two CTAs per SM, measured
+# the faster of the two on 8 x 2048).  ``prefill_tile_info`` and the
+# attention calls take the same ``tile_rows`` (both default to this).
 PREFILL_TILE = 128
 
 
-def prefill_tile_info(seq_lens, device, ctx=None) -> torch.Tensor:
-    """[n_tiles, 3] int32 (seq start row, seq length, first query of the 128-row tile);
+def prefill_tile_info(seq_lens, device, ctx=None, tile_rows: Optional[int] = None) -> torch.Tensor:
+    """[n_tiles, 3] int32 (seq start row, seq length, first query of the tile);
     with ``ctx`` (tokens already in the cache per sequence, chunked prefill)
     [n_tiles, 5] adding (context length, sequence index) for the paged kernel."""
+    step = tile_rows or PREFILL_TILE
     rows = []
     start = 0
     for i, n in enumerate(seq_lens):
-        for q0 in range(0, n, PREFILL_TILE):
+        for q0 in range(0, n, step):
             rows.append((start, n, q0) if ctx is None else (start, n, q0, int(ctx[i]), i))
         start += n
     width = 3 if ctx is None else 5
@@ -209,13 +214,14 @@ def prefill_tile_info(seq_lens, device, ctx=None) -> torch.Tensor:
 
 def prefill_attention(qkv: torch.Tensor, tile_info: torch.Tensor, n_q_heads: int, n_kv_heads: int,
                       out: Optional[torch.Tensor] = None, scale: Optional[float] = None,
-                      status: Optional[torch.Tensor] = None) -> torch.Tensor:
+                      status: Optional[torch.Tensor] = None, tile_rows: Optional[int] = None) -> torch.Tensor:
     """Causal varlen prefill attention on the tcgen05 tensor cores.  ``qkv``
-    is the fused [T, (Hq + 2 Hkv) * 128] projection output."""
+    is the fused [T, (Hq + 2 Hkv) * 128] projection output; ``tile_info``
+    from ``prefill_tile_info`` with the same ``tile_rows``."""
     if out is None:
         out = torch.empty(qkv.shape[0], n_q_heads * 128, dtype=qkv.dtype, device=qkv.device)
     _C.prefill_attention(qkv, out, tile_info, n_q_heads, n_kv_heads,
-                         scale if scale is not None else 1.0 / math.sqrt(128), status)
+                         scale if scale is not None else 1.0 / math.sqrt(128), status, tile_rows or PREFILL_TILE)
     _n()
     return out
 
@@ -223,7 +229,8 @@ def prefill_attention(qkv: torch.Tensor, tile_info: torch.Tensor, n_q_heads: int
 def prefill_attention_paged(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: torch.Tensor,
                             block_tables: torch.Tensor, tile_info: torch.Tensor, n_q_heads: int, n_kv_heads: int,
                             out: Optional[torch.Tensor] = None, scale: Optional[float] = None,
-                            status: Optional[torch.Tensor] = None) -> torch.Tensor:
+                            status: Optional[torch.Tensor] = None,
+                            tile_rows: Optional[int] = None) -> torch.Tensor:
     """Causal prefill attention of chunks that continue cached sequences (the
     tcgen05 kernel's paged variant): queries from ``qkv``, keys and values of
     the whole context -- this chunk's included, already written to the cache
@@ -233,7 +240,8 @@ def prefill_attention_paged(qkv: torch.Tensor, k_cache: torch.Tensor, v_cache: t
     if out is None:
         out = torch.empty(qkv.shape[0], n_q_heads * 128, dtype=qkv.dtype, device=qkv.device)
     _C.prefill_attention_paged(qkv, k_cache, v_cache, block_tables, out, tile_info, n_q_heads, n_kv_heads,
-                               scale if scale is not None else 1.0 / math.sqrt(128), status)
+                               scale if scale is not None else 1.0 / math.sqrt(128), status,
+                               tile_rows or PREFILL_TILE)
     _n()
     return out
 

@@ -24,9 +24,10 @@ def dev():
 
 
 @pytest.mark.parametrize("rows", [[(0, 100)], [(64, 128)], [(1000, 300), (17, 5)], [(2000, 1), (130, 513)],
-                                  [(5, 64), (0, 200), (4000, 129)]])
+                                  [(5, 64), (0, 200), (4000, 129)], [(2048, 2048)], [(50, 300)]])
 @pytest.mark.parametrize("G", [4, 1])
-def test_paged_prefill_attention(dev, rows, G):
+@pytest.mark.parametrize("tile", [256, 128])
+def test_paged_prefill_attention(dev, rows, G, tile):
     from connex_b200 import ops
     from connex_b200.ops import reference as R
     Hkv, BS, NB = 2, 16, 1024
@@ -48,9 +49,9 @@ def test_paged_prefill_attention(dev, rows, G):
             bt[b, last] = NB - 1
             break
     qkv = _rnd(T, (Hq + 2 * Hkv) * 128, dev=dev, seed=5)
-    ti = ops.prefill_tile_info(n_new, dev, ctx=ctx)
+    ti = ops.prefill_tile_info(n_new, dev, ctx=ctx, tile_rows=tile)
     st = ops.new_status(dev)
-    out = ops.prefill_attention_paged(qkv, kc, vc, bt, ti, Hq, Hkv, status=st)
+    out = ops.prefill_attention_paged(qkv, kc, vc, bt, ti, Hq, Hkv, status=st, tile_rows=tile)
     torch.cuda.synchronize()
     ops.check_status(st, "prefill_attention_paged")
     ref = R.paged_prefill_attention(qkv[:, :Hq * 128].view(T, Hq, 128), kc, vc, bt, ctx, n_new)

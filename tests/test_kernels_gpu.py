@@ -187,17 +187,20 @@ def test_embedding_argmax(dev):
     assert torch.equal(ops.argmax(logits).long(), logits.float().argmax(-1))
 
 
-@pytest.mark.parametrize("lens", [[1], [128], [100, 37, 1], [513, 130, 7], [1100]])
+@pytest.mark.parametrize("lens", [[1], [128], [100, 37, 1], [513, 130, 7], [1100], [300, 256], [4096]])
 @pytest.mark.parametrize("G", [4, 1])
-def test_prefill_attention(dev, lens, G):
+@pytest.mark.parametrize("tile", [256, 128])
+def test_prefill_attention(dev, lens, G, tile):
+    """Both kernels (two 128-row Q tiles per CTA, or one) against the fp32
+    reference: partial and empty second tiles, a 32-key-tile sequence."""
     from connex_b200 import ops
     from connex_b200.ops import reference as R
     Hkv = 2
     Hq, T = Hkv * G, sum(lens)
     qkv = _rnd(T, (Hq + 2 * Hkv) * 128, dev=dev, seed=31)
-    ti = ops.prefill_tile_info(lens, dev)
+    ti = ops.prefill_tile_info(lens, dev, tile_rows=tile)
     st = ops.new_status(dev)
-    out = ops.prefill_attention(qkv, ti, Hq, Hkv, status=st)
+    out = ops.prefill_attention(qkv, ti, Hq, Hkv, status=st, tile_rows=tile)
     torch.cuda.synchronize()
     ops.check_status(st, "prefill_attention")
     q = qkv[:, :Hq * 128].view(T, Hq, 128)
@@ -206,8 +209,9 @@ def test_prefill_attention(dev, lens, G):
     _close(out.view(T, Hq, 128), R.causal_attention(q, k, v, lens))
 
 
-@pytest.mark.parametrize("split", [2, 3])
-def test_prefill_attention_with_fma_pipe_exponentials(dev, split):
+@pytest.mark.parametrize("split", [2, 4])
+@pytest.mark.parametrize("tile", [256, 128])
+def test_prefill_attention_with_fma_pipe_exponentials(dev, split, tile):
     """Part of the softmax's 2^x on the FMA pipe (own cubic for 2^f): the
     output stays within the fp32 reference's tolerance."""
     from connex_b200 import ops
@@ -215,10 +219,10 @@ def test_prefill_attention_with_fma_pipe_exponentials(dev, split):
     lens, Hkv, G = [513, 130, 7], 2, 4
     Hq, T = Hkv * G, sum(lens)
     qkv = _rnd(T, (Hq + 2 * Hkv) * 128, dev=dev, seed=41)
-    ti = ops.prefill_tile_info(lens, dev)
+    ti = ops.prefill_tile_info(lens, dev, tile_rows=tile)
     try:
         ops._C.attention_exp_split(split)
-        out = ops.prefill_attention(qkv, ti, Hq, Hkv)
+        out = ops.prefill_attention(qkv, ti, Hq, Hkv, tile_rows=tile)
         torch.cuda.synchronize()
     finally:
         ops._C.attention_exp_split(0)
