@@ -301,9 +301,11 @@ def case_decode_step(dev, B=1, ctx=1024, graphs=True):
 CASES = {"gemm": lambda d: case_gemm(d), "gemm_qkv": lambda d: case_gemm(d, 8192, 6144, 4096),
          "gemm_silu": lambda d: case_gemm(d, 8192, 28672, 4096, silu=True), "attn": case_attn,
          "attn_paged": case_attn_paged, "attn_t128": lambda d: case_attn(d, tile=128),
+         "attn_t256": lambda d: case_attn(d, tile=256),
          "attn_paged_t128": lambda d: case_attn_paged(d, tile=128),
-         "attn_2x8192": lambda d: case_attn(d, n_seq=2, L=8192),
+         "attn_paged_t256": lambda d: case_attn_paged(d, tile=256),
          "attn_2x8192_t128": lambda d: case_attn(d, n_seq=2, L=8192, tile=128),
+         "attn_2x8192_t256": lambda d: case_attn(d, n_seq=2, L=8192, tile=256),
          "attn_cudnn_2x8192": lambda d: case_attn_library(d, "cudnn", n_seq=2, L=8192), "attn_cudnn": lambda d: case_attn_library(d, "cudnn"),
          "attn_torch_flash": lambda d: case_attn_library(d, "flash"),
          "decode_attn": case_decode_attn, "kv_push": case_kv_push, "wsync": case_wsync, "ep_gemm": case_ep_gemm,
@@ -343,6 +345,8 @@ def main() -> None:
         work["check"]()
     hbm, tf, src = _peaks()
     res = {"case": a.case, "ms": round(ms, 4)}
+    if a.exp_split is not None:
+        res["exp_split"] = a.exp_split
     if a.case in NEEDS_ARGS:
         res.update({"ctas": a.ctas, "pull": a.pull, "ce": a.ce})
     if "flops" in work:

@@ -132,7 +132,7 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
   uint64_t* v_empty = bars + 14;  // [2]
   uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 16);
 
-  const int tile = n_tiles - 1 - (int)blockIdx.x;  // heaviest (latest) tiles first
+  const int tile = (int)blockIdx.x;  // tile_info lists the heaviest tiles first
   const int h = blockIdx.y;
   const int* ti = tile_info + tile * (PAGED ? 5 : 3);
   const int seq_start = ti[0];                    // first row of the sequence's new tokens in QKV
@@ -427,12 +427,13 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
 }
 
 // ---------------------------------------------------------------------------
-// Two Q tiles per CTA.  One CTA per SM holds 256 query rows of one head as two
-// 128-row tiles X = 0, 1 that share every 128-key K/V tile, and the whole
-// tensor memory: S_X = Q_X.K_j^T (128 f32 columns each) and O_X (128 each).
-// P_X is written back over the first 64 columns of S_X as bf16 pairs and the
-// P.V MMA reads it from there (A operand in tensor memory), so the softmax
-// stores nothing to shared memory.  The MMA thread issues, per key tile j:
+// Two Q tiles per CTA, persistent.  One CTA per SM holds 256 query rows of
+// one head as two 128-row tiles X = 0, 1 that share every 128-key K/V tile,
+// and the whole tensor memory: S_X = Q_X.K_j^T (128 f32 columns each) and O_X
+// (128 each).  P_X is written back over the first 64 columns of S_X as bf16
+// pairs and the P.V MMA reads it from there (A operand in tensor memory), so
+// the softmax stores nothing to shared memory.  The MMA thread issues, per
+// key tile j:
 //   P_0.V_j, Q_0.K_{j+1}^T   once softmax 0 has written P_0(j),
 //   P_1.V_j, Q_1.K_{j+1}^T   once softmax 1 has written P_1(j),
 // so the tensor core runs one tile's P.V and next scores while the other
@@ -440,13 +441,19 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
 // one thread execute in issue order: Q_X.K_{j+1}^T overwrites S_X only after
 // P_X(j).V_j has read it, and the commit of S_X(j+1) also marks P_X(j).V_j
 // complete, so the softmax may rescale O_X as soon as it sees S_X(j+1).
+// The grid is one CTA per SM; each walks work items (256 query rows x one
+// head, heaviest first) in a fixed stride.  The rings and the tensor memory
+// carry over: the next item's Q loads as soon as the last Q.K^T of a tile is
+// done, its first scores are computed while the softmax warps still store
+// the previous item's O, and the next P.V (which overwrites O_X) waits for
+// P_X(0) -- which that warpgroup writes only after its epilogue read O_X.
 // Warps: 0 TMA producer, 1 MMA issuer, 2-5 softmax of tile 0, 6-9 of tile 1
 // (warp w reaches tensor-memory lanes 32 (w % 4) .. + 31).
 namespace fap {
 constexpr int D = 128;
 constexpr int BM = 128;                      // rows of one Q tile
 constexpr int BN = 128;                      // keys of one K/V tile
-constexpr int ROWS = 2 * BM;                 // query rows of a CTA
+constexpr int ROWS = 2 * BM;                 // query rows of a work item
 constexpr int THREADS = 320;
 constexpr int HALF_Q = BM * 64 * 2;          // [128 rows x 64 dims]: 16 KB
 constexpr int HALF_KV = BN * 64 * 2;         // [128 keys x 64 dims]: 16 KB
@@ -460,6 +467,39 @@ constexpr int SMEM = OFF_BAR + 256;          // 192.25 KB
 constexpr int TMEM_COLS = 512;
 constexpr int BPT = BN / 16;                 // paged: 16-token cache blocks per key tile
 static_assert(SMEM <= 227 * 1024, "shared memory");
+
+// One work item: 256 query rows of a sequence's new tokens, one query head.
+struct Item {
+  int seq_start, seq_len, q0, ctx, total, h, g, nkv;
+  int nt[2];          // key tiles that Q tile X takes part in (0: the tile lies past the sequence end)
+  const int* bt;      // paged: the sequence's block table
+};
+template <bool PAGED>
+__device__ __forceinline__ Item item_of(int w, const int* __restrict__ tile_info, int n_tiles, int Hq, int Hkv,
+                                        const int* __restrict__ block_tables, int bt_stride) {
+  Item it;
+  const int tile = w / Hq;   // tile_info lists the heaviest tiles first
+  it.h = w - tile * Hq;
+  const int* ti = tile_info + tile * (PAGED ? 5 : 3);
+  it.seq_start = ti[0];
+  it.seq_len = ti[1];
+  it.q0 = ti[2];
+  it.ctx = PAGED ? ti[3] : 0;
+  it.bt = PAGED ? block_tables + (size_t)ti[4] * bt_stride : nullptr;
+  it.total = it.ctx + it.seq_len;
+  it.g = it.h / (Hq / Hkv);
+#pragma unroll
+  for (int x = 0; x < 2; ++x) {
+    const int r0 = it.q0 + x * BM;
+    it.nt[x] = r0 < it.seq_len ? (min(it.total, it.ctx + r0 + BM) + BN - 1) / BN : 0;
+  }
+  it.nkv = max(it.nt[0], it.nt[1]);
+  return it;
+}
+// Item of round k for CTA b of G: rounds alternate direction (0..G-1, then
+// G-1..0), so over the heaviest-first list every CTA takes alternately
+// heavier and lighter positions of consecutive rounds.
+__device__ __forceinline__ int item_at(int k, int b, int G) { return k * G + ((k & 1) ? G - 1 - b : b); }
 }  // namespace fap
 
 template <bool PAGED, int EMU>
@@ -476,46 +516,31 @@ __global__ void __launch_bounds__(fap::THREADS, 1)
     return;
   }
   uint64_t* bars = reinterpret_cast<uint64_t*>(smem + OFF_BAR);
-  uint64_t* q_full = bars + 0;
-  uint64_t* k_full = bars + 1;    // [2 stages]
-  uint64_t* k_empty = bars + 3;   // [2]  committed once both tiles' Q.K^T of the stage are done
-  uint64_t* v_full = bars + 5;    // [2]
-  uint64_t* v_empty = bars + 7;   // [2]  committed once both tiles' P.V of the stage are done
-  uint64_t* s_full = bars + 9;    // [tile]  S_X(j) ready; after the tile's last P.V: O_X final
-  uint64_t* p_full = bars + 11;   // [tile]  P_X(j) in tensor memory, O_X rescaled (128 arrivals)
-  uint64_t* drain = bars + 13;
-  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 14);
-
-  const int tile = n_tiles - 1 - (int)blockIdx.x;  // heaviest (latest) tiles first
-  const int h = blockIdx.y;
-  const int* ti = tile_info + tile * (PAGED ? 5 : 3);
-  const int seq_start = ti[0];                    // first row of the sequence's new tokens in QKV
-  const int seq_len = ti[1];                      // its new tokens
-  const int q0 = ti[2];                           // first query of this CTA (among the new tokens)
-  const int ctx = PAGED ? ti[3] : 0;              // tokens already in the cache before them
-  const int* bt = PAGED ? block_tables + (size_t)ti[4] * bt_stride : nullptr;
-  const int total = ctx + seq_len;
-  const int g = h / (Hq / Hkv);
-  // key tiles that Q tile X takes part in (none for a tile past the sequence end)
-  int nt[2];
-#pragma unroll
-  for (int x = 0; x < 2; ++x) {
-    const int r0 = q0 + x * BM;
-    nt[x] = r0 < seq_len ? (min(total, ctx + r0 + BM) + BN - 1) / BN : 0;
-  }
-  const int nkv = max(nt[0], nt[1]);
-  const int qcol = h * D, kcol = (Hq + g) * D, vcol = (Hq + Hkv + g) * D;
+  uint64_t* q_full = bars + 0;    // [tile]
+  uint64_t* q_empty = bars + 2;   // [tile]  committed after the item's last Q_X.K^T
+  uint64_t* k_full = bars + 4;    // [2 stages]
+  uint64_t* k_empty = bars + 6;   // [2]  committed once both tiles' Q.K^T of the stage are done
+  uint64_t* v_full = bars + 8;    // [2]
+  uint64_t* v_empty = bars + 10;  // [2]  committed once both tiles' P.V of the stage are done
+  uint64_t* s_full = bars + 12;   // [tile]  S_X(j) ready
+  uint64_t* p_full = bars + 14;   // [tile]  P_X(j) in tensor memory, O_X rescaled (128 arrivals)
+  uint64_t* o_full = bars + 16;   // [tile]  O_X of the item final
+  uint64_t* drain = bars + 18;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(bars + 19);
+  const int n_items = n_tiles * Hq;
 
   const int warp = warp_id(), lane = lane_id();
   if (warp == 0 && lane == 0) {
-    mbar_init(q_full, 1);
     for (int s = 0; s < 2; ++s) {
+      mbar_init(&q_full[s], 1);
+      mbar_init(&q_empty[s], 1);
       mbar_init(&k_full[s], 1);
       mbar_init(&k_empty[s], 1);
       mbar_init(&v_full[s], 1);
       mbar_init(&v_empty[s], 1);
       mbar_init(&s_full[s], 1);
       mbar_init(&p_full[s], 128);
+      mbar_init(&o_full[s], 1);
     }
     mbar_init(drain, 1);
     fence_barrier_init();
@@ -536,73 +561,85 @@ __global__ void __launch_bounds__(fap::THREADS, 1)
 
   if (warp == 0) {
     if (lane == 0) {
-      mbar_arrive_expect_tx(q_full, 2 * TILE_Q);
+      bool good = true;
+      uint32_t kv = 0;   // key tiles loaded so far: ring position of the item's tile 0
+      for (int n_it = 0, w = item_at(0, blockIdx.x, gridDim.x); w < n_items && good;
+           ++n_it, w = item_at(n_it, blockIdx.x, gridDim.x)) {
+        const Item it = item_of<PAGED>(w, tile_info, n_tiles, Hq, Hkv, block_tables, bt_stride);
+        const int qcol = it.h * D, kcol = (Hq + it.g) * D, vcol = (Hq + Hkv + it.g) * D;
 #pragma unroll
-      for (int x = 0; x < 2; ++x) {   // rows past the tensor end are zero-filled, past the sequence unused
-        tma_load_2d(smem + OFF_Q + x * TILE_Q, &tmq, q_full, qcol, seq_start + q0 + x * BM);
-        tma_load_2d(smem + OFF_Q + x * TILE_Q + HALF_Q, &tmq, q_full, qcol + 64, seq_start + q0 + x * BM);
-      }
-      // paged: cache rows of the eight 16-token blocks of a key tile (tile j's
-      // block ids are fetched one tile ahead so their loads are in flight)
-      const int nblk = (total + 15) / 16;
-      auto rows_of = [&](int j, int (&r)[BPT]) {
-#pragma unroll
-        for (int i = 0; i < BPT; ++i) {
-          const int b = j * BPT + i;
-          r[i] = (bt[b < nblk ? b : 0] * Hkv + g) * 16;  // past the end: any valid block (masked)
+        for (int x = 0; x < 2; ++x) {   // rows past the tensor end are zero-filled, past the sequence unused
+          if (!mbar_wait(&q_empty[x], (n_it & 1) ^ 1, status)) { good = false; break; }
+          mbar_arrive_expect_tx(&q_full[x], TILE_Q);
+          tma_load_2d(smem + OFF_Q + x * TILE_Q, &tmq, &q_full[x], qcol, it.seq_start + it.q0 + x * BM);
+          tma_load_2d(smem + OFF_Q + x * TILE_Q + HALF_Q, &tmq, &q_full[x], qcol + 64,
+                      it.seq_start + it.q0 + x * BM);
         }
-      };
-      auto load_tile = [&](const CUtensorMap* map, uint8_t* buf, uint64_t* bar, int col, int j, const int (&r)[BPT]) {
-        if constexpr (PAGED) {
+        if (!good) break;
+        // paged: cache rows of the eight 16-token blocks of a key tile (tile j's
+        // block ids are fetched one tile ahead so their loads are in flight)
+        const int nblk = (it.total + 15) / 16;
+        auto rows_of = [&](int j, int (&r)[BPT]) {
 #pragma unroll
           for (int i = 0; i < BPT; ++i) {
-            tma_load_2d(buf + i * 2048, map, bar, 0, r[i]);
-            tma_load_2d(buf + HALF_KV + i * 2048, map, bar, 64, r[i]);
+            const int b = j * BPT + i;
+            r[i] = (it.bt[b < nblk ? b : 0] * Hkv + it.g) * 16;  // past the end: any valid block (masked)
           }
-        } else {
-          tma_load_2d(buf, map, bar, col, seq_start + j * BN);
-          tma_load_2d(buf + HALF_KV, map, bar, col + 64, seq_start + j * BN);
-        }
-      };
-      int r_cur[BPT] = {}, r_prev[BPT] = {}, r_next[BPT] = {};
-      if (PAGED) rows_of(0, r_cur);
-      auto load_k = [&](int j) -> bool {
-        const int s = j & 1;
-        if (!mbar_wait(&k_empty[s], ((j >> 1) & 1) ^ 1, status)) return false;
-        mbar_arrive_expect_tx(&k_full[s], TILE_KV);
-        load_tile(&tmk, smem + OFF_K + s * TILE_KV, &k_full[s], kcol, j, r_cur);
-        return true;
-      };
-      auto load_v = [&](int j, const int (&r)[BPT]) -> bool {
-        const int s = j & 1;
-        if (!mbar_wait(&v_empty[s], ((j >> 1) & 1) ^ 1, status)) return false;
-        mbar_arrive_expect_tx(&v_full[s], TILE_KV);
-        load_tile(&tmv, smem + OFF_V + s * TILE_KV, &v_full[s], vcol, j, r);
-        return true;
-      };
-      bool good = true;
-      for (int j = 0; j < nkv && good; ++j) {   // K_j goes out before V_{j-1}
-        good = load_k(j);
-        if (PAGED && j + 1 < nkv) rows_of(j + 1, r_next);
-        if (good && j >= 1) good = load_v(j - 1, r_prev);
+        };
+        auto load_tile = [&](const CUtensorMap* map, uint8_t* buf, uint64_t* bar, int col, int j,
+                             const int (&r)[BPT]) {
+          if constexpr (PAGED) {
 #pragma unroll
-        for (int i = 0; i < BPT; ++i) {
-          r_prev[i] = r_cur[i];
-          r_cur[i] = r_next[i];
+            for (int i = 0; i < BPT; ++i) {
+              tma_load_2d(buf + i * 2048, map, bar, 0, r[i]);
+              tma_load_2d(buf + HALF_KV + i * 2048, map, bar, 64, r[i]);
+            }
+          } else {
+            tma_load_2d(buf, map, bar, col, it.seq_start + j * BN);
+            tma_load_2d(buf + HALF_KV, map, bar, col + 64, it.seq_start + j * BN);
+          }
+        };
+        int r_cur[BPT] = {}, r_prev[BPT] = {}, r_next[BPT] = {};
+        if (PAGED) rows_of(0, r_cur);
+        auto load_k = [&](int j) -> bool {
+          const uint32_t u = kv + j, s = u & 1;
+          if (!mbar_wait(&k_empty[s], ((u >> 1) & 1) ^ 1, status)) return false;
+          mbar_arrive_expect_tx(&k_full[s], TILE_KV);
+          load_tile(&tmk, smem + OFF_K + s * TILE_KV, &k_full[s], kcol, j, r_cur);
+          return true;
+        };
+        auto load_v = [&](int j, const int (&r)[BPT]) -> bool {
+          const uint32_t u = kv + j, s = u & 1;
+          if (!mbar_wait(&v_empty[s], ((u >> 1) & 1) ^ 1, status)) return false;
+          mbar_arrive_expect_tx(&v_full[s], TILE_KV);
+          load_tile(&tmv, smem + OFF_V + s * TILE_KV, &v_full[s], vcol, j, r);
+          return true;
+        };
+        for (int j = 0; j < it.nkv && good; ++j) {   // K_j goes out before V_{j-1}
+          good = load_k(j);
+          if (PAGED && j + 1 < it.nkv) rows_of(j + 1, r_next);
+          if (good && j >= 1) good = load_v(j - 1, r_prev);
+#pragma unroll
+          for (int i = 0; i < BPT; ++i) {
+            r_prev[i] = r_cur[i];
+            r_cur[i] = r_next[i];
+          }
         }
+        if (good && it.nkv > 0) good = load_v(it.nkv - 1, r_prev);
+        kv += it.nkv;
       }
-      if (good && nkv > 0) load_v(nkv - 1, r_prev);
     }
     __syncwarp();
   } else if (warp == 1) {
     if (lane == 0) {
       constexpr uint32_t IDESC_QK = umma_idesc_bf16(BM, BN);
       constexpr uint32_t IDESC_PV = umma_idesc_bf16_bmn(BM, D);
-      bool ok = mbar_wait(q_full, 0, status);
-      bool issued = false;
-      auto qk = [&](int x, int j) {  // S_x = Q_x.K_j^T, then S_x(j) is signalled
+      bool ok = true, issued = false;
+      uint32_t kv = 0;               // ring position of the item's tile 0
+      uint32_t pf[2] = {0u, 0u};     // p_full phases consumed per tile
+      auto qk = [&](int x, uint32_t u) {  // S_x = Q_x.K_u^T, then S_x is signalled
         const uint32_t sQ = smem_u32(smem + OFF_Q + x * TILE_Q);
-        const uint32_t sK = smem_u32(smem + OFF_K + (j & 1) * TILE_KV);
+        const uint32_t sK = smem_u32(smem + OFF_K + (u & 1) * TILE_KV);
 #pragma unroll
         for (int k = 0; k < D / 16; ++k) {
           umma_bf16(tmem + x * BN, umma_desc_sw128(sQ + (k >> 2) * HALF_Q + (k & 3) * 32),
@@ -610,43 +647,54 @@ __global__ void __launch_bounds__(fap::THREADS, 1)
         }
         umma_commit(&s_full[x]);
       };
-      auto pv = [&](int x, int j) {  // O_x += P_x.V_j, P_x in the first 64 columns of S_x
-        const uint32_t sV = smem_u32(smem + OFF_V + (j & 1) * TILE_KV);
+      auto pv = [&](int x, uint32_t u, bool first) {  // O_x (+)= P_x.V_u, P_x in the first 64 columns of S_x
+        const uint32_t sV = smem_u32(smem + OFF_V + (u & 1) * TILE_KV);
 #pragma unroll
         for (int kk = 0; kk < BN / 16; ++kk) {
           umma_bf16_ts(tmem + 2 * BN + x * D, tmem + x * BN + kk * 8,
-                       fatc::umma_desc_sw128_mn(sV + kk * 2048, HALF_KV), IDESC_PV, (j > 0 || kk > 0) ? 1u : 0u);
+                       fatc::umma_desc_sw128_mn(sV + kk * 2048, HALF_KV), IDESC_PV, (!first || kk > 0) ? 1u : 0u);
         }
       };
-      if (ok && nkv > 0) {
-        ok = mbar_wait(&k_full[0], 0, status);
-        if (ok) {
-          tc_fence_after();
-          for (int x = 0; x < 2; ++x)
-            if (nt[x] > 0) qk(x, 0);
-          issued = true;
-          umma_commit(&k_empty[0]);
+      for (int n_it = 0, w = item_at(0, blockIdx.x, gridDim.x); w < n_items && ok;
+           ++n_it, w = item_at(n_it, blockIdx.x, gridDim.x)) {
+        const Item it = item_of<PAGED>(w, tile_info, n_tiles, Hq, Hkv, block_tables, bt_stride);
+        for (int x = 0; x < 2 && ok; ++x) ok = mbar_wait(&q_full[x], n_it & 1, status);
+        if (!ok) break;
+        if (!mbar_wait(&k_full[kv & 1], (kv >> 1) & 1, status)) { ok = false; break; }
+        tc_fence_after();
+        for (int x = 0; x < 2; ++x) {
+          if (it.nt[x] == 0) continue;
+          qk(x, kv);
+          if (it.nt[x] == 1) umma_commit(&q_empty[x]);   // Q_x done with
         }
-      }
-      for (int j = 0; j < nkv && ok; ++j) {
-        const int s = j & 1;
-        if (!mbar_wait(&v_full[s], (j >> 1) & 1, status)) { ok = false; break; }
-        for (int x = 0; x < 2 && ok; ++x) {
-          if (j >= nt[x]) continue;
-          if (!mbar_wait(&p_full[x], j & 1, status)) { ok = false; break; }
-          tc_fence_after();
-          pv(x, j);
-          if (j + 1 < nt[x]) {
-            if (!mbar_wait(&k_full[(j + 1) & 1], ((j + 1) >> 1) & 1, status)) { ok = false; break; }
+        issued = true;
+        umma_commit(&k_empty[kv & 1]);
+        for (int j = 0; j < it.nkv && ok; ++j) {
+          const uint32_t u = kv + j, s = u & 1;
+          if (!mbar_wait(&v_full[s], (u >> 1) & 1, status)) { ok = false; break; }
+          for (int x = 0; x < 2 && ok; ++x) {
+            if (j >= it.nt[x]) continue;
+            if (!mbar_wait(&p_full[x], pf[x] & 1, status)) { ok = false; break; }
+            ++pf[x];
             tc_fence_after();
-            qk(x, j + 1);
-          } else {
-            umma_commit(&s_full[x]);   // O_x final
+            pv(x, u, j == 0);
+            if (j + 1 < it.nt[x]) {
+              if (!mbar_wait(&k_full[(u + 1) & 1], ((u + 1) >> 1) & 1, status)) { ok = false; break; }
+              tc_fence_after();
+              qk(x, u + 1);
+              if (j + 2 == it.nt[x]) umma_commit(&q_empty[x]);
+            } else {
+              umma_commit(&o_full[x]);
+            }
           }
+          if (!ok) break;
+          umma_commit(&v_empty[s]);                                  // both tiles' P.V of tile u
+          if (j + 1 < it.nkv) umma_commit(&k_empty[(u + 1) & 1]);    // both tiles' Q.K^T of tile u+1
         }
         if (!ok) break;
-        umma_commit(&v_empty[s]);                                // both tiles' P.V_j
-        if (j + 1 < nkv) umma_commit(&k_empty[(j + 1) & 1]);     // both tiles' Q.K_{j+1}^T
+        for (int x = 0; x < 2; ++x)
+          if (it.nt[x] == 0) umma_commit(&q_empty[x]);
+        kv += it.nkv;
       }
       if (!ok && issued) {
         umma_commit(drain);
@@ -658,123 +706,136 @@ __global__ void __launch_bounds__(fap::THREADS, 1)
     const int x = (warp - 2) >> 2;        // Q tile of this warpgroup
     const int q = warp & 3;               // its tensor-memory lane quadrant
     const int row = q * 32 + lane;
-    const int r0 = q0 + x * BM;           // first query of the tile
-    const int qpos = ctx + r0 + row;      // position in the sequence
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
     const uint32_t tS = tmem + x * BN + lane_off, tO = tmem + 2 * BN + x * D + lane_off;
-    const int n = nt[x];
-    const int zero_x = nt[0] == nkv ? 0 : 1;   // the tile whose P.V reads the last V tile first
-    float m = -INFINITY, l = 0.f;
+    uint32_t sw = 0, ow = 0;              // s_full / o_full phases waited
+    uint32_t kv = 0;                      // ring position of the item's tile 0
     bool ok = true;
-    for (int j = 0; j < n; ++j) {
-      if (!mbar_wait(&s_full[x], j & 1, status)) { ok = false; break; }
-      tc_fence_after();
-      uint32_t r[BN];
+    for (int k = 0, w = item_at(0, blockIdx.x, gridDim.x); w < n_items && ok;
+         ++k, w = item_at(k, blockIdx.x, gridDim.x)) {
+      const Item it = item_of<PAGED>(w, tile_info, n_tiles, Hq, Hkv, block_tables, bt_stride);
+      const int r0 = it.q0 + x * BM;      // first query of the tile
+      const int qpos = it.ctx + r0 + row; // position in the sequence
+      const int n = it.nt[x];
+      const int zero_x = it.nt[0] == it.nkv ? 0 : 1;   // the tile whose P.V reads the last V tile first
+      float m = -INFINITY, l = 0.f;
+      for (int j = 0; j < n; ++j) {
+        if (!mbar_wait(&s_full[x], sw & 1, status)) { ok = false; break; }
+        ++sw;
+        tc_fence_after();
+        uint32_t r[BN];
 #pragma unroll
-      for (int c = 0; c < BN / 32; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
-      tmem_ld_wait();
-      const int key0 = j * BN;
-      // only tiles that cross the diagonal or the sequence end pay for the
-      // mask (one compare per score against the row's last valid key)
-      const bool mask = (key0 + BN - 1 > ctx + r0) || (key0 + BN > total);
-      if (mask) {
-        const int lim = min(qpos + 1, total) - key0;  // keys [0, lim) of the tile are valid for this row
+        for (int c = 0; c < BN / 32; ++c) tmem_ld32(tS + c * 32, *reinterpret_cast<uint32_t(*)[32]>(&r[c * 32]));
+        tmem_ld_wait();
+        const int key0 = j * BN;
+        // only tiles that cross the diagonal or the sequence end pay for the
+        // mask (one compare per score against the row's last valid key)
+        const bool mask = (key0 + BN - 1 > it.ctx + r0) || (key0 + BN > it.total);
+        if (mask) {
+          const int lim = min(qpos + 1, it.total) - key0;  // keys [0, lim) of the tile are valid for this row
 #pragma unroll
-        for (int e = 0; e < BN; ++e)
-          if (e >= lim) r[e] = __float_as_uint(-INFINITY);
-      }
-      // raw scores stay unscaled (scale > 0 commutes with the max); four
-      // independent running maxima, two scores per three-input max
-      float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
-#pragma unroll
-      for (int e = 0; e < BN; e += 2)
-        mx4[(e >> 1) & 3] = fmaxf(mx4[(e >> 1) & 3], fmaxf(__uint_as_float(r[e]), __uint_as_float(r[e + 1])));
-      const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * scale_log2;
-      float m_new = m;
-      bool resc = false;
-      if (j == 0 || mx > m + RESCALE_THRESHOLD) {  // lazy rescale
-        m_new = fmaxf(m, mx);
-        resc = (j > 0);
-      }
-      const float base = (m_new == -INFINITY) ? 0.f : m_new;
-      uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
-      const uint64_t sc2 = f32x2(scale_log2, scale_log2), nb2 = f32x2(-base, -base);
-#pragma unroll
-      for (int c = 0; c < BN / 32; ++c) {   // 32 keys -> 16 bf16 pairs -> 16 columns of S_x
-        uint32_t pk[16];
-#pragma unroll
-        for (int e2 = 0; e2 < 16; ++e2) {
-          const int e = c * 32 + 2 * e2;
-          const uint64_t t2 = fma_f32x2(f32x2(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), sc2, nb2);
-          uint64_t p2;
-          switch (e2 & 3) {   // compile-time after unrolling: each pair's unit is fixed
-            case 0: p2 = fatc::exp2_pair<EMU, 0>(t2); break;
-            case 1: p2 = fatc::exp2_pair<EMU, 1>(t2); break;
-            case 2: p2 = fatc::exp2_pair<EMU, 2>(t2); break;
-            default: p2 = fatc::exp2_pair<EMU, 3>(t2); break;
-          }
-          sum2[e2 & 3] = add_f32x2(sum2[e2 & 3], p2);
-          pk[e2] = pack_bf16x2(lo_f32(p2), hi_f32(p2));
+          for (int e = 0; e < BN; ++e)
+            if (e >= lim) r[e] = __float_as_uint(-INFINITY);
         }
-        tmem_st16(tS + c * 16, pk);
+        // raw scores stay unscaled (scale > 0 commutes with the max); four
+        // independent running maxima, two scores per three-input max
+        float mx4[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+        for (int e = 0; e < BN; e += 2)
+          mx4[(e >> 1) & 3] = fmaxf(mx4[(e >> 1) & 3], fmaxf(__uint_as_float(r[e]), __uint_as_float(r[e + 1])));
+        const float mx = fmaxf(fmaxf(mx4[0], mx4[1]), fmaxf(mx4[2], mx4[3])) * scale_log2;
+        float m_new = m;
+        bool resc = false;
+        if (j == 0 || mx > m + RESCALE_THRESHOLD) {  // lazy rescale
+          m_new = fmaxf(m, mx);
+          resc = (j > 0);
+        }
+        const float base = (m_new == -INFINITY) ? 0.f : m_new;
+        uint64_t sum2[4] = {0ull, 0ull, 0ull, 0ull};
+        const uint64_t sc2 = f32x2(scale_log2, scale_log2), nb2 = f32x2(-base, -base);
+#pragma unroll
+        for (int c = 0; c < BN / 32; ++c) {   // 32 keys -> 16 bf16 pairs -> 16 columns of S_x
+          uint32_t pk[16];
+#pragma unroll
+          for (int e2 = 0; e2 < 16; ++e2) {
+            const int e = c * 32 + 2 * e2;
+            const uint64_t t2 = fma_f32x2(f32x2(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), sc2, nb2);
+            uint64_t p2;
+            switch (e2 & 3) {   // compile-time after unrolling: each pair's unit is fixed
+              case 0: p2 = fatc::exp2_pair<EMU, 0>(t2); break;
+              case 1: p2 = fatc::exp2_pair<EMU, 1>(t2); break;
+              case 2: p2 = fatc::exp2_pair<EMU, 2>(t2); break;
+              default: p2 = fatc::exp2_pair<EMU, 3>(t2); break;
+            }
+            sum2[e2 & 3] = add_f32x2(sum2[e2 & 3], p2);
+            pk[e2] = pack_bf16x2(lo_f32(p2), hi_f32(p2));
+          }
+          tmem_st16(tS + c * 16, pk);
+        }
+        const uint64_t s4 = add_f32x2(add_f32x2(sum2[0], sum2[1]), add_f32x2(sum2[2], sum2[3]));
+        const float sum = lo_f32(s4) + hi_f32(s4);
+        const float alpha = resc ? fatc::fast_exp2(m - m_new) : 1.f;
+        l = l * alpha + sum;
+        m = m_new;
+        if (j >= 1 && __any_sync(0xffffffffu, resc)) {
+          // S_x(j) was committed after P_x(j-1).V_{j-1}: O_x is complete here
+#pragma unroll 1
+          for (int c = 0; c < D / 32; ++c) {
+            uint32_t o[32];
+            tmem_ld32(tO + c * 32, o);
+            tmem_ld_wait();
+#pragma unroll
+            for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
+            tmem_st32(tO + c * 32, o);
+          }
+        }
+        if (PAGED && x == zero_x && j == it.nkv - 1 && it.total - key0 < BN) {
+          // the last tile's keys past the sequence end are cache slots nobody
+          // wrote: their P is 0, but 0 x NaN would still poison O -- zero those
+          // V rows (whole 128-byte rows, so the swizzle does not matter)
+          const uint32_t u = kv + j;
+          if (!mbar_wait(&v_full[u & 1], (u >> 1) & 1, status)) { ok = false; break; }
+          uint8_t* vb = smem + OFF_V + (u & 1) * TILE_KV;
+          const int tail = it.total - key0, nz = (BN - tail) * 8;   // 16-byte chunks per half
+          for (int t = q * 32 + lane; t < 2 * nz; t += 128) {
+            const int half = t / nz, rem = t - half * nz;
+            *reinterpret_cast<uint4*>(vb + half * HALF_KV + (tail + rem / 8) * 128 + (rem % 8) * 16) =
+                make_uint4(0u, 0u, 0u, 0u);
+          }
+          fence_proxy_async_smem();
+        }
+        tmem_st_wait();
+        tc_fence_before();
+        mbar_arrive(&p_full[x]);
       }
-      const uint64_t s4 = add_f32x2(add_f32x2(sum2[0], sum2[1]), add_f32x2(sum2[2], sum2[3]));
-      const float sum = lo_f32(s4) + hi_f32(s4);
-      const float alpha = resc ? fatc::fast_exp2(m - m_new) : 1.f;
-      l = l * alpha + sum;
-      m = m_new;
-      if (j >= 1 && __any_sync(0xffffffffu, resc)) {
-        // S_x(j) was committed after P_x(j-1).V_{j-1}: O_x is complete here
+      if (!ok) break;
+      if (n > 0) {
+        if (!mbar_wait(&o_full[x], ow & 1, status)) { ok = false; break; }
+        ++ow;
+        tc_fence_after();
+        const float inv = l > 0.f ? 1.f / l : 0.f;
+        const bool valid = r0 + row < it.seq_len;
+        __nv_bfloat16* orow = out + (size_t)(it.seq_start + r0 + row) * ldo + (size_t)it.h * D;
 #pragma unroll 1
         for (int c = 0; c < D / 32; ++c) {
           uint32_t o[32];
           tmem_ld32(tO + c * 32, o);
           tmem_ld_wait();
+          if (valid) {
 #pragma unroll
-          for (int e = 0; e < 32; ++e) o[e] = __float_as_uint(__uint_as_float(o[e]) * alpha);
-          tmem_st32(tO + c * 32, o);
-        }
-      }
-      if (PAGED && x == zero_x && j == nkv - 1 && total - key0 < BN) {
-        // the last tile's keys past the sequence end are cache slots nobody
-        // wrote: their P is 0, but 0 x NaN would still poison O -- zero those
-        // V rows (whole 128-byte rows, so the swizzle does not matter)
-        if (!mbar_wait(&v_full[j & 1], (j >> 1) & 1, status)) { ok = false; break; }
-        uint8_t* vb = smem + OFF_V + (j & 1) * TILE_KV;
-        const int tail = total - key0, nz = (BN - tail) * 8;   // 16-byte chunks per half
-        for (int t = q * 32 + lane; t < 2 * nz; t += 128) {
-          const int half = t / nz, rem = t - half * nz;
-          *reinterpret_cast<uint4*>(vb + half * HALF_KV + (tail + rem / 8) * 128 + (rem % 8) * 16) =
-              make_uint4(0u, 0u, 0u, 0u);
-        }
-        fence_proxy_async_smem();
-      }
-      tmem_st_wait();
-      tc_fence_before();
-      mbar_arrive(&p_full[x]);
-    }
-    if (ok && n > 0 && mbar_wait(&s_full[x], n & 1, status)) {
-      tc_fence_after();
-      const float inv = l > 0.f ? 1.f / l : 0.f;
-      const bool valid = r0 + row < seq_len;
-      __nv_bfloat16* orow = out + (size_t)(seq_start + r0 + row) * ldo + (size_t)h * D;
-#pragma unroll 1
-      for (int c = 0; c < D / 32; ++c) {
-        uint32_t o[32];
-        tmem_ld32(tO + c * 32, o);
-        tmem_ld_wait();
-        if (valid) {
-#pragma unroll
-          for (int v = 0; v < 4; ++v) {
-            u128 w;
-            w.x = pack_bf16x2(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
-            w.y = pack_bf16x2(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
-            w.z = pack_bf16x2(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
-            w.w = pack_bf16x2(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
-            st_v4(orow + c * 32 + v * 8, w);
+            for (int v = 0; v < 4; ++v) {
+              u128 wv;
+              wv.x = pack_bf16x2(__uint_as_float(o[8 * v + 0]) * inv, __uint_as_float(o[8 * v + 1]) * inv);
+              wv.y = pack_bf16x2(__uint_as_float(o[8 * v + 2]) * inv, __uint_as_float(o[8 * v + 3]) * inv);
+              wv.z = pack_bf16x2(__uint_as_float(o[8 * v + 4]) * inv, __uint_as_float(o[8 * v + 5]) * inv);
+              wv.w = pack_bf16x2(__uint_as_float(o[8 * v + 6]) * inv, __uint_as_float(o[8 * v + 7]) * inv);
+              st_v4(orow + c * 32 + v * 8, wv);
+            }
           }
         }
+        tc_fence_before();   // the next item's P.V overwrites O_x after this warpgroup's next arrival
       }
+      kv += it.nkv;
     }
   }
   __syncthreads();
@@ -813,7 +874,13 @@ static void launch_attn(const AttnArgs& a, cudaStream_t s) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
     attr[dev & 63] = true;
   }
-  kern<<<dim3(a.n_tiles, a.Hq), PAIR ? fap::THREADS : fatc::THREADS, smem, s>>>(
+  dim3 grid(a.n_tiles, a.Hq);
+  if (PAIR) {   // persistent: one CTA per SM over all (tile, head) items
+    static int sms[64] = {0};
+    if (sms[dev & 63] == 0) cudaDeviceGetAttribute(&sms[dev & 63], cudaDevAttrMultiProcessorCount, dev);
+    grid = dim3(min(a.n_tiles * a.Hq, sms[dev & 63]), 1);
+  }
+  kern<<<grid, PAIR ? fap::THREADS : fatc::THREADS, smem, s>>>(
       a.tq, a.tk, a.tv, reinterpret_cast<__nv_bfloat16*>(a.out), a.ldo, a.tile_info, a.n_tiles, a.Hq, a.Hkv,
       a.scale_log2, a.bt, a.bt_stride, a.status);
 }

@@ -187,24 +187,32 @@ def gather_rows(src: torch.Tensor, idx: torch.Tensor, out: Optional[torch.Tensor
 
 
 # ---------------------------------------------------------- attention
-# Query rows per CTA of the prefill attention: 256 runs two 128-row tiles per
-# CTA (one CTA per SM), 128 the one-tile kernel (two CTAs per SM, measured
-# the faster of the two on 8 x 2048).  ``prefill_tile_info`` and the
-# attention calls take the same ``tile_rows`` (both default to this).
-PREFILL_TILE = 128
+# Query rows per work item of the prefill attention: 256 runs the persistent
+# kernel with two 128-row tiles per CTA (one CTA per SM; measured faster on
+# 8 x 2048, 2 x 8192 and the paged chunk case), 128 the one-tile kernel (two
+# CTAs per SM).  ``prefill_tile_info`` and the attention calls take the same
+# ``tile_rows`` (both default to this).
+PREFILL_TILE = 256
 
 
 def prefill_tile_info(seq_lens, device, ctx=None, tile_rows: Optional[int] = None) -> torch.Tensor:
     """[n_tiles, 3] int32 (seq start row, seq length, first query of the tile);
     with ``ctx`` (tokens already in the cache per sequence, chunked prefill)
-    [n_tiles, 5] adding (context length, sequence index) for the paged kernel."""
+    [n_tiles, 5] adding (context length, sequence index) for the paged kernel.
+    Rows are ordered by work, heaviest first (query rows x keys they attend
+    to): the kernels hand them out in that order, so the last wave holds the
+    lightest tiles."""
     step = tile_rows or PREFILL_TILE
-    rows = []
+    rows, work = [], []
     start = 0
     for i, n in enumerate(seq_lens):
+        c = 0 if ctx is None else int(ctx[i])
         for q0 in range(0, n, step):
-            rows.append((start, n, q0) if ctx is None else (start, n, q0, int(ctx[i]), i))
+            rows.append((start, n, q0) if ctx is None else (start, n, q0, c, i))
+            r = min(step, n - q0)
+            work.append(r * (c + q0 + r / 2))
         start += n
+    rows = [rows[k] for k in sorted(range(len(rows)), key=lambda k: -work[k])]
     width = 3 if ctx is None else 5
     t = torch.tensor(rows if rows else [(0,) * width], dtype=torch.int32)
     if not rows:
