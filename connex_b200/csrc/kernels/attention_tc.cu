@@ -447,14 +447,17 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
 // done, its first scores are computed while the softmax warps still store
 // the previous item's O, and the next P.V (which overwrites O_X) waits for
 // P_X(0) -- which that warpgroup writes only after its epilogue read O_X.
-// Warps: 0 TMA producer, 1 MMA issuer, 2-5 softmax of tile 0, 6-9 of tile 1
-// (warp w reaches tensor-memory lanes 32 (w % 4) .. + 31).
+// Warps: 0 TMA producer, 1 MMA issuer (2, 3 idle: warpgroup granularity of
+// the register split), 4-7 softmax of tile 0, 8-11 of tile 1 (warp w reaches
+// tensor-memory lanes 32 (w % 4) .. + 31).
 namespace fap {
 constexpr int D = 128;
 constexpr int BM = 128;                      // rows of one Q tile
 constexpr int BN = 128;                      // keys of one K/V tile
 constexpr int ROWS = 2 * BM;                 // query rows of a work item
-constexpr int THREADS = 320;
+constexpr int THREADS = 384;                 // three warpgroups
+constexpr int CTRL_REGS = 88, SOFTMAX_REGS = 208;   // per thread after setmaxnreg (no spills)
+static_assert(128 * CTRL_REGS + 256 * SOFTMAX_REGS <= THREADS * 168, "register split above the launch's total");
 constexpr int HALF_Q = BM * 64 * 2;          // [128 rows x 64 dims]: 16 KB
 constexpr int HALF_KV = BN * 64 * 2;         // [128 keys x 64 dims]: 16 KB
 constexpr int TILE_Q = 2 * HALF_Q;
@@ -559,151 +562,157 @@ __global__ void __launch_bounds__(fap::THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = *tmem_slot;
 
-  if (warp == 0) {
-    if (lane == 0) {
-      bool good = true;
-      uint32_t kv = 0;   // key tiles loaded so far: ring position of the item's tile 0
-      for (int n_it = 0, w = item_at(0, blockIdx.x, gridDim.x); w < n_items && good;
-           ++n_it, w = item_at(n_it, blockIdx.x, gridDim.x)) {
-        const Item it = item_of<PAGED>(w, tile_info, n_tiles, Hq, Hkv, block_tables, bt_stride);
-        const int qcol = it.h * D, kcol = (Hq + it.g) * D, vcol = (Hq + Hkv + it.g) * D;
-#pragma unroll
-        for (int x = 0; x < 2; ++x) {   // rows past the tensor end are zero-filled, past the sequence unused
-          if (!mbar_wait(&q_empty[x], (n_it & 1) ^ 1, status)) { good = false; break; }
-          mbar_arrive_expect_tx(&q_full[x], TILE_Q);
-          tma_load_2d(smem + OFF_Q + x * TILE_Q, &tmq, &q_full[x], qcol, it.seq_start + it.q0 + x * BM);
-          tma_load_2d(smem + OFF_Q + x * TILE_Q + HALF_Q, &tmq, &q_full[x], qcol + 64,
-                      it.seq_start + it.q0 + x * BM);
-        }
-        if (!good) break;
-        // paged: cache rows of the eight 16-token blocks of a key tile (tile j's
-        // block ids are fetched one tile ahead so their loads are in flight)
-        const int nblk = (it.total + 15) / 16;
-        auto rows_of = [&](int j, int (&r)[BPT]) {
-#pragma unroll
-          for (int i = 0; i < BPT; ++i) {
-            const int b = j * BPT + i;
-            r[i] = (it.bt[b < nblk ? b : 0] * Hkv + it.g) * 16;  // past the end: any valid block (masked)
+  if (warp < 4) {
+    // producer and MMA warps need few registers: hand them to the softmax
+    // warpgroups (4 x 32 x 88 + 8 x 32 x 208 = 384 x 168, the launch total)
+    asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(CTRL_REGS));
+    if (warp == 0) {
+      if (lane == 0) {
+        bool good = true;
+        uint32_t kv = 0;   // key tiles loaded so far: ring position of the item's tile 0
+        for (int n_it = 0, w = item_at(0, blockIdx.x, gridDim.x); w < n_items && good;
+             ++n_it, w = item_at(n_it, blockIdx.x, gridDim.x)) {
+          const Item it = item_of<PAGED>(w, tile_info, n_tiles, Hq, Hkv, block_tables, bt_stride);
+          const int qcol = it.h * D, kcol = (Hq + it.g) * D, vcol = (Hq + Hkv + it.g) * D;
+  #pragma unroll
+          for (int x = 0; x < 2; ++x) {   // rows past the tensor end are zero-filled, past the sequence unused
+            if (!mbar_wait(&q_empty[x], (n_it & 1) ^ 1, status)) { good = false; break; }
+            mbar_arrive_expect_tx(&q_full[x], TILE_Q);
+            tma_load_2d(smem + OFF_Q + x * TILE_Q, &tmq, &q_full[x], qcol, it.seq_start + it.q0 + x * BM);
+            tma_load_2d(smem + OFF_Q + x * TILE_Q + HALF_Q, &tmq, &q_full[x], qcol + 64,
+                        it.seq_start + it.q0 + x * BM);
           }
-        };
-        auto load_tile = [&](const CUtensorMap* map, uint8_t* buf, uint64_t* bar, int col, int j,
-                             const int (&r)[BPT]) {
-          if constexpr (PAGED) {
-#pragma unroll
+          if (!good) break;
+          // paged: cache rows of the eight 16-token blocks of a key tile (tile j's
+          // block ids are fetched one tile ahead so their loads are in flight)
+          const int nblk = (it.total + 15) / 16;
+          auto rows_of = [&](int j, int (&r)[BPT]) {
+  #pragma unroll
             for (int i = 0; i < BPT; ++i) {
-              tma_load_2d(buf + i * 2048, map, bar, 0, r[i]);
-              tma_load_2d(buf + HALF_KV + i * 2048, map, bar, 64, r[i]);
+              const int b = j * BPT + i;
+              r[i] = (it.bt[b < nblk ? b : 0] * Hkv + it.g) * 16;  // past the end: any valid block (masked)
             }
-          } else {
-            tma_load_2d(buf, map, bar, col, it.seq_start + j * BN);
-            tma_load_2d(buf + HALF_KV, map, bar, col + 64, it.seq_start + j * BN);
-          }
-        };
-        int r_cur[BPT] = {}, r_prev[BPT] = {}, r_next[BPT] = {};
-        if (PAGED) rows_of(0, r_cur);
-        auto load_k = [&](int j) -> bool {
-          const uint32_t u = kv + j, s = u & 1;
-          if (!mbar_wait(&k_empty[s], ((u >> 1) & 1) ^ 1, status)) return false;
-          mbar_arrive_expect_tx(&k_full[s], TILE_KV);
-          load_tile(&tmk, smem + OFF_K + s * TILE_KV, &k_full[s], kcol, j, r_cur);
-          return true;
-        };
-        auto load_v = [&](int j, const int (&r)[BPT]) -> bool {
-          const uint32_t u = kv + j, s = u & 1;
-          if (!mbar_wait(&v_empty[s], ((u >> 1) & 1) ^ 1, status)) return false;
-          mbar_arrive_expect_tx(&v_full[s], TILE_KV);
-          load_tile(&tmv, smem + OFF_V + s * TILE_KV, &v_full[s], vcol, j, r);
-          return true;
-        };
-        for (int j = 0; j < it.nkv && good; ++j) {   // K_j goes out before V_{j-1}
-          good = load_k(j);
-          if (PAGED && j + 1 < it.nkv) rows_of(j + 1, r_next);
-          if (good && j >= 1) good = load_v(j - 1, r_prev);
-#pragma unroll
-          for (int i = 0; i < BPT; ++i) {
-            r_prev[i] = r_cur[i];
-            r_cur[i] = r_next[i];
-          }
-        }
-        if (good && it.nkv > 0) good = load_v(it.nkv - 1, r_prev);
-        kv += it.nkv;
-      }
-    }
-    __syncwarp();
-  } else if (warp == 1) {
-    if (lane == 0) {
-      constexpr uint32_t IDESC_QK = umma_idesc_bf16(BM, BN);
-      constexpr uint32_t IDESC_PV = umma_idesc_bf16_bmn(BM, D);
-      bool ok = true, issued = false;
-      uint32_t kv = 0;               // ring position of the item's tile 0
-      uint32_t pf[2] = {0u, 0u};     // p_full phases consumed per tile
-      auto qk = [&](int x, uint32_t u) {  // S_x = Q_x.K_u^T, then S_x is signalled
-        const uint32_t sQ = smem_u32(smem + OFF_Q + x * TILE_Q);
-        const uint32_t sK = smem_u32(smem + OFF_K + (u & 1) * TILE_KV);
-#pragma unroll
-        for (int k = 0; k < D / 16; ++k) {
-          umma_bf16(tmem + x * BN, umma_desc_sw128(sQ + (k >> 2) * HALF_Q + (k & 3) * 32),
-                    umma_desc_sw128(sK + (k >> 2) * HALF_KV + (k & 3) * 32), IDESC_QK, k > 0 ? 1u : 0u);
-        }
-        umma_commit(&s_full[x]);
-      };
-      auto pv = [&](int x, uint32_t u, bool first) {  // O_x (+)= P_x.V_u, P_x in the first 64 columns of S_x
-        const uint32_t sV = smem_u32(smem + OFF_V + (u & 1) * TILE_KV);
-#pragma unroll
-        for (int kk = 0; kk < BN / 16; ++kk) {
-          umma_bf16_ts(tmem + 2 * BN + x * D, tmem + x * BN + kk * 8,
-                       fatc::umma_desc_sw128_mn(sV + kk * 2048, HALF_KV), IDESC_PV, (!first || kk > 0) ? 1u : 0u);
-        }
-      };
-      for (int n_it = 0, w = item_at(0, blockIdx.x, gridDim.x); w < n_items && ok;
-           ++n_it, w = item_at(n_it, blockIdx.x, gridDim.x)) {
-        const Item it = item_of<PAGED>(w, tile_info, n_tiles, Hq, Hkv, block_tables, bt_stride);
-        for (int x = 0; x < 2 && ok; ++x) ok = mbar_wait(&q_full[x], n_it & 1, status);
-        if (!ok) break;
-        if (!mbar_wait(&k_full[kv & 1], (kv >> 1) & 1, status)) { ok = false; break; }
-        tc_fence_after();
-        for (int x = 0; x < 2; ++x) {
-          if (it.nt[x] == 0) continue;
-          qk(x, kv);
-          if (it.nt[x] == 1) umma_commit(&q_empty[x]);   // Q_x done with
-        }
-        issued = true;
-        umma_commit(&k_empty[kv & 1]);
-        for (int j = 0; j < it.nkv && ok; ++j) {
-          const uint32_t u = kv + j, s = u & 1;
-          if (!mbar_wait(&v_full[s], (u >> 1) & 1, status)) { ok = false; break; }
-          for (int x = 0; x < 2 && ok; ++x) {
-            if (j >= it.nt[x]) continue;
-            if (!mbar_wait(&p_full[x], pf[x] & 1, status)) { ok = false; break; }
-            ++pf[x];
-            tc_fence_after();
-            pv(x, u, j == 0);
-            if (j + 1 < it.nt[x]) {
-              if (!mbar_wait(&k_full[(u + 1) & 1], ((u + 1) >> 1) & 1, status)) { ok = false; break; }
-              tc_fence_after();
-              qk(x, u + 1);
-              if (j + 2 == it.nt[x]) umma_commit(&q_empty[x]);
+          };
+          auto load_tile = [&](const CUtensorMap* map, uint8_t* buf, uint64_t* bar, int col, int j,
+                               const int (&r)[BPT]) {
+            if constexpr (PAGED) {
+  #pragma unroll
+              for (int i = 0; i < BPT; ++i) {
+                tma_load_2d(buf + i * 2048, map, bar, 0, r[i]);
+                tma_load_2d(buf + HALF_KV + i * 2048, map, bar, 64, r[i]);
+              }
             } else {
-              umma_commit(&o_full[x]);
+              tma_load_2d(buf, map, bar, col, it.seq_start + j * BN);
+              tma_load_2d(buf + HALF_KV, map, bar, col + 64, it.seq_start + j * BN);
             }
+          };
+          int r_cur[BPT] = {}, r_prev[BPT] = {}, r_next[BPT] = {};
+          if (PAGED) rows_of(0, r_cur);
+          auto load_k = [&](int j) -> bool {
+            const uint32_t u = kv + j, s = u & 1;
+            if (!mbar_wait(&k_empty[s], ((u >> 1) & 1) ^ 1, status)) return false;
+            mbar_arrive_expect_tx(&k_full[s], TILE_KV);
+            load_tile(&tmk, smem + OFF_K + s * TILE_KV, &k_full[s], kcol, j, r_cur);
+            return true;
+          };
+          auto load_v = [&](int j, const int (&r)[BPT]) -> bool {
+            const uint32_t u = kv + j, s = u & 1;
+            if (!mbar_wait(&v_empty[s], ((u >> 1) & 1) ^ 1, status)) return false;
+            mbar_arrive_expect_tx(&v_full[s], TILE_KV);
+            load_tile(&tmv, smem + OFF_V + s * TILE_KV, &v_full[s], vcol, j, r);
+            return true;
+          };
+          for (int j = 0; j < it.nkv && good; ++j) {   // K_j goes out before V_{j-1}
+            good = load_k(j);
+            if (PAGED && j + 1 < it.nkv) rows_of(j + 1, r_next);
+            if (good && j >= 1) good = load_v(j - 1, r_prev);
+  #pragma unroll
+            for (int i = 0; i < BPT; ++i) {
+              r_prev[i] = r_cur[i];
+              r_cur[i] = r_next[i];
+            }
+          }
+          if (good && it.nkv > 0) good = load_v(it.nkv - 1, r_prev);
+          kv += it.nkv;
+        }
+      }
+      __syncwarp();
+    } else if (warp == 1) {
+      if (lane == 0) {
+        constexpr uint32_t IDESC_QK = umma_idesc_bf16(BM, BN);
+        constexpr uint32_t IDESC_PV = umma_idesc_bf16_bmn(BM, D);
+        bool ok = true, issued = false;
+        uint32_t kv = 0;               // ring position of the item's tile 0
+        uint32_t pf[2] = {0u, 0u};     // p_full phases consumed per tile
+        auto qk = [&](int x, uint32_t u) {  // S_x = Q_x.K_u^T, then S_x is signalled
+          const uint32_t sQ = smem_u32(smem + OFF_Q + x * TILE_Q);
+          const uint32_t sK = smem_u32(smem + OFF_K + (u & 1) * TILE_KV);
+  #pragma unroll
+          for (int k = 0; k < D / 16; ++k) {
+            umma_bf16(tmem + x * BN, umma_desc_sw128(sQ + (k >> 2) * HALF_Q + (k & 3) * 32),
+                      umma_desc_sw128(sK + (k >> 2) * HALF_KV + (k & 3) * 32), IDESC_QK, k > 0 ? 1u : 0u);
+          }
+          umma_commit(&s_full[x]);
+        };
+        auto pv = [&](int x, uint32_t u, bool first) {  // O_x (+)= P_x.V_u, P_x in the first 64 columns of S_x
+          const uint32_t sV = smem_u32(smem + OFF_V + (u & 1) * TILE_KV);
+  #pragma unroll
+          for (int kk = 0; kk < BN / 16; ++kk) {
+            umma_bf16_ts(tmem + 2 * BN + x * D, tmem + x * BN + kk * 8,
+                         fatc::umma_desc_sw128_mn(sV + kk * 2048, HALF_KV), IDESC_PV, (!first || kk > 0) ? 1u : 0u);
+          }
+        };
+        for (int n_it = 0, w = item_at(0, blockIdx.x, gridDim.x); w < n_items && ok;
+             ++n_it, w = item_at(n_it, blockIdx.x, gridDim.x)) {
+          const Item it = item_of<PAGED>(w, tile_info, n_tiles, Hq, Hkv, block_tables, bt_stride);
+          for (int x = 0; x < 2 && ok; ++x) ok = mbar_wait(&q_full[x], n_it & 1, status);
+          if (!ok) break;
+          if (!mbar_wait(&k_full[kv & 1], (kv >> 1) & 1, status)) { ok = false; break; }
+          tc_fence_after();
+          for (int x = 0; x < 2; ++x) {
+            if (it.nt[x] == 0) continue;
+            qk(x, kv);
+            if (it.nt[x] == 1) umma_commit(&q_empty[x]);   // Q_x done with
+          }
+          issued = true;
+          umma_commit(&k_empty[kv & 1]);
+          for (int j = 0; j < it.nkv && ok; ++j) {
+            const uint32_t u = kv + j, s = u & 1;
+            if (!mbar_wait(&v_full[s], (u >> 1) & 1, status)) { ok = false; break; }
+            for (int x = 0; x < 2 && ok; ++x) {
+              if (j >= it.nt[x]) continue;
+              if (!mbar_wait(&p_full[x], pf[x] & 1, status)) { ok = false; break; }
+              ++pf[x];
+              tc_fence_after();
+              pv(x, u, j == 0);
+              if (j + 1 < it.nt[x]) {
+                if (!mbar_wait(&k_full[(u + 1) & 1], ((u + 1) >> 1) & 1, status)) { ok = false; break; }
+                tc_fence_after();
+                qk(x, u + 1);
+                if (j + 2 == it.nt[x]) umma_commit(&q_empty[x]);
+              } else {
+                umma_commit(&o_full[x]);
+              }
+            }
+            if (!ok) break;
+            umma_commit(&v_empty[s]);                                  // both tiles' P.V of tile u
+            if (j + 1 < it.nkv) umma_commit(&k_empty[(u + 1) & 1]);    // both tiles' Q.K^T of tile u+1
           }
           if (!ok) break;
-          umma_commit(&v_empty[s]);                                  // both tiles' P.V of tile u
-          if (j + 1 < it.nkv) umma_commit(&k_empty[(u + 1) & 1]);    // both tiles' Q.K^T of tile u+1
+          for (int x = 0; x < 2; ++x)
+            if (it.nt[x] == 0) umma_commit(&q_empty[x]);
+          kv += it.nkv;
         }
-        if (!ok) break;
-        for (int x = 0; x < 2; ++x)
-          if (it.nt[x] == 0) umma_commit(&q_empty[x]);
-        kv += it.nkv;
+        if (!ok && issued) {
+          umma_commit(drain);
+          mbar_wait(drain, 0, nullptr, 100000000ull);
+        }
       }
-      if (!ok && issued) {
-        umma_commit(drain);
-        mbar_wait(drain, 0, nullptr, 100000000ull);
-      }
+      __syncwarp();
     }
-    __syncwarp();
   } else {
-    const int x = (warp - 2) >> 2;        // Q tile of this warpgroup
+    asm volatile("setmaxnreg.inc.sync.aligned.u32 %0;\n" ::"n"(SOFTMAX_REGS));
+    const int x = (warp >> 2) - 1;        // Q tile of this warpgroup
     const int q = warp & 3;               // its tensor-memory lane quadrant
     const int row = q * 32 + lane;
     const uint32_t lane_off = (uint32_t)(q * 32) << 16;
