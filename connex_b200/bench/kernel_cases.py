@@ -329,7 +329,10 @@ def main() -> None:
     p.add_argument("--co", default="gemm", help="kv_push_beside: co-running kernel (gemm, attn, none)")
     p.add_argument("--exp-split", type=int, default=None,
                    help="attn cases: softmax exponentials of every 8 on the FMA pipe (0, 2, 4)")
+    p.add_argument("--raster-group", type=int, default=None, help="gemm cases: tile-rows per raster band")
     a = p.parse_args()
+    if a.raster_group is not None:
+        ops._C.gemm_raster_group(a.raster_group)
     if a.exp_split is not None:
         ops._C.attention_exp_split(a.exp_split)
     dev = torch.device("cuda", 0)
@@ -347,6 +350,8 @@ def main() -> None:
     res = {"case": a.case, "ms": round(ms, 4)}
     if a.exp_split is not None:
         res["exp_split"] = a.exp_split
+    if a.raster_group is not None:
+        res["raster_group"] = a.raster_group
     if a.case in NEEDS_ARGS:
         res.update({"ctas": a.ctas, "pull": a.pull, "ce": a.ce})
     if "flops" in work:

@@ -426,6 +426,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("decode_workspace_floats", &decode_workspace_floats);
   m.def("kv_push_layer", &kv_push_layer);
   m.def("gemm_splits", &gemm_splits);
+  m.def("gemm_raster_group", &cx::gemm_raster_group);
   m.def("copy_segments", &copy_segments);
   m.def("wsync", &wsync, py::arg("jobs_dev"), py::arg("jobs_cpu"), py::arg("dst_bytes"), py::arg("bases"),
         py::arg("flags"), py::arg("mc_base"), py::arg("mc_flag"), py::arg("max_ctas"), py::arg("scatter_bytes") = 0);

@@ -42,22 +42,23 @@ struct GemmCfg {
   static constexpr int SMEM = 1024 /*align slack*/ + STAGES * STAGE_BYTES + 256 /*barriers*/;
 };
 
-__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int& tm, int& tn) {
-  constexpr int GROUP = 8;
-  const int per_group = GROUP * num_n;
+// Grouped raster: bands of `group` tile-rows, each band walked column by
+// column, so the CTAs of one wave share A rows and B columns through L2.
+__device__ __forceinline__ void tile_coords(int t, int num_m, int num_n, int group, int& tm, int& tn) {
+  const int per_group = group * num_n;
   const int g = t / per_group;
-  const int first_m = g * GROUP;
-  const int gm = min(num_m - first_m, GROUP);
+  const int first_m = g * group;
+  const int gm = min(num_m - first_m, group);
   const int r = t - g * per_group;
   tm = first_m + r % gm;
   tn = r / gm;
 }
 
-__device__ __forceinline__ void tile_coords_split(int t, int num_m, int num_n, int splits, int& tm, int& tn,
-                                                  int& ks) {
+__device__ __forceinline__ void tile_coords_split(int t, int num_m, int num_n, int splits, int group, int& tm,
+                                                  int& tn, int& ks) {
   const int tt = t / splits;
   ks = t - tt * splits;
-  tile_coords(tt, num_m, num_n, tm, tn);
+  tile_coords(tt, num_m, num_n, group, tm, tn);
 }
 
 __device__ __forceinline__ float silu(float x) { return x / (1.0f + __expf(-x)); }
@@ -71,11 +72,15 @@ __device__ __forceinline__ void red_add_v4_f32(float* p, float a, float b, float
 // k-blocks, one work item each, and the epilogue adds the fp32 partial sums
 // into W (zero on entry) with vector reductions; gemm_splitk_finalize applies
 // the epilogue.  Small-M (decode) GEMMs get enough work items to fill the SMs.
+// Tile-rows per raster band (see tile_coords).
+static int g_gemm_group = 8;
+void gemm_raster_group(int rows) { g_gemm_group = rows >= 1 && rows <= 64 ? rows : 8; }
+
 template <int BN, int STAGES, int EPI, bool SPLIT>
 __global__ void __launch_bounds__(GEMM_THREADS, 1)
     gemm_bf16_tn_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
                         __nv_bfloat16* __restrict__ D, const __nv_bfloat16* R, int M, int N, int K, int ldd,
-                        int ldr, int* status, float* __restrict__ W, int ldw, int splits, int kper) {
+                        int ldr, int* status, float* __restrict__ W, int ldw, int splits, int kper, int group) {
   using Cfg = GemmCfg<BN, STAGES>;
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
@@ -124,7 +129,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
       uint32_t stage = 0, phase = 0;
       for (int t = blockIdx.x; t < total && ok; t += gridDim.x) {
         int tm, tn, ks;
-        tile_coords_split(t, num_m, num_n, splits, tm, tn, ks);
+        tile_coords_split(t, num_m, num_n, splits, group, tm, tn, ks);
         const int kb0 = ks * kper, kb1 = min(nk, kb0 + kper);
         for (int kb = kb0; kb < kb1; ++kb) {
           if (!mbar_wait(&empty[stage], phase ^ 1, status)) {
@@ -198,7 +203,7 @@ __global__ void __launch_bounds__(GEMM_THREADS, 1)
     uint32_t acc = 0, acc_phase = 0;
     for (int t = blockIdx.x; t < total; t += gridDim.x) {
       int tm, tn, ks;
-      tile_coords_split(t, num_m, num_n, splits, tm, tn, ks);
+      tile_coords_split(t, num_m, num_n, splits, group, tm, tn, ks);
       if (!mbar_wait(&tfull[acc], acc_phase, status)) break;
       tc_fence_after();
       const int row = tm * GEMM_BM + q * 32 + lane;
@@ -402,7 +407,7 @@ static void launch_gemm(const void* A, const void* B, void* D, const void* R, in
   if (kper <= 0) kper = (K + GEMM_BK - 1) / GEMM_BK;
   kern<<<grid, GEMM_THREADS, Cfg::SMEM, stream>>>(ta, tb, reinterpret_cast<__nv_bfloat16*>(D),
                                                    reinterpret_cast<const __nv_bfloat16*>(R), M, N, K, ldd, ldr,
-                                                   status, W, N, splits, kper);
+                                                   status, W, N, splits, kper, g_gemm_group);
 }
 
 // Work-item split of the K loop: only when the output tiles alone would
