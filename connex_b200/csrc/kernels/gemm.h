@@ -20,7 +20,7 @@ void gemm_bf16_tn(const void* A, const void* B, void* D, const void* R, int M, i
                   float* W = nullptr, int splits = 1);
 // The K split gemm_bf16_tn would profit from (1 = none).
 int gemm_splits(int M, int N, int K, int epi, int bn);
-// Tile-rows per band of the GEMM's grouped raster (default 8).
+// Tile-rows per band of the GEMM's grouped raster (default 16).
 void gemm_raster_group(int rows);
 
 // M <= GEMV_MAX_M rows (decode steps): the weight-streaming CUDA-core kernel
