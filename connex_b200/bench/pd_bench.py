@@ -20,7 +20,7 @@ from connex_b200.parallel.peer import PeerHandle, PeerMapper, export_tensor
 from connex_b200.runtime.pd import (DecodeBatch, KVDestination, LayerReadySignal, LayerwiseKVPuller,
                                     LayerwiseKVPusher, block_pairs, build_prefill_batch, decode_step)
 
-PUSH_CTAS = int(os.environ.get("CX_PD_PUSH_CTAS", "296"))   # CTAs per layer push (2 per SM by default)
+PUSH_CTAS = int(os.environ.get("CX_PD_PUSH_CTAS", "0"))   # CTAs per layer push (0: one 128-thread CTA per SM)
 PUSH_AFTER_ATTENTION = os.environ.get("CX_PD_PUSH_AFTER", "kv") == "attention"
 PULL_CTAS = int(os.environ.get("CX_PD_PULL_CTAS", "592"))   # the decode GPU is otherwise idle during prefill
 TOKEN_BYTES = 64         # first-token inbox copy (16 int32)
@@ -389,7 +389,7 @@ def run_pd_bench(args, ClockSampler, finalize: bool = True):
                        "seq_len": f"uniform {args.min_len}-{args.max_len}",
                        "parallelism": "colocated 1P1D" if world == 1 else f"pd {world // 2}P{world // 2}D (TP1)",
                        "kv_block_tokens": cfg.block_size, "l2": "inputs larger than L2 (16 GB weights, GB-scale KV)",
-                       "kv_ctas": PULL_CTAS if mode == "pull" else PUSH_CTAS,
+                       "kv_ctas": PULL_CTAS if mode == "pull" else (PUSH_CTAS or "one 128-thread CTA per SM"),
                        "push_after": "attention" if PUSH_AFTER_ATTENTION else "kv write"},
         }
     if rank == 0 and result is not None and result["kv_check"] != "ok":

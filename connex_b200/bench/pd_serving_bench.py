@@ -56,7 +56,7 @@ from connex_b200.parallel.peer import PeerHandle, PeerMapper, export_tensor
 from connex_b200.runtime.pd import (DecodeBatch, KVDestination, LayerwiseKVPusher, block_pairs,
                                     build_prefill_batch, decode_step)
 
-PUSH_CTAS = 296
+PUSH_CTAS = 0   # one 128-thread CTA per SM (see LayerwiseKVPusher)
 
 
 def arrivals(seed: int, pair: int, qps: float, duration: float, lo: int, hi: int, vocab: int):

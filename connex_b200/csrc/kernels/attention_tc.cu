@@ -456,8 +456,12 @@ constexpr int BM = 128;                      // rows of one Q tile
 constexpr int BN = 128;                      // keys of one K/V tile
 constexpr int ROWS = 2 * BM;                 // query rows of a work item
 constexpr int THREADS = 384;                 // three warpgroups
-constexpr int CTRL_REGS = 88, SOFTMAX_REGS = 208;   // per thread after setmaxnreg (no spills)
-static_assert(128 * CTRL_REGS + 256 * SOFTMAX_REGS <= THREADS * 168, "register split above the launch's total");
+// Registers per thread at launch, and after the setmaxnreg split (no spills).
+// 3 warps x 32 x 152 = 14592 of a sub-partition's 16384 leaves 1792: the one
+// warp (32 x 48) of a 128-thread KV-push CTA that runs beside this kernel.
+constexpr int LAUNCH_REGS = 152;
+constexpr int CTRL_REGS = 88, SOFTMAX_REGS = 184;
+static_assert(128 * CTRL_REGS + 256 * SOFTMAX_REGS <= THREADS * LAUNCH_REGS, "register split above the launch's total");
 constexpr int HALF_Q = BM * 64 * 2;          // [128 rows x 64 dims]: 16 KB
 constexpr int HALF_KV = BN * 64 * 2;         // [128 keys x 64 dims]: 16 KB
 constexpr int TILE_Q = 2 * HALF_Q;
@@ -506,7 +510,7 @@ __device__ __forceinline__ int item_at(int k, int b, int G) { return k * G + ((k
 }  // namespace fap
 
 template <bool PAGED, int EMU>
-__global__ void __launch_bounds__(fap::THREADS, 1)
+__global__ void __maxnreg__(fap::LAUNCH_REGS)
     prefill_attn_pair_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                              const __grid_constant__ CUtensorMap tmv, __nv_bfloat16* __restrict__ out, int ldo,
                              const int* __restrict__ tile_info, int n_tiles, int Hq, int Hkv, float scale_log2,
@@ -564,7 +568,7 @@ __global__ void __launch_bounds__(fap::THREADS, 1)
 
   if (warp < 4) {
     // producer and MMA warps need few registers: hand them to the softmax
-    // warpgroups (4 x 32 x 88 + 8 x 32 x 208 = 384 x 168, the launch total)
+    // warpgroups (4 x 32 x 88 + 8 x 32 x 184 = 384 x 152, the launch total)
     asm volatile("setmaxnreg.dec.sync.aligned.u32 %0;\n" ::"n"(CTRL_REGS));
     if (warp == 0) {
       if (lane == 0) {

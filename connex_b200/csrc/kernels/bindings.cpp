@@ -220,14 +220,15 @@ int64_t decode_workspace_floats(int64_t B, int64_t Hq, int64_t max_ctx) {
 int64_t kv_push_layer(int64_t src_k, int64_t src_v, int64_t dst_k, int64_t dst_v, const at::Tensor& pairs,
                       int64_t src_heads, int64_t dst_heads, int64_t src_h0, int64_t dst_h0, int64_t n_heads,
                       int64_t chunk_bytes, int64_t src_blocks, int64_t dst_blocks, int64_t ready, int64_t max_ctas,
-                      const c10::optional<at::Tensor>& status, int64_t span) {
+                      const c10::optional<at::Tensor>& status, int64_t span, int64_t threads) {
   TORCH_CHECK(pairs.scalar_type() == at::kInt && pairs.is_cuda(), "pairs must be int32 CUDA [n, 2]");
   const c10::cuda::CUDAGuard g(pairs.device());
   return cx::kv_push_layer(reinterpret_cast<const void*>(src_k), reinterpret_cast<const void*>(src_v),
                            reinterpret_cast<void*>(dst_k), reinterpret_cast<void*>(dst_v), pairs.data_ptr<int>(),
                            (int)pairs.size(0), (int)src_heads, (int)dst_heads, (int)src_h0, (int)dst_h0, (int)n_heads,
                            (int)chunk_bytes, (int)src_blocks, (int)dst_blocks, reinterpret_cast<uint32_t*>(ready),
-                           (int)max_ctas, status_ptr(status), cur_stream(pairs), reinterpret_cast<uint64_t*>(span));
+                           (int)max_ctas, status_ptr(status), cur_stream(pairs), reinterpret_cast<uint64_t*>(span),
+                           (int)threads);
 }
 
 int64_t copy_segments(const at::Tensor& segs, int64_t total_bytes, int64_t ready, int64_t max_ctas,

@@ -10,11 +10,13 @@ int num_sms_comm();
 
 // Returns the number of CTAs launched (each releases `ready` by one).
 // `span` (optional, 2 x u64 initialised to {UINT64_MAX, 0}): receives the
-// kernel's execution window in %globaltimer nanoseconds.
+// kernel's execution window in %globaltimer nanoseconds.  `threads` per CTA:
+// 256, or 128 for a push that runs beside the prefill's persistent kernels
+// (one 128-thread CTA fits in the registers they leave free on each SM).
 int kv_push_layer(const void* src_k, const void* src_v, void* dst_k, void* dst_v, const int* pairs, int n_pairs,
                   int src_heads, int dst_heads, int src_h0, int dst_h0, int n_heads, int chunk_bytes, int src_blocks,
                   int dst_blocks, uint32_t* ready, int max_ctas, int* status, cudaStream_t s,
-                  uint64_t* span = nullptr);
+                  uint64_t* span = nullptr, int threads = 256);
 
 int copy_segments(const int64_t* segs, int n, int64_t total_bytes, uint32_t* ready, int max_ctas, int* status,
                   cudaStream_t s);

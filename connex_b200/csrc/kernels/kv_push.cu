@@ -74,14 +74,17 @@ __global__ void __launch_bounds__(256) kv_push_kernel(const uint8_t* __restrict_
 
 int kv_push_layer(const void* src_k, const void* src_v, void* dst_k, void* dst_v, const int* pairs, int n_pairs,
                   int src_heads, int dst_heads, int src_h0, int dst_h0, int n_heads, int chunk_bytes, int src_blocks,
-                  int dst_blocks, uint32_t* ready, int max_ctas, int* status, cudaStream_t s, uint64_t* span) {
+                  int dst_blocks, uint32_t* ready, int max_ctas, int* status, cudaStream_t s, uint64_t* span,
+                  int threads) {
   if (n_pairs <= 0) return 0;
   if (chunk_bytes % 16 != 0) throw std::runtime_error("cx kv_push: head slice must be a multiple of 16 bytes");
+  if (threads != 128 && threads != 256) throw std::runtime_error("cx kv_push: 128 or 256 threads per CTA");
   const long warps = (long)n_pairs * 2 * n_heads;
-  long ctas = (warps + 7) / 8;
+  const int wpb = threads / 32;
+  long ctas = (warps + wpb - 1) / wpb;
   const long cap = max_ctas > 0 ? max_ctas : 4L * num_sms_comm();
   if (ctas > cap) ctas = cap;
-  kv_push_kernel<<<(int)ctas, 256, 0, s>>>(
+  kv_push_kernel<<<(int)ctas, threads, 0, s>>>(
       reinterpret_cast<const uint8_t*>(src_k), reinterpret_cast<const uint8_t*>(src_v),
       reinterpret_cast<uint8_t*>(dst_k), reinterpret_cast<uint8_t*>(dst_v), pairs, n_pairs, src_heads, dst_heads,
       src_h0, dst_h0, n_heads, chunk_bytes, src_blocks, dst_blocks, ready, status,

@@ -277,17 +277,19 @@ def kv_push_layer(src_k: int, src_v: int, dst_k: int, dst_v: int, pairs: torch.T
                   src_heads: int, dst_heads: int, src_h0: int = 0, dst_h0: int = 0,
                   n_heads: Optional[int] = None, chunk_bytes: int, src_blocks: int, dst_blocks: int,
                   ready: int = 0, max_ctas: int = 0, status: Optional[torch.Tensor] = None,
-                  span: int = 0) -> int:
+                  span: int = 0, threads: int = 256) -> int:
     """Push one layer's paged KV blocks (pairs: int32 [n, 2] of src/dst block
     ids) from local caches to (peer-mapped) destination caches.  Returns the
     number of CTAs, each of which adds 1 to the u32 at ``ready`` when done.
     ``span``: address of two int64 set to (-1, 0); the kernel stores its
     execution window there (``%globaltimer`` ns of the first CTA's start and
-    the last CTA's end)."""
+    the last CTA's end).  ``threads`` per CTA: 256, or 128 for a push beside
+    the prefill's persistent kernels (one such CTA fits on each SM next to
+    them)."""
     _n()
     return _C.kv_push_layer(src_k, src_v, dst_k, dst_v, pairs, src_heads, dst_heads, src_h0, dst_h0,
                             n_heads if n_heads is not None else src_heads, chunk_bytes, src_blocks,
-                            dst_blocks, ready, max_ctas, status, span)
+                            dst_blocks, ready, max_ctas, status, span, threads)
 
 
 def copy_segments(segs: torch.Tensor, total_bytes: int, ready: int = 0, max_ctas: int = 0,

@@ -71,13 +71,18 @@ class LayerwiseKVPusher:
     """Launches one ``kv_push_layer`` per layer on a side stream, in step with
     the prefill's per-layer hook; counts the CTAs the decode side must see."""
 
-    def __init__(self, src: PagedKVCache, max_ctas: int = 0, priority: int = -1):
+    def __init__(self, src: PagedKVCache, max_ctas: int = 0, priority: int = -1, threads: int = 128):
         self.src = src
         # High priority: push CTAs take SM slots ahead of the queued prefill
-        # CTAs (they need no shared memory, so they co-reside with GEMM CTAs).
+        # CTAs.  The prefill's GEMM and attention kernels are persistent (one
+        # CTA per SM, most of its shared memory); the attention kernel leaves
+        # exactly the registers of one 128-thread push CTA free on each SM, so
+        # the push runs beside them with one such CTA per SM (max_ctas 0: the
+        # SM count) instead of waiting for a kernel to end.
         self.stream = torch.cuda.Stream(device=src.kv.device, priority=priority)
         self.status = ops.new_status(src.kv.device)
-        self.max_ctas = max_ctas
+        self.max_ctas = max_ctas or torch.cuda.get_device_properties(src.kv.device).multi_processor_count
+        self.threads = threads
         self._pairs: Optional[torch.Tensor] = None
         self._dst: Optional[KVDestination] = None
         self.launched = 0
@@ -119,7 +124,7 @@ class LayerwiseKVPusher:
                                   chunk_bytes=c.head_slice_bytes, src_blocks=c.num_blocks,
                                   dst_blocks=d.num_blocks, ready=d.ready_addr, max_ctas=self.max_ctas,
                                   status=self.status,
-                                  span=self._span[layer].data_ptr() if self.timing else 0)
+                                  span=self._span[layer].data_ptr() if self.timing else 0, threads=self.threads)
             if self.timing:
                 e1 = torch.cuda.Event(enable_timing=True)
                 e1.record(self.stream)
