@@ -319,6 +319,30 @@ CASES = {"gemm": lambda d: case_gemm(d), "gemm_qkv": lambda d: case_gemm(d, 8192
 NEEDS_ARGS = {"kv_push_nvlink": case_kv_push_nvlink}
 
 
+PROF_NAMES = ["mma_wait_q", "mma_wait_k", "mma_wait_v", "mma_wait_p0", "mma_wait_p1", "mma_total",
+              "sm0_wait_s", "sm0_softmax", "sm0_epilogue", "sm0_wait_o",
+              "sm1_wait_s", "sm1_softmax", "sm1_epilogue", "sm1_wait_o", "producer_wait", "unused"]
+
+
+def attn_profile(fn, dev) -> dict:
+    """One launch of the two-tile prefill attention with its per-CTA cycle
+    counters (clock64 of the MMA thread and one lane of each softmax
+    warpgroup); returns the mean over CTAs of each counter, in thousands of
+    cycles, and each as a share of the MMA thread's total."""
+    sms = torch.cuda.get_device_properties(dev).multi_processor_count
+    buf = torch.zeros(sms * 16, dtype=torch.int64, device=dev)
+    ops._C.attention_profile(buf.data_ptr())
+    try:
+        fn()
+        torch.cuda.synchronize(dev)
+    finally:
+        ops._C.attention_profile(0)
+    m = buf.view(sms, 16).double().mean(0).tolist()
+    total = m[5] or 1.0
+    return {"attn_profile_kcycles": {n: round(v / 1e3, 1) for n, v in zip(PROF_NAMES, m) if n != "unused"},
+            "share_of_mma_total": {n: round(v / total, 3) for n, v in zip(PROF_NAMES, m) if n != "unused"}}
+
+
 def main() -> None:
     p = argparse.ArgumentParser()
     p.add_argument("case", choices=sorted(CASES) + sorted(NEEDS_ARGS) + ["kv_push_beside"])
@@ -330,6 +354,8 @@ def main() -> None:
     p.add_argument("--exp-split", type=int, default=None,
                    help="attn cases: softmax exponentials of every 8 on the FMA pipe (0, 2, 4)")
     p.add_argument("--raster-group", type=int, default=None, help="gemm cases: tile-rows per raster band")
+    p.add_argument("--attn-profile", action="store_true",
+                   help="attn cases: one more launch of the two-tile kernel with its per-CTA cycle counters")
     a = p.parse_args()
     if a.raster_group is not None:
         ops._C.gemm_raster_group(a.raster_group)
@@ -346,6 +372,8 @@ def main() -> None:
     ms = _time(fn, a.iters, device=work.get("device"))
     if "check" in work:
         work["check"]()
+    if a.attn_profile:
+        print(json.dumps(attn_profile(fn, dev)), flush=True)
     hbm, tf, src = _peaks()
     res = {"case": a.case, "ms": round(ms, 4)}
     if a.exp_split is not None:

@@ -112,7 +112,8 @@ __global__ void __launch_bounds__(fatc::THREADS, 2)
     prefill_attn_tc_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                            const __grid_constant__ CUtensorMap tmv, __nv_bfloat16* __restrict__ out, int ldo,
                            const int* __restrict__ tile_info, int n_tiles, int Hq, int Hkv, float scale_log2,
-                           const int* __restrict__ block_tables, int bt_stride, int* status) {
+                           const int* __restrict__ block_tables, int bt_stride, int* status,
+                           unsigned long long* /*prof: two-tile kernel only*/) {
   using namespace fatc;
   extern __shared__ __align__(1024) uint8_t smem[];
   if ((smem_u32(smem) & 1023u) != 0) {  // swizzled operands need a 1 KB-aligned base
@@ -473,6 +474,11 @@ constexpr int OFF_BAR = OFF_V + 2 * TILE_KV;
 constexpr int SMEM = OFF_BAR + 256;          // 192.25 KB
 constexpr int TMEM_COLS = 512;
 constexpr int BPT = BN / 16;                 // paged: 16-token cache blocks per key tile
+// Optional per-CTA cycle counters (clock64), 16 per CTA: 0-4 MMA thread waiting
+// on q_full / k_full / v_full / p_full[0] / p_full[1], 5 MMA thread total,
+// 6-9 and 10-13 softmax warpgroup 0 / 1: waiting on S, softmax (S seen to P
+// published), epilogue (O wait + stores), O wait; 14 producer waiting.
+constexpr int PROF_SLOTS = 16;
 static_assert(SMEM <= 227 * 1024, "shared memory");
 
 // One work item: 256 query rows of a sequence's new tokens, one query head.
@@ -509,13 +515,15 @@ __device__ __forceinline__ Item item_of(int w, const int* __restrict__ tile_info
 __device__ __forceinline__ int item_at(int k, int b, int G) { return k * G + ((k & 1) ? G - 1 - b : b); }
 }  // namespace fap
 
-template <bool PAGED, int EMU>
+template <bool PAGED, int EMU, bool PROF>
 __global__ void __maxnreg__(fap::LAUNCH_REGS)
     prefill_attn_pair_kernel(const __grid_constant__ CUtensorMap tmq, const __grid_constant__ CUtensorMap tmk,
                              const __grid_constant__ CUtensorMap tmv, __nv_bfloat16* __restrict__ out, int ldo,
                              const int* __restrict__ tile_info, int n_tiles, int Hq, int Hkv, float scale_log2,
-                             const int* __restrict__ block_tables, int bt_stride, int* status) {
+                             const int* __restrict__ block_tables, int bt_stride, int* status,
+                             unsigned long long* prof) {
   using namespace fap;
+  if constexpr (!PROF) prof = nullptr;   // counters compiled out
   using fatc::RESCALE_THRESHOLD;
   extern __shared__ __align__(1024) uint8_t smem[];
   if ((smem_u32(smem) & 1023u) != 0) {  // swizzled operands need a 1 KB-aligned base
@@ -573,6 +581,13 @@ __global__ void __maxnreg__(fap::LAUNCH_REGS)
     if (warp == 0) {
       if (lane == 0) {
         bool good = true;
+        long long t_wait = 0;
+        auto pwait = [&](uint64_t* bar, uint32_t par) -> bool {
+          const long long t0 = prof ? clock64() : 0;
+          const bool r = mbar_wait(bar, par, status);
+          if (prof) t_wait += clock64() - t0;
+          return r;
+        };
         uint32_t kv = 0;   // key tiles loaded so far: ring position of the item's tile 0
         for (int n_it = 0, w = item_at(0, blockIdx.x, gridDim.x); w < n_items && good;
              ++n_it, w = item_at(n_it, blockIdx.x, gridDim.x)) {
@@ -580,7 +595,7 @@ __global__ void __maxnreg__(fap::LAUNCH_REGS)
           const int qcol = it.h * D, kcol = (Hq + it.g) * D, vcol = (Hq + Hkv + it.g) * D;
   #pragma unroll
           for (int x = 0; x < 2; ++x) {   // rows past the tensor end are zero-filled, past the sequence unused
-            if (!mbar_wait(&q_empty[x], (n_it & 1) ^ 1, status)) { good = false; break; }
+            if (!pwait(&q_empty[x], (n_it & 1) ^ 1)) { good = false; break; }
             mbar_arrive_expect_tx(&q_full[x], TILE_Q);
             tma_load_2d(smem + OFF_Q + x * TILE_Q, &tmq, &q_full[x], qcol, it.seq_start + it.q0 + x * BM);
             tma_load_2d(smem + OFF_Q + x * TILE_Q + HALF_Q, &tmq, &q_full[x], qcol + 64,
@@ -614,14 +629,14 @@ __global__ void __maxnreg__(fap::LAUNCH_REGS)
           if (PAGED) rows_of(0, r_cur);
           auto load_k = [&](int j) -> bool {
             const uint32_t u = kv + j, s = u & 1;
-            if (!mbar_wait(&k_empty[s], ((u >> 1) & 1) ^ 1, status)) return false;
+            if (!pwait(&k_empty[s], ((u >> 1) & 1) ^ 1)) return false;
             mbar_arrive_expect_tx(&k_full[s], TILE_KV);
             load_tile(&tmk, smem + OFF_K + s * TILE_KV, &k_full[s], kcol, j, r_cur);
             return true;
           };
           auto load_v = [&](int j, const int (&r)[BPT]) -> bool {
             const uint32_t u = kv + j, s = u & 1;
-            if (!mbar_wait(&v_empty[s], ((u >> 1) & 1) ^ 1, status)) return false;
+            if (!pwait(&v_empty[s], ((u >> 1) & 1) ^ 1)) return false;
             mbar_arrive_expect_tx(&v_full[s], TILE_KV);
             load_tile(&tmv, smem + OFF_V + s * TILE_KV, &v_full[s], vcol, j, r);
             return true;
@@ -639,6 +654,7 @@ __global__ void __maxnreg__(fap::LAUNCH_REGS)
           if (good && it.nkv > 0) good = load_v(it.nkv - 1, r_prev);
           kv += it.nkv;
         }
+        if (prof) prof[blockIdx.x * PROF_SLOTS + 14] = (unsigned long long)t_wait;
       }
       __syncwarp();
     } else if (warp == 1) {
@@ -646,6 +662,14 @@ __global__ void __maxnreg__(fap::LAUNCH_REGS)
         constexpr uint32_t IDESC_QK = umma_idesc_bf16(BM, BN);
         constexpr uint32_t IDESC_PV = umma_idesc_bf16_bmn(BM, D);
         bool ok = true, issued = false;
+        long long tw[5] = {0, 0, 0, 0, 0};   // profiling: waits on q_full, k_full, v_full, p_full[0], p_full[1]
+        const long long t_start = prof ? clock64() : 0;
+        auto mwait = [&](int slot, uint64_t* bar, uint32_t par) -> bool {
+          const long long t0 = prof ? clock64() : 0;
+          const bool r = mbar_wait(bar, par, status);
+          if (prof) tw[slot] += clock64() - t0;
+          return r;
+        };
         uint32_t kv = 0;               // ring position of the item's tile 0
         uint32_t pf[2] = {0u, 0u};     // p_full phases consumed per tile
         auto qk = [&](int x, uint32_t u) {  // S_x = Q_x.K_u^T, then S_x is signalled
@@ -669,9 +693,9 @@ __global__ void __maxnreg__(fap::LAUNCH_REGS)
         for (int n_it = 0, w = item_at(0, blockIdx.x, gridDim.x); w < n_items && ok;
              ++n_it, w = item_at(n_it, blockIdx.x, gridDim.x)) {
           const Item it = item_of<PAGED>(w, tile_info, n_tiles, Hq, Hkv, block_tables, bt_stride);
-          for (int x = 0; x < 2 && ok; ++x) ok = mbar_wait(&q_full[x], n_it & 1, status);
+          for (int x = 0; x < 2 && ok; ++x) ok = mwait(0, &q_full[x], n_it & 1);
           if (!ok) break;
-          if (!mbar_wait(&k_full[kv & 1], (kv >> 1) & 1, status)) { ok = false; break; }
+          if (!mwait(1, &k_full[kv & 1], (kv >> 1) & 1)) { ok = false; break; }
           tc_fence_after();
           for (int x = 0; x < 2; ++x) {
             if (it.nt[x] == 0) continue;
@@ -682,15 +706,15 @@ __global__ void __maxnreg__(fap::LAUNCH_REGS)
           umma_commit(&k_empty[kv & 1]);
           for (int j = 0; j < it.nkv && ok; ++j) {
             const uint32_t u = kv + j, s = u & 1;
-            if (!mbar_wait(&v_full[s], (u >> 1) & 1, status)) { ok = false; break; }
+            if (!mwait(2, &v_full[s], (u >> 1) & 1)) { ok = false; break; }
             for (int x = 0; x < 2 && ok; ++x) {
               if (j >= it.nt[x]) continue;
-              if (!mbar_wait(&p_full[x], pf[x] & 1, status)) { ok = false; break; }
+              if (!mwait(3 + x, &p_full[x], pf[x] & 1)) { ok = false; break; }
               ++pf[x];
               tc_fence_after();
               pv(x, u, j == 0);
               if (j + 1 < it.nt[x]) {
-                if (!mbar_wait(&k_full[(u + 1) & 1], ((u + 1) >> 1) & 1, status)) { ok = false; break; }
+                if (!mwait(1, &k_full[(u + 1) & 1], ((u + 1) >> 1) & 1)) { ok = false; break; }
                 tc_fence_after();
                 qk(x, u + 1);
                 if (j + 2 == it.nt[x]) umma_commit(&q_empty[x]);
@@ -711,6 +735,11 @@ __global__ void __maxnreg__(fap::LAUNCH_REGS)
           umma_commit(drain);
           mbar_wait(drain, 0, nullptr, 100000000ull);
         }
+        if (prof) {
+          unsigned long long* pr = prof + blockIdx.x * PROF_SLOTS;
+          for (int i = 0; i < 5; ++i) pr[i] = (unsigned long long)tw[i];
+          pr[5] = (unsigned long long)(clock64() - t_start);
+        }
       }
       __syncwarp();
     }
@@ -724,6 +753,8 @@ __global__ void __maxnreg__(fap::LAUNCH_REGS)
     uint32_t sw = 0, ow = 0;              // s_full / o_full phases waited
     uint32_t kv = 0;                      // ring position of the item's tile 0
     bool ok = true;
+    const bool rec = prof != nullptr && q == 0 && lane == 0;   // profiling: waits / softmax / epilogue cycles
+    long long t_s = 0, t_c = 0, t_e = 0, t_o = 0, t_mark = 0;
     for (int k = 0, w = item_at(0, blockIdx.x, gridDim.x); w < n_items && ok;
          ++k, w = item_at(k, blockIdx.x, gridDim.x)) {
       const Item it = item_of<PAGED>(w, tile_info, n_tiles, Hq, Hkv, block_tables, bt_stride);
@@ -733,8 +764,14 @@ __global__ void __maxnreg__(fap::LAUNCH_REGS)
       const int zero_x = it.nt[0] == it.nkv ? 0 : 1;   // the tile whose P.V reads the last V tile first
       float m = -INFINITY, l = 0.f;
       for (int j = 0; j < n; ++j) {
+        if (rec) t_mark = clock64();
         if (!mbar_wait(&s_full[x], sw & 1, status)) { ok = false; break; }
         ++sw;
+        if (rec) {
+          const long long t = clock64();
+          t_s += t - t_mark;
+          t_mark = t;
+        }
         tc_fence_after();
         uint32_t r[BN];
 #pragma unroll
@@ -820,11 +857,14 @@ __global__ void __maxnreg__(fap::LAUNCH_REGS)
         tmem_st_wait();
         tc_fence_before();
         mbar_arrive(&p_full[x]);
+        if (rec) t_c += clock64() - t_mark;
       }
       if (!ok) break;
       if (n > 0) {
+        const long long te0 = rec ? clock64() : 0;
         if (!mbar_wait(&o_full[x], ow & 1, status)) { ok = false; break; }
         ++ow;
+        if (rec) t_o += clock64() - te0;
         tc_fence_after();
         const float inv = l > 0.f ? 1.f / l : 0.f;
         const bool valid = r0 + row < it.seq_len;
@@ -847,8 +887,16 @@ __global__ void __maxnreg__(fap::LAUNCH_REGS)
           }
         }
         tc_fence_before();   // the next item's P.V overwrites O_x after this warpgroup's next arrival
+        if (rec) t_e += clock64() - te0;
       }
       kv += it.nkv;
+    }
+    if (rec) {
+      unsigned long long* pr = prof + blockIdx.x * PROF_SLOTS + 6 + 4 * x;
+      pr[0] = (unsigned long long)t_s;
+      pr[1] = (unsigned long long)t_c;
+      pr[2] = (unsigned long long)t_e;
+      pr[3] = (unsigned long long)t_o;
     }
   }
   __syncthreads();
@@ -861,6 +909,10 @@ __global__ void __maxnreg__(fap::LAUNCH_REGS)
 // How many of every 8 softmax exponentials run on the FMA pipe (0, 2 or 4).
 static int g_exp_split = 0;
 void attention_exp_split(int n) { g_exp_split = n == 2 || n == 4 ? n : 0; }
+
+// Per-CTA cycle counters of the two-tile kernel (0: off), see fap::PROF_SLOTS.
+static unsigned long long* g_attn_prof = nullptr;
+void attention_profile(int64_t ptr) { g_attn_prof = reinterpret_cast<unsigned long long*>(ptr); }
 
 struct AttnArgs {
   CUtensorMap tq, tk, tv;
@@ -875,13 +927,14 @@ struct AttnArgs {
 };
 
 // PAIR: the two-tile kernel (256 query rows per CTA, one CTA per SM);
-// otherwise the one-tile kernel (128 rows, two CTAs per SM).
-template <bool PAIR, bool PAGED, int EMU>
+// otherwise the one-tile kernel (128 rows, two CTAs per SM).  PROF: the
+// two-tile kernel with its cycle counters.
+template <bool PAIR, bool PAGED, int EMU, bool PROF = false>
 static void launch_attn(const AttnArgs& a, cudaStream_t s) {
   static bool attr[64] = {false};
   int dev;
   cudaGetDevice(&dev);
-  auto* kern = PAIR ? prefill_attn_pair_kernel<PAGED, EMU> : prefill_attn_tc_kernel<PAGED, EMU>;
+  auto* kern = PAIR ? prefill_attn_pair_kernel<PAGED, EMU, PROF> : prefill_attn_tc_kernel<PAGED, EMU>;
   const int smem = PAIR ? fap::SMEM : fatc::SMEM;
   if (!attr[dev & 63]) {
     cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, smem);
@@ -895,12 +948,14 @@ static void launch_attn(const AttnArgs& a, cudaStream_t s) {
   }
   kern<<<grid, PAIR ? fap::THREADS : fatc::THREADS, smem, s>>>(
       a.tq, a.tk, a.tv, reinterpret_cast<__nv_bfloat16*>(a.out), a.ldo, a.tile_info, a.n_tiles, a.Hq, a.Hkv,
-      a.scale_log2, a.bt, a.bt_stride, a.status);
+      a.scale_log2, a.bt, a.bt_stride, a.status, PAIR ? g_attn_prof : nullptr);
 }
 
 template <bool PAIR, bool PAGED>
 static void launch_attn_split(const AttnArgs& a, cudaStream_t s) {
-  if (g_exp_split == 2)
+  if (PAIR && g_attn_prof != nullptr)
+    launch_attn<PAIR, PAGED, 0, true>(a, s);
+  else if (g_exp_split == 2)
     launch_attn<PAIR, PAGED, 2>(a, s);
   else if (g_exp_split == 4)
     launch_attn<PAIR, PAGED, 4>(a, s);

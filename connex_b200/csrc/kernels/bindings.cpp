@@ -422,6 +422,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("prefill_attention", &prefill_attention_tc);
   m.def("prefill_attention_paged", &prefill_attention_paged);
   m.def("attention_exp_split", &cx::attention_exp_split);
+  m.def("attention_profile", &cx::attention_profile);
   m.def("decode_attention", &decode_attention);
   m.def("decode_attention_plan", &decode_attention_plan);
   m.def("decode_workspace_floats", &decode_workspace_floats);

@@ -25,6 +25,9 @@ void prefill_attention_tc(const void* qkv, int ldq, int qkv_cols, int T, void* o
 // How many of every 8 softmax exponentials of the prefill attention run on
 // the FMA pipe instead of the special-function unit: 0 (default), 2 or 4.
 void attention_exp_split(int n);
+// Device address of a zeroed u64 buffer [CTAs x 16] for the two-tile prefill
+// attention's per-CTA cycle counters (0: off).
+void attention_profile(int64_t ptr);
 
 // The same over a paged cache (chunked prefill): q rows from QKV; K/V of the
 // whole context from the caches [blocks, Hkv, 16, 128] (cache_rows =
