@@ -80,6 +80,12 @@ __device__ __forceinline__ uint64_t poly_exp2_x2(uint64_t x2) {
   const uint32_t hi = __float_as_uint(hi_f32(p)) + (__float_as_uint(hi_f32(t)) << 23);
   return f32x2(__uint_as_float(lo), __uint_as_float(hi));
 }
+// 2^x of a bf16 pair with one packed special-function instruction.
+__device__ __forceinline__ uint32_t exp2_bf16x2(uint32_t x) {
+  uint32_t y;
+  asm("ex2.approx.ftz.bf16x2 %0, %1;" : "=r"(y) : "r"(x));
+  return y;
+}
 // pair P of a row (elements 2P, 2P+1): EMU of every 8 elements (EMU / 2 of
 // every 4 pairs) go to the polynomial, the rest to ex2.approx.  EMU is a
 // template parameter of the kernel, chosen by attention_exp_split.
@@ -810,15 +816,23 @@ __global__ void __maxnreg__(fap::LAUNCH_REGS)
           for (int e2 = 0; e2 < 16; ++e2) {
             const int e = c * 32 + 2 * e2;
             const uint64_t t2 = fma_f32x2(f32x2(__uint_as_float(r[e]), __uint_as_float(r[e + 1])), sc2, nb2);
-            uint64_t p2;
-            switch (e2 & 3) {   // compile-time after unrolling: each pair's unit is fixed
-              case 0: p2 = fatc::exp2_pair<EMU, 0>(t2); break;
-              case 1: p2 = fatc::exp2_pair<EMU, 1>(t2); break;
-              case 2: p2 = fatc::exp2_pair<EMU, 2>(t2); break;
-              default: p2 = fatc::exp2_pair<EMU, 3>(t2); break;
+            if constexpr (EMU == 1) {
+              // the pair's exponent rounded to bf16 and one packed ex2 for both
+              // (P is stored as bf16 anyway); the row sum stays fp32
+              const uint32_t pb = fatc::exp2_bf16x2(pack_bf16x2(lo_f32(t2), hi_f32(t2)));
+              sum2[e2 & 3] = add_f32x2(sum2[e2 & 3], f32x2(bf16_lo(pb), bf16_hi(pb)));
+              pk[e2] = pb;
+            } else {
+              uint64_t p2;
+              switch (e2 & 3) {   // compile-time after unrolling: each pair's unit is fixed
+                case 0: p2 = fatc::exp2_pair<EMU, 0>(t2); break;
+                case 1: p2 = fatc::exp2_pair<EMU, 1>(t2); break;
+                case 2: p2 = fatc::exp2_pair<EMU, 2>(t2); break;
+                default: p2 = fatc::exp2_pair<EMU, 3>(t2); break;
+              }
+              sum2[e2 & 3] = add_f32x2(sum2[e2 & 3], p2);
+              pk[e2] = pack_bf16x2(lo_f32(p2), hi_f32(p2));
             }
-            sum2[e2 & 3] = add_f32x2(sum2[e2 & 3], p2);
-            pk[e2] = pack_bf16x2(lo_f32(p2), hi_f32(p2));
           }
           tmem_st16(tS + c * 16, pk);
         }
@@ -906,9 +920,10 @@ __global__ void __maxnreg__(fap::LAUNCH_REGS)
   }
 }
 
-// How many of every 8 softmax exponentials run on the FMA pipe (0, 2 or 4).
+// Softmax exponentials: 0 all on ex2.approx.f32; 2 or 4 of every 8 on the
+// FMA pipe; 1 (two-tile kernel) one packed bf16x2 ex2 per pair.
 static int g_exp_split = 0;
-void attention_exp_split(int n) { g_exp_split = n == 2 || n == 4 ? n : 0; }
+void attention_exp_split(int n) { g_exp_split = n == 1 || n == 2 || n == 4 ? n : 0; }
 
 // Per-CTA cycle counters of the two-tile kernel (0: off), see fap::PROF_SLOTS.
 static unsigned long long* g_attn_prof = nullptr;
@@ -955,6 +970,8 @@ template <bool PAIR, bool PAGED>
 static void launch_attn_split(const AttnArgs& a, cudaStream_t s) {
   if (PAIR && g_attn_prof != nullptr)
     launch_attn<PAIR, PAGED, 0, true>(a, s);
+  else if (g_exp_split == 1 && PAIR)
+    launch_attn<PAIR, PAGED, 1>(a, s);
   else if (g_exp_split == 2)
     launch_attn<PAIR, PAGED, 2>(a, s);
   else if (g_exp_split == 4)

@@ -209,7 +209,7 @@ def test_prefill_attention(dev, lens, G, tile):
     _close(out.view(T, Hq, 128), R.causal_attention(q, k, v, lens))
 
 
-@pytest.mark.parametrize("split", [2, 4])
+@pytest.mark.parametrize("split", [1, 2, 4])
 @pytest.mark.parametrize("tile", [256, 128])
 def test_prefill_attention_with_fma_pipe_exponentials(dev, split, tile):
     """Part of the softmax's 2^x on the FMA pipe (own cubic for 2^f): the
