@@ -595,6 +595,7 @@ __global__ void __maxnreg__(fap::LAUNCH_REGS)
           return r;
         };
         uint32_t kv = 0;   // key tiles loaded so far: ring position of the item's tile 0
+        uint32_t nq[2] = {0u, 0u}, nk[2] = {0u, 0u}, nv[2] = {0u, 0u};   // loads issued per barrier
         for (int n_it = 0, w = item_at(0, blockIdx.x, gridDim.x); w < n_items && good;
              ++n_it, w = item_at(n_it, blockIdx.x, gridDim.x)) {
           const Item it = item_of<PAGED>(w, tile_info, n_tiles, Hq, Hkv, block_tables, bt_stride);
@@ -602,6 +603,7 @@ __global__ void __maxnreg__(fap::LAUNCH_REGS)
   #pragma unroll
           for (int x = 0; x < 2; ++x) {   // rows past the tensor end are zero-filled, past the sequence unused
             if (!pwait(&q_empty[x], (n_it & 1) ^ 1)) { good = false; break; }
+            ++nq[x];
             mbar_arrive_expect_tx(&q_full[x], TILE_Q);
             tma_load_2d(smem + OFF_Q + x * TILE_Q, &tmq, &q_full[x], qcol, it.seq_start + it.q0 + x * BM);
             tma_load_2d(smem + OFF_Q + x * TILE_Q + HALF_Q, &tmq, &q_full[x], qcol + 64,
@@ -636,6 +638,7 @@ __global__ void __maxnreg__(fap::LAUNCH_REGS)
           auto load_k = [&](int j) -> bool {
             const uint32_t u = kv + j, s = u & 1;
             if (!pwait(&k_empty[s], ((u >> 1) & 1) ^ 1)) return false;
+            ++nk[s];
             mbar_arrive_expect_tx(&k_full[s], TILE_KV);
             load_tile(&tmk, smem + OFF_K + s * TILE_KV, &k_full[s], kcol, j, r_cur);
             return true;
@@ -643,6 +646,7 @@ __global__ void __maxnreg__(fap::LAUNCH_REGS)
           auto load_v = [&](int j, const int (&r)[BPT]) -> bool {
             const uint32_t u = kv + j, s = u & 1;
             if (!pwait(&v_empty[s], ((u >> 1) & 1) ^ 1)) return false;
+            ++nv[s];
             mbar_arrive_expect_tx(&v_full[s], TILE_KV);
             load_tile(&tmv, smem + OFF_V + s * TILE_KV, &v_full[s], vcol, j, r);
             return true;
@@ -659,6 +663,15 @@ __global__ void __maxnreg__(fap::LAUNCH_REGS)
           }
           if (good && it.nkv > 0) good = load_v(it.nkv - 1, r_prev);
           kv += it.nkv;
+        }
+        if (!good) {
+          // a wait ran out: let the loads already issued land (bounded) before
+          // this CTA can leave, so none writes into shared memory a later CTA owns
+          for (int s = 0; s < 2; ++s) {
+            if (nq[s]) mbar_wait(&q_full[s], (nq[s] - 1) & 1, nullptr, 100000000ull);
+            if (nk[s]) mbar_wait(&k_full[s], (nk[s] - 1) & 1, nullptr, 100000000ull);
+            if (nv[s]) mbar_wait(&v_full[s], (nv[s] - 1) & 1, nullptr, 100000000ull);
+          }
         }
         if (prof) prof[blockIdx.x * PROF_SLOTS + 14] = (unsigned long long)t_wait;
       }

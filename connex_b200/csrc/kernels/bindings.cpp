@@ -347,6 +347,25 @@ void ep_combine(const at::Tensor& comb, const at::Tensor& slot_of, int64_t T, in
                  status_ptr(status), cur_stream(comb));
 }
 
+// The whole EP layer in one call: count, dispatch, the two grouped GEMMs and
+// combine, launched back to back on the current stream (one crossing from
+// Python instead of five; the kernels' own waits order the phases across
+// ranks).  Targets are the cumulative u32 counter values this forward waits for.
+void ep_forward(const at::Tensor& x, const at::Tensor& topk_idx, const at::Tensor& topk_w, const at::Tensor& l2p,
+                const at::Tensor& l2p_cnt, at::Tensor& out, const at::Tensor& w13, const at::Tensor& w2,
+                at::Tensor& pos, at::Tensor& slot_of, const at::Tensor& counts, const at::Tensor& recv,
+                const at::Tensor& recv_meta, at::Tensor& mid, const at::Tensor& comb, at::Tensor& comb_expect,
+                const at::Tensor& peers, int64_t S, int64_t me, int64_t ffn, int64_t R_max, int64_t count_target,
+                int64_t data_flag, int64_t data_target, int64_t comb_flag, const c10::optional<at::Tensor>& status) {
+  const int64_t T = x.size(0), H = x.size(1), K = topk_idx.size(1);
+  TORCH_CHECK(H % 256 == 0, "ep_forward: hidden size must be a multiple of 256");
+  ep_count(topk_idx, l2p, l2p_cnt, S, me, pos, slot_of, peers, comb_expect, H / 256, status);
+  ep_dispatch(x, topk_w, pos, slot_of, counts, K, S, me, R_max, count_target, peers, status);
+  ep_grouped_gemm(recv, w13, 2 * ffn, mid, counts, S, me, 0, recv_meta, peers, H, data_flag, data_target, status);
+  ep_grouped_gemm(mid, w2, H, mid, counts, S, me, 1, recv_meta, peers, H, data_flag, data_target, status);
+  ep_combine(comb, slot_of, T, K, out, comb_flag, comb_expect, status);
+}
+
 // ---- CUDA IPC ---------------------------------------------------------------
 // Export the allocation that contains `ptr`: returns (handle bytes, offset of
 // ptr inside the allocation).
@@ -444,6 +463,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ep_dispatch", &ep_dispatch);
   m.def("ep_grouped_gemm", &ep_grouped_gemm);
   m.def("ep_combine", &ep_combine);
+  m.def("ep_forward", &ep_forward);
   m.attr("EP_DISPATCH_CTAS") = cx::EP_DISPATCH_CTAS;
   m.def("ipc_export", &ipc_export);
   m.def("ipc_open", &ipc_open);

@@ -474,6 +474,32 @@ void ep_dispatch(const void* x, const float* topk_w, const int* pos, const int* 
       count_target, peers, status);
 }
 
+// Small per-thread cache of 128-byte-swizzled bf16 tensor maps, keyed by
+// everything the map encodes (base, extents, stride, box).
+static CUtensorMap cached_tmap(const void* base, uint64_t inner, uint64_t outer, uint64_t stride, uint32_t box_in,
+                               uint32_t box_out) {
+  struct Entry {
+    const void* base;
+    uint64_t inner, outer, stride;
+    uint32_t box_in, box_out;
+    CUtensorMap map;
+  };
+  constexpr int CAP = 16;
+  thread_local Entry cache[CAP];
+  thread_local int used = 0, next = 0;
+  for (int i = 0; i < used; ++i) {
+    const Entry& e = cache[i];
+    if (e.base == base && e.inner == inner && e.outer == outer && e.stride == stride && e.box_in == box_in &&
+        e.box_out == box_out)
+      return e.map;
+  }
+  Entry& e = cache[next];
+  e = Entry{base, inner, outer, stride, box_in, box_out, make_tmap_bf16_2d(base, inner, outer, stride, box_in, box_out, true)};
+  next = (next + 1) % CAP;
+  if (used < CAP) ++used;
+  return e.map;
+}
+
 void ep_grouped_gemm(const void* A, int lda, const void* B, int n_per_expert, int K, void* D, int ldd,
                      const int* counts_local, int N, int S, int me, int R_max, int mode, const int* recv_meta,
                      EpPeers peers, int H, const uint32_t* wait_flag, uint32_t wait_target, int* status,
@@ -489,8 +515,10 @@ void ep_grouped_gemm(const void* A, int lda, const void* B, int n_per_expert, in
     cudaFuncSetAttribute(ep_grouped_gemm_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, SMEM);
     attr[dev & 63] = true;
   }
-  const CUtensorMap ta = make_tmap_bf16_2d(A, (uint64_t)K, (uint64_t)R_max, (uint64_t)lda * 2, BK, BM, true);
-  const CUtensorMap tb = make_tmap_bf16_2d(B, (uint64_t)K, (uint64_t)S * n_per_expert, (uint64_t)K * 2, BK, BN, true);
+  // The operands of a layer's two GEMMs (receive / mid buffers, expert
+  // weights) stay put between forwards: their tensor maps are encoded once.
+  const CUtensorMap ta = cached_tmap(A, (uint64_t)K, (uint64_t)R_max, (uint64_t)lda * 2, BK, BM);
+  const CUtensorMap tb = cached_tmap(B, (uint64_t)K, (uint64_t)S * n_per_expert, (uint64_t)K * 2, BK, BN);
   ep_grouped_gemm_kernel<<<num_sms(), THREADS, SMEM, s>>>(ta, tb, n_per_expert, K,
                                                           reinterpret_cast<__nv_bfloat16*>(D), ldd, counts_local, N, S,
                                                           me, mode, reinterpret_cast<const int4*>(recv_meta), peers, H,

@@ -100,6 +100,7 @@ class EPMoE:
         self.count_expected = 0      # cumulative u32 targets: + live ranks per forward
         self.data_expected = 0
         self._sink = None
+        self._fwd = None             # (combine-expect view, data flag address, combine flag address)
 
     @property
     def n_live(self) -> int:
@@ -168,18 +169,26 @@ class EPMoE:
         return out
 
     def forward(self, x, topk_idx, topk_w, l2p, l2p_cnt, out: Optional[torch.Tensor] = None):
-        T = x.shape[0]
+        """The five phases in one native call (``ep_forward``): at a few
+        hundred tokens the layer's device work is tens of microseconds, so
+        five separate crossings from Python would set its time."""
+        c, b = self.cfg, self.b
+        if topk_idx.shape[0] > c.max_tokens or topk_idx.shape[1] != c.top_k:
+            raise ValueError(f"EP layer holds {c.max_tokens} tokens x top-{c.top_k}; got {tuple(topk_idx.shape)}")
         out = torch.empty_like(x) if out is None else out
-        with nvtx_range("ep count"):
-            self.phase_count(topk_idx, l2p, l2p_cnt)
-        with nvtx_range("ep dispatch"):
-            self.phase_dispatch(x, topk_w)
-        with nvtx_range("ep gate_up"):
-            self.phase_gate_up()
-        with nvtx_range("ep down"):
-            self.phase_down()
-        with nvtx_range("ep combine"):
-            return self.phase_combine(T, out)
+        self.epoch += 1
+        self.count_expected = (self.count_expected + self.n_live) & 0xFFFFFFFF
+        self.data_expected = (self.data_expected + self.n_live * _C.EP_DISPATCH_CTAS) & 0xFFFFFFFF
+        if self._fwd is None:
+            self._fwd = (b.flags[FLAG_EXPECT:FLAG_EXPECT + 1], b.flag_addr(FLAG_DATA), b.flag_addr(FLAG_COMB))
+        expect, data_flag, comb_flag = self._fwd
+        with nvtx_range("ep forward"):
+            _C.ep_forward(x, topk_idx, topk_w, l2p, l2p_cnt, out, self.w13, self.w2, b.pos, b.slot_of, b.counts,
+                          b.recv, b.recv_meta, b.mid, b.comb, expect, self.peers, c.slots_per_rank, self.rank,
+                          c.ffn, c.recv_rows, self.count_expected, data_flag, self.data_expected, comb_flag,
+                          b.status)
+        ops._n(5)
+        return out
 
 
 def emulated_group(cfg: EPConfig, w13_all: torch.Tensor, w2_all: torch.Tensor, device) -> List[EPMoE]:
