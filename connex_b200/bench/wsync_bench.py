@@ -276,12 +276,49 @@ def probe(cfg: LlamaConfig, iters: int = 3, warmup: int = 2) -> Dict:
     return out
 
 
+def relay_timeline(cfg: LlamaConfig, warmup: int = 2) -> Dict:
+    """One relay broadcast with per-round events on every rank: when the
+    trainer's round kernels end, and when each receiver saw a round land and
+    finished forwarding it (ms from each rank's own start after the opening
+    barrier).  Rank 0 gets the trainer's list and, per round, the earliest
+    and latest receiver times."""
+    world, rank = dist.get_world_size(), dist.get_rank()
+    dev = torch.device("cuda", torch.cuda.current_device())
+    m = engine_manifest(cfg)
+    named = random_trainer_weights(cfg, dev, dtype=torch.float32, seed=1) if rank == 0 else None
+    bc = WeightBroadcast(cfg, mode="relay")
+    n_tasks = plan_jobs(cfg, m, named)[1] if rank == 0 else None
+    box = [n_tasks]
+    dist.broadcast_object_list(box, src=0)
+    for _ in range(warmup):
+        bc.sync(named, box[0])
+    torch.cuda.synchronize()
+    bc.timeline = []
+    bc.sync(named, box[0])
+    torch.cuda.synchronize()
+    bc.check()
+    mine = bc.timeline[-1] if bc.timeline else {}
+    allt = [None] * world
+    dist.all_gather_object(allt, mine)
+    bc.close()
+    if rank != 0:
+        return {}
+    recv = [t for r, t in enumerate(allt) if r != 0]
+    rounds = sorted({int(k[6:]) for t in recv for k in t if k.startswith("landed")})
+    out = {"scatter_end_ms": [allt[0].get(f"scatter{r}") for r in rounds]}
+    for tag in ("landed", "forwarded"):
+        out[f"{tag}_ms_min_max"] = [(min(t[f"{tag}{r}"] for t in recv), max(t[f"{tag}{r}"] for t in recv))
+                                    for r in rounds]
+    return out
+
+
 def main() -> None:
     import argparse
     p = argparse.ArgumentParser()
     p.add_argument("--iters", type=int, default=5)
     p.add_argument("--layers", type=int, default=32)
     p.add_argument("--probe", action="store_true", help="time multicast / scatter / all-gather halves instead")
+    p.add_argument("--relay-timeline", action="store_true", help="per-round events of one relay broadcast")
     a = p.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
@@ -289,6 +326,13 @@ def main() -> None:
     if world > 1:
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
     cfg = LlamaConfig(layers=a.layers)
+    if a.relay_timeline:
+        res = relay_timeline(cfg)
+        if dist.get_rank() == 0:
+            print(json.dumps({"relay_timeline": res, "n_gpus": world}), flush=True)
+        dist.barrier()
+        dist.destroy_process_group()
+        return
     if a.probe:
         res = probe(cfg, a.iters)
         if dist.get_rank() == 0:

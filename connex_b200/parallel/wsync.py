@@ -316,6 +316,7 @@ class WeightBroadcast:
         self.rounds_seen = 0       # rounds whose flag increments reached this rank
         self.round = 0
         self._jobs = None
+        self.timeline: Optional[list] = None   # set to [] to record the relay's per-round events
         dist.barrier(group=self.group)
 
     @property
@@ -433,21 +434,44 @@ class WeightBroadcast:
         self.round += 1
         dist.barrier(group=self.group)      # receivers are off their weights from here on
         ops._n()
+        tl = self.timeline is not None
+        if tl:                              # per-round events, relative to this rank's start
+            ev0 = torch.cuda.Event(enable_timing=True)
+            ev0.record()
+            marks = []
+
+        def mark(tag):
+            if tl:
+                e = torch.cuda.Event(enable_timing=True)
+                e.record()
+                marks.append((tag, e))
         if self.is_src:
             dst = [self.peers[r] for r in st["recv"]]
-            for jobs, jobs_dev in st["rounds"]:
+            for r, (jobs, jobs_dev) in enumerate(st["rounds"]):
                 ops._C.wsync(jobs_dev, jobs, self.total, dst, [p + self.total for p in dst], 0, 0, 0, st["slice"])
+                mark(f"scatter{r}")
             self.relay_received += st["fwd_ctas_total"]      # the forwards land in this arena too
+            if tl:
+                self._record_timeline(ev0, marks)
             return
-        for (jobs, jobs_dev), ctas in zip(st["fwd"], st["src_ctas"]):
+        for r, ((jobs, jobs_dev), ctas) in enumerate(zip(st["fwd"], st["src_ctas"])):
             self.received += ctas                            # this round's scatter has landed here...
             ops.wait_flag(self.flag_addr, self.received & 0xFFFFFFFF, self.status, self.timeout_s)
+            mark(f"landed{r}")
             if jobs_dev is not None:                         # ...so pass this rank's share on to every arena
                 ops._C.wsync(jobs_dev, jobs, self.total, [], [], self.mc, self.mc + self.total + RELAY_FLAG, 0)
+            mark(f"forwarded{r}")
+        if tl:
+            self._record_timeline(ev0, marks)
         self.relay_received += st["fwd_ctas_total"]
         self.rounds_seen = self.round
         if wait:
             ops.wait_flag(self.relay_flag_addr, self.relay_received & 0xFFFFFFFF, self.status, self.timeout_s)
+
+    def _record_timeline(self, ev0, marks) -> None:
+        """Milliseconds from this rank's start of the relay to each mark."""
+        torch.cuda.synchronize(self.device)
+        self.timeline.append({tag: round(ev0.elapsed_time(e), 3) for tag, e in marks})
 
     def catch_up(self, from_rank: int, max_ctas: int = 64) -> None:
         """Copy member ``from_rank``'s arena (the latest version) into this
