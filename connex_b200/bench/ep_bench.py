@@ -199,8 +199,8 @@ class FusedEP:
         self.l2p = torch.arange(E, dtype=torch.int32, device=device).view(E, 1).contiguous()
         self.cnt = torch.ones(E, dtype=torch.int32, device=device)
 
-    def forward(self, x, idx, w, out=None):
-        return self.layer.forward(x, idx, w, self.l2p, self.cnt, out)
+    def forward(self, x, idx, w, out=None, events=None):
+        return self.layer.forward(x, idx, w, self.l2p, self.cnt, out, events=events)
 
     def close(self):
         self.mapper.close()
@@ -210,22 +210,20 @@ PHASES = ("count", "dispatch", "gate_up", "down", "combine")
 
 
 def _phase_times(fused: "FusedEP", x, idx, w, out, iters: int, warmup: int, barrier) -> Dict[str, float]:
-    """Mean device time of each phase of the fused layer (events between the
-    phases on this rank's stream; a phase's time includes its peer waits)."""
-    L, T = fused.layer, x.shape[0]
-    steps = [lambda: L.phase_count(idx, fused.l2p, fused.cnt), lambda: L.phase_dispatch(x, w), L.phase_gate_up,
-             L.phase_down, lambda: L.phase_combine(T, out)]
+    """Mean device time of each phase of the fused layer: events recorded by
+    the single native forward call between its own launches (a phase's time
+    includes its waits for the peers, none of it host time between phases)."""
     for _ in range(warmup):
-        for f in steps:
-            f()
+        fused.forward(x, idx, w, out)
     barrier()
     torch.cuda.synchronize()
-    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(steps) + 1)] for _ in range(iters)]
+    ev = [[torch.cuda.Event(enable_timing=True) for _ in range(len(PHASES) + 1)] for _ in range(iters)]
+    for row in ev:                       # create the events before they are handed over as raw handles
+        for e in row:
+            e.record()
+    torch.cuda.synchronize()
     for it in range(iters):
-        ev[it][0].record()
-        for k, f in enumerate(steps):
-            f()
-            ev[it][k + 1].record()
+        fused.forward(x, idx, w, out, events=ev[it])
     torch.cuda.synchronize()
     return {name: 1000.0 * sum(e[k].elapsed_time(e[k + 1]) for e in ev) / iters for k, name in enumerate(PHASES)}
 

@@ -356,14 +356,27 @@ void ep_forward(const at::Tensor& x, const at::Tensor& topk_idx, const at::Tenso
                 at::Tensor& pos, at::Tensor& slot_of, const at::Tensor& counts, const at::Tensor& recv,
                 const at::Tensor& recv_meta, at::Tensor& mid, const at::Tensor& comb, at::Tensor& comb_expect,
                 const at::Tensor& peers, int64_t S, int64_t me, int64_t ffn, int64_t R_max, int64_t count_target,
-                int64_t data_flag, int64_t data_target, int64_t comb_flag, const c10::optional<at::Tensor>& status) {
+                int64_t data_flag, int64_t data_target, int64_t comb_flag, const c10::optional<at::Tensor>& status,
+                const std::vector<int64_t>& events) {
   const int64_t T = x.size(0), H = x.size(1), K = topk_idx.size(1);
   TORCH_CHECK(H % 256 == 0, "ep_forward: hidden size must be a multiple of 256");
+  TORCH_CHECK(events.empty() || events.size() == 6, "ep_forward: events are 6 CUDA event handles or none");
+  // optional per-phase timing: events[i] recorded before phase i (and after the last)
+  const cudaStream_t st = cur_stream(x);
+  auto mark = [&](int i) {
+    if (!events.empty()) C10_CUDA_CHECK(cudaEventRecord(reinterpret_cast<cudaEvent_t>(events[i]), st));
+  };
+  mark(0);
   ep_count(topk_idx, l2p, l2p_cnt, S, me, pos, slot_of, peers, comb_expect, H / 256, status);
+  mark(1);
   ep_dispatch(x, topk_w, pos, slot_of, counts, K, S, me, R_max, count_target, peers, status);
+  mark(2);
   ep_grouped_gemm(recv, w13, 2 * ffn, mid, counts, S, me, 0, recv_meta, peers, H, data_flag, data_target, status);
+  mark(3);
   ep_grouped_gemm(mid, w2, H, mid, counts, S, me, 1, recv_meta, peers, H, data_flag, data_target, status);
+  mark(4);
   ep_combine(comb, slot_of, T, K, out, comb_flag, comb_expect, status);
+  mark(5);
 }
 
 // ---- CUDA IPC ---------------------------------------------------------------

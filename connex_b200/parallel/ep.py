@@ -168,10 +168,13 @@ class EPMoE:
         ops._n()
         return out
 
-    def forward(self, x, topk_idx, topk_w, l2p, l2p_cnt, out: Optional[torch.Tensor] = None):
+    def forward(self, x, topk_idx, topk_w, l2p, l2p_cnt, out: Optional[torch.Tensor] = None,
+                events: Optional[list] = None):
         """The five phases in one native call (``ep_forward``): at a few
         hundred tokens the layer's device work is tens of microseconds, so
-        five separate crossings from Python would set its time."""
+        five separate crossings from Python would set its time.  ``events``:
+        six recorded-once ``torch.cuda.Event`` (timing) to mark the phase
+        boundaries on the stream."""
         c, b = self.cfg, self.b
         if topk_idx.shape[0] > c.max_tokens or topk_idx.shape[1] != c.top_k:
             raise ValueError(f"EP layer holds {c.max_tokens} tokens x top-{c.top_k}; got {tuple(topk_idx.shape)}")
@@ -186,7 +189,7 @@ class EPMoE:
             _C.ep_forward(x, topk_idx, topk_w, l2p, l2p_cnt, out, self.w13, self.w2, b.pos, b.slot_of, b.counts,
                           b.recv, b.recv_meta, b.mid, b.comb, expect, self.peers, c.slots_per_rank, self.rank,
                           c.ffn, c.recv_rows, self.count_expected, data_flag, self.data_expected, comb_flag,
-                          b.status)
+                          b.status, [e.cuda_event for e in events] if events else [])
         ops._n(5)
         return out
 
