@@ -50,7 +50,7 @@ def run_sub_metrics(world: int, rank: int, dev, layers: int = 32) -> Optional[di
     if world == 1:
         out["weight_convert_ms_local"] = round(ws["local_ms"], 3)
     else:
-        for k in ("fused_multicast_ms", "fused_relay_ms", "fused_p2p_ms", "nccl_ms"):
+        for k in ("fused_multicast_ms", "fused_relay_ms", "fused_relay_p2p_ms", "fused_p2p_ms", "nccl_ms"):
             if ws.get(k) is not None:
                 out[f"weight_sync_{k}"] = round(ws[k], 3)
         if wsh is not None:

@@ -74,7 +74,7 @@ def run(cfg: LlamaConfig, iters: int = 5, warmup: int = 3) -> Dict:
             apply_local(jobs, arena)
         out["local_ms"] = _time(lambda: apply_local(jobs, arena), iters, 1)
         return out
-    for mode in ("multicast", "relay", "p2p"):
+    for mode in ("multicast", "relay", "relay_p2p", "p2p"):
         try:
             bc = WeightBroadcast(cfg, mode=mode)
         except RuntimeError as e:
@@ -276,7 +276,7 @@ def probe(cfg: LlamaConfig, iters: int = 3, warmup: int = 2) -> Dict:
     return out
 
 
-def relay_timeline(cfg: LlamaConfig, warmup: int = 2) -> Dict:
+def relay_timeline(cfg: LlamaConfig, warmup: int = 2, mode: str = "relay") -> Dict:
     """One relay broadcast with per-round events on every rank: when the
     trainer's round kernels end, and when each receiver saw a round land and
     finished forwarding it (ms from each rank's own start after the opening
@@ -286,7 +286,7 @@ def relay_timeline(cfg: LlamaConfig, warmup: int = 2) -> Dict:
     dev = torch.device("cuda", torch.cuda.current_device())
     m = engine_manifest(cfg)
     named = random_trainer_weights(cfg, dev, dtype=torch.float32, seed=1) if rank == 0 else None
-    bc = WeightBroadcast(cfg, mode="relay")
+    bc = WeightBroadcast(cfg, mode=mode)
     n_tasks = plan_jobs(cfg, m, named)[1] if rank == 0 else None
     box = [n_tasks]
     dist.broadcast_object_list(box, src=0)
@@ -319,6 +319,7 @@ def main() -> None:
     p.add_argument("--layers", type=int, default=32)
     p.add_argument("--probe", action="store_true", help="time multicast / scatter / all-gather halves instead")
     p.add_argument("--relay-timeline", action="store_true", help="per-round events of one relay broadcast")
+    p.add_argument("--relay-mode", default="relay", choices=["relay", "relay_p2p"])
     a = p.parse_args()
     world = int(os.environ.get("WORLD_SIZE", "1"))
     dev = torch.device("cuda", int(os.environ.get("LOCAL_RANK", "0")))
@@ -327,7 +328,7 @@ def main() -> None:
         dist.init_process_group("nccl", device_id=dev, timeout=timedelta(seconds=120))
     cfg = LlamaConfig(layers=a.layers)
     if a.relay_timeline:
-        res = relay_timeline(cfg)
+        res = relay_timeline(cfg, mode=a.relay_mode)
         if dist.get_rank() == 0:
             print(json.dumps({"relay_timeline": res, "n_gpus": world}), flush=True)
         dist.barrier()

@@ -268,9 +268,13 @@ class WeightBroadcast:
     ``RELAY_ROUNDS`` rounds; as soon as a round has landed, each receiver
     multicasts its share of that round to every arena.  Measured on 8 B200:
     one trainer multicasting to 7 receivers is limited by the switch's
-    replication (16 GB in 39 ms), while the scatter alone takes 23 ms and the
-    receivers' concurrent multicasts of their slices 25 ms -- pipelined, the
-    two halves overlap.
+    replication (16 GB in 39 ms), the scatter alone takes 23 ms and the
+    receivers' concurrent multicasts of their slices 25 ms; run together
+    (per-round events, ``wsync_bench --relay-timeline``) the forwards lag the
+    scatter by up to 10 ms a round and the whole takes 45 ms, since every
+    receiver's ingress carries its own multicast echo and six others' shares
+    while the scatter competes for it.  ``"relay_p2p"`` forwards with peer
+    stores to the other receivers instead (no echo, no switch replication).
 
     Membership per round (``sync(members=...)``): in multicast mode NVSwitch
     delivers every round to every GPU bound to the group, so a rank that
@@ -302,9 +306,12 @@ class WeightBroadcast:
         mc = int(getattr(self.handle, "multicast_ptr", 0) or 0)
         if mode in ("multicast", "relay") and not mc:
             raise RuntimeError("NVLink multicast is not available on this group")
-        if mode == "relay" and len(self.srcs) != 1:
+        if mode in ("relay", "relay_p2p") and len(self.srcs) != 1:
             raise ValueError("relay mode has one source")
-        self.relay = mode == "relay"
+        self.relay = mode in ("relay", "relay_p2p")
+        # relay_p2p: receivers pass their share on with peer stores to the
+        # other receivers instead of one multicast store to every arena
+        self.relay_p2p = mode == "relay_p2p"
         self.mc = mc if mode in ("auto", "multicast", "relay") else 0
         self.peers = [int(p) for p in self.handle.buffer_ptrs]
         self.weights = LlamaWeights.from_arena(cfg, self.arena[:self.total], self.manifest)
@@ -411,11 +418,14 @@ class WeightBroadcast:
         dist.broadcast_object_list(meta, src=self.src, group=self.group)
         src_tasks, per_round = meta[0]
         st = {"slice": slice_bytes, "recv": recv, "src_ctas": [n_ctas(t, self.device) for t in src_tasks]}
-        fwd_ctas = 0
+        fwd_ctas, fwd_by = 0, [0] * len(recv)
         for ivs in per_round:
             for k in range(len(recv)):
-                fwd_ctas += n_ctas(copy_jobs(ivs[k], 0)[1], self.device) if ivs[k] else 0
+                n = n_ctas(copy_jobs(ivs[k], 0)[1], self.device) if ivs[k] else 0
+                fwd_ctas += n
+                fwd_by[k] += n
         st["fwd_ctas_total"] = fwd_ctas
+        st["fwd_by_recv"] = fwd_by
         if self.is_src:
             st["rounds"] = [(j, j.to(self.device)) for j in split_rounds(self._jobs[0], RELAY_ROUNDS)]
         else:
@@ -450,7 +460,8 @@ class WeightBroadcast:
             for r, (jobs, jobs_dev) in enumerate(st["rounds"]):
                 ops._C.wsync(jobs_dev, jobs, self.total, dst, [p + self.total for p in dst], 0, 0, 0, st["slice"])
                 mark(f"scatter{r}")
-            self.relay_received += st["fwd_ctas_total"]      # the forwards land in this arena too
+            if not self.relay_p2p:
+                self.relay_received += st["fwd_ctas_total"]  # the multicast forwards land in this arena too
             if tl:
                 self._record_timeline(ev0, marks)
             return
@@ -459,11 +470,20 @@ class WeightBroadcast:
             ops.wait_flag(self.flag_addr, self.received & 0xFFFFFFFF, self.status, self.timeout_s)
             mark(f"landed{r}")
             if jobs_dev is not None:                         # ...so pass this rank's share on to every arena
-                ops._C.wsync(jobs_dev, jobs, self.total, [], [], self.mc, self.mc + self.total + RELAY_FLAG, 0)
+                if self.relay_p2p:
+                    others = [self.peers[q] for q in st["recv"] if q != self.rank]
+                    if others:
+                        ops._C.wsync(jobs_dev, jobs, self.total, others,
+                                     [b + self.total + RELAY_FLAG for b in others], 0, 0, 0)
+                else:
+                    ops._C.wsync(jobs_dev, jobs, self.total, [], [], self.mc, self.mc + self.total + RELAY_FLAG, 0)
             mark(f"forwarded{r}")
         if tl:
             self._record_timeline(ev0, marks)
-        self.relay_received += st["fwd_ctas_total"]
+        mine = st["fwd_by_recv"][st["recv"].index(self.rank)]
+        # every forward CTA releases each destination once: multicast reaches
+        # every arena (this one included), peer stores only the other receivers
+        self.relay_received += st["fwd_ctas_total"] - (mine if self.relay_p2p else 0)
         self.rounds_seen = self.round
         if wait:
             ops.wait_flag(self.relay_flag_addr, self.relay_received & 0xFFFFFFFF, self.status, self.timeout_s)
