@@ -274,7 +274,11 @@ class WeightBroadcast:
     scatter by up to 10 ms a round and the whole takes 45 ms, since every
     receiver's ingress carries its own multicast echo and six others' shares
     while the scatter competes for it.  ``"relay_p2p"`` forwards with peer
-    stores to the other receivers instead (no echo, no switch replication).
+    stores to the other receivers instead (no echo, no switch replication);
+    measured on 8 B200 it is slower still (53.9 ms against 46.1 ms relay,
+    40.0 ms one-source multicast and 40.4 ms NCCL), with the same lagging
+    forwards: the receivers' ingress under the concurrent scatter, not the
+    multicast, sets the time.  ``"auto"`` stays one-source multicast.
 
     Membership per round (``sync(members=...)``): in multicast mode NVSwitch
     delivers every round to every GPU bound to the group, so a rank that
