@@ -120,7 +120,7 @@ dist.destroy_process_group()
 
 
 @pytest.mark.gpu
-@pytest.mark.parametrize("mode", ["auto", "p2p", "relay", "relay_p2p"])
+@pytest.mark.parametrize("mode", ["auto", "multicast", "p2p", "relay", "relay_p2p"])
 def test_wsync_broadcast_two_gpus(mode, tmp_path):
     if torch.cuda.device_count() < 2:
         pytest.skip("needs 2 GPUs")
