@@ -323,6 +323,7 @@ class TPStepper(Stepper):
     def __init__(self, inner: Stepper, cpu_group=None, src: int = 0):
         self.inner, self.pg, self.src = inner, cpu_group, src
         self.broken: Optional[str] = None
+        self._abort_thread = None
         for k in ("max_batch", "max_ctx", "max_step_tokens", "num_blocks", "block_size", "vocab_size",
                   "supports_mixed"):
             setattr(self, k, getattr(inner, k))
@@ -344,7 +345,8 @@ class TPStepper(Stepper):
                 dist.broadcast_object_list([("abort", self.broken)], src=self.src, group=self.pg)
             except Exception:  # noqa: BLE001 - the followers may be gone or stuck; nothing more to do
                 pass
-        _th.Thread(target=tell, name="cx-tp-abort", daemon=True).start()
+        self._abort_thread = _th.Thread(target=tell, name="cx-tp-abort", daemon=True)
+        self._abort_thread.start()
         return GroupStepError(f"step failed on rank {self.src}; the tensor-parallel group stops: {self.broken}")
 
     def _run(self, kind, rids, seqs, *extra):
@@ -380,6 +382,10 @@ class TPStepper(Stepper):
                 self._send(("stop",))
             except Exception:  # noqa: BLE001 - the followers are gone; close this rank anyway
                 pass
+        elif self._abort_thread is not None:
+            # give the abort notice a bounded chance to reach the followers
+            # before this rank's process group can be torn down under it
+            self._abort_thread.join(timeout=5.0)
         self.inner.close()
 
 

@@ -330,7 +330,8 @@ def _tp_rank_failing(rank, port, q, failing_rank):
             return rank == failing_rank and kind == "decode" and seen["decode"] == 3
         inner = RuleStepper(step_delay_s=0.001, fail_on=fail_on)
         if rank == 0:
-            eng = GenerationEngine(TPStepper(inner)).start()
+            stepper = TPStepper(inner)
+            eng = GenerationEngine(stepper).start()
             out = _collect(eng, [1, 5, 6], 12)
             assert out["done"].wait(30)
             assert wait_until(lambda: not eng.alive, 30)
@@ -341,6 +342,7 @@ def _tp_rank_failing(rank, port, q, failing_rank):
                 refused = True
             q.put((0, eng.error, out["reason"], len(out["toks"]), refused))
             eng.stop()
+            stepper.close()        # as the server does at shutdown: the abort notice goes out first
         else:
             try:
                 tp_follow(inner)
