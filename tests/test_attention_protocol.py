@@ -43,6 +43,7 @@ class Model:
     def __init__(self, items, rng, o_final_on_s=False):
         self.rng = rng
         self.o_final_on_s = o_final_on_s      # the rejected design (negative control)
+        self.partial_tail = {i for i in range(len(items)) if rng.random() < 0.5}   # paged items
         self.items = items
         b = {}
         for x in range(2):
@@ -166,7 +167,9 @@ class Model:
 
     def softmax(self, x):
         sw = ow = steps = 0          # phases waited on s_full / o_full; score steps taken
-        for nt, nkv in self.items:
+        kv = 0                       # ring position of the item's key tile 0
+        for n_it, (nt, nkv) in enumerate(self.items):
+            zero_x = 0 if nt[0] == nkv else 1     # the tile whose P.V reads the last V tile first
             for j in range(nt[x]):
                 yield from self.wait(self.b[f"s_full{x}"], sw)
                 sw += 1
@@ -174,6 +177,11 @@ class Model:
                 if self.qk_exec[x] != steps:       # exactly the scores this step waited for
                     self.errors.append(f"softmax {x} step {steps - 1} saw {self.qk_exec[x]} Q.K^T done")
                 yield                                   # compute
+                if x == zero_x and j == nkv - 1 and n_it in self.partial_tail:
+                    # paged: unwritten cache rows of the last V tile are zeroed
+                    # before this tile's P.V (a second consumer of v_full)
+                    u = kv + j
+                    yield from self.wait(self.b[f"v_full{u & 1}"], u >> 1)
                 self.b[f"p_full{x}"].arrive()
             if nt[x]:
                 if self.o_final_on_s:
@@ -183,6 +191,7 @@ class Model:
                     yield from self.wait(self.b[f"o_full{x}"], ow)
                     ow += 1
                 yield                                   # epilogue
+            kv += nkv
 
     def run(self, max_steps=200000):
         roles = [self.producer(), self.mma_thread(), self.softmax(0), self.softmax(1)]
